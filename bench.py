@@ -1,0 +1,394 @@
+"""Benchmark: FP4 delta-CSR sparse layer, forward + fused backward/update.
+
+Workload: one 8192 x 8192 layer at 95 % sparsity
+(410 synapses per input row, columns uniform without replacement), batch 64,
+x = ReLU(N(0,1)) with a further 60 % zeroed (~80 % zeros), dy ~ N(0,1); a
+step is forward_dense + backward_dense(learning_rate=0.01, lr_per_row_nnz)
+-- grad-input plus the in-place update of the existing synapses, the
+reference's training step.  Weights follow the reference's load path
+(N(0,0.02) pre-scaled per row by max|w|/6, value_scale set).  Steps rotate
+over --layers independent layer copies (each with its own x/dy/y/dx), whose
+combined footprint exceeds the 126 MB L2, so every step streams from HBM.
+
+metric: effective GB/s = algorithmic bytes per step / time per step, with
+algorithmic bytes = forward (W stream + x + y) + backward (W stream read +
+value bytes written + x + dy + dx + per-row/per-column state); the W stream
+is the ULEB128 index bytes + 1 FP4 byte per synapse + 2 x (n_in+1) x 4 B of
+row offsets.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Under torchrun (N > 1) each rank runs its own layers (the single-layer
+config does not shard: replicas), and value sums over ranks with the time
+taken as the max over ranks.  --impl reference times the reference's own
+C++/OpenMP CPU path (built from its sources into oracle/_ref/) on the host
+cores with all threads.
+"""
+from __future__ import annotations
+
+import argparse
+import glob
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "tests"))
+
+N_IN = N_OUT = 8192
+PER_ROW = 410
+BATCH = 64
+LR = 0.01
+METRIC = "sparse fwd+bwd effective HBM GB/s (8192^2, 95% sparse, batch 64, FP4 delta-CSR)"
+
+
+def make_workload(seed=0):
+    from helpers import random_layer, relu_sparse_x
+    p, i, w, vs = random_layer(N_IN, N_OUT, PER_ROW, seed=seed)
+    rng = np.random.default_rng(seed + 1)
+    x = relu_sparse_x(rng, BATCH, N_IN)
+    dy = rng.normal(0.0, 1.0, (BATCH, N_OUT)).astype(np.float32)
+    return p, i, w, vs, x, dy
+
+
+def algorithmic_bytes(idx_bytes, nnz):
+    w_stream = idx_bytes + nnz + 2 * (N_IN + 1) * 4
+    act = BATCH * 4
+    fwd = w_stream + act * N_IN + act * N_OUT
+    state = N_IN * 32 + N_OUT * 12   # value_scale/importance/step r+w, accumulators r+w
+    bwd = w_stream + nnz + act * N_IN + act * N_OUT + act * N_IN + state
+    return fwd, bwd
+
+
+def load_layer(S_cls, p, i, w, vs, device=0):
+    layer = S_cls(N_IN, N_OUT, int(len(i) * 1.25), 1, device)
+    layer.load_weights(p, i, w)
+    for r in range(N_IN):
+        layer.set_value_scale_raw(r, float(vs[r]))
+        layer.set_importance_scale_raw(r, LR / 6.0)
+    return layer
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [t.strip() for t in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def traffic_from_profile():
+    """Per-launch DRAM bytes of the backward update kernel from the committed
+    ncu summary (profiles/*.json written from an ncu capture), or None."""
+    for f in sorted(glob.glob(os.path.join(ROOT, "profiles", "*traffic*.json"))):
+        try:
+            d = json.load(open(f))
+            return d.get("k_backward_update_bytes_per_launch")
+        except (OSError, ValueError):
+            continue
+    return None
+
+
+# ── CPU reference (the reference's own C++/OpenMP build) ────────────────────
+def reference_module():
+    """Imports the reference's pybind11 module built by oracle/build_ref.py."""
+    import importlib.util
+    flags_file = os.path.join(ROOT, "oracle", "_ref", "native", "cpu_flags.txt")
+    variant = "x86-64-v3"
+    try:
+        need = set(open(flags_file).read().split())
+        have = set()
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("flags"):
+                have = set(line.split(":", 1)[1].split())
+                break
+        if need and need <= have:
+            variant = "native"
+    except OSError:
+        pass
+    paths = glob.glob(os.path.join(ROOT, "oracle", "_ref", variant, "_cpu*.so"))
+    if not paths:
+        return None, variant
+    spec = importlib.util.spec_from_file_location("_cpu", paths[0])
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod, variant
+
+
+def run_reference_cpu(work, budget_s, threads, max_steps=None):
+    """Times forward_dense + backward_dense on the reference's CPU path."""
+    mod, variant = reference_module()
+    if mod is None:
+        return None
+    p, i, w, vs, x, dy = work
+    layer = mod.SparseLinearLayer(N_IN, N_OUT, int(len(i) * 1.25), threads)
+    layer.load_weights(p, i, w)
+    for r in range(N_IN):
+        layer.set_value_scale_raw(r, float(vs[r]))
+        layer.set_importance_scale_raw(r, LR / 6.0)
+    layer.forward_dense(x)
+    layer.backward_dense(dy, LR, lr_per_row_nnz=True)        # warm-up
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        layer.forward_dense(x)
+        layer.backward_dense(dy, LR, lr_per_row_nnz=True)
+        n += 1
+        el = time.perf_counter() - t0
+        if (max_steps and n >= max_steps) or (el >= budget_s and n >= 2):
+            break
+    return el / n, n, variant
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--layers", type=int, default=16)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        work = make_workload()
+        threads = os.cpu_count() or 1
+        res = run_reference_cpu(work, budget_s=max(args.cpu_seconds, 5.0), threads=threads,
+                                max_steps=max(args.steps, 2))
+        if res is None:
+            print(json.dumps({"impl": "reference", "unavailable": "reference CPU build missing from oracle/_ref"}))
+            return 0
+        per_step, n, variant = res
+        fwd_b, bwd_b = algorithmic_bytes(_uleb_bytes(work), len(work[1]))
+        v = (fwd_b + bwd_b) / per_step / 1e9
+        line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": args.gpus,
+                "steps": n, "warmup": 1, "ms_per_step": per_step * 1e3, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "fp32 activations, FP4 weights",
+                "data": "synthetic", "config": {"workload": "config2: 8192x8192, 95% sparse, batch 64, fwd+bwd(lr=0.01)"},
+                "cpu_baseline": {"value": v, "unit": "GB/s", "cores": threads, "kind": "reference",
+                                 "sample": f"{n} steps of the full workload (sili._cpu built -march={variant})"},
+                "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        return 0
+
+    import torch
+    import sili__new_b200 as S
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300))
+    dev = local if world > 1 else 0
+    torch.cuda.set_device(dev)
+
+    work = make_workload()
+    p, i, w, vs, x_np, dy_np = work
+    layers = [load_layer(S.SparseLinearLayer, p, i, w, vs, device=dev) for _ in range(args.layers)]
+    xs = [torch.from_numpy(x_np).cuda(dev) for _ in range(args.layers)]
+    dys = [torch.from_numpy(dy_np).cuda(dev) for _ in range(args.layers)]
+    ys = [torch.empty(BATCH, N_OUT, device=f"cuda:{dev}") for _ in range(args.layers)]
+    dxs = [torch.empty(BATCH, N_IN, device=f"cuda:{dev}") for _ in range(args.layers)]
+    idx_bytes = int(layers[0].raw_state()["byte_end"].sum() - layers[0].raw_state()["byte_start"][:-1].sum())
+    fwd_b, bwd_b = algorithmic_bytes(idx_bytes, len(i))
+    step_bytes = fwd_b + bwd_b
+    stream = torch.cuda.current_stream(dev)
+    sh = stream.cuda_stream
+
+    def step(j, timed_kernels=False):
+        L = layers[j % len(layers)]
+        L.forward_dense_ptr(xs[j % len(layers)].data_ptr(), BATCH, ys[j % len(layers)].data_ptr(), sh)
+        L.backward_dense_ptr(dys[j % len(layers)].data_ptr(), BATCH, LR, True, True, 0.999, 1e-8,
+                             dxs[j % len(layers)].data_ptr(), sh, 0)
+
+    for j in range(args.warmup):
+        step(j)
+    torch.cuda.synchronize(dev)
+
+    # ── device-resident throughput (value) ─────────────────────────────────
+    clocks = ClockSampler(dev)
+    clocks.start()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    launches0 = S.kernel_launches()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for j in range(args.steps):
+        step(j)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    launches = S.kernel_launches() - launches0
+    ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([ms], device=f"cuda:{dev}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    clk = clocks.stop()
+    per_step_ms = ms / args.steps
+    value = world * step_bytes / (per_step_ms * 1e-3) / 1e9
+
+    # ── per-kernel timing for the roofline (same stream, CUDA events) ──────
+    for L in layers:
+        L.set_kernel_timing(True)
+    fw, bw = [], []
+    for j in range(min(args.steps, 3 * len(layers))):
+        step(j)
+        f, b = layers[j % len(layers)].kernel_ms()
+        fw.append(f)
+        bw.append(b)
+    for L in layers:
+        L.set_kernel_timing(False)
+    fwd_ms, bwd_ms = float(np.mean(fw)), float(np.mean(bw))
+    hbm_peak, peak_kind = peaks()
+    # dominant kernel: the fused backward/update
+    bwd_kernel_bytes = bwd_b
+    achieved = bwd_kernel_bytes / (bwd_ms * 1e-3) / 1e9
+
+    # ── end to end through the public API with pinned host buffers ─────────
+    hx = [torch.from_numpy(x_np).pin_memory() for _ in range(2)]
+    hdy = [torch.from_numpy(dy_np).pin_memory() for _ in range(2)]
+    hy = [torch.empty(BATCH, N_OUT).pin_memory() for _ in range(2)]
+    hdx = [torch.empty(BATCH, N_IN).pin_memory() for _ in range(2)]
+    e2e_steps = max(5, min(args.steps, 50))
+
+    def e2e_step(j):
+        L = layers[j % len(layers)]
+        L.forward_dense_ptr(hx[j % 2].data_ptr(), BATCH, hy[j % 2].data_ptr(), sh)
+        L.backward_dense_ptr(hdy[j % 2].data_ptr(), BATCH, LR, True, True, 0.999, 1e-8, hdx[j % 2].data_ptr(), sh, 0)
+
+    for j in range(3):
+        e2e_step(j)
+    torch.cuda.synchronize(dev)
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for j in range(e2e_steps):
+        e2e_step(j)
+    torch.cuda.synchronize(dev)
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([e2e_s], device=f"cuda:{dev}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e_value = world * step_bytes * e2e_steps / e2e_s / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        res = run_reference_cpu(work, budget_s=args.cpu_seconds, threads=threads)
+        if res is not None:
+            per, n, variant = res
+            cpu = {"value": step_bytes / per / 1e9, "unit": "GB/s", "cores": threads, "kind": "reference",
+                   "sample": f"{n} fwd+bwd steps of the full config-2 workload on sili._cpu "
+                             f"(reference source built -march={variant}, num_cpus={threads})"}
+
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    line = {
+        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": per_step_ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp32 activations, FP4 (E2M1-with-NaN) weights",
+        "data": "synthetic",
+        "config": {"workload": "config2: 8192x8192, 95% sparse (410/row), batch 64, forward_dense + "
+                               "backward_dense(lr=0.01, lr_per_row_nnz) on FP4 delta-CSR",
+                   "layers_rotated": args.layers, "l2": "inputs larger than L2 (16 layer copies rotated)",
+                   "parallelism": f"replicas x{world}", "bytes_per_step": step_bytes,
+                   "forward_kernel_ms": fwd_ms, "backward_kernel_ms": bwd_ms},
+        "roofline": {"bound": "hbm", "kernel": "k_backward_update", "achieved": achieved, "peak": hbm_peak,
+                     "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / hbm_peak,
+                     "traffic": traffic_from_profile(), "algorithmic_bytes_per_launch": bwd_kernel_bytes},
+        "cpu_baseline": cpu,
+        "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": BATCH * (N_IN + N_OUT) * 4,
+                "d2h_bytes_per_step": BATCH * (N_IN + N_OUT) * 4},
+        "gpu_launches": launches,
+        "clocks": clk,
+    }
+    print(json.dumps(line))
+    return 0
+
+
+def _uleb_bytes(work):
+    p, i = work[0], work[1]
+    d = np.diff(np.concatenate([[0], i]).astype(np.int64))
+    # first delta of each row is the absolute column
+    starts = p[:-1]
+    d[starts[starts < len(i)]] = i[starts[starts < len(i)]]
+    return int(np.sum(np.where(d < 128, 1, np.where(d < 16384, 2, np.where(d < 2097152, 3, 4)))))
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,179 @@
+/* sili_b200 -- C ABI of the B200 (sm_100a) FP4 delta-CSR sparse-layer library.
+ *
+ * One opaque handle per sparse linear layer.  The layer's state (ULEB128
+ * column-delta bytes, FP4 weight/importance bytes, per-row offsets and
+ * headroom, per-row/per-column scales, synaptogenesis accumulators, probes)
+ * lives in device memory of the device the layer was created on.
+ *
+ * Every entry point mirrors one method of the reference's pybind11 class
+ * sili._cpu.SparseLinearLayer (sili/cpu_backend.cpp:349-1013, bound at
+ * :1506-1738) and is cited below.  Conventions:
+ *
+ *  - Return value: SILI_OK (0) or an error code.  sili_last_error() gives the
+ *    message of the calling thread's last failure.  The pybind11 module maps
+ *    SILI_EINVAL -> ValueError, SILI_ENOMEM -> MemoryError, SILI_EHEADROOM and
+ *    SILI_ECUDA -> RuntimeError, as the reference's C++ exceptions map.
+ *  - Array pointers may be host or device memory (detected per pointer).
+ *    Host arrays are copied in / out inside the call and the call returns
+ *    after the copy back; device arrays are used in place and the work is
+ *    enqueued on `stream` (NULL = the layer's own stream) without a host
+ *    synchronisation.
+ *  - Activations and gradients are fp32, row-major [batch, features].
+ *  - Sizes are C int, as in the reference (S = int, cpu_backend.cpp:353).
+ *
+ * There is no CPU fallback: every compute entry point runs CUDA kernels and
+ * fails with SILI_ECUDA when no CUDA device is usable.
+ */
+#ifndef SILI_B200_H
+#define SILI_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SILI_OK 0
+#define SILI_EINVAL 1     /* std::invalid_argument -> ValueError */
+#define SILI_ENOMEM 2     /* std::bad_alloc (budget) -> MemoryError */
+#define SILI_EHEADROOM 3  /* std::runtime_error (row out of blank space) */
+#define SILI_ECUDA 4      /* CUDA error / no device */
+#define SILI_ETIMEOUT 5   /* a bounded device-side wait gave up */
+
+/* backward flags */
+#define SILI_LR_PER_ROW_NNZ 1u
+#define SILI_DAMP_BY_IMPORTANCE 2u
+
+typedef struct sili_layer sili_layer;
+
+const char* sili_last_error(void);
+int sili_device_count(int* count);
+/* Number of CUDA kernels this library has launched in this process (all
+ * layers, all devices) -- lets a caller count the device work of a region. */
+int sili_kernel_launches(int64_t* count);
+/* Profiling: when enabled, every compute call records CUDA events around its
+ * main kernel; sili_layer_kernel_ms returns the last forward / backward main
+ * kernels' durations in milliseconds (synchronising the layer's stream). */
+int sili_layer_set_kernel_timing(sili_layer* h, int enable);
+int sili_layer_kernel_ms(sili_layer* h, float* forward_ms, float* backward_ms);
+
+/* ── lifetime / loading ──────────────────────────────────────────────────── */
+/* SparseLinearLayerImpl(n_inputs, n_outputs, max_weights, num_cpus),
+ * cpu_backend.cpp:375-447.  stochastic = 1 for SparseLinearLayer,
+ * 0 for SparseLinearLayerDeterministic (aliases :992-1013). */
+int sili_layer_create(int n_in, int n_out, int max_weights, int device, int stochastic,
+                      sili_layer** out);
+int sili_layer_destroy(sili_layer* h);
+/* load_weights(ptrs, indices, weights), cpu_backend.cpp:859-901 */
+int sili_layer_load_weights(sili_layer* h, const int* ptrs, const int* idx, const float* vals, int nnz);
+/* fp4_seed_stochastic_rng(seed), fp4quant.hpp:186-188 (per-layer here) */
+int sili_layer_seed_rng(sili_layer* h, uint64_t seed);
+int sili_layer_sync(sili_layer* h);
+
+/* ── scales (cpu_backend.cpp:465-471, :792-829, bindings :1578-1650) ────── */
+#define SILI_SCALE_VALUE 0              /* value_scale[row*rank+k]          */
+#define SILI_SCALE_OUTPUT 1             /* output_scale[col*rank+k]         */
+#define SILI_SCALE_IMPORTANCE 2         /* importance_scale[row]            */
+#define SILI_SCALE_OUTPUT_IMPORTANCE 3  /* output_importance_scale[col]     */
+#define SILI_SCALE_VALUE_IMPORTANCE 4   /* value_scale_importance (read)    */
+#define SILI_SCALE_OUTPUT_SCALE_IMPORTANCE 5 /* output_scale_importance (read) */
+#define SILI_SCALE_VALUE_MOMENTUM 6     /* value_scale_momentum (read)      */
+int sili_layer_set_scale_rank(sili_layer* h, int rank);
+int sili_layer_get_scale_rank(sili_layer* h, int* rank);
+/* set_*_scale_raw(_k): kind SILI_SCALE_VALUE/OUTPUT/IMPORTANCE/OUTPUT_IMPORTANCE */
+int sili_layer_set_scale(sili_layer* h, int kind, int index, int k, float v);
+int sili_layer_get_scale(sili_layer* h, int kind, int index, int k, float* v);
+/* bulk read of a whole scale vector (n entries of the [n_rows_or_cols * rank] view) */
+int sili_layer_get_scales(sili_layer* h, int kind, float* out, int n);
+/* value_scale_step / output_scale_step counters (bias correction) */
+int sili_layer_get_steps(sili_layer* h, int which /*0 value, 1 output*/, uint32_t* out, int n);
+/* rescale_value_row / rescale_importance_row, cpu_backend.cpp:815-829 */
+int sili_layer_rescale_row(sili_layer* h, int kind, int row, float new_scale);
+
+/* ── compute ─────────────────────────────────────────────────────────────── */
+/* forward_dense(x), cpu_backend.cpp:475-492 -> disldo_forward
+ * (linear_disldo.hpp:68-345).  Keeps x as the layer's last input. */
+int sili_layer_forward_dense(sili_layer* h, const float* x, int batch, float* y, void* stream);
+/* backward_dense(dy, lr, lr_per_row_nnz, damp_by_importance, beta2, eps),
+ * cpu_backend.cpp:496-529 -> disldo_backward (linear_disldo.hpp:462-2113)
+ * with beta1 0.9, min_decay_frac 0, max_abs_delta 2, max_ci 100.
+ * x = NULL uses the last forward input. */
+int sili_layer_backward_dense(sili_layer* h, const float* x, const float* dy, int batch, float lr,
+                              unsigned flags, float beta2, float eps, float* dx, void* stream);
+/* forward_sparse(ptrs, indices, values, batch), cpu_backend.cpp:571-585
+ * -> sisldo_forward (sisldo_ops.hpp:198-551) */
+int sili_layer_forward_sparse(sili_layer* h, const int* ptrs, const int* idx, const float* vals,
+                              int nnz, int batch, float* y, void* stream);
+/* backward_sparse(x, dy_ptrs, dy_indices, dy_values, batch, lr, ...),
+ * cpu_backend.cpp:587-603 -> disldo_backward_sparse_grad (sisldo_ops.hpp:589-1104) */
+int sili_layer_backward_sparse(sili_layer* h, const float* x, const int* dptrs, const int* didx,
+                               const float* dvals, int dnnz, int batch, float lr, unsigned flags,
+                               float beta2, float eps, float* dx, void* stream);
+
+/* ── synaptogenesis and headroom management ─────────────────────────────── */
+/* build_probes(k, per_row), cpu_backend.cpp:607-610 -> delta_csr_build_probes
+ * (delta_csr_memory.hpp:1308-1427) */
+int sili_layer_build_probes(sili_layer* h, int k, int per_row);
+int sili_layer_num_probes(sili_layer* h, int64_t* n);
+int sili_layer_get_probes(sili_layer* h, int* rows, int* cols, float* scores);
+/* synap_row_step over rows [row0, row0+nrows) (wrapping), cpu_backend.cpp:611-635
+ * -> delta_csr_synap_row_step (delta_csr_memory.hpp:1019-1258) once per row, in
+ * row order.  did_any (may be NULL) gets 1 if any row step returned true. */
+int sili_layer_synap_rows(sili_layer* h, int row0, int nrows, float importance_cutoff,
+                          int max_row_weights, int max_prune_per_step, float importance_eps,
+                          int* did_any);
+/* equalizer_step() for one row, cpu_backend.cpp:649-657 -> delta_csr_equalize_step */
+int sili_layer_equalize_row(sili_layer* h, int row);
+/* equalize_to_capacity, cpu_backend.cpp:684-729 */
+int sili_layer_equalize_to_capacity(sili_layer* h, int target_elems_per_row, int target_bytes_per_row);
+/* compact / expand_headroom / expand_headroom_to, cpu_backend.cpp:737-785 */
+int sili_layer_compact(sili_layer* h);
+int sili_layer_expand_headroom(sili_layer* h, float blank_fraction);
+int sili_layer_expand_headroom_to(sili_layer* h, int min_nnz_per_row, float blank_fraction);
+/* zero_accum(), cpu_backend.cpp:851-854 */
+int sili_layer_zero_accum(sili_layer* h);
+/* BASELINE config-3 rule (no reference function): exact top-k of
+ * |sum_b x[b,r]*dy[b,c]| over non-existing (r,c), prune the same number of
+ * smallest |FP4(w)*S(r,c)|, rebuild the arrays.  x [batch,n_in], dy [batch,n_out]. */
+int sili_layer_topk_dyx_step(sili_layer* h, const float* x, const float* dy, int batch, int64_t k,
+                             void* stream);
+
+/* ── state export (cpu_backend.cpp:946-983, 1667-1738) ──────────────────── */
+/* sizes[0..5] = n_in, n_out, nnz, index bytes, value bytes, block4 tiles */
+int sili_layer_sizes(sili_layer* h, int64_t* sizes);
+/* absolute CSR of the live synapses: ptrs[n_in+1], idx[nnz], weights
+ * (stored FP4 units), importance (stored FP4 units) -- any may be NULL */
+int sili_layer_export(sili_layer* h, int* ptrs, int* idx, float* w, float* imp);
+/* raw delta-CSR state: byte_start[n_in+1], byte_end[n_in], elem_start[n_in+1],
+ * elem_end[n_in] (int64), indices bytes, value bytes -- any may be NULL */
+int sili_layer_raw(sili_layer* h, int64_t* byte_start, int64_t* byte_end, int64_t* elem_start,
+                   int64_t* elem_end, uint8_t* indices, uint8_t* values);
+/* overwrite the stored value bytes (weight code << 4 | importance code) */
+int sili_layer_set_value_bytes(sili_layer* h, const uint8_t* values, int64_t n);
+int sili_layer_accums(sili_layer* h, float* input_accum, float* grad_accum);
+int sili_layer_set_accums(sili_layer* h, const float* input_accum, const float* grad_accum);
+int sili_layer_out_degree(sili_layer* h, int* out);
+/* stats[0..5] = value_l1, value_l2_sq, value_max_abs, importance_l1,
+ * importance_l2_sq, importance_max_abs (delta_csr_types.hpp:1265-1270) */
+int sili_layer_stats(sili_layer* h, double* stats);
+int sili_layer_recompute_stats(sili_layer* h);
+/* last forward input [batch, n_in] (NULL out -> only batch/cols) */
+int sili_layer_last_input(sili_layer* h, float* out, int* batch, int* cols);
+
+/* ── module functions (cpu_backend.cpp:3075-3196) ───────────────────────── */
+/* fp4_quantize_array: deterministic FP4 encode, fp4quant.hpp:86-121 */
+int sili_fp4_quantize(const float* vals, uint8_t* codes, int64_t n, void* stream);
+/* dense_to_csr(x, threshold): |v| > threshold, row-major.  Two-phase: call
+ * with idx/vals NULL to get nnz in *nnz_out and ptrs, then again to fill. */
+int sili_dense_to_csr(const float* x, int rows, int cols, float threshold, int* ptrs, int* idx,
+                      float* vals, int64_t* nnz_out, void* stream);
+/* dense_to_top_k_csr(x, k): global exact top-k by |v|, row-major CSR,
+ * ascending columns; ties at the k-th magnitude go to the lower flat index. */
+int sili_dense_to_top_k_csr(const float* x, int rows, int cols, int64_t k, int* ptrs, int* idx,
+                            float* vals, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -502,7 +502,10 @@ class RefLayer(_LayerBase):
         b = np.ascontiguousarray(b, np.uint8)
         self.L.ref_set_value_bytes(self.h, _ptr(b), len(b))
 
-    def set_scale_rank(self, rank): self.L.ref_set_scale_rank(self.h, rank)
+    def set_scale_rank(self, rank):
+        self._rank = rank
+        self.L.ref_set_scale_rank(self.h, rank)
+
     def get_scale_rank(self):
         # The shim does not expose the rank; it is only ever set through set_scale_rank.
         return getattr(self, "_rank", 1)

@@ -526,7 +526,7 @@ void o_backward_dense(OLayer* L, const float* x, const float* dy, int batch, flo
                     float* m = &L->value_scale_momentum.d[i];
                     float* v = &L->value_scale_importance.d[i];
                     const float nm = fmaf(0.9f, *m, (1.0f - 0.9f) * g);
-                    const float nv = fmaf(beta2, *v, (1.0f - beta2) * g * g);
+                    const float nv = fmaf(beta2, *v, (1.0f - beta2) * (g * g));
                     if (!isfinite(nm) || !isfinite(nv)) continue;
                     const float nvs = L->value_scale.d[i] - dead_lr * nm / (sqrtf(nv) + eps);
                     if (!isfinite(nvs)) continue;
@@ -589,6 +589,7 @@ void o_backward_sparse(OLayer* L, const float* x, const int* dptrs, const int* d
     if (L->value_scale.n < n_in) fvec_resize(&L->value_scale, n_in, 1.0f);
     if (L->value_scale_importance.n < n_in) fvec_resize(&L->value_scale_importance, n_in, 0.0f);
     memset(dx, 0, (size_t)batch * n_in * sizeof(float));
+    L->call++;
     if (L->total_nnz == 0) return;
     double* sgs = (double*)calloc((size_t)n_in + 1, sizeof(double));
     double* sgc = (double*)calloc((size_t)n_in + 1, sizeof(double));

@@ -1,0 +1,127 @@
+// Launch wrappers for the sili_b200 kernels (host-callable, stream-ordered).
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace sili {
+
+// process-wide count of kernel launches made through the launch_* wrappers
+void count_launch(int n = 1);
+long long launch_count();
+
+// Everything a kernel needs to read or write one layer's device state.
+struct LayerView {
+    int64_t n_in, n_out;
+    int rank;
+    const int64_t* bs;   // byte_start [n_in+1]
+    const int64_t* be;   // byte_end   [n_in]
+    const int64_t* es;   // elem_start [n_in+1]
+    const int64_t* ee;   // elem_end   [n_in]
+    const uint8_t* idx;  // ULEB128 column deltas
+    uint8_t* val;        // FP4BiPacked bytes: weight code << 4 | importance code
+    float* vs;           // value_scale [n_in*rank]
+    float* os;           // output_scale [n_out*rank]
+    float* vsi;          // value_scale_importance [n_in*rank]
+    float* osi;          // output_scale_importance [n_out*rank]
+    float* vsm;          // value_scale_momentum [n_in*rank]
+    uint32_t* vstep;     // value_scale_step [n_in*rank]
+    uint32_t* ostep;     // output_scale_step [n_out*rank]
+    const float* is;     // importance_scale [n_in]
+    const float* ois;    // output_importance_scale [n_out]
+    // derived index (rebuilt after structural changes)
+    const int* rowptr;   // [n_in+1] exclusive scan of row nnz
+    const int* abs_cols; // [nnz] absolute column of every live synapse, row-major
+    const int* colptr;   // [n_out+1] CSC shadow: synapses of column c at [colptr[c], colptr[c+1])
+    const int* crow;     // [nnz] their rows, ascending within a column
+    const int* cvpos;    // [nnz] their positions in val[]
+};
+
+struct UpdateParams {
+    float lr, beta2, eps;
+    bool lr_per_row_nnz, damp, stochastic, os_trainable;
+    uint64_t call_key;
+    const float* pow_tab;  // pow_tab[s] = powf(beta2, s) (host libm), s < pow_n
+    int pow_n;
+    float* colg;           // [n_out*rank] output_scale gradient sums (os_trainable)
+    float* colc;           // [n_out*rank] forward-contribution sums
+    double* stats;         // [4] importance l1 new-old, l2 new-old (sums)
+    float* stat_max;       // [1] importance max (float bits as uint max)
+};
+
+void launch_transpose(const float* in, float* out, int64_t R, int64_t C, cudaStream_t s);
+void launch_accum_abs(const float* x, float* acc, int B, int64_t n, cudaStream_t s);
+void launch_accum_abs_t(const float* xT, float* acc, int B, int64_t n, cudaStream_t s);
+void launch_accum_abs_csr(const int* ptrs, const int* idx, const float* vals, int rows, int ncols, float* acc,
+                          cudaStream_t s);
+
+// forward: y[B, n_out] from xT [n_in, B]; sparse_formula selects the
+// sisldo_forward arithmetic (sisldo_ops.hpp:289-308) over disldo_forward's.
+void launch_forward(const LayerView& L, const float* xT, int B, float* y, bool sparse_formula,
+                    cudaStream_t s);
+// dense backward at lr == 0: dx [B, n_in] from dyT [n_out, B] (bit-exact order)
+void launch_backward_dx(const LayerView& L, const float* dyT, int B, float* dx, cudaStream_t s);
+// dense backward at lr != 0: fused per-synapse update + dxT [n_in, B]
+void launch_backward_update(const LayerView& L, const float* xT, const float* dyT, int B,
+                            const UpdateParams& P, float* dxT, cudaStream_t s);
+void launch_output_scale_update(const LayerView& L, const int* out_degree, const UpdateParams& P,
+                                cudaStream_t s);
+void launch_dead_rows(const LayerView& L, const float* xT, const float* dy, int B, double* scratchS,
+                      const UpdateParams& P, cudaStream_t s);
+// sparse-gradient backward: dyT/presT dense [n_out, B] with a presence mask
+void launch_backward_sparse(const LayerView& L, const float* xT, const float* dyT,
+                            const uint8_t* presT, int B, const UpdateParams& P, double* sgs,
+                            double* sgc, float* dxT, cudaStream_t s);
+void launch_sparse_scale_update(const LayerView& L, const double* sgs, const double* sgc,
+                                const UpdateParams& P, cudaStream_t s);
+// densify a row-major CSR [rows, cols] into a transposed dense [cols, rows]
+// (+ optional presence bytes); outputs must be zero-filled by the caller.
+void launch_csr_to_dense_t(const int* ptrs, const int* idx, const float* vals, int rows, int cols,
+                           float* outT, uint8_t* presT, cudaStream_t s);
+
+// structural index
+void launch_row_nnz(const int64_t* es, const int64_t* ee, int64_t n_in, int* rowptr_plus1, cudaStream_t s);
+void launch_decode_rows(const LayerView& L, int* abs_cols, int* frow, int* fvpos, int* colcount,
+                        cudaStream_t s);
+void launch_gather_csc(const int* sorted_f, const int* frow, const int* fvpos, int64_t nnz, int* crow,
+                       int* cvpos, cudaStream_t s);
+
+// state helpers
+void launch_fill_f32(float* p, int64_t n, float v, cudaStream_t s);
+void launch_fill_scale_default(float* p, int64_t begin, int64_t end, int rank, cudaStream_t s);
+void launch_recode_values(uint8_t* val, int64_t n, cudaStream_t s);
+void launch_stats(const LayerView& L, double* sums, float* maxes, cudaStream_t s);
+void launch_export(const LayerView& L, int* idx, float* w, float* imp, cudaStream_t s);
+void launch_copy_rows(const LayerView& L, const int64_t* new_bs, const int64_t* new_es, uint8_t* new_idx,
+                      uint8_t* new_val, bool recode, cudaStream_t s);
+// load_weights import (delta_csr_from_absolute): per-synapse ULEB128 length,
+// per-row byte/elem counts, and the encode/write pass.
+void launch_import_lengths(const int* ptrs, const int* idx, int n_in, int* len, cudaStream_t s);
+void launch_import_rows(const int* ptrs, const int* boff, int n_in, int64_t* row_bytes, int64_t* row_n,
+                        cudaStream_t s);
+void launch_import_write(const int* ptrs, const int* idx, const float* vals, const int* boff, int n_in,
+                         const int64_t* bs, const int64_t* es, uint8_t* ibuf, uint8_t* vbuf, cudaStream_t s);
+void launch_add_offset(int64_t* p, int64_t begin, int64_t end, int64_t delta, cudaStream_t s);
+void launch_rescale_row(const LayerView& L, int row, float old_scale, float new_scale, bool weight,
+                        cudaStream_t s);
+void launch_set_bytes(uint8_t* dst, const uint8_t* src, int64_t n, cudaStream_t s);
+void launch_fp4_quantize(const float* v, uint8_t* out, int64_t n, cudaStream_t s);
+void launch_dense_to_csr_count(const float* x, int rows, int cols, float thr, int* counts, cudaStream_t s);
+void launch_dense_to_csr_fill(const float* x, int rows, int cols, float thr, const int* ptrs, int* idx,
+                              float* vals, cudaStream_t s);
+void launch_abs_keys(const float* x, int64_t n, uint32_t* keys, int* ids, cudaStream_t s);
+void launch_topk_emit(const float* x, const int* flat_sorted, int64_t k, int cols, int* rowcount,
+                      int* idx, float* vals, cudaStream_t s);
+
+// probes (delta_csr_build_probes)
+void launch_iota(int* p, int64_t n, cudaStream_t s);
+void launch_probe_flags(const LayerView& L, const int* in_sorted, int kin, const int* out_sorted, int kout,
+                        int* flags, cudaStream_t s);
+void launch_probe_emit(const int* in_sorted, int kin, const int* out_sorted, int kout, const int* flags,
+                       const int* pos, const float* in_acc, const float* grad_acc, int* prow, int* pcol,
+                       float* pval, cudaStream_t s);
+void launch_probe_per_row(const LayerView& L, const int* in_sorted, int kin, const int* out_sorted,
+                          int64_t n_out, int k, const float* in_acc, const float* grad_acc, int* prow,
+                          int* pcol, float* pval, int* counts, cudaStream_t s);
+
+}  // namespace sili

@@ -1,0 +1,713 @@
+// Compute kernels of the FP4 delta-CSR sparse layer: forward, dense backward
+// (dx and the fused per-synapse update), sparse-gradient backward and the
+// row/column scale optimisers.
+//
+// Floating point: this file is compiled with --fmad=false; every fused
+// multiply-add below is an explicit __fmaf_rn, placed where the reference's
+// own build fuses (the CPU oracle uses the same placement and is pinned
+// bit-exact against the reference), so codes and scales match bit for bit.
+#include "common.cuh"
+#include "kernels.cuh"
+
+#include <atomic>
+#include <cmath>
+
+namespace sili {
+
+static std::atomic<long long> g_launches{0};
+void count_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+long long launch_count() { return g_launches.load(std::memory_order_relaxed); }
+
+// ── layout helpers ─────────────────────────────────────────────────────────
+__global__ void k_transpose(const float* __restrict__ in, float* __restrict__ out, int64_t R, int64_t C) {
+    __shared__ float tile[32][33];
+    const int64_t c0 = (int64_t)blockIdx.x * 32, r0 = (int64_t)blockIdx.y * 32;
+    for (int j = threadIdx.y; j < 32; j += 8) {
+        const int64_t r = r0 + j, c = c0 + threadIdx.x;
+        if (r < R && c < C) tile[j][threadIdx.x] = in[r * C + c];
+    }
+    __syncthreads();
+    for (int j = threadIdx.y; j < 32; j += 8) {
+        const int64_t c = c0 + j, r = r0 + threadIdx.x;
+        if (r < R && c < C) out[c * R + r] = tile[threadIdx.x][j];
+    }
+}
+
+void launch_transpose(const float* in, float* out, int64_t R, int64_t C, cudaStream_t s) {
+    if (R == 0 || C == 0) return;
+    dim3 grid((unsigned)((C + 31) / 32), (unsigned)((R + 31) / 32)), block(32, 8);
+    k_transpose<<<grid, block, 0, s>>>(in, out, R, C); count_launch();
+}
+
+// neuron_*_accum[j] += |x[b, j]| for b ascending (linear_disldo.hpp:515-520).
+__global__ void k_accum_abs(const float* __restrict__ x, float* __restrict__ acc, int B, int64_t n) {
+    const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= n) return;
+    float a = acc[j];
+    for (int b = 0; b < B; ++b) a = __fadd_rn(a, fabsf(x[(int64_t)b * n + j]));
+    acc[j] = a;
+}
+void launch_accum_abs(const float* x, float* acc, int B, int64_t n, cudaStream_t s) {
+    if (n == 0 || B == 0) return;
+    k_accum_abs<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(x, acc, B, n); count_launch();
+}
+
+// Same accumulation from the transposed input xT [n, B].
+__global__ void k_accum_abs_t(const float* __restrict__ xT, float* __restrict__ acc, int B, int64_t n) {
+    const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= n) return;
+    float a = acc[j];
+    const float* row = xT + j * (int64_t)B;
+    for (int b = 0; b < B; ++b) a = __fadd_rn(a, fabsf(row[b]));
+    acc[j] = a;
+}
+void launch_accum_abs_t(const float* xT, float* acc, int B, int64_t n, cudaStream_t s) {
+    if (n == 0 || B == 0) return;
+    k_accum_abs_t<<<(unsigned)((n + 127) / 128), 128, 0, s>>>(xT, acc, B, n); count_launch();
+}
+
+// neuron_grad_accum[idx] += |v| over a CSR in entry order (sisldo_ops.hpp:614-617):
+// one thread per batch row would race on shared columns, so a single warp
+// walks the entries in order (the CSR gradient is small: a top-k of dy).
+__global__ void k_accum_abs_csr(const int* __restrict__ ptrs, const int* __restrict__ idx,
+                                const float* __restrict__ vals, int rows, int ncols, float* __restrict__ acc) {
+    if (threadIdx.x != 0) return;
+    const int n = ptrs[rows];
+    for (int j = ptrs[0]; j < n; ++j) {
+        const int c = idx[j];
+        if (c >= 0 && c < ncols) acc[c] = __fadd_rn(acc[c], fabsf(vals[j]));
+    }
+}
+void launch_accum_abs_csr(const int* ptrs, const int* idx, const float* vals, int rows, int ncols, float* acc,
+                          cudaStream_t s) {
+    k_accum_abs_csr<<<1, 32, 0, s>>>(ptrs, idx, vals, rows, ncols, acc); count_launch();
+}
+
+// ── forward ────────────────────────────────────────────────────────────────
+// Output-stationary gather over the CSC shadow: one warp per output column,
+// lanes over batch samples, rows visited in ascending order.  This is the
+// reference's single-thread summation order, so y is bit-identical to
+// disldo_forward (linear_disldo.hpp:93-120: w = stored*S(r,c); y += w*x,
+// x == 0 skipped) or, with SPARSE, to sisldo_forward's (w*x)*(vs*os).
+template <int NB, bool SPARSE>
+__global__ void __launch_bounds__(256) k_forward_gather(LayerView L, const float* __restrict__ xT, int B,
+                                                        float* __restrict__ y) {
+    __shared__ float ys[8][32 * NB + 1];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t c0 = (int64_t)blockIdx.x * 8, c = c0 + warp;
+    const int b0 = blockIdx.y * 32 * NB;
+    float acc[NB];
+#pragma unroll
+    for (int t = 0; t < NB; ++t) acc[t] = 0.0f;
+    if (c < L.n_out) {
+        float osk[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) osk[k] = k < L.rank ? L.os[c * L.rank + k] : 0.0f;
+        const int k0 = L.colptr[c], k1 = L.colptr[c + 1];
+        for (int kb = k0; kb < k1; kb += 32) {
+            const int kk = kb + lane;
+            int r = 0;
+            float w = 0.0f, cs = 0.0f;
+            if (kk < k1) {
+                r = L.crow[kk];
+                const float wq = fp4_decode(L.val[L.cvpos[kk]] >> 4);
+                if (SPARSE) {
+                    w = wq;
+                    cs = __fmul_rn(L.vs[(int64_t)r * L.rank], osk[0]);
+                } else {
+                    float sc = 0.0f;
+                    for (int k = 0; k < L.rank; ++k) sc = __fmaf_rn(L.vs[(int64_t)r * L.rank + k], osk[k], sc);
+                    w = __fmul_rn(wq, sc);
+                }
+            }
+            const int n = min(32, k1 - kb);
+            for (int j = 0; j < n; ++j) {
+                const float wj = __shfl_sync(0xffffffffu, w, j);
+                const int rj = __shfl_sync(0xffffffffu, r, j);
+                const float csj = SPARSE ? __shfl_sync(0xffffffffu, cs, j) : 0.0f;
+                const float* xr = xT + (int64_t)rj * B;
+#pragma unroll
+                for (int t = 0; t < NB; ++t) {
+                    const int b = b0 + t * 32 + lane;
+                    const float xv = b < B ? __ldg(xr + b) : 0.0f;
+                    if (xv != 0.0f)
+                        acc[t] = SPARSE ? __fadd_rn(acc[t], __fmul_rn(__fmul_rn(wj, xv), csj))
+                                        : __fmaf_rn(wj, xv, acc[t]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < NB; ++t) ys[warp][t * 32 + lane] = acc[t];
+    __syncthreads();
+    for (int i = threadIdx.x; i < 8 * 32 * NB; i += 256) {
+        const int w = i & 7, bl = i >> 3;
+        const int b = b0 + bl;
+        const int64_t cc = c0 + w;
+        if (b < B && cc < L.n_out) y[(int64_t)b * L.n_out + cc] = ys[w][bl];
+    }
+}
+
+// Small batches: lanes over a column's synapses, per-lane partial sums over
+// the batch, then a fixed warp tree (deterministic; not the reference's
+// sequential order, so equal to it within fp32 rounding).
+template <int BMAX, bool SPARSE>
+__global__ void __launch_bounds__(256) k_forward_small(LayerView L, const float* __restrict__ xT, int B,
+                                                       float* __restrict__ y) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t c = (int64_t)blockIdx.x * 8 + warp;
+    if (c >= L.n_out) return;
+    float osk[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) osk[k] = k < L.rank ? L.os[c * L.rank + k] : 0.0f;
+    float acc[BMAX];
+#pragma unroll
+    for (int b = 0; b < BMAX; ++b) acc[b] = 0.0f;
+    const int k0 = L.colptr[c], k1 = L.colptr[c + 1];
+    for (int kk = k0 + lane; kk < k1; kk += 32) {
+        const int r = L.crow[kk];
+        const float wq = fp4_decode(L.val[L.cvpos[kk]] >> 4);
+        float w, cs = 0.0f;
+        if (SPARSE) {
+            w = wq;
+            cs = __fmul_rn(L.vs[(int64_t)r * L.rank], osk[0]);
+        } else {
+            float sc = 0.0f;
+            for (int k = 0; k < L.rank; ++k) sc = __fmaf_rn(L.vs[(int64_t)r * L.rank + k], osk[k], sc);
+            w = __fmul_rn(wq, sc);
+        }
+        const float* xr = xT + (int64_t)r * B;
+#pragma unroll
+        for (int b = 0; b < BMAX; ++b) {
+            if (b < B) {
+                const float xv = __ldg(xr + b);
+                if (xv != 0.0f)
+                    acc[b] = SPARSE ? __fadd_rn(acc[b], __fmul_rn(__fmul_rn(w, xv), cs)) : __fmaf_rn(w, xv, acc[b]);
+            }
+        }
+    }
+#pragma unroll
+    for (int b = 0; b < BMAX; ++b) {
+        if (b < B) {
+            const float v = warp_sum(acc[b]);
+            if (lane == 0) y[(int64_t)b * L.n_out + c] = v;
+        }
+    }
+}
+
+void launch_forward(const LayerView& L, const float* xT, int B, float* y, bool sparse, cudaStream_t s) {
+    if (L.n_out == 0 || B == 0) return;
+    const unsigned gx = (unsigned)((L.n_out + 7) / 8);
+    if (B <= 8) {
+        if (sparse) k_forward_small<8, true><<<gx, 256, 0, s>>>(L, xT, B, y);
+        else k_forward_small<8, false><<<gx, 256, 0, s>>>(L, xT, B, y);
+        count_launch();
+        return;
+    }
+    if (B <= 32) {
+        dim3 g(gx, 1);
+        if (sparse) k_forward_gather<1, true><<<g, 256, 0, s>>>(L, xT, B, y);
+        else k_forward_gather<1, false><<<g, 256, 0, s>>>(L, xT, B, y);
+    } else {
+        dim3 g(gx, (unsigned)((B + 63) / 64));
+        if (sparse) k_forward_gather<2, true><<<g, 256, 0, s>>>(L, xT, B, y);
+        else k_forward_gather<2, false><<<g, 256, 0, s>>>(L, xT, B, y);
+    }
+    count_launch();
+}
+
+// ── dense backward, learning_rate == 0 ─────────────────────────────────────
+// dx[b, r] = sum over the row's synapses, in stored order, of
+// fma(w*S(r,c), dy[b,c], .) -- linear_disldo.hpp:884 with cw = quant*S and no
+// update.  Lanes over batch samples, so the sum order is the reference's.
+template <int NB>
+__global__ void __launch_bounds__(256) k_backward_dx(LayerView L, const float* __restrict__ dyT, int B,
+                                                     float* __restrict__ dx) {
+    __shared__ float xs[8][32 * NB + 1];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t r0 = (int64_t)blockIdx.x * 8, r = r0 + warp;
+    const int b0 = blockIdx.y * 32 * NB;
+    float acc[NB];
+#pragma unroll
+    for (int t = 0; t < NB; ++t) acc[t] = 0.0f;
+    if (r < L.n_in) {
+        const int64_t es = L.es[r];
+        const int nnz = (int)(L.ee[r] - es);
+        const int f0 = L.rowptr[r];
+        float vsk[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) vsk[k] = k < L.rank ? L.vs[r * L.rank + k] : 0.0f;
+        for (int eb = 0; eb < nnz; eb += 32) {
+            const int e = eb + lane;
+            int c = 0;
+            float cw = 0.0f;
+            if (e < nnz) {
+                c = L.abs_cols[f0 + e];
+                const float wq = fp4_decode(L.val[es + e] >> 4);
+                float sc = 0.0f;
+                for (int k = 0; k < L.rank; ++k) sc = __fmaf_rn(vsk[k], L.os[(int64_t)c * L.rank + k], sc);
+                cw = __fmul_rn(wq, sc);
+            }
+            const int n = min(32, nnz - eb);
+            for (int j = 0; j < n; ++j) {
+                const float cwj = __shfl_sync(0xffffffffu, cw, j);
+                const int cj = __shfl_sync(0xffffffffu, c, j);
+                const float* dr = dyT + (int64_t)cj * B;
+#pragma unroll
+                for (int t = 0; t < NB; ++t) {
+                    const int b = b0 + t * 32 + lane;
+                    if (b < B) acc[t] = __fmaf_rn(cwj, __ldg(dr + b), acc[t]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < NB; ++t) xs[warp][t * 32 + lane] = acc[t];
+    __syncthreads();
+    for (int i = threadIdx.x; i < 8 * 32 * NB; i += 256) {
+        const int w = i & 7, bl = i >> 3;
+        const int b = b0 + bl;
+        const int64_t rr = r0 + w;
+        if (b < B && rr < L.n_in) dx[(int64_t)b * L.n_in + rr] = xs[w][bl];
+    }
+}
+
+void launch_backward_dx(const LayerView& L, const float* dyT, int B, float* dx, cudaStream_t s) {
+    if (L.n_in == 0 || B == 0) return;
+    const unsigned gx = (unsigned)((L.n_in + 7) / 8);
+    if (B <= 32) {
+        k_backward_dx<1><<<dim3(gx, 1), 256, 0, s>>>(L, dyT, B, dx); count_launch();
+    } else {
+        k_backward_dx<2><<<dim3(gx, (unsigned)((B + 63) / 64)), 256, 0, s>>>(L, dyT, B, dx); count_launch();
+    }
+}
+
+// ── scale optimiser (RMSpropScalePolicy::update, delta_csr_types.hpp:445-466) ──
+__device__ __forceinline__ float bias_pow(const UpdateParams& P, uint32_t step) {
+    if ((int)step < P.pow_n) return P.pow_tab[step];
+    return powf(P.beta2, (float)step);   // beyond the table powf(beta2, s) < 2^-25: 1 - p == 1
+}
+
+__device__ __forceinline__ void rmsprop_scale(float* scale, float* state, float g, float lr, float c,
+                                              uint32_t* step, const UpdateParams& P) {
+    if (!isfinite(g) || !isfinite(c)) return;
+    const float onem = __fsub_rn(1.0f, P.beta2);
+    const float ns = __fmaf_rn(P.beta2, *state, __fmul_rn(onem, __fmaf_rn(g, g, __fmul_rn(c, c))));
+    if (!isfinite(ns)) return;
+    float hat = ns;
+    const uint32_t st = *step + 1u;
+    *step = st;
+    const float bc = __fsub_rn(1.0f, bias_pow(P, st));
+    if (bc > 0.0f) hat = __fdiv_rn(ns, bc);
+    if (!isfinite(hat)) return;
+    const float nsc = __fsub_rn(*scale, __fdiv_rn(__fmul_rn(lr, g), __fadd_rn(__fsqrt_rn(hat), P.eps)));
+    if (!isfinite(nsc)) return;
+    *state = ns;
+    *scale = nsc;
+}
+
+// BoundedRMSpropSynapsePolicy::update_ci (delta_csr_types.hpp:707-713) at the
+// production arguments min_decay_frac = 0, max_ci = 100 (cpu_backend.cpp:518-525).
+__device__ __forceinline__ float bounded_ci(float ci, float g, float contrib, float beta2, float onem) {
+    const float ema = __fmaf_rn(beta2, ci, __fmul_rn(onem, __fmaf_rn(g, g, __fmul_rn(contrib, contrib))));
+    const float fl = __fmul_rn(0.0f, ci);
+    float r = (ema < fl) ? fl : ema;
+    return (100.0f < r) ? 100.0f : r;
+}
+
+// ── dense backward, learning_rate != 0: the fused update ───────────────────
+// disldo_backward's scattered non-deferred path (linear_disldo.hpp:625-925).
+// One warp per input row; lanes own synapses (32 at a time); each lane runs
+// its synapse's recurrence over the batch IN ORDER -- ci, quant and cw evolve
+// per sample and dx uses the post-update weight of that sample -- exactly as
+// the reference.  Samples with x == 0 take the closed form of the same
+// arithmetic (g = contrib = 0: ci <- min(max(fma(b2, ci, (1-b2)*0), 0*ci), 100),
+// quant unchanged), which is bit-identical to evaluating the full update.
+// dx partials of the 32 lanes are combined per sample by a butterfly
+// transpose-reduction into dxT[r, b] (fixed order, fp32 tolerance vs the
+// reference's sequential sum).  The row's value_scale is updated at the end
+// by lane 0 from double sums, as in the reference.
+template <bool STOCH, int RANK>
+__global__ void __launch_bounds__(256) k_backward_update(LayerView L, const float* __restrict__ xT,
+                                                         const float* __restrict__ dyT, int B,
+                                                         UpdateParams P, float* __restrict__ dxT) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t r = (int64_t)blockIdx.x * 8 + warp;
+    if (r >= L.n_in) return;
+    const int64_t es = L.es[r];
+    const int nnz = (int)(L.ee[r] - es);
+    float* dxr = dxT + r * (int64_t)B;
+    if (nnz == 0) {
+        for (int b = lane; b < B; b += 32) dxr[b] = 0.0f;
+        return;
+    }
+    constexpr int rank = RANK;
+    const int f0 = L.rowptr[r];
+    const float eff_lr = P.lr_per_row_nnz ? __fdiv_rn(P.lr, (float)nnz) : P.lr;
+    const float scale_eff_lr = __fdiv_rn(P.lr, (float)nnz);
+    const float onem = __fsub_rn(1.0f, P.beta2);
+    const float zterm = __fmul_rn(onem, 0.0f);
+    const bool fast_ok = !P.damp || P.eps > 0.0f;
+    const float imp_scale = L.is[r];
+    float vsr[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) vsr[k] = k < RANK ? L.vs[r * RANK + k] : 0.0f;
+    const float* xr = xT + r * (int64_t)B;
+
+    double sgs[4] = {0.0, 0.0, 0.0, 0.0}, sgc[4] = {0.0, 0.0, 0.0, 0.0};
+    double sa_new = 0.0, sa_old = 0.0, sq_new = 0.0, sq_old = 0.0;
+    float mx_new = 0.0f;
+
+    for (int e0 = 0; e0 < nnz; e0 += 32) {
+        const int e = e0 + lane;
+        const bool valid = e < nnz;
+        int c = 0;
+        uint8_t byte = 0;
+        if (valid) {
+            c = L.abs_cols[f0 + e];
+            byte = L.val[es + e];
+        }
+        const float cw_orig = fp4_decode(byte >> 4), ci_orig = fp4_decode(byte & 15u);
+        float osk[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) osk[k] = (valid && k < rank) ? L.os[(int64_t)c * rank + k] : 0.0f;
+        const float cis = valid ? __fmul_rn(imp_scale, L.ois[c]) : 1.0f;
+        float S = 0.0f;
+        #pragma unroll
+        for (int k = 0; k < RANK; ++k) S = __fmaf_rn(vsr[k], osk[k], S);
+        float ci = __fmul_rn(ci_orig, cis);
+        float quant = cw_orig;
+        float cw = __fmul_rn(quant, S);
+        const bool lane_ok = isfinite(S) && fast_ok;
+        float cg[4] = {0.f, 0.f, 0.f, 0.f}, cc[4] = {0.f, 0.f, 0.f, 0.f};
+        const float* dyc = dyT + (int64_t)c * B;
+
+        for (int t0 = 0; t0 < B; t0 += 32) {
+            const int nb = min(32, B - t0);
+            const float xl = (lane < nb) ? __ldg(xr + t0 + lane) : 0.0f;
+            const unsigned act = __ballot_sync(0xffffffffu, xl != 0.0f);
+            float p[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                p[j] = 0.0f;
+                if (j < nb) {
+                    const float iv = __shfl_sync(0xffffffffu, xl, j);
+                    if (valid) {
+                        const float dyv = __ldg(dyc + t0 + j);
+                        const bool fast = !((act >> j) & 1u) && lane_ok && isfinite(dyv) && ci >= 0.0f;
+                        if (fast) {
+                            const float ema = __fmaf_rn(P.beta2, ci, zterm);
+                            const float fl = __fmul_rn(0.0f, ci);
+                            float rr = (ema < fl) ? fl : ema;
+                            ci = (100.0f < rr) ? 100.0f : rr;
+                        } else {
+                            const float g = __fmul_rn(dyv, iv);
+                            const float contrib = __fmul_rn(iv, cw_orig);
+                            ci = bounded_ci(ci, g, contrib, P.beta2, onem);
+                            const float ngS = __fmul_rn(-g, S);
+                            float raw = P.damp ? __fdiv_rn(ngS, __fadd_rn(__fsqrt_rn(ci), P.eps)) : ngS;
+                            if (raw > 2.0f) raw = 2.0f;
+                            if (raw < -2.0f) raw = -2.0f;
+                            quant = __fmaf_rn(eff_lr, raw, quant);
+                            cw = __fmul_rn(quant, S);
+                            const float qf = (quant == 0.0f) ? 0.1f : quant;
+#pragma unroll
+                            for (int k = 0; k < RANK; ++k) {
+                                const double qo = (double)qf * (double)osk[k];
+                                sgs[k] = __fma_rn(qo, (double)g, sgs[k]);
+                                sgc[k] = __fma_rn(qo, (double)contrib, sgc[k]);
+                                if (P.os_trainable) {
+                                    const float qv = __fmul_rn(qf, vsr[k]);
+                                    cg[k] = __fmaf_rn(qv, g, cg[k]);
+                                    cc[k] = __fmaf_rn(qv, contrib, cc[k]);
+                                }
+                            }
+                        }
+                        p[j] = __fmul_rn(cw, dyv);
+                    }
+                }
+            }
+            // butterfly transpose-reduction: lane j ends with sum over lanes of p[j]
+#pragma unroll
+            for (int o = 16, h = 16; o > 0; o >>= 1, h >>= 1) {
+                const bool up = (lane & o) != 0;
+#pragma unroll
+                for (int i = 0; i < h; ++i) {
+                    const float send = up ? p[i] : p[i + h];
+                    const float keep = up ? p[i + h] : p[i];
+                    p[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, o));
+                }
+            }
+            if (lane < nb) {
+                float* d = dxr + t0 + lane;
+                *d = (e0 == 0) ? p[0] : __fadd_rn(*d, p[0]);
+            }
+        }
+        if (valid) {
+            const float imp_st = __fdiv_rn(ci, cis);
+            uint32_t nbyte;
+            if (STOCH) {
+                const uint64_t vp = (uint64_t)(es + e);
+                nbyte = (fp4_quantize_stochastic(quant, rng_draw(P.call_key, vp, 0)) << 4) |
+                        fp4_quantize_stochastic(imp_st, rng_draw(P.call_key, vp, 1));
+            } else {
+                nbyte = (fp4_encode(quant) << 4) | fp4_encode(imp_st);
+            }
+            L.val[es + e] = (uint8_t)nbyte;
+            const float ai = fp4_decode(nbyte & 15u);
+            sa_new += fabs((double)ai);
+            sa_old += fabs((double)ci_orig);
+            sq_new += (double)ai * (double)ai;
+            sq_old += (double)ci_orig * (double)ci_orig;
+            mx_new = fmaxf(mx_new, fabsf(ai));
+            if (P.os_trainable) {
+#pragma unroll
+                for (int k = 0; k < RANK; ++k) {
+                    atomicAdd(P.colg + (int64_t)c * rank + k, cg[k]);
+                    atomicAdd(P.colc + (int64_t)c * rank + k, cc[k]);
+                }
+            }
+        }
+    }
+    // value_scale update (linear_disldo.hpp:901-925)
+#pragma unroll
+    for (int k = 0; k < RANK; ++k) {
+        sgs[k] = warp_sum(sgs[k]);
+        sgc[k] = warp_sum(sgc[k]);
+    }
+    if (lane == 0) {
+#pragma unroll
+        for (int k = 0; k < RANK; ++k) {
+            const int64_t i = r * rank + k;
+            rmsprop_scale(L.vs + i, L.vsi + i, (float)sgs[k], scale_eff_lr, (float)sgc[k], L.vstep + i, P);
+        }
+    }
+    sa_new = warp_sum(sa_new); sa_old = warp_sum(sa_old);
+    sq_new = warp_sum(sq_new); sq_old = warp_sum(sq_old);
+    for (int o = 16; o > 0; o >>= 1) mx_new = fmaxf(mx_new, __shfl_xor_sync(0xffffffffu, mx_new, o));
+    if (lane == 0) {
+        atomicAdd(P.stats + 0, sa_new - sa_old);
+        atomicAdd(P.stats + 1, sq_new - sq_old);
+        atomicMax(reinterpret_cast<unsigned int*>(P.stat_max), __float_as_uint(mx_new));
+    }
+}
+
+void launch_backward_update(const LayerView& L, const float* xT, const float* dyT, int B,
+                            const UpdateParams& P, float* dxT, cudaStream_t s) {
+    if (L.n_in == 0) return;
+    const unsigned g = (unsigned)((L.n_in + 7) / 8);
+#define SILI_BWD(R)                                                                         \
+    if (P.stochastic) k_backward_update<true, R><<<g, 256, 0, s>>>(L, xT, dyT, B, P, dxT);  \
+    else k_backward_update<false, R><<<g, 256, 0, s>>>(L, xT, dyT, B, P, dxT);
+    switch (L.rank) {
+    case 1: SILI_BWD(1) break;
+    case 2: SILI_BWD(2) break;
+    case 3: SILI_BWD(3) break;
+    default: SILI_BWD(4) break;
+    }
+#undef SILI_BWD
+    count_launch();
+}
+
+// output_scale update, linear_disldo.hpp:2051-2080
+__global__ void k_output_scale_update(LayerView L, const int* __restrict__ out_degree, UpdateParams P) {
+    const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= L.n_out) return;
+    const int deg = out_degree[c];
+    if (deg == 0) return;
+    const float col_lr = __fdiv_rn(P.lr, (float)deg);
+    for (int k = 0; k < L.rank; ++k) {
+        const int64_t i = c * L.rank + k;
+        rmsprop_scale(L.os + i, L.osi + i, P.colg[i], col_lr, P.colc[i], L.ostep + i, P);
+    }
+}
+void launch_output_scale_update(const LayerView& L, const int* out_degree, const UpdateParams& P,
+                                cudaStream_t s) {
+    if (L.n_out == 0) return;
+    k_output_scale_update<<<(unsigned)((L.n_out + 255) / 256), 256, 0, s>>>(L, out_degree, P); count_launch();
+}
+
+// Dead-row bootstrap, linear_disldo.hpp:1985-2042: S[b,k] = sum_c os[c,k]*dy[b,c]
+// in double, then an Adam step on value_scale of every row with no synapse.
+__global__ void k_dead_S(LayerView L, const float* __restrict__ dy, int B, double* __restrict__ S) {
+    const int b = blockIdx.x, k = blockIdx.y;
+    double s = 0.0;
+    for (int64_t c = threadIdx.x; c < L.n_out; c += blockDim.x)
+        s = __fma_rn((double)L.os[c * L.rank + k], (double)dy[(int64_t)b * L.n_out + c], s);
+    __shared__ double red[8];
+    s = warp_sum(s);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += red[i];
+        S[(int64_t)b * L.rank + k] = t;
+    }
+}
+__global__ void k_dead_rows(LayerView L, const float* __restrict__ xT, int B, const double* __restrict__ S,
+                            UpdateParams P) {
+    const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= L.n_in) return;
+    if (L.ee[r] != L.es[r]) return;
+    const float dead_lr = __fdiv_rn(P.lr, (float)L.n_out);
+    const float onem = __fsub_rn(1.0f, P.beta2);
+    for (int k = 0; k < L.rank; ++k) {
+        double sum = 0.0;
+        for (int b = 0; b < B; ++b) {
+            const float iv = xT[r * B + b];
+            if (iv == 0.0f) continue;
+            sum = __fma_rn((double)iv, S[(int64_t)b * L.rank + k], sum);
+        }
+        if (sum == 0.0) continue;
+        const float g = (float)sum;
+        if (!isfinite(g)) continue;
+        const int64_t i = r * L.rank + k;
+        const float m = L.vsm[i], v = L.vsi[i];
+        const float nm = __fmaf_rn(0.9f, m, __fmul_rn(__fsub_rn(1.0f, 0.9f), g));
+        const float nv = __fmaf_rn(P.beta2, v, __fmul_rn(onem, __fmul_rn(g, g)));
+        if (!isfinite(nm) || !isfinite(nv)) continue;
+        const float nvs = __fsub_rn(L.vs[i], __fdiv_rn(__fmul_rn(dead_lr, nm), __fadd_rn(__fsqrt_rn(nv), P.eps)));
+        if (!isfinite(nvs)) continue;
+        L.vsm[i] = nm;
+        L.vsi[i] = nv;
+        L.vs[i] = nvs;
+    }
+}
+void launch_dead_rows(const LayerView& L, const float* xT, const float* dy, int B, double* S,
+                      const UpdateParams& P, cudaStream_t s) {
+    if (L.n_in == 0 || B == 0) return;
+    k_dead_S<<<dim3((unsigned)B, (unsigned)L.rank), 256, 0, s>>>(L, dy, B, S); count_launch();
+    k_dead_rows<<<(unsigned)((L.n_in + 127) / 128), 128, 0, s>>>(L, xT, B, S, P); count_launch();
+}
+
+// ── sparse-gradient backward (disldo_backward_sparse_grad, sisldo_ops.hpp:589-799) ──
+// One warp per row, batch samples in order (each sample requantizes the
+// row's codes before the next reads them), lanes over the row's synapses.
+// A synapse takes part in sample b only if dy's CSR holds an entry at its
+// column (presT), whatever that entry's value.
+__global__ void __launch_bounds__(256) k_backward_sparse(LayerView L, const float* __restrict__ xT,
+                                                         const float* __restrict__ dyT,
+                                                         const uint8_t* __restrict__ presT, int B,
+                                                         UpdateParams P, double* __restrict__ sgs_out,
+                                                         double* __restrict__ sgc_out, float* __restrict__ dxT) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t r = (int64_t)blockIdx.x * 8 + warp;
+    if (r >= L.n_in) return;
+    const int64_t es = L.es[r];
+    const int nnz = (int)(L.ee[r] - es);
+    float* dxr = dxT + r * (int64_t)B;
+    if (nnz == 0) {
+        for (int b = lane; b < B; b += 32) dxr[b] = 0.0f;
+        return;
+    }
+    const int f0 = L.rowptr[r];
+    const float eff_lr = P.lr_per_row_nnz ? __fdiv_rn(P.lr, (float)nnz) : P.lr;
+    const float onem = __fsub_rn(1.0f, P.beta2);
+    const float imp_scale = L.is[r];
+    const float val_scale = L.vs[r * L.rank];
+    double sgs = 0.0, sgc = 0.0, sa_new = 0.0, sa_old = 0.0, sq_new = 0.0, sq_old = 0.0;
+    float mx_new = 0.0f;
+    for (int b = 0; b < B; ++b) {
+        const float in_val = xT[r * B + b];
+        float dxa = 0.0f;
+        for (int e0 = 0; e0 < nnz; e0 += 32) {
+            const int e = e0 + lane;
+            if (e >= nnz) continue;
+            const int c = L.abs_cols[f0 + e];
+            if (!presT[(int64_t)c * B + b]) continue;
+            const uint8_t byte = L.val[es + e];
+            const float w_stored = fp4_decode(byte >> 4);
+            const float out_scale = L.os[(int64_t)c * L.rank];
+            const float cs = __fmul_rn(val_scale, out_scale);
+            const float w = __fmul_rn(w_stored, cs);
+            const float dyv = dyT[(int64_t)c * B + b];
+            dxa = __fmaf_rn(w, dyv, dxa);
+            if (P.lr != 0.0f) {
+                const float cis = __fmul_rn(imp_scale, L.ois[c]);
+                const float grad = __fmul_rn(dyv, in_val);
+                const float stored_imp = fp4_decode(byte & 15u);
+                float imp = __fmul_rn(stored_imp, cis);
+                const float contrib = __fmul_rn(in_val, w);
+                imp = __fmaf_rn(P.beta2, imp, __fmul_rn(onem, __fmaf_rn(grad, grad, __fmul_rn(contrib, contrib))));
+                const float num = __fmul_rn(-eff_lr, grad);
+                const float step = P.damp ? __fdiv_rn(num, __fadd_rn(__fsqrt_rn(imp), P.eps)) : num;
+                const float new_w = __fadd_rn(w, step);
+                const uint32_t nbyte = (fp4_encode(__fdiv_rn(new_w, cs)) << 4) | fp4_encode(__fdiv_rn(imp, cis));
+                L.val[es + e] = (uint8_t)nbyte;
+                const float ai = fp4_decode(nbyte & 15u);
+                sa_new += fabs((double)ai); sa_old += fabs((double)stored_imp);
+                sq_new += (double)ai * (double)ai; sq_old += (double)stored_imp * (double)stored_imp;
+                mx_new = fmaxf(mx_new, fabsf(ai));
+                sgs += (double)w_stored * (double)out_scale * (double)grad;
+                sgc += (double)w_stored * (double)out_scale * (double)contrib;
+            }
+        }
+        dxa = warp_sum(dxa);
+        if (lane == 0) dxr[b] = dxa;
+        __syncwarp();
+    }
+    sgs = warp_sum(sgs); sgc = warp_sum(sgc);
+    sa_new = warp_sum(sa_new); sa_old = warp_sum(sa_old);
+    sq_new = warp_sum(sq_new); sq_old = warp_sum(sq_old);
+    for (int o = 16; o > 0; o >>= 1) mx_new = fmaxf(mx_new, __shfl_xor_sync(0xffffffffu, mx_new, o));
+    if (lane == 0) {
+        sgs_out[r] = sgs;
+        sgc_out[r] = sgc;
+        if (P.lr != 0.0f) {
+            atomicAdd(P.stats + 0, sa_new - sa_old);
+            atomicAdd(P.stats + 1, sq_new - sq_old);
+            atomicMax(reinterpret_cast<unsigned int*>(P.stat_max), __float_as_uint(mx_new));
+        }
+    }
+}
+void launch_backward_sparse(const LayerView& L, const float* xT, const float* dyT, const uint8_t* presT, int B,
+                            const UpdateParams& P, double* sgs, double* sgc, float* dxT, cudaStream_t s) {
+    if (L.n_in == 0) return;
+    k_backward_sparse<<<(unsigned)((L.n_in + 7) / 8), 256, 0, s>>>(L, xT, dyT, presT, B, P, sgs, sgc, dxT); count_launch();
+}
+
+// value_scale after all samples, sisldo_ops.hpp:772-797 (no finiteness guards there).
+__global__ void k_sparse_scale_update(LayerView L, const double* __restrict__ sgs, const double* __restrict__ sgc,
+                                      UpdateParams P) {
+    const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= L.n_in) return;
+    if (sgs[r] == 0.0 && sgc[r] == 0.0) return;
+    const int64_t nnz = L.ee[r] - L.es[r];
+    if (nnz == 0) return;
+    const float se = __fdiv_rn(P.lr, (float)nnz);
+    const float g = (float)sgs[r], cg = (float)sgc[r];
+    const float onem = __fsub_rn(1.0f, P.beta2);
+    const float nv = __fmaf_rn(P.beta2, L.vsi[r], __fmul_rn(onem, __fmaf_rn(g, g, __fmul_rn(cg, cg))));
+    const uint32_t st = L.vstep[r * L.rank] + 1u;
+    L.vstep[r * L.rank] = st;
+    const float bc = __fsub_rn(1.0f, bias_pow(P, st));
+    const float hat = bc > 0.0f ? __fdiv_rn(nv, bc) : nv;
+    L.vsi[r] = nv;
+    L.vs[r] = __fsub_rn(L.vs[r], __fdiv_rn(__fmul_rn(se, g), __fadd_rn(__fsqrt_rn(hat), P.eps)));
+}
+void launch_sparse_scale_update(const LayerView& L, const double* sgs, const double* sgc, const UpdateParams& P,
+                                cudaStream_t s) {
+    if (L.n_in == 0) return;
+    k_sparse_scale_update<<<(unsigned)((L.n_in + 255) / 256), 256, 0, s>>>(L, sgs, sgc, P); count_launch();
+}
+
+__global__ void k_csr_to_dense_t(const int* __restrict__ ptrs, const int* __restrict__ idx,
+                                 const float* __restrict__ vals, int rows, int cols, float* __restrict__ outT,
+                                 uint8_t* __restrict__ presT) {
+    const int b = blockIdx.x;
+    if (b >= rows) return;
+    for (int j = ptrs[b] + threadIdx.x; j < ptrs[b + 1]; j += blockDim.x) {
+        const int c = idx[j];
+        if (c < 0 || c >= cols) continue;   // out-of-range entries are rejected on the host for host input
+        const int64_t o = (int64_t)c * rows + b;
+        outT[o] = vals[j];
+        if (presT) presT[o] = 1;
+    }
+}
+void launch_csr_to_dense_t(const int* ptrs, const int* idx, const float* vals, int rows, int cols, float* outT,
+                           uint8_t* presT, cudaStream_t s) {
+    if (rows == 0) return;
+    k_csr_to_dense_t<<<(unsigned)rows, 128, 0, s>>>(ptrs, idx, vals, rows, cols, outT, presT); count_launch();
+}
+
+}  // namespace sili

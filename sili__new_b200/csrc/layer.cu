@@ -1,0 +1,1455 @@
+// Host side of sili_b200: per-layer device state and the C ABI declared in
+// include/sili_b200.h.  Mirrors sili._cpu.SparseLinearLayerImpl
+// (sili/cpu_backend.cpp:349-1013); every compute path runs CUDA kernels.
+#include "../../include/sili_b200.h"
+#include "common.cuh"
+#include "kernels.cuh"
+
+#include <cub/cub.cuh>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <string>
+#include <vector>
+
+using namespace sili;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const std::string& msg) {
+    g_err = msg;
+    return code;
+}
+
+#define CK(x)                                                                                   \
+    do {                                                                                        \
+        cudaError_t e_ = (x);                                                                   \
+        if (e_ != cudaSuccess) return fail(SILI_ECUDA, std::string(#x) + ": " + cudaGetErrorString(e_)); \
+    } while (0)
+#define RC(x)                   \
+    do {                        \
+        int r_ = (x);           \
+        if (r_) return r_;      \
+    } while (0)
+
+// Grow-only device buffer.
+template <typename T>
+struct DBuf {
+    T* p = nullptr;
+    int64_t cap = 0;
+    DBuf() = default;
+    DBuf(const DBuf&) = delete;
+    DBuf& operator=(const DBuf&) = delete;
+    ~DBuf() { if (p) cudaFree(p); }
+    int reserve(int64_t n) {            // contents not preserved
+        if (n <= cap) return SILI_OK;
+        if (p) cudaFree(p);
+        p = nullptr;
+        cap = 0;
+        const int64_t want = std::max<int64_t>(n, 1);
+        cudaError_t e = cudaMalloc((void**)&p, (size_t)want * sizeof(T));
+        if (e != cudaSuccess) return fail(SILI_ECUDA, std::string("cudaMalloc: ") + cudaGetErrorString(e));
+        cap = want;
+        return SILI_OK;
+    }
+    int grow(int64_t n, int64_t keep, cudaStream_t s) {   // preserves [0, keep)
+        if (n <= cap) return SILI_OK;
+        T* q = nullptr;
+        const int64_t want = std::max<int64_t>(n, cap + cap / 2);
+        cudaError_t e = cudaMalloc((void**)&q, (size_t)want * sizeof(T));
+        if (e != cudaSuccess) return fail(SILI_ECUDA, std::string("cudaMalloc: ") + cudaGetErrorString(e));
+        if (p && keep > 0) {
+            e = cudaMemcpyAsync(q, p, (size_t)keep * sizeof(T), cudaMemcpyDeviceToDevice, s);
+            if (e != cudaSuccess) return fail(SILI_ECUDA, cudaGetErrorString(e));
+            cudaStreamSynchronize(s);
+        }
+        if (p) cudaFree(p);
+        p = q;
+        cap = want;
+        return SILI_OK;
+    }
+    void swap(DBuf& o) { std::swap(p, o.p); std::swap(cap, o.cap); }
+};
+
+bool is_device_ptr(const void* ptr) {
+    if (!ptr) return false;
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, ptr) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+}  // namespace
+
+struct sili_layer {
+    int dev = 0;
+    cudaStream_t stream = nullptr;
+    int64_t rows = 0, cols = 0;
+    int rank = 1;
+    bool stochastic = true;
+    uint64_t seed = 0x5EEDu, call = 0;
+    // delta-CSR (DeltaCSRWeights, delta_csr_types.hpp:898-939)
+    DBuf<uint8_t> idx, val;
+    int64_t idx_n = 0, val_n = 0;
+    DBuf<int64_t> bs, be, es, ee;
+    int64_t total_nnz = 0;
+    int64_t max_idx_bytes = INT64_MAX, max_val_bytes = INT64_MAX;
+    int64_t idx_budget = 4096, val_budget = 64;
+    // scales (SparseLinearWeightsDelta, delta_csr_types.hpp:1004-1240).  The
+    // device arrays are full size and hold the reference's default read value
+    // where the reference's lazily-sized vector has no entry yet; n_vs / n_os
+    // track that vector's logical size, because growing it fills with 1.0 even
+    // at components k >= 1 (set_value_scale_raw_k, :1105-1110).
+    DBuf<float> vs, os, vsi, osi, vsm, is, ois;
+    DBuf<uint32_t> vstep, ostep;
+    int64_t n_vs = 0, n_os = 0;
+    bool os_trainable = false;
+    DBuf<float> in_acc, grad_acc;
+    DBuf<int> out_degree;
+    DBuf<int> prow, pcol;
+    DBuf<float> pval;
+    int64_t n_probes = 0;
+    // running stats (delta_csr_types.hpp:1265-1281)
+    double st[4] = {0, 0, 0, 0};   // value_l1, value_l2_sq, importance_l1, importance_l2_sq
+    float st_vmax = 0.f, st_imax = 0.f, max_abs_decay = 1.f;
+    DBuf<double> d_st;             // pending importance l1/l2 deltas
+    DBuf<float> d_stmax;
+    bool st_pending = false;
+    // derived index
+    bool aux_dirty = true;
+    DBuf<int> rowptr, abs_cols, frow, fvpos, colcount, colptr, crow, cvpos, sort_k, sort_ko, sort_v, sort_vo;
+    DBuf<uint8_t> cub_tmp;
+    // scratch
+    DBuf<float> xT, dyT, dxT, colg, colc, ytmp, x_stage, dy_stage, dx_stage;
+    bool has_dead_rows = false;
+    DBuf<uint8_t> presT;
+    DBuf<double> dS, sgs, sgc;
+    DBuf<int> i_tmp0, i_tmp1, i_tmp2;
+    DBuf<float> f_tmp0;
+    int last_batch = 0;
+    DBuf<float> pow_tab;
+    float pow_beta2 = NAN;
+    int pow_n = 0;
+    // optional CUDA-event timing of the main forward / backward kernels
+    bool timing = false;
+    cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
+    bool ev_fwd = false, ev_bwd = false;
+
+    LayerView view() const {
+        LayerView v;
+        v.n_in = rows; v.n_out = cols; v.rank = rank;
+        v.bs = bs.p; v.be = be.p; v.es = es.p; v.ee = ee.p;
+        v.idx = idx.p; v.val = val.p;
+        v.vs = vs.p; v.os = os.p; v.vsi = vsi.p; v.osi = osi.p; v.vsm = vsm.p;
+        v.vstep = vstep.p; v.ostep = ostep.p; v.is = is.p; v.ois = ois.p;
+        v.rowptr = rowptr.p; v.abs_cols = abs_cols.p; v.colptr = colptr.p; v.crow = crow.p; v.cvpos = cvpos.p;
+        return v;
+    }
+};
+
+namespace {
+
+int use(sili_layer* h) {
+    if (!h) return fail(SILI_EINVAL, "null layer handle");
+    CK(cudaSetDevice(h->dev));
+    return SILI_OK;
+}
+
+cudaStream_t pick(sili_layer* h, void* stream) { return stream ? (cudaStream_t)stream : h->stream; }
+
+// ── cub helpers ─────────────────────────────────────────────────────────────
+int scan_excl_int(sili_layer* h, const int* in, int* out, int64_t n, cudaStream_t s) {
+    size_t bytes = 0;
+    cub::DeviceScan::ExclusiveSum(nullptr, bytes, in, out, (int)n, s);
+    RC(h->cub_tmp.reserve((int64_t)bytes + 1));
+    CK(cub::DeviceScan::ExclusiveSum(h->cub_tmp.p, bytes, in, out, (int)n, s));
+    return SILI_OK;
+}
+int scan_incl_int(sili_layer* h, const int* in, int* out, int64_t n, cudaStream_t s) {
+    size_t bytes = 0;
+    cub::DeviceScan::InclusiveSum(nullptr, bytes, in, out, (int)n, s);
+    RC(h->cub_tmp.reserve((int64_t)bytes + 1));
+    CK(cub::DeviceScan::InclusiveSum(h->cub_tmp.p, bytes, in, out, (int)n, s));
+    return SILI_OK;
+}
+
+// copy helpers: host or device source/destination
+int to_dev(const void* src, void* dst, size_t bytes, cudaStream_t s) {
+    if (bytes == 0) return SILI_OK;
+    CK(cudaMemcpyAsync(dst, src, bytes, is_device_ptr(src) ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, s));
+    return SILI_OK;
+}
+int from_dev(const void* src, void* dst, size_t bytes, cudaStream_t s) {
+    if (bytes == 0 || !dst) return SILI_OK;
+    CK(cudaMemcpyAsync(dst, src, bytes, is_device_ptr(dst) ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, s));
+    return SILI_OK;
+}
+
+// Device view of an input array: the array itself when it is device memory,
+// else a copy in the given staging buffer.
+int stage_in(sili_layer* h, const float* src, size_t n, DBuf<float>& stage, const float** out, cudaStream_t s) {
+    if (is_device_ptr(src)) { *out = src; return SILI_OK; }
+    RC(stage.reserve((int64_t)n + 1));
+    CK(cudaMemcpyAsync(stage.p, src, n * 4, cudaMemcpyHostToDevice, s));
+    *out = stage.p;
+    return SILI_OK;
+}
+// dst = transpose of the row-major [rows, cols] array src (host or device).
+int stage_transposed(sili_layer* h, const float* src, int64_t rows, int64_t cols, DBuf<float>& dst, cudaStream_t s) {
+    const float* d = nullptr;
+    RC(stage_in(h, src, (size_t)(rows * cols), h->x_stage, &d, s));
+    RC(dst.reserve(rows * cols + 1));
+    launch_transpose(d, dst.p, rows, cols, s);
+    return SILI_OK;
+}
+UpdateParams update_params(sili_layer* h, float lr, unsigned flags, float beta2, float eps) {
+    UpdateParams P;
+    P.lr = lr; P.beta2 = beta2; P.eps = eps;
+    P.lr_per_row_nnz = (flags & SILI_LR_PER_ROW_NNZ) != 0;
+    P.damp = (flags & SILI_DAMP_BY_IMPORTANCE) != 0;
+    P.stochastic = false;
+    P.os_trainable = false;
+    P.call_key = host_mix64(h->seed ^ (h->call * 0x9E3779B97F4A7C15ULL));
+    P.pow_tab = h->pow_tab.p; P.pow_n = h->pow_n;
+    P.colg = h->colg.p; P.colc = h->colc.p;
+    P.stats = h->d_st.p; P.stat_max = h->d_stmax.p;
+    return P;
+}
+
+// Validates a row-major CSR argument: ptrs[0] == 0, non-decreasing,
+// ptrs[rows] == nnz and (for host arrays) every index in [0, cols).
+int check_csr(const int* ptrs, const int* idx, int rows, int nnz, int64_t cols, const char* what) {
+    std::vector<int> hp((size_t)rows + 1);
+    if (is_device_ptr(ptrs)) CK(cudaMemcpy(hp.data(), ptrs, hp.size() * 4, cudaMemcpyDeviceToHost));
+    else std::memcpy(hp.data(), ptrs, hp.size() * 4);
+    if (hp[0] != 0 || hp[rows] != nnz) return fail(SILI_EINVAL, std::string(what) + ": ptrs[0] must be 0 and ptrs[batch] == nnz");
+    for (int b = 0; b < rows; ++b)
+        if (hp[b + 1] < hp[b]) return fail(SILI_EINVAL, std::string(what) + ": ptrs must be non-decreasing");
+    if (idx && !is_device_ptr(idx))
+        for (int j = 0; j < nnz; ++j)
+            if (idx[j] < 0 || idx[j] >= cols) return fail(SILI_EINVAL, std::string(what) + ": index out of range");
+    return SILI_OK;
+}
+
+// ── derived index: flat decode + CSC shadow ─────────────────────────────────
+int ensure_aux(sili_layer* h, cudaStream_t s) {
+    if (!h->aux_dirty) return SILI_OK;
+    const int64_t R = h->rows, C = h->cols, nnz = h->total_nnz;
+    RC(h->rowptr.reserve(R + 1));
+    RC(h->colptr.reserve(C + 1));
+    RC(h->colcount.reserve(C + 1));
+    const int64_t nz = std::max<int64_t>(nnz, 1);
+    RC(h->abs_cols.reserve(nz)); RC(h->frow.reserve(nz)); RC(h->fvpos.reserve(nz));
+    RC(h->crow.reserve(nz)); RC(h->cvpos.reserve(nz));
+    RC(h->sort_k.reserve(nz)); RC(h->sort_ko.reserve(nz)); RC(h->sort_v.reserve(nz)); RC(h->sort_vo.reserve(nz));
+    CK(cudaMemsetAsync(h->rowptr.p, 0, sizeof(int), s));
+    launch_row_nnz(h->es.p, h->ee.p, R, h->rowptr.p + 1, s);
+    if (R > 0) RC(scan_incl_int(h, h->rowptr.p + 1, h->rowptr.p + 1, R, s));
+    CK(cudaMemsetAsync(h->colcount.p, 0, (size_t)(C + 1) * sizeof(int), s));
+    LayerView v = h->view();
+    launch_decode_rows(v, h->abs_cols.p, h->frow.p, h->fvpos.p, h->colcount.p, s);
+    if (nnz > 0) {
+        CK(cudaMemcpyAsync(h->sort_k.p, h->abs_cols.p, (size_t)nnz * sizeof(int), cudaMemcpyDeviceToDevice, s));
+        launch_iota(h->sort_v.p, nnz, s);
+        int bits = 1;
+        while ((int64_t(1) << bits) < C) ++bits;
+        size_t bytes = 0;
+        cub::DeviceRadixSort::SortPairs(nullptr, bytes, h->sort_k.p, h->sort_ko.p, h->sort_v.p, h->sort_vo.p,
+                                        (int)nnz, 0, bits, s);
+        RC(h->cub_tmp.reserve((int64_t)bytes + 1));
+        CK(cub::DeviceRadixSort::SortPairs(h->cub_tmp.p, bytes, h->sort_k.p, h->sort_ko.p, h->sort_v.p,
+                                           h->sort_vo.p, (int)nnz, 0, bits, s));
+        launch_gather_csc(h->sort_vo.p, h->frow.p, h->fvpos.p, nnz, h->crow.p, h->cvpos.p, s);
+    }
+    RC(scan_excl_int(h, h->colcount.p, h->colptr.p, C + 1, s));
+    CK(cudaGetLastError());
+    {   // rows with no synapse take the dead-row bootstrap (linear_disldo.hpp:1985-2042)
+        std::vector<int> rp((size_t)R + 1);
+        CK(cudaMemcpyAsync(rp.data(), h->rowptr.p, (size_t)(R + 1) * 4, cudaMemcpyDeviceToHost, s));
+        CK(cudaStreamSynchronize(s));
+        h->has_dead_rows = false;
+        for (int64_t r = 0; r < R; ++r) if (rp[r + 1] == rp[r]) { h->has_dead_rows = true; break; }
+    }
+    h->aux_dirty = false;
+    return SILI_OK;
+}
+
+// ── layout helpers on the host (O(rows) metadata) ───────────────────────────
+struct HostLayout {
+    std::vector<int64_t> bs, be, es, ee;
+};
+int get_layout(sili_layer* h, HostLayout& L) {
+    const int64_t R = h->rows;
+    L.bs.resize(R + 1); L.be.resize(R + 1); L.es.resize(R + 1); L.ee.resize(R + 1);
+    CK(cudaMemcpyAsync(L.bs.data(), h->bs.p, (R + 1) * 8, cudaMemcpyDeviceToHost, h->stream));
+    CK(cudaMemcpyAsync(L.es.data(), h->es.p, (R + 1) * 8, cudaMemcpyDeviceToHost, h->stream));
+    if (R > 0) {
+        CK(cudaMemcpyAsync(L.be.data(), h->be.p, R * 8, cudaMemcpyDeviceToHost, h->stream));
+        CK(cudaMemcpyAsync(L.ee.data(), h->ee.p, R * 8, cudaMemcpyDeviceToHost, h->stream));
+    }
+    CK(cudaStreamSynchronize(h->stream));
+    return SILI_OK;
+}
+int put_layout(sili_layer* h, const HostLayout& L) {
+    const int64_t R = h->rows;
+    RC(h->bs.reserve(R + 1)); RC(h->be.reserve(R + 1)); RC(h->es.reserve(R + 1)); RC(h->ee.reserve(R + 1));
+    CK(cudaMemcpyAsync(h->bs.p, L.bs.data(), (R + 1) * 8, cudaMemcpyHostToDevice, h->stream));
+    CK(cudaMemcpyAsync(h->es.p, L.es.data(), (R + 1) * 8, cudaMemcpyHostToDevice, h->stream));
+    if (R > 0) {
+        CK(cudaMemcpyAsync(h->be.p, L.be.data(), R * 8, cudaMemcpyHostToDevice, h->stream));
+        CK(cudaMemcpyAsync(h->ee.p, L.ee.data(), R * 8, cudaMemcpyHostToDevice, h->stream));
+    }
+    CK(cudaStreamSynchronize(h->stream));
+    return SILI_OK;
+}
+
+// Moves every row to the offsets in N (allocations may change), copying the
+// live bytes/values; new buffers are zero-filled.
+int relayout(sili_layer* h, const HostLayout& N, int64_t new_idx_n, int64_t new_val_n, bool recode) {
+    cudaStream_t s = h->stream;
+    DBuf<int64_t> nbs, nes;
+    RC(nbs.reserve(h->rows + 1));
+    RC(nes.reserve(h->rows + 1));
+    CK(cudaMemcpyAsync(nbs.p, N.bs.data(), (h->rows + 1) * 8, cudaMemcpyHostToDevice, s));
+    CK(cudaMemcpyAsync(nes.p, N.es.data(), (h->rows + 1) * 8, cudaMemcpyHostToDevice, s));
+    DBuf<uint8_t> nidx, nval;
+    RC(nidx.reserve(new_idx_n + 64));
+    RC(nval.reserve(new_val_n + 64));
+    CK(cudaMemsetAsync(nidx.p, 0, (size_t)nidx.cap, s));
+    CK(cudaMemsetAsync(nval.p, 0, (size_t)nval.cap, s));
+    launch_copy_rows(h->view(), nbs.p, nes.p, nidx.p, nval.p, recode, s);
+    CK(cudaGetLastError());
+    CK(cudaStreamSynchronize(s));
+    h->idx.swap(nidx);
+    h->val.swap(nval);
+    h->idx_n = new_idx_n;
+    h->val_n = new_val_n;
+    RC(put_layout(h, N));
+    h->aux_dirty = true;
+    return SILI_OK;
+}
+
+// ── scale bookkeeping ───────────────────────────────────────────────────────
+int alloc_scales(sili_layer* h) {
+    cudaStream_t s = h->stream;
+    const int64_t R = h->rows, C = h->cols, k = h->rank;
+    RC(h->vs.reserve(R * k + 1)); RC(h->vsi.reserve(R * k + 1)); RC(h->vsm.reserve(R * k + 1));
+    RC(h->vstep.reserve(R * k + 1));
+    RC(h->os.reserve(C * k + 1)); RC(h->osi.reserve(C * k + 1)); RC(h->ostep.reserve(C * k + 1));
+    RC(h->colg.reserve(C * k + 1)); RC(h->colc.reserve(C * k + 1));
+    return SILI_OK;
+}
+
+// Rebuild a rank-strided vector for a new rank from its logical prefix.
+int relayout_scale(sili_layer* h, DBuf<float>& v, int64_t n_entities, int old_rank, int new_rank,
+                   int64_t logical_n, bool scale_default) {
+    std::vector<float> old((size_t)(n_entities * old_rank));
+    if (!old.empty())
+        CK(cudaMemcpy(old.data(), v.p, old.size() * sizeof(float), cudaMemcpyDeviceToHost));
+    std::vector<float> nv((size_t)(n_entities * new_rank));
+    for (size_t i = 0; i < nv.size(); ++i) {
+        if ((int64_t)i < logical_n && i < old.size()) nv[i] = old[i];
+        else nv[i] = scale_default ? ((i % new_rank) == 0 ? 1.0f : 0.0f) : 0.0f;
+    }
+    DBuf<float> q;
+    RC(q.reserve((int64_t)nv.size() + 1));
+    if (!nv.empty()) CK(cudaMemcpy(q.p, nv.data(), nv.size() * sizeof(float), cudaMemcpyHostToDevice));
+    v.swap(q);
+    return SILI_OK;
+}
+int relayout_steps(sili_layer* h, DBuf<uint32_t>& v, int64_t n_entities, int old_rank, int new_rank) {
+    std::vector<uint32_t> old((size_t)(n_entities * old_rank));
+    if (!old.empty()) CK(cudaMemcpy(old.data(), v.p, old.size() * 4, cudaMemcpyDeviceToHost));
+    std::vector<uint32_t> nv((size_t)(n_entities * new_rank), 0u);
+    for (size_t i = 0; i < nv.size() && i < old.size(); ++i) nv[i] = old[i];
+    DBuf<uint32_t> q;
+    RC(q.reserve((int64_t)nv.size() + 1));
+    if (!nv.empty()) CK(cudaMemcpy(q.p, nv.data(), nv.size() * 4, cudaMemcpyHostToDevice));
+    v.swap(q);
+    return SILI_OK;
+}
+
+// Grows the logical size of value_scale / output_scale to n, filling new
+// entries with `fill` (std::vector::resize semantics of the reference).
+void grow_logical(sili_layer* h, DBuf<float>& v, int64_t& n_logical, int64_t n, float fill) {
+    if (n <= n_logical) return;
+    launch_fill_f32(v.p + n_logical, n - n_logical, fill, h->stream);
+    n_logical = n;
+}
+
+// Bias-correction table: pow_tab[s] = powf(beta2, s) evaluated by the host
+// libm, exactly the reference's std::pow(beta2, (float)step)
+// (delta_csr_types.hpp:457, linear_disldo.hpp:1941, sisldo_ops.hpp:793).
+int ensure_pow_table(sili_layer* h, float beta2, uint32_t need) {
+    const bool same = (beta2 == h->pow_beta2) || (std::isnan(beta2) && std::isnan(h->pow_beta2));
+    if (same && (int64_t)need < h->pow_n) return SILI_OK;
+    int n = 1;
+    if (beta2 > 0.0f && beta2 < 1.0f) {
+        // entries until powf(beta2, s) <= 2^-26, after which 1 - p == 1 in fp32
+        while (n < (1 << 22) && std::pow(beta2, (float)n) > 1.4901161e-08f) ++n;
+        n += 1;
+    } else {
+        n = 1 << 16;
+    }
+    n = std::max<int>(n, (int)need + 1);
+    std::vector<float> t((size_t)n);
+    for (int i = 0; i < n; ++i) t[i] = std::pow(beta2, (float)i);
+    RC(h->pow_tab.reserve(n));
+    CK(cudaMemcpy(h->pow_tab.p, t.data(), (size_t)n * sizeof(float), cudaMemcpyHostToDevice));
+    h->pow_beta2 = beta2;
+    h->pow_n = n;
+    return SILI_OK;
+}
+
+int flush_stats(sili_layer* h) {
+    if (!h->st_pending) return SILI_OK;
+    double d[2];
+    float m;
+    CK(cudaMemcpy(d, h->d_st.p, 2 * sizeof(double), cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(&m, h->d_stmax.p, sizeof(float), cudaMemcpyDeviceToHost));
+    h->st[2] += d[0];
+    h->st[3] += d[1];
+    h->st_imax = std::max(h->st_imax * h->max_abs_decay, m);
+    CK(cudaMemset(h->d_st.p, 0, 2 * sizeof(double)));
+    CK(cudaMemset(h->d_stmax.p, 0, sizeof(float)));
+    h->st_pending = false;
+    return SILI_OK;
+}
+
+int recompute_stats(sili_layer* h) {
+    RC(flush_stats(h));
+    DBuf<double> sums;
+    DBuf<float> mx;
+    RC(sums.reserve(4));
+    RC(mx.reserve(2));
+    CK(cudaMemsetAsync(sums.p, 0, 4 * sizeof(double), h->stream));
+    CK(cudaMemsetAsync(mx.p, 0, 2 * sizeof(float), h->stream));
+    launch_stats(h->view(), sums.p, mx.p, h->stream);
+    double d[4];
+    float m[2];
+    CK(cudaMemcpyAsync(d, sums.p, sizeof d, cudaMemcpyDeviceToHost, h->stream));
+    CK(cudaMemcpyAsync(m, mx.p, sizeof m, cudaMemcpyDeviceToHost, h->stream));
+    CK(cudaStreamSynchronize(h->stream));
+    h->st[0] = d[0]; h->st[1] = d[1]; h->st[2] = d[2]; h->st[3] = d[3];
+    h->st_vmax = m[0]; h->st_imax = m[1];
+    return SILI_OK;
+}
+
+// delta_csr_from_absolute on device (delta_csr_memory.hpp:16-93): per-synapse
+// ULEB128 lengths and a scan give each row's byte count; the host lays out the
+// per-row headroom (0.2 * bytes + 5 bytes, max(1, 0.2 * n + 1) elements) and a
+// kernel writes every delta and FP4 byte in place.
+int import_csr(sili_layer* h, const int* d_ptrs, const int* d_idx, const float* d_vals, int nnz) {
+    cudaStream_t s = h->stream;
+    const int R = (int)h->rows;
+    DBuf<int> len, boff;
+    RC(len.reserve(nnz + 1));
+    RC(boff.reserve(nnz + 1));
+    CK(cudaMemsetAsync(len.p, 0, (size_t)(nnz + 1) * sizeof(int), s));
+    launch_import_lengths(d_ptrs, d_idx, R, len.p, s);
+    RC(scan_excl_int(h, len.p, boff.p, nnz + 1, s));
+    DBuf<int64_t> rb, rn;
+    RC(rb.reserve(R + 1));
+    RC(rn.reserve(R + 1));
+    launch_import_rows(d_ptrs, boff.p, R, rb.p, rn.p, s);
+    std::vector<int64_t> hrb(R + 1), hrn(R + 1);
+    if (R > 0) {
+        CK(cudaMemcpyAsync(hrb.data(), rb.p, (size_t)R * 8, cudaMemcpyDeviceToHost, s));
+        CK(cudaMemcpyAsync(hrn.data(), rn.p, (size_t)R * 8, cudaMemcpyDeviceToHost, s));
+    }
+    CK(cudaStreamSynchronize(s));
+    HostLayout N;
+    N.bs.assign(R + 1, 0); N.be.assign(R + 1, 0); N.es.assign(R + 1, 0); N.ee.assign(R + 1, 0);
+    for (int r = 0; r < R; ++r) {
+        const int64_t nb = hrb[r], n = hrn[r];
+        N.be[r] = N.bs[r] + nb;
+        N.bs[r + 1] = N.be[r] + (int64_t)((float)nb * 0.2f) + 5;
+        N.ee[r] = N.es[r] + n;
+        N.es[r + 1] = N.ee[r] + std::max<int64_t>(1, (int64_t)((float)n * 0.2f) + 1);
+    }
+    RC(put_layout(h, N));
+    const int64_t ib = N.bs[R], vb = N.es[R];
+    DBuf<uint8_t> nidx, nval;
+    RC(nidx.reserve(ib + 64));
+    RC(nval.reserve(vb + 64));
+    CK(cudaMemsetAsync(nidx.p, 0, (size_t)nidx.cap, s));
+    CK(cudaMemsetAsync(nval.p, 0, (size_t)nval.cap, s));
+    launch_import_write(d_ptrs, d_idx, d_vals, boff.p, R, h->bs.p, h->es.p, nidx.p, nval.p, s);
+    CK(cudaGetLastError());
+    CK(cudaStreamSynchronize(s));
+    h->idx.swap(nidx);
+    h->val.swap(nval);
+    h->idx_n = ib;
+    h->val_n = vb;
+    h->total_nnz = nnz;
+    h->aux_dirty = true;
+    return SILI_OK;
+}
+
+int make_layer(int n_in, int n_out, int max_weights, int device, int stochastic, sili_layer** out) {
+    if (n_in < 0 || n_out < 0 || max_weights < 0) return fail(SILI_EINVAL, "negative layer size");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+        cudaGetLastError();
+        return fail(SILI_ECUDA, "sili_b200: no CUDA device available (this library has no CPU path)");
+    }
+    if (device < 0 || device >= ndev) return fail(SILI_EINVAL, "device index out of range");
+    CK(cudaSetDevice(device));
+    sili_layer* h = new sili_layer();
+    h->dev = device;
+    h->rows = n_in;
+    h->cols = n_out;
+    h->stochastic = stochastic != 0;
+    if (cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess) {
+        delete h;
+        return fail(SILI_ECUDA, "cudaStreamCreate failed");
+    }
+    int rc = SILI_OK;
+    auto chk = [&](int r) { if (!rc) rc = r; };
+    chk(alloc_scales(h));
+    chk(h->is.reserve(n_in + 1)); chk(h->ois.reserve(n_out + 1));
+    chk(h->in_acc.reserve(n_in + 1)); chk(h->grad_acc.reserve(n_out + 1)); chk(h->out_degree.reserve(n_out + 1));
+    chk(h->d_st.reserve(2)); chk(h->d_stmax.reserve(1));
+    if (rc) { delete h; return rc; }
+    cudaStream_t s = h->stream;
+    launch_fill_scale_default(h->vs.p, 0, (int64_t)n_in, 1, s);
+    launch_fill_scale_default(h->os.p, 0, (int64_t)n_out, 1, s);
+    cudaMemsetAsync(h->vsi.p, 0, (size_t)h->vsi.cap * 4, s);
+    cudaMemsetAsync(h->vsm.p, 0, (size_t)h->vsm.cap * 4, s);
+    cudaMemsetAsync(h->osi.p, 0, (size_t)h->osi.cap * 4, s);
+    cudaMemsetAsync(h->vstep.p, 0, (size_t)h->vstep.cap * 4, s);
+    cudaMemsetAsync(h->ostep.p, 0, (size_t)h->ostep.cap * 4, s);
+    launch_fill_f32(h->is.p, n_in, 1.0f, s);
+    launch_fill_f32(h->ois.p, n_out, 1.0f, s);
+    cudaMemsetAsync(h->in_acc.p, 0, (size_t)(n_in + 1) * 4, s);
+    cudaMemsetAsync(h->grad_acc.p, 0, (size_t)(n_out + 1) * 4, s);
+    cudaMemsetAsync(h->out_degree.p, 0, (size_t)(n_out + 1) * 4, s);
+    cudaMemsetAsync(h->d_st.p, 0, 2 * sizeof(double), s);
+    cudaMemsetAsync(h->d_stmax.p, 0, sizeof(float), s);
+    // empty delta-CSR with per-row headroom (cpu_backend.cpp:380-389)
+    h->idx_budget = (int64_t)max_weights * 8 + 4096;
+    h->val_budget = (int64_t)max_weights + 64;
+    std::vector<int> zp((size_t)n_in + 1, 0);
+    DBuf<int> dp;
+    rc = dp.reserve(n_in + 1);
+    if (!rc && cudaMemcpy(dp.p, zp.data(), zp.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) rc = SILI_ECUDA;
+    if (!rc) rc = import_csr(h, dp.p, dp.p, nullptr, 0);
+    if (rc) { cudaStreamDestroy(h->stream); delete h; return rc; }
+    h->max_idx_bytes = h->idx_budget;
+    h->max_val_bytes = h->val_budget;
+    *out = h;
+    return SILI_OK;
+}
+
+}  // namespace
+
+// ═══════════════════════════════════════════════════════════════════════════
+extern "C" {
+
+const char* sili_last_error(void) { return g_err.c_str(); }
+
+int sili_kernel_launches(int64_t* count) {
+    if (count) *count = (int64_t)launch_count();
+    return SILI_OK;
+}
+
+int sili_layer_set_kernel_timing(sili_layer* h, int enable) {
+    RC(use(h));
+    if (enable && !h->ev[0])
+        for (auto& e : h->ev) CK(cudaEventCreate(&e));
+    h->timing = enable != 0;
+    h->ev_fwd = h->ev_bwd = false;
+    return SILI_OK;
+}
+
+int sili_layer_kernel_ms(sili_layer* h, float* fwd, float* bwd) {
+    RC(use(h));
+    if (fwd) *fwd = 0.f;
+    if (bwd) *bwd = 0.f;
+    if (h->ev_fwd && fwd) { CK(cudaEventSynchronize(h->ev[1])); CK(cudaEventElapsedTime(fwd, h->ev[0], h->ev[1])); }
+    if (h->ev_bwd && bwd) { CK(cudaEventSynchronize(h->ev[3])); CK(cudaEventElapsedTime(bwd, h->ev[2], h->ev[3])); }
+    return SILI_OK;
+}
+
+int sili_device_count(int* count) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) { cudaGetLastError(); n = 0; }
+    if (count) *count = n;
+    return SILI_OK;
+}
+
+int sili_layer_create(int n_in, int n_out, int max_weights, int device, int stochastic, sili_layer** out) {
+    if (!out) return fail(SILI_EINVAL, "null out pointer");
+    return make_layer(n_in, n_out, max_weights, device, stochastic, out);
+}
+
+int sili_layer_destroy(sili_layer* h) {
+    if (!h) return SILI_OK;
+    cudaSetDevice(h->dev);
+    cudaStreamSynchronize(h->stream);
+    cudaStream_t s = h->stream;
+    for (auto& e : h->ev) if (e) cudaEventDestroy(e);
+    delete h;
+    cudaStreamDestroy(s);
+    return SILI_OK;
+}
+
+int sili_layer_sync(sili_layer* h) {
+    RC(use(h));
+    CK(cudaStreamSynchronize(h->stream));
+    return SILI_OK;
+}
+
+int sili_layer_seed_rng(sili_layer* h, uint64_t seed) {
+    RC(use(h));
+    h->seed = seed;
+    h->call = 0;
+    return SILI_OK;
+}
+
+int sili_layer_load_weights(sili_layer* h, const int* ptrs, const int* idx, const float* vals, int nnz) {
+    RC(use(h));
+    if (nnz < 0 || !ptrs) return fail(SILI_EINVAL, "load_weights: bad arguments");
+    const int R = (int)h->rows;
+    cudaStream_t s = h->stream;
+    std::vector<int> hp(R + 1);
+    if (is_device_ptr(ptrs)) CK(cudaMemcpy(hp.data(), ptrs, (R + 1) * 4, cudaMemcpyDeviceToHost));
+    else std::memcpy(hp.data(), ptrs, (R + 1) * 4);
+    if (hp[0] != 0 || hp[R] != nnz) return fail(SILI_EINVAL, "load_weights: ptrs[0] must be 0 and ptrs[n_in] == nnz");
+    for (int r = 0; r < R; ++r)
+        if (hp[r + 1] < hp[r]) return fail(SILI_EINVAL, "load_weights: ptrs must be non-decreasing");
+    DBuf<int> dp, di;
+    DBuf<float> dv;
+    RC(dp.reserve(R + 1)); RC(di.reserve(nnz + 1)); RC(dv.reserve(nnz + 1));
+    CK(cudaMemcpyAsync(dp.p, hp.data(), (R + 1) * 4, cudaMemcpyHostToDevice, s));
+    RC(to_dev(idx, di.p, (size_t)nnz * 4, s));
+    RC(to_dev(vals, dv.p, (size_t)nnz * 4, s));
+    // column range / ordering check on the host copy (the reference assumes sorted input)
+    std::vector<int> hi(nnz);
+    if (nnz) CK(cudaMemcpyAsync(hi.data(), di.p, (size_t)nnz * 4, cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    for (int r = 0; r < R; ++r)
+        for (int f = hp[r]; f < hp[r + 1]; ++f) {
+            if (hi[f] < 0 || hi[f] >= h->cols) return fail(SILI_EINVAL, "load_weights: column index out of range");
+            if (f > hp[r] && hi[f] < hi[f - 1]) return fail(SILI_EINVAL, "load_weights: columns must be sorted within a row");
+        }
+    RC(import_csr(h, dp.p, di.p, dv.p, nnz));
+    h->idx_budget = std::max<int64_t>(h->idx_budget, (int64_t)nnz * 8 + 4096);
+    h->val_budget = std::max<int64_t>(h->val_budget, (int64_t)nnz + 64);
+    h->max_idx_bytes = h->idx_budget;
+    h->max_val_bytes = h->val_budget;
+    // out_degree rebuilt from the loaded indices (cpu_backend.cpp:899-900)
+    std::vector<int> deg((size_t)h->cols, 0);
+    for (int f = 0; f < nnz; ++f) deg[hi[f]]++;
+    if (h->cols) CK(cudaMemcpy(h->out_degree.p, deg.data(), (size_t)h->cols * 4, cudaMemcpyHostToDevice));
+    h->st_pending = false;
+    CK(cudaMemset(h->d_st.p, 0, 2 * sizeof(double)));
+    CK(cudaMemset(h->d_stmax.p, 0, sizeof(float)));
+    return recompute_stats(h);
+}
+
+int sili_layer_set_value_bytes(sili_layer* h, const uint8_t* values, int64_t n) {
+    RC(use(h));
+    n = std::min<int64_t>(n, h->val_n);
+    RC(to_dev(values, h->val.p, (size_t)n, h->stream));
+    CK(cudaStreamSynchronize(h->stream));
+    return SILI_OK;
+}
+
+// ── scales ──────────────────────────────────────────────────────────────────
+int sili_layer_set_scale_rank(sili_layer* h, int rank) {
+    RC(use(h));
+    if (rank < 1) return fail(SILI_EINVAL, "scale_rank must be >= 1");
+    if (rank > 4) return fail(SILI_EINVAL, "scale_rank exceeds SCALE_RANK_MAX (4)");
+    if (rank == h->rank) return SILI_OK;
+    const int old = h->rank;
+    CK(cudaStreamSynchronize(h->stream));
+    RC(relayout_scale(h, h->vs, h->rows, old, rank, h->n_vs, true));
+    RC(relayout_scale(h, h->os, h->cols, old, rank, h->n_os, true));
+    RC(relayout_scale(h, h->vsi, h->rows, old, rank, h->rows * old, false));
+    RC(relayout_scale(h, h->osi, h->cols, old, rank, h->cols * old, false));
+    RC(relayout_scale(h, h->vsm, h->rows, old, rank, h->rows * old, false));
+    RC(relayout_steps(h, h->vstep, h->rows, old, rank));
+    RC(relayout_steps(h, h->ostep, h->cols, old, rank));
+    h->rank = rank;
+    RC(h->colg.reserve(h->cols * rank + 1));
+    RC(h->colc.reserve(h->cols * rank + 1));
+    return SILI_OK;
+}
+
+int sili_layer_get_scale_rank(sili_layer* h, int* rank) {
+    RC(use(h));
+    *rank = h->rank;
+    return SILI_OK;
+}
+
+int sili_layer_set_scale(sili_layer* h, int kind, int index, int k, float v) {
+    RC(use(h));
+    CK(cudaStreamSynchronize(h->stream));
+    switch (kind) {
+    case SILI_SCALE_VALUE: {
+        if (index < 0 || index >= h->rows || k < 0 || k >= h->rank) return fail(SILI_EINVAL, "value_scale index out of range");
+        const int64_t i = (int64_t)index * h->rank + k;
+        grow_logical(h, h->vs, h->n_vs, i + 1, 1.0f);
+        CK(cudaMemcpyAsync(h->vs.p + i, &v, 4, cudaMemcpyHostToDevice, h->stream));
+        break;
+    }
+    case SILI_SCALE_OUTPUT: {
+        if (index < 0 || index >= h->cols || k < 0 || k >= h->rank) return fail(SILI_EINVAL, "output_scale index out of range");
+        const int64_t i = (int64_t)index * h->rank + k;
+        grow_logical(h, h->os, h->n_os, i + 1, 1.0f);
+        CK(cudaMemcpyAsync(h->os.p + i, &v, 4, cudaMemcpyHostToDevice, h->stream));
+        h->os_trainable = true;
+        break;
+    }
+    case SILI_SCALE_IMPORTANCE:
+        if (index < 0 || index >= h->rows) return fail(SILI_EINVAL, "importance_scale index out of range");
+        CK(cudaMemcpyAsync(h->is.p + index, &v, 4, cudaMemcpyHostToDevice, h->stream));
+        break;
+    case SILI_SCALE_OUTPUT_IMPORTANCE:
+        if (index < 0 || index >= h->cols) return fail(SILI_EINVAL, "output_importance_scale index out of range");
+        CK(cudaMemcpyAsync(h->ois.p + index, &v, 4, cudaMemcpyHostToDevice, h->stream));
+        break;
+    default:
+        return fail(SILI_EINVAL, "set_scale: unknown kind");
+    }
+    CK(cudaStreamSynchronize(h->stream));
+    return SILI_OK;
+}
+
+static float* scale_ptr(sili_layer* h, int kind, int64_t* n_entities, int* stride) {
+    *stride = h->rank;
+    switch (kind) {
+    case SILI_SCALE_VALUE: *n_entities = h->rows; return h->vs.p;
+    case SILI_SCALE_OUTPUT: *n_entities = h->cols; return h->os.p;
+    case SILI_SCALE_IMPORTANCE: *n_entities = h->rows; *stride = 1; return h->is.p;
+    case SILI_SCALE_OUTPUT_IMPORTANCE: *n_entities = h->cols; *stride = 1; return h->ois.p;
+    case SILI_SCALE_VALUE_IMPORTANCE: *n_entities = h->rows; return h->vsi.p;
+    case SILI_SCALE_OUTPUT_SCALE_IMPORTANCE: *n_entities = h->cols; return h->osi.p;
+    case SILI_SCALE_VALUE_MOMENTUM: *n_entities = h->rows; return h->vsm.p;
+    default: return nullptr;
+    }
+}
+
+int sili_layer_get_scale(sili_layer* h, int kind, int index, int k, float* v) {
+    RC(use(h));
+    int64_t n;
+    int stride;
+    float* p = scale_ptr(h, kind, &n, &stride);
+    if (!p) return fail(SILI_EINVAL, "get_scale: unknown kind");
+    if (index < 0 || index >= n || k < 0 || k >= stride) return fail(SILI_EINVAL, "get_scale: index out of range");
+    CK(cudaStreamSynchronize(h->stream));
+    CK(cudaMemcpy(v, p + (int64_t)index * stride + k, 4, cudaMemcpyDeviceToHost));
+    return SILI_OK;
+}
+
+int sili_layer_get_scales(sili_layer* h, int kind, float* out, int n_req) {
+    RC(use(h));
+    int64_t n;
+    int stride;
+    float* p = scale_ptr(h, kind, &n, &stride);
+    if (!p) return fail(SILI_EINVAL, "get_scales: unknown kind");
+    const int64_t m = std::min<int64_t>(n_req, n * stride);
+    CK(cudaStreamSynchronize(h->stream));
+    RC(from_dev(p, out, (size_t)m * 4, h->stream));
+    CK(cudaStreamSynchronize(h->stream));
+    return SILI_OK;
+}
+
+int sili_layer_get_steps(sili_layer* h, int which, uint32_t* out, int n_req) {
+    RC(use(h));
+    const int64_t n = (which == 0 ? h->rows : h->cols) * h->rank;
+    const int64_t m = std::min<int64_t>(n_req, n);
+    CK(cudaStreamSynchronize(h->stream));
+    RC(from_dev(which == 0 ? h->vstep.p : h->ostep.p, out, (size_t)m * 4, h->stream));
+    CK(cudaStreamSynchronize(h->stream));
+    return SILI_OK;
+}
+
+// rescale_value_row / rescale_importance_row (delta_csr_types.hpp:1389-1431)
+int sili_layer_rescale_row(sili_layer* h, int kind, int row, float new_scale) {
+    RC(use(h));
+    if (kind != SILI_SCALE_VALUE && kind != SILI_SCALE_IMPORTANCE) return fail(SILI_EINVAL, "rescale_row: kind");
+    float old;
+    if (row < 0 || row >= h->rows) return SILI_OK;   // reference: `if (row >= L.rows) return;`
+    RC(sili_layer_get_scale(h, kind, row, 0, &old));
+    if (new_scale == old) return SILI_OK;
+    launch_rescale_row(h->view(), row, old, new_scale, kind == SILI_SCALE_VALUE, h->stream);
+    CK(cudaGetLastError());
+    return sili_layer_set_scale(h, kind, row, 0, new_scale);
+}
+
+// ── compute ─────────────────────────────────────────────────────────────────
+int sili_layer_forward_dense(sili_layer* h, const float* x, int batch, float* y, void* stream) {
+    RC(use(h));
+    if (batch < 0 || !x || !y) return fail(SILI_EINVAL, "forward_dense: bad arguments");
+    cudaStream_t s = pick(h, stream);
+    const int64_t n_in = h->rows, n_out = h->cols;
+    RC(ensure_aux(h, s));
+    // the layer keeps x (as xT [n_in, batch]) for backward_dense, like _last_input
+    RC(stage_transposed(h, x, batch, n_in, h->xT, s));
+    h->last_batch = batch;
+    const bool dev_out = is_device_ptr(y);
+    float* yd = y;
+    if (!dev_out) {
+        RC(h->ytmp.reserve((int64_t)batch * n_out + 1));
+        yd = h->ytmp.p;
+    }
+    if (h->timing) CK(cudaEventRecord(h->ev[0], s));
+    launch_forward(h->view(), h->xT.p, batch, yd, false, s);
+    if (h->timing) { CK(cudaEventRecord(h->ev[1], s)); h->ev_fwd = true; }
+    CK(cudaGetLastError());
+    if (!dev_out) {
+        CK(cudaMemcpyAsync(y, yd, (size_t)batch * n_out * 4, cudaMemcpyDeviceToHost, s));
+    }
+    if (!dev_out || !is_device_ptr(x)) CK(cudaStreamSynchronize(s));
+    return SILI_OK;
+}
+
+int sili_layer_backward_dense(sili_layer* h, const float* x, const float* dy, int batch, float lr, unsigned flags,
+                              float beta2, float eps, float* dx, void* stream) {
+    RC(use(h));
+    if (batch < 0 || !dy || !dx) return fail(SILI_EINVAL, "backward_dense: bad arguments");
+    cudaStream_t s = pick(h, stream);
+    const int64_t n_in = h->rows, n_out = h->cols;
+    if (x) {
+        RC(stage_transposed(h, x, batch, n_in, h->xT, s));
+        h->last_batch = batch;
+    } else if (h->last_batch != batch) {
+        return fail(SILI_EINVAL, "backward_dense: dy batch differs from the last forward input");
+    }
+    RC(ensure_aux(h, s));
+    const float* dyd = nullptr;
+    RC(stage_in(h, dy, (size_t)batch * n_out, h->dy_stage, &dyd, s));
+    RC(h->dyT.reserve((int64_t)batch * n_out + 1));
+    launch_transpose(dyd, h->dyT.p, batch, n_out, s);
+    // accumulators, linear_disldo.hpp:515-520
+    launch_accum_abs_t(h->xT.p, h->in_acc.p, batch, n_in, s);
+    launch_accum_abs(dyd, h->grad_acc.p, batch, n_out, s);
+    const bool dev_out = is_device_ptr(dx);
+    float* dxd = dx;
+    if (!dev_out) {
+        RC(h->dx_stage.reserve((int64_t)batch * n_in + 1));
+        dxd = h->dx_stage.p;
+    }
+    LayerView v = h->view();
+    if (lr == 0.0f) {
+        if (h->timing) CK(cudaEventRecord(h->ev[2], s));
+        launch_backward_dx(v, h->dyT.p, batch, dxd, s);
+        if (h->timing) { CK(cudaEventRecord(h->ev[3], s)); h->ev_bwd = true; }
+    } else {
+        RC(h->dxT.reserve((int64_t)batch * n_in + 1));
+        // pre-size the lazily sized scale vectors (linear_disldo.hpp:571-594)
+        grow_logical(h, h->vs, h->n_vs, n_in * h->rank, 1.0f);
+        grow_logical(h, h->os, h->n_os, n_out * h->rank, 1.0f);
+        RC(ensure_pow_table(h, beta2, (uint32_t)(h->call + 2)));
+        UpdateParams P = update_params(h, lr, flags, beta2, eps);
+        P.stochastic = h->stochastic;
+        P.os_trainable = h->os_trainable;
+        h->call++;
+        if (h->os_trainable) {
+            CK(cudaMemsetAsync(h->colg.p, 0, (size_t)n_out * h->rank * 4, s));
+            CK(cudaMemsetAsync(h->colc.p, 0, (size_t)n_out * h->rank * 4, s));
+        }
+        if (h->total_nnz > 0) {
+            if (h->timing) CK(cudaEventRecord(h->ev[2], s));
+            launch_backward_update(v, h->xT.p, h->dyT.p, batch, P, h->dxT.p, s);
+            if (h->timing) { CK(cudaEventRecord(h->ev[3], s)); h->ev_bwd = true; }
+            h->st_pending = true;
+        } else {
+            CK(cudaMemsetAsync(h->dxT.p, 0, (size_t)batch * n_in * 4, s));
+        }
+        if (h->has_dead_rows) {
+            RC(h->dS.reserve((int64_t)batch * h->rank + 1));
+            launch_dead_rows(v, h->xT.p, dyd, batch, h->dS.p, P, s);
+        }
+        if (h->os_trainable) launch_output_scale_update(v, h->out_degree.p, P, s);
+        launch_transpose(h->dxT.p, dxd, n_in, batch, s);
+    }
+    CK(cudaGetLastError());
+    if (!dev_out) CK(cudaMemcpyAsync(dx, dxd, (size_t)batch * n_in * 4, cudaMemcpyDeviceToHost, s));
+    if (!dev_out || !is_device_ptr(dy) || (x && !is_device_ptr(x))) CK(cudaStreamSynchronize(s));
+    return SILI_OK;
+}
+
+int sili_layer_forward_sparse(sili_layer* h, const int* ptrs, const int* idx, const float* vals, int nnz, int batch,
+                              float* y, void* stream) {
+    RC(use(h));
+    if (batch < 0 || !ptrs || !y || nnz < 0) return fail(SILI_EINVAL, "forward_sparse: bad arguments");
+    cudaStream_t s = pick(h, stream);
+    const int64_t n_in = h->rows, n_out = h->cols;
+    RC(check_csr(ptrs, idx, batch, nnz, n_in, "forward_sparse"));
+    RC(ensure_aux(h, s));
+    DBuf<int> dp, di;
+    DBuf<float> dv;
+    RC(dp.reserve(batch + 1)); RC(di.reserve(nnz + 1)); RC(dv.reserve(nnz + 1));
+    RC(to_dev(ptrs, dp.p, (size_t)(batch + 1) * 4, s));
+    RC(to_dev(idx, di.p, (size_t)nnz * 4, s));
+    RC(to_dev(vals, dv.p, (size_t)nnz * 4, s));
+    RC(h->xT.reserve((int64_t)batch * n_in + 1));
+    CK(cudaMemsetAsync(h->xT.p, 0, (size_t)batch * n_in * 4, s));
+    launch_csr_to_dense_t(dp.p, di.p, dv.p, batch, (int)n_in, h->xT.p, nullptr, s);
+    const bool dev_out = is_device_ptr(y);
+    float* yd = y;
+    if (!dev_out) {
+        RC(h->ytmp.reserve((int64_t)batch * n_out + 1));
+        yd = h->ytmp.p;
+    }
+    if (h->total_nnz > 0) launch_forward(h->view(), h->xT.p, batch, yd, true, s);
+    else CK(cudaMemsetAsync(yd, 0, (size_t)batch * n_out * 4, s));
+    CK(cudaGetLastError());
+    if (!dev_out) CK(cudaMemcpyAsync(y, yd, (size_t)batch * n_out * 4, cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    return SILI_OK;
+}
+
+int sili_layer_backward_sparse(sili_layer* h, const float* x, const int* dptrs, const int* didx, const float* dvals,
+                               int dnnz, int batch, float lr, unsigned flags, float beta2, float eps, float* dx,
+                               void* stream) {
+    RC(use(h));
+    if (batch < 0 || !x || !dptrs || !dx || dnnz < 0) return fail(SILI_EINVAL, "backward_sparse: bad arguments");
+    cudaStream_t s = pick(h, stream);
+    const int64_t n_in = h->rows, n_out = h->cols;
+    RC(check_csr(dptrs, didx, batch, dnnz, n_out, "backward_sparse"));
+    RC(ensure_aux(h, s));
+    DBuf<float> dxin;
+    RC(dxin.reserve((int64_t)batch * n_in + 1));
+    RC(to_dev(x, dxin.p, (size_t)batch * n_in * 4, s));
+    DBuf<int> dp, di;
+    DBuf<float> dv;
+    RC(dp.reserve(batch + 1)); RC(di.reserve(dnnz + 1)); RC(dv.reserve(dnnz + 1));
+    RC(to_dev(dptrs, dp.p, (size_t)(batch + 1) * 4, s));
+    RC(to_dev(didx, di.p, (size_t)dnnz * 4, s));
+    RC(to_dev(dvals, dv.p, (size_t)dnnz * 4, s));
+    // accumulators, sisldo_ops.hpp:611-617
+    launch_accum_abs(dxin.p, h->in_acc.p, batch, n_in, s);
+    launch_accum_abs_csr(dp.p, di.p, dv.p, batch, (int)n_out, h->grad_acc.p, s);
+    // value_scale / value_scale_importance sized to n_in (sisldo_ops.hpp:622-625)
+    grow_logical(h, h->vs, h->n_vs, n_in, 1.0f);
+    RC(h->xT.reserve((int64_t)batch * n_in + 1));
+    launch_transpose(dxin.p, h->xT.p, batch, n_in, s);
+    RC(h->dyT.reserve((int64_t)batch * n_out + 1));
+    RC(h->presT.reserve((int64_t)batch * n_out + 1));
+    CK(cudaMemsetAsync(h->dyT.p, 0, (size_t)batch * n_out * 4, s));
+    CK(cudaMemsetAsync(h->presT.p, 0, (size_t)batch * n_out, s));
+    launch_csr_to_dense_t(dp.p, di.p, dv.p, batch, (int)n_out, h->dyT.p, h->presT.p, s);
+    RC(h->dxT.reserve((int64_t)batch * n_in + 1));
+    RC(h->sgs.reserve(n_in + 1)); RC(h->sgc.reserve(n_in + 1));
+    RC(ensure_pow_table(h, beta2, (uint32_t)(h->call + 2)));
+    UpdateParams P = update_params(h, lr, flags, beta2, eps);
+    h->call++;
+    LayerView v = h->view();
+    if (h->total_nnz > 0) {
+        launch_backward_sparse(v, h->xT.p, h->dyT.p, h->presT.p, batch, P, h->sgs.p, h->sgc.p, h->dxT.p, s);
+        if (lr != 0.0f) {
+            h->st_pending = true;
+            launch_sparse_scale_update(v, h->sgs.p, h->sgc.p, P, s);
+        }
+    } else {
+        CK(cudaMemsetAsync(h->dxT.p, 0, (size_t)batch * n_in * 4, s));
+    }
+    const bool dev_out = is_device_ptr(dx);
+    float* dxd = dx;
+    DBuf<float> dxtmp;
+    if (!dev_out) {
+        RC(dxtmp.reserve((int64_t)batch * n_in + 1));
+        dxd = dxtmp.p;
+    }
+    launch_transpose(h->dxT.p, dxd, n_in, batch, s);
+    CK(cudaGetLastError());
+    if (!dev_out) CK(cudaMemcpyAsync(dx, dxd, (size_t)batch * n_in * 4, cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    return SILI_OK;
+}
+
+// ── synaptogenesis: probes ──────────────────────────────────────────────────
+// delta_csr_build_probes (delta_csr_memory.hpp:1308-1427).  Top-k by a stable
+// descending radix sort (ties keep ascending index; the reference's
+// partial_sort leaves tie order unspecified).
+static int sorted_desc(sili_layer* h, const float* keys, int64_t n, DBuf<int>& out_idx) {
+    cudaStream_t s = h->stream;
+    DBuf<float> ko;
+    DBuf<int> vin;
+    RC(ko.reserve(n + 1)); RC(vin.reserve(n + 1)); RC(out_idx.reserve(n + 1));
+    launch_iota(vin.p, n, s);
+    size_t bytes = 0;
+    cub::DeviceRadixSort::SortPairsDescending(nullptr, bytes, keys, ko.p, vin.p, out_idx.p, (int)n, 0, 32, s);
+    RC(h->cub_tmp.reserve((int64_t)bytes + 1));
+    CK(cub::DeviceRadixSort::SortPairsDescending(h->cub_tmp.p, bytes, keys, ko.p, vin.p, out_idx.p, (int)n, 0, 32, s));
+    return SILI_OK;
+}
+
+int sili_layer_build_probes(sili_layer* h, int k, int per_row) {
+    RC(use(h));
+    if (k > 0 && (int64_t)k * std::min<int64_t>(k, h->rows) > (int64_t)1 << 30)
+        return fail(SILI_EINVAL, "build_probes: k too large");
+    cudaStream_t s = h->stream;
+    const int64_t R = h->rows, C = h->cols;
+    h->n_probes = 0;
+    if (R == 0 || C == 0 || k <= 0) return SILI_OK;
+    RC(ensure_aux(h, s));
+    const int kin = (int)std::min<int64_t>(k, R);
+    DBuf<int> in_sorted, out_sorted;
+    RC(sorted_desc(h, h->in_acc.p, R, in_sorted));
+    RC(sorted_desc(h, h->grad_acc.p, C, out_sorted));
+    LayerView v = h->view();
+    if (!per_row) {
+        const int kout = (int)std::min<int64_t>(k, C);
+        const int64_t n = (int64_t)kin * kout;
+        DBuf<int> flags, pos;
+        RC(flags.reserve(n + 1)); RC(pos.reserve(n + 1));
+        CK(cudaMemsetAsync(flags.p, 0, (size_t)(n + 1) * 4, s));
+        launch_probe_flags(v, in_sorted.p, kin, out_sorted.p, kout, flags.p, s);
+        RC(scan_excl_int(h, flags.p, pos.p, n + 1, s));
+        int total = 0;
+        CK(cudaMemcpyAsync(&total, pos.p + n, 4, cudaMemcpyDeviceToHost, s));
+        CK(cudaStreamSynchronize(s));
+        RC(h->prow.reserve(total + 1)); RC(h->pcol.reserve(total + 1)); RC(h->pval.reserve(total + 1));
+        launch_probe_emit(in_sorted.p, kin, out_sorted.p, kout, flags.p, pos.p, h->in_acc.p, h->grad_acc.p,
+                          h->prow.p, h->pcol.p, h->pval.p, s);
+        h->n_probes = total;
+    } else {
+        const int64_t cap = (int64_t)kin * k;
+        DBuf<int> tr, tc, counts;
+        DBuf<float> tv;
+        RC(tr.reserve(cap + 1)); RC(tc.reserve(cap + 1)); RC(tv.reserve(cap + 1)); RC(counts.reserve(kin + 1));
+        launch_probe_per_row(v, in_sorted.p, kin, out_sorted.p, C, k, h->in_acc.p, h->grad_acc.p, tr.p, tc.p, tv.p,
+                             counts.p, s);
+        std::vector<int> hc(kin);
+        CK(cudaMemcpyAsync(hc.data(), counts.p, (size_t)kin * 4, cudaMemcpyDeviceToHost, s));
+        CK(cudaStreamSynchronize(s));
+        int64_t total = 0;
+        for (int a = 0; a < kin; ++a) total += hc[a];
+        RC(h->prow.reserve(total + 1)); RC(h->pcol.reserve(total + 1)); RC(h->pval.reserve(total + 1));
+        int64_t o = 0;
+        for (int a = 0; a < kin; ++a) {
+            if (!hc[a]) continue;
+            const size_t off = (size_t)a * k;
+            CK(cudaMemcpyAsync(h->prow.p + o, tr.p + off, (size_t)hc[a] * 4, cudaMemcpyDeviceToDevice, s));
+            CK(cudaMemcpyAsync(h->pcol.p + o, tc.p + off, (size_t)hc[a] * 4, cudaMemcpyDeviceToDevice, s));
+            CK(cudaMemcpyAsync(h->pval.p + o, tv.p + off, (size_t)hc[a] * 4, cudaMemcpyDeviceToDevice, s));
+            o += hc[a];
+        }
+        h->n_probes = total;
+    }
+    CK(cudaGetLastError());
+    CK(cudaStreamSynchronize(s));
+    return SILI_OK;
+}
+
+int sili_layer_num_probes(sili_layer* h, int64_t* n) {
+    RC(use(h));
+    *n = h->n_probes;
+    return SILI_OK;
+}
+
+int sili_layer_get_probes(sili_layer* h, int* rows, int* cols, float* scores) {
+    RC(use(h));
+    const size_t n = (size_t)h->n_probes;
+    RC(from_dev(h->prow.p, rows, n * 4, h->stream));
+    RC(from_dev(h->pcol.p, cols, n * 4, h->stream));
+    RC(from_dev(h->pval.p, scores, n * 4, h->stream));
+    CK(cudaStreamSynchronize(h->stream));
+    return SILI_OK;
+}
+
+int sili_layer_synap_rows(sili_layer* h, int row0, int nrows, float importance_cutoff, int max_row_weights,
+                          int max_prune_per_step, float importance_eps, int* did_any) {
+    RC(use(h));
+    (void)row0; (void)nrows; (void)importance_cutoff; (void)max_row_weights; (void)max_prune_per_step;
+    (void)importance_eps; (void)did_any;
+    return fail(SILI_EINVAL, "synap_rows: not built yet");
+}
+
+// ── headroom management ─────────────────────────────────────────────────────
+// delta_csr_shift_row (delta_csr_memory.hpp:225-293) for one row: the tail of
+// both buffers after the row moves by the allocation change (a memmove, as in
+// the reference, so blank bytes keep their old contents).
+static int shift_row(sili_layer* h, HostLayout& L, int64_t row, int64_t tb, int64_t te) {
+    cudaStream_t s = h->stream;
+    const int64_t R = h->rows;
+    const int64_t cb = L.bs[row + 1] - L.bs[row];
+    if (cb != tb && row + 1 < R) {
+        const int64_t src = L.bs[row + 1], len = L.bs[R] - src, dst = L.bs[row] + tb;
+        int64_t nt = h->idx_n;
+        if (tb > cb) {
+            nt = h->idx_n + (tb - cb);
+            if (nt > h->max_idx_bytes) return fail(SILI_ENOMEM, "std::bad_alloc");
+            RC(h->idx.grow(nt + 64, h->idx_n, s));
+            CK(cudaMemsetAsync(h->idx.p + h->idx_n, 0, (size_t)(nt - h->idx_n), s));
+        }
+        if (len > 0) {
+            DBuf<uint8_t> tmp;
+            RC(tmp.reserve(len));
+            CK(cudaMemcpyAsync(tmp.p, h->idx.p + src, (size_t)len, cudaMemcpyDeviceToDevice, s));
+            CK(cudaMemcpyAsync(h->idx.p + dst, tmp.p, (size_t)len, cudaMemcpyDeviceToDevice, s));
+            CK(cudaStreamSynchronize(s));
+        }
+        if (tb < cb) nt = h->idx_n - (cb - tb);
+        h->idx_n = nt;
+        const int64_t d = tb - cb;
+        for (int64_t r = row + 1; r <= R; ++r) L.bs[r] += d;
+        for (int64_t r = row + 1; r < R; ++r) L.be[r] += d;
+    }
+    const int64_t ce = L.es[row + 1] - L.es[row];
+    if (ce != te && row + 1 < R) {
+        const int64_t src = L.es[row + 1], len = L.es[R] - src, dst = L.es[row] + te;
+        const int64_t cur = L.es[R];
+        if (te > ce) {
+            const int64_t nt = cur + (te - ce);
+            if (nt > h->max_val_bytes) { RC(put_layout(h, L)); return fail(SILI_ENOMEM, "std::bad_alloc"); }
+            RC(h->val.grow(nt + 64, h->val_n, s));
+            CK(cudaMemsetAsync(h->val.p + h->val_n, 0, (size_t)(nt - h->val_n), s));
+            h->val_n = nt;
+        }
+        if (len > 0) {
+            DBuf<uint8_t> tmp;
+            RC(tmp.reserve(len));
+            CK(cudaMemcpyAsync(tmp.p, h->val.p + src, (size_t)len, cudaMemcpyDeviceToDevice, s));
+            CK(cudaMemcpyAsync(h->val.p + dst, tmp.p, (size_t)len, cudaMemcpyDeviceToDevice, s));
+            CK(cudaStreamSynchronize(s));
+        }
+        if (te < ce) h->val_n = cur - (ce - te);
+        const int64_t d = te - ce;
+        for (int64_t r = row + 1; r <= R; ++r) L.es[r] += d;
+        for (int64_t r = row + 1; r < R; ++r) L.ee[r] += d;
+    }
+    return SILI_OK;
+}
+
+int sili_layer_equalize_row(sili_layer* h, int row_in) {
+    RC(use(h));
+    if (h->rows == 0) return SILI_OK;
+    const int64_t R = h->rows, row = row_in % R;
+    HostLayout L;
+    RC(get_layout(h, L));
+    const int64_t tb = (L.bs[R] + R - 1) / R, te = (L.es[R] + R - 1) / R;
+    const int rc = shift_row(h, L, row, tb, te);
+    RC(put_layout(h, L));
+    h->aux_dirty = true;
+    return rc;
+}
+
+// equalize_to_capacity (cpu_backend.cpp:684-729).  The reference shifts rows
+// one by one; the final allocations are max(current, target) per row, so the
+// arrays are rebuilt once.  A budget failure leaves the rows before the
+// failing one grown, as the reference's sequence of shifts would.
+int sili_layer_equalize_to_capacity(sili_layer* h, int target_elems, int target_bytes) {
+    RC(use(h));
+    const int64_t R = h->rows;
+    const int64_t te = target_elems, tb = target_bytes > 0 ? target_bytes : te * 5 + 4;
+    HostLayout L;
+    RC(get_layout(h, L));
+    HostLayout N = L;
+    int64_t idx_total = h->idx_n, val_total = L.es[R];
+    int status = SILI_OK;
+    std::vector<int64_t> ab(R), ae(R);
+    for (int64_t r = 0; r < R; ++r) { ab[r] = L.bs[r + 1] - L.bs[r]; ae[r] = L.es[r + 1] - L.es[r]; }
+    for (int64_t r = 0; r + 1 < R; ++r) {
+        const int64_t ub = std::max(ab[r], tb), ue = std::max(ae[r], te);
+        if (ub == ab[r] && ue == ae[r]) continue;
+        if (ub > ab[r]) {
+            if (idx_total + (ub - ab[r]) > h->max_idx_bytes) { status = SILI_ENOMEM; break; }
+            idx_total += ub - ab[r];
+        }
+        ab[r] = ub;
+        if (ue > ae[r]) {
+            if (val_total + (ue - ae[r]) > h->max_val_bytes) { status = SILI_ENOMEM; break; }
+            val_total += ue - ae[r];
+        }
+        ae[r] = ue;
+    }
+    if (status == SILI_OK && R > 0) {
+        const int64_t r = R - 1;
+        const int64_t ub = std::max(ab[r], tb), ue = std::max(ae[r], te);
+        if (ub > ab[r]) { idx_total += ub - ab[r]; ab[r] = ub; }
+        if (ue > ae[r]) { val_total += ue - ae[r]; ae[r] = ue; }
+    }
+    for (int64_t r = 0; r < R; ++r) {
+        N.bs[r + 1] = N.bs[r] + ab[r];
+        N.be[r] = N.bs[r] + (L.be[r] - L.bs[r]);
+        N.es[r + 1] = N.es[r] + ae[r];
+        N.ee[r] = N.es[r] + (L.ee[r] - L.es[r]);
+    }
+    RC(relayout(h, N, N.bs[R], N.es[R], false));
+    if (status) return fail(status, "std::bad_alloc");
+    return SILI_OK;
+}
+
+// compact (sisldo_ops.hpp:44-96): rows packed back to back, zero headroom.
+int sili_layer_compact(sili_layer* h) {
+    RC(use(h));
+    const int64_t R = h->rows;
+    HostLayout L, N;
+    RC(get_layout(h, L));
+    N = L;
+    N.bs[0] = N.es[0] = 0;
+    for (int64_t r = 0; r < R; ++r) {
+        N.be[r] = N.bs[r] + (L.be[r] - L.bs[r]);
+        N.bs[r + 1] = N.be[r];
+        N.ee[r] = N.es[r] + (L.ee[r] - L.es[r]);
+        N.es[r + 1] = N.ee[r];
+    }
+    return relayout(h, N, N.bs[R], N.es[R], true);
+}
+
+// expand_headroom / expand_headroom_to (sisldo_ops.hpp:127-186): the
+// delta_csr_from_absolute layout of the live content, after the same budget
+// requests the reference makes against the layer's limits.
+static int expand(sili_layer* h, int64_t budget, float bf) {
+    const double f = 1.0 + (double)bf;
+    const int64_t ibytes = (int64_t)((double)budget * f * 6.0 + 4096.0);
+    const int64_t vbytes = (int64_t)((double)budget * f) + 64;
+    if (vbytes > h->max_val_bytes || ibytes > h->max_idx_bytes) return fail(SILI_ENOMEM, "std::bad_alloc");
+    const int64_t R = h->rows;
+    HostLayout L, N;
+    RC(get_layout(h, L));
+    N = L;
+    N.bs[0] = N.es[0] = 0;
+    for (int64_t r = 0; r < R; ++r) {
+        const int64_t nb = L.be[r] - L.bs[r], n = L.ee[r] - L.es[r];
+        N.be[r] = N.bs[r] + nb;
+        N.bs[r + 1] = N.be[r] + (int64_t)((float)nb * bf) + 5;
+        N.ee[r] = N.es[r] + n;
+        N.es[r + 1] = N.ee[r] + std::max<int64_t>(1, (int64_t)((float)n * bf) + 1);
+    }
+    RC(relayout(h, N, N.bs[R], N.es[R], true));
+    h->max_idx_bytes = h->idx_budget;
+    h->max_val_bytes = h->val_budget;
+    return SILI_OK;
+}
+int sili_layer_expand_headroom(sili_layer* h, float bf) {
+    RC(use(h));
+    return expand(h, h->total_nnz, bf);
+}
+int sili_layer_expand_headroom_to(sili_layer* h, int min_nnz_per_row, float bf) {
+    RC(use(h));
+    return expand(h, std::max<int64_t>(h->total_nnz, h->rows * (int64_t)min_nnz_per_row), bf);
+}
+
+int sili_layer_zero_accum(sili_layer* h) {
+    RC(use(h));
+    CK(cudaMemsetAsync(h->in_acc.p, 0, (size_t)h->rows * 4, h->stream));
+    CK(cudaMemsetAsync(h->grad_acc.p, 0, (size_t)h->cols * 4, h->stream));
+    CK(cudaStreamSynchronize(h->stream));
+    return SILI_OK;
+}
+
+int sili_layer_topk_dyx_step(sili_layer* h, const float* x, const float* dy, int batch, int64_t k, void* stream) {
+    RC(use(h));
+    (void)x; (void)dy; (void)batch; (void)k; (void)stream;
+    return fail(SILI_EINVAL, "topk_dyx_step: not built yet");
+}
+
+// ── export ──────────────────────────────────────────────────────────────────
+int sili_layer_sizes(sili_layer* h, int64_t* sizes) {
+    RC(use(h));
+    sizes[0] = h->rows; sizes[1] = h->cols; sizes[2] = h->total_nnz;
+    sizes[3] = h->idx_n; sizes[4] = h->val_n; sizes[5] = 0;
+    return SILI_OK;
+}
+
+int sili_layer_export(sili_layer* h, int* ptrs, int* idx, float* w, float* imp) {
+    RC(use(h));
+    cudaStream_t s = h->stream;
+    RC(ensure_aux(h, s));
+    const int64_t nnz = h->total_nnz;
+    DBuf<int> di;
+    DBuf<float> dw, dm;
+    RC(di.reserve(nnz + 1)); RC(dw.reserve(nnz + 1)); RC(dm.reserve(nnz + 1));
+    launch_export(h->view(), di.p, dw.p, dm.p, s);
+    CK(cudaGetLastError());
+    RC(from_dev(h->rowptr.p, ptrs, (size_t)(h->rows + 1) * 4, s));
+    RC(from_dev(di.p, idx, (size_t)nnz * 4, s));
+    RC(from_dev(dw.p, w, (size_t)nnz * 4, s));
+    RC(from_dev(dm.p, imp, (size_t)nnz * 4, s));
+    CK(cudaStreamSynchronize(s));
+    return SILI_OK;
+}
+
+int sili_layer_raw(sili_layer* h, int64_t* bs, int64_t* be, int64_t* es, int64_t* ee, uint8_t* indices,
+                   uint8_t* values) {
+    RC(use(h));
+    cudaStream_t s = h->stream;
+    const size_t R = (size_t)h->rows;
+    RC(from_dev(h->bs.p, bs, (R + 1) * 8, s));
+    RC(from_dev(h->be.p, be, R * 8, s));
+    RC(from_dev(h->es.p, es, (R + 1) * 8, s));
+    RC(from_dev(h->ee.p, ee, R * 8, s));
+    RC(from_dev(h->idx.p, indices, (size_t)h->idx_n, s));
+    RC(from_dev(h->val.p, values, (size_t)h->val_n, s));
+    CK(cudaStreamSynchronize(s));
+    return SILI_OK;
+}
+
+int sili_layer_accums(sili_layer* h, float* a, float* g) {
+    RC(use(h));
+    RC(from_dev(h->in_acc.p, a, (size_t)h->rows * 4, h->stream));
+    RC(from_dev(h->grad_acc.p, g, (size_t)h->cols * 4, h->stream));
+    CK(cudaStreamSynchronize(h->stream));
+    return SILI_OK;
+}
+
+int sili_layer_set_accums(sili_layer* h, const float* a, const float* g) {
+    RC(use(h));
+    if (a) RC(to_dev(a, h->in_acc.p, (size_t)h->rows * 4, h->stream));
+    if (g) RC(to_dev(g, h->grad_acc.p, (size_t)h->cols * 4, h->stream));
+    CK(cudaStreamSynchronize(h->stream));
+    return SILI_OK;
+}
+
+int sili_layer_out_degree(sili_layer* h, int* out) {
+    RC(use(h));
+    RC(from_dev(h->out_degree.p, out, (size_t)h->cols * 4, h->stream));
+    CK(cudaStreamSynchronize(h->stream));
+    return SILI_OK;
+}
+
+int sili_layer_stats(sili_layer* h, double* stats) {
+    RC(use(h));
+    CK(cudaStreamSynchronize(h->stream));
+    RC(flush_stats(h));
+    stats[0] = h->st[0]; stats[1] = h->st[1]; stats[2] = h->st_vmax;
+    stats[3] = h->st[2]; stats[4] = h->st[3]; stats[5] = h->st_imax;
+    return SILI_OK;
+}
+
+int sili_layer_recompute_stats(sili_layer* h) {
+    RC(use(h));
+    return recompute_stats(h);
+}
+
+int sili_layer_last_input(sili_layer* h, float* out, int* batch, int* cols) {
+    RC(use(h));
+    if (batch) *batch = h->last_batch;
+    if (cols) *cols = (int)h->rows;
+    if (out && h->last_batch > 0) {
+        DBuf<float> t;
+        RC(t.reserve((int64_t)h->last_batch * h->rows + 1));
+        launch_transpose(h->xT.p, t.p, h->rows, h->last_batch, h->stream);
+        RC(from_dev(t.p, out, (size_t)h->last_batch * h->rows * 4, h->stream));
+        CK(cudaStreamSynchronize(h->stream));
+    }
+    return SILI_OK;
+}
+
+// ── module functions ────────────────────────────────────────────────────────
+int sili_fp4_quantize(const float* vals, uint8_t* codes, int64_t n, void* stream) {
+    if (n < 0) return fail(SILI_EINVAL, "negative size");
+    if (n == 0) return SILI_OK;
+    cudaStream_t s = (cudaStream_t)stream;
+    float* dv = nullptr;
+    uint8_t* dc = nullptr;
+    CK(cudaMallocAsync((void**)&dv, (size_t)n * 4, s));
+    CK(cudaMallocAsync((void**)&dc, (size_t)n, s));
+    RC(to_dev(vals, dv, (size_t)n * 4, s));
+    launch_fp4_quantize(dv, dc, n, s);
+    RC(from_dev(dc, codes, (size_t)n, s));
+    cudaFreeAsync(dv, s);
+    cudaFreeAsync(dc, s);
+    CK(cudaStreamSynchronize(s));
+    return SILI_OK;
+}
+
+int sili_dense_to_csr(const float* x, int rows, int cols, float thr, int* ptrs, int* idx, float* vals,
+                      int64_t* nnz_out, void* stream) {
+    if (rows < 0 || cols < 0) return fail(SILI_EINVAL, "negative size");
+    cudaStream_t s = (cudaStream_t)stream;
+    const size_t n = (size_t)rows * cols;
+    float* dx = nullptr;
+    int *dcount = nullptr, *dptrs = nullptr;
+    CK(cudaMallocAsync((void**)&dx, n * 4 + 4, s));
+    CK(cudaMallocAsync((void**)&dcount, (size_t)(rows + 1) * 4, s));
+    CK(cudaMallocAsync((void**)&dptrs, (size_t)(rows + 1) * 4, s));
+    RC(to_dev(x, dx, n * 4, s));
+    CK(cudaMemsetAsync(dcount, 0, (size_t)(rows + 1) * 4, s));
+    launch_dense_to_csr_count(dx, rows, cols, thr, dcount, s);
+    size_t bytes = 0;
+    cub::DeviceScan::ExclusiveSum(nullptr, bytes, dcount, dptrs, rows + 1, s);
+    void* tmp = nullptr;
+    CK(cudaMallocAsync(&tmp, bytes + 1, s));
+    CK(cub::DeviceScan::ExclusiveSum(tmp, bytes, dcount, dptrs, rows + 1, s));
+    int total = 0;
+    CK(cudaMemcpyAsync(&total, dptrs + rows, 4, cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    if (nnz_out) *nnz_out = total;
+    RC(from_dev(dptrs, ptrs, (size_t)(rows + 1) * 4, s));
+    if (idx && vals) {
+        int* di = nullptr;
+        float* dv = nullptr;
+        CK(cudaMallocAsync((void**)&di, (size_t)total * 4 + 4, s));
+        CK(cudaMallocAsync((void**)&dv, (size_t)total * 4 + 4, s));
+        launch_dense_to_csr_fill(dx, rows, cols, thr, dptrs, di, dv, s);
+        RC(from_dev(di, idx, (size_t)total * 4, s));
+        RC(from_dev(dv, vals, (size_t)total * 4, s));
+        cudaFreeAsync(di, s);
+        cudaFreeAsync(dv, s);
+    }
+    cudaFreeAsync(tmp, s);
+    cudaFreeAsync(dx, s);
+    cudaFreeAsync(dcount, s);
+    cudaFreeAsync(dptrs, s);
+    CK(cudaStreamSynchronize(s));
+    return SILI_OK;
+}
+
+// dense_to_top_k_csr: stable descending radix sort of |v| (ties -> lower flat
+// index), first k, re-sorted by flat index, emitted as row-major CSR.
+int sili_dense_to_top_k_csr(const float* x, int rows, int cols, int64_t k, int* ptrs, int* idx, float* vals,
+                            void* stream) {
+    if (rows < 0 || cols < 0 || k < 0) return fail(SILI_EINVAL, "negative size");
+    cudaStream_t s = (cudaStream_t)stream;
+    const int64_t n = (int64_t)rows * cols;
+    if (k > n) k = n;
+    float* dx = nullptr;
+    uint32_t *keys = nullptr, *keys_o = nullptr;
+    int *ids = nullptr, *ids_o = nullptr, *fl = nullptr, *fl_o = nullptr, *rc = nullptr, *dptrs = nullptr;
+    int* di = nullptr;
+    float* dv = nullptr;
+    const size_t nn = (size_t)n + 1;
+    CK(cudaMallocAsync((void**)&dx, nn * 4, s));
+    CK(cudaMallocAsync((void**)&keys, nn * 4, s));
+    CK(cudaMallocAsync((void**)&keys_o, nn * 4, s));
+    CK(cudaMallocAsync((void**)&ids, nn * 4, s));
+    CK(cudaMallocAsync((void**)&ids_o, nn * 4, s));
+    CK(cudaMallocAsync((void**)&fl, (size_t)k * 4 + 4, s));
+    CK(cudaMallocAsync((void**)&fl_o, (size_t)k * 4 + 4, s));
+    CK(cudaMallocAsync((void**)&rc, (size_t)(rows + 1) * 4, s));
+    CK(cudaMallocAsync((void**)&dptrs, (size_t)(rows + 1) * 4, s));
+    CK(cudaMallocAsync((void**)&di, (size_t)k * 4 + 4, s));
+    CK(cudaMallocAsync((void**)&dv, (size_t)k * 4 + 4, s));
+    RC(to_dev(x, dx, (size_t)n * 4, s));
+    launch_abs_keys(dx, n, keys, ids, s);
+    size_t b1 = 0, b2 = 0, b3 = 0;
+    cub::DeviceRadixSort::SortPairsDescending(nullptr, b1, keys, keys_o, ids, ids_o, (int)n, 0, 32, s);
+    cub::DeviceRadixSort::SortKeys(nullptr, b2, fl, fl_o, (int)k, 0, 32, s);
+    cub::DeviceScan::ExclusiveSum(nullptr, b3, rc, dptrs, rows + 1, s);
+    const size_t bytes = std::max(b1, std::max(b2, b3)) + 1;
+    void* tmp = nullptr;
+    CK(cudaMallocAsync(&tmp, bytes, s));
+    size_t bb = bytes;
+    CK(cub::DeviceRadixSort::SortPairsDescending(tmp, bb, keys, keys_o, ids, ids_o, (int)n, 0, 32, s));
+    CK(cudaMemcpyAsync(fl, ids_o, (size_t)k * 4, cudaMemcpyDeviceToDevice, s));
+    bb = bytes;
+    CK(cub::DeviceRadixSort::SortKeys(tmp, bb, fl, fl_o, (int)k, 0, 32, s));
+    CK(cudaMemsetAsync(rc, 0, (size_t)(rows + 1) * 4, s));
+    launch_topk_emit(dx, fl_o, k, cols, rc, di, dv, s);
+    bb = bytes;
+    CK(cub::DeviceScan::ExclusiveSum(tmp, bb, rc, dptrs, rows + 1, s));
+    RC(from_dev(dptrs, ptrs, (size_t)(rows + 1) * 4, s));
+    RC(from_dev(di, idx, (size_t)k * 4, s));
+    RC(from_dev(dv, vals, (size_t)k * 4, s));
+    CK(cudaStreamSynchronize(s));
+    for (void* p : {(void*)dx, (void*)keys, (void*)keys_o, (void*)ids, (void*)ids_o, (void*)fl, (void*)fl_o,
+                    (void*)rc, (void*)dptrs, (void*)di, (void*)dv, tmp})
+        cudaFreeAsync(p, s);
+    CK(cudaStreamSynchronize(s));
+    return SILI_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,433 @@
+// sili__new_b200._cuda: the drop-in counterpart of the reference's pybind11
+// module sili._cpu (sili/cpu_backend.cpp:1425-3246) for the FP4 delta-CSR
+// sparse layer.  Same class names, method names, argument names and defaults;
+// every call goes through the C ABI of libsili_b200 (include/sili_b200.h),
+// whose compute runs on the GPU.  Host numpy arrays are copied in and fresh
+// numpy arrays are returned, as the reference does (cpu_backend.cpp:487-491).
+// The *_ptr methods take device pointers (e.g. torch CUDA tensors'
+// data_ptr()) and enqueue work on a CUDA stream without copies.
+#include <pybind11/numpy.h>
+#include <pybind11/pybind11.h>
+
+#include <cmath>
+#include <cstdint>
+#include <mutex>
+#include <set>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../../include/sili_b200.h"
+
+namespace py = pybind11;
+
+namespace {
+
+void check(int rc) {
+    if (rc == SILI_OK) return;
+    const std::string msg = sili_last_error();
+    if (rc == SILI_EINVAL) throw py::value_error(msg);
+    if (rc == SILI_ENOMEM) {
+        PyErr_SetString(PyExc_MemoryError, msg.c_str());
+        throw py::error_already_set();
+    }
+    throw std::runtime_error(msg);
+}
+
+using farr = py::array_t<float, py::array::c_style | py::array::forcecast>;
+using iarr = py::array_t<int, py::array::c_style | py::array::forcecast>;
+using u8arr = py::array_t<uint8_t, py::array::c_style | py::array::forcecast>;
+
+std::mutex g_live_mu;
+std::set<sili_layer*> g_live;
+uint64_t g_seed = 0x5EEDu;
+bool g_seeded = false;
+
+class Layer;
+
+struct Block4View {
+    // block4 tiles are not built by this library yet: the scattered
+    // delta-CSR holds every synapse, so the view reports an empty store.
+    std::size_t tiles() const { return 0; }
+    std::size_t synapses() const { return 0; }
+    uint32_t switch_point = 10;
+};
+
+class Layer {
+public:
+    sili_layer* h = nullptr;
+    int n_in, n_out, cpus;
+    int synap_row = 0, eq_row = 0;
+
+    Layer(int n_inputs, int n_outputs, int max_weights, int num_cpus, bool stochastic, int device)
+        : n_in(n_inputs), n_out(n_outputs), cpus(num_cpus) {
+        check(sili_layer_create(n_inputs, n_outputs, max_weights, device, stochastic ? 1 : 0, &h));
+        std::lock_guard<std::mutex> g(g_live_mu);
+        g_live.insert(h);
+        if (g_seeded) sili_layer_seed_rng(h, g_seed);
+    }
+    ~Layer() {
+        {
+            std::lock_guard<std::mutex> g(g_live_mu);
+            g_live.erase(h);
+        }
+        sili_layer_destroy(h);
+    }
+
+    int get_scale_rank() const {
+        int r;
+        check(sili_layer_get_scale_rank(h, &r));
+        return r;
+    }
+    void set_scale_rank(int r) { check(sili_layer_set_scale_rank(h, r)); }
+
+    py::array_t<float> forward_dense(farr x) {
+        auto b = x.request();
+        const int batch = b.ndim == 2 ? (int)b.shape[0] : 1;
+        const int cols = b.ndim == 2 ? (int)b.shape[1] : (int)b.shape[0];
+        if (cols != n_in) throw py::value_error("forward_dense: x has " + std::to_string(cols) + " features, layer has " + std::to_string(n_in));
+        py::array_t<float> y({(py::ssize_t)batch, (py::ssize_t)n_out});
+        check(sili_layer_forward_dense(h, (const float*)b.ptr, batch, y.mutable_data(), nullptr));
+        return y;
+    }
+
+    py::array_t<float> backward_dense(farr dy, float lr, bool lr_per_row_nnz, bool damp, float beta2, float eps) {
+        auto b = dy.request();
+        int batch = 0, cols = 0;
+        check(sili_layer_last_input(h, nullptr, &batch, &cols));
+        if (batch == 0) throw std::runtime_error("backward_dense: no forward_dense input to differentiate");
+        if ((int64_t)b.size != (int64_t)batch * n_out) throw py::value_error("backward_dense: dy shape does not match the last forward");
+        warn_lr(lr);
+        py::array_t<float> dx({(py::ssize_t)batch, (py::ssize_t)n_in});
+        unsigned flags = (lr_per_row_nnz ? SILI_LR_PER_ROW_NNZ : 0u) | (damp ? SILI_DAMP_BY_IMPORTANCE : 0u);
+        check(sili_layer_backward_dense(h, nullptr, (const float*)b.ptr, batch, lr, flags, beta2, eps,
+                                        dx.mutable_data(), nullptr));
+        return dx;
+    }
+
+    // cpu_backend.cpp:28-41: one-time warning above the validated lr range.
+    static void warn_lr(float lr) {
+        static bool warned = false;
+        if (!warned && lr > 0.2f) {
+            warned = true;
+            std::fprintf(stderr,
+                "sili: WARNING -- backward() called with learning_rate=%.4f, above the ~0.2 ceiling the "
+                "bounded RMSprop synapse policy's max_abs_delta=2.0 was validated for.\n", lr);
+        }
+    }
+
+    py::array_t<float> forward_sparse(iarr ptrs, iarr idx, farr vals, int batch) {
+        auto pi = idx.request();
+        if ((int)ptrs.size() < batch + 1) throw py::value_error("forward_sparse: ptrs shorter than batch+1");
+        py::array_t<float> y({(py::ssize_t)batch, (py::ssize_t)n_out});
+        check(sili_layer_forward_sparse(h, ptrs.data(), idx.data(), vals.data(), (int)pi.size, batch,
+                                        y.mutable_data(), nullptr));
+        return y;
+    }
+
+    py::array_t<float> backward_sparse(farr x, iarr dptrs, iarr didx, farr dvals, int batch, float lr,
+                                       bool lr_per_row_nnz, bool damp, float beta2, float eps) {
+        if ((int64_t)x.size() != (int64_t)batch * n_in) throw py::value_error("backward_sparse: x must be [batch, n_inputs]");
+        py::array_t<float> dx({(py::ssize_t)batch, (py::ssize_t)n_in});
+        unsigned flags = (lr_per_row_nnz ? SILI_LR_PER_ROW_NNZ : 0u) | (damp ? SILI_DAMP_BY_IMPORTANCE : 0u);
+        check(sili_layer_backward_sparse(h, x.data(), dptrs.data(), didx.data(), dvals.data(), (int)didx.size(), batch,
+                                         lr, flags, beta2, eps, dx.mutable_data(), nullptr));
+        return dx;
+    }
+
+    // device-pointer entry points (no copies, stream-ordered)
+    void forward_dense_ptr(uintptr_t x, int batch, uintptr_t y, uintptr_t stream) {
+        check(sili_layer_forward_dense(h, (const float*)x, batch, (float*)y, (void*)stream));
+    }
+    void backward_dense_ptr(uintptr_t dy, int batch, float lr, bool lr_per_row_nnz, bool damp, float beta2, float eps,
+                            uintptr_t dx, uintptr_t stream, uintptr_t x) {
+        unsigned flags = (lr_per_row_nnz ? SILI_LR_PER_ROW_NNZ : 0u) | (damp ? SILI_DAMP_BY_IMPORTANCE : 0u);
+        check(sili_layer_backward_dense(h, (const float*)x, (const float*)dy, batch, lr, flags, beta2, eps, (float*)dx,
+                                        (void*)stream));
+    }
+    void sync() { check(sili_layer_sync(h)); }
+    void set_kernel_timing(bool on) { check(sili_layer_set_kernel_timing(h, on ? 1 : 0)); }
+    py::tuple kernel_ms() {
+        float f = 0.f, b = 0.f;
+        check(sili_layer_kernel_ms(h, &f, &b));
+        return py::make_tuple(f, b);
+    }
+
+    void build_probes(int k, bool per_row) { check(sili_layer_build_probes(h, k, per_row ? 1 : 0)); }
+    py::tuple probes() {
+        int64_t n;
+        check(sili_layer_num_probes(h, &n));
+        py::array_t<int> r((py::ssize_t)n), c((py::ssize_t)n);
+        py::array_t<float> v((py::ssize_t)n);
+        if (n) check(sili_layer_get_probes(h, r.mutable_data(), c.mutable_data(), v.mutable_data()));
+        return py::make_tuple(r, c, v);
+    }
+    bool synap_row_step(int row, float cutoff, int max_rw, int max_prune, float eps) {
+        int did = 0;
+        check(sili_layer_synap_rows(h, row, 1, cutoff, max_rw, max_prune, eps, &did));
+        return did != 0;
+    }
+    bool synap_step(float cutoff, int max_rw, int max_prune, float eps) {
+        const int row = synap_row;
+        synap_row = n_in > 0 ? (synap_row + 1) % n_in : 0;
+        return synap_row_step(row, cutoff, max_rw, max_prune, eps);
+    }
+    void equalizer_step() {
+        const int row = eq_row;
+        eq_row = n_in > 0 ? (eq_row + 1) % n_in : 0;
+        check(sili_layer_equalize_row(h, row));
+    }
+    void equalize_to_capacity(int te, int tb) { check(sili_layer_equalize_to_capacity(h, te, tb)); }
+    void compact() { check(sili_layer_compact(h)); }
+    void expand_headroom(float bf) { check(sili_layer_expand_headroom(h, bf)); }
+    void expand_headroom_to(int m, float bf) { check(sili_layer_expand_headroom_to(h, m, bf)); }
+
+    float gs(int kind, int i, int k) const {
+        float v;
+        check(sili_layer_get_scale(h, kind, i, k, &v));
+        return v;
+    }
+    void ss(int kind, int i, int k, float v) { check(sili_layer_set_scale(h, kind, i, k, v)); }
+    // get_scale, delta_csr_types.hpp:1235-1240
+    float get_scale(int row, int col) const {
+        float s = 0.0f;
+        const int rank = get_scale_rank();
+        for (int k = 0; k < rank; ++k) s = std::fma(gs(SILI_SCALE_VALUE, row, k), gs(SILI_SCALE_OUTPUT, col, k), s);
+        return s;
+    }
+    void rescale_importance(float v) { for (int r = 0; r < n_in; ++r) check(sili_layer_rescale_row(h, SILI_SCALE_IMPORTANCE, r, v)); }
+    void rescale_value(float v) { for (int r = 0; r < n_in; ++r) check(sili_layer_rescale_row(h, SILI_SCALE_VALUE, r, v)); }
+
+    std::vector<double> stats() const {
+        std::vector<double> s(6);
+        check(sili_layer_stats(h, s.data()));
+        return s;
+    }
+    int64_t scattered_nnz() const {
+        int64_t s[6];
+        check(sili_layer_sizes(h, s));
+        return s[2];
+    }
+    // Hoyer's measure from running stats (delta_csr_types.hpp:1371-1378)
+    float hoyer(double l1, double l2_sq) const {
+        const int64_t n = scattered_nnz();
+        if (n <= 1) return 0.0f;
+        const double l2 = std::sqrt(l2_sq);
+        if (l2 <= 0.0) return 1.0f;
+        const double sn = std::sqrt((double)n);
+        return (float)((sn - l1 / l2) / (sn - 1.0));
+    }
+
+    py::tuple export_csr() {
+        int64_t s[6];
+        check(sili_layer_sizes(h, s));
+        py::array_t<int> p((py::ssize_t)n_in + 1), i((py::ssize_t)s[2]);
+        py::array_t<float> w((py::ssize_t)s[2]), m((py::ssize_t)s[2]);
+        check(sili_layer_export(h, p.mutable_data(), i.mutable_data(), w.mutable_data(), m.mutable_data()));
+        return py::make_tuple(p, i, w, m);
+    }
+    py::tuple accums() {
+        py::array_t<float> a((py::ssize_t)n_in), g((py::ssize_t)n_out);
+        check(sili_layer_accums(h, a.mutable_data(), g.mutable_data()));
+        return py::make_tuple(a, g);
+    }
+    void set_accums(farr a, farr g) { check(sili_layer_set_accums(h, a.data(), g.data())); }
+    py::dict raw_state() {
+        int64_t s[6];
+        check(sili_layer_sizes(h, s));
+        py::array_t<int64_t> bs((py::ssize_t)n_in + 1), be((py::ssize_t)n_in), es((py::ssize_t)n_in + 1), ee((py::ssize_t)n_in);
+        py::array_t<uint8_t> ib((py::ssize_t)s[3]), vb((py::ssize_t)s[4]);
+        check(sili_layer_raw(h, bs.mutable_data(), be.mutable_data(), es.mutable_data(), ee.mutable_data(),
+                             ib.mutable_data(), vb.mutable_data()));
+        py::dict d;
+        d["rows"] = n_in; d["cols"] = n_out; d["nnz"] = s[2];
+        d["byte_start"] = bs; d["byte_end"] = be; d["elem_start"] = es; d["elem_end"] = ee;
+        d["indices_buf"] = ib; d["values"] = vb; d["tiles"] = s[5];
+        return d;
+    }
+    py::array_t<float> scales(int kind) {
+        const int rank = get_scale_rank();
+        const int64_t n = (kind == SILI_SCALE_VALUE || kind == SILI_SCALE_VALUE_IMPORTANCE || kind == SILI_SCALE_VALUE_MOMENTUM)
+                              ? (int64_t)n_in * rank
+                              : (kind == SILI_SCALE_IMPORTANCE ? n_in : (kind == SILI_SCALE_OUTPUT_IMPORTANCE ? n_out : (int64_t)n_out * rank));
+        py::array_t<float> out((py::ssize_t)n);
+        check(sili_layer_get_scales(h, kind, out.mutable_data(), (int)n));
+        return out;
+    }
+    py::array_t<uint32_t> steps(int which) {
+        const int64_t n = (int64_t)(which == 0 ? n_in : n_out) * get_scale_rank();
+        py::array_t<uint32_t> out((py::ssize_t)n);
+        check(sili_layer_get_steps(h, which, out.mutable_data(), (int)n));
+        return out;
+    }
+    void set_value_bytes(u8arr b) { check(sili_layer_set_value_bytes(h, b.data(), (int64_t)b.size())); }
+    py::object last_input() {
+        int batch = 0, cols = 0;
+        check(sili_layer_last_input(h, nullptr, &batch, &cols));
+        if (batch == 0) return py::none();
+        py::array_t<float> x({(py::ssize_t)batch, (py::ssize_t)cols});
+        check(sili_layer_last_input(h, x.mutable_data(), &batch, &cols));
+        return x;
+    }
+};
+
+template <bool STOCH>
+struct LayerT : Layer {
+    LayerT(int a, int b, int c, int d, int dev) : Layer(a, b, c, d, STOCH, dev) {}
+};
+
+template <typename T>
+void bind_layer(py::module_& m, const char* name) {
+    py::class_<T>(m, name)
+        .def(py::init<int, int, int, int, int>(), py::arg("n_inputs"), py::arg("n_outputs"), py::arg("max_weights"),
+             py::arg("num_cpus") = 4, py::arg("device") = 0)
+        .def("get_scale_rank", &T::get_scale_rank)
+        .def("set_scale_rank", &T::set_scale_rank, py::arg("rank"))
+        .def("forward_dense", &T::forward_dense, py::arg("x"))
+        .def("backward_dense", &T::backward_dense, py::arg("dy"), py::arg("learning_rate"),
+             py::arg("lr_per_row_nnz") = false, py::arg("damp_by_importance") = true, py::arg("beta2") = 0.999f,
+             py::arg("eps") = 1e-8f)
+        .def("forward_sparse", &T::forward_sparse, py::arg("ptrs"), py::arg("indices"), py::arg("values"), py::arg("batch"))
+        .def("backward_sparse", &T::backward_sparse, py::arg("x"), py::arg("dy_ptrs"), py::arg("dy_indices"),
+             py::arg("dy_values"), py::arg("batch"), py::arg("learning_rate") = 0.01f, py::arg("lr_per_row_nnz") = false,
+             py::arg("damp_by_importance") = true, py::arg("beta2") = 0.999f, py::arg("eps") = 1e-8f)
+        .def("forward_dense_ptr", &T::forward_dense_ptr, py::arg("x_ptr"), py::arg("batch"), py::arg("y_ptr"),
+             py::arg("stream") = 0)
+        .def("backward_dense_ptr", &T::backward_dense_ptr, py::arg("dy_ptr"), py::arg("batch"), py::arg("learning_rate"),
+             py::arg("lr_per_row_nnz") = false, py::arg("damp_by_importance") = true, py::arg("beta2") = 0.999f,
+             py::arg("eps") = 1e-8f, py::arg("dx_ptr") = 0, py::arg("stream") = 0, py::arg("x_ptr") = 0)
+        .def("sync", &T::sync)
+        .def("set_kernel_timing", &T::set_kernel_timing, py::arg("enable"))
+        .def("kernel_ms", &T::kernel_ms)
+        .def("build_probes", &T::build_probes, py::arg("k"), py::arg("per_row") = false)
+        .def("probes", &T::probes)
+        .def("synap_row_step", &T::synap_row_step, py::arg("current_row"), py::arg("importance_cutoff"),
+             py::arg("max_row_weights"), py::arg("max_prune_per_step") = 8, py::arg("importance_eps") = 1e-3f)
+        .def("synap_step", &T::synap_step, py::arg("importance_cutoff"), py::arg("max_row_weights"),
+             py::arg("max_prune_per_step") = 8, py::arg("importance_eps") = 1e-3f)
+        .def("equalizer_step", &T::equalizer_step)
+        .def("equalize_to_capacity", &T::equalize_to_capacity, py::arg("target_elems_per_row"),
+             py::arg("target_bytes_per_row") = 0)
+        .def("compact", &T::compact)
+        .def("expand_headroom", &T::expand_headroom, py::arg("blank_fraction") = 0.2f)
+        .def("expand_headroom_to", &T::expand_headroom_to, py::arg("min_nnz_per_row"), py::arg("blank_fraction") = 0.2f)
+        .def("get_importance_scale", [](T& s, int r) { return s.gs(SILI_SCALE_IMPORTANCE, r, 0); }, py::arg("row"))
+        .def("get_value_scale", [](T& s, int r) { return s.gs(SILI_SCALE_VALUE, r, 0); }, py::arg("row"))
+        .def("get_value_scale_k", [](T& s, int r, int k) { return s.gs(SILI_SCALE_VALUE, r, k); }, py::arg("row"), py::arg("k"))
+        .def("get_output_scale_k", [](T& s, int c, int k) { return s.gs(SILI_SCALE_OUTPUT, c, k); }, py::arg("col"), py::arg("k"))
+        .def("set_value_scale_raw_k", [](T& s, int r, int k, float v) { s.ss(SILI_SCALE_VALUE, r, k, v); },
+             py::arg("row"), py::arg("k"), py::arg("v"))
+        .def("set_output_scale_raw_k", [](T& s, int c, int k, float v) { s.ss(SILI_SCALE_OUTPUT, c, k, v); },
+             py::arg("col"), py::arg("k"), py::arg("v"))
+        .def("get_scale", &T::get_scale, py::arg("row"), py::arg("col"))
+        .def("set_value_scale_raw", [](T& s, int r, float v) { s.ss(SILI_SCALE_VALUE, r, 0, v); }, py::arg("row"), py::arg("scale"))
+        .def("set_importance_scale_raw", [](T& s, int r, float v) { s.ss(SILI_SCALE_IMPORTANCE, r, 0, v); },
+             py::arg("row"), py::arg("scale"))
+        .def("get_output_scale", [](T& s, int c) { return s.gs(SILI_SCALE_OUTPUT, c, 0); }, py::arg("col"))
+        .def("set_output_scale_raw", [](T& s, int c, float v) { s.ss(SILI_SCALE_OUTPUT, c, 0, v); }, py::arg("col"), py::arg("scale"))
+        .def("get_value_scale_importance", [](T& s, int r) { return s.gs(SILI_SCALE_VALUE_IMPORTANCE, r, 0); }, py::arg("row"))
+        .def("get_output_scale_importance", [](T& s, int c) { return s.gs(SILI_SCALE_OUTPUT_SCALE_IMPORTANCE, c, 0); }, py::arg("col"))
+        .def("get_output_importance_scale", [](T& s, int c) { return s.gs(SILI_SCALE_OUTPUT_IMPORTANCE, c, 0); }, py::arg("col"))
+        .def("set_output_importance_scale_raw", [](T& s, int c, float v) { s.ss(SILI_SCALE_OUTPUT_IMPORTANCE, c, 0, v); },
+             py::arg("col"), py::arg("scale"))
+        .def("rescale_importance_row", [](T& s, int r, float v) { check(sili_layer_rescale_row(s.h, SILI_SCALE_IMPORTANCE, r, v)); },
+             py::arg("row"), py::arg("new_scale"))
+        .def("rescale_value_row", [](T& s, int r, float v) { check(sili_layer_rescale_row(s.h, SILI_SCALE_VALUE, r, v)); },
+             py::arg("row"), py::arg("new_scale"))
+        .def("rescale_importance", &T::rescale_importance, py::arg("new_scale"))
+        .def("rescale_value", &T::rescale_value, py::arg("new_scale"))
+        .def_property_readonly("value_l1", [](T& s) { return (float)s.stats()[0]; })
+        .def_property_readonly("value_l2_sq", [](T& s) { return (float)s.stats()[1]; })
+        .def_property_readonly("value_max_abs", [](T& s) { return (float)s.stats()[2]; })
+        .def_property_readonly("importance_l1", [](T& s) { return (float)s.stats()[3]; })
+        .def_property_readonly("importance_l2_sq", [](T& s) { return (float)s.stats()[4]; })
+        .def_property_readonly("importance_max_abs", [](T& s) { return (float)s.stats()[5]; })
+        .def("hoyer_value", [](T& s) { auto st = s.stats(); return s.hoyer(st[0], st[1]); })
+        .def("hoyer_importance", [](T& s) { auto st = s.stats(); return s.hoyer(st[3], st[4]); })
+        .def("recompute_stats", [](T& s) { check(sili_layer_recompute_stats(s.h)); })
+        .def("zero_accum", [](T& s) { check(sili_layer_zero_accum(s.h)); })
+        .def_property_readonly("neuron_input_accum", [](T& s) { return s.accums()[0]; })
+        .def_property_readonly("neuron_grad_accum", [](T& s) { return s.accums()[1]; })
+        .def("accums", &T::accums)
+        .def("set_accums", &T::set_accums, py::arg("input_accum"), py::arg("grad_accum"))
+        .def_property_readonly("weights_vals", [](T& s) { return s.export_csr()[2]; })
+        .def_property_readonly("importance", [](T& s) { return s.export_csr()[3]; })
+        .def_property_readonly("indices", [](T& s) { return s.export_csr()[1]; })
+        .def_property_readonly("ptrs", [](T& s) { return s.export_csr()[0]; })
+        .def("export", &T::export_csr)
+        .def("raw_state", &T::raw_state)
+        .def("scales", &T::scales, py::arg("kind"))
+        .def("steps", &T::steps, py::arg("which"))
+        .def("set_value_bytes", &T::set_value_bytes, py::arg("values"))
+        .def("load_weights", [](T& s, iarr p, iarr i, farr w) {
+            if ((int)p.size() != s.n_in + 1) throw py::value_error("load_weights: ptrs must have n_inputs+1 entries");
+            check(sili_layer_load_weights(s.h, p.data(), i.data(), w.data(), (int)i.size()));
+        }, py::arg("ptrs"), py::arg("indices"), py::arg("weights"))
+        .def_property_readonly("out_degree", [](T& s) {
+            py::array_t<int> o((py::ssize_t)s.n_out);
+            check(sili_layer_out_degree(s.h, o.mutable_data()));
+            return o;
+        })
+        .def_property_readonly("num_cpus", [](T& s) { return s.cpus; })
+        .def_property_readonly("n_inputs", [](T& s) { return s.n_in; })
+        .def_property_readonly("n_outputs", [](T& s) { return s.n_out; })
+        .def_property_readonly("nnz", [](T& s) { return (int)s.scattered_nnz(); })
+        .def_property_readonly("block4", [](T&) { return Block4View(); })
+        .def_property_readonly("last_input", &T::last_input);
+}
+
+}  // namespace
+
+PYBIND11_MODULE(_cuda, m) {
+    m.doc() = "B200 (sm_100a) FP4 delta-CSR sparse layer: drop-in for sili._cpu's SparseLinearLayer";
+    py::class_<Block4View>(m, "Block4View")
+        .def_property_readonly("tiles", &Block4View::tiles)
+        .def_property_readonly("synapses", &Block4View::synapses)
+        .def_readwrite("switch_point", &Block4View::switch_point);
+    bind_layer<LayerT<true>>(m, "SparseLinearLayer");
+    bind_layer<LayerT<false>>(m, "SparseLinearLayerDeterministic");
+    m.attr("SCALE_VALUE") = SILI_SCALE_VALUE;
+    m.attr("SCALE_OUTPUT") = SILI_SCALE_OUTPUT;
+    m.attr("SCALE_IMPORTANCE") = SILI_SCALE_IMPORTANCE;
+    m.attr("SCALE_OUTPUT_IMPORTANCE") = SILI_SCALE_OUTPUT_IMPORTANCE;
+    m.attr("SCALE_VALUE_IMPORTANCE") = SILI_SCALE_VALUE_IMPORTANCE;
+    m.attr("SCALE_OUTPUT_SCALE_IMPORTANCE") = SILI_SCALE_OUTPUT_SCALE_IMPORTANCE;
+    m.attr("SCALE_VALUE_MOMENTUM") = SILI_SCALE_VALUE_MOMENTUM;
+
+    m.def("device_count", []() { int n = 0; sili_device_count(&n); return n; });
+    m.def("kernel_launches", []() { int64_t n = 0; sili_kernel_launches(&n); return n; });
+    m.def("dense_to_csr", [](farr x, float thr) {
+        auto b = x.request();
+        const int rows = b.ndim == 2 ? (int)b.shape[0] : 1;
+        const int cols = b.ndim == 2 ? (int)b.shape[1] : (int)b.shape[0];
+        py::array_t<int> p((py::ssize_t)rows + 1);
+        int64_t n = 0;
+        check(sili_dense_to_csr(x.data(), rows, cols, thr, p.mutable_data(), nullptr, nullptr, &n, nullptr));
+        py::array_t<int> i((py::ssize_t)n);
+        py::array_t<float> v((py::ssize_t)n);
+        check(sili_dense_to_csr(x.data(), rows, cols, thr, p.mutable_data(), i.mutable_data(), v.mutable_data(), &n, nullptr));
+        return py::make_tuple(p, i, v);
+    }, py::arg("x"), py::arg("threshold") = 1e-4f);
+    m.def("dense_to_top_k_csr", [](farr x, int k, int num_threads) {
+        (void)num_threads;
+        auto b = x.request();
+        const int rows = b.ndim == 2 ? (int)b.shape[0] : 1;
+        const int cols = b.ndim == 2 ? (int)b.shape[1] : (int)b.shape[0];
+        const int64_t kk = std::min<int64_t>(std::max(k, 0), (int64_t)rows * cols);
+        py::array_t<int> p((py::ssize_t)rows + 1), i((py::ssize_t)kk);
+        py::array_t<float> v((py::ssize_t)kk);
+        check(sili_dense_to_top_k_csr(x.data(), rows, cols, kk, p.mutable_data(), i.mutable_data(), v.mutable_data(), nullptr));
+        return py::make_tuple(p, i, v);
+    }, py::arg("x"), py::arg("k"), py::arg("num_threads") = 4);
+    m.def("fp4_quantize_array", [](farr v) {
+        py::array_t<uint8_t> out((py::ssize_t)v.size());
+        check(sili_fp4_quantize(v.data(), out.mutable_data(), (int64_t)v.size(), nullptr));
+        return out;
+    }, py::arg("vals"));
+    m.def("seed_fp4_stochastic_rng", [](uint64_t seed) {
+        std::lock_guard<std::mutex> g(g_live_mu);
+        g_seed = seed;
+        g_seeded = true;
+        for (sili_layer* h : g_live) sili_layer_seed_rng(h, seed);
+    }, py::arg("seed"));
+}

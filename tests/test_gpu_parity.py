@@ -1,0 +1,187 @@
+"""CUDA path vs the reference (golden fixtures) and vs the CPU oracle.
+
+Contract (per quantity):
+  * ULEB128 bytes, FP4 codes, row offsets, out_degree, accumulators, probes,
+    value_scale / importance state and steps: bit-exact.
+  * forward y (batch >= 9) and dx at learning_rate == 0: bit-exact (the
+    kernels sum in the reference's single-thread order).
+  * dx at learning_rate != 0, forward at batch <= 8, output_scale (trained from
+    fp32 column sums): within fp32 accumulation tolerance, 1e-5 relative.
+"""
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from helpers import compare_snapshot, random_layer, relu_sparse_x, setup_layer, snapshot
+from replay import assert_close_sum, build, replay_dense
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def load(name):
+    return dict(np.load(os.path.join(GOLD, name + ".npz")))
+
+
+@pytest.fixture(scope="module")
+def S():
+    import sili__new_b200 as S
+    assert S.device_count() > 0
+    return S
+
+
+def det(S):
+    return lambda a, b, c: S.SparseLinearLayerDeterministic(a, b, c)
+
+
+@pytest.mark.parametrize("name", ["dense_small", "dense_rank2_os", "dense_os_train"])
+def test_dense_golden(S, name):
+    fx = load(name)
+    os_trained = "os" in fx and name != "dense_small"
+    for layer, s in replay_dense(det(S), fx, dx_exact=False, dx_rtol=1e-5):
+        snap = snapshot(layer)
+        if os_trained:
+            # output_scale is trained from fp32 column sums whose order differs
+            compare_snapshot(snap, fx, f"s{s}_", skip=("sc_output_scale", "sc_output_scale_importance"))
+            np.testing.assert_allclose(snap["sc_output_scale"], fx[f"s{s}_sc_output_scale"], rtol=1e-5)
+            np.testing.assert_allclose(snap["sc_output_scale_importance"], fx[f"s{s}_sc_output_scale_importance"],
+                                       rtol=1e-4, atol=1e-12)
+            break   # later steps see the (tolerance-equal) output_scale, so codes may legitimately drift
+        compare_snapshot(snap, fx, f"s{s}_")
+        np.testing.assert_allclose(snap["stats"], fx[f"s{s}_stats"], rtol=1e-9)
+
+
+def test_load_layout_golden(S):
+    fx = load("dense_small")
+    layer = build(det(S), fx)
+    compare_snapshot(snapshot(layer), fx, "load_")
+
+
+def test_sparse_golden(S):
+    fx = load("sparse_small")
+    layer = build(det(S), fx)
+    for r in range(int(fx["n_in"][0])):
+        layer.set_importance_scale_raw(r, 0.01 / 6)
+    B = int(fx["B"][0])
+    assert np.array_equal(layer.forward_sparse(fx["px"], fx["ix"], fx["vx"], B), fx["y"])
+    assert_close_sum(layer.backward_sparse(fx["x"], fx["pd"], fx["idd"], fx["vd"], B, 0.0, True), fx["dx0"], 1e-5)
+    assert_close_sum(layer.backward_sparse(fx["x"], fx["pd"], fx["idd"], fx["vd"], B, 0.02, True), fx["dx"], 1e-5)
+    compare_snapshot(snapshot(layer), fx, "after_")
+
+
+@pytest.mark.parametrize("per_row", [0, 1])
+def test_probes_golden(S, per_row):
+    fx = load("probes_small")
+    layer = build(det(S), dict(fx, budget=np.array([len(fx["idx"]) * 3])))
+    layer.forward_dense(fx["x"])
+    layer.backward_dense(fx["dy"], 0.0)
+    layer.build_probes(9, bool(per_row))
+    r, c, v = layer.probes()
+    assert np.array_equal(r, fx[f"pr{per_row}_rows"]) and np.array_equal(c, fx[f"pr{per_row}_cols"])
+    assert np.array_equal(v, fx[f"pr{per_row}_scores"])
+
+
+def test_headroom_golden(S):
+    fx = load("headroom_small")
+    layer = build(det(S), fx)
+    layer.compact()
+    compare_snapshot(snapshot(layer), fx, "compact_")
+    layer.expand_headroom(0.3)
+    compare_snapshot(snapshot(layer), fx, "expand_")
+    layer.expand_headroom_to(12, 0.2)
+    compare_snapshot(snapshot(layer), fx, "expandto_")
+    for _ in range(int(fx["n_in"][0]) + 3):
+        layer.equalizer_step()
+    compare_snapshot(snapshot(layer), fx, "equalize_")
+
+
+def test_sparsifiers_golden(S):
+    fx = load("topk_small")
+    for k in (1, 37, 600):
+        p, i, v = S.dense_to_top_k_csr(fx["x"], k)
+        assert np.array_equal(p, fx[f"k{k}_ptrs"]) and np.array_equal(i, fx[f"k{k}_idx"])
+        assert np.array_equal(v, fx[f"k{k}_vals"])
+    x = fx["x"]
+    for thr in (0.0, 0.5):
+        got, want = S.dense_to_csr(x, thr), O.dense_to_csr(x, thr)
+        for a, b in zip(got, want):
+            assert np.array_equal(a, b)
+
+
+def test_codec_golden(S):
+    fx = load("codec")
+    assert np.array_equal(S.fp4_quantize_array(fx["enc_in"]), fx["enc_out"])
+
+
+# ── larger seeded cases vs the CPU oracle ──────────────────────────────────
+@pytest.mark.parametrize("B", [1, 5, 16, 33, 64])
+def test_forward_vs_oracle(S, B):
+    n_in, n_out = 300, 500
+    p, i, w, vs = random_layer(n_in, n_out, 25, seed=B, empty_rows=(0, 7))
+    g = setup_layer(S.SparseLinearLayerDeterministic(n_in, n_out, len(i) * 2), p, i, w, vs)
+    o = setup_layer(O.OracleLayer(n_in, n_out, len(i) * 2), p, i, w, vs)
+    rng = np.random.default_rng(B)
+    x = relu_sparse_x(rng, B, n_in)
+    yg, yo = g.forward_dense(x), o.forward_dense(x)
+    if B >= 9:
+        assert np.array_equal(yg, yo)
+    else:
+        assert_close_sum(yg, yo, 1e-5)
+
+
+@pytest.mark.parametrize("B,lr,flags", [(64, 0.01, (True, True)), (40, 0.05, (False, True)),
+                                        (7, 0.02, (True, False)), (96, 0.01, (True, True))])
+def test_backward_update_vs_oracle(S, B, lr, flags):
+    n_in, n_out = 256, 384
+    p, i, w, vs = random_layer(n_in, n_out, 30, seed=11 + B, empty_rows=(3,))
+    g = setup_layer(S.SparseLinearLayerDeterministic(n_in, n_out, len(i) * 2), p, i, w, vs, imp_scale=lr / 6)
+    o = setup_layer(O.OracleLayer(n_in, n_out, len(i) * 2), p, i, w, vs, imp_scale=lr / 6)
+    rng = np.random.default_rng(B)
+    for step in range(3):
+        x = relu_sparse_x(rng, B, n_in)
+        dy = rng.normal(0, 1, (B, n_out)).astype(np.float32)
+        g.forward_dense(x)
+        o.forward_dense(x)
+        dxg = g.backward_dense(dy, lr, *flags)
+        dxo = o.backward_dense(dy, lr, *flags)
+        assert_close_sum(dxg, dxo, 1e-5)
+        sg, so = snapshot(g), snapshot(o)
+        for k in ("live_idx", "live_val", "byte_end", "elem_end", "in_acc", "grad_acc",
+                  "sc_value_scale", "sc_value_scale_importance", "sc_value_scale_step", "sc_value_scale_momentum"):
+            assert np.array_equal(sg[k], so[k][: len(sg[k])] if k.endswith("_end") else so[k]), f"step {step}: {k}"
+
+
+def test_stochastic_rounding_unbiased(S):
+    """Stochastic layer: codes differ from the deterministic layer only by
+    unbiased rounding -- the mean decoded weight over many synapses matches."""
+    n_in, n_out, B = 512, 512, 32
+    p, i, w, vs = random_layer(n_in, n_out, 40, seed=5)
+    gs = setup_layer(S.SparseLinearLayer(n_in, n_out, len(i) * 2), p, i, w, vs, imp_scale=0.05 / 6)
+    o = setup_layer(O.OracleLayer(n_in, n_out, len(i) * 2, stochastic=True, seed=0x5EED), p, i, w, vs,
+                    imp_scale=0.05 / 6)
+    rng = np.random.default_rng(0)
+    x = relu_sparse_x(rng, B, n_in)
+    dy = rng.normal(0, 1, (B, n_out)).astype(np.float32)
+    gs.forward_dense(x); o.forward_dense(x)
+    gs.backward_dense(dy, 0.05, True); o.backward_dense(dy, 0.05, True)
+    # same counter-based draws on both sides -> identical codes
+    assert np.array_equal(snapshot(gs)["live_val"], snapshot(o)["live_val"])
+
+
+def test_empty_and_dead_layers(S):
+    n_in, n_out, B = 20, 30, 12
+    layer = S.SparseLinearLayerDeterministic(n_in, n_out, 100)
+    o = O.OracleLayer(n_in, n_out, 100)
+    rng = np.random.default_rng(1)
+    x = rng.normal(0, 1, (B, n_in)).astype(np.float32)
+    dy = rng.normal(0, 1, (B, n_out)).astype(np.float32)
+    assert np.array_equal(layer.forward_dense(x), np.zeros((B, n_out), np.float32))
+    o.forward_dense(x)
+    dxg = layer.backward_dense(dy, 0.02, True)
+    dxo = o.backward_dense(dy, 0.02, True)
+    assert np.array_equal(dxg, dxo)
+    sg, so = snapshot(layer), snapshot(o)
+    for k in ("sc_value_scale", "sc_value_scale_importance", "sc_value_scale_momentum"):
+        assert np.array_equal(sg[k], so[k]), k
