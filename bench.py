@@ -262,8 +262,12 @@ def main():
     idx_bytes = int(layers[0].raw_state()["byte_end"].sum() - layers[0].raw_state()["byte_start"][:-1].sum())
     fwd_b, bwd_b = algorithmic_bytes(idx_bytes, len(i))
     step_bytes = fwd_b + bwd_b
-    stream = torch.cuda.current_stream(dev)
+    # an explicit stream: the library maps stream handle 0 to the layer's own
+    # stream, so the events must be recorded on the stream the work is given to
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.set_stream(stream)
     sh = stream.cuda_stream
+    assert sh != 0
 
     def step(j, timed_kernels=False):
         L = layers[j % len(layers)]
@@ -271,13 +275,18 @@ def main():
         L.backward_dense_ptr(dys[j % len(layers)].data_ptr(), BATCH, LR, True, True, 0.999, 1e-8,
                              dxs[j % len(layers)].data_ptr(), sh, 0)
 
-    for j in range(args.warmup):
+    # every layer copy runs at least once before timing (first-use index
+    # builds and allocations stay out of the timed region)
+    for j in range(max(args.warmup, len(layers))):
         step(j)
     torch.cuda.synchronize(dev)
 
     # ── device-resident throughput (value) ─────────────────────────────────
     clocks = ClockSampler(dev)
     clocks.start()
+    t_wait = time.time()
+    while not clocks.lines and time.time() - t_wait < 5.0:   # sampler running before timing
+        time.sleep(0.05)
     if dist:
         dist.barrier()
     torch.cuda.synchronize(dev)

@@ -30,9 +30,10 @@ from ._cuda import (  # noqa: E402,F401
     fp4_quantize_array,
     seed_fp4_stochastic_rng,
     device_count,
+    kernel_launches,
 )
 from .backend import CudaBackend, install_as_sili_cuda, register  # noqa: E402,F401
 
 __all__ = ["SparseLinearLayer", "SparseLinearLayerDeterministic", "dense_to_csr", "dense_to_top_k_csr",
-           "fp4_quantize_array", "seed_fp4_stochastic_rng", "device_count", "CudaBackend", "register",
+           "fp4_quantize_array", "seed_fp4_stochastic_rng", "device_count", "kernel_launches", "CudaBackend", "register",
            "install_as_sili_cuda", "LIBRARY_PATH"]

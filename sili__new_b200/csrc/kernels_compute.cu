@@ -121,18 +121,30 @@ __global__ void __launch_bounds__(256) k_forward_gather(LayerView L, const float
                 }
             }
             const int n = min(32, k1 - kb);
-            for (int j = 0; j < n; ++j) {
-                const float wj = __shfl_sync(0xffffffffu, w, j);
-                const int rj = __shfl_sync(0xffffffffu, r, j);
-                const float csj = SPARSE ? __shfl_sync(0xffffffffu, cs, j) : 0.0f;
-                const float* xr = xT + (int64_t)rj * B;
+            for (int j0 = 0; j0 < n; j0 += 8) {
+                // issue 8 synapses' x loads first, then accumulate in row order
+                float wj[8], csj[8], xv[8][NB];
 #pragma unroll
-                for (int t = 0; t < NB; ++t) {
-                    const int b = b0 + t * 32 + lane;
-                    const float xv = b < B ? __ldg(xr + b) : 0.0f;
-                    if (xv != 0.0f)
-                        acc[t] = SPARSE ? __fadd_rn(acc[t], __fmul_rn(__fmul_rn(wj, xv), csj))
-                                        : __fmaf_rn(wj, xv, acc[t]);
+                for (int u = 0; u < 8; ++u) {
+                    const int jj = (j0 + u) & 31;
+                    wj[u] = __shfl_sync(0xffffffffu, w, jj);
+                    const int rj = __shfl_sync(0xffffffffu, r, jj);
+                    csj[u] = SPARSE ? __shfl_sync(0xffffffffu, cs, jj) : 0.0f;
+                    const float* xr = xT + (int64_t)rj * B;
+#pragma unroll
+                    for (int t = 0; t < NB; ++t) {
+                        const int b = b0 + t * 32 + lane;
+                        xv[u][t] = (j0 + u < n && b < B) ? __ldg(xr + b) : 0.0f;
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+#pragma unroll
+                    for (int t = 0; t < NB; ++t) {
+                        if (xv[u][t] != 0.0f)
+                            acc[t] = SPARSE ? __fadd_rn(acc[t], __fmul_rn(__fmul_rn(wj[u], xv[u][t]), csj[u]))
+                                            : __fmaf_rn(wj[u], xv[u][t], acc[t]);
+                    }
                 }
             }
         }
@@ -249,14 +261,26 @@ __global__ void __launch_bounds__(256) k_backward_dx(LayerView L, const float* _
                 cw = __fmul_rn(wq, sc);
             }
             const int n = min(32, nnz - eb);
-            for (int j = 0; j < n; ++j) {
-                const float cwj = __shfl_sync(0xffffffffu, cw, j);
-                const int cj = __shfl_sync(0xffffffffu, c, j);
-                const float* dr = dyT + (int64_t)cj * B;
+            for (int j0 = 0; j0 < n; j0 += 8) {
+                float cwj[8], dv[8][NB];
 #pragma unroll
-                for (int t = 0; t < NB; ++t) {
-                    const int b = b0 + t * 32 + lane;
-                    if (b < B) acc[t] = __fmaf_rn(cwj, __ldg(dr + b), acc[t]);
+                for (int u = 0; u < 8; ++u) {
+                    const int jj = (j0 + u) & 31;
+                    cwj[u] = __shfl_sync(0xffffffffu, cw, jj);
+                    const int cj = __shfl_sync(0xffffffffu, c, jj);
+                    const float* dr = dyT + (int64_t)cj * B;
+#pragma unroll
+                    for (int t = 0; t < NB; ++t) {
+                        const int b = b0 + t * 32 + lane;
+                        dv[u][t] = (j0 + u < n && b < B) ? __ldg(dr + b) : 0.0f;
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    if (j0 + u < n) {
+#pragma unroll
+                        for (int t = 0; t < NB; ++t) acc[t] = __fmaf_rn(cwj[u], dv[u][t], acc[t]);
+                    }
                 }
             }
         }
@@ -317,22 +341,28 @@ __device__ __forceinline__ float bounded_ci(float ci, float g, float contrib, fl
 
 // ── dense backward, learning_rate != 0: the fused update ───────────────────
 // disldo_backward's scattered non-deferred path (linear_disldo.hpp:625-925).
-// One warp per input row; lanes own synapses (32 at a time); each lane runs
-// its synapse's recurrence over the batch IN ORDER -- ci, quant and cw evolve
-// per sample and dx uses the post-update weight of that sample -- exactly as
-// the reference.  Samples with x == 0 take the closed form of the same
-// arithmetic (g = contrib = 0: ci <- min(max(fma(b2, ci, (1-b2)*0), 0*ci), 100),
-// quant unchanged), which is bit-identical to evaluating the full update.
-// dx partials of the 32 lanes are combined per sample by a butterfly
-// transpose-reduction into dxT[r, b] (fixed order, fp32 tolerance vs the
-// reference's sequential sum).  The row's value_scale is updated at the end
-// by lane 0 from double sums, as in the reference.
+// One warp per input row, synapses in chunks of 32, samples in blocks of 32.
+// Per (chunk, block):
+//  1. stage dy[block, chunk columns] in shared memory, one coalesced
+//     128-byte line per synapse (dyT is [n_out, B]);
+//  2. lanes = synapses: each lane runs its synapse's recurrence over the
+//     block's samples IN ORDER (ci, quant, cw evolve per sample, exactly as
+//     the reference); samples with x == 0 take the closed form of the same
+//     arithmetic, and the lane's cw after every x != 0 sample is recorded;
+//  3. lanes = samples: dx[b, r] += cw_e(b) * dy[b, c_e] over the chunk's
+//     synapses in stored order with fmaf, cw_e(b) being synapse e's weight
+//     after sample b -- the reference's summation order, so dx is bit-exact.
+// The row's value_scale is updated at the end by lane 0 from double sums.
+constexpr int kUpdWarps = 4;
 template <bool STOCH, int RANK>
-__global__ void __launch_bounds__(256) k_backward_update(LayerView L, const float* __restrict__ xT,
-                                                         const float* __restrict__ dyT, int B,
-                                                         UpdateParams P, float* __restrict__ dxT) {
+__global__ void __launch_bounds__(kUpdWarps * 32, 6) k_backward_update(LayerView L, const float* __restrict__ xT,
+                                                                       const float* __restrict__ dyT, int B,
+                                                                       UpdateParams P, float* __restrict__ dxT) {
+    __shared__ float dys_s[kUpdWarps][32][33];   // [synapse][sample]
+    __shared__ float cws_s[kUpdWarps][33][33];   // [segment][synapse]
+    __shared__ float xs_s[kUpdWarps][32];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t r = (int64_t)blockIdx.x * 8 + warp;
+    const int64_t r = (int64_t)blockIdx.x * kUpdWarps + warp;
     if (r >= L.n_in) return;
     const int64_t es = L.es[r];
     const int nnz = (int)(L.ee[r] - es);
@@ -341,106 +371,144 @@ __global__ void __launch_bounds__(256) k_backward_update(LayerView L, const floa
         for (int b = lane; b < B; b += 32) dxr[b] = 0.0f;
         return;
     }
-    constexpr int rank = RANK;
+    float (*dys)[33] = dys_s[warp];
+    float (*cws)[33] = cws_s[warp];
+    float* xs = xs_s[warp];
     const int f0 = L.rowptr[r];
     const float eff_lr = P.lr_per_row_nnz ? __fdiv_rn(P.lr, (float)nnz) : P.lr;
     const float scale_eff_lr = __fdiv_rn(P.lr, (float)nnz);
     const float onem = __fsub_rn(1.0f, P.beta2);
     const float zterm = __fmul_rn(onem, 0.0f);
-    const bool fast_ok = !P.damp || P.eps > 0.0f;
+    const bool fast_ok = (!P.damp || P.eps > 0.0f) && isfinite(eff_lr) && P.beta2 >= 0.0f && P.beta2 <= 1.0f;
     const float imp_scale = L.is[r];
-    float vsr[4];
+    float vsr[RANK];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) vsr[k] = k < RANK ? L.vs[r * RANK + k] : 0.0f;
+    for (int k = 0; k < RANK; ++k) vsr[k] = L.vs[r * RANK + k];
     const float* xr = xT + r * (int64_t)B;
+    const bool vec4 = (B & 3) == 0;
 
-    double sgs[4] = {0.0, 0.0, 0.0, 0.0}, sgc[4] = {0.0, 0.0, 0.0, 0.0};
+    double sgs[RANK], sgc[RANK];
+#pragma unroll
+    for (int k = 0; k < RANK; ++k) { sgs[k] = 0.0; sgc[k] = 0.0; }
     double sa_new = 0.0, sa_old = 0.0, sq_new = 0.0, sq_old = 0.0;
     float mx_new = 0.0f;
 
     for (int e0 = 0; e0 < nnz; e0 += 32) {
         const int e = e0 + lane;
-        const bool valid = e < nnz;
+        const int nsyn = min(32, nnz - e0);
+        const bool valid = lane < nsyn;
         int c = 0;
-        uint8_t byte = 0;
+        uint32_t byte = 0;
         if (valid) {
             c = L.abs_cols[f0 + e];
             byte = L.val[es + e];
         }
         const float cw_orig = fp4_decode(byte >> 4), ci_orig = fp4_decode(byte & 15u);
-        float osk[4];
+        float osk[RANK];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) osk[k] = (valid && k < rank) ? L.os[(int64_t)c * rank + k] : 0.0f;
+        for (int k = 0; k < RANK; ++k) osk[k] = valid ? L.os[(int64_t)c * RANK + k] : 0.0f;
         const float cis = valid ? __fmul_rn(imp_scale, L.ois[c]) : 1.0f;
         float S = 0.0f;
-        #pragma unroll
+#pragma unroll
         for (int k = 0; k < RANK; ++k) S = __fmaf_rn(vsr[k], osk[k], S);
         float ci = __fmul_rn(ci_orig, cis);
         float quant = cw_orig;
         float cw = __fmul_rn(quant, S);
-        const bool lane_ok = isfinite(S) && fast_ok;
-        float cg[4] = {0.f, 0.f, 0.f, 0.f}, cc[4] = {0.f, 0.f, 0.f, 0.f};
-        const float* dyc = dyT + (int64_t)c * B;
+        const bool lane_static_ok = fast_ok && isfinite(S) && isfinite(cw_orig);
+        float cg[RANK], cc[RANK];
+#pragma unroll
+        for (int k = 0; k < RANK; ++k) { cg[k] = 0.0f; cc[k] = 0.0f; }
 
         for (int t0 = 0; t0 < B; t0 += 32) {
             const int nb = min(32, B - t0);
+            __syncwarp();
+            // 1. stage dy: row l of the tile is synapse l's column.  Full
+            //    blocks load 16 bytes per lane with 8 lanes covering one
+            //    128-byte line (synapse q*4 + lane/8, samples 4*(lane%8)..+3).
+            float nf = 0.0f;   // NaN iff a staged dy is inf / NaN (0 * inf = NaN)
+            if (vec4 && nb == 32) {
+                const int sub = lane >> 3, s4 = (lane & 7) * 4;
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const int l = q * 4 + sub;
+                    const int cl = __shfl_sync(0xffffffffu, c, l);
+                    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (l < nsyn) v = __ldg(reinterpret_cast<const float4*>(dyT + (int64_t)cl * B + t0 + s4));
+                    dys[l][s4 + 0] = v.x; dys[l][s4 + 1] = v.y; dys[l][s4 + 2] = v.z; dys[l][s4 + 3] = v.w;
+                    nf = __fmaf_rn(v.x, 0.0f, nf); nf = __fmaf_rn(v.y, 0.0f, nf);
+                    nf = __fmaf_rn(v.z, 0.0f, nf); nf = __fmaf_rn(v.w, 0.0f, nf);
+                }
+            } else {
+                for (int l = 0; l < 32; ++l) {
+                    const int cl = __shfl_sync(0xffffffffu, c, l);
+                    const float v = (l < nsyn && lane < nb) ? __ldg(dyT + (int64_t)cl * B + t0 + lane) : 0.0f;
+                    dys[l][lane] = v;
+                    nf = __fmaf_rn(v, 0.0f, nf);
+                }
+            }
             const float xl = (lane < nb) ? __ldg(xr + t0 + lane) : 0.0f;
+            xs[lane] = xl;
             const unsigned act = __ballot_sync(0xffffffffu, xl != 0.0f);
-            float p[32];
+            const bool dy_finite = __all_sync(0xffffffffu, nf == 0.0f);
+            const bool lane_fast = lane_static_ok && ci >= 0.0f && ci <= 100.0f;
+            // Samples where some lane's weight may change: x != 0, or every
+            // sample when a lane cannot use the x == 0 closed form.
+            const unsigned full_mask = nb >= 32 ? 0xffffffffu : ((1u << nb) - 1u);
+            const unsigned bnd = (dy_finite && __all_sync(0xffffffffu, lane_fast)) ? act : full_mask;
+            __syncwarp();
+            // 2. lanes = synapses: the recurrence, recording cw after each boundary sample
+            cws[0][lane] = cw;
+            unsigned rem = bnd;
+            int j = 0, seg = 0;
+            while (true) {
+                const int ja = rem ? (__ffs(rem) - 1) : nb;
+                for (; j + 4 <= ja; j += 4) {                                // x == 0 run
+                    ci = __fmaf_rn(P.beta2, ci, zterm); ci = __fmaf_rn(P.beta2, ci, zterm);
+                    ci = __fmaf_rn(P.beta2, ci, zterm); ci = __fmaf_rn(P.beta2, ci, zterm);
+                }
+                for (; j < ja; ++j) ci = __fmaf_rn(P.beta2, ci, zterm);
+                if (ja >= nb) break;
+                rem &= rem - 1u;
+                const float dyv = dys[lane][ja];
+                const float iv = xs[ja];
+                const float g = __fmul_rn(dyv, iv);
+                const float contrib = __fmul_rn(iv, cw_orig);
+                ci = bounded_ci(ci, g, contrib, P.beta2, onem);
+                const float ngS = __fmul_rn(-g, S);
+                float raw = P.damp ? __fdiv_rn(ngS, __fadd_rn(__fsqrt_rn(ci), P.eps)) : ngS;
+                if (raw > 2.0f) raw = 2.0f;
+                if (raw < -2.0f) raw = -2.0f;
+                quant = __fmaf_rn(eff_lr, raw, quant);
+                cw = __fmul_rn(quant, S);
+                const float qf = (quant == 0.0f) ? 0.1f : quant;
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                p[j] = 0.0f;
-                if (j < nb) {
-                    const float iv = __shfl_sync(0xffffffffu, xl, j);
-                    if (valid) {
-                        const float dyv = __ldg(dyc + t0 + j);
-                        const bool fast = !((act >> j) & 1u) && lane_ok && isfinite(dyv) && ci >= 0.0f;
-                        if (fast) {
-                            const float ema = __fmaf_rn(P.beta2, ci, zterm);
-                            const float fl = __fmul_rn(0.0f, ci);
-                            float rr = (ema < fl) ? fl : ema;
-                            ci = (100.0f < rr) ? 100.0f : rr;
-                        } else {
-                            const float g = __fmul_rn(dyv, iv);
-                            const float contrib = __fmul_rn(iv, cw_orig);
-                            ci = bounded_ci(ci, g, contrib, P.beta2, onem);
-                            const float ngS = __fmul_rn(-g, S);
-                            float raw = P.damp ? __fdiv_rn(ngS, __fadd_rn(__fsqrt_rn(ci), P.eps)) : ngS;
-                            if (raw > 2.0f) raw = 2.0f;
-                            if (raw < -2.0f) raw = -2.0f;
-                            quant = __fmaf_rn(eff_lr, raw, quant);
-                            cw = __fmul_rn(quant, S);
-                            const float qf = (quant == 0.0f) ? 0.1f : quant;
-#pragma unroll
-                            for (int k = 0; k < RANK; ++k) {
-                                const double qo = (double)qf * (double)osk[k];
-                                sgs[k] = __fma_rn(qo, (double)g, sgs[k]);
-                                sgc[k] = __fma_rn(qo, (double)contrib, sgc[k]);
-                                if (P.os_trainable) {
-                                    const float qv = __fmul_rn(qf, vsr[k]);
-                                    cg[k] = __fmaf_rn(qv, g, cg[k]);
-                                    cc[k] = __fmaf_rn(qv, contrib, cc[k]);
-                                }
-                            }
-                        }
-                        p[j] = __fmul_rn(cw, dyv);
+                for (int k = 0; k < RANK; ++k) {
+                    const double qo = (double)qf * (double)osk[k];
+                    sgs[k] = __fma_rn(qo, (double)g, sgs[k]);
+                    sgc[k] = __fma_rn(qo, (double)contrib, sgc[k]);
+                    if (P.os_trainable) {
+                        const float qv = __fmul_rn(qf, vsr[k]);
+                        cg[k] = __fmaf_rn(qv, g, cg[k]);
+                        cc[k] = __fmaf_rn(qv, contrib, cc[k]);
                     }
                 }
+                cws[++seg][lane] = cw;
+                j = ja + 1;
             }
-            // butterfly transpose-reduction: lane j ends with sum over lanes of p[j]
-#pragma unroll
-            for (int o = 16, h = 16; o > 0; o >>= 1, h >>= 1) {
-                const bool up = (lane & o) != 0;
-#pragma unroll
-                for (int i = 0; i < h; ++i) {
-                    const float send = up ? p[i] : p[i + h];
-                    const float keep = up ? p[i + h] : p[i];
-                    p[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, o));
-                }
-            }
+            __syncwarp();
+            // 3. lanes = samples: dx in the reference's order (synapses ascending)
             if (lane < nb) {
+                const int sg = __popc(bnd & ((2u << lane) - 1u));
                 float* d = dxr + t0 + lane;
-                *d = (e0 == 0) ? p[0] : __fadd_rn(*d, p[0]);
+                float acc = (e0 == 0) ? 0.0f : *d;
+                const float* cwrow = cws[sg];
+                if (nsyn == 32) {
+#pragma unroll
+                    for (int l = 0; l < 32; ++l) acc = __fmaf_rn(cwrow[l], dys[l][lane], acc);
+                } else {
+                    for (int l = 0; l < nsyn; ++l) acc = __fmaf_rn(cwrow[l], dys[l][lane], acc);
+                }
+                *d = acc;
             }
         }
         if (valid) {
@@ -463,8 +531,8 @@ __global__ void __launch_bounds__(256) k_backward_update(LayerView L, const floa
             if (P.os_trainable) {
 #pragma unroll
                 for (int k = 0; k < RANK; ++k) {
-                    atomicAdd(P.colg + (int64_t)c * rank + k, cg[k]);
-                    atomicAdd(P.colc + (int64_t)c * rank + k, cc[k]);
+                    atomicAdd(P.colg + (int64_t)c * RANK + k, cg[k]);
+                    atomicAdd(P.colc + (int64_t)c * RANK + k, cc[k]);
                 }
             }
         }
@@ -478,7 +546,7 @@ __global__ void __launch_bounds__(256) k_backward_update(LayerView L, const floa
     if (lane == 0) {
 #pragma unroll
         for (int k = 0; k < RANK; ++k) {
-            const int64_t i = r * rank + k;
+            const int64_t i = r * RANK + k;
             rmsprop_scale(L.vs + i, L.vsi + i, (float)sgs[k], scale_eff_lr, (float)sgc[k], L.vstep + i, P);
         }
     }
@@ -495,10 +563,10 @@ __global__ void __launch_bounds__(256) k_backward_update(LayerView L, const floa
 void launch_backward_update(const LayerView& L, const float* xT, const float* dyT, int B,
                             const UpdateParams& P, float* dxT, cudaStream_t s) {
     if (L.n_in == 0) return;
-    const unsigned g = (unsigned)((L.n_in + 7) / 8);
+    const unsigned g = (unsigned)((L.n_in + kUpdWarps - 1) / kUpdWarps);
 #define SILI_BWD(R)                                                                         \
-    if (P.stochastic) k_backward_update<true, R><<<g, 256, 0, s>>>(L, xT, dyT, B, P, dxT);  \
-    else k_backward_update<false, R><<<g, 256, 0, s>>>(L, xT, dyT, B, P, dxT);
+    if (P.stochastic) k_backward_update<true, R><<<g, kUpdWarps * 32, 0, s>>>(L, xT, dyT, B, P, dxT);  \
+    else k_backward_update<false, R><<<g, kUpdWarps * 32, 0, s>>>(L, xT, dyT, B, P, dxT);
     switch (L.rank) {
     case 1: SILI_BWD(1) break;
     case 2: SILI_BWD(2) break;

@@ -5,8 +5,10 @@ Contract (per quantity):
     value_scale / importance state and steps: bit-exact.
   * forward y (batch >= 9) and dx at learning_rate == 0: bit-exact (the
     kernels sum in the reference's single-thread order).
-  * dx at learning_rate != 0, forward at batch <= 8, output_scale (trained from
-    fp32 column sums): within fp32 accumulation tolerance, 1e-5 relative.
+  * dx at learning_rate != 0: bit-exact (synapses summed in stored order).
+  * forward at batch <= 8, the sparse-gradient backward's dx and output_scale
+    (trained from fp32 column sums): within fp32 accumulation tolerance, 1e-5
+    relative.
 """
 import os
 
@@ -40,7 +42,7 @@ def det(S):
 def test_dense_golden(S, name):
     fx = load(name)
     os_trained = "os" in fx and name != "dense_small"
-    for layer, s in replay_dense(det(S), fx, dx_exact=False, dx_rtol=1e-5):
+    for layer, s in replay_dense(det(S), fx, dx_exact=True):
         snap = snapshot(layer)
         if os_trained:
             # output_scale is trained from fp32 column sums whose order differs
@@ -146,7 +148,7 @@ def test_backward_update_vs_oracle(S, B, lr, flags):
         o.forward_dense(x)
         dxg = g.backward_dense(dy, lr, *flags)
         dxo = o.backward_dense(dy, lr, *flags)
-        assert_close_sum(dxg, dxo, 1e-5)
+        assert np.array_equal(dxg, dxo), f"step {step}: dx differs"   # same summation order as the reference
         sg, so = snapshot(g), snapshot(o)
         for k in ("live_idx", "live_val", "byte_end", "elem_end", "in_acc", "grad_acc",
                   "sc_value_scale", "sc_value_scale_importance", "sc_value_scale_step", "sc_value_scale_momentum"):
@@ -185,3 +187,49 @@ def test_empty_and_dead_layers(S):
     sg, so = snapshot(layer), snapshot(o)
     for k in ("sc_value_scale", "sc_value_scale_importance", "sc_value_scale_momentum"):
         assert np.array_equal(sg[k], so[k]), k
+
+
+@pytest.mark.parametrize("case", ["big_importance", "nonfinite_dy", "nan_x", "beta2_one"])
+def test_backward_update_edge_cases(S, case):
+    """Cases that must leave the x == 0 shortcut and take the full update:
+    initial ci above the 100 cap, non-finite gradients, NaN inputs, beta2 = 1."""
+    n_in, n_out, B = 96, 160, 48
+    p, i, w, vs = random_layer(n_in, n_out, 20, seed=21)
+    imp = 50.0 if case == "big_importance" else 0.01 / 6
+    g = setup_layer(S.SparseLinearLayerDeterministic(n_in, n_out, len(i) * 2), p, i, w, vs, imp_scale=imp)
+    o = setup_layer(O.OracleLayer(n_in, n_out, len(i) * 2), p, i, w, vs, imp_scale=imp)
+    rng = np.random.default_rng(3)
+    codes = rng.integers(0, 16, len(i)).astype(np.uint8)
+    codes[codes == 8] = 7
+    vb = ((np.frombuffer(bytes(snapshot(o)["live_val"]), np.uint8) & 0xF0) | codes).astype(np.uint8)
+    # give every synapse a non-zero importance code (same bytes on both sides)
+    so = o.state()
+    full = so["values"].copy()
+    f = 0
+    for r in range(n_in):
+        n = so["elem_end"][r] - so["elem_start"][r]
+        full[so["elem_start"][r]:so["elem_end"][r]] = vb[f:f + n]
+        f += n
+    o.set_value_bytes(full)
+    g.set_value_bytes(full)
+    x = relu_sparse_x(rng, B, n_in)
+    dy = rng.normal(0, 1, (B, n_out)).astype(np.float32)
+    if case == "nonfinite_dy":
+        dy[3, 5] = np.inf
+        dy[10, 40] = np.nan
+        dy[20, 7] = -np.inf
+    if case == "nan_x":
+        x[4, 2] = np.nan
+    beta2 = 1.0 if case == "beta2_one" else 0.999
+    g.forward_dense(x)
+    o.forward_dense(x)
+    dxg = g.backward_dense(dy, 0.02, True, True, beta2)
+    dxo = o.backward_dense(dy, 0.02, True, True, beta2)
+    assert np.array_equal(np.isnan(dxg), np.isnan(dxo))
+    m = np.isfinite(dxo)
+    assert np.array_equal(np.isfinite(dxg), m)
+    assert_close_sum(np.where(m, dxg, 0), np.where(m, dxo, 0), 1e-5)
+    sg, so2 = snapshot(g), snapshot(o)
+    assert np.array_equal(sg["live_val"], so2["live_val"])
+    for k in ("sc_value_scale", "sc_value_scale_importance", "sc_value_scale_step"):
+        assert np.array_equal(sg[k], so2[k], equal_nan=True), k
