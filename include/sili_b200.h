@@ -95,6 +95,18 @@ int sili_layer_rescale_row(sili_layer* h, int kind, int row, float new_scale);
 /* forward_dense(x), cpu_backend.cpp:475-492 -> disldo_forward
  * (linear_disldo.hpp:68-345).  Keeps x as the layer's last input. */
 int sili_layer_forward_dense(sili_layer* h, const float* x, int batch, float* y, void* stream);
+/* forward_dense without any allocation.  No counterpart in the reference:
+ * for callers that cannot call cudaMalloc.  x [batch, n_in] and y
+ * [batch, n_out] must be device pointers; the transposed-input scratch is a
+ * fixed per-device array of SILI_STATIC_FWD_MAX_ELEMS floats (4 MiB), so
+ * batch * n_in above that is rejected with SILI_EINVAL.  The column index
+ * must be current (one forward_dense after load_weights or a structural
+ * change), else SILI_EINVAL.  Does not keep x for backward_dense.  The first
+ * call on a device looks up the scratch address (cudaGetSymbolAddress); make
+ * it before work that must see only launches.  Calls on one device share the
+ * scratch: overlapping calls race, so order them (one stream). */
+#define SILI_STATIC_FWD_MAX_ELEMS 1048576
+int sili_layer_forward_dense_static(sili_layer* h, const float* x, int batch, float* y, void* stream);
 /* backward_dense(dy, lr, lr_per_row_nnz, damp_by_importance, beta2, eps),
  * cpu_backend.cpp:496-529 -> disldo_backward (linear_disldo.hpp:462-2113)
  * with beta1 0.9, min_decay_frac 0, max_abs_delta 2, max_ci 100.

@@ -10,6 +10,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -1453,3 +1454,66 @@ int sili_dense_to_top_k_csr(const float* x, int rows, int cols, int64_t k, int* 
 }
 
 }  // extern "C"
+
+// ── forward_dense with no allocation ────────────────────────────────────────
+// Some callers cannot call cudaMalloc: a host framework that has already
+// reserved the device's memory for its own caching allocator (a cudaMalloc
+// from inside it fails or steals from its pool), or a loop that must not
+// stall, since cudaMalloc may synchronise the whole device and so wait on
+// every other stream.  sili_layer_forward_dense_static serves them: the only
+// scratch the forward needs, the transposed input xT [n_in, batch], lives in
+// the file-scope array below instead of a per-layer buffer, and x / y must
+// already be device memory, so nothing is staged.
+//
+// The array is one per device and shared by every layer on it: two calls
+// whose executions overlap on one device (different streams, or different
+// host threads without ordering) race on it and give wrong results.  Calls
+// must be ordered, e.g. issued on one stream.
+//
+// Nothing in the scratch has to start at zero: the transpose writes every
+// element xT[0, n_in * batch) before the gather kernel reads any of it.
+namespace {
+constexpr int64_t kStaticFwdScratch = SILI_STATIC_FWD_MAX_ELEMS;  // floats, 4 MiB
+constexpr int kStaticMaxDevices = 64;
+static __device__ __align__(256) float g_fwd_xT_scratch[kStaticFwdScratch];
+std::mutex g_static_mu;
+float* g_static_xT[kStaticMaxDevices] = {};
+
+// Device address of the scratch array on the current device, looked up once
+// per device (the first call on a device does this lookup; make that first
+// call before any work that must not see a runtime call other than launches).
+int static_fwd_scratch(int dev, float** out) {
+    if (dev < 0 || dev >= kStaticMaxDevices) return fail(SILI_EINVAL, "forward_dense_static: device id out of range");
+    std::lock_guard<std::mutex> lk(g_static_mu);
+    if (!g_static_xT[dev]) {
+        float* ptr = nullptr;
+        cudaError_t e = cudaGetSymbolAddress((void**)&ptr, g_fwd_xT_scratch);
+        if (e != cudaSuccess || !ptr)
+            return fail(SILI_ECUDA, std::string("forward_dense_static: cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+        g_static_xT[dev] = ptr;
+    }
+    *out = g_static_xT[dev];
+    return SILI_OK;
+}
+}  // namespace
+
+extern "C" int sili_layer_forward_dense_static(sili_layer* h, const float* x, int batch, float* y, void* stream) {
+    RC(use(h));
+    if (batch < 0 || !x || !y) return fail(SILI_EINVAL, "forward_dense_static: bad arguments");
+    const int64_t n_in = h->rows;
+    if ((int64_t)batch * n_in > kStaticFwdScratch)
+        return fail(SILI_EINVAL, "forward_dense_static: batch * n_inputs = " + std::to_string((int64_t)batch * n_in) +
+                                     " exceeds the static scratch of " + std::to_string(kStaticFwdScratch) + " floats");
+    if (!is_device_ptr(x) || !is_device_ptr(y))
+        return fail(SILI_EINVAL, "forward_dense_static: x and y must be device pointers");
+    if (h->aux_dirty)
+        return fail(SILI_EINVAL, "forward_dense_static: the column index is stale (load_weights or a structural "
+                                 "change since the last forward_dense); call forward_dense once to rebuild it");
+    float* xT = nullptr;
+    RC(static_fwd_scratch(h->dev, &xT));
+    cudaStream_t s = pick(h, stream);
+    launch_transpose(x, xT, batch, n_in, s);
+    launch_forward(h->view(), xT, batch, y, false, s);
+    CK(cudaGetLastError());
+    return SILI_OK;
+}
