@@ -110,6 +110,15 @@ def lib():
             ("o_top_k_csr", _I64, [_P, _I, _I, _I64, _P, _P, _P]),
             ("o_topk_dyx_candidates", _I64, [_P, _P, _P, _I, _I64, _P, _P, _P]),
             ("o_topk_dyx_step", _I, [_P, _P, _P, _I, _I64]),
+            ("o_load_dense_codes", _I, [_P, _P, _P]),
+            ("o_b4_expand_headroom", _I, [_P, _F, _I64]),
+            ("o_b4_equalize_step", _I, [_P, _I64]),
+            ("o_b4_set_switch_point", None, [_P, C.c_uint32]),
+            ("o_b4_ntiles", _I64, [_P]),
+            ("o_b4_export", None, [_P, _P, _P, _P, _P]),
+            ("o_b4_rows", None, [_P, _P]),
+            ("o_b4_view", None, [_P, _P]),
+            ("o_std_sort_keys", None, [_P, _I64, _I, _P]),
         ]:
             f = getattr(_lib, name)
             f.restype = res
@@ -246,7 +255,17 @@ class _LayerBase:
         return r[:n], c[:n], v[:n]
 
     @property
-    def nnz(self): return int(self._sizes()[2])
+    def nnz(self): return int(self.export()[1].size) if self.b4_view()[0] else int(self._sizes()[2])
+
+    # ── block4 (Block4View, cpu_backend.cpp:51-98) ──
+    def b4_view(self):
+        v = np.zeros(8, np.int64)
+        self._fn("b4_view")(self.h, _ptr(v))
+        return v
+
+    @property
+    def block4(self):
+        return _Block4View(self)
 
     def get_value_scale(self, row): return self.get_value_scale_k(row, 0)
     def get_output_scale(self, col): return self.get_output_scale_k(col, 0)
@@ -269,6 +288,34 @@ class _LayerBase:
             output_scale_step=u(self.get_output_scale_step_k, Cc))
 
 
+class _Block4View:
+    """Mirror of the reference's Block4View counters."""
+
+    def __init__(self, layer):
+        self._l = layer
+
+    def tiles(self): return int(self._l.b4_view()[0])
+    def synapses(self): return int(self._l.b4_view()[1])
+    def get_switch_point(self): return int(self._l.b4_view()[2])
+    def set_switch_point(self, v): self._l.set_switch_point(v)
+    def dropped_growth_events(self): return int(self._l.b4_view()[3])
+    def row_merge_overflow_events(self): return int(self._l.b4_view()[4])
+    def row_merge_overflow_bytes_dropped(self): return int(self._l.b4_view()[5])
+    def used_bytes(self): return int(self._l.b4_view()[6])
+    def alloc_bytes(self): return int(self._l.b4_view()[7])
+
+
+def std_sort_keys(keys, desc=False, which="oracle", variant="native"):
+    """Permutation std::sort produces for indices ordered by keys."""
+    k = np.ascontiguousarray(keys, np.float32)
+    perm = np.zeros(max(len(k), 1), np.int64)
+    if which == "oracle":
+        lib().o_std_sort_keys(_ptr(k), len(k), int(desc), _ptr(perm))
+    else:
+        ref_lib(variant).ref_std_sort_keys(_ptr(k), len(k), int(desc), _ptr(perm))
+    return perm[:len(k)]
+
+
 class OracleLayer(_LayerBase):
     """The C restatement behind the reference's SparseLinearLayer method names.
 
@@ -285,6 +332,7 @@ class OracleLayer(_LayerBase):
         self._last = None
         self._synap_row = 0
         self._eq_row = 0
+        self._b4_eq_row = 0
 
     def _fn(self, name):
         return getattr(self.L, "o_" + name)
@@ -382,10 +430,41 @@ class OracleLayer(_LayerBase):
         return self.synap_row_step(row, importance_cutoff, max_row_weights, max_prune_per_step, importance_eps)
 
     def equalizer_step(self):
-        rc = self.L.o_equalizer_step(self.h, self._eq_row)
-        self._eq_row = (self._eq_row + 1) % max(self.n_inputs, 1)
-        if rc:
+        """equalizer_step, cpu_backend.cpp:631-641: scattered rows, then block4 rows."""
+        if self.L.o_equalizer_step(self.h, self._eq_row):
             raise MemoryError("equalizer_step: budget exceeded")
+        self._eq_row = (self._eq_row + 1) % max(self.n_inputs, 1)
+        if self.L.o_b4_equalize_step(self.h, self._b4_eq_row):
+            raise MemoryError("equalizer_step: block4 budget exceeded")
+        self._b4_eq_row = (self._b4_eq_row + 1) % max((self.n_inputs + 3) // 4, 1)
+
+    def load_dense_codes(self, weight_codes, importance_codes):
+        w = np.ascontiguousarray(weight_codes, np.uint8); i = np.ascontiguousarray(importance_codes, np.uint8)
+        if self.L.o_load_dense_codes(self.h, _ptr(w), _ptr(i)):
+            raise MemoryError("load_dense_codes: block4 budget exceeded")
+
+    def expand_block4_headroom(self, blank_fraction=0.2):
+        if self.L.o_b4_expand_headroom(self.h, blank_fraction, 16):
+            raise MemoryError("expand_block4_headroom: budget exceeded")
+
+    def compact_block4(self):
+        if self.L.o_b4_expand_headroom(self.h, 0.0, 0):
+            raise MemoryError("compact_block4: budget exceeded")
+
+    def set_switch_point(self, v): self.L.o_b4_set_switch_point(self.h, v)
+
+    def b4_tiles(self):
+        n = int(self.L.o_b4_ntiles(self.h))
+        br = np.zeros(max(n, 1), np.int32); bc = np.zeros(max(n, 1), np.int32)
+        sl = np.zeros(max(n, 1) * 16, np.uint8); sp = np.zeros(max(n, 1), np.uint8)
+        self.L.o_b4_export(self.h, _ptr(br), _ptr(bc), _ptr(sl), _ptr(sp))
+        return br[:n], bc[:n], sl[:n * 16].reshape(n, 16), sp[:n]
+
+    def b4_rows(self):
+        R = (self.n_inputs + 3) // 4
+        o = np.zeros(max(R, 1) * 6, np.int64)
+        self.L.o_b4_rows(self.h, _ptr(o))
+        return o[:R * 6].reshape(R, 6)
 
     def equalize_to_capacity(self, target_elems_per_row, target_bytes_per_row=0):
         if self.L.o_equalize_to_capacity(self.h, target_elems_per_row, target_bytes_per_row):
@@ -466,6 +545,15 @@ def ref_lib(variant: str = "native"):
             ("ref_fp4_decode", _F, [C.c_uint8]), ("ref_fp4_encode", C.c_uint8, [_F]),
             ("ref_fp4_quantize_stochastic", C.c_uint8, [_F]),
             ("ref_top_k_csr", _I, [_P, _I, _I, _I, _P, _P, _P]),
+            ("ref_load_dense_codes", _I, [_P, _P, _P]),
+            ("ref_b4_expand_headroom", _I, [_P, _F]),
+            ("ref_b4_compact", _I, [_P]),
+            ("ref_b4_set_switch_point", None, [_P, C.c_uint32]),
+            ("ref_b4_rows_n", _I64, [_P]),
+            ("ref_b4_rows", None, [_P, _P]),
+            ("ref_b4_sparse", None, [_P, _P]),
+            ("ref_b4_view", None, [_P, _P]),
+            ("ref_std_sort_keys", None, [_P, _I64, _I, _P]),
         ]:
             f = getattr(L, name)
             f.restype = res
@@ -583,6 +671,33 @@ class RefLayer(_LayerBase):
     def expand_headroom_to(self, min_nnz_per_row, blank_fraction=0.2):
         if self.L.ref_expand_headroom_to(self.h, min_nnz_per_row, blank_fraction) < 0:
             raise MemoryError(self.L.ref_last_error(self.h).decode())
+
+    def load_dense_codes(self, weight_codes, importance_codes):
+        w = np.ascontiguousarray(weight_codes, np.uint8); i = np.ascontiguousarray(importance_codes, np.uint8)
+        if self.L.ref_load_dense_codes(self.h, _ptr(w), _ptr(i)) < 0:
+            raise MemoryError(self.L.ref_last_error(self.h).decode())
+
+    def expand_block4_headroom(self, blank_fraction=0.2):
+        if self.L.ref_b4_expand_headroom(self.h, blank_fraction) < 0:
+            raise MemoryError(self.L.ref_last_error(self.h).decode())
+
+    def compact_block4(self):
+        if self.L.ref_b4_compact(self.h) < 0:
+            raise MemoryError(self.L.ref_last_error(self.h).decode())
+
+    def set_switch_point(self, v): self.L.ref_b4_set_switch_point(self.h, v)
+
+    def b4_tiles(self):
+        br, bc, sl = self.block4_tiles()
+        sp = np.zeros(max(len(br), 1), np.uint8)
+        self.L.ref_b4_sparse(self.h, _ptr(sp))
+        return br, bc, sl, sp[:len(br)]
+
+    def b4_rows(self):
+        R = int(self.L.ref_b4_rows_n(self.h))
+        o = np.zeros(max(R, 1) * 6, np.int64)
+        self.L.ref_b4_rows(self.h, _ptr(o))
+        return o[:R * 6].reshape(R, 6)
 
     def block4_tiles(self):
         n = int(self.L.ref_block4_tiles(self.h))

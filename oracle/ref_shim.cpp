@@ -11,6 +11,7 @@
 // exports that internal state through a C ABI.  Every call runs with
 // num_cpus = 1, so the reference's thread-local stochastic-rounding stream is
 // the calling thread's and fp4_seed_stochastic_rng() makes it reproducible.
+#include <algorithm>
 #include <cstdint>
 #include <cstring>
 #include <stdexcept>
@@ -321,6 +322,67 @@ void ref_block4_export(void* h, int* br_out, int* bc_out, uint8_t* slots) {
                     slots[t * 16 + lj * 4 + li] = tile.at(li, lj);
         }
     }
+}
+
+// load_dense_codes (cpu_backend.cpp:910-921)
+int ref_load_dense_codes(void* h, const uint8_t* wc, const uint8_t* ic) {
+    auto* L = static_cast<RefLayer*>(h);
+    const std::size_t rows = L->w.connections.layout.rows, cols = L->w.connections.layout.cols;
+    try {
+        block4_load_dense<S, FP4BiPacked, COL>(L->w, wc, ic, rows, cols);
+    } catch (const std::exception& e) { L->err = e.what(); return -1; }
+    L->w.out_degree.assign(cols, S(rows));
+    return 0;
+}
+int ref_b4_expand_headroom(void* h, float bf) {
+    auto* L = static_cast<RefLayer*>(h);
+    try { block4_expand_headroom<S, FP4BiPacked, COL>(L->w, bf); }
+    catch (const std::exception& e) { L->err = e.what(); return -1; }
+    return 0;
+}
+int ref_b4_compact(void* h) {
+    auto* L = static_cast<RefLayer*>(h);
+    try { block4_compact<S, FP4BiPacked, COL>(L->w); }
+    catch (const std::exception& e) { L->err = e.what(); return -1; }
+    return 0;
+}
+void ref_b4_set_switch_point(void* h, uint32_t v) { static_cast<RefLayer*>(h)->w.block4.switch_point = v; }
+// per block-row: idx alloc, idx used, tile alloc, tile used, elem alloc, tiles
+int64_t ref_b4_rows_n(void* h) { return static_cast<int64_t>(static_cast<RefLayer*>(h)->w.block4.block_layout.rows); }
+void ref_b4_rows(void* h, int64_t* out) {
+    auto& st = static_cast<RefLayer*>(h)->w.block4;
+    const auto& BL = st.block_layout;
+    for (std::size_t br = 0; br < BL.rows; ++br) {
+        out[6 * br + 0] = BL.byte_start[br + 1] - BL.byte_start[br];
+        out[6 * br + 1] = BL.byte_end[br] - BL.byte_start[br];
+        out[6 * br + 2] = st.tile_byte_start[br + 1] - st.tile_byte_start[br];
+        out[6 * br + 3] = st.tile_byte_end[br] - st.tile_byte_start[br];
+        out[6 * br + 4] = BL.elem_start[br + 1] - BL.elem_start[br];
+        out[6 * br + 5] = BL.elem_end[br] - BL.elem_start[br];
+    }
+}
+// sparse flag of every tile, in export order
+void ref_b4_sparse(void* h, uint8_t* out) {
+    auto& st = static_cast<RefLayer*>(h)->w.block4;
+    std::size_t t = 0;
+    for (std::size_t br = 0; br < st.block_layout.rows; ++br)
+        for (std::size_t e = st.block_layout.elem_start[br]; e < st.block_layout.elem_end[br]; ++e) out[t++] = st.tile_is_sparse[e];
+}
+// Block4View counters (cpu_backend.cpp:51-98)
+void ref_b4_view(void* h, int64_t* v) {
+    auto& st = static_cast<RefLayer*>(h)->w.block4;
+    v[0] = st.n_tiles(); v[1] = st.live_synapses(); v[2] = st.switch_point; v[3] = st.dropped_growth_events;
+    v[4] = st.row_merge_overflow_events; v[5] = st.row_merge_overflow_bytes_dropped;
+    v[6] = st.total_tile_used_bytes(); v[7] = st.total_tile_alloc_bytes();
+}
+// std::sort of indices by float keys, with the comparators the synaptogenesis
+// step uses (delta_csr_memory.hpp:1149-1152, :1182-1185)
+void ref_std_sort_keys(const float* keys, int64_t n, int desc, int64_t* perm) {
+    std::vector<std::size_t> idx(static_cast<std::size_t>(n));
+    for (std::size_t i = 0; i < idx.size(); ++i) idx[i] = i;
+    if (desc) std::sort(idx.begin(), idx.end(), [&](std::size_t a, std::size_t b) { return keys[a] > keys[b]; });
+    else std::sort(idx.begin(), idx.end(), [&](std::size_t a, std::size_t b) { return keys[a] < keys[b]; });
+    for (std::size_t i = 0; i < idx.size(); ++i) perm[i] = static_cast<int64_t>(idx[i]);
 }
 
 // Codec entry points (fp4quant.hpp:68-121, :238-273) for pinning the restatement.

@@ -52,9 +52,34 @@ struct OLayer {
     double importance_l1, importance_l2_sq, value_l1, value_l2_sq;
     float importance_max_abs, value_max_abs, max_abs_decay;
     int stochastic; uint64_t seed; uint64_t call;
+    /* block4 store (block4.hpp:1016-1490): per block-row tile lists plus the
+     * reference's per-block-row allocations (index bytes, tile bytes, tile
+     * slots), which decide headroom growth, eviction and budget errors. */
+    int64_t b4_rows, b4_cols;
+    struct OTileRow* b4;
+    int64_t *b4_idx_alloc, *b4_tile_alloc, *b4_elem_alloc;
+    int64_t b4_max_idx, b4_max_tile;
+    uint32_t b4_switch;
+    uint64_t b4_dropped, b4_ovf_events, b4_ovf_bytes;
 };
 
 #define NO_LIMIT INT64_MAX
+
+/* block4 store, defined with the block4 section near the end of the file */
+static void b4_init(OLayer* L);
+static void b4_free(OLayer* L);
+static void b4_forward(const OLayer* L, const float* x, int batch, float* y);
+static void b4_backward(OLayer* L, const float* x, const float* dy, int batch, float lr, int lr_per_row_nnz,
+                        int damp, float beta2, float eps, float* dx, float* colg, float* colc, uint64_t call);
+static int64_t b4_row_live(const OLayer* L, int64_t row);
+typedef int (*o_less_fn)(int64_t a, int64_t b, const void* ctx);
+void o_std_sort(int64_t* a, int64_t n, o_less_fn lt, const void* c);
+int64_t o_b4_ntiles(const OLayer* L);
+/* a block4 tile: block-column, 16 slot bytes (slot = lj*4 + li,
+ * Block4Tile::slot_index, block4.hpp:309), sparse-packed flag */
+typedef struct OTile { int32_t bc; uint8_t s[16]; uint8_t sparse; } OTile;
+struct OTileRow { OTile* t; int64_t n, cap; };
+#define B4_SLOT(li, lj) ((lj) * 4 + (li))
 
 /* ── codec: fp4quant.hpp ─────────────────────────────────────────────────── */
 static inline uint32_t f2u(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
@@ -304,6 +329,10 @@ OLayer* o_create(int n_in, int n_out, int max_weights) {
     L->in_acc = (float*)calloc((size_t)n_in + 1, sizeof(float));
     L->grad_acc = (float*)calloc((size_t)n_out + 1, sizeof(float));
     L->out_degree = (int*)calloc((size_t)n_out + 1, sizeof(int));
+    b4_init(L);
+    L->b4_max_idx = (int64_t)max_weights * 8 + 4096;
+    L->b4_max_tile = ((int64_t)max_weights / 16 > 4 ? (int64_t)max_weights / 16 : 4) * 16;
+    L->b4_switch = 10;
     return L;
 }
 
@@ -316,6 +345,7 @@ void o_destroy(OLayer* L) {
     free(L->value_scale_step.d); free(L->output_scale_step.d);
     free(L->in_acc); free(L->grad_acc); free(L->out_degree);
     free(L->prow); free(L->pcol); free(L->pval);
+    b4_free(L);
     free(L);
 }
 
@@ -358,6 +388,7 @@ void o_forward_dense(OLayer* L, const float* x, int batch, float* y) {
             }
         }
     }
+    b4_forward(L, x, batch, y);
 }
 
 /* ── scale policy, delta_csr_types.hpp:445-466 (RMSpropScalePolicy) ────── */
@@ -496,10 +527,11 @@ void o_backward_dense(OLayer* L, const float* x, const float* dy, int batch, flo
             L->importance_max_abs = fmaxf(L->importance_max_abs * L->max_abs_decay, mx_new);
         }
     }
-    /* dead-row bootstrap, linear_disldo.hpp:1985-2042 (block4 empty) */
+    b4_backward(L, x, dy, batch, lr, lr_per_row_nnz, damp, beta2, eps, dx, colg, colc, call);
+    /* dead-row bootstrap, linear_disldo.hpp:1985-2042 */
     if (lr != 0.0f) {
         int any_dead = 0;
-        for (int64_t r = 0; r < n_in; ++r) if (row_nnz(L, r) == 0) { any_dead = 1; break; }
+        for (int64_t r = 0; r < n_in; ++r) if (row_nnz(L, r) == 0 && b4_row_live(L, r) == 0) { any_dead = 1; break; }
         if (any_dead) {
             double* S = (double*)calloc((size_t)(batch * rank) + 1, sizeof(double));
             for (int b = 0; b < batch; ++b)
@@ -511,7 +543,7 @@ void o_backward_dense(OLayer* L, const float* x, const float* dy, int batch, flo
                 }
             const float dead_lr = lr / (float)n_out;
             for (int64_t r = 0; r < n_in; ++r) {
-                if (row_nnz(L, r) != 0) continue;
+                if (row_nnz(L, r) != 0 || b4_row_live(L, r) != 0) continue;
                 for (int64_t k = 0; k < rank; ++k) {
                     double sum = 0.0;
                     for (int b = 0; b < batch; ++b) {
@@ -791,97 +823,7 @@ static int insert_fits(const OLayer* L, int64_t r, const uint32_t* cols, int64_t
     return 1;
 }
 
-/* delta_csr_synap_row_step, delta_csr_memory.hpp:1019-1258, scattered storage.
- * Sort ties: the reference uses std::sort (unstable); this restatement breaks
- * importance ties by stored position and score ties by probe order, which is
- * what std::sort yields for rows of at most 16 entries (insertion sort). */
-typedef struct { float key; int64_t pos; } KP;
-static int cmp_kp_asc(const void* a, const void* b) {
-    const KP* x = (const KP*)a; const KP* y = (const KP*)b;
-    if (x->key < y->key) return -1;
-    if (x->key > y->key) return 1;
-    return (x->pos > y->pos) - (x->pos < y->pos);
-}
-static int cmp_kp_desc(const void* a, const void* b) {
-    const KP* x = (const KP*)a; const KP* y = (const KP*)b;
-    if (x->key > y->key) return -1;
-    if (x->key < y->key) return 1;
-    return (x->pos > y->pos) - (x->pos < y->pos);
-}
-static int cmp_u32_desc(const void* a, const void* b) {
-    const uint32_t x = *(const uint32_t*)a, y = *(const uint32_t*)b;
-    return (x < y) - (x > y);
-}
-
-int o_synap_row_step(OLayer* L, int row_in, float cutoff, int max_rw, int max_prune, float imp_eps, int* did) {
-    *did = 0;
-    if (L->rows == 0) return O_OK;
-    const int64_t r = (int64_t)row_in % L->rows;
-    const int64_t n = row_nnz(L, r);
-    const int has_probes = L->n_probes > 0;
-    if (n == 0 && !has_probes) return O_OK;
-    uint32_t* cols = (uint32_t*)malloc((size_t)(n + L->n_probes + 1) * sizeof(uint32_t));
-    uint8_t* vals = (uint8_t*)malloc((size_t)(n + L->n_probes + 1));
-    decode_row(L, r, cols);
-    memcpy(vals, L->val + L->elem_start[r], (size_t)n);
-    /* step 2: probes of this row, in COO order (:1133-1144) */
-    KP* pr = (KP*)malloc((size_t)(L->n_probes + 1) * sizeof(KP));
-    int64_t np = 0;
-    for (int64_t p = 0; p < L->n_probes; ++p)
-        if (L->prow[p] == r) { pr[np].key = L->pval[p]; pr[np].pos = p; ++np; }
-    /* step 3: removals (:1147-1167) */
-    KP* bi = (KP*)malloc((size_t)(n + 1) * sizeof(KP));
-    for (int64_t i = 0; i < n; ++i) { bi[i].key = o_fp4_decode(vals[i] & 0xF); bi[i].pos = i; }
-    qsort(bi, (size_t)n, sizeof(KP), cmp_kp_asc);
-    uint8_t* rm = (uint8_t*)calloc((size_t)n + 1, 1);
-    int64_t nrm = 0;
-    for (int64_t a = 0; a < n && nrm < max_prune; ++a) {
-        const int64_t k = bi[a].pos;
-        const int64_t keep = n - nrm;
-        const float imp = bi[a].key;
-        const float fl = (imp < imp_eps) ? imp_eps : imp;   /* std::max(imp, eps) */
-        if (fl < cutoff || keep > max_rw) { rm[k] = 1; ++nrm; }
-    }
-    /* step 4: adds (:1171-1201) */
-    qsort(pr, (size_t)np, sizeof(KP), cmp_kp_desc);
-    const int64_t slots = (int64_t)max_rw - (n - nrm);
-    uint32_t* add_c = (uint32_t*)malloc((size_t)(np + 1) * sizeof(uint32_t));
-    float* add_s = (float*)malloc((size_t)(np + 1) * sizeof(float));
-    int64_t nadd = 0;
-    for (int64_t a = 0; a < np; ++a) {
-        if ((uint64_t)nadd >= (uint64_t)slots) break;
-        const uint32_t c = (uint32_t)L->pcol[pr[a].pos];
-        int exists = 0;
-        for (int64_t i = 0; i < n; ++i) if (cols[i] == c) { exists = 1; break; }
-        if (!exists) { add_c[nadd] = c; add_s[nadd] = pr[a].key; ++nadd; }
-    }
-    /* step 5: apply removes high col first (:1203-1233) */
-    int64_t m = 0;
-    for (int64_t i = 0; i < n; ++i) {
-        if (rm[i]) { if (L->out_degree[cols[i]] > 0) L->out_degree[cols[i]]--; continue; }
-        cols[m] = cols[i]; vals[m] = vals[i]; ++m;
-    }
-    int rc = row_write(L, r, cols, vals, m);
-    /* step 6: inserts in score order (:1235-1255) */
-    for (int64_t a = 0; a < nadd && rc == O_OK; ++a) {
-        const uint32_t c = add_c[a];
-        int64_t i = 0;
-        while (i < m && cols[i] < c) ++i;
-        if (i < m && cols[i] == c) { rc = O_EHEADROOM; break; }   /* insert_col false -> throw */
-        if (!insert_fits(L, r, cols, m, c)) { rc = O_EHEADROOM; break; }
-        memmove(cols + i + 1, cols + i, (size_t)(m - i) * sizeof(uint32_t));
-        memmove(vals + i + 1, vals + i, (size_t)(m - i));
-        cols[i] = c;
-        vals[i] = (uint8_t)((o_fp4_encode(0.0f) << 4) | o_fp4_encode(add_s[a]));
-        ++m;
-        rc = row_write(L, r, cols, vals, m);
-        if (rc == O_OK) L->out_degree[c]++;
-    }
-    (void)cmp_u32_desc;
-    free(cols); free(vals); free(pr); free(bi); free(rm); free(add_c); free(add_s);
-    if (rc == O_OK) *did = 1;
-    return rc;
-}
+/* o_synap_row_step: after the block4 section below */
 
 /* ── headroom management ─────────────────────────────────────────────────── */
 /* delta_csr_shift_row, delta_csr_memory.hpp:225-293 */
@@ -1079,8 +1021,50 @@ void o_stats(const OLayer* L, double* s) {
     s[0] = L->value_l1; s[1] = L->value_l2_sq; s[2] = L->value_max_abs;
     s[3] = L->importance_l1; s[4] = L->importance_l2_sq; s[5] = L->importance_max_abs;
 }
-int64_t o_export_nnz(const OLayer* L) { return L->total_nnz; }
-void o_export(const OLayer* L, int* ptrs, int* idx, float* w, float* imp) { to_absolute(L, ptrs, idx, w, imp); }
+/* delta_csr_combined_to_absolute, delta_csr_memory.hpp:127-213: per row the
+ * scattered synapses then the row's live block4 slots, std::sort by column */
+static int lt_i32_asc(int64_t a, int64_t b, const void* c) { const int* k = (const int*)c; return k[a] < k[b]; }
+static int64_t b4_live_slots(const OLayer* L) {
+    int64_t n = 0;
+    for (int64_t br = 0; br < L->b4_rows; ++br)
+        for (int64_t e = 0; e < L->b4[br].n; ++e)
+            for (int li = 0; li < 4; ++li)
+                for (int lj = 0; lj < 4; ++lj)
+                    if (L->b4[br].t[e].s[B4_SLOT(li, lj)] && br * 4 + li < L->rows && (int64_t)L->b4[br].t[e].bc * 4 + lj < L->cols) ++n;
+    return n;
+}
+int64_t o_export_nnz(const OLayer* L) { return L->total_nnz + (o_b4_ntiles(L) ? b4_live_slots(L) : 0); }
+void o_export(const OLayer* L, int* ptrs, int* idx, float* w, float* imp) {
+    if (o_b4_ntiles(L) == 0) { to_absolute(L, ptrs, idx, w, imp); return; }
+    ptrs[0] = 0;
+    int64_t o = 0;
+    for (int64_t r = 0; r < L->rows; ++r) {
+        const int64_t n = row_nnz(L, r), br = r / 4, li = r % 4;
+        const int64_t cap = n + 4 * L->b4[br].n + 1;
+        int* cc = (int*)malloc((size_t)cap * sizeof(int));
+        float* ww = (float*)malloc((size_t)cap * sizeof(float));
+        float* ii = (float*)malloc((size_t)cap * sizeof(float));
+        int64_t* pm = (int64_t*)malloc((size_t)cap * sizeof(int64_t));
+        uint32_t* cols = (uint32_t*)malloc((size_t)n * 4 + 4);
+        decode_row(L, r, cols);
+        int64_t m = 0;
+        for (int64_t k = 0; k < n; ++k) {
+            cc[m] = (int)cols[k]; ww[m] = get_w(L, L->elem_start[r] + k); ii[m] = get_imp(L, L->elem_start[r] + k); ++m;
+        }
+        for (int64_t e = 0; e < L->b4[br].n; ++e)
+            for (int lj = 0; lj < 4; ++lj) {
+                const uint8_t byte = L->b4[br].t[e].s[B4_SLOT(li, lj)];
+                const int64_t col = (int64_t)L->b4[br].t[e].bc * 4 + lj;
+                if (byte == 0 || col >= L->cols) continue;
+                cc[m] = (int)col; ww[m] = o_fp4_decode(byte & 0xF); ii[m] = o_fp4_decode((uint8_t)(byte >> 4)); ++m;
+            }
+        for (int64_t q = 0; q < m; ++q) pm[q] = q;
+        o_std_sort(pm, m, lt_i32_asc, cc);
+        for (int64_t q = 0; q < m; ++q) { idx[o] = cc[pm[q]]; w[o] = ww[pm[q]]; imp[o] = ii[pm[q]]; ++o; }
+        ptrs[r + 1] = (int)o;
+        free(cc); free(ww); free(ii); free(pm); free(cols);
+    }
+}
 
 /* ── activation sparsifiers ─────────────────────────────────────────────── */
 /* dense_to_csr, cpu_backend.cpp:3075-3116 */
@@ -1235,5 +1219,833 @@ int o_topk_dyx_step(OLayer* L, const float* x, const float* dy, int batch, int64
                                  (int64_t)nn * 8 + 4096, (int64_t)nn + 64, 0.2f, L->max_idx_bytes, L->max_val_bytes);
     free(cr); free(cc); free(cs); free(p); free(ix); free(w); free(im); free(e); free(drop);
     free(np_); free(nix); free(nw); free(nim);
+    return rc;
+}
+
+/* ══ std::sort restatement ══════════════════════════════════════════════════
+ * The reference orders synapses by stored importance and probes by score with
+ * std::sort (delta_csr_memory.hpp:1149-1152, :1182-1185), which is not stable;
+ * stored importances take only 15 values, so which tied synapses are pruned is
+ * decided by the sort's own permutation.  This is the introsort of GCC's
+ * libstdc++ (the reference's toolchain): median-of-three pivot moved to the
+ * front, unguarded Hoare partition, depth limit 2*floor(log2 n) with heapsort
+ * fallback, final insertion sort with threshold 16.  Restated from the
+ * algorithm so the same permutation can be produced here and on the GPU. */
+
+static void ss_adjust_heap(int64_t* f, int64_t hole, int64_t len, int64_t val, o_less_fn lt, const void* c) {
+    const int64_t top = hole;
+    int64_t child = hole;
+    while (child < (len - 1) / 2) {
+        child = 2 * (child + 1);
+        if (lt(f[child], f[child - 1], c)) child--;
+        f[hole] = f[child];
+        hole = child;
+    }
+    if ((len & 1) == 0 && child == (len - 2) / 2) {
+        child = 2 * (child + 1);
+        f[hole] = f[child - 1];
+        hole = child - 1;
+    }
+    int64_t parent = (hole - 1) / 2;
+    while (hole > top && lt(f[parent], val, c)) {
+        f[hole] = f[parent];
+        hole = parent;
+        parent = (hole - 1) / 2;
+    }
+    f[hole] = val;
+}
+static void ss_heapsort(int64_t* f, int64_t n, o_less_fn lt, const void* c) {
+    if (n >= 2)
+        for (int64_t parent = (n - 2) / 2;; --parent) {
+            ss_adjust_heap(f, parent, n, f[parent], lt, c);
+            if (parent == 0) break;
+        }
+    for (int64_t last = n; last > 1;) {
+        --last;
+        const int64_t v = f[last];
+        f[last] = f[0];
+        ss_adjust_heap(f, 0, last, v, lt, c);
+    }
+}
+static void ss_swap(int64_t* a, int64_t* b) { const int64_t t = *a; *a = *b; *b = t; }
+static void ss_introsort(int64_t* f, int64_t* l, int64_t depth, o_less_fn lt, const void* c) {
+    while (l - f > 16) {
+        if (depth == 0) { ss_heapsort(f, l - f, lt, c); return; }
+        --depth;
+        int64_t *a = f + 1, *b = f + (l - f) / 2, *z = l - 1;
+        if (lt(*a, *b, c)) {
+            if (lt(*b, *z, c)) ss_swap(f, b);
+            else if (lt(*a, *z, c)) ss_swap(f, z);
+            else ss_swap(f, a);
+        } else if (lt(*a, *z, c)) ss_swap(f, a);
+        else if (lt(*b, *z, c)) ss_swap(f, z);
+        else ss_swap(f, b);
+        int64_t *lo = f + 1, *hi = l;
+        for (;;) {
+            while (lt(*lo, *f, c)) ++lo;
+            --hi;
+            while (lt(*f, *hi, c)) --hi;
+            if (!(lo < hi)) break;
+            ss_swap(lo, hi);
+            ++lo;
+        }
+        ss_introsort(lo, l, depth, lt, c);
+        l = lo;
+    }
+}
+static void ss_linear_insert(int64_t* p, o_less_fn lt, const void* c) {
+    const int64_t v = *p;
+    int64_t* q = p - 1;
+    while (lt(v, *q, c)) { *p = *q; p = q; --q; }
+    *p = v;
+}
+static void ss_insertion(int64_t* f, int64_t* l, o_less_fn lt, const void* c) {
+    if (f == l) return;
+    for (int64_t* i = f + 1; i != l; ++i) {
+        if (lt(*i, *f, c)) {
+            const int64_t v = *i;
+            memmove(f + 1, f, (size_t)(i - f) * sizeof(int64_t));
+            *f = v;
+        } else ss_linear_insert(i, lt, c);
+    }
+}
+void o_std_sort(int64_t* a, int64_t n, o_less_fn lt, const void* c) {
+    if (n <= 1) return;
+    int lg = 0;
+    while (((int64_t)1 << (lg + 1)) <= n) ++lg;
+    ss_introsort(a, a + n, 2 * (int64_t)lg, lt, c);
+    if (n > 16) {
+        ss_insertion(a, a + 16, lt, c);
+        for (int64_t* i = a + 16; i != a + n; ++i) ss_linear_insert(i, lt, c);
+    } else ss_insertion(a, a + n, lt, c);
+}
+
+/* test hook: sort indices 0..n-1 by keys ascending (desc != 0: descending) */
+static int lt_f_asc(int64_t a, int64_t b, const void* c) { const float* k = (const float*)c; return k[a] < k[b]; }
+static int lt_f_desc(int64_t a, int64_t b, const void* c) { const float* k = (const float*)c; return k[a] > k[b]; }
+void o_std_sort_keys(const float* keys, int64_t n, int desc, int64_t* perm) {
+    for (int64_t i = 0; i < n; ++i) perm[i] = i;
+    o_std_sort(perm, n, desc ? lt_f_desc : lt_f_asc, keys);
+}
+
+/* ══ block4: 4x4 dense FP4 tiles ════════════════════════════════════════════
+ * Logical content of the reference's Block4Store (block4.hpp:1016-1490): per
+ * block-row br (input rows 4br..4br+3) the tiles in ascending block-column bc,
+ * 16 slot bytes each, slot = lj*4 + li (Block4Tile::slot_index,
+ * block4.hpp:309), byte = importance code << 4 | weight code.  The sparse
+ * packing of tiles with <= switch_point live slots is represented by a flag
+ * and its byte length (block4_sparse_packed_len, :340-343), which is all the
+ * reference's accounting needs: per block-row allocations of index bytes,
+ * tile bytes and tile slots, grown and shifted exactly as the reference does,
+ * because they decide headroom growth, budget errors and the eviction in
+ * merge_row_workspace. */
+
+static int b4_live(const uint8_t* s) { int n = 0; for (int i = 0; i < 16; ++i) n += s[i] != 0; return n; }
+static int64_t b4_sparse_len(int n) { return 1 + (n + 1) / 2 + n; }
+static int64_t b4_tlen(const OTile* t) { return t->sparse ? b4_sparse_len(b4_live(t->s)) : 16; }
+static int64_t b4_tile_used(const OLayer* L, int64_t br) {
+    int64_t u = 0;
+    for (int64_t e = 0; e < L->b4[br].n; ++e) u += b4_tlen(&L->b4[br].t[e]);
+    return u;
+}
+static int64_t b4_idx_used(const OLayer* L, int64_t br) {
+    int64_t u = 0; uint32_t prev = 0;
+    for (int64_t e = 0; e < L->b4[br].n; ++e) { u += uleb_len((uint32_t)L->b4[br].t[e].bc - prev); prev = (uint32_t)L->b4[br].t[e].bc; }
+    return u;
+}
+static int64_t b4_sum(const int64_t* a, int64_t n) { int64_t s = 0; for (int64_t i = 0; i < n; ++i) s += a[i]; return s; }
+int64_t o_b4_ntiles(const OLayer* L) {
+    int64_t n = 0;
+    for (int64_t br = 0; br < L->b4_rows; ++br) n += L->b4[br].n;
+    return n;
+}
+
+static void b4_free(OLayer* L) {
+    if (L->b4) for (int64_t br = 0; br < L->b4_rows; ++br) free(L->b4[br].t);
+    free(L->b4); free(L->b4_idx_alloc); free(L->b4_tile_alloc); free(L->b4_elem_alloc);
+    L->b4 = NULL; L->b4_idx_alloc = L->b4_tile_alloc = L->b4_elem_alloc = NULL;
+}
+/* Block4Store::init, block4.hpp:1103-1117 */
+static void b4_init(OLayer* L) {
+    b4_free(L);
+    L->b4_rows = (L->rows + 3) / 4;
+    L->b4_cols = (L->cols + 3) / 4;
+    L->b4 = (struct OTileRow*)calloc((size_t)L->b4_rows + 1, sizeof(struct OTileRow));
+    L->b4_idx_alloc = (int64_t*)calloc((size_t)L->b4_rows + 1, 8);
+    L->b4_tile_alloc = (int64_t*)calloc((size_t)L->b4_rows + 1, 8);
+    L->b4_elem_alloc = (int64_t*)calloc((size_t)L->b4_rows + 1, 8);
+}
+static int64_t b4_find(const OLayer* L, int64_t br, int32_t bc) {
+    const struct OTileRow* R = &L->b4[br];
+    for (int64_t e = 0; e < R->n; ++e) {
+        if (R->t[e].bc == bc) return e;
+        if (R->t[e].bc > bc) break;
+    }
+    return -1;
+}
+
+/* block4_row_shift, block4.hpp:497-609: set one block-row's allocations to
+ * the targets, never below what it uses; the last block-row never moves. */
+static int b4_row_shift(OLayer* L, int64_t br, int64_t ti, int64_t tt, int64_t te) {
+    const int64_t ui = b4_idx_used(L, br), ut = b4_tile_used(L, br), ue = L->b4[br].n;
+    if (ti < ui) ti = ui;
+    if (tt < ut) tt = ut;
+    if (te < ue) te = ue;
+    if (br + 1 >= L->b4_rows) return O_OK;
+    if (L->b4_idx_alloc[br] != ti) {
+        if (ti > L->b4_idx_alloc[br] && b4_sum(L->b4_idx_alloc, L->b4_rows) + (ti - L->b4_idx_alloc[br]) > L->b4_max_idx)
+            return O_ENOMEM;
+        L->b4_idx_alloc[br] = ti;
+    }
+    if (L->b4_tile_alloc[br] != tt) {
+        if (tt > L->b4_tile_alloc[br] && b4_sum(L->b4_tile_alloc, L->b4_rows) + (tt - L->b4_tile_alloc[br]) > L->b4_max_tile)
+            return O_ENOMEM;
+        L->b4_tile_alloc[br] = tt;
+    }
+    L->b4_elem_alloc[br] = te;
+    return O_OK;
+}
+/* block4_grow_last_row, block4.hpp:611-646 */
+static int b4_grow_last(OLayer* L, int64_t ti, int64_t tt, int64_t te) {
+    const int64_t r = L->b4_rows - 1;
+    if (r < 0) return O_OK;
+    if (ti > L->b4_idx_alloc[r]) {
+        if (b4_sum(L->b4_idx_alloc, L->b4_rows) + (ti - L->b4_idx_alloc[r]) > L->b4_max_idx) return O_ENOMEM;
+        L->b4_idx_alloc[r] = ti;
+    }
+    if (tt > L->b4_tile_alloc[r]) {
+        if (b4_sum(L->b4_tile_alloc, L->b4_rows) + (tt - L->b4_tile_alloc[r]) > L->b4_max_tile) return O_ENOMEM;
+        L->b4_tile_alloc[r] = tt;
+    }
+    if (te > L->b4_elem_alloc[r]) L->b4_elem_alloc[r] = te;
+    return O_OK;
+}
+/* block4_ensure_row_headroom, block4.hpp:648-668: room for one more tile */
+static int b4_ensure_headroom(OLayer* L, int64_t br) {
+    const int64_t ti = L->b4_idx_alloc[br] + 5, tt = L->b4_tile_alloc[br] + 1, te = L->b4_elem_alloc[br] + 1;
+    return br + 1 < L->b4_rows ? b4_row_shift(L, br, ti, tt, te) : b4_grow_last(L, ti, tt, te);
+}
+/* block4_row_insert_tile, block4.hpp:670-771: an empty sparse tile (1 byte) */
+static int b4_insert_tile(OLayer* L, int64_t br, int32_t bc) {
+    struct OTileRow* R = &L->b4[br];
+    int64_t p = 0;
+    while (p < R->n && R->t[p].bc < bc) ++p;
+    if (p < R->n && R->t[p].bc == bc) return 0;
+    const uint32_t prev = p > 0 ? (uint32_t)R->t[p - 1].bc : 0u;
+    int64_t delta = uleb_len((uint32_t)bc - prev);
+    if (p < R->n) delta += uleb_len((uint32_t)R->t[p].bc - (uint32_t)bc) - uleb_len((uint32_t)R->t[p].bc - prev);
+    if (delta > 0 && delta > L->b4_idx_alloc[br] - b4_idx_used(L, br)) return 0;
+    if (R->n >= L->b4_elem_alloc[br]) return 0;
+    if (1 > L->b4_tile_alloc[br] - b4_tile_used(L, br)) return 0;
+    if (R->n + 1 > R->cap) {
+        R->cap = R->cap ? R->cap * 2 : 8;
+        R->t = (OTile*)realloc(R->t, (size_t)R->cap * sizeof(OTile));
+    }
+    memmove(R->t + p + 1, R->t + p, (size_t)(R->n - p) * sizeof(OTile));
+    memset(&R->t[p], 0, sizeof(OTile));
+    R->t[p].bc = bc;
+    R->t[p].sparse = 1;
+    R->n++;
+    return 1;
+}
+/* Block4Store::get_or_create, block4.hpp:1168-1184 */
+static int b4_get_or_create(OLayer* L, int64_t br, int32_t bc, int64_t* e) {
+    *e = b4_find(L, br, bc);
+    if (*e >= 0) return O_OK;
+    if (!b4_insert_tile(L, br, bc)) {
+        const int rc = b4_ensure_headroom(L, br);
+        if (rc) return rc;
+        b4_insert_tile(L, br, bc);
+    }
+    *e = b4_find(L, br, bc);
+    return O_OK;
+}
+/* commit_dirty_sparse_tile, block4.hpp:1223-1268: repack, sparse iff live <=
+ * switch_point; growth past the row's headroom takes the shortfall from the
+ * buffer (block4_resize_tile_in_row, :906-957) or, over budget, is dropped. */
+static void b4_commit(OLayer* L, int64_t br, int64_t e, const uint8_t* s) {
+    OTile* t = &L->b4[br].t[e];
+    const int n = b4_live(s);
+    const int sp = (uint32_t)n <= L->b4_switch;
+    const int64_t nl = sp ? b4_sparse_len(n) : 16, cl = b4_tlen(t);
+    if (nl > cl) {
+        const int64_t head = L->b4_tile_alloc[br] - b4_tile_used(L, br);
+        if (nl - cl > head) {
+            const int64_t sf = nl - cl - head;
+            if (b4_sum(L->b4_tile_alloc, L->b4_rows) + sf > L->b4_max_tile) { L->b4_dropped++; return; }
+            L->b4_tile_alloc[br] += sf;
+        }
+    }
+    memcpy(t->s, s, 16);
+    t->sparse = (uint8_t)sp;
+}
+/* a write through a Block4TileHandle: sparse tiles are unpacked to scratch
+ * and committed when the handle dies; dense tiles are written in place */
+static void b4_write(OLayer* L, int64_t br, int64_t e, const uint8_t* s) {
+    OTile* t = &L->b4[br].t[e];
+    if (t->sparse) b4_commit(L, br, e, s);
+    else memcpy(t->s, s, 16);
+}
+/* Block4Store::maybe_compress, block4.hpp:1193-1206 */
+static void b4_maybe_compress(OLayer* L, int64_t br, int64_t e) {
+    OTile* t = &L->b4[br].t[e];
+    if (t->sparse || (uint32_t)b4_live(t->s) > L->b4_switch) return;
+    t->sparse = 1;
+}
+/* Block4Store::erase -> block4_row_remove_tile, block4.hpp:773-888 */
+static void b4_erase(OLayer* L, int64_t br, int32_t bc) {
+    const int64_t e = b4_find(L, br, bc);
+    if (e < 0) return;
+    struct OTileRow* R = &L->b4[br];
+    memmove(R->t + e, R->t + e + 1, (size_t)(R->n - e - 1) * sizeof(OTile));
+    R->n--;
+}
+
+/* block4_expand_headroom, delta_csr_memory.hpp:769-823 (compact_block4 is
+ * blank_fraction 0, min_slack 0) */
+int o_b4_expand_headroom(OLayer* L, float bf, int64_t min_slack) {
+    if (L->b4_rows == 0) return O_OK;
+    int64_t total = 0;
+    int64_t* na = (int64_t*)malloc((size_t)L->b4_rows * 8);
+    for (int64_t br = 0; br < L->b4_rows; ++br) {
+        const int64_t rb = b4_tile_used(L, br);
+        na[br] = rb + (int64_t)((float)rb * bf) + min_slack;
+        total += na[br];
+    }
+    if (total > L->b4_max_tile) { free(na); return O_ENOMEM; }
+    memcpy(L->b4_tile_alloc, na, (size_t)L->b4_rows * 8);
+    free(na);
+    return O_OK;
+}
+/* Block4Store::equalize_step, block4.hpp:1208-1221 */
+int o_b4_equalize_step(OLayer* L, int64_t row) {
+    const int64_t R = L->b4_rows;
+    if (R == 0) return O_OK;
+    row %= R;
+    const int64_t ti = (b4_sum(L->b4_idx_alloc, R) + R - 1) / R;
+    const int64_t tt = (b4_sum(L->b4_tile_alloc, R) + R - 1) / R;
+    const int64_t te = (b4_sum(L->b4_elem_alloc, R) + R - 1) / R;
+    return b4_row_shift(L, row, ti, tt, te);
+}
+void o_b4_set_switch_point(OLayer* L, uint32_t v) { L->b4_switch = v; }
+
+/* block4_load_dense, delta_csr_memory.hpp:843-945, via load_dense_codes
+ * (cpu_backend.cpp:910-921): every (br, bc) tile is created, codes written
+ * raw (weight | importance << 4), then block4_expand_headroom(0.2, 16);
+ * out_degree = n_in for every column.  The scattered CSR is left as is. */
+int o_load_dense_codes(OLayer* L, const uint8_t* wc, const uint8_t* ic) {
+    const int64_t n_in = L->rows, n_out = L->cols;
+    b4_init(L);
+    const int64_t BR = L->b4_rows, BC = L->b4_cols;
+    const int64_t dense = BR * BC * 16;
+    L->b4_max_idx = BR * BC * 16;
+    L->b4_max_tile = (int64_t)((double)dense * (1.0 + (double)0.2f)) + BR * 16;
+    for (int64_t br = 0; br < BR; ++br) {
+        for (int64_t bc = 0; bc < BC; ++bc) {
+            int64_t e;
+            const int rc = b4_get_or_create(L, br, (int32_t)bc, &e);
+            if (rc) return rc;
+            uint8_t s[16];
+            memcpy(s, L->b4[br].t[e].s, 16);
+            for (int64_t row = br * 4; row < br * 4 + 4 && row < n_in; ++row)
+                for (int64_t col = bc * 4; col < bc * 4 + 4 && col < n_out; ++col) {
+                    const int64_t i = row * n_out + col;
+                    s[B4_SLOT(row - br * 4, col - bc * 4)] = (uint8_t)(wc[i] | (ic[i] << 4));
+                }
+            b4_write(L, br, e, s);
+        }
+    }
+    const int rc = o_b4_expand_headroom(L, 0.2f, 16);
+    for (int64_t c = 0; c < n_out; ++c) L->out_degree[c] = (int)n_in;
+    return rc;
+}
+
+/* ── block4 state export ─────────────────────────────────────────────────── */
+void o_b4_export(const OLayer* L, int* br_out, int* bc_out, uint8_t* slots, uint8_t* sparse) {
+    int64_t t = 0;
+    for (int64_t br = 0; br < L->b4_rows; ++br)
+        for (int64_t e = 0; e < L->b4[br].n; ++e, ++t) {
+            br_out[t] = (int)br; bc_out[t] = L->b4[br].t[e].bc;
+            memcpy(slots + 16 * t, L->b4[br].t[e].s, 16);
+            if (sparse) sparse[t] = L->b4[br].t[e].sparse;
+        }
+}
+/* per block-row: idx alloc, idx used, tile alloc, tile used, elem alloc, tiles */
+void o_b4_rows(const OLayer* L, int64_t* out) {
+    for (int64_t br = 0; br < L->b4_rows; ++br) {
+        out[6 * br + 0] = L->b4_idx_alloc[br]; out[6 * br + 1] = b4_idx_used(L, br);
+        out[6 * br + 2] = L->b4_tile_alloc[br]; out[6 * br + 3] = b4_tile_used(L, br);
+        out[6 * br + 4] = L->b4_elem_alloc[br]; out[6 * br + 5] = L->b4[br].n;
+    }
+}
+/* Block4View counters (cpu_backend.cpp:51-98): tiles, live synapses,
+ * switch_point, dropped_growth_events, row_merge_overflow_events,
+ * row_merge_overflow_bytes_dropped, used_bytes, alloc_bytes */
+void o_b4_view(const OLayer* L, int64_t* v) {
+    int64_t live = 0, used = 0;
+    for (int64_t br = 0; br < L->b4_rows; ++br) {
+        for (int64_t e = 0; e < L->b4[br].n; ++e) live += b4_live(L->b4[br].t[e].s);
+        used += b4_tile_used(L, br);
+    }
+    v[0] = o_b4_ntiles(L); v[1] = live; v[2] = L->b4_switch; v[3] = (int64_t)L->b4_dropped;
+    v[4] = (int64_t)L->b4_ovf_events; v[5] = (int64_t)L->b4_ovf_bytes; v[6] = used;
+    v[7] = b4_sum(L->b4_tile_alloc, L->b4_rows);
+}
+
+/* ── block4 forward, linear_disldo.hpp:128-339 (num_cpus = 1) ───────────── */
+static void b4_forward(const OLayer* L, const float* x, int batch, float* y) {
+    const int64_t n_in = L->rows, n_out = L->cols;
+    if (o_b4_ntiles(L) == 0) return;
+    float* mo = (float*)calloc((size_t)batch * n_out + 1, sizeof(float));
+    for (int64_t br = 0; br < L->b4_rows; ++br)
+        for (int64_t e = 0; e < L->b4[br].n; ++e) {
+            const OTile* t = &L->b4[br].t[e];
+            for (int lj = 0; lj < 4; ++lj) {
+                const int64_t col = (int64_t)t->bc * 4 + lj;
+                if (col >= n_out) continue;
+                float w4[4]; int64_t ri[4];
+                for (int li = 0; li < 4; ++li) {
+                    const int64_t row = br * 4 + li;
+                    if (row < n_in) { w4[li] = o_fp4_decode(t->s[B4_SLOT(li, lj)] & 0xF) * o_get_scale(L, (int)row, (int)col); ri[li] = row; }
+                    else { w4[li] = 0.0f; ri[li] = 0; }
+                }
+                for (int b = 0; b < batch; ++b) {
+                    const float* xr = x + (int64_t)b * n_in;
+                    /* the reference build's evaluation of acc += w4[li]*x (li = 0..3) */
+                    const float acc = fmaf(w4[0], xr[ri[0]], w4[1] * xr[ri[1]]) + fmaf(w4[2], xr[ri[2]], w4[3] * xr[ri[3]]);
+                    mo[(int64_t)b * n_out + col] += acc;
+                }
+            }
+        }
+    for (int64_t i = 0; i < (int64_t)batch * n_out; ++i) y[i] += mo[i];
+    free(mo);
+}
+
+/* ── block4 backward, linear_disldo.hpp:939-1951 (num_cpus = 1) ─────────── */
+/* Block4Vec horizontal sum of the per-row scale-gradient terms
+ * (block4_vec_hsum, block4.hpp:75-77) as the reference's build evaluates it:
+ * lanes 0+2 and 1+3 first (pinned against the reference build) */
+static inline float b4_hsum(const float* p) { return (p[0] + p[2]) + (p[1] + p[3]); }
+
+static void b4_true_importance_evict(OLayer* L, int64_t br, OTile* ws, int64_t n) {
+    /* Block4Store::merge_row_workspace, block4.hpp:1368-1465: while the row's
+     * packed bytes exceed its allocation, zero the live slot of smallest
+     * |decoded importance * importance_scale(row) * output_importance_scale(col)|
+     * (first in tile, li, lj order on ties) and repack that tile. */
+    const int64_t cap = L->b4_tile_alloc[br];
+    for (;;) {
+        int64_t used = 0;
+        for (int64_t e = 0; e < n; ++e) used += b4_tlen(&ws[e]);
+        if (used <= cap) break;
+        double best = -1.0; int64_t be = 0; int bli = 0, blj = 0;
+        for (int64_t e = 0; e < n; ++e)
+            for (int li = 0; li < 4; ++li)
+                for (int lj = 0; lj < 4; ++lj) {
+                    const uint8_t byte = ws[e].s[B4_SLOT(li, lj)];
+                    if (byte == 0) continue;
+                    const int64_t row = br * 4 + li, col = (int64_t)ws[e].bc * 4 + lj;
+                    const double ti = (double)o_fp4_decode((uint8_t)((byte >> 4) & 0xF)) *
+                                      (double)o_get_importance_scale(L, (int)row) *
+                                      (double)o_get_output_importance_scale(L, (int)col);
+                    const double a = fabs(ti);
+                    if (best < 0.0 || a < best) { best = a; be = e; bli = li; blj = lj; }
+                }
+        if (best < 0.0) break;
+        ws[be].s[B4_SLOT(bli, blj)] = 0;
+        ws[be].sparse = (uint32_t)b4_live(ws[be].s) <= L->b4_switch;
+    }
+    int64_t used = 0, fit = 0, ft = 0;
+    for (int64_t e = 0; e < n; ++e) used += b4_tlen(&ws[e]);
+    for (int64_t e = 0; e < n; ++e) {
+        const int64_t tl = b4_tlen(&ws[e]);
+        if (fit + tl > cap) break;
+        fit += tl; ++ft;
+    }
+    if (ft < n) { L->b4_ovf_events++; L->b4_ovf_bytes += (uint64_t)(used - fit); }
+}
+
+static void b4_backward(OLayer* L, const float* x, const float* dy, int batch, float lr, int lr_per_row_nnz,
+                        int damp, float beta2, float eps, float* dx, float* colg, float* colc, uint64_t call) {
+    const int64_t n_in = L->rows, n_out = L->cols, rank = L->rank;
+    if (o_b4_ntiles(L) == 0) return;
+    uint32_t* rlc = (uint32_t*)calloc((size_t)n_in + 1, sizeof(uint32_t));
+    for (int64_t br = 0; br < L->b4_rows; ++br) {
+        if (L->b4[br].n == 0) continue;
+        for (int li = 0; li < 4; ++li)
+            if (br * 4 + li < n_in) rlc[br * 4 + li] = (uint32_t)L->b4[br].n * 4u;
+    }
+    double* trg = (double*)calloc((size_t)(n_in * rank) + 1, sizeof(double));
+    double* trc = (double*)calloc((size_t)(n_in * rank) + 1, sizeof(double));
+    const int training = lr != 0.0f;
+    for (int64_t br = 0; br < L->b4_rows; ++br) {
+        struct OTileRow* R = &L->b4[br];
+        if (R->n == 0) continue;
+        OTile* ws = (OTile*)malloc((size_t)R->n * sizeof(OTile));
+        memcpy(ws, R->t, (size_t)R->n * sizeof(OTile));
+        for (int64_t e = 0; e < R->n; ++e) {
+            uint8_t* td = ws[e].s;
+            const int64_t bc = ws[e].bc;
+            int dirty = 0;
+            for (int li = 0; li < 4; ++li) {
+                const int64_t row = br * 4 + li;
+                if (row >= n_in) continue;
+                const uint32_t nnz_row = rlc[row];
+                if (nnz_row == 0) continue;
+                const float imp_scale = o_get_importance_scale(L, (int)row);
+                const float eff_lr = lr_per_row_nnz ? lr / (float)nnz_row : lr;
+                float vsk[4];
+                for (int64_t k = 0; k < rank; ++k) vsk[k] = o_get_value_scale_k(L, (int)row, (int)k);
+                int64_t col4[4]; int valid[4];
+                float S4[4], cis4[4], quant[4], ci[4], qorig[4], osk[4][4];
+                for (int lj = 0; lj < 4; ++lj) {
+                    const int64_t col = bc * 4 + lj;
+                    valid[lj] = col < n_out;
+                    if (!valid[lj]) {
+                        col4[lj] = 0; S4[lj] = cis4[lj] = quant[lj] = ci[lj] = qorig[lj] = 0.0f;
+                        for (int64_t k = 0; k < rank; ++k) osk[k][lj] = 0.0f;
+                        continue;
+                    }
+                    col4[lj] = col;
+                    const uint8_t byte = td[B4_SLOT(li, lj)];
+                    const float ois = o_get_output_importance_scale(L, (int)col);
+                    S4[lj] = o_get_scale(L, (int)row, (int)col);
+                    cis4[lj] = imp_scale * ois;
+                    quant[lj] = qorig[lj] = o_fp4_decode(byte & 0xF);
+                    ci[lj] = o_fp4_decode((uint8_t)(byte >> 4)) * cis4[lj];
+                    for (int64_t k = 0; k < rank; ++k) osk[k][lj] = o_get_output_scale_k(L, (int)col, (int)k);
+                }
+                float mcol[4][4] = {{0}}, mcolc[4][4] = {{0}};
+                double mrow[4] = {0, 0, 0, 0}, mrowc[4] = {0, 0, 0, 0};
+                const int full = bc * 4 + 4 <= n_out;
+                for (int b = 0; b < batch; ++b) {
+                    const float iv = x[(int64_t)b * n_in + row];
+                    float* d = &dx[(int64_t)b * n_in + row];
+                    if (full) {
+                        float dyv[4], g[4], qf[4], cb[4];
+                        for (int lj = 0; lj < 4; ++lj) { dyv[lj] = dy[(int64_t)b * n_out + col4[lj]]; g[lj] = dyv[lj] * iv; }
+                        if (training) {
+                            for (int lj = 0; lj < 4; ++lj) {
+                                cb[lj] = qorig[lj] * iv;
+                                ci[lj] = bounded_ci(ci[lj], g[lj], cb[lj], beta2);
+                                quant[lj] = fmaf(eff_lr, bounded_raw(g[lj], ci[lj], S4[lj], eps, damp), quant[lj]);
+                                qf[lj] = (quant[lj] == 0.0f) ? 0.1f : quant[lj];
+                            }
+                            for (int64_t k = 0; k < rank; ++k) {
+                                float p[4], pc[4];
+                                for (int lj = 0; lj < 4; ++lj) { p[lj] = (qf[lj] * osk[k][lj]) * g[lj]; pc[lj] = (qf[lj] * osk[k][lj]) * cb[lj]; }
+                                mrow[k] += (double)b4_hsum(p);
+                                for (int lj = 0; lj < 4; ++lj) mcol[k][lj] = fmaf(qf[lj] * vsk[k], g[lj], mcol[k][lj]);
+                                mrowc[k] += (double)b4_hsum(pc);
+                                for (int lj = 0; lj < 4; ++lj) mcolc[k][lj] = fmaf(qf[lj] * vsk[k], cb[lj], mcolc[k][lj]);
+                            }
+                        }
+                        /* hsum(quant*S*dy): the reference build forms quant*(S*dy) per lane
+                         * and sums the lanes pairwise */
+                        float p[4];
+                        for (int lj = 0; lj < 4; ++lj) p[lj] = quant[lj] * (S4[lj] * dyv[lj]);
+                        *d += (p[0] + p[1]) + (p[2] + p[3]);
+                    } else {
+                        for (int lj = 0; lj < 4; ++lj) {
+                            if (!valid[lj]) continue;
+                            const float dyv = dy[(int64_t)b * n_out + col4[lj]];
+                            const float g = dyv * iv, S = S4[lj];
+                            if (training) {
+                                const float cb = iv * qorig[lj];
+                                ci[lj] = bounded_ci(ci[lj], g, cb, beta2);
+                                quant[lj] = fmaf(eff_lr, bounded_raw(g, ci[lj], S, eps, damp), quant[lj]);
+                                const float qf = (quant[lj] == 0.0f) ? 0.1f : quant[lj];
+                                for (int64_t k = 0; k < rank; ++k) {
+                                    mrow[k] = fma((double)qf * (double)osk[k][lj], (double)g, mrow[k]);
+                                    mcol[k][lj] = fmaf(qf * vsk[k], g, mcol[k][lj]);
+                                    mrowc[k] = fma((double)qf * (double)osk[k][lj], (double)cb, mrowc[k]);
+                                    mcolc[k][lj] = fmaf(qf * vsk[k], cb, mcolc[k][lj]);
+                                }
+                            }
+                            *d = fmaf(quant[lj], S * dyv, *d);   /* quant*(S*dy), fused */
+                        }
+                    }
+                }
+                if (training) {
+                    for (int64_t k = 0; k < rank; ++k) { trg[row * rank + k] += mrow[k]; trc[row * rank + k] += mrowc[k]; }
+                    for (int lj = 0; lj < 4; ++lj) {
+                        if (!valid[lj]) continue;
+                        for (int64_t k = 0; k < rank; ++k) {
+                            colg[col4[lj] * rank + k] += mcol[k][lj];
+                            colc[col4[lj] * rank + k] += mcolc[k][lj];
+                        }
+                        const float imp_ratio = ci[lj] / cis4[lj];
+                        uint8_t wq, iq;
+                        if (L->stochastic) {
+                            const uint64_t el = (uint64_t)row * (uint64_t)n_out + (uint64_t)col4[lj];
+                            wq = o_fp4_quantize_stochastic_r(quant[lj], o_rng_draw(L->seed, call, el, 2));
+                            iq = o_fp4_quantize_stochastic_r(imp_ratio, o_rng_draw(L->seed, call, el, 3));
+                        } else {
+                            wq = o_fp4_encode(quant[lj]);
+                            iq = o_fp4_encode(imp_ratio);
+                        }
+                        td[B4_SLOT(li, lj)] = (uint8_t)((iq << 4) | wq);
+                        dirty = 1;
+                    }
+                }
+            }
+            if (training && dirty) ws[e].sparse = (uint32_t)b4_live(td) <= L->b4_switch;
+        }
+        if (training) {
+            b4_true_importance_evict(L, br, ws, R->n);
+            memcpy(R->t, ws, (size_t)R->n * sizeof(OTile));
+        }
+        free(ws);
+    }
+    /* block4 value_scale step, linear_disldo.hpp:1882-1950 */
+    if (training) {
+        for (int64_t row = 0; row < n_in; ++row) {
+            const uint32_t nnz_row = rlc[row];
+            if (nnz_row == 0) continue;
+            const float scale_eff_lr = lr / (float)nnz_row;
+            for (int64_t k = 0; k < rank; ++k) {
+                const double s = trg[row * rank + k], sc = trc[row * rank + k];
+                if (s == 0.0 && sc == 0.0) continue;
+                const int64_t i = row * rank + k;
+                const float g = (float)s, c = (float)sc;
+                if (!isfinite(g) || !isfinite(c)) continue;
+                float* vi = &L->value_scale_importance.d[i];
+                const float nv = fmaf(beta2, *vi, (1.0f - beta2) * fmaf(g, g, c * c));
+                if (!isfinite(nv)) continue;
+                uint32_t* st = &L->value_scale_step.d[i];
+                ++(*st);
+                const float bcor = 1.0f - powf(beta2, (float)(*st));
+                const float hat = bcor > 0.0f ? nv / bcor : nv;
+                if (!isfinite(hat)) continue;
+                const float nvs = L->value_scale.d[i] - scale_eff_lr * g / (sqrtf(hat) + eps);
+                if (!isfinite(nvs)) continue;
+                *vi = nv;
+                L->value_scale.d[i] = nvs;
+            }
+        }
+    }
+    free(rlc); free(trg); free(trc);
+}
+
+/* live block4 slots of input row r (for the dead-row test, :1961-1967) */
+static int64_t b4_row_live(const OLayer* L, int64_t row) {
+    if (L->b4_rows == 0) return 0;
+    const int64_t br = row / 4;
+    if (br >= L->b4_rows) return 0;
+    return L->b4[br].n * 4;
+}
+
+/* ── scattered row edits ─────────────────────────────────────────────────── */
+/* delta_csr_row_remove_col, delta_csr_memory.hpp:429-492 */
+static int sc_remove_col(OLayer* L, int64_t r, uint32_t c) {
+    const int64_t n = row_nnz(L, r);
+    uint32_t* cols = (uint32_t*)malloc((size_t)n * 4 + 4);
+    uint8_t* vals = (uint8_t*)malloc((size_t)n + 1);
+    decode_row(L, r, cols);
+    memcpy(vals, L->val + L->elem_start[r], (size_t)n);
+    int64_t i = 0;
+    while (i < n && cols[i] != c) ++i;
+    int found = i < n;
+    if (found) {
+        memmove(cols + i, cols + i + 1, (size_t)(n - i - 1) * 4);
+        memmove(vals + i, vals + i + 1, (size_t)(n - i - 1));
+        row_write(L, r, cols, vals, n - 1);
+    }
+    free(cols); free(vals);
+    return found;
+}
+/* delta_csr_row_insert_col, delta_csr_memory.hpp:500-585, storing
+ * ValueAccessor::set(w, imp) (deterministic codes) */
+static int sc_insert_col(OLayer* L, int64_t r, uint32_t c, float w, float imp) {
+    const int64_t n = row_nnz(L, r);
+    uint32_t* cols = (uint32_t*)malloc((size_t)n * 4 + 8);
+    uint8_t* vals = (uint8_t*)malloc((size_t)n + 2);
+    decode_row(L, r, cols);
+    memcpy(vals, L->val + L->elem_start[r], (size_t)n);
+    int64_t i = 0;
+    while (i < n && cols[i] < c) ++i;
+    int ok = !(i < n && cols[i] == c) && insert_fits(L, r, cols, n, c);
+    if (ok) {
+        memmove(cols + i + 1, cols + i, (size_t)(n - i) * 4);
+        memmove(vals + i + 1, vals + i, (size_t)(n - i));
+        cols[i] = c;
+        vals[i] = (uint8_t)((o_fp4_encode(w) << 4) | o_fp4_encode(imp));
+        row_write(L, r, cols, vals, n + 1);
+    }
+    free(cols); free(vals);
+    return ok;
+}
+
+/* block4_demote_tile, delta_csr_memory.hpp:946-1003 */
+static int b4_demote(OLayer* L, int64_t br, int32_t bc) {
+    const int64_t e = b4_find(L, br, bc);
+    if (e < 0) return O_OK;
+    uint8_t s[16];
+    memcpy(s, L->b4[br].t[e].s, 16);
+    for (int li = 0; li < 4; ++li) {
+        const int64_t row = br * 4 + li;
+        if (row >= L->rows) continue;
+        for (int lj = 0; lj < 4; ++lj) {
+            const uint8_t byte = s[B4_SLOT(li, lj)];
+            if (byte == 0) continue;
+            const int64_t col = (int64_t)bc * 4 + lj;
+            if (col >= L->cols) continue;
+            if (!sc_insert_col(L, row, (uint32_t)col, o_fp4_decode(byte & 0xF), o_fp4_decode((uint8_t)(byte >> 4))))
+                return O_EHEADROOM;
+        }
+    }
+    b4_erase(L, br, bc);
+    return O_OK;
+}
+
+/* block4_maybe_promote, delta_csr_memory.hpp:593-702 */
+static int b4_maybe_promote(OLayer* L, int64_t row, uint32_t col) {
+    const int64_t br = row / 4, bc = col / 4, li = row % 4, lj = col % 4;
+    int64_t e = b4_find(L, br, (int32_t)bc);
+    if (e >= 0) {
+        const int64_t n = row_nnz(L, row);
+        uint32_t* cols = (uint32_t*)malloc((size_t)n * 4 + 4);
+        decode_row(L, row, cols);
+        int64_t k = 0;
+        while (k < n && cols[k] != col) ++k;
+        free(cols);
+        if (k == n) return O_OK;
+        const uint8_t v = L->val[L->elem_start[row] + k];
+        uint8_t s[16];
+        memcpy(s, L->b4[br].t[e].s, 16);
+        s[B4_SLOT(li, lj)] = (uint8_t)(o_fp4_encode(o_fp4_decode(v >> 4)) | (o_fp4_encode(o_fp4_decode(v & 0xF)) << 4));
+        b4_write(L, br, e, s);
+        b4_maybe_compress(L, br, e);
+        sc_remove_col(L, row, col);
+        return O_OK;
+    }
+    const int64_t row_lo = br * 4, row_hi = row_lo + 4 < L->rows ? row_lo + 4 : L->rows;
+    const int64_t col_lo = bc * 4, col_hi = col_lo + 4 < L->cols ? col_lo + 4 : L->cols;
+    int64_t fr[16], fc[16], fv[16], nf = 0;
+    for (int64_t r = row_lo; r < row_hi; ++r) {
+        const int64_t n = row_nnz(L, r);
+        if (n == 0) continue;
+        uint32_t* cols = (uint32_t*)malloc((size_t)n * 4 + 4);
+        decode_row(L, r, cols);
+        for (int64_t k = 0; k < n; ++k)
+            if ((int64_t)cols[k] >= col_lo && (int64_t)cols[k] < col_hi && nf < 16) {
+                fr[nf] = r; fc[nf] = cols[k]; fv[nf] = L->elem_start[r] + k; ++nf;
+            }
+        free(cols);
+    }
+    if (nf < 2) return O_OK;
+    const int rc = b4_get_or_create(L, br, (int32_t)bc, &e);
+    if (rc) return rc;
+    uint8_t s[16];
+    memcpy(s, L->b4[br].t[e].s, 16);
+    for (int64_t f = 0; f < nf; ++f) {
+        const uint8_t v = L->val[fv[f]];
+        s[B4_SLOT(fr[f] - row_lo, fc[f] - col_lo)] =
+            (uint8_t)(o_fp4_encode(o_fp4_decode(v >> 4)) | (o_fp4_encode(o_fp4_decode(v & 0xF)) << 4));
+    }
+    b4_write(L, br, e, s);
+    b4_maybe_compress(L, br, e);
+    for (int64_t f = 0; f < nf; ++f) sc_remove_col(L, fr[f], (uint32_t)fc[f]);
+    return O_OK;
+}
+
+/* delta_csr_synap_row_step, delta_csr_memory.hpp:1019-1258, scattered and
+ * block4 synapses, with the reference's std::sort orderings (o_std_sort). */
+static int lt_u32_desc(int64_t a, int64_t b, const void* c) { const uint32_t* k = (const uint32_t*)c; return k[a] > k[b]; }
+
+int o_synap_row_step(OLayer* L, int row_in, float cutoff, int max_rw, int max_prune, float imp_eps, int* did) {
+    *did = 0;
+    if (L->rows == 0) return O_OK;
+    const int64_t r = (int64_t)row_in % L->rows;
+    const int64_t n_sc = row_nnz(L, r);
+    const int has_probes = L->n_probes > 0;
+    const int64_t br = r / 4, li = r % 4;
+    const int64_t nt = (br < L->b4_rows) ? L->b4[br].n : 0;
+    const int64_t cap = n_sc + 4 * nt + 1;
+    uint32_t* cols = (uint32_t*)malloc((size_t)cap * 4);
+    float* imp = (float*)malloc((size_t)cap * 4);
+    uint8_t* isb4 = (uint8_t*)calloc((size_t)cap, 1);
+    decode_row(L, r, cols);
+    for (int64_t k = 0; k < n_sc; ++k) imp[k] = o_fp4_decode(L->val[L->elem_start[r] + k] & 0xF);
+    int64_t n_exist = n_sc;
+    for (int64_t e = 0; e < nt; ++e)
+        for (int lj = 0; lj < 4; ++lj) {
+            const uint8_t byte = L->b4[br].t[e].s[B4_SLOT(li, lj)];
+            if (byte == 0) continue;
+            const int64_t col = (int64_t)L->b4[br].t[e].bc * 4 + lj;
+            if (col >= L->cols) continue;
+            cols[n_exist] = (uint32_t)col;
+            imp[n_exist] = o_fp4_decode((uint8_t)(byte >> 4));
+            isb4[n_exist] = 1;
+            ++n_exist;
+        }
+    if (n_exist == 0 && !has_probes) { free(cols); free(imp); free(isb4); return O_OK; }
+    /* probes of this row in COO order (:1133-1144) */
+    uint32_t* pc = (uint32_t*)malloc((size_t)(L->n_probes + 1) * 4);
+    float* ps = (float*)malloc((size_t)(L->n_probes + 1) * 4);
+    int64_t np = 0;
+    for (int64_t p = 0; p < L->n_probes; ++p)
+        if (L->prow[p] == r) { pc[np] = (uint32_t)L->pcol[p]; ps[np] = L->pval[p]; ++np; }
+    /* removals by stored importance ascending (:1147-1167) */
+    int64_t* by = (int64_t*)malloc((size_t)(n_exist + 1) * 8);
+    for (int64_t i = 0; i < n_exist; ++i) by[i] = i;
+    o_std_sort(by, n_exist, lt_f_asc, imp);
+    uint32_t* rmc = (uint32_t*)malloc((size_t)(n_exist + 1) * 4);
+    uint8_t* rmb = (uint8_t*)malloc((size_t)(n_exist + 1));
+    int64_t nrm = 0;
+    for (int64_t a = 0; a < n_exist && nrm < max_prune; ++a) {
+        const int64_t k = by[a];
+        const int64_t keep = n_exist - nrm;
+        const float fl = (imp[k] < imp_eps) ? imp_eps : imp[k];   /* std::max(imp, eps) */
+        if (fl < cutoff || keep > max_rw) { rmc[nrm] = cols[k]; rmb[nrm] = isb4[k]; ++nrm; }
+    }
+    int64_t* rperm = (int64_t*)malloc((size_t)(nrm + 1) * 8);
+    for (int64_t i = 0; i < nrm; ++i) rperm[i] = i;
+    o_std_sort(rperm, nrm, lt_u32_desc, rmc);
+    /* adds by score descending (:1171-1201) */
+    int64_t* pidx = (int64_t*)malloc((size_t)(np + 1) * 8);
+    for (int64_t i = 0; i < np; ++i) pidx[i] = i;
+    o_std_sort(pidx, np, lt_f_desc, ps);
+    const uint64_t slots = (uint64_t)((int64_t)max_rw - (n_exist - nrm));
+    uint32_t* add_c = (uint32_t*)malloc((size_t)(np + 1) * 4);
+    float* add_s = (float*)malloc((size_t)(np + 1) * 4);
+    int64_t nadd = 0;
+    for (int64_t a = 0; a < np; ++a) {
+        if ((uint64_t)nadd >= slots) break;
+        const uint32_t c = pc[pidx[a]];
+        int exists = 0;
+        for (int64_t i = 0; i < n_exist; ++i) if (cols[i] == c) { exists = 1; break; }
+        if (!exists) { add_c[nadd] = c; add_s[nadd] = ps[pidx[a]]; ++nadd; }
+    }
+    int rc = O_OK;
+    /* removals, highest column first (:1203-1233) */
+    for (int64_t q = 0; q < nrm && rc == O_OK; ++q) {
+        const uint32_t c = rmc[rperm[q]];
+        if (rmb[rperm[q]]) {
+            const int32_t bc = (int32_t)(c / 4);
+            const int lj = (int)(c % 4);
+            const int64_t e = b4_find(L, br, bc);
+            int demote = 0;
+            if (e >= 0 && L->b4[br].t[e].s[B4_SLOT(li, lj)] != 0) {
+                uint8_t s[16];
+                memcpy(s, L->b4[br].t[e].s, 16);
+                s[B4_SLOT(li, lj)] = 0;
+                demote = b4_live(s) < 2;
+                b4_write(L, br, e, s);
+            }
+            if (demote) rc = b4_demote(L, br, bc);
+        } else {
+            sc_remove_col(L, r, c);
+        }
+        if (rc == O_OK && L->out_degree[c] > 0) L->out_degree[c]--;
+    }
+    /* inserts in score order, each followed by the block4 promotion (:1235-1255) */
+    for (int64_t a = 0; a < nadd && rc == O_OK; ++a) {
+        if (!sc_insert_col(L, r, add_c[a], 0.0f, add_s[a])) { rc = O_EHEADROOM; break; }
+        L->out_degree[add_c[a]]++;
+        rc = b4_maybe_promote(L, r, add_c[a]);
+    }
+    free(cols); free(imp); free(isb4); free(pc); free(ps); free(by); free(rmc); free(rmb);
+    free(rperm); free(pidx); free(add_c); free(add_s);
+    if (rc == O_OK) *did = 1;
     return rc;
 }

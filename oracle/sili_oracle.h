@@ -94,6 +94,19 @@ void    o_recompute_stats(OLayer* L);
 int64_t o_export_nnz(const OLayer* L);
 void    o_export(const OLayer* L, int* ptrs, int* idx, float* w, float* imp);
 
+/* block4 tiles, sili/lib/headers/block4.hpp + delta_csr_memory.hpp:769-945 */
+int     o_load_dense_codes(OLayer* L, const uint8_t* weight_codes, const uint8_t* importance_codes);
+int     o_b4_expand_headroom(OLayer* L, float blank_fraction, int64_t min_slack);
+int     o_b4_equalize_step(OLayer* L, int64_t row);
+void    o_b4_set_switch_point(OLayer* L, uint32_t v);
+int64_t o_b4_ntiles(const OLayer* L);
+void    o_b4_export(const OLayer* L, int* br, int* bc, uint8_t* slots, uint8_t* sparse);
+void    o_b4_rows(const OLayer* L, int64_t* out);   /* 6 per block-row */
+void    o_b4_view(const OLayer* L, int64_t* v);     /* 8 counters */
+
+/* libstdc++ std::sort restatement (permutation of 0..n-1 by keys) */
+void    o_std_sort_keys(const float* keys, int64_t n, int desc, int64_t* perm);
+
 /* activation sparsifiers, sili/cpu_backend.cpp:3075-3143 */
 int64_t o_dense_to_csr(const float* x, int rows, int cols, float threshold, int* ptrs, int* idx, float* vals);
 int64_t o_top_k_csr(const float* x, int rows, int cols, int64_t k, int* ptrs, int* idx, float* vals);

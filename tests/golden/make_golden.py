@@ -178,6 +178,110 @@ def topk_fixture(seed=3):
     np.savez_compressed(os.path.join(HERE, "topk_small.npz"), **out)
 
 
+def b4_arrays(layer, prefix):
+    """block4 tiles (block-row, block-col, 16 slot bytes, sparse flag), the
+    per-block-row allocations and the Block4View counters."""
+    br, bc, sl, sp = layer.b4_tiles()
+    return {f"{prefix}b4_br": br, f"{prefix}b4_bc": bc, f"{prefix}b4_slots": sl, f"{prefix}b4_sparse": sp,
+            f"{prefix}b4_rows": layer.b4_rows(), f"{prefix}b4_view": layer.b4_view()}
+
+
+def export_arrays(layer, prefix):
+    p, i, w, m = layer.export()
+    return {f"{prefix}ex_ptrs": p, f"{prefix}ex_idx": i, f"{prefix}ex_w": w, f"{prefix}ex_imp": m}
+
+
+def block4_dense_fixture(seed=11):
+    """load_dense_codes on a layer with partial edge tiles, then forward,
+    dx at lr = 0, three deterministic training steps, compact_block4 (no
+    slack) and two more steps, which makes merge_row_workspace evict."""
+    n_in, n_out, B = 37, 53, 12
+    rng = np.random.default_rng(seed)
+    mask = rng.random((n_in, n_out)) < 0.3
+    wc = np.where(mask, rng.integers(1, 16, (n_in, n_out)), 0).astype(np.uint8)
+    wc[wc == 8] = 1
+    ic = np.where(mask & (rng.random((n_in, n_out)) < 0.5), rng.integers(1, 8, (n_in, n_out)), 0).astype(np.uint8)
+    vs = (0.01 * (1 + np.arange(n_in) % 5)).astype(np.float32)
+    ref = RefLayerFactory(n_in, n_out, n_in * n_out)
+    ref.load_dense_codes(wc, ic)
+    for r in range(n_in):
+        ref.set_value_scale_raw(r, float(vs[r]))
+        ref.set_importance_scale_raw(r, 0.05)
+    out = dict(wc=wc, ic=ic, vs=vs, n_in=np.array([n_in]), n_out=np.array([n_out]), budget=np.array([n_in * n_out]))
+    out.update(b4_arrays(ref, "load_"))
+    x = relu_sparse_x(rng, B, n_in)
+    dy = rng.normal(0, 1, (B, n_out)).astype(np.float32)
+    out["x0"], out["dy0"] = x, dy
+    out["y0"] = ref.forward_dense(x)
+    out["dx0"] = ref.backward_dense(dy, 0.0, True)
+    for t in range(5):
+        if t == 3:
+            ref.compact_block4()
+            out.update(b4_arrays(ref, "compact_"))
+        x = relu_sparse_x(rng, B, n_in)
+        dy = rng.normal(0, 1, (B, n_out)).astype(np.float32)
+        out[f"x{t + 1}"], out[f"dy{t + 1}"] = x, dy
+        out[f"y{t + 1}"] = ref.forward_dense(x)
+        out[f"dx{t + 1}"] = ref.backward_dense(dy, 0.05, True)
+        out.update(b4_arrays(ref, f"s{t + 1}_"))
+        out.update(state_arrays(ref, f"s{t + 1}_"))
+    np.savez_compressed(os.path.join(HERE, "block4_dense.npz"), **out)
+
+
+def synap_fixture(seed=12):
+    """Two training steps, build_probes, two full synap_row_step sweeps with
+    block4 promotion / demotion, then two more training steps over the mixed
+    scattered + block4 layer."""
+    n_in, n_out, per, B = 64, 64, 10, 16
+    rng = np.random.default_rng(seed)
+    p, i, w, vs = random_layer(n_in, n_out, per, seed=seed)
+    ref = RefLayerFactory(n_in, n_out, len(i) * 3)
+    setup_layer(ref, p, i, w, vs, imp_scale=0.01 / 6)
+    out = dict(ptrs=p, idx=i, w=w, vs=vs, n_in=np.array([n_in]), n_out=np.array([n_out]),
+               budget=np.array([len(i) * 3]), per=np.array([per]))
+    for t in range(2):
+        x = relu_sparse_x(rng, B, n_in)
+        dy = rng.normal(0, 1, (B, n_out)).astype(np.float32)
+        out[f"px{t}"], out[f"pdy{t}"] = x, dy
+        ref.forward_dense(x)
+        ref.backward_dense(dy, 0.01, True)
+    k = int(np.ceil(np.sqrt(0.05 * len(i))))
+    ref.build_probes(k)
+    r_, c_, v_ = ref.probes()
+    out.update(k=np.array([k]), pr_rows=r_, pr_cols=c_, pr_scores=v_)
+    out["synap_args"] = np.array([0.002, per + 2, 3, 1e-3], np.float64)
+    rets = []
+    for sweep in range(2):
+        for row in range(n_in):
+            rets.append(int(ref.synap_row_step(row, 0.002, per + 2, 3)))
+        out.update(state_arrays(ref, f"sw{sweep}_"))
+        out.update(b4_arrays(ref, f"sw{sweep}_"))
+        out.update(export_arrays(ref, f"sw{sweep}_"))
+    out["synap_ret"] = np.array(rets, np.int32)
+    for t in range(2):
+        x = relu_sparse_x(rng, B, n_in)
+        dy = rng.normal(0, 1, (B, n_out)).astype(np.float32)
+        out[f"x{t}"], out[f"dy{t}"] = x, dy
+        out[f"y{t}"] = ref.forward_dense(x)
+        out[f"dx{t}"] = ref.backward_dense(dy, 0.01, True)
+        out.update(state_arrays(ref, f"post{t}_"))
+        out.update(b4_arrays(ref, f"post{t}_"))
+    np.savez_compressed(os.path.join(HERE, "synap_block4.npz"), **out)
+
+
+def std_sort_fixture(seed=13):
+    """std::sort permutations (the orderings synap_row_step uses) on keys with
+    many ties, for the restatement of libstdc++'s introsort."""
+    rng = np.random.default_rng(seed)
+    out = {}
+    for n in (5, 16, 17, 40, 333, 2000):
+        keys = O.FP4_TABLE[rng.integers(0, 8, n)].astype(np.float32)
+        out[f"k{n}"] = keys
+        out[f"asc{n}"] = O.std_sort_keys(keys, False, "ref")
+        out[f"desc{n}"] = O.std_sort_keys(keys, True, "ref")
+    np.savez_compressed(os.path.join(HERE, "std_sort.npz"), **out)
+
+
 def main():
     if not O.ref_available():
         raise SystemExit("reference not built: run python oracle/build_ref.py --variant native")
@@ -189,6 +293,9 @@ def main():
     probes_fixture()
     headroom_fixture()
     topk_fixture()
+    block4_dense_fixture()
+    synap_fixture()
+    std_sort_fixture()
     print("fixtures written to", HERE)
 
 

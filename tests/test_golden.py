@@ -106,3 +106,31 @@ def test_headroom_ops():
     for _ in range(int(fx["n_in"][0]) + 3):
         layer.equalizer_step()
     compare_snapshot(snapshot(layer), fx, "equalize_")
+
+
+def test_std_sort_restatement():
+    """The libstdc++ introsort restatement gives the reference build's permutations."""
+    fx = load("std_sort")
+    for key in [k for k in fx if k.startswith("k")]:
+        n = key[1:]
+        assert np.array_equal(O.std_sort_keys(fx[key], False), fx[f"asc{n}"]), f"ascending n={n}"
+        assert np.array_equal(O.std_sort_keys(fx[key], True), fx[f"desc{n}"]), f"descending n={n}"
+
+
+def test_block4_dense_sequence():
+    from replay import replay_block4_dense
+    fx = load("block4_dense")
+    steps = 0
+    for layer, t in replay_block4_dense(oracle_factory, fx):
+        compare_snapshot(snapshot(layer), fx, f"s{t}_", skip=("byte_start", "byte_end", "elem_start", "elem_end",
+                                                               "live_idx", "live_val"))
+        steps += 1
+    assert steps == 5
+
+
+def test_synaptogenesis_with_block4():
+    from replay import replay_synap
+    fx = load("synap_block4")
+    stages = [s for _, s in replay_synap(oracle_factory, fx)]
+    assert stages == ["sweep0", "sweep1", "post0", "post1"]
+    assert fx["sw1_b4_view"][0] > 0, "fixture exercises block4 promotion"
