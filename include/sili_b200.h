@@ -173,6 +173,35 @@ int sili_layer_recompute_stats(sili_layer* h);
 /* last forward input [batch, n_in] (NULL out -> only batch/cols) */
 int sili_layer_last_input(sili_layer* h, float* out, int* batch, int* cols);
 
+/* ── block4 tiles (4x4 dense FP4 tiles beside the scattered synapses) ───── */
+/* synapses in the combined export (scattered + live block4 slots) -- the
+ * reference's nnz(), cpu_backend.cpp:451 */
+int sili_layer_export_nnz(sili_layer* h, int64_t* n);
+/* load_dense_codes(weight_codes, importance_codes), cpu_backend.cpp:910-921 ->
+ * block4_load_dense (delta_csr_memory.hpp:843-945): u8 [n_in, n_out] codes
+ * each, host or device */
+int sili_layer_load_dense_codes(sili_layer* h, const uint8_t* weight_codes, const uint8_t* importance_codes);
+/* expand_block4_headroom(blank_fraction) / compact_block4 (min_slack 16 / 0,
+ * blank 0), cpu_backend.cpp:932-942 -> block4_expand_headroom
+ * (delta_csr_memory.hpp:769-823) */
+int sili_layer_b4_expand_headroom(sili_layer* h, float blank_fraction, int64_t min_slack);
+/* the block4 half of equalizer_step (Block4Store::equalize_step,
+ * block4.hpp:1208-1221); row is the block-row cursor */
+int sili_layer_b4_equalize_row(sili_layer* h, int64_t row);
+/* Block4View.switch_point setter (cpu_backend.cpp:61-62) */
+int sili_layer_b4_set_switch_point(sili_layer* h, uint32_t v);
+/* Block4View counters, cpu_backend.cpp:51-98: tiles, synapses, switch_point,
+ * dropped_growth_events, row_merge_overflow_events,
+ * row_merge_overflow_bytes_dropped, used_bytes, alloc_bytes */
+int sili_layer_b4_view(sili_layer* h, int64_t* v8);
+/* live tiles in block-row order: block-row, block-column, 16 slot bytes
+ * (slot = lj*4 + li, byte = importance << 4 | weight), packed flag;
+ * sizes[5] of sili_layer_sizes is the tile count */
+int sili_layer_b4_export(sili_layer* h, int* br, int* bc, uint8_t* slots, uint8_t* sparse);
+/* per block-row: index-byte alloc, index bytes used, tile-byte alloc, tile
+ * bytes used, tile-slot alloc, tiles (the reference's Block4Store layout) */
+int sili_layer_b4_rows(sili_layer* h, int64_t* out6);
+
 /* ── module functions (cpu_backend.cpp:3075-3196) ───────────────────────── */
 /* fp4_quantize_array: deterministic FP4 encode, fp4quant.hpp:86-121 */
 int sili_fp4_quantize(const float* vals, uint8_t* codes, int64_t n, void* stream);

@@ -1,0 +1,559 @@
+// block4 kernels: 4x4 dense FP4 tiles (block4.hpp) beside the scattered
+// delta-CSR synapses.  Loading (block4_load_dense), the forward part of
+// disldo_forward (linear_disldo.hpp:128-339), the backward part of
+// disldo_backward (linear_disldo.hpp:939-1951) with the per-row workspace
+// merge and its eviction (Block4Store::merge_row_workspace,
+// block4.hpp:1368-1465), and the tile column index.
+//
+// Floating point: compiled with --fmad=false; each fused multiply-add and
+// each horizontal-sum order below is the one the reference's own build
+// evaluates (pinned through the CPU oracle against that build).
+#include "common.cuh"
+#include "kernels.cuh"
+#include "update_math.cuh"
+
+#include <algorithm>
+
+namespace sili {
+
+namespace {
+
+__device__ __forceinline__ uint32_t tile_byte(const uint4& t, int s) {
+    const uint32_t w = s < 8 ? (s < 4 ? t.x : t.y) : (s < 12 ? t.z : t.w);
+    return (w >> ((s & 3) * 8)) & 0xFFu;
+}
+__device__ __forceinline__ void set_tile_byte(uint4& t, int s, uint32_t b) {
+    const uint32_t sh = (uint32_t)(s & 3) * 8u, m = ~(0xFFu << sh), v = (b & 0xFFu) << sh;
+    if (s < 4) t.x = (t.x & m) | v;
+    else if (s < 8) t.y = (t.y & m) | v;
+    else if (s < 12) t.z = (t.z & m) | v;
+    else t.w = (t.w & m) | v;
+}
+// live slots (non-zero bytes) of a tile (Block4Tile::count_live, block4.hpp:314-319)
+__device__ __forceinline__ int nz_bytes(uint32_t w) {
+    const uint32_t t = ((w & 0x7F7F7F7Fu) + 0x7F7F7F7Fu) | w;
+    return __popc(t & 0x80808080u);
+}
+__device__ __forceinline__ int tile_live(const uint4& t) {
+    return nz_bytes(t.x) + nz_bytes(t.y) + nz_bytes(t.z) + nz_bytes(t.w);
+}
+// block4_stored_tile_len (block4.hpp:340-343, 386-388)
+__device__ __forceinline__ int tile_len(int live, bool sparse) { return sparse ? 1 + (live + 1) / 2 + live : 16; }
+
+// S(row, col) = sum_k value_scale_k(row) * output_scale_k(col)
+// (SparseLinearWeightsDelta::get_scale, delta_csr_types.hpp:1235-1240)
+__device__ __forceinline__ float scale_of(const LayerView& L, int64_t row, int64_t col) {
+    float s = 0.0f;
+    for (int k = 0; k < L.rank; ++k) s = __fmaf_rn(L.vs[row * L.rank + k], L.os[col * L.rank + k], s);
+    return s;
+}
+
+}  // namespace
+
+// ── load_dense_codes ────────────────────────────────────────────────────────
+// block4_load_dense (delta_csr_memory.hpp:843-945): a tile for every
+// (br, bc), bytes weight | importance << 4 straight from the codes, packed
+// sparse when live <= switch_point (commit_dirty_sparse_tile of a new tile).
+__global__ void k_b4_load_dense(const uint8_t* __restrict__ wc, const uint8_t* __restrict__ ic, int64_t n_in,
+                                int64_t n_out, B4View V, unsigned long long* __restrict__ row_used) {
+    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= V.BR * V.BC) return;
+    const int64_t br = t / V.BC, bc = t % V.BC;
+    uint4 tile = make_uint4(0, 0, 0, 0);
+    for (int li = 0; li < 4; ++li) {
+        const int64_t row = br * 4 + li;
+        if (row >= n_in) break;
+        for (int lj = 0; lj < 4; ++lj) {
+            const int64_t col = bc * 4 + lj;
+            if (col >= n_out) break;
+            const int64_t i = row * n_out + col;
+            set_tile_byte(tile, lj * 4 + li, (uint32_t)(uint8_t)(wc[i] | (ic[i] << 4)));
+        }
+    }
+    const int64_t slot = V.es[br] + bc;
+    V.tile[slot] = tile;
+    V.bc[slot] = (int)bc;
+    const int live = tile_live(tile);
+    const bool sp = (uint32_t)live <= V.switch_point;
+    V.sparse[slot] = sp ? 1 : 0;
+    atomicAdd(row_used + br, (unsigned long long)tile_len(live, sp));
+}
+void launch_b4_load_dense(const uint8_t* wc, const uint8_t* ic, int64_t n_in, int64_t n_out, const B4View& V,
+                          int64_t* row_used, cudaStream_t s) {
+    const int64_t n = V.BR * V.BC;
+    if (n == 0) return;
+    k_b4_load_dense<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(wc, ic, n_in, n_out, V,
+                                                               reinterpret_cast<unsigned long long*>(row_used));
+    count_launch();
+}
+
+// per block-row: packed tile bytes in use, ULEB128 bytes of the block-column
+// deltas, live slots (for the allocation bookkeeping and Block4View)
+__global__ void k_b4_row_used(B4View V, int64_t* __restrict__ out) {
+    const int64_t br = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (br >= V.BR) return;
+    long long u = 0, ib = 0, lv = 0;
+    for (int e = lane; e < V.nt[br]; e += 32) {
+        const int64_t ti = V.es[br] + e;
+        const int live = tile_live(V.tile[ti]);
+        u += tile_len(live, V.sparse[ti] != 0);
+        lv += live;
+        const uint32_t prev = e > 0 ? (uint32_t)V.bc[ti - 1] : 0u;
+        uint32_t d = (uint32_t)V.bc[ti] - prev;
+        int n = 0;
+        do { d >>= 7; ++n; } while (d);
+        ib += n;
+    }
+    u = warp_sum(u); ib = warp_sum(ib); lv = warp_sum(lv);
+    if (lane == 0) { out[br] = u; out[V.BR + br] = ib; out[2 * V.BR + br] = lv; }
+}
+void launch_b4_row_used(const B4View& V, int64_t* out, cudaStream_t s) {
+    if (V.BR == 0) return;
+    k_b4_row_used<<<(unsigned)((V.BR + 7) / 8), 256, 0, s>>>(V, out);
+    count_launch();
+}
+
+// ── forward ─────────────────────────────────────────────────────────────────
+// One warp per block-column, lanes over batch samples.  Per tile, in
+// ascending block-row (the reference's single-thread tile order), each of
+// the 4 columns gets acc = fma(w0, x0, w1*x1) + fma(w2, x2, w3*x3) -- the
+// reference build's evaluation of `acc += w4[li] * x` -- summed into a
+// per-column total that is added to the scattered result at the end
+// (linear_disldo.hpp:235-335).  Rows past n_in contribute 0 * x[b, 0].
+__global__ void __launch_bounds__(128) k_b4_forward(LayerView L, B4View V, const float* __restrict__ xT, int B,
+                                                    float* __restrict__ y) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t bcol = (int64_t)blockIdx.x * 4 + warp;
+    const int b = blockIdx.y * 32 + lane;
+    if (bcol >= V.BC) return;
+    const bool bok = b < B;
+    float mo[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    const int64_t col0 = bcol * 4;
+    for (int t = V.cptr[bcol]; t < V.cptr[bcol + 1]; ++t) {
+        const int64_t br = V.cbr[t];
+        const uint4 tw = V.tile[V.ctile[t]];
+        float x[4];
+        int64_t rows[4];
+#pragma unroll
+        for (int li = 0; li < 4; ++li) {
+            const int64_t row = br * 4 + li;
+            rows[li] = row;
+            x[li] = bok ? xT[(row < L.n_in ? row : 0) * B + b] : 0.0f;
+        }
+#pragma unroll
+        for (int lj = 0; lj < 4; ++lj) {
+            const int64_t col = col0 + lj;
+            if (col >= L.n_out) continue;
+            float w[4];
+#pragma unroll
+            for (int li = 0; li < 4; ++li)
+                w[li] = rows[li] < L.n_in
+                    ? __fmul_rn(fp4_decode(tile_byte(tw, lj * 4 + li) & 0xFu), scale_of(L, rows[li], col))
+                    : 0.0f;
+            const float acc = __fadd_rn(__fmaf_rn(w[0], x[0], __fmul_rn(w[1], x[1])),
+                                        __fmaf_rn(w[2], x[2], __fmul_rn(w[3], x[3])));
+            mo[lj] = __fadd_rn(mo[lj], acc);
+        }
+    }
+    if (!bok) return;
+#pragma unroll
+    for (int lj = 0; lj < 4; ++lj) {
+        const int64_t col = col0 + lj;
+        if (col < L.n_out) {
+            float* o = y + (int64_t)b * L.n_out + col;
+            *o = __fadd_rn(*o, mo[lj]);
+        }
+    }
+}
+void launch_b4_forward(const LayerView& L, const B4View& V, const float* xT, int B, float* y, cudaStream_t s) {
+    if (V.BC == 0 || B == 0) return;
+    dim3 g((unsigned)((V.BC + 3) / 4), (unsigned)((B + 31) / 32));
+    k_b4_forward<<<g, 128, 0, s>>>(L, V, xT, B, y);
+    count_launch();
+}
+
+// ── dx at lr == 0 ───────────────────────────────────────────────────────────
+// One warp per block-row, lanes over samples.  Per tile in stored order, row
+// li adds quant*(S*dy) over its 4 columns: pairwise (p0+p1)+(p2+p3) for a
+// tile of full width (Block4Vec path), a fused chain over the valid columns
+// at the matrix edge (scalar path) -- linear_disldo.hpp:1512-1703.
+__global__ void __launch_bounds__(128) k_b4_dx(LayerView L, B4View V, const float* __restrict__ dyT, int B,
+                                               float* __restrict__ dx) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t br = (int64_t)blockIdx.x * 4 + warp;
+    const int b = blockIdx.y * 32 + lane;
+    if (br >= V.BR || b >= B) return;
+    const int nt = V.nt[br];
+    if (nt == 0) return;
+    float d[4];
+#pragma unroll
+    for (int li = 0; li < 4; ++li) {
+        const int64_t row = br * 4 + li;
+        d[li] = row < L.n_in ? dx[(int64_t)b * L.n_in + row] : 0.0f;
+    }
+    for (int e = 0; e < nt; ++e) {
+        const int64_t ti = V.es[br] + e;
+        const uint4 tw = V.tile[ti];
+        const int64_t col0 = (int64_t)V.bc[ti] * 4;
+        const bool full = col0 + 4 <= L.n_out;
+        float dyv[4];
+#pragma unroll
+        for (int lj = 0; lj < 4; ++lj) dyv[lj] = col0 + lj < L.n_out ? dyT[(col0 + lj) * B + b] : 0.0f;
+#pragma unroll
+        for (int li = 0; li < 4; ++li) {
+            const int64_t row = br * 4 + li;
+            if (row >= L.n_in) continue;
+            if (full) {
+                float p[4];
+#pragma unroll
+                for (int lj = 0; lj < 4; ++lj)
+                    p[lj] = __fmul_rn(fp4_decode(tile_byte(tw, lj * 4 + li) & 0xFu),
+                                      __fmul_rn(scale_of(L, row, col0 + lj), dyv[lj]));
+                d[li] = __fadd_rn(d[li], __fadd_rn(__fadd_rn(p[0], p[1]), __fadd_rn(p[2], p[3])));
+            } else {
+                for (int lj = 0; lj < 4; ++lj) {
+                    if (col0 + lj >= L.n_out) continue;
+                    d[li] = __fmaf_rn(fp4_decode(tile_byte(tw, lj * 4 + li) & 0xFu),
+                                      __fmul_rn(scale_of(L, row, col0 + lj), dyv[lj]), d[li]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int li = 0; li < 4; ++li) {
+        const int64_t row = br * 4 + li;
+        if (row < L.n_in) dx[(int64_t)b * L.n_in + row] = d[li];
+    }
+}
+void launch_b4_dx(const LayerView& L, const B4View& V, const float* dyT, int B, float* dx, cudaStream_t s) {
+    if (V.BR == 0 || B == 0) return;
+    dim3 g((unsigned)((V.BR + 3) / 4), (unsigned)((B + 31) / 32));
+    k_b4_dx<<<g, 128, 0, s>>>(L, V, dyT, B, dx);
+    count_launch();
+}
+
+// ── backward with update (lr != 0) ─────────────────────────────────────────
+// One half-warp per block-row; lane s (0..15) owns slot s of the current
+// tile (li = s & 3, lj = s >> 2).  Tiles are processed in stored order; for
+// each, every slot runs its per-sample recurrence (the scattered path's
+// bounded RMSprop step, here over the tile's 4 columns as the reference's
+// Block4Vec code does, linear_disldo.hpp:1497-1703) and the row's dx terms
+// are combined with half-warp shuffles in the reference build's order:
+//   dx   += (p0 + p1) + (p2 + p3),  p = quant * (S * dy)      (full width)
+//   mrow += (double)((q0 + q2) + (q1 + q3)),  q = (qf * os) * g
+// or sequential fused chains over the valid columns at the matrix edge.
+// dx partial sums live in dbuf (shared memory when it fits, else dxT).
+// After all tiles: canonical repacking, the row's eviction down to its tile
+// byte allocation (merge_row_workspace) and the block4 value_scale step
+// (linear_disldo.hpp:1882-1950).
+template <int RANK, bool STOCH>
+__global__ void __launch_bounds__(128) k_b4_update(LayerView L, B4View V, const float* __restrict__ xT,
+                                                   const float* __restrict__ dyT, int B, UpdateParams P,
+                                                   float* __restrict__ dxT, int use_smem) {
+    extern __shared__ float sh_d[];
+    const int lane = threadIdx.x & 31, half = lane >> 4, s = lane & 15;
+    const int hw = (threadIdx.x >> 4);                     // half-warp within the block
+    const int64_t br = (int64_t)blockIdx.x * (blockDim.x >> 4) + hw;
+    const unsigned hmask = half ? 0xFFFF0000u : 0x0000FFFFu;
+    if (br >= V.BR) return;
+    const int nt = V.nt[br];
+    if (nt == 0) return;
+    const int li = s & 3, lj = s >> 2;
+    const int64_t row = br * 4 + li;
+    const bool row_ok = row < L.n_in;
+    const bool leader = lj == 0;                           // lanes s = 0..3 own row li's sums
+    float* dbuf = use_smem ? sh_d + (size_t)hw * 4 * B + (size_t)li * B : dxT + (row_ok ? row : 0) * B;
+    if (use_smem && leader && row_ok)
+        for (int b = 0; b < B; ++b) dbuf[b] = dxT[row * B + b];
+    __syncwarp(hmask);
+    const uint32_t nnz_row = (uint32_t)nt * 4u;
+    const float eff_lr = P.lr_per_row_nnz ? __fdiv_rn(P.lr, (float)nnz_row) : P.lr;
+    const float onem = __fsub_rn(1.0f, P.beta2);
+    float vsk[RANK];
+#pragma unroll
+    for (int k = 0; k < RANK; ++k) vsk[k] = row_ok ? L.vs[row * RANK + k] : 0.0f;
+    const float isr = row_ok ? L.is[row] : 0.0f;
+    double trg[RANK], trc[RANK];
+#pragma unroll
+    for (int k = 0; k < RANK; ++k) { trg[k] = 0.0; trc[k] = 0.0; }
+    const int64_t base = V.es[br];
+    for (int e = 0; e < nt; ++e) {
+        const int64_t ti = base + e;
+        uint4 tw = V.tile[ti];
+        const int64_t col0 = (int64_t)V.bc[ti] * 4, col = col0 + lj;
+        const bool col_ok = col < L.n_out;
+        const bool act = row_ok && col_ok;
+        const bool full = col0 + 4 <= L.n_out;
+        const uint32_t byte = tile_byte(tw, s);
+        float osk[RANK];
+        float S = 0.0f;
+#pragma unroll
+        for (int k = 0; k < RANK; ++k) {
+            osk[k] = col_ok ? L.os[col * RANK + k] : 0.0f;
+            S = __fmaf_rn(vsk[k], osk[k], S);
+        }
+        if (!act) S = 0.0f;
+        const float cis = act ? __fmul_rn(isr, L.ois[col]) : 0.0f;
+        const float qorig = act ? fp4_decode(byte & 0xFu) : 0.0f;
+        float quant = qorig;
+        float ci = act ? __fmul_rn(fp4_decode(byte >> 4), cis) : 0.0f;
+        float mcol[RANK], mcolc[RANK];
+        double mrow[RANK], mrowc[RANK];
+#pragma unroll
+        for (int k = 0; k < RANK; ++k) { mcol[k] = mcolc[k] = 0.0f; mrow[k] = mrowc[k] = 0.0; }
+        for (int b = 0; b < B; ++b) {
+            const float x = row_ok ? xT[row * B + b] : 0.0f;
+            const float dy = col_ok ? dyT[col * B + b] : 0.0f;
+            const float g = __fmul_rn(dy, x);
+            float cb = 0.0f, qf = 0.0f;
+            if (act) {
+                cb = __fmul_rn(qorig, x);
+                ci = bounded_ci(ci, g, cb, P.beta2, onem);
+                const float ngS = __fmul_rn(-g, S);
+                float raw = P.damp ? __fdiv_rn(ngS, __fadd_rn(__fsqrt_rn(ci), P.eps)) : ngS;
+                if (raw > 2.0f) raw = 2.0f;
+                if (raw < -2.0f) raw = -2.0f;
+                quant = __fmaf_rn(eff_lr, raw, quant);
+                qf = (quant == 0.0f) ? 0.1f : quant;
+            }
+            const float sdy = __fmul_rn(S, dy);
+            if (full) {
+#pragma unroll
+                for (int k = 0; k < RANK; ++k) {
+                    const float qo = __fmul_rn(qf, osk[k]);
+                    const float pg = __fmul_rn(qo, g), pc = __fmul_rn(qo, cb);
+                    const float ag = __fadd_rn(pg, __shfl_xor_sync(hmask, pg, 8));
+                    const float ac = __fadd_rn(pc, __shfl_xor_sync(hmask, pc, 8));
+                    const float hg = __fadd_rn(ag, __shfl_xor_sync(hmask, ag, 4));
+                    const float hc = __fadd_rn(ac, __shfl_xor_sync(hmask, ac, 4));
+                    mrow[k] = __dadd_rn(mrow[k], (double)hg);
+                    mrowc[k] = __dadd_rn(mrowc[k], (double)hc);
+                    mcol[k] = __fmaf_rn(__fmul_rn(qf, vsk[k]), g, mcol[k]);
+                    mcolc[k] = __fmaf_rn(__fmul_rn(qf, vsk[k]), cb, mcolc[k]);
+                }
+                const float p = __fmul_rn(quant, sdy);
+                const float a = __fadd_rn(p, __shfl_xor_sync(hmask, p, 4));
+                const float hs = __fadd_rn(a, __shfl_xor_sync(hmask, a, 8));
+                if (leader && row_ok) dbuf[b] = __fadd_rn(dbuf[b], hs);
+            } else {
+                // matrix-edge tile: sequential fused chains over the valid columns
+                const int src0 = (lane & 16) | li;
+                float dsum = leader && row_ok ? dbuf[b] : 0.0f;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int src = src0 + 4 * j;
+                    const float qj = __shfl_sync(hmask, quant, src);
+                    const float tj = __shfl_sync(hmask, sdy, src);
+                    const float qfj = __shfl_sync(hmask, qf, src);
+                    const float gj = __shfl_sync(hmask, g, src);
+                    const float cj = __shfl_sync(hmask, cb, src);
+                    const int okj = __shfl_sync(hmask, (int)col_ok, src);
+                    if (okj) {
+#pragma unroll
+                        for (int k = 0; k < RANK; ++k) {
+                            const float osj = __shfl_sync(hmask, osk[k], src);
+                            const double qo = (double)qfj * (double)osj;
+                            mrow[k] = __fma_rn(qo, (double)gj, mrow[k]);
+                            mrowc[k] = __fma_rn(qo, (double)cj, mrowc[k]);
+                        }
+                        dsum = __fmaf_rn(qj, tj, dsum);
+                    } else {
+#pragma unroll
+                        for (int k = 0; k < RANK; ++k) (void)__shfl_sync(hmask, osk[k], src);
+                    }
+                }
+#pragma unroll
+                for (int k = 0; k < RANK; ++k) {
+                    mcol[k] = __fmaf_rn(__fmul_rn(qf, vsk[k]), g, mcol[k]);
+                    mcolc[k] = __fmaf_rn(__fmul_rn(qf, vsk[k]), cb, mcolc[k]);
+                }
+                if (leader && row_ok) dbuf[b] = dsum;
+            }
+        }
+        __syncwarp(hmask);
+        // per-tile sums into the row's totals (t_row_grad), in tile order
+#pragma unroll
+        for (int k = 0; k < RANK; ++k) {
+            trg[k] = __dadd_rn(trg[k], mrow[k]);
+            trc[k] = __dadd_rn(trc[k], mrowc[k]);
+        }
+        if (act && P.os_trainable) {
+#pragma unroll
+            for (int k = 0; k < RANK; ++k) {
+                atomicAdd(P.colg + col * RANK + k, mcol[k]);
+                atomicAdd(P.colc + col * RANK + k, mcolc[k]);
+            }
+        }
+        // re-quantize the slot (deterministic set or stochastic draw)
+        if (act) {
+            const float imp_ratio = __fdiv_rn(ci, cis);
+            uint32_t wq, iq;
+            if (STOCH) {
+                const uint64_t el = (1ULL << 61) | ((uint64_t)row * (uint64_t)L.n_out + (uint64_t)col);
+                wq = fp4_quantize_stochastic(quant, rng_draw(P.call_key, el, 0));
+                iq = fp4_quantize_stochastic(imp_ratio, rng_draw(P.call_key, el, 1));
+            } else {
+                wq = fp4_encode(quant);
+                iq = fp4_encode(imp_ratio);
+            }
+            set_tile_byte(tw, s, (iq << 4) | wq);
+        }
+        // gather the 16 bytes back into one tile word (lane s holds slot s)
+        const uint32_t mine = tile_byte(tw, s);
+        uint32_t words[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            uint32_t w = 0;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) w |= __shfl_sync(hmask, mine, (lane & 16) | (q * 4 + k)) << (8 * k);
+            words[q] = w;
+        }
+        if (s == 0) {
+            const uint4 nw = make_uint4(words[0], words[1], words[2], words[3]);
+            V.tile[ti] = nw;
+            V.sparse[ti] = (uint32_t)tile_live(nw) <= V.switch_point ? 1 : 0;
+        }
+        __syncwarp(hmask);
+    }
+    // ── merge_row_workspace: evict until the row fits its tile allocation ──
+    const int64_t cap = V.alloc[V.BR + br];
+    long long used = 0;
+    for (int e = s; e < nt; e += 16) used += tile_len(tile_live(V.tile[base + e]), V.sparse[base + e] != 0);
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) used += __shfl_xor_sync(hmask, used, o);
+    while (used > cap) {
+        double best = -1.0;
+        long long best_key = -1;
+        for (int e = s; e < nt; e += 16) {
+            const uint4 tw = V.tile[base + e];
+            const int64_t c0 = (int64_t)V.bc[base + e] * 4;
+            for (int l_i = 0; l_i < 4; ++l_i)
+                for (int l_j = 0; l_j < 4; ++l_j) {
+                    const uint32_t byte = tile_byte(tw, l_j * 4 + l_i);
+                    if (byte == 0) continue;
+                    const int64_t r = br * 4 + l_i, c = c0 + l_j;
+                    const double ti = (double)fp4_decode(byte >> 4) * (double)L.is[r] * (double)L.ois[c];
+                    const double a = fabs(ti);
+                    const long long key = (long long)e * 16 + l_i * 4 + l_j;
+                    if (best < 0.0 || a < best) { best = a; best_key = key; }
+                }
+        }
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) {
+            const double ob = __shfl_xor_sync(hmask, best, o);
+            const long long ok = __shfl_xor_sync(hmask, best_key, o);
+            const bool take = ob >= 0.0 && (best < 0.0 || ob < best || (ob == best && ok < best_key));
+            if (take) { best = ob; best_key = ok; }
+        }
+        if (best < 0.0) break;   // nothing live left
+        const int e = (int)(best_key / 16), l_i = (int)((best_key / 4) % 4), l_j = (int)(best_key % 4);
+        const int64_t ti = base + e;
+        uint4 tw = V.tile[ti];
+        const int old_len = tile_len(tile_live(tw), V.sparse[ti] != 0);
+        set_tile_byte(tw, l_j * 4 + l_i, 0u);
+        const int live = tile_live(tw);
+        const bool sp = (uint32_t)live <= V.switch_point;
+        used -= old_len - tile_len(live, sp);
+        __syncwarp(hmask);
+        if (s == 0) { V.tile[ti] = tw; V.sparse[ti] = sp ? 1 : 0; }
+        __syncwarp(hmask);
+    }
+    if (s == 0) {
+        // tiles that do not fit even after eviction (the reference counts them)
+        long long fit = 0;
+        int fitted = 0;
+        for (int e = 0; e < nt; ++e) {
+            const int tl = tile_len(tile_live(V.tile[base + e]), V.sparse[base + e] != 0);
+            if (fit + tl > cap) break;
+            fit += tl;
+            ++fitted;
+        }
+        if (fitted < nt) {
+            atomicAdd(V.counters + 1, 1ull);
+            atomicAdd(V.counters + 2, (unsigned long long)(used - fit));
+        }
+    }
+    // ── block4 value_scale step and dx write-back (leader lane of each row) ──
+    if (leader && row_ok) {
+        const float scale_eff_lr = __fdiv_rn(P.lr, (float)nnz_row);
+#pragma unroll
+        for (int k = 0; k < RANK; ++k) {
+            if (trg[k] == 0.0 && trc[k] == 0.0) continue;
+            const int64_t i = row * RANK + k;
+            rmsprop_scale(L.vs + i, L.vsi + i, (float)trg[k], scale_eff_lr, (float)trc[k], L.vstep + i, P);
+        }
+        if (use_smem)
+            for (int b = 0; b < B; ++b) dxT[row * B + b] = dbuf[b];
+    }
+}
+
+void launch_b4_update(const LayerView& L, const B4View& V, const float* xT, const float* dyT, int B,
+                      const UpdateParams& P, float* dxT, cudaStream_t s) {
+    if (V.BR == 0 || B == 0) return;
+    // 8 half-warps (block-rows) per 128-thread block; dx partials in shared
+    // memory when 8 * 4 * B floats fit
+    const size_t smem = (size_t)8 * 4 * B * sizeof(float);
+    const int use_smem = smem <= 96 * 1024 ? 1 : 0;
+    const unsigned grid = (unsigned)((V.BR + 7) / 8);
+#define SILI_B4(R, ST)                                                                                       \
+    do {                                                                                                     \
+        if (use_smem && smem > 48 * 1024)                                                                    \
+            cudaFuncSetAttribute(k_b4_update<R, ST>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+        k_b4_update<R, ST><<<grid, 128, use_smem ? smem : 0, s>>>(L, V, xT, dyT, B, P, dxT, use_smem);       \
+    } while (0)
+    switch (L.rank * 2 + (P.stochastic ? 1 : 0)) {
+        case 2: SILI_B4(1, false); break;
+        case 3: SILI_B4(1, true); break;
+        case 4: SILI_B4(2, false); break;
+        case 5: SILI_B4(2, true); break;
+        case 6: SILI_B4(3, false); break;
+        case 7: SILI_B4(3, true); break;
+        case 8: SILI_B4(4, false); break;
+        default: SILI_B4(4, true); break;
+    }
+#undef SILI_B4
+    count_launch();
+}
+
+// ── tile column index ───────────────────────────────────────────────────────
+__global__ void k_b4_list(B4View V, const int* __restrict__ tile_off, int* __restrict__ keys,
+                          int* __restrict__ slots, int* __restrict__ brs) {
+    const int64_t br = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (br >= V.BR) return;
+    for (int e = lane; e < V.nt[br]; e += 32) {
+        const int o = tile_off[br] + e;
+        const int64_t ti = V.es[br] + e;
+        keys[o] = V.bc[ti];
+        slots[o] = (int)ti;
+        brs[o] = (int)br;
+    }
+}
+void launch_b4_list(const B4View& V, const int* tile_off, int* keys, int* slots, int* brs, cudaStream_t s) {
+    if (V.BR == 0) return;
+    k_b4_list<<<(unsigned)((V.BR + 7) / 8), 256, 0, s>>>(V, tile_off, keys, slots, brs);
+    count_launch();
+}
+
+// column pointers from the sorted keys (lower bound of each block-column) and
+// the (slot, block-row) pairs gathered in sorted order
+__global__ void k_b4_index(const int* __restrict__ sorted_keys, const int* __restrict__ perm, int n, int64_t BC,
+                           const int* __restrict__ slots, const int* __restrict__ brs, int* __restrict__ cptr,
+                           int* __restrict__ ctile, int* __restrict__ cbr) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) { ctile[i] = slots[perm[i]]; cbr[i] = brs[perm[i]]; }
+    if (i <= BC) {
+        int lo = 0, hi = n;
+        while (lo < hi) { const int mid = (lo + hi) >> 1; if (sorted_keys[mid] < (int)i) lo = mid + 1; else hi = mid; }
+        cptr[i] = lo;
+    }
+}
+void launch_b4_index(const int* sorted_keys, const int* perm, int n, int64_t BC, const int* slots, const int* brs,
+                     int* cptr, int* ctile, int* cbr, cudaStream_t s) {
+    const int64_t m = std::max<int64_t>(n, BC + 1);
+    k_b4_index<<<(unsigned)((m + 255) / 256), 256, 0, s>>>(sorted_keys, perm, n, BC, slots, brs, cptr, ctile, cbr);
+    count_launch();
+}
+
+}  // namespace sili

@@ -35,6 +35,32 @@ struct LayerView {
     const int* colptr;   // [n_out+1] CSC shadow: synapses of column c at [colptr[c], colptr[c+1])
     const int* crow;     // [nnz] their rows, ascending within a column
     const int* cvpos;    // [nnz] their positions in val[]
+    const int* b4_nt = nullptr;  // [ceil(n_in/4)] block4 tiles per block-row (null: no block4)
+};
+
+// One layer's block4 store (4x4 dense FP4 tiles, block4.hpp:1016-1490) on the
+// device.  Block-row br (input rows 4br..4br+3) owns the tile slots
+// [es[br], es[br] + capacity) of which the first nt[br] are live, in
+// ascending block-column.  A tile is 16 slot bytes, slot = lj*4 + li
+// (Block4Tile::slot_index, block4.hpp:309), byte = importance << 4 | weight.
+// sparse[] and alloc[] carry the reference's packed-tile flag and per
+// block-row allocations (index bytes, tile bytes, tile slots), which decide
+// growth, budget errors and eviction exactly as the reference's do.
+struct B4View {
+    int64_t BR = 0, BC = 0;
+    const int64_t* es = nullptr;    // [BR+1] tile region start per block-row
+    int* nt = nullptr;              // [BR] live tiles per block-row
+    int* bc = nullptr;              // [cap] block-column of each tile
+    uint4* tile = nullptr;          // [cap] 16 slot bytes
+    uint8_t* sparse = nullptr;      // [cap] packed-tile flag
+    int64_t* alloc = nullptr;       // [3*BR] idx bytes, tile bytes, tile slots
+    unsigned long long* counters = nullptr;  // [3] dropped growth, overflow events, overflow bytes
+    uint32_t switch_point = 10;
+    // tile column index (rebuilt after structural changes): tiles of
+    // block-column c at [cptr[c], cptr[c+1]), ascending block-row
+    const int* cptr = nullptr;
+    const int* ctile = nullptr;     // global tile slot
+    const int* cbr = nullptr;       // its block-row
 };
 
 struct UpdateParams {
@@ -124,4 +150,26 @@ void launch_probe_per_row(const LayerView& L, const int* in_sorted, int kin, con
                           int64_t n_out, int k, const float* in_acc, const float* grad_acc, int* prow,
                           int* pcol, float* pval, int* counts, cudaStream_t s);
 
+}  // namespace sili
+
+namespace sili {
+// ── block4 (csrc/block4.cu) ──────────────────────────────────────────────────
+// load_dense_codes: every tile of the [BR, BC] grid from row-major codes;
+// row_used[br] receives the reference's packed byte length of the row.
+void launch_b4_load_dense(const uint8_t* wc, const uint8_t* ic, int64_t n_in, int64_t n_out, const B4View& V,
+                          int64_t* row_used, cudaStream_t s);
+// per block-row [3*BR]: packed tile bytes in use, ULEB128 index bytes, live slots
+void launch_b4_row_used(const B4View& V, int64_t* out, cudaStream_t s);
+// forward contribution y[B, n_out] += block4 part (after the scattered part)
+void launch_b4_forward(const LayerView& L, const B4View& V, const float* xT, int B, float* y, cudaStream_t s);
+// dx at lr == 0: dx[B, n_in] += block4 part, tiles in stored order per row
+void launch_b4_dx(const LayerView& L, const B4View& V, const float* dyT, int B, float* dx, cudaStream_t s);
+// lr != 0: fused update of every tile slot + dxT [n_in, B] += block4 part,
+// then merge_row_workspace's eviction and the block4 value_scale step
+void launch_b4_update(const LayerView& L, const B4View& V, const float* xT, const float* dyT, int B,
+                      const UpdateParams& P, float* dxT, cudaStream_t s);
+// tile list for the column index: (bc key, global slot, block-row) of every live tile
+void launch_b4_list(const B4View& V, const int* tile_off, int* keys, int* slots, int* brs, cudaStream_t s);
+void launch_b4_index(const int* sorted_keys, const int* perm, int n, int64_t BC, const int* slots, const int* brs,
+                     int* cptr, int* ctile, int* cbr, cudaStream_t s);
 }  // namespace sili

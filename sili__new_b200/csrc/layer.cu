@@ -75,6 +75,13 @@ struct DBuf {
     void swap(DBuf& o) { std::swap(p, o.p); std::swap(cap, o.cap); }
 };
 
+// FP4_TABLE (fp4quant.hpp:16-33), code 8 = NaN
+float fp4_decode_host(uint32_t code) {
+    static const float t[16] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f, NAN,
+                                -0.5f, -1.0f, -1.5f, -2.0f, -3.0f, -4.0f, -6.0f};
+    return t[code & 15u];
+}
+
 bool is_device_ptr(const void* ptr) {
     if (!ptr) return false;
     cudaPointerAttributes a;
@@ -136,6 +143,18 @@ struct sili_layer {
     DBuf<float> pow_tab;
     float pow_beta2 = NAN;
     int pow_n = 0;
+    // block4 store (Block4Store, block4.hpp:1016-1490); device layout in B4View
+    int64_t b4_BR = 0, b4_BC = 0;
+    DBuf<int64_t> b4_es, b4_alloc, b4_used;
+    DBuf<int> b4_nt, b4_bc;
+    DBuf<uint4> b4_tile;
+    DBuf<uint8_t> b4_sparse;
+    DBuf<unsigned long long> b4_cnt;
+    DBuf<int> b4_cptr, b4_ctile, b4_cbr, b4_keys, b4_keys_o, b4_perm, b4_perm_o, b4_slots, b4_brs, b4_off;
+    int64_t b4_ntiles = 0;                 // live tiles (host mirror)
+    int64_t b4_max_idx = INT64_MAX, b4_max_tile = INT64_MAX;
+    uint32_t b4_switch = 10;
+    bool b4_dirty = true;                  // tile column index stale
     // optional CUDA-event timing of the main forward / backward kernels
     bool timing = false;
     cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
@@ -149,6 +168,15 @@ struct sili_layer {
         v.vs = vs.p; v.os = os.p; v.vsi = vsi.p; v.osi = osi.p; v.vsm = vsm.p;
         v.vstep = vstep.p; v.ostep = ostep.p; v.is = is.p; v.ois = ois.p;
         v.rowptr = rowptr.p; v.abs_cols = abs_cols.p; v.colptr = colptr.p; v.crow = crow.p; v.cvpos = cvpos.p;
+        v.b4_nt = b4_ntiles > 0 ? b4_nt.p : nullptr;
+        return v;
+    }
+    B4View b4view() const {
+        B4View v;
+        v.BR = b4_BR; v.BC = b4_BC;
+        v.es = b4_es.p; v.nt = b4_nt.p; v.bc = b4_bc.p; v.tile = b4_tile.p; v.sparse = b4_sparse.p;
+        v.alloc = b4_alloc.p; v.counters = b4_cnt.p; v.switch_point = b4_switch;
+        v.cptr = b4_cptr.p; v.ctile = b4_ctile.p; v.cbr = b4_cbr.p;
         return v;
     }
 };
@@ -492,6 +520,80 @@ int import_csr(sili_layer* h, const int* d_ptrs, const int* d_idx, const float* 
     return SILI_OK;
 }
 
+// ── block4 store management ─────────────────────────────────────────────────
+// Block4Store::init (block4.hpp:1103-1117): empty, every allocation zero.
+// Each block-row gets `cap` tile slots of device capacity.
+int b4_init(sili_layer* h, int64_t cap, cudaStream_t s) {
+    h->b4_BR = (h->rows + 3) / 4;
+    h->b4_BC = (h->cols + 3) / 4;
+    const int64_t BR = h->b4_BR, total = std::max<int64_t>(BR * cap, 1);
+    RC(h->b4_es.reserve(BR + 1)); RC(h->b4_nt.reserve(BR + 1)); RC(h->b4_alloc.reserve(3 * BR + 1));
+    RC(h->b4_used.reserve(3 * BR + 1)); RC(h->b4_cnt.reserve(3));
+    RC(h->b4_bc.reserve(total)); RC(h->b4_tile.reserve(total)); RC(h->b4_sparse.reserve(total));
+    std::vector<int64_t> es((size_t)BR + 1);
+    for (int64_t br = 0; br <= BR; ++br) es[(size_t)br] = br * cap;
+    CK(cudaMemcpyAsync(h->b4_es.p, es.data(), es.size() * 8, cudaMemcpyHostToDevice, s));
+    CK(cudaMemsetAsync(h->b4_nt.p, 0, (size_t)(BR + 1) * 4, s));
+    CK(cudaMemsetAsync(h->b4_alloc.p, 0, (size_t)(3 * BR + 1) * 8, s));
+    CK(cudaMemsetAsync(h->b4_cnt.p, 0, 3 * sizeof(unsigned long long), s));
+    CK(cudaStreamSynchronize(s));
+    h->b4_ntiles = 0;
+    h->b4_dirty = true;
+    return SILI_OK;
+}
+
+// per block-row [3*BR]: tile bytes used, index bytes used, live slots
+int b4_row_stats(sili_layer* h, std::vector<int64_t>& out, cudaStream_t s) {
+    const int64_t BR = h->b4_BR;
+    out.assign((size_t)(3 * BR), 0);
+    if (BR == 0) return SILI_OK;
+    launch_b4_row_used(h->b4view(), h->b4_used.p, s);
+    CK(cudaMemcpyAsync(out.data(), h->b4_used.p, (size_t)(3 * BR) * 8, cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    return SILI_OK;
+}
+int b4_get_allocs(sili_layer* h, std::vector<int64_t>& a, cudaStream_t s) {
+    a.assign((size_t)(3 * h->b4_BR), 0);
+    if (h->b4_BR == 0) return SILI_OK;
+    CK(cudaMemcpyAsync(a.data(), h->b4_alloc.p, a.size() * 8, cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    return SILI_OK;
+}
+int b4_put_allocs(sili_layer* h, const std::vector<int64_t>& a, cudaStream_t s) {
+    if (h->b4_BR == 0) return SILI_OK;
+    CK(cudaMemcpyAsync(h->b4_alloc.p, a.data(), a.size() * 8, cudaMemcpyHostToDevice, s));
+    CK(cudaStreamSynchronize(s));
+    return SILI_OK;
+}
+
+// Tile column index for the forward: every live tile keyed by its
+// block-column, stably sorted, so each block-column lists its tiles in
+// ascending block-row.
+int ensure_b4_index(sili_layer* h, cudaStream_t s) {
+    if (!h->b4_dirty || h->b4_ntiles == 0) return SILI_OK;
+    const int64_t BR = h->b4_BR, BC = h->b4_BC, n = h->b4_ntiles;
+    RC(h->b4_off.reserve(BR + 1));
+    RC(h->b4_keys.reserve(n)); RC(h->b4_keys_o.reserve(n)); RC(h->b4_perm.reserve(n)); RC(h->b4_perm_o.reserve(n));
+    RC(h->b4_slots.reserve(n)); RC(h->b4_brs.reserve(n));
+    RC(h->b4_cptr.reserve(BC + 1)); RC(h->b4_ctile.reserve(n)); RC(h->b4_cbr.reserve(n));
+    RC(scan_excl_int(h, h->b4_nt.p, h->b4_off.p, BR, s));
+    launch_b4_list(h->b4view(), h->b4_off.p, h->b4_keys.p, h->b4_slots.p, h->b4_brs.p, s);
+    launch_iota(h->b4_perm.p, n, s);
+    int bits = 1;
+    while ((int64_t(1) << bits) < BC) ++bits;
+    size_t bytes = 0;
+    cub::DeviceRadixSort::SortPairs(nullptr, bytes, h->b4_keys.p, h->b4_keys_o.p, h->b4_perm.p, h->b4_perm_o.p,
+                                    (int)n, 0, bits, s);
+    RC(h->cub_tmp.reserve((int64_t)bytes + 1));
+    CK(cub::DeviceRadixSort::SortPairs(h->cub_tmp.p, bytes, h->b4_keys.p, h->b4_keys_o.p, h->b4_perm.p,
+                                       h->b4_perm_o.p, (int)n, 0, bits, s));
+    launch_b4_index(h->b4_keys_o.p, h->b4_perm_o.p, (int)n, BC, h->b4_slots.p, h->b4_brs.p, h->b4_cptr.p,
+                    h->b4_ctile.p, h->b4_cbr.p, s);
+    CK(cudaGetLastError());
+    h->b4_dirty = false;
+    return SILI_OK;
+}
+
 int make_layer(int n_in, int n_out, int max_weights, int device, int stochastic, sili_layer** out) {
     if (n_in < 0 || n_out < 0 || max_weights < 0) return fail(SILI_EINVAL, "negative layer size");
     int ndev = 0;
@@ -543,11 +645,115 @@ int make_layer(int n_in, int n_out, int max_weights, int device, int stochastic,
     if (rc) { cudaStreamDestroy(h->stream); delete h; return rc; }
     h->max_idx_bytes = h->idx_budget;
     h->max_val_bytes = h->val_budget;
+    // block4 store with the constructor's limits (cpu_backend.cpp:390-393)
+    rc = b4_init(h, 0, s);
+    if (rc) { cudaStreamDestroy(h->stream); delete h; return rc; }
+    h->b4_max_idx = (int64_t)max_weights * 8 + 4096;
+    h->b4_max_tile = std::max<int64_t>(4, (int64_t)max_weights / 16) * 16;
     *out = h;
     return SILI_OK;
 }
 
 }  // namespace
+
+// Host copy of the live block4 tiles, in block-row / stored order.
+struct HostTiles {
+    std::vector<int> br, bc;
+    std::vector<uint8_t> slots, sparse;   // 16 per tile, 1 per tile
+};
+int b4_download(sili_layer* h, HostTiles& T, cudaStream_t s) {
+    const int64_t BR = h->b4_BR;
+    std::vector<int64_t> es((size_t)BR + 1);
+    std::vector<int> nt((size_t)BR + 1);
+    if (BR > 0) {
+        CK(cudaMemcpyAsync(es.data(), h->b4_es.p, es.size() * 8, cudaMemcpyDeviceToHost, s));
+        CK(cudaMemcpyAsync(nt.data(), h->b4_nt.p, (size_t)BR * 4, cudaMemcpyDeviceToHost, s));
+    }
+    CK(cudaStreamSynchronize(s));
+    const int64_t cap = BR > 0 ? es[(size_t)BR] : 0;
+    std::vector<int> bc((size_t)std::max<int64_t>(cap, 1));
+    std::vector<uint4> tl((size_t)std::max<int64_t>(cap, 1));
+    std::vector<uint8_t> sp((size_t)std::max<int64_t>(cap, 1));
+    if (cap > 0) {
+        CK(cudaMemcpyAsync(bc.data(), h->b4_bc.p, (size_t)cap * 4, cudaMemcpyDeviceToHost, s));
+        CK(cudaMemcpyAsync(tl.data(), h->b4_tile.p, (size_t)cap * 16, cudaMemcpyDeviceToHost, s));
+        CK(cudaMemcpyAsync(sp.data(), h->b4_sparse.p, (size_t)cap, cudaMemcpyDeviceToHost, s));
+        CK(cudaStreamSynchronize(s));
+    }
+    T = HostTiles();
+    for (int64_t br = 0; br < BR; ++br)
+        for (int e = 0; e < nt[(size_t)br]; ++e) {
+            const int64_t ti = es[(size_t)br] + e;
+            T.br.push_back((int)br);
+            T.bc.push_back(bc[(size_t)ti]);
+            const uint8_t* b = reinterpret_cast<const uint8_t*>(&tl[(size_t)ti]);
+            T.slots.insert(T.slots.end(), b, b + 16);
+            T.sparse.push_back(sp[(size_t)ti]);
+        }
+    return SILI_OK;
+}
+
+int put_out(const void* host_src, void* dst, size_t bytes) {
+    if (bytes == 0) return SILI_OK;
+    if (is_device_ptr(dst)) CK(cudaMemcpy(dst, host_src, bytes, cudaMemcpyHostToDevice));
+    else std::memcpy(dst, host_src, bytes);
+    return SILI_OK;
+}
+
+// delta_csr_combined_to_absolute (delta_csr_memory.hpp:127-213): per row the
+// scattered synapses then the row's live block4 slots, ordered by std::sort
+// on the column with the reference's comparator (same algorithm here).
+int export_combined(sili_layer* h, int* ptrs, int* idx, float* w, float* imp, cudaStream_t s) {
+    const int64_t nnz = h->total_nnz, R = h->rows;
+    DBuf<int> di;
+    DBuf<float> dw, dm;
+    RC(di.reserve(nnz + 1)); RC(dw.reserve(nnz + 1)); RC(dm.reserve(nnz + 1));
+    launch_export(h->view(), di.p, dw.p, dm.p, s);
+    CK(cudaGetLastError());
+    std::vector<int> sp((size_t)R + 1), si((size_t)nnz + 1);
+    std::vector<float> sw((size_t)nnz + 1), sm((size_t)nnz + 1);
+    RC(from_dev(h->rowptr.p, sp.data(), (size_t)(R + 1) * 4, s));
+    RC(from_dev(di.p, si.data(), (size_t)nnz * 4, s));
+    RC(from_dev(dw.p, sw.data(), (size_t)nnz * 4, s));
+    RC(from_dev(dm.p, sm.data(), (size_t)nnz * 4, s));
+    CK(cudaStreamSynchronize(s));
+    HostTiles T;
+    RC(b4_download(h, T, s));
+    std::vector<std::vector<size_t>> row_tiles((size_t)h->b4_BR);
+    for (size_t t = 0; t < T.br.size(); ++t) row_tiles[(size_t)T.br[t]].push_back(t);
+    struct Entry { int col; float w, imp; };
+    std::vector<int> op((size_t)R + 1, 0), oi;
+    std::vector<float> ow, om;
+    std::vector<Entry> ent;
+    for (int64_t r = 0; r < R; ++r) {
+        ent.clear();
+        for (int k = sp[(size_t)r]; k < sp[(size_t)r + 1]; ++k) ent.push_back({si[(size_t)k], sw[(size_t)k], sm[(size_t)k]});
+        const int li = (int)(r % 4);
+        for (size_t t : row_tiles[(size_t)(r / 4)])
+            for (int lj = 0; lj < 4; ++lj) {
+                const uint8_t byte = T.slots[t * 16 + (size_t)(lj * 4 + li)];
+                const int64_t col = (int64_t)T.bc[t] * 4 + lj;
+                if (byte == 0 || col >= h->cols) continue;
+                ent.push_back({(int)col, fp4_decode_host(byte & 0xF), fp4_decode_host((uint8_t)(byte >> 4))});
+            }
+        std::sort(ent.begin(), ent.end(), [](const Entry& a, const Entry& b) { return a.col < b.col; });
+        for (const Entry& e : ent) { oi.push_back(e.col); ow.push_back(e.w); om.push_back(e.imp); }
+        op[(size_t)r + 1] = (int)oi.size();
+    }
+    RC(put_out(op.data(), ptrs, (size_t)(R + 1) * 4));
+    RC(put_out(oi.data(), idx, oi.size() * 4));
+    RC(put_out(ow.data(), w, ow.size() * 4));
+    RC(put_out(om.data(), imp, om.size() * 4));
+    return SILI_OK;
+}
+
+int64_t b4_live_total(sili_layer* h, cudaStream_t s) {
+    std::vector<int64_t> st;
+    if (b4_row_stats(h, st, s)) return -1;
+    int64_t n = 0;
+    for (int64_t br = 0; br < h->b4_BR; ++br) n += st[(size_t)(2 * h->b4_BR + br)];
+    return n;
+}
 
 // ═══════════════════════════════════════════════════════════════════════════
 extern "C" {
@@ -803,6 +1009,10 @@ int sili_layer_forward_dense(sili_layer* h, const float* x, int batch, float* y,
     }
     if (h->timing) CK(cudaEventRecord(h->ev[0], s));
     launch_forward(h->view(), h->xT.p, batch, yd, false, s);
+    if (h->b4_ntiles > 0) {
+        RC(ensure_b4_index(h, s));
+        launch_b4_forward(h->view(), h->b4view(), h->xT.p, batch, yd, s);
+    }
     if (h->timing) { CK(cudaEventRecord(h->ev[1], s)); h->ev_fwd = true; }
     CK(cudaGetLastError());
     if (!dev_out) {
@@ -842,6 +1052,7 @@ int sili_layer_backward_dense(sili_layer* h, const float* x, const float* dy, in
     if (lr == 0.0f) {
         if (h->timing) CK(cudaEventRecord(h->ev[2], s));
         launch_backward_dx(v, h->dyT.p, batch, dxd, s);
+        if (h->b4_ntiles > 0) launch_b4_dx(v, h->b4view(), h->dyT.p, batch, dxd, s);
         if (h->timing) { CK(cudaEventRecord(h->ev[3], s)); h->ev_bwd = true; }
     } else {
         RC(h->dxT.reserve((int64_t)batch * n_in + 1));
@@ -865,6 +1076,8 @@ int sili_layer_backward_dense(sili_layer* h, const float* x, const float* dy, in
         } else {
             CK(cudaMemsetAsync(h->dxT.p, 0, (size_t)batch * n_in * 4, s));
         }
+        // block4 part after the scattered one (linear_disldo.hpp:939-1951)
+        if (h->b4_ntiles > 0) launch_b4_update(v, h->b4view(), h->xT.p, h->dyT.p, batch, P, h->dxT.p, s);
         if (h->has_dead_rows) {
             RC(h->dS.reserve((int64_t)batch * h->rank + 1));
             launch_dead_rows(v, h->xT.p, dyd, batch, h->dS.p, P, s);
@@ -1251,7 +1464,7 @@ int sili_layer_topk_dyx_step(sili_layer* h, const float* x, const float* dy, int
 int sili_layer_sizes(sili_layer* h, int64_t* sizes) {
     RC(use(h));
     sizes[0] = h->rows; sizes[1] = h->cols; sizes[2] = h->total_nnz;
-    sizes[3] = h->idx_n; sizes[4] = h->val_n; sizes[5] = 0;
+    sizes[3] = h->idx_n; sizes[4] = h->val_n; sizes[5] = h->b4_ntiles;
     return SILI_OK;
 }
 
@@ -1259,6 +1472,7 @@ int sili_layer_export(sili_layer* h, int* ptrs, int* idx, float* w, float* imp) 
     RC(use(h));
     cudaStream_t s = h->stream;
     RC(ensure_aux(h, s));
+    if (h->b4_ntiles > 0) return export_combined(h, ptrs, idx, w, imp, s);
     const int64_t nnz = h->total_nnz;
     DBuf<int> di;
     DBuf<float> dw, dm;
@@ -1450,6 +1664,178 @@ int sili_dense_to_top_k_csr(const float* x, int rows, int cols, int64_t k, int* 
                     (void*)rc, (void*)dptrs, (void*)di, (void*)dv, tmp})
         cudaFreeAsync(p, s);
     CK(cudaStreamSynchronize(s));
+    return SILI_OK;
+}
+
+// ── block4 ──────────────────────────────────────────────────────────────────
+int sili_layer_export_nnz(sili_layer* h, int64_t* n) {
+    RC(use(h));
+    int64_t live = 0;
+    if (h->b4_ntiles > 0) {
+        live = b4_live_total(h, h->stream);
+        if (live < 0) return SILI_ECUDA;
+    }
+    *n = h->total_nnz + live;
+    return SILI_OK;
+}
+
+int sili_layer_load_dense_codes(sili_layer* h, const uint8_t* wc, const uint8_t* ic) {
+    RC(use(h));
+    if (!wc || !ic) return fail(SILI_EINVAL, "load_dense_codes: null codes");
+    cudaStream_t s = h->stream;
+    const int64_t n = h->rows * h->cols;
+    DBuf<uint8_t> dw, di;
+    const uint8_t* pw = wc;
+    const uint8_t* pi = ic;
+    if (!is_device_ptr(wc)) { RC(dw.reserve(n + 1)); RC(to_dev(wc, dw.p, (size_t)n, s)); pw = dw.p; }
+    if (!is_device_ptr(ic)) { RC(di.reserve(n + 1)); RC(to_dev(ic, di.p, (size_t)n, s)); pi = di.p; }
+    const int64_t BC = (h->cols + 3) / 4;
+    RC(b4_init(h, BC, s));
+    const int64_t BR = h->b4_BR;
+    std::vector<int> nt((size_t)BR + 1, (int)BC);
+    if (BR > 0) CK(cudaMemcpyAsync(h->b4_nt.p, nt.data(), (size_t)BR * 4, cudaMemcpyHostToDevice, s));
+    CK(cudaMemsetAsync(h->b4_used.p, 0, (size_t)(3 * BR + 1) * 8, s));
+    launch_b4_load_dense(pw, pi, h->rows, h->cols, h->b4view(), h->b4_used.p, s);
+    CK(cudaGetLastError());
+    std::vector<int64_t> used((size_t)BR + 1, 0);
+    if (BR > 0) CK(cudaMemcpyAsync(used.data(), h->b4_used.p, (size_t)BR * 8, cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    // limits block4_load_dense sets (delta_csr_memory.hpp:857-899)
+    const int64_t dense = BR * BC * 16;
+    h->b4_max_idx = BR * BC * 16;
+    h->b4_max_tile = (int64_t)((double)dense * (1.0 + (double)0.2f)) + BR * 16;
+    // Each tile insertion finds the row full (block4_row_insert_tile) and
+    // grows it by block4_ensure_row_headroom (+5 index bytes, +1 tile byte,
+    // +1 slot); the commit then grows the tile bytes to exactly the packed
+    // length.  So: index alloc 5*BC, slots BC, tile bytes = used, and
+    // block4_expand_headroom(0.2, 16) adds the slack.
+    std::vector<int64_t> a((size_t)(3 * BR), 0);
+    int64_t total = 0;
+    for (int64_t br = 0; br < BR; ++br) {
+        const int64_t u = used[(size_t)br];
+        a[(size_t)br] = 5 * BC;
+        a[(size_t)(BR + br)] = u + (int64_t)((float)u * 0.2f) + 16;
+        a[(size_t)(2 * BR + br)] = BC;
+        total += a[(size_t)(BR + br)];
+    }
+    if (total > h->b4_max_tile) return fail(SILI_ENOMEM, "load_dense_codes: block4 tile budget exceeded");
+    RC(b4_put_allocs(h, a, s));
+    h->b4_ntiles = BR * BC;
+    h->b4_dirty = true;
+    // out_degree[c] = n_in for every column (cpu_backend.cpp:916-920)
+    std::vector<int> od((size_t)h->cols + 1, (int)h->rows);
+    if (h->cols > 0) CK(cudaMemcpyAsync(h->out_degree.p, od.data(), (size_t)h->cols * 4, cudaMemcpyHostToDevice, s));
+    CK(cudaStreamSynchronize(s));
+    return SILI_OK;
+}
+
+int sili_layer_b4_expand_headroom(sili_layer* h, float blank_fraction, int64_t min_slack) {
+    RC(use(h));
+    cudaStream_t s = h->stream;
+    const int64_t BR = h->b4_BR;
+    if (BR == 0) return SILI_OK;
+    std::vector<int64_t> st, a;
+    RC(b4_row_stats(h, st, s));
+    RC(b4_get_allocs(h, a, s));
+    int64_t total = 0;
+    for (int64_t br = 0; br < BR; ++br) {
+        const int64_t rb = st[(size_t)br];
+        a[(size_t)(BR + br)] = rb + (int64_t)((float)rb * blank_fraction) + min_slack;
+        total += a[(size_t)(BR + br)];
+    }
+    if (total > h->b4_max_tile) return fail(SILI_ENOMEM, "expand_block4_headroom: block4 tile budget exceeded");
+    return b4_put_allocs(h, a, s);
+}
+
+int sili_layer_b4_equalize_row(sili_layer* h, int64_t row) {
+    RC(use(h));
+    cudaStream_t s = h->stream;
+    const int64_t R = h->b4_BR;
+    if (R == 0) return SILI_OK;
+    row %= R;
+    std::vector<int64_t> st, a;
+    RC(b4_row_stats(h, st, s));
+    RC(b4_get_allocs(h, a, s));
+    std::vector<int> nt((size_t)R);
+    CK(cudaMemcpyAsync(nt.data(), h->b4_nt.p, (size_t)R * 4, cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    int64_t si = 0, stt = 0, se = 0;
+    for (int64_t br = 0; br < R; ++br) { si += a[(size_t)br]; stt += a[(size_t)(R + br)]; se += a[(size_t)(2 * R + br)]; }
+    // Block4Store::equalize_step (block4.hpp:1208-1221) -> block4_row_shift (:497-609)
+    int64_t ti = (si + R - 1) / R, tt = (stt + R - 1) / R, te = (se + R - 1) / R;
+    ti = std::max(ti, st[(size_t)(R + row)]);
+    tt = std::max(tt, st[(size_t)row]);
+    te = std::max(te, (int64_t)nt[(size_t)row]);
+    if (row + 1 >= R) return SILI_OK;
+    int64_t& ai = a[(size_t)row];
+    if (ai != ti) {
+        if (ti > ai && si + (ti - ai) > h->b4_max_idx) return fail(SILI_ENOMEM, "equalizer_step: block4 index budget exceeded");
+        ai = ti;
+    }
+    int64_t& at = a[(size_t)(R + row)];
+    if (at != tt) {
+        if (tt > at && stt + (tt - at) > h->b4_max_tile) {
+            RC(b4_put_allocs(h, a, s));
+            return fail(SILI_ENOMEM, "equalizer_step: block4 tile budget exceeded");
+        }
+        at = tt;
+    }
+    a[(size_t)(2 * R + row)] = te;
+    return b4_put_allocs(h, a, s);
+}
+
+int sili_layer_b4_set_switch_point(sili_layer* h, uint32_t v) {
+    RC(use(h));
+    h->b4_switch = v;
+    return SILI_OK;
+}
+
+int sili_layer_b4_view(sili_layer* h, int64_t* v) {
+    RC(use(h));
+    cudaStream_t s = h->stream;
+    std::vector<int64_t> st, a;
+    RC(b4_row_stats(h, st, s));
+    RC(b4_get_allocs(h, a, s));
+    unsigned long long c[3] = {0, 0, 0};
+    CK(cudaMemcpyAsync(c, h->b4_cnt.p, sizeof(c), cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    const int64_t R = h->b4_BR;
+    int64_t live = 0, used = 0, alloc = 0;
+    for (int64_t br = 0; br < R; ++br) { used += st[(size_t)br]; live += st[(size_t)(2 * R + br)]; alloc += a[(size_t)(R + br)]; }
+    v[0] = h->b4_ntiles; v[1] = live; v[2] = h->b4_switch; v[3] = (int64_t)c[0];
+    v[4] = (int64_t)c[1]; v[5] = (int64_t)c[2]; v[6] = used; v[7] = alloc;
+    return SILI_OK;
+}
+
+int sili_layer_b4_export(sili_layer* h, int* br, int* bc, uint8_t* slots, uint8_t* sparse) {
+    RC(use(h));
+    HostTiles T;
+    RC(b4_download(h, T, h->stream));
+    RC(put_out(T.br.data(), br, T.br.size() * 4));
+    RC(put_out(T.bc.data(), bc, T.bc.size() * 4));
+    RC(put_out(T.slots.data(), slots, T.slots.size()));
+    if (sparse) RC(put_out(T.sparse.data(), sparse, T.sparse.size()));
+    return SILI_OK;
+}
+
+int sili_layer_b4_rows(sili_layer* h, int64_t* out) {
+    RC(use(h));
+    cudaStream_t s = h->stream;
+    const int64_t R = h->b4_BR;
+    std::vector<int64_t> st, a;
+    RC(b4_row_stats(h, st, s));
+    RC(b4_get_allocs(h, a, s));
+    std::vector<int> nt((size_t)R + 1);
+    if (R > 0) CK(cudaMemcpyAsync(nt.data(), h->b4_nt.p, (size_t)R * 4, cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    for (int64_t br = 0; br < R; ++br) {
+        out[6 * br + 0] = a[(size_t)br];
+        out[6 * br + 1] = st[(size_t)(R + br)];
+        out[6 * br + 2] = a[(size_t)(R + br)];
+        out[6 * br + 3] = st[(size_t)br];
+        out[6 * br + 4] = a[(size_t)(2 * R + br)];
+        out[6 * br + 5] = nt[(size_t)br];
+    }
     return SILI_OK;
 }
 

@@ -45,19 +45,30 @@ bool g_seeded = false;
 
 class Layer;
 
+// Block4View (cpu_backend.cpp:51-98): live counters of the layer's block4 store.
 struct Block4View {
-    // block4 tiles are not built by this library yet: the scattered
-    // delta-CSR holds every synapse, so the view reports an empty store.
-    std::size_t tiles() const { return 0; }
-    std::size_t synapses() const { return 0; }
-    uint32_t switch_point = 10;
+    sili_layer* h = nullptr;
+    std::vector<int64_t> v() const {
+        std::vector<int64_t> out(8, 0);
+        check(sili_layer_b4_view(h, out.data()));
+        return out;
+    }
+    std::size_t tiles() const { return (std::size_t)v()[0]; }
+    std::size_t synapses() const { return (std::size_t)v()[1]; }
+    uint32_t get_switch_point() const { return (uint32_t)v()[2]; }
+    void set_switch_point(uint32_t x) { check(sili_layer_b4_set_switch_point(h, x)); }
+    uint64_t dropped_growth_events() const { return (uint64_t)v()[3]; }
+    uint64_t row_merge_overflow_events() const { return (uint64_t)v()[4]; }
+    uint64_t row_merge_overflow_bytes_dropped() const { return (uint64_t)v()[5]; }
+    std::size_t used_bytes() const { return (std::size_t)v()[6]; }
+    std::size_t alloc_bytes() const { return (std::size_t)v()[7]; }
 };
 
 class Layer {
 public:
     sili_layer* h = nullptr;
     int n_in, n_out, cpus;
-    int synap_row = 0, eq_row = 0;
+    int synap_row = 0, eq_row = 0, b4_eq_row = 0;
 
     Layer(int n_inputs, int n_outputs, int max_weights, int num_cpus, bool stochastic, int device)
         : n_in(n_inputs), n_out(n_outputs), cpus(num_cpus) {
@@ -172,10 +183,47 @@ public:
         synap_row = n_in > 0 ? (synap_row + 1) % n_in : 0;
         return synap_row_step(row, cutoff, max_rw, max_prune, eps);
     }
+    // equalizer_step, cpu_backend.cpp:631-641: scattered rows, then block4 rows,
+    // each with its own cursor (advanced only when its step succeeds)
     void equalizer_step() {
-        const int row = eq_row;
+        check(sili_layer_equalize_row(h, eq_row));
         eq_row = n_in > 0 ? (eq_row + 1) % n_in : 0;
-        check(sili_layer_equalize_row(h, row));
+        const int br = (n_in + 3) / 4;
+        check(sili_layer_b4_equalize_row(h, b4_eq_row));
+        b4_eq_row = br > 0 ? (b4_eq_row + 1) % br : 0;
+    }
+    void load_dense_codes(py::array_t<uint8_t, py::array::c_style | py::array::forcecast> w,
+                          py::array_t<uint8_t, py::array::c_style | py::array::forcecast> imp) {
+        if ((int64_t)w.size() != (int64_t)n_in * n_out || (int64_t)imp.size() != (int64_t)n_in * n_out)
+            throw py::value_error("load_dense_codes: codes must be [n_inputs, n_outputs]");
+        check(sili_layer_load_dense_codes(h, w.data(), imp.data()));
+    }
+    void expand_block4_headroom(float bf) { check(sili_layer_b4_expand_headroom(h, bf, 16)); }
+    void compact_block4() { check(sili_layer_b4_expand_headroom(h, 0.0f, 0)); }
+    py::tuple b4_tiles() {
+        int64_t sz[6];
+        check(sili_layer_sizes(h, sz));
+        const py::ssize_t n = (py::ssize_t)sz[5];
+        py::array_t<int> br(n), bc(n);
+        py::array_t<uint8_t> sl({n, (py::ssize_t)16}), sp(n);
+        check(sili_layer_b4_export(h, br.mutable_data(), bc.mutable_data(), sl.mutable_data(), sp.mutable_data()));
+        return py::make_tuple(br, bc, sl, sp);
+    }
+    py::array_t<int64_t> b4_rows() {
+        const py::ssize_t R = (n_in + 3) / 4;
+        py::array_t<int64_t> out({R, (py::ssize_t)6});
+        check(sili_layer_b4_rows(h, out.mutable_data()));
+        return out;
+    }
+    py::array_t<int64_t> b4_view() {
+        py::array_t<int64_t> out((py::ssize_t)8);
+        check(sili_layer_b4_view(h, out.mutable_data()));
+        return out;
+    }
+    int64_t combined_nnz() const {
+        int64_t n = 0;
+        check(sili_layer_export_nnz(h, &n));
+        return n;
     }
     void equalize_to_capacity(int te, int tb) { check(sili_layer_equalize_to_capacity(h, te, tb)); }
     void compact() { check(sili_layer_compact(h)); }
@@ -219,10 +267,9 @@ public:
     }
 
     py::tuple export_csr() {
-        int64_t s[6];
-        check(sili_layer_sizes(h, s));
-        py::array_t<int> p((py::ssize_t)n_in + 1), i((py::ssize_t)s[2]);
-        py::array_t<float> w((py::ssize_t)s[2]), m((py::ssize_t)s[2]);
+        const py::ssize_t n = (py::ssize_t)combined_nnz();
+        py::array_t<int> p((py::ssize_t)n_in + 1), i(n);
+        py::array_t<float> w(n), m(n);
         check(sili_layer_export(h, p.mutable_data(), i.mutable_data(), w.mutable_data(), m.mutable_data()));
         return py::make_tuple(p, i, w, m);
     }
@@ -371,8 +418,16 @@ void bind_layer(py::module_& m, const char* name) {
         .def_property_readonly("num_cpus", [](T& s) { return s.cpus; })
         .def_property_readonly("n_inputs", [](T& s) { return s.n_in; })
         .def_property_readonly("n_outputs", [](T& s) { return s.n_out; })
-        .def_property_readonly("nnz", [](T& s) { return (int)s.scattered_nnz(); })
-        .def_property_readonly("block4", [](T&) { return Block4View(); })
+        .def_property_readonly("nnz", [](T& s) { return (int)s.combined_nnz(); })
+        .def_property_readonly("block4", py::cpp_function([](T& s) { Block4View v; v.h = s.h; return v; },
+                                                          py::keep_alive<0, 1>()))
+        .def("load_dense_codes", &T::load_dense_codes, py::arg("weight_codes"), py::arg("importance_codes"))
+        .def("expand_block4_headroom", &T::expand_block4_headroom, py::arg("blank_fraction") = 0.2f)
+        .def("compact_block4", &T::compact_block4)
+        .def("b4_tiles", &T::b4_tiles)
+        .def("b4_rows", &T::b4_rows)
+        .def("b4_view", &T::b4_view)
+        .def("set_switch_point", [](T& s, uint32_t v) { check(sili_layer_b4_set_switch_point(s.h, v)); })
         .def_property_readonly("last_input", &T::last_input);
 }
 
@@ -383,7 +438,12 @@ PYBIND11_MODULE(_cuda, m) {
     py::class_<Block4View>(m, "Block4View")
         .def_property_readonly("tiles", &Block4View::tiles)
         .def_property_readonly("synapses", &Block4View::synapses)
-        .def_readwrite("switch_point", &Block4View::switch_point);
+        .def_property("switch_point", &Block4View::get_switch_point, &Block4View::set_switch_point)
+        .def_property_readonly("dropped_growth_events", &Block4View::dropped_growth_events)
+        .def_property_readonly("row_merge_overflow_events", &Block4View::row_merge_overflow_events)
+        .def_property_readonly("row_merge_overflow_bytes_dropped", &Block4View::row_merge_overflow_bytes_dropped)
+        .def_property_readonly("used_bytes", &Block4View::used_bytes)
+        .def_property_readonly("alloc_bytes", &Block4View::alloc_bytes);
     bind_layer<LayerT<true>>(m, "SparseLinearLayer");
     bind_layer<LayerT<false>>(m, "SparseLinearLayerDeterministic");
     m.attr("SCALE_VALUE") = SILI_SCALE_VALUE;
