@@ -1776,9 +1776,10 @@ static void b4_backward(OLayer* L, const float* x, const float* dy, int batch, f
                         const float imp_ratio = ci[lj] / cis4[lj];
                         uint8_t wq, iq;
                         if (L->stochastic) {
-                            const uint64_t el = (uint64_t)row * (uint64_t)n_out + (uint64_t)col4[lj];
-                            wq = o_fp4_quantize_stochastic_r(quant[lj], o_rng_draw(L->seed, call, el, 2));
-                            iq = o_fp4_quantize_stochastic_r(imp_ratio, o_rng_draw(L->seed, call, el, 3));
+                            /* block4 draws use their own element space: bit 61 | row*n_out + col */
+                            const uint64_t el = (1ULL << 61) | ((uint64_t)row * (uint64_t)n_out + (uint64_t)col4[lj]);
+                            wq = o_fp4_quantize_stochastic_r(quant[lj], o_rng_draw(L->seed, call, el, 0));
+                            iq = o_fp4_quantize_stochastic_r(imp_ratio, o_rng_draw(L->seed, call, el, 1));
                         } else {
                             wq = o_fp4_encode(quant[lj]);
                             iq = o_fp4_encode(imp_ratio);
