@@ -129,12 +129,18 @@ int sili_layer_backward_sparse(sili_layer* h, const float* x, const int* dptrs, 
 int sili_layer_build_probes(sili_layer* h, int k, int per_row);
 int sili_layer_num_probes(sili_layer* h, int64_t* n);
 int sili_layer_get_probes(sili_layer* h, int* rows, int* cols, float* scores);
-/* synap_row_step over rows [row0, row0+nrows) (wrapping), cpu_backend.cpp:611-635
- * -> delta_csr_synap_row_step (delta_csr_memory.hpp:1019-1258) once per row, in
- * row order.  did_any (may be NULL) gets 1 if any row step returned true. */
+/* synap_row_step over the sweep rows (row0 + i) % n_in, i = 0..nrows-1,
+ * cpu_backend.cpp:611-635 -> delta_csr_synap_row_step
+ * (delta_csr_memory.hpp:1019-1258, with block4 promotion / demotion) once per
+ * row in sweep order; the result equals nrows calls of the reference's
+ * synap_row_step.  did (may be NULL; host or device, nrows bytes) receives
+ * each step's return value.  A row that runs out of blank space stops the
+ * sweep there with SILI_EHEADROOM (the reference's runtime_error), rows
+ * before it done, that row partly done as the reference leaves it; a block4
+ * budget overrun gives SILI_ENOMEM the same way. */
 int sili_layer_synap_rows(sili_layer* h, int row0, int nrows, float importance_cutoff,
                           int max_row_weights, int max_prune_per_step, float importance_eps,
-                          int* did_any);
+                          uint8_t* did);
 /* equalizer_step() for one row, cpu_backend.cpp:649-657 -> delta_csr_equalize_step */
 int sili_layer_equalize_row(sili_layer* h, int row);
 /* equalize_to_capacity, cpu_backend.cpp:684-729 */

@@ -422,6 +422,8 @@ class OracleLayer(_LayerBase):
                                      max_prune_per_step, importance_eps, C.byref(did))
         if rc == STATUS_EHEADROOM:
             raise RuntimeError(f"synap_row_step: row {current_row % self.n_inputs} ran out of blank space")
+        if rc == STATUS_ENOMEM:
+            raise MemoryError(f"synap_row_step: block4 budget exceeded at row {current_row % self.n_inputs}")
         return bool(did.value)
 
     def synap_step(self, importance_cutoff, max_row_weights, max_prune_per_step=8, importance_eps=1e-3):

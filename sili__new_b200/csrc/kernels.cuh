@@ -153,6 +153,59 @@ void launch_probe_per_row(const LayerView& L, const int* in_sorted, int kin, con
 }  // namespace sili
 
 namespace sili {
+// ── synaptogenesis (csrc/synap.cu) ──────────────────────────────────────────
+struct SynView {
+    int64_t n_in = 0, n_out = 0;
+    const int64_t* bs = nullptr;
+    int64_t* be = nullptr;
+    const int64_t* es = nullptr;
+    int64_t* ee = nullptr;
+    uint8_t* idx = nullptr;
+    uint8_t* val = nullptr;
+    int* out_degree = nullptr;
+    int* od_decs = nullptr;                 // [n_out] decrements requested per column
+    // block4 (same layout as B4View)
+    const int64_t* b4_es = nullptr;
+    int* nt = nullptr;
+    int* b4_bc = nullptr;
+    uint4* b4_tile = nullptr;
+    uint8_t* b4_sparse = nullptr;
+    int64_t* alloc = nullptr;
+    unsigned long long* counters = nullptr;
+    uint32_t switch_point = 10;
+    int64_t max_idx = 0, max_tile = 0, tot_idx0 = 0, tot_tile0 = 0;
+    unsigned long long* grow = nullptr;     // [2] allocation growth: index bytes, tile bytes
+    // probes (COO in the reference's order) and their per-row index
+    int64_t n_probes = 0;
+    const int* pcol = nullptr;
+    const float* pval = nullptr;
+    const int* pr_ptr = nullptr;            // [n_in+1]
+    const int* pr_idx = nullptr;            // probe ids grouped by row, COO order kept
+    // results
+    unsigned long long* nnz_delta = nullptr;
+    long long* err_i = nullptr;             // first failing sweep position
+    int* err_code = nullptr;
+    int* flags = nullptr;                   // 1: out_degree clamp possible, 4: tile capacity short
+    uint8_t* did = nullptr;                 // per sweep position
+    // per-thread scratch
+    uint8_t* scratch = nullptr;
+    int64_t scratch_stride = 0, scratch_m = 0, scratch_p = 0;
+};
+struct SynParams {
+    int64_t row0 = 0, nrows = 0, limit = 0;
+    float cutoff = 0.0f, eps = 1e-3f;
+    int max_rw = 0, max_prune = 8;
+};
+void launch_synap(const SynView& V, const SynParams& P, bool sequential, cudaStream_t s);
+void launch_od_check(const int* od0, const int* decs, int64_t n, int* flags, cudaStream_t s);
+void launch_lower_bound(const int* sorted_keys, int n, int64_t nkeys, int* ptr, cudaStream_t s);
+// bytes of per-thread scratch for rows of up to m entries and p probes
+inline int64_t synap_scratch_stride(int64_t m, int64_t p) {
+    auto r = [](int64_t b) { return (b + 15) & ~int64_t(15); };
+    return r(m * 4) + r(m) + r(m * 4) + r(m * 4) + r(m) + r(m * 4) + r(m * 4) + r(m) + r(m * 4) +
+           5 * r(p * 4);
+}
+
 // ── block4 (csrc/block4.cu) ──────────────────────────────────────────────────
 // load_dense_codes: every tile of the [BR, BC] grid from row-major codes;
 // row_used[br] receives the reference's packed byte length of the row.

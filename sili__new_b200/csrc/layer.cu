@@ -155,6 +155,14 @@ struct sili_layer {
     int64_t b4_max_idx = INT64_MAX, b4_max_tile = INT64_MAX;
     uint32_t b4_switch = 10;
     bool b4_dirty = true;                  // tile column index stale
+    // synaptogenesis working set (probe-by-row index, scratch, snapshot)
+    struct SynStateT {
+        DBuf<int> pr_ptr, keys, keys_o, ids, ids_o, od0, od_decs;
+        DBuf<uint8_t> scratch, did;
+        DBuf<long long> res;
+        DBuf<uint8_t> s_idx, s_val, s_be, s_ee, s_od, s_nt, s_bc, s_tile, s_sp, s_alloc, s_cnt;
+        int64_t m = 0, p = 0, stride = 0;
+    } syn;
     // optional CUDA-event timing of the main forward / backward kernels
     bool timing = false;
     cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
@@ -180,6 +188,7 @@ struct sili_layer {
         return v;
     }
 };
+using SynState = sili_layer::SynStateT;
 
 namespace {
 
@@ -755,6 +764,166 @@ int64_t b4_live_total(sili_layer* h, cudaStream_t s) {
     return n;
 }
 
+// ── synaptogenesis support ──────────────────────────────────────────────────
+// Re-lay the block4 store out so block-row br has newcap[br] tile slots.
+int b4_relayout(sili_layer* h, const std::vector<int64_t>& newcap, cudaStream_t s) {
+    const int64_t BR = h->b4_BR;
+    std::vector<int64_t> es((size_t)BR + 1);
+    std::vector<int> nt((size_t)BR + 1);
+    CK(cudaMemcpyAsync(es.data(), h->b4_es.p, (size_t)(BR + 1) * 8, cudaMemcpyDeviceToHost, s));
+    CK(cudaMemcpyAsync(nt.data(), h->b4_nt.p, (size_t)BR * 4, cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    std::vector<int64_t> ne((size_t)BR + 1, 0);
+    for (int64_t br = 0; br < BR; ++br) ne[(size_t)br + 1] = ne[(size_t)br] + std::max<int64_t>(newcap[(size_t)br], nt[(size_t)br]);
+    const int64_t total = std::max<int64_t>(ne[(size_t)BR], 1);
+    DBuf<int> nbc;
+    DBuf<uint4> ntile;
+    DBuf<uint8_t> nsp;
+    RC(nbc.reserve(total)); RC(ntile.reserve(total)); RC(nsp.reserve(total));
+    for (int64_t br = 0; br < BR; ++br) {
+        const int n = nt[(size_t)br];
+        if (!n) continue;
+        CK(cudaMemcpyAsync(nbc.p + ne[(size_t)br], h->b4_bc.p + es[(size_t)br], (size_t)n * 4, cudaMemcpyDeviceToDevice, s));
+        CK(cudaMemcpyAsync(ntile.p + ne[(size_t)br], h->b4_tile.p + es[(size_t)br], (size_t)n * 16, cudaMemcpyDeviceToDevice, s));
+        CK(cudaMemcpyAsync(nsp.p + ne[(size_t)br], h->b4_sparse.p + es[(size_t)br], (size_t)n, cudaMemcpyDeviceToDevice, s));
+    }
+    CK(cudaMemcpyAsync(h->b4_es.p, ne.data(), (size_t)(BR + 1) * 8, cudaMemcpyHostToDevice, s));
+    CK(cudaStreamSynchronize(s));
+    h->b4_bc.swap(nbc); h->b4_tile.swap(ntile); h->b4_sparse.swap(nsp);
+    h->b4_dirty = true;
+    return SILI_OK;
+}
+
+// Probe-by-row index, scratch sizing and block4 capacity for a sweep of
+// nrows rows.
+int synap_prepare(sili_layer* h, int64_t nrows, cudaStream_t s) {
+    SynState& Z = h->syn;
+    const int64_t R = h->rows, C = h->cols, BR = h->b4_BR, np = h->n_probes;
+    RC(Z.pr_ptr.reserve(R + 1));
+    RC(Z.keys.reserve(np + 1)); RC(Z.keys_o.reserve(np + 1)); RC(Z.ids.reserve(np + 1)); RC(Z.ids_o.reserve(np + 1));
+    if (np > 0) {
+        CK(cudaMemcpyAsync(Z.keys.p, h->prow.p, (size_t)np * 4, cudaMemcpyDeviceToDevice, s));
+        launch_iota(Z.ids.p, np, s);
+        int bits = 1;
+        while ((int64_t(1) << bits) <= R) ++bits;
+        size_t bytes = 0;
+        cub::DeviceRadixSort::SortPairs(nullptr, bytes, Z.keys.p, Z.keys_o.p, Z.ids.p, Z.ids_o.p, (int)np, 0, bits, s);
+        RC(h->cub_tmp.reserve((int64_t)bytes + 1));
+        CK(cub::DeviceRadixSort::SortPairs(h->cub_tmp.p, bytes, Z.keys.p, Z.keys_o.p, Z.ids.p, Z.ids_o.p, (int)np, 0,
+                                           bits, s));
+    }
+    launch_lower_bound(Z.keys_o.p, (int)np, R, Z.pr_ptr.p, s);
+    std::vector<int> pp((size_t)R + 1);
+    CK(cudaMemcpyAsync(pp.data(), Z.pr_ptr.p, (size_t)(R + 1) * 4, cudaMemcpyDeviceToHost, s));
+    HostLayout L;
+    RC(get_layout(h, L));
+    std::vector<int> nt((size_t)BR + 1, 0);
+    std::vector<int64_t> es4((size_t)BR + 1, 0);
+    if (BR > 0) {
+        CK(cudaMemcpyAsync(nt.data(), h->b4_nt.p, (size_t)BR * 4, cudaMemcpyDeviceToHost, s));
+        CK(cudaMemcpyAsync(es4.data(), h->b4_es.p, (size_t)(BR + 1) * 8, cudaMemcpyDeviceToHost, s));
+    }
+    CK(cudaStreamSynchronize(s));
+    // tile capacity: every add of a row may create one tile in its block-row
+    const int64_t passes = (nrows + R - 1) / R;
+    std::vector<int64_t> need((size_t)BR, 0);
+    bool grow = false;
+    int64_t maxp = 0, maxcap_tiles = 0, maxrow = 0;
+    for (int64_t r = 0; r < R; ++r) {
+        const int64_t pr = pp[(size_t)r + 1] - pp[(size_t)r];
+        maxp = std::max(maxp, pr);
+        need[(size_t)(r / 4)] += pr * passes;
+        maxrow = std::max(maxrow, L.es[(size_t)r + 1] - L.es[(size_t)r]);
+    }
+    for (int64_t br = 0; br < BR; ++br) {
+        need[(size_t)br] += nt[(size_t)br];
+        if (need[(size_t)br] > es4[(size_t)br + 1] - es4[(size_t)br]) grow = true;
+    }
+    if (grow) {
+        for (int64_t br = 0; br < BR; ++br)
+            need[(size_t)br] = std::max(need[(size_t)br] + 8, es4[(size_t)br + 1] - es4[(size_t)br]);
+        RC(b4_relayout(h, need, s));
+    }
+    for (int64_t br = 0; br < BR; ++br)
+        maxcap_tiles = std::max(maxcap_tiles, grow ? need[(size_t)br] : es4[(size_t)br + 1] - es4[(size_t)br]);
+    Z.m = maxrow + 4 * maxcap_tiles + 16;
+    Z.p = maxp + 1;
+    Z.stride = synap_scratch_stride(Z.m, Z.p);
+    const int64_t threads = std::max<int64_t>(BR, 1);
+    RC(Z.scratch.reserve(Z.stride * threads + 16));
+    RC(Z.od0.reserve(C + 1)); RC(Z.od_decs.reserve(C + 1)); RC(Z.did.reserve(nrows + 1)); RC(Z.res.reserve(8));
+    return SILI_OK;
+}
+
+// Save (save=true) or restore the state a sweep changes.
+int snapshot_state(sili_layer* h, bool save, cudaStream_t s) {
+    SynState& Z = h->syn;
+    const int64_t R = h->rows, C = h->cols, BR = h->b4_BR;
+    int64_t cap4 = 0;
+    if (BR > 0) {
+        CK(cudaMemcpyAsync(&cap4, h->b4_es.p + BR, 8, cudaMemcpyDeviceToHost, s));
+        CK(cudaStreamSynchronize(s));
+    }
+    struct Item { void* live; DBuf<uint8_t>* snap; size_t bytes; };
+    Item items[] = {
+        {h->idx.p, &Z.s_idx, (size_t)h->idx_n}, {h->val.p, &Z.s_val, (size_t)h->val_n},
+        {h->be.p, &Z.s_be, (size_t)R * 8}, {h->ee.p, &Z.s_ee, (size_t)R * 8},
+        {h->out_degree.p, &Z.s_od, (size_t)C * 4}, {h->b4_nt.p, &Z.s_nt, (size_t)BR * 4},
+        {h->b4_bc.p, &Z.s_bc, (size_t)cap4 * 4}, {h->b4_tile.p, &Z.s_tile, (size_t)cap4 * 16},
+        {h->b4_sparse.p, &Z.s_sp, (size_t)cap4}, {h->b4_alloc.p, &Z.s_alloc, (size_t)(3 * BR) * 8},
+        {h->b4_cnt.p, &Z.s_cnt, 3 * sizeof(unsigned long long)},
+    };
+    for (Item& it : items) {
+        if (it.bytes == 0) continue;
+        if (save) {
+            RC(it.snap->reserve((int64_t)it.bytes));
+            CK(cudaMemcpyAsync(it.snap->p, it.live, it.bytes, cudaMemcpyDeviceToDevice, s));
+        } else {
+            CK(cudaMemcpyAsync(it.live, it.snap->p, it.bytes, cudaMemcpyDeviceToDevice, s));
+        }
+    }
+    if (save && C > 0) CK(cudaMemcpyAsync(Z.od0.p, h->out_degree.p, (size_t)C * 4, cudaMemcpyDeviceToDevice, s));
+    CK(cudaStreamSynchronize(s));
+    return SILI_OK;
+}
+
+int synap_reset_results(sili_layer* h, int64_t nrows, cudaStream_t s) {
+    SynState& Z = h->syn;
+    long long init[8] = {0, 0, 0, LLONG_MAX, 0, 0, 0, 0};
+    CK(cudaMemcpyAsync(Z.res.p, init, sizeof(init), cudaMemcpyHostToDevice, s));
+    CK(cudaMemsetAsync(Z.od_decs.p, 0, (size_t)(h->cols + 1) * 4, s));
+    CK(cudaMemsetAsync(Z.did.p, 0, (size_t)nrows + 1, s));
+    return SILI_OK;
+}
+
+SynView synap_view(sili_layer* h) {
+    SynState& Z = h->syn;
+    SynView V;
+    V.n_in = h->rows; V.n_out = h->cols;
+    V.bs = h->bs.p; V.be = h->be.p; V.es = h->es.p; V.ee = h->ee.p;
+    V.idx = h->idx.p; V.val = h->val.p;
+    V.out_degree = h->out_degree.p; V.od_decs = Z.od_decs.p;
+    V.b4_es = h->b4_es.p; V.nt = h->b4_nt.p; V.b4_bc = h->b4_bc.p; V.b4_tile = h->b4_tile.p;
+    V.b4_sparse = h->b4_sparse.p; V.alloc = h->b4_alloc.p; V.counters = h->b4_cnt.p; V.switch_point = h->b4_switch;
+    V.max_idx = h->b4_max_idx; V.max_tile = h->b4_max_tile;
+    std::vector<int64_t> a((size_t)(3 * h->b4_BR), 0);
+    if (h->b4_BR > 0) {
+        cudaMemcpy(a.data(), h->b4_alloc.p, a.size() * 8, cudaMemcpyDeviceToHost);
+        for (int64_t br = 0; br < h->b4_BR; ++br) { V.tot_idx0 += a[(size_t)br]; V.tot_tile0 += a[(size_t)(h->b4_BR + br)]; }
+    }
+    long long* r = reinterpret_cast<long long*>(Z.res.p);
+    V.grow = reinterpret_cast<unsigned long long*>(r);         // res[0..1]
+    V.nnz_delta = reinterpret_cast<unsigned long long*>(r + 2);
+    V.err_i = r + 3;
+    V.err_code = reinterpret_cast<int*>(r + 4);
+    V.flags = reinterpret_cast<int*>(r + 6);
+    V.n_probes = h->n_probes; V.pcol = h->pcol.p; V.pval = h->pval.p;
+    V.pr_ptr = Z.pr_ptr.p; V.pr_idx = Z.ids_o.p;
+    V.did = Z.did.p;
+    V.scratch = Z.scratch.p; V.scratch_stride = Z.stride; V.scratch_m = Z.m; V.scratch_p = Z.p;
+    return V;
+}
+
 // ═══════════════════════════════════════════════════════════════════════════
 extern "C" {
 
@@ -1273,11 +1442,68 @@ int sili_layer_get_probes(sili_layer* h, int* rows, int* cols, float* scores) {
 }
 
 int sili_layer_synap_rows(sili_layer* h, int row0, int nrows, float importance_cutoff, int max_row_weights,
-                          int max_prune_per_step, float importance_eps, int* did_any) {
+                          int max_prune_per_step, float importance_eps, uint8_t* did) {
     RC(use(h));
-    (void)row0; (void)nrows; (void)importance_cutoff; (void)max_row_weights; (void)max_prune_per_step;
-    (void)importance_eps; (void)did_any;
-    return fail(SILI_EINVAL, "synap_rows: not built yet");
+    cudaStream_t s = h->stream;
+    const int64_t R = h->rows, C = h->cols, BR = h->b4_BR;
+    if (nrows <= 0 || R == 0) return SILI_OK;
+    if (max_prune_per_step < 0) return fail(SILI_EINVAL, "synap_rows: max_prune_per_step < 0");
+    RC(synap_prepare(h, nrows, s));
+    SynState& Z = h->syn;
+    // snapshot of everything a sweep may change
+    RC(snapshot_state(h, true, s));
+    SynView V = synap_view(h);
+    SynParams P;
+    P.row0 = row0; P.nrows = nrows; P.limit = nrows - 1;
+    P.cutoff = importance_cutoff; P.eps = importance_eps; P.max_rw = max_row_weights; P.max_prune = max_prune_per_step;
+    bool sequential = false;
+    for (int attempt = 0; attempt < 4; ++attempt) {
+        RC(synap_reset_results(h, nrows, s));
+        launch_synap(V, P, sequential, s);
+        CK(cudaGetLastError());
+        launch_od_check(Z.od0.p, Z.od_decs.p, C, reinterpret_cast<int*>(Z.res.p + 6), s);
+        long long res[8];
+        CK(cudaMemcpyAsync(res, Z.res.p, sizeof(res), cudaMemcpyDeviceToHost, s));
+        CK(cudaStreamSynchronize(s));
+        const unsigned long long grow_i = (unsigned long long)res[0], grow_t = (unsigned long long)res[1];
+        const long long err_i = res[3];
+        const int err_code = (int)(res[4] & 0xFFFFFFFF), flags = (int)(res[6] & 0xFFFFFFFF);
+        if (flags & 4) return fail(SILI_ECUDA, "synap_rows: block4 tile capacity reservation too small");
+        const bool over_budget = V.tot_idx0 + (int64_t)grow_i > h->b4_max_idx || V.tot_tile0 + (int64_t)grow_t > h->b4_max_tile;
+        if (!sequential && ((flags & 1) || over_budget)) {
+            // order-dependent: re-run the whole sweep in order, in one thread
+            RC(snapshot_state(h, false, s));
+            sequential = true;
+            continue;
+        }
+        if (!sequential && err_i != LLONG_MAX && P.limit != err_i) {
+            // stop at the first failing row, as the reference does
+            RC(snapshot_state(h, false, s));
+            P.limit = err_i;
+            continue;
+        }
+        h->total_nnz += (int64_t)res[2];
+        h->aux_dirty = true;
+        h->b4_dirty = true;
+        std::vector<int> nt((size_t)BR + 1, 0);
+        if (BR > 0) CK(cudaMemcpyAsync(nt.data(), h->b4_nt.p, (size_t)BR * 4, cudaMemcpyDeviceToHost, s));
+        CK(cudaStreamSynchronize(s));
+        h->b4_ntiles = 0;
+        for (int64_t br = 0; br < BR; ++br) h->b4_ntiles += nt[(size_t)br];
+        if (did) RC(from_dev(Z.did.p, did, (size_t)nrows, s));
+        CK(cudaStreamSynchronize(s));
+        if (err_i != LLONG_MAX) {
+            const int64_t r = ((int64_t)row0 + err_i) % R;
+            if (err_code == SILI_ENOMEM)
+                return fail(SILI_ENOMEM, "synap_row_step: block4 budget exceeded at row " + std::to_string(r));
+            return fail(SILI_EHEADROOM, "delta_csr_synap_row_step: row " + std::to_string(r) +
+                                            " ran out of blank space. Call equalizer_step() to redistribute space "
+                                            "from adjacent rows before retrying, or reduce max_row_weights / raise "
+                                            "importance_cutoff.");
+        }
+        return SILI_OK;
+    }
+    return fail(SILI_ECUDA, "synap_rows: no consistent result");
 }
 
 // ── headroom management ─────────────────────────────────────────────────────

@@ -174,9 +174,16 @@ public:
         return py::make_tuple(r, c, v);
     }
     bool synap_row_step(int row, float cutoff, int max_rw, int max_prune, float eps) {
-        int did = 0;
+        uint8_t did = 0;
         check(sili_layer_synap_rows(h, row, 1, cutoff, max_rw, max_prune, eps, &did));
         return did != 0;
+    }
+    // nrows consecutive synap_row_step calls from row0 (wrapping) in one
+    // device sweep; returns each step's result
+    py::array_t<uint8_t> synap_rows(int row0, int nrows, float cutoff, int max_rw, int max_prune, float eps) {
+        py::array_t<uint8_t> did((py::ssize_t)std::max(nrows, 0));
+        check(sili_layer_synap_rows(h, row0, nrows, cutoff, max_rw, max_prune, eps, did.mutable_data()));
+        return did;
     }
     bool synap_step(float cutoff, int max_rw, int max_prune, float eps) {
         const int row = synap_row;
@@ -349,6 +356,8 @@ void bind_layer(py::module_& m, const char* name) {
         .def("build_probes", &T::build_probes, py::arg("k"), py::arg("per_row") = false)
         .def("probes", &T::probes)
         .def("synap_row_step", &T::synap_row_step, py::arg("current_row"), py::arg("importance_cutoff"),
+             py::arg("max_row_weights"), py::arg("max_prune_per_step") = 8, py::arg("importance_eps") = 1e-3f)
+        .def("synap_rows", &T::synap_rows, py::arg("row0"), py::arg("nrows"), py::arg("importance_cutoff"),
              py::arg("max_row_weights"), py::arg("max_prune_per_step") = 8, py::arg("importance_eps") = 1e-3f)
         .def("synap_step", &T::synap_step, py::arg("importance_cutoff"), py::arg("max_row_weights"),
              py::arg("max_prune_per_step") = 8, py::arg("importance_eps") = 1e-3f)

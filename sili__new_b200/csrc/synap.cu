@@ -1,0 +1,670 @@
+// Synaptogenesis on the device: delta_csr_synap_row_step
+// (delta_csr_memory.hpp:1019-1258) with block4 promotion / demotion
+// (block4_maybe_promote :593-702, block4_demote_tile :946-1003) over a sweep
+// of rows, bit-exact with the reference's single-thread result.
+//
+// Work split.  A row's step reads and writes only its own scattered row, the
+// tiles of its block-row (input rows 4br..4br+3) and, through promotion and
+// demotion, the other scattered rows of that block-row.  Block-rows are
+// therefore independent except through three global quantities: the
+// block4 byte budgets (the reference throws / drops when a running total
+// would pass them), out_degree's clamp at zero, and the first row that runs
+// out of blank space (the reference stops the sweep there).  The kernel runs
+// one thread per block-row, each taking its rows in sweep order; the host
+// checks afterwards whether any of the three could have depended on the
+// order and, if so, restores the snapshot and re-runs exactly: truncated at
+// the first failing row, or in one thread over the whole sweep in order.
+//
+// Sorting uses the same introsort as GCC's std::sort (the reference's
+// orderings are std::sort, which is not stable), so ties among the 15
+// stored importance values are broken exactly as the reference breaks them.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace sili {
+
+namespace {
+
+// ── std::sort (GCC libstdc++ introsort), iterative, on int index arrays ──
+// Comparators: 0 = key ascending, 1 = key descending (float keys),
+// 2 = unsigned key descending.
+struct SortKeys {
+    const float* f;
+    const uint32_t* u;
+    int mode;
+    __device__ __forceinline__ bool lt(int a, int b) const {
+        if (mode == 0) return f[a] < f[b];
+        if (mode == 1) return f[a] > f[b];
+        return u[a] > u[b];
+    }
+};
+
+__device__ void ss_adjust_heap(int* f, int hole, int len, int val, const SortKeys& K) {
+    const int top = hole;
+    int child = hole;
+    while (child < (len - 1) / 2) {
+        child = 2 * (child + 1);
+        if (K.lt(f[child], f[child - 1])) child--;
+        f[hole] = f[child];
+        hole = child;
+    }
+    if ((len & 1) == 0 && child == (len - 2) / 2) {
+        child = 2 * (child + 1);
+        f[hole] = f[child - 1];
+        hole = child - 1;
+    }
+    int parent = (hole - 1) / 2;
+    while (hole > top && K.lt(f[parent], val)) {
+        f[hole] = f[parent];
+        hole = parent;
+        parent = (hole - 1) / 2;
+    }
+    f[hole] = val;
+}
+__device__ void ss_heapsort(int* f, int n, const SortKeys& K) {
+    if (n >= 2)
+        for (int parent = (n - 2) / 2;; --parent) {
+            ss_adjust_heap(f, parent, n, f[parent], K);
+            if (parent == 0) break;
+        }
+    for (int last = n; last > 1;) {
+        --last;
+        const int v = f[last];
+        f[last] = f[0];
+        ss_adjust_heap(f, 0, last, v, K);
+    }
+}
+__device__ __forceinline__ void ss_swap(int* a, int* b) { const int t = *a; *a = *b; *b = t; }
+__device__ void ss_linear_insert(int* p, const SortKeys& K) {
+    const int v = *p;
+    int* q = p - 1;
+    while (K.lt(v, *q)) { *p = *q; p = q; --q; }
+    *p = v;
+}
+__device__ void ss_insertion(int* f, int* l, const SortKeys& K) {
+    if (f == l) return;
+    for (int* i = f + 1; i != l; ++i) {
+        if (K.lt(*i, *f)) {
+            const int v = *i;
+            for (int* j = i; j != f; --j) *j = *(j - 1);
+            *f = v;
+        } else {
+            ss_linear_insert(i, K);
+        }
+    }
+}
+// Partitions of disjoint ranges do not interact, so the explicit stack may
+// visit them in any order and still give std::sort's permutation.
+__device__ void std_sort(int* a, int n, const SortKeys& K) {
+    if (n <= 1) return;
+    int lg = 0;
+    while ((1 << (lg + 1)) <= n) ++lg;
+    struct Frame { int* f; int* l; int depth; };
+    Frame st[64];
+    int sp = 0;
+    st[sp++] = {a, a + n, 2 * lg};
+    while (sp > 0) {
+        Frame fr = st[--sp];
+        int* f = fr.f;
+        int* l = fr.l;
+        int depth = fr.depth;
+        while (l - f > 16) {
+            if (depth == 0) { ss_heapsort(f, (int)(l - f), K); break; }
+            --depth;
+            int *x = f + 1, *y = f + (l - f) / 2, *z = l - 1;
+            if (K.lt(*x, *y)) {
+                if (K.lt(*y, *z)) ss_swap(f, y);
+                else if (K.lt(*x, *z)) ss_swap(f, z);
+                else ss_swap(f, x);
+            } else if (K.lt(*x, *z)) ss_swap(f, x);
+            else if (K.lt(*y, *z)) ss_swap(f, z);
+            else ss_swap(f, y);
+            int *lo = f + 1, *hi = l;
+            for (;;) {
+                while (K.lt(*lo, *f)) ++lo;
+                --hi;
+                while (K.lt(*f, *hi)) --hi;
+                if (!(lo < hi)) break;
+                ss_swap(lo, hi);
+                ++lo;
+            }
+            if (sp < 64) st[sp++] = {lo, l, depth};
+            l = lo;
+        }
+    }
+    if (n > 16) {
+        ss_insertion(a, a + 16, K);
+        for (int* i = a + 16; i != a + n; ++i) ss_linear_insert(i, K);
+    } else {
+        ss_insertion(a, a + n, K);
+    }
+}
+
+__device__ __forceinline__ int uleb_len(uint32_t v) { int n = 0; do { v >>= 7; ++n; } while (v); return n; }
+__device__ __forceinline__ int uleb_put(uint32_t v, uint8_t* p) {
+    int n = 0;
+    do { uint8_t b = v & 0x7Fu; v >>= 7; if (v) b |= 0x80u; p[n++] = b; } while (v);
+    return n;
+}
+__device__ __forceinline__ uint32_t uleb_get(const uint8_t* buf, int64_t& pos) {
+    uint32_t v = 0; int sh = 0;
+    for (;;) { const uint8_t b = buf[pos++]; v |= (uint32_t)(b & 0x7Fu) << sh; if (!(b & 0x80u)) break; sh += 7; }
+    return v;
+}
+__device__ __forceinline__ uint32_t tb(const uint4& t, int s) {
+    const uint32_t w = s < 8 ? (s < 4 ? t.x : t.y) : (s < 12 ? t.z : t.w);
+    return (w >> ((s & 3) * 8)) & 0xFFu;
+}
+__device__ __forceinline__ void set_tb(uint4& t, int s, uint32_t b) {
+    const uint32_t sh = (uint32_t)(s & 3) * 8u, m = ~(0xFFu << sh), v = (b & 0xFFu) << sh;
+    if (s < 4) t.x = (t.x & m) | v;
+    else if (s < 8) t.y = (t.y & m) | v;
+    else if (s < 12) t.z = (t.z & m) | v;
+    else t.w = (t.w & m) | v;
+}
+__device__ __forceinline__ int live_of(const uint4& t) {
+    int n = 0;
+    for (int s = 0; s < 16; ++s) n += tb(t, s) != 0;
+    return n;
+}
+__device__ __forceinline__ int64_t tlen(const uint4& t, uint8_t sp) {
+    const int n = live_of(t);
+    return sp ? 1 + (n + 1) / 2 + n : 16;
+}
+
+constexpr int kOK = 0, kENOMEM = 2, kEHEADROOM = 3;
+
+// Per-thread context: the layer state plus this thread's scratch.
+struct Ctx {
+    SynView V;
+    int64_t R, C, BR;
+    // scratch (per thread)
+    uint32_t* rc;   // row-op columns [M]
+    uint8_t* rv;    // row-op values  [M]
+    // block4 running totals (sequential mode only)
+    int64_t tot_idx, tot_tile;
+    bool seq;
+};
+
+// ── scattered rows ──
+__device__ int row_nnz(const Ctx& c, int64_t r) { return (int)(c.V.ee[r] - c.V.es[r]); }
+__device__ int decode_row(const Ctx& c, int64_t r, uint32_t* cols) {
+    const int n = row_nnz(c, r);
+    int64_t pos = c.V.bs[r];
+    uint32_t col = 0;
+    for (int k = 0; k < n; ++k) { col += uleb_get(c.V.idx, pos); cols[k] = col; }
+    return n;
+}
+// rewrite the live part of row r (the state delta_csr_row_remove_col /
+// _insert_col leave behind, delta_csr_memory.hpp:429-585)
+__device__ int row_write(Ctx& c, int64_t r, const uint32_t* cols, const uint8_t* vals, int n) {
+    int64_t nb = 0;
+    uint32_t prev = 0;
+    for (int i = 0; i < n; ++i) { nb += uleb_len(cols[i] - prev); prev = cols[i]; }
+    if (nb > c.V.bs[r + 1] - c.V.bs[r]) return kEHEADROOM;
+    if (n > c.V.es[r + 1] - c.V.es[r]) return kEHEADROOM;
+    int64_t bp = c.V.bs[r];
+    prev = 0;
+    for (int i = 0; i < n; ++i) { bp += uleb_put(cols[i] - prev, c.V.idx + bp); prev = cols[i]; }
+    c.V.be[r] = bp;
+    for (int i = 0; i < n; ++i) c.V.val[c.V.es[r] + i] = vals[i];
+    atomicAdd(c.V.nnz_delta, (unsigned long long)(long long)(n - row_nnz(c, r)));
+    c.V.ee[r] = c.V.es[r] + n;
+    return kOK;
+}
+__device__ bool insert_fits(const Ctx& c, int64_t r, const uint32_t* cols, int n, uint32_t col) {
+    int i = 0;
+    uint32_t prev = 0;
+    while (i < n && cols[i] < col) { prev = cols[i]; ++i; }
+    int64_t delta = uleb_len(col - prev);
+    if (i < n) delta += uleb_len(cols[i] - col) - uleb_len(cols[i] - prev);
+    const int64_t used = c.V.be[r] - c.V.bs[r];
+    if (delta > 0 && delta > (c.V.bs[r + 1] - c.V.bs[r]) - used) return false;
+    if (n >= c.V.es[r + 1] - c.V.es[r]) return false;
+    return true;
+}
+__device__ bool sc_remove_col(Ctx& c, int64_t r, uint32_t col) {
+    const int n = decode_row(c, r, c.rc);
+    int i = 0;
+    while (i < n && c.rc[i] != col) ++i;
+    if (i == n) return false;
+    for (int k = 0; k < n; ++k) c.rv[k] = c.V.val[c.V.es[r] + k];
+    for (int k = i; k + 1 < n; ++k) { c.rc[k] = c.rc[k + 1]; c.rv[k] = c.rv[k + 1]; }
+    row_write(c, r, c.rc, c.rv, n - 1);
+    return true;
+}
+// delta_csr_row_insert_col with ValueAccessor::set (deterministic codes)
+__device__ bool sc_insert_col(Ctx& c, int64_t r, uint32_t col, float w, float imp) {
+    const int n = decode_row(c, r, c.rc);
+    int i = 0;
+    while (i < n && c.rc[i] < col) ++i;
+    if (i < n && c.rc[i] == col) return false;
+    if (!insert_fits(c, r, c.rc, n, col)) return false;
+    for (int k = 0; k < n; ++k) c.rv[k] = c.V.val[c.V.es[r] + k];
+    for (int k = n; k > i; --k) { c.rc[k] = c.rc[k - 1]; c.rv[k] = c.rv[k - 1]; }
+    c.rc[i] = col;
+    c.rv[i] = (uint8_t)((fp4_encode(w) << 4) | fp4_encode(imp));
+    row_write(c, r, c.rc, c.rv, n + 1);
+    return true;
+}
+
+// ── block4 store (reference accounting, block4.hpp) ──
+__device__ int b4_find(const Ctx& c, int64_t br, int bc) {
+    const int nt = c.V.nt[br];
+    const int64_t base = c.V.b4_es[br];
+    for (int e = 0; e < nt; ++e) {
+        const int v = c.V.b4_bc[base + e];
+        if (v == bc) return e;
+        if (v > bc) break;
+    }
+    return -1;
+}
+__device__ int64_t b4_tile_used(const Ctx& c, int64_t br) {
+    int64_t u = 0;
+    const int64_t base = c.V.b4_es[br];
+    for (int e = 0; e < c.V.nt[br]; ++e) u += tlen(c.V.b4_tile[base + e], c.V.b4_sparse[base + e]);
+    return u;
+}
+__device__ int64_t b4_idx_used(const Ctx& c, int64_t br) {
+    int64_t u = 0;
+    uint32_t prev = 0;
+    const int64_t base = c.V.b4_es[br];
+    for (int e = 0; e < c.V.nt[br]; ++e) {
+        const uint32_t v = (uint32_t)c.V.b4_bc[base + e];
+        u += uleb_len(v - prev);
+        prev = v;
+    }
+    return u;
+}
+__device__ int64_t& A_idx(Ctx& c, int64_t br) { return c.V.alloc[br]; }
+__device__ int64_t& A_tile(Ctx& c, int64_t br) { return c.V.alloc[c.BR + br]; }
+__device__ int64_t& A_elem(Ctx& c, int64_t br) { return c.V.alloc[2 * c.BR + br]; }
+
+// block4_row_shift (block4.hpp:497-609) / block4_grow_last_row (:611-646)
+__device__ int b4_ensure_headroom(Ctx& c, int64_t br) {
+    int64_t ti = A_idx(c, br) + 5, tt = A_tile(c, br) + 1, te = A_elem(c, br) + 1;
+    if (br + 1 < c.BR) {
+        ti = max(ti, b4_idx_used(c, br));
+        tt = max(tt, b4_tile_used(c, br));
+        te = max(te, (int64_t)c.V.nt[br]);
+        if (A_idx(c, br) != ti) {
+            if (c.seq && ti > A_idx(c, br) && c.tot_idx + (ti - A_idx(c, br)) > c.V.max_idx) return kENOMEM;
+            c.tot_idx += ti - A_idx(c, br);
+            atomicAdd(c.V.grow, (unsigned long long)(ti - A_idx(c, br)));
+            A_idx(c, br) = ti;
+        }
+        if (A_tile(c, br) != tt) {
+            if (c.seq && tt > A_tile(c, br) && c.tot_tile + (tt - A_tile(c, br)) > c.V.max_tile) return kENOMEM;
+            c.tot_tile += tt - A_tile(c, br);
+            atomicAdd(c.V.grow + 1, (unsigned long long)(tt - A_tile(c, br)));
+            A_tile(c, br) = tt;
+        }
+        A_elem(c, br) = te;
+    } else {
+        if (ti > A_idx(c, br)) {
+            if (c.seq && c.tot_idx + (ti - A_idx(c, br)) > c.V.max_idx) return kENOMEM;
+            c.tot_idx += ti - A_idx(c, br);
+            atomicAdd(c.V.grow, (unsigned long long)(ti - A_idx(c, br)));
+            A_idx(c, br) = ti;
+        }
+        if (tt > A_tile(c, br)) {
+            if (c.seq && c.tot_tile + (tt - A_tile(c, br)) > c.V.max_tile) return kENOMEM;
+            c.tot_tile += tt - A_tile(c, br);
+            atomicAdd(c.V.grow + 1, (unsigned long long)(tt - A_tile(c, br)));
+            A_tile(c, br) = tt;
+        }
+        if (te > A_elem(c, br)) A_elem(c, br) = te;
+    }
+    return kOK;
+}
+// block4_row_insert_tile (block4.hpp:670-771): an empty sparse tile
+__device__ bool b4_insert_tile(Ctx& c, int64_t br, int bc) {
+    const int nt = c.V.nt[br];
+    const int64_t base = c.V.b4_es[br];
+    int p = 0;
+    while (p < nt && c.V.b4_bc[base + p] < bc) ++p;
+    if (p < nt && c.V.b4_bc[base + p] == bc) return false;
+    const uint32_t prev = p > 0 ? (uint32_t)c.V.b4_bc[base + p - 1] : 0u;
+    int64_t delta = uleb_len((uint32_t)bc - prev);
+    if (p < nt) {
+        const uint32_t nx = (uint32_t)c.V.b4_bc[base + p];
+        delta += uleb_len(nx - (uint32_t)bc) - uleb_len(nx - prev);
+    }
+    if (delta > 0 && delta > A_idx(c, br) - b4_idx_used(c, br)) return false;
+    if (nt >= A_elem(c, br)) return false;
+    if (1 > A_tile(c, br) - b4_tile_used(c, br)) return false;
+    if (base + nt + 1 > c.V.b4_es[br + 1]) { atomicOr(c.V.flags, 4); return false; }   // device capacity
+    for (int e = nt; e > p; --e) {
+        c.V.b4_bc[base + e] = c.V.b4_bc[base + e - 1];
+        c.V.b4_tile[base + e] = c.V.b4_tile[base + e - 1];
+        c.V.b4_sparse[base + e] = c.V.b4_sparse[base + e - 1];
+    }
+    c.V.b4_bc[base + p] = bc;
+    c.V.b4_tile[base + p] = make_uint4(0, 0, 0, 0);
+    c.V.b4_sparse[base + p] = 1;
+    c.V.nt[br] = nt + 1;
+    return true;
+}
+// commit_dirty_sparse_tile (block4.hpp:1223-1268)
+__device__ void b4_commit(Ctx& c, int64_t br, int e, const uint4& t) {
+    const int64_t ti = c.V.b4_es[br] + e;
+    const int n = live_of(t);
+    const bool sp = (uint32_t)n <= c.V.switch_point;
+    const int64_t nl = sp ? 1 + (n + 1) / 2 + n : 16;
+    const int64_t cl = tlen(c.V.b4_tile[ti], c.V.b4_sparse[ti]);
+    if (nl > cl) {
+        const int64_t head = A_tile(c, br) - b4_tile_used(c, br);
+        if (nl - cl > head) {
+            const int64_t sf = nl - cl - head;
+            if (c.seq && c.tot_tile + sf > c.V.max_tile) { atomicAdd(c.V.counters, 1ull); return; }
+            c.tot_tile += sf;
+            atomicAdd(c.V.grow + 1, (unsigned long long)sf);
+            A_tile(c, br) += sf;
+        }
+    }
+    c.V.b4_tile[ti] = t;
+    c.V.b4_sparse[ti] = sp ? 1 : 0;
+}
+__device__ void b4_write(Ctx& c, int64_t br, int e, const uint4& t) {
+    const int64_t ti = c.V.b4_es[br] + e;
+    if (c.V.b4_sparse[ti]) b4_commit(c, br, e, t);
+    else c.V.b4_tile[ti] = t;
+}
+__device__ void b4_maybe_compress(Ctx& c, int64_t br, int e) {
+    const int64_t ti = c.V.b4_es[br] + e;
+    if (c.V.b4_sparse[ti] || (uint32_t)live_of(c.V.b4_tile[ti]) > c.V.switch_point) return;
+    c.V.b4_sparse[ti] = 1;
+}
+__device__ void b4_erase(Ctx& c, int64_t br, int bc) {
+    const int e = b4_find(c, br, bc);
+    if (e < 0) return;
+    const int nt = c.V.nt[br];
+    const int64_t base = c.V.b4_es[br];
+    for (int k = e; k + 1 < nt; ++k) {
+        c.V.b4_bc[base + k] = c.V.b4_bc[base + k + 1];
+        c.V.b4_tile[base + k] = c.V.b4_tile[base + k + 1];
+        c.V.b4_sparse[base + k] = c.V.b4_sparse[base + k + 1];
+    }
+    c.V.nt[br] = nt - 1;
+}
+// block4_demote_tile (delta_csr_memory.hpp:946-1003)
+__device__ int b4_demote(Ctx& c, int64_t br, int bc) {
+    const int e = b4_find(c, br, bc);
+    if (e < 0) return kOK;
+    const uint4 t = c.V.b4_tile[c.V.b4_es[br] + e];
+    for (int li = 0; li < 4; ++li) {
+        const int64_t row = br * 4 + li;
+        if (row >= c.R) continue;
+        for (int lj = 0; lj < 4; ++lj) {
+            const uint32_t byte = tb(t, lj * 4 + li);
+            if (byte == 0) continue;
+            const int64_t col = (int64_t)bc * 4 + lj;
+            if (col >= c.C) continue;
+            if (!sc_insert_col(c, row, (uint32_t)col, fp4_decode(byte & 0xFu), fp4_decode(byte >> 4))) return kEHEADROOM;
+        }
+    }
+    b4_erase(c, br, bc);
+    return kOK;
+}
+// block4_maybe_promote (delta_csr_memory.hpp:593-702)
+__device__ int b4_maybe_promote(Ctx& c, int64_t row, uint32_t col) {
+    const int64_t br = row / 4;
+    const int bc = (int)(col / 4), li = (int)(row % 4), lj = (int)(col % 4);
+    int e = b4_find(c, br, bc);
+    if (e >= 0) {
+        const int n = decode_row(c, row, c.rc);
+        int k = 0;
+        while (k < n && c.rc[k] != col) ++k;
+        if (k == n) return kOK;
+        const uint8_t v = c.V.val[c.V.es[row] + k];
+        uint4 t = c.V.b4_tile[c.V.b4_es[br] + e];
+        set_tb(t, lj * 4 + li, fp4_encode(fp4_decode(v >> 4)) | (fp4_encode(fp4_decode(v & 0xFu)) << 4));
+        b4_write(c, br, e, t);
+        b4_maybe_compress(c, br, e);
+        sc_remove_col(c, row, col);
+        return kOK;
+    }
+    const int64_t row_lo = br * 4, row_hi = min(row_lo + 4, c.R);
+    const int64_t col_lo = (int64_t)bc * 4, col_hi = min(col_lo + 4, c.C);
+    int fr[16], fcol[16];
+    uint8_t fv[16];
+    int nf = 0;
+    for (int64_t r = row_lo; r < row_hi; ++r) {
+        const int n = decode_row(c, r, c.rc);
+        for (int k = 0; k < n; ++k)
+            if ((int64_t)c.rc[k] >= col_lo && (int64_t)c.rc[k] < col_hi && nf < 16) {
+                fr[nf] = (int)r; fcol[nf] = (int)c.rc[k]; fv[nf] = c.V.val[c.V.es[r] + k]; ++nf;
+            }
+    }
+    if (nf < 2) return kOK;
+    // Block4Store::get_or_create (block4.hpp:1168-1184)
+    if (!b4_insert_tile(c, br, bc)) {
+        if (*c.V.flags & 4) return kOK;
+        const int rc = b4_ensure_headroom(c, br);
+        if (rc) return rc;
+        b4_insert_tile(c, br, bc);
+        if (*c.V.flags & 4) return kOK;
+    }
+    e = b4_find(c, br, bc);
+    uint4 t = c.V.b4_tile[c.V.b4_es[br] + e];
+    for (int f = 0; f < nf; ++f)
+        set_tb(t, (fcol[f] - (int)col_lo) * 4 + (fr[f] - (int)row_lo),
+               fp4_encode(fp4_decode(fv[f] >> 4)) | (fp4_encode(fp4_decode(fv[f] & 0xFu)) << 4));
+    b4_write(c, br, e, t);
+    b4_maybe_compress(c, br, e);
+    for (int f = 0; f < nf; ++f) sc_remove_col(c, fr[f], (uint32_t)fcol[f]);
+    return kOK;
+}
+
+// out_degree decrement with the reference's clamp (if > 0)
+__device__ void od_dec(Ctx& c, uint32_t col) {
+    atomicAdd(c.V.od_decs + col, 1);
+    int cur = c.V.out_degree[col];
+    while (cur > 0) {
+        const int prev = atomicCAS(c.V.out_degree + col, cur, cur - 1);
+        if (prev == cur) break;
+        cur = prev;
+    }
+}
+
+// delta_csr_synap_row_step for one row (oracle: o_synap_row_step)
+__device__ int synap_row(Ctx& c, int64_t r, const SynParams& P, uint32_t* ecol, float* eimp, uint8_t* eb4, int* by,
+                         uint32_t* pcs, float* pss, int* pidx, uint32_t* rmc, uint8_t* rmb, int* rperm, uint32_t* addc,
+                         float* adds, bool* did) {
+    *did = false;
+    const int n_sc = row_nnz(c, r);
+    const bool has_probes = c.V.n_probes > 0;
+    const int64_t br = r / 4;
+    const int li = (int)(r % 4);
+    const int nt = c.V.nt[br];
+    decode_row(c, r, ecol);
+    for (int k = 0; k < n_sc; ++k) { eimp[k] = fp4_decode(c.V.val[c.V.es[r] + k] & 0xFu); eb4[k] = 0; }
+    int n_exist = n_sc;
+    const int64_t base = c.V.b4_es[br];
+    for (int e = 0; e < nt; ++e) {
+        const uint4 t = c.V.b4_tile[base + e];
+        const int64_t c0 = (int64_t)c.V.b4_bc[base + e] * 4;
+        for (int lj = 0; lj < 4; ++lj) {
+            const uint32_t byte = tb(t, lj * 4 + li);
+            if (byte == 0 || c0 + lj >= c.C) continue;
+            ecol[n_exist] = (uint32_t)(c0 + lj);
+            eimp[n_exist] = fp4_decode(byte >> 4);
+            eb4[n_exist] = 1;
+            ++n_exist;
+        }
+    }
+    if (n_exist == 0 && !has_probes) return kOK;
+    // probes of this row, COO order
+    int np = 0;
+    for (int q = c.V.pr_ptr[r]; q < c.V.pr_ptr[r + 1]; ++q) {
+        const int p = c.V.pr_idx[q];
+        pcs[np] = (uint32_t)c.V.pcol[p];
+        pss[np] = c.V.pval[p];
+        ++np;
+    }
+    // removals by stored importance ascending (:1147-1167)
+    for (int i = 0; i < n_exist; ++i) by[i] = i;
+    std_sort(by, n_exist, SortKeys{eimp, nullptr, 0});
+    int nrm = 0;
+    for (int a = 0; a < n_exist && nrm < P.max_prune; ++a) {
+        const int k = by[a];
+        const int keep = n_exist - nrm;
+        const float fl = (eimp[k] < P.eps) ? P.eps : eimp[k];
+        if (fl < P.cutoff || keep > P.max_rw) { rmc[nrm] = ecol[k]; rmb[nrm] = eb4[k]; ++nrm; }
+    }
+    for (int i = 0; i < nrm; ++i) rperm[i] = i;
+    std_sort(rperm, nrm, SortKeys{nullptr, rmc, 2});
+    // adds by score descending (:1171-1201)
+    for (int i = 0; i < np; ++i) pidx[i] = i;
+    std_sort(pidx, np, SortKeys{pss, nullptr, 1});
+    const unsigned long long slots = (unsigned long long)((long long)P.max_rw - (long long)(n_exist - nrm));
+    int nadd = 0;
+    for (int a = 0; a < np; ++a) {
+        if ((unsigned long long)nadd >= slots) break;
+        const uint32_t col = pcs[pidx[a]];
+        bool exists = false;
+        for (int i = 0; i < n_exist; ++i) if (ecol[i] == col) { exists = true; break; }
+        if (!exists) { addc[nadd] = col; adds[nadd] = pss[pidx[a]]; ++nadd; }
+    }
+    // removals, highest column first (:1203-1233)
+    for (int q = 0; q < nrm; ++q) {
+        const uint32_t col = rmc[rperm[q]];
+        if (rmb[rperm[q]]) {
+            const int bc = (int)(col / 4), lj = (int)(col % 4);
+            const int e = b4_find(c, br, bc);
+            bool demote = false;
+            if (e >= 0) {
+                uint4 t = c.V.b4_tile[base + e];
+                if (tb(t, lj * 4 + li) != 0) {
+                    set_tb(t, lj * 4 + li, 0u);
+                    demote = live_of(t) < 2;
+                    b4_write(c, br, e, t);
+                }
+            }
+            if (demote) {
+                const int rc = b4_demote(c, br, bc);
+                if (rc) return rc;
+            }
+        } else {
+            sc_remove_col(c, r, col);
+        }
+        od_dec(c, col);
+    }
+    // inserts in score order, each followed by the block4 promotion (:1235-1255)
+    for (int a = 0; a < nadd; ++a) {
+        if (!sc_insert_col(c, r, addc[a], 0.0f, adds[a])) return kEHEADROOM;
+        atomicAdd(c.V.out_degree + addc[a], 1);
+        const int rc = b4_maybe_promote(c, r, addc[a]);
+        if (rc) return rc;
+        if (*c.V.flags & 4) return kOK;
+    }
+    *did = true;
+    return kOK;
+}
+
+}  // namespace
+
+// One thread per block-row (or one thread for the whole sweep when
+// sequential).  Sweep position i covers row (row0 + i) % R; rows at
+// positions > limit are left alone.
+__global__ void k_synap(SynView V, SynParams P, int sequential) {
+    const int64_t R = V.n_in, BR = (R + 3) / 4;
+    const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (sequential ? tid != 0 : tid >= BR) return;
+    Ctx c;
+    c.V = V;
+    c.R = R; c.C = V.n_out; c.BR = BR;
+    c.seq = sequential != 0;
+    c.tot_idx = V.tot_idx0; c.tot_tile = V.tot_tile0;
+    const int64_t M = V.scratch_m, PM = V.scratch_p;
+    uint8_t* sb = V.scratch + (size_t)(sequential ? 0 : tid) * (size_t)V.scratch_stride;
+    // carve the thread's scratch: row ops, exist lists, probe lists
+    auto take = [&](size_t bytes) { uint8_t* p = sb; sb += (bytes + 15) & ~(size_t)15; return p; };
+    c.rc = (uint32_t*)take((size_t)M * 4);
+    c.rv = take((size_t)M);
+    uint32_t* ecol = (uint32_t*)take((size_t)M * 4);
+    float* eimp = (float*)take((size_t)M * 4);
+    uint8_t* eb4 = take((size_t)M);
+    int* by = (int*)take((size_t)M * 4);
+    uint32_t* rmc = (uint32_t*)take((size_t)M * 4);
+    uint8_t* rmb = take((size_t)M);
+    int* rperm = (int*)take((size_t)M * 4);
+    uint32_t* pcs = (uint32_t*)take((size_t)PM * 4);
+    float* pss = (float*)take((size_t)PM * 4);
+    int* pidx = (int*)take((size_t)PM * 4);
+    uint32_t* addc = (uint32_t*)take((size_t)PM * 4);
+    float* adds = (float*)take((size_t)PM * 4);
+    if (R == 0) return;
+    const int64_t row0 = ((P.row0 % R) + R) % R;
+    if (sequential) {
+        for (int64_t i = 0; i < P.nrows && i <= P.limit; ++i) {
+            const int64_t r = (row0 + i) % R;
+            bool did = false;
+            const int rc = synap_row(c, r, P, ecol, eimp, eb4, by, pcs, pss, pidx, rmc, rmb, rperm, addc, adds, &did);
+            if (V.did) V.did[i] = did ? 1 : 0;
+            if (rc || (*V.flags & 4)) {
+                if (rc) { atomicMin(V.err_i, (long long)i); atomicMax(V.err_code, rc); }
+                return;
+            }
+        }
+        return;
+    }
+    // rows of block-row tid in sweep order: positions i = (4*tid + li - row0) mod R + k*R
+    const int64_t br = tid;
+    int64_t next[4];
+    for (int li = 0; li < 4; ++li) {
+        const int64_t r = br * 4 + li;
+        next[li] = r < R ? ((r - row0) % R + R) % R : INT64_MAX;
+    }
+    for (;;) {
+        int best = -1;
+        for (int li = 0; li < 4; ++li)
+            if (next[li] < P.nrows && next[li] <= P.limit && (best < 0 || next[li] < next[best])) best = li;
+        if (best < 0) break;
+        const int64_t i = next[best];
+        next[best] += R;
+        bool did = false;
+        const int rc = synap_row(c, br * 4 + best, P, ecol, eimp, eb4, by, pcs, pss, pidx, rmc, rmb, rperm, addc,
+                                 adds, &did);
+        if (V.did) V.did[i] = did ? 1 : 0;
+        if (rc) { atomicMin(V.err_i, (long long)i); atomicMax(V.err_code, rc); return; }
+        if (*V.flags & 4) return;
+    }
+}
+
+void launch_synap(const SynView& V, const SynParams& P, bool sequential, cudaStream_t s) {
+    const int64_t BR = (V.n_in + 3) / 4;
+    if (sequential) {
+        k_synap<<<1, 1, 0, s>>>(V, P, 1);
+    } else {
+        k_synap<<<(unsigned)((BR + 63) / 64), 64, 0, s>>>(V, P, 0);
+    }
+    count_launch();
+}
+
+// ptr[k] = first position of key k in sorted_keys (k = 0..nkeys)
+__global__ void k_lower_bound(const int* __restrict__ keys, int n, int64_t nkeys, int* __restrict__ ptr) {
+    const int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (k > nkeys) return;
+    int lo = 0, hi = n;
+    while (lo < hi) { const int mid = (lo + hi) >> 1; if (keys[mid] < (int)k) lo = mid + 1; else hi = mid; }
+    ptr[k] = lo;
+}
+void launch_lower_bound(const int* sorted_keys, int n, int64_t nkeys, int* ptr, cudaStream_t s) {
+    k_lower_bound<<<(unsigned)((nkeys + 256) / 256), 256, 0, s>>>(sorted_keys, n, nkeys, ptr);
+    count_launch();
+}
+
+// out_degree clamp check: a column whose decrements exceed its starting count
+// could have been clamped in an order-dependent way
+__global__ void k_od_check(const int* __restrict__ od0, const int* __restrict__ decs, int64_t n, int* __restrict__ flags) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n && decs[i] > od0[i]) atomicOr(flags, 1);
+}
+void launch_od_check(const int* od0, const int* decs, int64_t n, int* flags, cudaStream_t s) {
+    if (n == 0) return;
+    k_od_check<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(od0, decs, n, flags);
+    count_launch();
+}
+
+}  // namespace sili
