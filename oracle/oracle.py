@@ -119,6 +119,7 @@ def lib():
             ("o_b4_rows", None, [_P, _P]),
             ("o_b4_view", None, [_P, _P]),
             ("o_std_sort_keys", None, [_P, _I64, _I, _P]),
+            ("o_set_ref_stream", None, [_P, _I, C.c_uint64]),
         ]:
             f = getattr(_lib, name)
             f.restype = res
@@ -454,6 +455,10 @@ class OracleLayer(_LayerBase):
             raise MemoryError("compact_block4: budget exceeded")
 
     def set_switch_point(self, v): self.L.o_b4_set_switch_point(self.h, v)
+
+    def use_reference_stream(self, seed):
+        """Sparse-gradient block4 draws from the reference's xorshift64* stream."""
+        self.L.o_set_ref_stream(self.h, 1, seed)
 
     def b4_tiles(self):
         n = int(self.L.o_b4_ntiles(self.h))

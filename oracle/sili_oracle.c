@@ -61,6 +61,10 @@ struct OLayer {
     int64_t b4_max_idx, b4_max_tile;
     uint32_t b4_switch;
     uint64_t b4_dropped, b4_ovf_events, b4_ovf_bytes;
+    /* stochastic draws of the sparse-gradient block4 update: 0 = counter
+     * draws (o_rng_draw, the CUDA path's), 1 = the reference's xorshift64*
+     * stream (fp4quant.hpp:170-190) for pinning against its build */
+    int ref_stream; uint64_t ref_state;
 };
 
 #define NO_LIMIT INT64_MAX
@@ -588,11 +592,15 @@ void o_backward_dense(OLayer* L, const float* x, const float* dy, int batch, flo
 }
 
 /* ── sisldo_forward, sisldo_ops.hpp:198-340 (scattered part, num_cpus = 1) ─ */
+static void b4_forward_sparse(const OLayer* L, const int* ptrs, const int* idx, const float* vals, int batch,
+                              float* y);
+static void b4_backward_sparse(OLayer* L, const float* x, const int* dptrs, const int* didx, const float* dvals,
+                               int batch, float lr, int lr_per_row_nnz, int damp, float beta2, float eps, float* dx,
+                               uint64_t call);
 void o_forward_sparse(OLayer* L, const int* ptrs, const int* idx, const float* vals, int batch, float* y) {
     const int64_t n_out = L->cols;
     memset(y, 0, (size_t)batch * n_out * sizeof(float));
-    if (L->total_nnz == 0) return;
-    for (int b = 0; b < batch; ++b) {
+    if (L->total_nnz > 0) for (int b = 0; b < batch; ++b) {
         for (int i = ptrs[b]; i < ptrs[b + 1]; ++i) {
             const int r = idx[i];
             const float iv = vals[i];
@@ -608,6 +616,7 @@ void o_forward_sparse(OLayer* L, const int* ptrs, const int* idx, const float* v
             }
         }
     }
+    b4_forward_sparse(L, ptrs, idx, vals, batch, y);
 }
 
 /* ── disldo_backward_sparse_grad, sisldo_ops.hpp:589-799 (scattered, num_cpus = 1) */
@@ -621,8 +630,11 @@ void o_backward_sparse(OLayer* L, const float* x, const int* dptrs, const int* d
     if (L->value_scale.n < n_in) fvec_resize(&L->value_scale, n_in, 1.0f);
     if (L->value_scale_importance.n < n_in) fvec_resize(&L->value_scale_importance, n_in, 0.0f);
     memset(dx, 0, (size_t)batch * n_in * sizeof(float));
-    L->call++;
-    if (L->total_nnz == 0) return;
+    const uint64_t call = L->call++;
+    if (L->total_nnz == 0) {
+        b4_backward_sparse(L, x, dptrs, didx, dvals, batch, lr, lr_per_row_nnz, damp, beta2, eps, dx, call);
+        return;
+    }
     double* sgs = (double*)calloc((size_t)n_in + 1, sizeof(double));
     double* sgc = (double*)calloc((size_t)n_in + 1, sizeof(double));
     double sa_new = 0, sa_old = 0, sq_new = 0, sq_old = 0; float mx_new = 0.0f;
@@ -691,6 +703,7 @@ void o_backward_sparse(OLayer* L, const float* x, const int* dptrs, const int* d
         }
     }
     free(sgs); free(sgc);
+    b4_backward_sparse(L, x, dptrs, didx, dvals, batch, lr, lr_per_row_nnz, damp, beta2, eps, dx, call);
 }
 
 /* ── synaptogenesis candidates, delta_csr_memory.hpp:1308-1427 ──────────── */
@@ -2049,4 +2062,187 @@ int o_synap_row_step(OLayer* L, int row_in, float cutoff, int max_rw, int max_pr
     free(rperm); free(pidx); free(add_c); free(add_s);
     if (rc == O_OK) *did = 1;
     return rc;
+}
+
+/* ── sisldo_forward block4 windows, sisldo_ops.hpp:379-549 (num_cpus = 1) ──
+ * Per sample, each run of input indices inside one block-row forms a window
+ * of 4 input values; every tile of that block-row adds, per column, the sum
+ * over its live slots of (w * value_scale(row) * output_scale(col)) * x. */
+static void b4_forward_sparse(const OLayer* L, const int* ptrs, const int* idx, const float* vals, int batch,
+                              float* y) {
+    const int64_t n_in = L->rows, n_out = L->cols;
+    if (o_b4_ntiles(L) == 0) return;
+    float* mo = (float*)calloc((size_t)batch * n_out + 1, sizeof(float));
+    for (int b = 0; b < batch; ++b) {
+        int i = ptrs[b];
+        while (i < ptrs[b + 1]) {
+            const int64_t br = idx[i] / 4, lo = br * 4, hi = lo + 4;
+            float local[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            int j = i;
+            while (j < ptrs[b + 1] && idx[j] < hi) { local[idx[j] - lo] = vals[j]; ++j; }
+            if (br < L->b4_rows && L->b4[br].n > 0) {
+                for (int64_t e = 0; e < L->b4[br].n; ++e) {
+                    const OTile* t = &L->b4[br].t[e];
+                    for (int lj = 0; lj < 4; ++lj) {
+                        const int64_t col = (int64_t)t->bc * 4 + lj;
+                        if (col >= n_out) continue;
+                        const float os = o_get_output_scale_k(L, (int)col, 0);
+                        float acc = 0.0f;
+                        for (int li = 0; li < 4; ++li) {
+                            const int64_t row = br * 4 + li;
+                            if (row >= n_in) continue;
+                            const uint8_t byte = t->s[B4_SLOT(li, lj)];
+                            if (byte == 0) continue;
+                            /* acc += w * value_scale * out_scale * x as the reference's build
+                             * evaluates it: fma(os*vs, x*w, acc) */
+                            const float vsr = o_get_value_scale_k(L, (int)row, 0);
+                            acc = fmaf(os * vsr, local[li] * o_fp4_decode(byte & 0xF), acc);
+                        }
+                        mo[(int64_t)b * n_out + col] += acc;
+                    }
+                }
+            }
+            i = j;
+        }
+    }
+    for (int64_t q = 0; q < (int64_t)batch * n_out; ++q) y[q] += mo[q];
+    free(mo);
+}
+
+/* ── disldo_backward_sparse_grad block4 part, sisldo_ops.hpp:835-1104 ─────
+ * Per sample, per block-row: every tile whose 4-column window holds gradient
+ * entries takes them; dx adds w*dy over the window; at lr != 0 each touched
+ * slot gets the plain RMSprop step (no clip) and a stochastic requantize,
+ * then the row's workspace merge evicts down to its allocation.  After all
+ * samples: importance statistics and the rank-1 value_scale step. */
+void o_set_ref_stream(OLayer* L, int on, uint64_t seed) {
+    L->ref_stream = on;
+    L->ref_state = (seed ^ 0x9E3779B97F4A7C15ULL) | 1ULL;
+}
+static uint8_t b4_qstoch(OLayer* L, float v, uint64_t call, uint64_t el, uint32_t lane) {
+    if (L->ref_stream) {
+        const uint32_t a = f2u(v) & 0x7FFFFFFFu;
+        const uint64_t r = (a > 0x7F800000u || a >= 0x40C00000u) ? 0 : o_xorshift_next(&L->ref_state);
+        return o_fp4_quantize_stochastic_r(v, r);
+    }
+    return o_fp4_quantize_stochastic_r(v, o_rng_draw(L->seed, call, el, lane));
+}
+static void b4_backward_sparse(OLayer* L, const float* x, const int* dptrs, const int* didx, const float* dvals,
+                               int batch, float lr, int lr_per_row_nnz, int damp, float beta2, float eps, float* dx,
+                               uint64_t call) {
+    const int64_t n_in = L->rows, n_out = L->cols;
+    if (o_b4_ntiles(L) == 0) return;
+    double* rs = (double*)calloc((size_t)n_in + 1, sizeof(double));
+    double* rc = (double*)calloc((size_t)n_in + 1, sizeof(double));
+    double t_an = 0, t_ao = 0, t_sn = 0, t_so = 0; float t_mx = 0.0f;
+    for (int b = 0; b < batch; ++b) {
+        const int og0 = dptrs[b], og1 = dptrs[b + 1];
+        double an = 0, ao = 0, sn = 0, so = 0; float mx = 0.0f;
+        for (int64_t br = 0; br < L->b4_rows; ++br) {
+            struct OTileRow* R = &L->b4[br];
+            const int64_t nt = R->n;
+            if (nt == 0) continue;
+            const int64_t nnz_row = nt * 4;
+            float dxa[4] = {0, 0, 0, 0};
+            double rgl[4] = {0, 0, 0, 0}, rglc[4] = {0, 0, 0, 0};
+            OTile* ws = (OTile*)malloc((size_t)nt * sizeof(OTile));
+            memcpy(ws, R->t, (size_t)nt * sizeof(OTile));
+            int og = og0;
+            for (int64_t e = 0; e < nt; ++e) {
+                const int64_t lo = (int64_t)ws[e].bc * 4, hi = lo + 4;
+                while (og < og1 && didx[og] < lo) ++og;
+                float dyl[4] = {0, 0, 0, 0};
+                int any = 0;
+                for (int p = og; p < og1 && didx[p] < hi; ++p) { dyl[didx[p] - lo] = dvals[p]; any = 1; }
+                if (!any) continue;
+                uint8_t* td = ws[e].s;
+                int dirty = 0;
+                for (int li = 0; li < 4; ++li) {
+                    const int64_t row = br * 4 + li;
+                    if (row >= n_in) continue;
+                    const float in_val = x[(int64_t)b * n_in + row];
+                    const float vs = o_get_value_scale_k(L, (int)row, 0);
+                    const float imp_scale = o_get_importance_scale(L, (int)row);
+                    const float eff_lr = lr_per_row_nnz ? lr / (float)nnz_row : lr;
+                    for (int lj = 0; lj < 4; ++lj) {
+                        if (dyl[lj] == 0.0f) continue;
+                        const int64_t col = lo + lj;
+                        if (col >= n_out) continue;
+                        const uint8_t byte = td[B4_SLOT(li, lj)];
+                        const float wd = o_fp4_decode(byte & 0xF);
+                        const float os = o_get_output_scale_k(L, (int)col, 0);
+                        const float cs = vs * os;
+                        const float w = wd * cs;
+                        const float dyv = dyl[lj];
+                        if (lr == 0.0f) {
+                            /* w*dy with w = w_dec*vs*os, as the reference's build
+                             * evaluates it at lr = 0: fma(os*vs, dy*w_dec, acc) */
+                            dxa[li] = fmaf(os * vs, dyv * wd, dxa[li]);
+                            continue;
+                        }
+                        dxa[li] = fmaf(w, dyv, dxa[li]);
+                        const float cis = imp_scale * o_get_output_importance_scale(L, (int)col);
+                        const float imp_dec = o_fp4_decode((uint8_t)(byte >> 4));
+                        const float grad = dyv * in_val;
+                        float imp = imp_dec * cis;
+                        const float contrib = in_val * w;
+                        imp = fmaf(beta2, imp, (1.0f - beta2) * fmaf(grad, grad, contrib * contrib));
+                        const float step = damp ? (-eff_lr * grad) / (sqrtf(imp) + eps) : (-eff_lr * grad);
+                        const float new_w = w + step;
+                        /* counter key: bit 61 | (sample, row, col) -- a slot can be
+                         * updated once per sample within one call */
+                        const uint64_t el = (1ULL << 61) |
+                                            (((uint64_t)b * (uint64_t)n_in + (uint64_t)row) * (uint64_t)n_out + (uint64_t)col);
+                        const uint8_t wq = b4_qstoch(L, new_w / cs, call, el, 0);
+                        const uint8_t iq = b4_qstoch(L, imp / cis, call, el, 1);
+                        td[B4_SLOT(li, lj)] = (uint8_t)((iq << 4) | wq);
+                        dirty = 1;
+                        const float actual = o_fp4_decode(iq) * cis, stored = imp_dec * cis;
+                        an += fabs((double)actual); ao += fabs((double)stored);
+                        sn += (double)actual * actual; so += (double)stored * stored;
+                        if (fabsf(actual) > mx) mx = fabsf(actual);
+                        rgl[li] += (double)wd * (double)os * (double)(dyv * in_val);
+                        rglc[li] += (double)wd * (double)os * (double)contrib;
+                    }
+                }
+                if (dirty) ws[e].sparse = (uint32_t)b4_live(td) <= L->b4_switch;
+            }
+            if (lr != 0.0f) {
+                b4_true_importance_evict(L, br, ws, nt);
+                memcpy(R->t, ws, (size_t)nt * sizeof(OTile));
+            }
+            free(ws);
+            for (int li = 0; li < 4; ++li) {
+                const int64_t row = br * 4 + li;
+                if (row >= n_in) continue;
+                dx[(int64_t)b * n_in + row] += dxa[li];
+                if (lr != 0.0f) { rs[row] += rgl[li]; rc[row] += rglc[li]; }
+            }
+        }
+        t_an += an; t_ao += ao; t_sn += sn; t_so += so;
+        if (mx > t_mx) t_mx = mx;
+    }
+    if (lr != 0.0f) {
+        L->importance_l1 += t_an - t_ao;
+        L->importance_l2_sq += t_sn - t_so;
+        L->importance_max_abs = fmaxf(L->importance_max_abs * L->max_abs_decay, t_mx);
+        if (L->value_scale_step.n < n_in * L->rank) uvec_resize(&L->value_scale_step, n_in * L->rank, 0u);
+        for (int64_t r = 0; r < n_in; ++r) {
+            if (rs[r] == 0.0 && rc[r] == 0.0) continue;
+            const int64_t br = r / 4;
+            const int64_t nnz_row = (br < L->b4_rows ? L->b4[br].n : 0) * 4;
+            if (nnz_row == 0) continue;
+            const float se = lr / (float)nnz_row;
+            const float g = (float)rs[r], cg = (float)rc[r];
+            float* vsi = &L->value_scale_importance.d[r];
+            const float nv = fmaf(beta2, *vsi, (1.0f - beta2) * fmaf(g, g, cg * cg));
+            uint32_t* st = &L->value_scale_step.d[r * L->rank];
+            ++(*st);
+            const float bcor = 1.0f - powf(beta2, (float)(*st));
+            const float hat = bcor > 0.0f ? nv / bcor : nv;
+            *vsi = nv;
+            L->value_scale.d[r] -= se * g / (sqrtf(hat) + eps);
+        }
+    }
+    free(rs); free(rc);
 }

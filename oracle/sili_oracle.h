@@ -99,6 +99,8 @@ int     o_load_dense_codes(OLayer* L, const uint8_t* weight_codes, const uint8_t
 int     o_b4_expand_headroom(OLayer* L, float blank_fraction, int64_t min_slack);
 int     o_b4_equalize_step(OLayer* L, int64_t row);
 void    o_b4_set_switch_point(OLayer* L, uint32_t v);
+/* sparse-gradient block4 draws from the reference's xorshift64* stream (pinning) */
+void    o_set_ref_stream(OLayer* L, int on, uint64_t seed);
 int64_t o_b4_ntiles(const OLayer* L);
 void    o_b4_export(const OLayer* L, int* br, int* bc, uint8_t* slots, uint8_t* sparse);
 void    o_b4_rows(const OLayer* L, int64_t* out);   /* 6 per block-row */

@@ -233,6 +233,72 @@ void launch_b4_dx(const LayerView& L, const B4View& V, const float* dyT, int B, 
     count_launch();
 }
 
+// Block4Store::merge_row_workspace (block4.hpp:1368-1465) for one block-row,
+// run by its half-warp: while the packed bytes exceed the row's tile
+// allocation, zero the live slot of smallest |importance * importance_scale *
+// output_importance_scale| (first in tile, li, lj order on ties) and repack
+// that tile; then count tiles that still do not fit.
+__device__ void b4_evict_row(const LayerView& L, const B4View& V, int64_t br, int64_t base, int nt, int s,
+                             unsigned hmask) {
+    const int64_t cap = V.alloc[V.BR + br];
+    long long used = 0;
+    for (int e = s; e < nt; e += 16) used += tile_len(tile_live(V.tile[base + e]), V.sparse[base + e] != 0);
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) used += __shfl_xor_sync(hmask, used, o);
+    while (used > cap) {
+        double best = -1.0;
+        long long best_key = -1;
+        for (int e = s; e < nt; e += 16) {
+            const uint4 tw = V.tile[base + e];
+            const int64_t c0 = (int64_t)V.bc[base + e] * 4;
+            for (int l_i = 0; l_i < 4; ++l_i)
+                for (int l_j = 0; l_j < 4; ++l_j) {
+                    const uint32_t byte = tile_byte(tw, l_j * 4 + l_i);
+                    if (byte == 0) continue;
+                    const int64_t r = br * 4 + l_i, c = c0 + l_j;
+                    const double ti = (double)fp4_decode(byte >> 4) * (double)L.is[r] * (double)L.ois[c];
+                    const double a = fabs(ti);
+                    const long long key = (long long)e * 16 + l_i * 4 + l_j;
+                    if (best < 0.0 || a < best) { best = a; best_key = key; }
+                }
+        }
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) {
+            const double ob = __shfl_xor_sync(hmask, best, o);
+            const long long ok = __shfl_xor_sync(hmask, best_key, o);
+            const bool take = ob >= 0.0 && (best < 0.0 || ob < best || (ob == best && ok < best_key));
+            if (take) { best = ob; best_key = ok; }
+        }
+        if (best < 0.0) break;   // nothing live left
+        const int e = (int)(best_key / 16), l_i = (int)((best_key / 4) % 4), l_j = (int)(best_key % 4);
+        const int64_t ti = base + e;
+        uint4 tw = V.tile[ti];
+        const int old_len = tile_len(tile_live(tw), V.sparse[ti] != 0);
+        set_tile_byte(tw, l_j * 4 + l_i, 0u);
+        const int live = tile_live(tw);
+        const bool sp = (uint32_t)live <= V.switch_point;
+        used -= old_len - tile_len(live, sp);
+        __syncwarp(hmask);
+        if (s == 0) { V.tile[ti] = tw; V.sparse[ti] = sp ? 1 : 0; }
+        __syncwarp(hmask);
+    }
+    if (s == 0) {
+        // tiles that do not fit even after eviction (the reference counts them)
+        long long fit = 0;
+        int fitted = 0;
+        for (int e = 0; e < nt; ++e) {
+            const int tl = tile_len(tile_live(V.tile[base + e]), V.sparse[base + e] != 0);
+            if (fit + tl > cap) break;
+            fit += tl;
+            ++fitted;
+        }
+        if (fitted < nt) {
+            atomicAdd(V.counters + 1, 1ull);
+            atomicAdd(V.counters + 2, (unsigned long long)(used - fit));
+        }
+    }
+}
+
 // ── backward with update (lr != 0) ─────────────────────────────────────────
 // One half-warp per block-row; lane s (0..15) owns slot s of the current
 // tile (li = s & 3, lj = s >> 2).  Tiles are processed in stored order; for
@@ -416,64 +482,7 @@ __global__ void __launch_bounds__(128) k_b4_update(LayerView L, B4View V, const 
         }
         __syncwarp(hmask);
     }
-    // ── merge_row_workspace: evict until the row fits its tile allocation ──
-    const int64_t cap = V.alloc[V.BR + br];
-    long long used = 0;
-    for (int e = s; e < nt; e += 16) used += tile_len(tile_live(V.tile[base + e]), V.sparse[base + e] != 0);
-#pragma unroll
-    for (int o = 8; o > 0; o >>= 1) used += __shfl_xor_sync(hmask, used, o);
-    while (used > cap) {
-        double best = -1.0;
-        long long best_key = -1;
-        for (int e = s; e < nt; e += 16) {
-            const uint4 tw = V.tile[base + e];
-            const int64_t c0 = (int64_t)V.bc[base + e] * 4;
-            for (int l_i = 0; l_i < 4; ++l_i)
-                for (int l_j = 0; l_j < 4; ++l_j) {
-                    const uint32_t byte = tile_byte(tw, l_j * 4 + l_i);
-                    if (byte == 0) continue;
-                    const int64_t r = br * 4 + l_i, c = c0 + l_j;
-                    const double ti = (double)fp4_decode(byte >> 4) * (double)L.is[r] * (double)L.ois[c];
-                    const double a = fabs(ti);
-                    const long long key = (long long)e * 16 + l_i * 4 + l_j;
-                    if (best < 0.0 || a < best) { best = a; best_key = key; }
-                }
-        }
-#pragma unroll
-        for (int o = 8; o > 0; o >>= 1) {
-            const double ob = __shfl_xor_sync(hmask, best, o);
-            const long long ok = __shfl_xor_sync(hmask, best_key, o);
-            const bool take = ob >= 0.0 && (best < 0.0 || ob < best || (ob == best && ok < best_key));
-            if (take) { best = ob; best_key = ok; }
-        }
-        if (best < 0.0) break;   // nothing live left
-        const int e = (int)(best_key / 16), l_i = (int)((best_key / 4) % 4), l_j = (int)(best_key % 4);
-        const int64_t ti = base + e;
-        uint4 tw = V.tile[ti];
-        const int old_len = tile_len(tile_live(tw), V.sparse[ti] != 0);
-        set_tile_byte(tw, l_j * 4 + l_i, 0u);
-        const int live = tile_live(tw);
-        const bool sp = (uint32_t)live <= V.switch_point;
-        used -= old_len - tile_len(live, sp);
-        __syncwarp(hmask);
-        if (s == 0) { V.tile[ti] = tw; V.sparse[ti] = sp ? 1 : 0; }
-        __syncwarp(hmask);
-    }
-    if (s == 0) {
-        // tiles that do not fit even after eviction (the reference counts them)
-        long long fit = 0;
-        int fitted = 0;
-        for (int e = 0; e < nt; ++e) {
-            const int tl = tile_len(tile_live(V.tile[base + e]), V.sparse[base + e] != 0);
-            if (fit + tl > cap) break;
-            fit += tl;
-            ++fitted;
-        }
-        if (fitted < nt) {
-            atomicAdd(V.counters + 1, 1ull);
-            atomicAdd(V.counters + 2, (unsigned long long)(used - fit));
-        }
-    }
+    b4_evict_row(L, V, br, base, nt, s, hmask);
     // ── block4 value_scale step and dx write-back (leader lane of each row) ──
     if (leader && row_ok) {
         const float scale_eff_lr = __fdiv_rn(P.lr, (float)nnz_row);
@@ -513,6 +522,219 @@ void launch_b4_update(const LayerView& L, const B4View& V, const float* xT, cons
         default: SILI_B4(4, true); break;
     }
 #undef SILI_B4
+    count_launch();
+}
+
+// ── sparse-input forward: sisldo_forward's block4 windows ─────────────────
+// sisldo_ops.hpp:379-549.  For sample b, a block-row forms a window when any
+// of its 4 input rows has an entry in the sparse input; each column of each
+// tile of that block-row adds, over its live slots in li order,
+// fma(os * vs, x * w, acc) -- the reference build's evaluation of
+// acc += (w * vs * os) * x.  Windows are taken in ascending block-row.
+__global__ void __launch_bounds__(128) k_b4_forward_sparse(LayerView L, B4View V, const float* __restrict__ xT,
+                                                           const uint8_t* __restrict__ presT, int B,
+                                                           float* __restrict__ y) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t bcol = (int64_t)blockIdx.x * 4 + warp;
+    const int b = blockIdx.y * 32 + lane;
+    if (bcol >= V.BC) return;
+    const bool bok = b < B;
+    float mo[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    const int64_t col0 = bcol * 4;
+    float osc[4];
+#pragma unroll
+    for (int lj = 0; lj < 4; ++lj) osc[lj] = col0 + lj < L.n_out ? L.os[(col0 + lj) * L.rank] : 0.0f;
+    for (int t = V.cptr[bcol]; t < V.cptr[bcol + 1]; ++t) {
+        const int64_t br = V.cbr[t];
+        bool win = false;
+        float x[4], vsr[4];
+#pragma unroll
+        for (int li = 0; li < 4; ++li) {
+            const int64_t row = br * 4 + li;
+            const bool ok = bok && row < L.n_in;
+            win = win || (ok && presT[row * B + b] != 0);
+            x[li] = ok ? xT[row * B + b] : 0.0f;
+            vsr[li] = row < L.n_in ? L.vs[row * L.rank] : 0.0f;
+        }
+        if (!win) continue;
+        const uint4 tw = V.tile[V.ctile[t]];
+#pragma unroll
+        for (int lj = 0; lj < 4; ++lj) {
+            if (col0 + lj >= L.n_out) continue;
+            float acc = 0.0f;
+#pragma unroll
+            for (int li = 0; li < 4; ++li) {
+                if (br * 4 + li >= L.n_in) continue;
+                const uint32_t byte = tile_byte(tw, lj * 4 + li);
+                if (byte == 0) continue;
+                acc = __fmaf_rn(__fmul_rn(osc[lj], vsr[li]), __fmul_rn(x[li], fp4_decode(byte & 0xFu)), acc);
+            }
+            mo[lj] = __fadd_rn(mo[lj], acc);
+        }
+    }
+    if (!bok) return;
+#pragma unroll
+    for (int lj = 0; lj < 4; ++lj) {
+        const int64_t col = col0 + lj;
+        if (col < L.n_out) {
+            float* o = y + (int64_t)b * L.n_out + col;
+            *o = __fadd_rn(*o, mo[lj]);
+        }
+    }
+}
+void launch_b4_forward_sparse(const LayerView& L, const B4View& V, const float* xT, const uint8_t* presT, int B,
+                              float* y, cudaStream_t s) {
+    if (V.BC == 0 || B == 0) return;
+    dim3 g((unsigned)((V.BC + 3) / 4), (unsigned)((B + 31) / 32));
+    k_b4_forward_sparse<<<g, 128, 0, s>>>(L, V, xT, presT, B, y);
+    count_launch();
+}
+
+// ── sparse-gradient backward: disldo_backward_sparse_grad's block4 part ────
+// sisldo_ops.hpp:835-1104.  One half-warp per block-row, samples in order;
+// lane s owns slot s (li = s & 3, lj = s >> 2) of the current tile.  A tile
+// takes part for sample b when its 4-column window holds gradient entries;
+// slots whose dy is non-zero add to dx (fused chains over the window's
+// columns, li's chain carried by lane li) and, at lr != 0, get the plain
+// RMSprop step with a stochastic requantize.  After each sample the row's
+// workspace merge evicts down to its allocation; after all samples the
+// rank-1 value_scale step (no finite checks, as the reference).
+__global__ void __launch_bounds__(128) k_b4_backward_sparse(LayerView L, B4View V, const float* __restrict__ xT,
+                                                            const float* __restrict__ dyT,
+                                                            const uint8_t* __restrict__ presT, int B,
+                                                            UpdateParams P, float* __restrict__ dxT) {
+    const int lane = threadIdx.x & 31, s = lane & 15;
+    const int64_t br = (int64_t)blockIdx.x * (blockDim.x >> 4) + (threadIdx.x >> 4);
+    const unsigned hmask = (lane >> 4) ? 0xFFFF0000u : 0x0000FFFFu;
+    if (br >= V.BR) return;
+    const int nt = V.nt[br];
+    if (nt == 0) return;
+    const int li = s & 3, lj = s >> 2;
+    const int64_t row = br * 4 + li;
+    const bool row_ok = row < L.n_in, leader = lj == 0;
+    const int64_t base = V.es[br];
+    const int64_t nnz_row = (int64_t)nt * 4;
+    const bool training = P.lr != 0.0f;
+    const float eff_lr = P.lr_per_row_nnz ? __fdiv_rn(P.lr, (float)nnz_row) : P.lr;
+    const float onem = __fsub_rn(1.0f, P.beta2);
+    const float vs = row_ok ? L.vs[row * L.rank] : 0.0f;
+    const float isr = row_ok ? L.is[row] : 0.0f;
+    double rgs = 0.0, rgc = 0.0;                  // row sums (leader lanes)
+    double an = 0.0, ao = 0.0, sn = 0.0, so = 0.0;
+    float mx = 0.0f;
+    const int src0 = (lane & 16) | li;
+    for (int b = 0; b < B; ++b) {
+        const float in_val = row_ok ? xT[row * B + b] : 0.0f;
+        float dxa = 0.0f;
+        double rgl = 0.0, rglc = 0.0;              // this sample's row sums, added per sample
+        for (int e = 0; e < nt; ++e) {
+            const int64_t ti = base + e;
+            const int64_t col = (int64_t)V.bc[ti] * 4 + lj;
+            const bool col_ok = col < L.n_out;
+            const bool pres = col_ok && presT[col * B + b] != 0;
+            if (!__any_sync(hmask, pres)) continue;   // no gradient entry in the window
+            const float dyv = pres ? dyT[col * B + b] : 0.0f;
+            const bool act = row_ok && col_ok && dyv != 0.0f;
+            uint4 tw = V.tile[ti];
+            const uint32_t byte = tile_byte(tw, s);
+            const float wd = fp4_decode(byte & 0xFu);
+            const float osv = col_ok ? L.os[col * L.rank] : 0.0f;
+            const float cs = __fmul_rn(vs, osv);
+            const float w = __fmul_rn(wd, cs);
+            // dx terms a*b, chained by the row's leader in column order
+            const float ta = training ? w : __fmul_rn(osv, vs);
+            const float tb = training ? dyv : __fmul_rn(dyv, wd);
+            double qg = 0.0, qc = 0.0;
+            uint32_t nb = byte;
+            if (act && training) {
+                const float cis = __fmul_rn(isr, L.ois[col]);
+                const float imp_dec = fp4_decode(byte >> 4);
+                const float grad = __fmul_rn(dyv, in_val);
+                const float contrib = __fmul_rn(in_val, w);
+                float imp = __fmul_rn(imp_dec, cis);
+                imp = __fmaf_rn(P.beta2, imp, __fmul_rn(onem, __fmaf_rn(grad, grad, __fmul_rn(contrib, contrib))));
+                const float ng = __fmul_rn(-eff_lr, grad);
+                const float step = P.damp ? __fdiv_rn(ng, __fadd_rn(__fsqrt_rn(imp), P.eps)) : ng;
+                const float new_w = __fadd_rn(w, step);
+                const uint64_t el = (1ULL << 61) | (((uint64_t)b * (uint64_t)L.n_in + (uint64_t)row) * (uint64_t)L.n_out +
+                                                    (uint64_t)col);
+                const uint32_t wq = fp4_quantize_stochastic(__fdiv_rn(new_w, cs), rng_draw(P.call_key, el, 0));
+                const uint32_t iq = fp4_quantize_stochastic(__fdiv_rn(imp, cis), rng_draw(P.call_key, el, 1));
+                nb = (iq << 4) | wq;
+                const float actual = __fmul_rn(fp4_decode(iq), cis), stored = __fmul_rn(imp_dec, cis);
+                an += fabs((double)actual); ao += fabs((double)stored);
+                sn += (double)actual * (double)actual; so += (double)stored * (double)stored;
+                mx = fmaxf(mx, fabsf(actual));
+                const double wo = __dmul_rn((double)wd, (double)osv);
+                qg = __dmul_rn(wo, (double)__fmul_rn(dyv, in_val));
+                qc = __dmul_rn(wo, (double)contrib);
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int src = src0 + 4 * j;
+                const float aj = __shfl_sync(hmask, ta, src);
+                const float bj = __shfl_sync(hmask, tb, src);
+                const int okj = __shfl_sync(hmask, (int)act, src);
+                const double gj = __shfl_sync(hmask, qg, src);
+                const double cj = __shfl_sync(hmask, qc, src);
+                if (okj) {
+                    dxa = __fmaf_rn(aj, bj, dxa);
+                    if (training) { rgl = __dadd_rn(rgl, gj); rglc = __dadd_rn(rglc, cj); }
+                }
+            }
+            if (training) {
+                const bool dirty = __any_sync(hmask, act);
+                set_tile_byte(tw, s, nb);
+                uint32_t words[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    uint32_t wv = 0;
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) wv |= __shfl_sync(hmask, nb, (lane & 16) | (q * 4 + k)) << (8 * k);
+                    words[q] = wv;
+                }
+                if (dirty && s == 0) {
+                    const uint4 nw = make_uint4(words[0], words[1], words[2], words[3]);
+                    V.tile[ti] = nw;
+                    V.sparse[ti] = (uint32_t)tile_live(nw) <= V.switch_point ? 1 : 0;
+                }
+                __syncwarp(hmask);
+            }
+        }
+        if (training) b4_evict_row(L, V, br, base, nt, s, hmask);
+        if (leader && row_ok) {
+            float* d = dxT + row * B + b;
+            *d = __fadd_rn(*d, dxa);
+            rgs = __dadd_rn(rgs, rgl);
+            rgc = __dadd_rn(rgc, rglc);
+        }
+        __syncwarp(hmask);
+    }
+    if (!training) return;
+    if (an != 0.0 || ao != 0.0 || sn != 0.0 || so != 0.0) {
+        atomicAdd(P.stats + 0, an - ao);
+        atomicAdd(P.stats + 1, sn - so);
+    }
+    atomicMax(reinterpret_cast<unsigned int*>(P.stat_max), __float_as_uint(mx));
+    if (leader && row_ok && !(rgs == 0.0 && rgc == 0.0)) {
+        // the rank-1 value_scale step of sisldo_ops.hpp:1080-1101
+        const float se = __fdiv_rn(P.lr, (float)nnz_row);
+        const float g = (float)rgs, c = (float)rgc;
+        float* vsi = L.vsi + row * L.rank;
+        const float nv = __fmaf_rn(P.beta2, *vsi, __fmul_rn(onem, __fmaf_rn(g, g, __fmul_rn(c, c))));
+        uint32_t* st = L.vstep + row * L.rank;
+        const uint32_t step = *st + 1u;
+        *st = step;
+        const float bc = __fsub_rn(1.0f, bias_pow(P, step));
+        const float hat = bc > 0.0f ? __fdiv_rn(nv, bc) : nv;
+        *vsi = nv;
+        L.vs[row * L.rank] = __fsub_rn(L.vs[row * L.rank], __fdiv_rn(__fmul_rn(se, g), __fadd_rn(__fsqrt_rn(hat), P.eps)));
+    }
+}
+void launch_b4_backward_sparse(const LayerView& L, const B4View& V, const float* xT, const float* dyT,
+                               const uint8_t* presT, int B, const UpdateParams& P, float* dxT, cudaStream_t s) {
+    if (V.BR == 0 || B == 0) return;
+    k_b4_backward_sparse<<<(unsigned)((V.BR + 7) / 8), 128, 0, s>>>(L, V, xT, dyT, presT, B, P, dxT);
     count_launch();
 }
 

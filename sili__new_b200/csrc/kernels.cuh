@@ -221,6 +221,12 @@ void launch_b4_dx(const LayerView& L, const B4View& V, const float* dyT, int B, 
 // then merge_row_workspace's eviction and the block4 value_scale step
 void launch_b4_update(const LayerView& L, const B4View& V, const float* xT, const float* dyT, int B,
                       const UpdateParams& P, float* dxT, cudaStream_t s);
+// sparse-input forward block4 windows: y[B, n_out] += (xT/presT [n_in, B])
+void launch_b4_forward_sparse(const LayerView& L, const B4View& V, const float* xT, const uint8_t* presT, int B,
+                              float* y, cudaStream_t s);
+// sparse-gradient backward block4 part (dyT/presT [n_out, B]); dxT [n_in, B] +=
+void launch_b4_backward_sparse(const LayerView& L, const B4View& V, const float* xT, const float* dyT,
+                               const uint8_t* presT, int B, const UpdateParams& P, float* dxT, cudaStream_t s);
 // tile list for the column index: (bc key, global slot, block-row) of every live tile
 void launch_b4_list(const B4View& V, const int* tile_off, int* keys, int* slots, int* brs, cudaStream_t s);
 void launch_b4_index(const int* sorted_keys, const int* perm, int n, int64_t BC, const int* slots, const int* brs,

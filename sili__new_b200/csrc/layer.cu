@@ -135,7 +135,7 @@ struct sili_layer {
     // scratch
     DBuf<float> xT, dyT, dxT, colg, colc, ytmp, x_stage, dy_stage, dx_stage;
     bool has_dead_rows = false;
-    DBuf<uint8_t> presT;
+    DBuf<uint8_t> presT, presX;
     DBuf<double> dS, sgs, sgc;
     DBuf<int> i_tmp0, i_tmp1, i_tmp2;
     DBuf<float> f_tmp0;
@@ -1223,6 +1223,7 @@ int sili_layer_backward_dense(sili_layer* h, const float* x, const float* dy, in
         launch_backward_dx(v, h->dyT.p, batch, dxd, s);
         if (h->b4_ntiles > 0) launch_b4_dx(v, h->b4view(), h->dyT.p, batch, dxd, s);
         if (h->timing) { CK(cudaEventRecord(h->ev[3], s)); h->ev_bwd = true; }
+        h->call++;   // every backward call advances the stochastic-rounding counter
     } else {
         RC(h->dxT.reserve((int64_t)batch * n_in + 1));
         // pre-size the lazily sized scale vectors (linear_disldo.hpp:571-594)
@@ -1276,7 +1277,13 @@ int sili_layer_forward_sparse(sili_layer* h, const int* ptrs, const int* idx, co
     RC(to_dev(vals, dv.p, (size_t)nnz * 4, s));
     RC(h->xT.reserve((int64_t)batch * n_in + 1));
     CK(cudaMemsetAsync(h->xT.p, 0, (size_t)batch * n_in * 4, s));
-    launch_csr_to_dense_t(dp.p, di.p, dv.p, batch, (int)n_in, h->xT.p, nullptr, s);
+    uint8_t* xpres = nullptr;
+    if (h->b4_ntiles > 0) {
+        RC(h->presX.reserve((int64_t)batch * n_in + 1));
+        CK(cudaMemsetAsync(h->presX.p, 0, (size_t)batch * n_in, s));
+        xpres = h->presX.p;
+    }
+    launch_csr_to_dense_t(dp.p, di.p, dv.p, batch, (int)n_in, h->xT.p, xpres, s);
     const bool dev_out = is_device_ptr(y);
     float* yd = y;
     if (!dev_out) {
@@ -1285,6 +1292,10 @@ int sili_layer_forward_sparse(sili_layer* h, const int* ptrs, const int* idx, co
     }
     if (h->total_nnz > 0) launch_forward(h->view(), h->xT.p, batch, yd, true, s);
     else CK(cudaMemsetAsync(yd, 0, (size_t)batch * n_out * 4, s));
+    if (h->b4_ntiles > 0) {
+        RC(ensure_b4_index(h, s));
+        launch_b4_forward_sparse(h->view(), h->b4view(), h->xT.p, xpres, batch, yd, s);
+    }
     CK(cudaGetLastError());
     if (!dev_out) CK(cudaMemcpyAsync(y, yd, (size_t)batch * n_out * 4, cudaMemcpyDeviceToHost, s));
     CK(cudaStreamSynchronize(s));
@@ -1335,6 +1346,11 @@ int sili_layer_backward_sparse(sili_layer* h, const float* x, const int* dptrs, 
         }
     } else {
         CK(cudaMemsetAsync(h->dxT.p, 0, (size_t)batch * n_in * 4, s));
+    }
+    // block4 part after the scattered one (sisldo_ops.hpp:835-1104)
+    if (h->b4_ntiles > 0) {
+        launch_b4_backward_sparse(v, h->b4view(), h->xT.p, h->dyT.p, h->presT.p, batch, P, h->dxT.p, s);
+        if (lr != 0.0f) h->st_pending = true;
     }
     const bool dev_out = is_device_ptr(dx);
     float* dxd = dx;

@@ -269,6 +269,47 @@ def synap_fixture(seed=12):
     np.savez_compressed(os.path.join(HERE, "synap_block4.npz"), **out)
 
 
+def block4_sparse_fixture(seed=14):
+    """forward_sparse and backward_sparse on a layer with block4 tiles and
+    scattered synapses; the block4 part of backward_sparse always rounds
+    stochastically, so the reference's stream is seeded (seed_fp4_stochastic_rng)
+    and the oracle replays that stream."""
+    n_in, n_out, B = 64, 96, 12
+    rng = np.random.default_rng(seed)
+    mask = rng.random((n_in, n_out)) < 0.3
+    wc = np.where(mask, rng.integers(1, 16, (n_in, n_out)), 0).astype(np.uint8)
+    wc[wc == 8] = 1
+    ic = np.where(mask & (rng.random((n_in, n_out)) < 0.5), rng.integers(1, 8, (n_in, n_out)), 0).astype(np.uint8)
+    p, i, w, _ = random_layer(n_in, n_out, 9, seed=seed)
+    vs = (0.005 + 0.02 * rng.random(n_in)).astype(np.float32)
+    osc = (0.5 + rng.random(n_out)).astype(np.float32)
+    ref = RefLayerFactory(n_in, n_out, n_in * n_out)
+    ref.load_dense_codes(wc, ic)
+    ref.load_weights(p, i, w)
+    for r in range(n_in):
+        ref.set_value_scale_raw(r, float(vs[r]))
+        ref.set_importance_scale_raw(r, 0.05)
+    for c in range(n_out):
+        ref.set_output_scale_raw(c, float(osc[c]))
+    ref.compact_block4()
+    O.ref_lib().ref_seed_rng(4321)
+    out = dict(wc=wc, ic=ic, ptrs=p, idx=i, w=w, vs=vs, osc=osc, n_in=np.array([n_in]), n_out=np.array([n_out]),
+               budget=np.array([n_in * n_out]), rng_seed=np.array([4321], np.uint64), B=np.array([B]))
+    for t in range(3):
+        x = relu_sparse_x(rng, B, n_in)
+        px, ix, vx = O.dense_to_csr(x, 0.0)
+        dy = rng.normal(0, 1, (B, n_out)).astype(np.float32)
+        pd, idd, vd = O.top_k_csr(dy, int(0.2 * B * n_out))
+        lr = 0.0 if t == 0 else 0.03
+        out.update({f"x{t}": x, f"px{t}": px, f"ix{t}": ix, f"vx{t}": vx, f"pd{t}": pd, f"idd{t}": idd, f"vd{t}": vd,
+                    f"lr{t}": np.array([lr], np.float32)})
+        out[f"y{t}"] = ref.forward_sparse(px, ix, vx, B)
+        out[f"dx{t}"] = ref.backward_sparse(x, pd, idd, vd, B, lr, True)
+        out.update(b4_arrays(ref, f"s{t}_"))
+        out.update(state_arrays(ref, f"s{t}_"))
+    np.savez_compressed(os.path.join(HERE, "block4_sparse.npz"), **out)
+
+
 def std_sort_fixture(seed=13):
     """std::sort permutations (the orderings synap_row_step uses) on keys with
     many ties, for the restatement of libstdc++'s introsort."""
@@ -296,6 +337,7 @@ def main():
     block4_dense_fixture()
     synap_fixture()
     std_sort_fixture()
+    block4_sparse_fixture()
     print("fixtures written to", HERE)
 
 

@@ -130,3 +130,27 @@ def replay_synap(factory, fx, probes_from_fixture=False):
         compare_snapshot(snapshot(layer), fx, f"post{t}_")
         compare_b4(layer, fx, f"post{t}_")
         yield layer, f"post{t}"
+
+
+def replay_block4_sparse(factory, fx, reference_stream=False):
+    """forward_sparse / backward_sparse on a block4 + scattered layer."""
+    n_in, n_out = int(fx["n_in"][0]), int(fx["n_out"][0])
+    layer = factory(n_in, n_out, int(fx["budget"][0]))
+    if reference_stream:
+        layer.use_reference_stream(int(fx["rng_seed"][0]))
+    layer.load_dense_codes(fx["wc"], fx["ic"])
+    layer.load_weights(fx["ptrs"], fx["idx"], fx["w"])
+    for r in range(n_in):
+        layer.set_value_scale_raw(r, float(fx["vs"][r]))
+        layer.set_importance_scale_raw(r, 0.05)
+    for c in range(n_out):
+        layer.set_output_scale_raw(c, float(fx["osc"][c]))
+    layer.compact_block4()
+    B = int(fx["B"][0])
+    t = 0
+    while f"x{t}" in fx:
+        y = layer.forward_sparse(fx[f"px{t}"], fx[f"ix{t}"], fx[f"vx{t}"], B)
+        dx = layer.backward_sparse(fx[f"x{t}"], fx[f"pd{t}"], fx[f"idd{t}"], fx[f"vd{t}"], B,
+                                   float(fx[f"lr{t}"][0]), True)
+        yield layer, t, y, dx
+        t += 1

@@ -11,7 +11,7 @@ import pytest
 
 from oracle import oracle as O
 from helpers import compare_snapshot, setup_layer, snapshot
-from replay import build, replay_dense
+from replay import build, compare_b4, replay_dense
 
 GOLD = os.path.join(os.path.dirname(__file__), "golden")
 
@@ -134,3 +134,14 @@ def test_synaptogenesis_with_block4():
     stages = [s for _, s in replay_synap(oracle_factory, fx)]
     assert stages == ["sweep0", "sweep1", "post0", "post1"]
     assert fx["sw1_b4_view"][0] > 0, "fixture exercises block4 promotion"
+
+
+def test_block4_sparse_input_and_gradient():
+    """Pinned on the reference's own stochastic stream (seeded)."""
+    from replay import replay_block4_sparse
+    fx = load("block4_sparse")
+    for layer, t, y, dx in replay_block4_sparse(oracle_factory, fx, reference_stream=True):
+        assert np.array_equal(y, fx[f"y{t}"]), f"step {t}: forward_sparse differs"
+        assert np.array_equal(dx, fx[f"dx{t}"]), f"step {t}: backward_sparse dx differs"
+        compare_b4(layer, fx, f"s{t}_")
+        compare_snapshot(snapshot(layer), fx, f"s{t}_")

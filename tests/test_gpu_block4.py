@@ -12,7 +12,7 @@ import pytest
 
 from oracle import oracle as O
 from helpers import compare_snapshot, random_layer, relu_sparse_x, snapshot
-from replay import compare_b4, replay_block4_dense
+from replay import assert_close_sum, compare_b4, replay_block4_dense
 
 pytestmark = pytest.mark.gpu
 GOLD = os.path.join(os.path.dirname(__file__), "golden")
@@ -170,3 +170,24 @@ def test_block4_headroom_ops_and_view():
     assert v.used_bytes == o.block4.used_bytes() and v.alloc_bytes == o.block4.alloc_bytes()
     v.switch_point = 3
     assert g.block4.switch_point == 3
+
+
+def test_block4_sparse_input_and_gradient_vs_oracle():
+    """forward_sparse / backward_sparse with tiles: the GPU against the oracle
+    (both with the counter-based draws of the block4 sparse-gradient update)."""
+    from replay import replay_block4_sparse
+    fx = load("block4_sparse")
+    gpu = replay_block4_sparse(cuda_det, fx)
+    # the block4 sparse-gradient update always rounds stochastically: both
+    # sides use the library's default seed
+    cpu = replay_block4_sparse(lambda a, b, c: O.OracleLayer(a, b, c, seed=0x5EED), fx)
+    steps = 0
+    for (g, t, yg, dg), (o, _, yo, do) in zip(gpu, cpu):
+        assert np.array_equal(yg, yo), f"step {t}: forward_sparse differs (max {np.abs(yg - yo).max()})"
+        # the scattered part of the sparse-gradient dx sums with a warp tree
+        # (fp32 tolerance, as in the scattered-only parity tests)
+        assert_close_sum(dg, do, 1e-5)
+        _check_state(g, o, f"sparse step {t}")
+        np.testing.assert_allclose(snapshot(g)["stats"], snapshot(o)["stats"], rtol=1e-6, atol=1e-9)
+        steps += 1
+    assert steps == 3
