@@ -1188,10 +1188,18 @@ static int cmp_ex(const void* a, const void* b) {
 }
 int o_topk_dyx_step(OLayer* L, const float* x, const float* dy, int batch, int64_t k) {
     const int64_t nnz = L->total_nnz;
+    if (o_b4_ntiles(L) > 0) return O_EINVAL;   /* defined on the scattered store */
     int* cr = (int*)malloc((size_t)(k + 1) * sizeof(int));
     int* cc = (int*)malloc((size_t)(k + 1) * sizeof(int));
     float* cs = (float*)malloc((size_t)(k + 1) * sizeof(float));
     const int64_t nc = o_topk_dyx_candidates(L, x, dy, batch, k, cr, cc, cs);
+    {   /* the rebuild's reserve requests against the hard limits, before any change */
+        const int64_t nn0 = nnz - (nc < nnz ? nc : nnz) + nc;
+        if (nn0 + 64 > L->max_val_bytes || nn0 * 8 + 4096 > L->max_idx_bytes) {
+            free(cr); free(cc); free(cs);
+            return O_ENOMEM;
+        }
+    }
     int* p = (int*)malloc((size_t)(L->rows + 1) * sizeof(int));
     int* ix = (int*)malloc((size_t)(nnz + 1) * sizeof(int));
     float* w = (float*)malloc((size_t)(nnz + 1) * sizeof(float));

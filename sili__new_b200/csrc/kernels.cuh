@@ -125,8 +125,8 @@ void launch_copy_rows(const LayerView& L, const int64_t* new_bs, const int64_t* 
 void launch_import_lengths(const int* ptrs, const int* idx, int n_in, int* len, cudaStream_t s);
 void launch_import_rows(const int* ptrs, const int* boff, int n_in, int64_t* row_bytes, int64_t* row_n,
                         cudaStream_t s);
-void launch_import_write(const int* ptrs, const int* idx, const float* vals, const int* boff, int n_in,
-                         const int64_t* bs, const int64_t* es, uint8_t* ibuf, uint8_t* vbuf, cudaStream_t s);
+void launch_import_write(const int* ptrs, const int* idx, const float* vals, const float* imps, const int* boff,
+                         int n_in, const int64_t* bs, const int64_t* es, uint8_t* ibuf, uint8_t* vbuf, cudaStream_t s);
 void launch_add_offset(int64_t* p, int64_t begin, int64_t end, int64_t delta, cudaStream_t s);
 void launch_rescale_row(const LayerView& L, int row, float old_scale, float new_scale, bool weight,
                         cudaStream_t s);
@@ -209,6 +209,21 @@ inline int64_t synap_scratch_stride(int64_t m, int64_t p) {
 // ── block4 (csrc/block4.cu) ──────────────────────────────────────────────────
 // load_dense_codes: every tile of the [BR, BC] grid from row-major codes;
 // row_used[br] receives the reference's packed byte length of the row.
+// ── top-k |dy^T x| growth rule (csrc/topk.cu) ───────────────────────────────
+void launch_exist_bits(const int* rowptr, const int* abs_cols, int64_t n_in, int64_t words, uint32_t* bits,
+                       cudaStream_t s);
+void launch_dyx_scores(const float* x, const float* dy, int B, int64_t n_in, int64_t n_out, const uint32_t* bits,
+                       int64_t words, uint32_t* keys, cudaStream_t s);
+void launch_digit_hist(const uint32_t* keys, int64_t n, int shift, uint32_t mask, uint32_t prefix, unsigned int* hist,
+                       int sms, cudaStream_t s);
+void launch_prune_keys(const LayerView& L, const float* w, uint32_t* keys, int* ids, cudaStream_t s);
+void launch_mark_drop(const int* sorted_ids, int npr, const int* abs_cols, uint8_t* drop, int* out_degree,
+                      cudaStream_t s);
+void launch_cand_rowptr(const int64_t* cand, int nc, int64_t n_out, int64_t n_in, int* cptr, cudaStream_t s);
+void launch_topk_merge(const LayerView& L, const float* w, const float* imp, const uint8_t* drop, const int64_t* cand,
+                       const uint32_t* keys, const int* cptr, int pass, int* cnt, const int* newptr, int* nidx,
+                       float* nw, float* nimp, int* out_degree, cudaStream_t s);
+
 void launch_b4_load_dense(const uint8_t* wc, const uint8_t* ic, int64_t n_in, int64_t n_out, const B4View& V,
                           int64_t* row_used, cudaStream_t s);
 // per block-row [3*BR]: packed tile bytes in use, ULEB128 index bytes, live slots

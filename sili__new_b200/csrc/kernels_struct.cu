@@ -410,7 +410,8 @@ void launch_import_rows(const int* ptrs, const int* boff, int n_in, int64_t* row
 // Writes each synapse's ULEB128 delta at its row's byte offset and its value
 // byte (deterministic FP4 of the weight, importance code 0) at its element slot.
 __global__ void k_import_write(const int* __restrict__ ptrs, const int* __restrict__ idx,
-                               const float* __restrict__ vals, const int* __restrict__ boff, int n_in,
+                               const float* __restrict__ vals, const float* __restrict__ imps,
+                               const int* __restrict__ boff, int n_in,
                                const int64_t* __restrict__ bs, const int64_t* __restrict__ es,
                                uint8_t* __restrict__ ibuf, uint8_t* __restrict__ vbuf) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -426,13 +427,14 @@ __global__ void k_import_write(const int* __restrict__ ptrs, const int* __restri
             if (v) b |= 0x80u;
             ibuf[o++] = b;
         } while (v);
-        vbuf[es[r] + (f - p0)] = (uint8_t)(fp4_encode(vals[f]) << 4);
+        vbuf[es[r] + (f - p0)] = (uint8_t)((fp4_encode(vals[f]) << 4) | (imps ? fp4_encode(imps[f]) : 0u));
     }
 }
-void launch_import_write(const int* ptrs, const int* idx, const float* vals, const int* boff, int n_in,
-                         const int64_t* bs, const int64_t* es, uint8_t* ibuf, uint8_t* vbuf, cudaStream_t s) {
+void launch_import_write(const int* ptrs, const int* idx, const float* vals, const float* imps, const int* boff,
+                         int n_in, const int64_t* bs, const int64_t* es, uint8_t* ibuf, uint8_t* vbuf, cudaStream_t s) {
     if (n_in == 0) return;
-    k_import_write<<<(unsigned)((n_in + 7) / 8), 256, 0, s>>>(ptrs, idx, vals, boff, n_in, bs, es, ibuf, vbuf); count_launch();
+    k_import_write<<<(unsigned)((n_in + 7) / 8), 256, 0, s>>>(ptrs, idx, vals, imps, boff, n_in, bs, es, ibuf, vbuf);
+    count_launch();
 }
 
 }  // namespace sili

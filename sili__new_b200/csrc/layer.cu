@@ -163,6 +163,14 @@ struct sili_layer {
         DBuf<uint8_t> s_idx, s_val, s_be, s_ee, s_od, s_nt, s_bc, s_tile, s_sp, s_alloc, s_cnt;
         int64_t m = 0, p = 0, stride = 0;
     } syn;
+    // top-k |dy^T x| working set
+    struct TopkStateT {
+        DBuf<uint32_t> bits, keys, pk, pk_o;
+        DBuf<unsigned int> hist;
+        DBuf<int64_t> cand, cand_o, eq, nsel;
+        DBuf<int> pid, pid_o, cptr, cnt, nptr;
+        DBuf<uint8_t> drop;
+    } topk;
     // optional CUDA-event timing of the main forward / backward kernels
     bool timing = false;
     cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
@@ -189,6 +197,7 @@ struct sili_layer {
     }
 };
 using SynState = sili_layer::SynStateT;
+using TopkState = sili_layer::TopkStateT;
 
 namespace {
 
@@ -482,7 +491,8 @@ int recompute_stats(sili_layer* h) {
 // ULEB128 lengths and a scan give each row's byte count; the host lays out the
 // per-row headroom (0.2 * bytes + 5 bytes, max(1, 0.2 * n + 1) elements) and a
 // kernel writes every delta and FP4 byte in place.
-int import_csr(sili_layer* h, const int* d_ptrs, const int* d_idx, const float* d_vals, int nnz) {
+int import_csr(sili_layer* h, const int* d_ptrs, const int* d_idx, const float* d_vals, int nnz,
+               const float* d_imps = nullptr) {
     cudaStream_t s = h->stream;
     const int R = (int)h->rows;
     DBuf<int> len, boff;
@@ -517,7 +527,7 @@ int import_csr(sili_layer* h, const int* d_ptrs, const int* d_idx, const float* 
     RC(nval.reserve(vb + 64));
     CK(cudaMemsetAsync(nidx.p, 0, (size_t)nidx.cap, s));
     CK(cudaMemsetAsync(nval.p, 0, (size_t)nval.cap, s));
-    launch_import_write(d_ptrs, d_idx, d_vals, boff.p, R, h->bs.p, h->es.p, nidx.p, nval.p, s);
+    launch_import_write(d_ptrs, d_idx, d_vals, d_imps, boff.p, R, h->bs.p, h->es.p, nidx.p, nval.p, s);
     CK(cudaGetLastError());
     CK(cudaStreamSynchronize(s));
     h->idx.swap(nidx);
@@ -1696,10 +1706,123 @@ int sili_layer_zero_accum(sili_layer* h) {
     return SILI_OK;
 }
 
+// Predicates for cub::DeviceSelect over flat (r, c) positions
+struct KeyGreater {
+    const uint32_t* keys; uint32_t t;
+    __host__ __device__ bool operator()(const int64_t& i) const { return keys[i] > t; }
+};
+struct KeyEqual {
+    const uint32_t* keys; uint32_t t;
+    __host__ __device__ bool operator()(const int64_t& i) const { return keys[i] == t; }
+};
+
 int sili_layer_topk_dyx_step(sili_layer* h, const float* x, const float* dy, int batch, int64_t k, void* stream) {
     RC(use(h));
-    (void)x; (void)dy; (void)batch; (void)k; (void)stream;
-    return fail(SILI_EINVAL, "topk_dyx_step: not built yet");
+    if (batch <= 0 || !x || !dy || k < 0) return fail(SILI_EINVAL, "topk_dyx_step: bad arguments");
+    if (h->b4_ntiles > 0) return fail(SILI_EINVAL, "topk_dyx_step: defined on the scattered store (layer has block4 tiles)");
+    cudaStream_t s = pick(h, stream);
+    const int64_t R = h->rows, C = h->cols, n = R * C, nnz = h->total_nnz;
+    if (n >= ((int64_t)1 << 31)) return fail(SILI_EINVAL, "topk_dyx_step: n_in * n_out must be below 2^31");
+    RC(ensure_aux(h, s));
+    const int64_t total_ne = n - nnz;
+    if (k > total_ne) k = total_ne;
+    const int64_t nc = std::max<int64_t>(k, 0);
+    const int64_t npr = std::min(nc, nnz), nn = nnz - npr + nc;
+    if (nn + 64 > h->max_val_bytes || nn * 8 + 4096 > h->max_idx_bytes)
+        return fail(SILI_ENOMEM, "topk_dyx_step: rebuild exceeds the layer's byte budget");
+    TopkState& T = h->topk;
+    const float* dx_ = nullptr;
+    const float* ddy = nullptr;
+    RC(stage_in(h, x, (size_t)batch * R, h->x_stage, &dx_, s));
+    RC(stage_in(h, dy, (size_t)batch * C, h->dy_stage, &ddy, s));
+    const int64_t words = (C + 31) / 32;
+    RC(T.bits.reserve(R * words + 1)); RC(T.keys.reserve(n + 1));
+    CK(cudaMemsetAsync(T.bits.p, 0, (size_t)(R * words + 1) * 4, s));
+    LayerView v = h->view();
+    launch_exist_bits(h->rowptr.p, h->abs_cols.p, R, words, T.bits.p, s);
+    launch_dyx_scores(dx_, ddy, batch, R, C, T.bits.p, words, T.keys.p, s);
+    // radix select: the k-th largest key, 8 bits at a time from the top
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, h->dev);
+    RC(T.hist.reserve(256));
+    uint32_t prefix = 0, mask = 0;
+    int64_t need = nc, eq_count = 0;
+    for (int shift = 24; shift >= 0 && nc > 0; shift -= 8) {
+        CK(cudaMemsetAsync(T.hist.p, 0, 256 * sizeof(unsigned int), s));
+        launch_digit_hist(T.keys.p, n, shift, mask, prefix, T.hist.p, sms, s);
+        unsigned int hh[256];
+        CK(cudaMemcpyAsync(hh, T.hist.p, sizeof(hh), cudaMemcpyDeviceToHost, s));
+        CK(cudaStreamSynchronize(s));
+        int64_t cum = 0;
+        int d = 255;
+        for (; d > 0; --d) {
+            if (cum + (int64_t)hh[d] >= need) break;
+            cum += hh[d];
+        }
+        need -= cum;
+        eq_count = hh[d];
+        prefix |= (uint32_t)d << shift;
+        mask |= 0xFFu << shift;
+    }
+    const uint32_t thr = prefix;
+    // candidates: every key above the threshold, then the first `need` equal
+    // keys in (r, c) order; merged into (r, c) order
+    RC(T.cand.reserve(nc + 1)); RC(T.cand_o.reserve(nc + 1)); RC(T.nsel.reserve(2));
+    int64_t n_gt = 0;
+    if (nc > 0) {
+        cub::CountingInputIterator<int64_t> it(0);
+        RC(T.eq.reserve(eq_count + 1));
+        size_t b1 = 0, b2 = 0;
+        cub::DeviceSelect::If(nullptr, b1, it, T.cand.p, T.nsel.p, (int)n, KeyGreater{T.keys.p, thr}, s);
+        cub::DeviceSelect::If(nullptr, b2, it, T.eq.p, T.nsel.p + 1, (int)n, KeyEqual{T.keys.p, thr}, s);
+        RC(h->cub_tmp.reserve((int64_t)std::max(b1, b2) + 1));
+        b1 = std::max(b1, b2);
+        CK(cub::DeviceSelect::If(h->cub_tmp.p, b1, it, T.cand.p, T.nsel.p, (int)n, KeyGreater{T.keys.p, thr}, s));
+        int64_t sel[2] = {0, 0};
+        CK(cudaMemcpyAsync(sel, T.nsel.p, 8, cudaMemcpyDeviceToHost, s));
+        CK(cudaStreamSynchronize(s));
+        n_gt = sel[0];
+        b2 = b1;
+        CK(cub::DeviceSelect::If(h->cub_tmp.p, b2, it, T.eq.p, T.nsel.p + 1, (int)n, KeyEqual{T.keys.p, thr}, s));
+        if (n_gt + need != nc) return fail(SILI_ECUDA, "topk_dyx_step: selection count mismatch");
+        CK(cudaMemcpyAsync(T.cand.p + n_gt, T.eq.p, (size_t)need * 8, cudaMemcpyDeviceToDevice, s));
+        size_t b3 = 0;
+        cub::DeviceRadixSort::SortKeys(nullptr, b3, T.cand.p, T.cand_o.p, (int)nc, 0, 64, s);
+        RC(h->cub_tmp.reserve((int64_t)b3 + 1));
+        CK(cub::DeviceRadixSort::SortKeys(h->cub_tmp.p, b3, T.cand.p, T.cand_o.p, (int)nc, 0, 64, s));
+    }
+    // prune: the npr existing synapses of smallest |w * S|, ties in (r, c) order
+    DBuf<int> di;
+    DBuf<float> dw, dm;
+    RC(di.reserve(nnz + 1)); RC(dw.reserve(nnz + 1)); RC(dm.reserve(nnz + 1));
+    launch_export(v, di.p, dw.p, dm.p, s);
+    RC(T.pk.reserve(nnz + 1)); RC(T.pk_o.reserve(nnz + 1)); RC(T.pid.reserve(nnz + 1)); RC(T.pid_o.reserve(nnz + 1));
+    RC(T.drop.reserve(nnz + 1));
+    CK(cudaMemsetAsync(T.drop.p, 0, (size_t)nnz + 1, s));
+    if (npr > 0) {
+        launch_prune_keys(v, dw.p, T.pk.p, T.pid.p, s);
+        size_t b4 = 0;
+        cub::DeviceRadixSort::SortPairs(nullptr, b4, T.pk.p, T.pk_o.p, T.pid.p, T.pid_o.p, (int)nnz, 0, 32, s);
+        RC(h->cub_tmp.reserve((int64_t)b4 + 1));
+        CK(cub::DeviceRadixSort::SortPairs(h->cub_tmp.p, b4, T.pk.p, T.pk_o.p, T.pid.p, T.pid_o.p, (int)nnz, 0, 32, s));
+        launch_mark_drop(T.pid_o.p, (int)npr, h->abs_cols.p, T.drop.p, h->out_degree.p, s);
+    }
+    // merge rows, rebuild with delta_csr_from_absolute's headroom
+    RC(T.cptr.reserve(R + 1)); RC(T.cnt.reserve(R + 1)); RC(T.nptr.reserve(R + 1));
+    launch_cand_rowptr(T.cand_o.p, (int)nc, C, R, T.cptr.p, s);
+    CK(cudaMemsetAsync(T.cnt.p, 0, (size_t)(R + 1) * 4, s));
+    launch_topk_merge(v, dw.p, dm.p, T.drop.p, T.cand_o.p, T.keys.p, T.cptr.p, 0, T.cnt.p, nullptr, nullptr, nullptr,
+                      nullptr, h->out_degree.p, s);
+    RC(scan_excl_int(h, T.cnt.p, T.nptr.p, R + 1, s));
+    DBuf<int> nidx;
+    DBuf<float> nw, nimp;
+    RC(nidx.reserve(nn + 1)); RC(nw.reserve(nn + 1)); RC(nimp.reserve(nn + 1));
+    launch_topk_merge(v, dw.p, dm.p, T.drop.p, T.cand_o.p, T.keys.p, T.cptr.p, 1, T.cnt.p, T.nptr.p, nidx.p, nw.p,
+                      nimp.p, h->out_degree.p, s);
+    CK(cudaGetLastError());
+    RC(import_csr(h, T.nptr.p, nidx.p, nw.p, (int)nn, nimp.p));
+    CK(cudaStreamSynchronize(s));
+    return SILI_OK;
 }
 
 // ── export ──────────────────────────────────────────────────────────────────

@@ -178,6 +178,16 @@ public:
         check(sili_layer_synap_rows(h, row, 1, cutoff, max_rw, max_prune, eps, &did));
         return did != 0;
     }
+    // BASELINE config-3 growth rule: exact top-k of |dy^T x| over non-existing
+    // synapses, prune as many smallest |w*S|, rebuild (host or device arrays)
+    void topk_dyx_step(farr x, farr dy, int64_t k) {
+        if (x.ndim() != 2 || dy.ndim() != 2 || x.shape(0) != dy.shape(0) || x.shape(1) != n_in || dy.shape(1) != n_out)
+            throw py::value_error("topk_dyx_step: x [B, n_inputs] and dy [B, n_outputs] expected");
+        check(sili_layer_topk_dyx_step(h, x.data(), dy.data(), (int)x.shape(0), k, nullptr));
+    }
+    void topk_dyx_step_ptr(uintptr_t x, uintptr_t dy, int batch, int64_t k, uintptr_t stream) {
+        check(sili_layer_topk_dyx_step(h, (const float*)x, (const float*)dy, batch, k, (void*)stream));
+    }
     // nrows consecutive synap_row_step calls from row0 (wrapping) in one
     // device sweep; returns each step's result
     py::array_t<uint8_t> synap_rows(int row0, int nrows, float cutoff, int max_rw, int max_prune, float eps) {
@@ -357,6 +367,9 @@ void bind_layer(py::module_& m, const char* name) {
         .def("probes", &T::probes)
         .def("synap_row_step", &T::synap_row_step, py::arg("current_row"), py::arg("importance_cutoff"),
              py::arg("max_row_weights"), py::arg("max_prune_per_step") = 8, py::arg("importance_eps") = 1e-3f)
+        .def("topk_dyx_step", &T::topk_dyx_step, py::arg("x"), py::arg("dy"), py::arg("k"))
+        .def("topk_dyx_step_ptr", &T::topk_dyx_step_ptr, py::arg("x"), py::arg("dy"), py::arg("batch"), py::arg("k"),
+             py::arg("stream") = 0)
         .def("synap_rows", &T::synap_rows, py::arg("row0"), py::arg("nrows"), py::arg("importance_cutoff"),
              py::arg("max_row_weights"), py::arg("max_prune_per_step") = 8, py::arg("importance_eps") = 1e-3f)
         .def("synap_step", &T::synap_step, py::arg("importance_cutoff"), py::arg("max_row_weights"),

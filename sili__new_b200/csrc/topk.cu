@@ -1,0 +1,209 @@
+// BASELINE config-3 growth rule on the device: exact top-k of
+// |sum_b x[b,r] dy[b,c]| over non-existing (r, c), prune as many existing
+// synapses of smallest |w * S(r,c)|, rebuild the delta-CSR.  No reference
+// function exists; the rule is defined (and restated on the CPU by
+// oracle/sili_oracle.c, o_topk_dyx_*) as: s = fma(x[b,r], dy[b,c], s) for
+// b = 0..B-1 from s = 0 (so the score is bit-reproducible), ties toward lower
+// (r, c) on both sides, new synapses stored as delta_csr_synap_row_step
+// stores them (weight 0, importance fp4(score)).
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace sili {
+
+// existence bitmap [n_in, ceil(n_out/32)] from the decoded columns
+__global__ void k_exist_bits(const int* __restrict__ rowptr, const int* __restrict__ abs_cols, int64_t n_in,
+                             int64_t words, uint32_t* __restrict__ bits) {
+    const int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (r >= n_in) return;
+    for (int f = rowptr[r] + lane; f < rowptr[r + 1]; f += 32) {
+        const int c = abs_cols[f];
+        atomicOr(bits + r * words + (c >> 5), 1u << (c & 31));
+    }
+}
+void launch_exist_bits(const int* rowptr, const int* abs_cols, int64_t n_in, int64_t words, uint32_t* bits,
+                       cudaStream_t s) {
+    if (n_in == 0) return;
+    k_exist_bits<<<(unsigned)((n_in + 7) / 8), 256, 0, s>>>(rowptr, abs_cols, n_in, words, bits);
+    count_launch();
+}
+
+// Scores as 32-bit keys: 0 for an existing synapse, bits(|s|) + 1 otherwise
+// (|s| >= 0, so key order is score order).  128 x 128 output tile per block,
+// 8 x 8 per thread, samples staged 16 at a time; each output accumulates its
+// fma chain over b in ascending order, as the rule defines.
+constexpr int kTM = 128, kTN = 128, kTK = 16;
+__global__ void __launch_bounds__(256) k_dyx_scores(const float* __restrict__ x, const float* __restrict__ dy, int B,
+                                                    int64_t n_in, int64_t n_out, const uint32_t* __restrict__ bits,
+                                                    int64_t words, uint32_t* __restrict__ keys) {
+    __shared__ float xs[kTK][kTM];
+    __shared__ float ds[kTK][kTN];
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const int64_t r0 = (int64_t)blockIdx.y * kTM, c0 = (int64_t)blockIdx.x * kTN;
+    float acc[8][8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+    for (int b0 = 0; b0 < B; b0 += kTK) {
+        for (int t = threadIdx.x; t < kTK * kTM; t += 256) {
+            const int k = t / kTM, i = t % kTM;
+            const int b = b0 + k;
+            xs[k][i] = (b < B && r0 + i < n_in) ? x[(int64_t)b * n_in + r0 + i] : 0.0f;
+            ds[k][i] = (b < B && c0 + i < n_out) ? dy[(int64_t)b * n_out + c0 + i] : 0.0f;
+        }
+        __syncthreads();
+        const int kn = min(kTK, B - b0);
+        for (int k = 0; k < kn; ++k) {
+            float xv[8], dv[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) xv[i] = xs[k][ty * 8 + i];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) dv[j] = ds[k][tx + 16 * j];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[i][j] = __fmaf_rn(xv[i], dv[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int64_t r = r0 + ty * 8 + i;
+        if (r >= n_in) continue;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int64_t c = c0 + tx + 16 * j;
+            if (c >= n_out) continue;
+            const bool ex = (bits[r * words + (c >> 5)] >> (c & 31)) & 1u;
+            keys[r * n_out + c] = ex ? 0u : __float_as_uint(fabsf(acc[i][j])) + 1u;
+        }
+    }
+}
+void launch_dyx_scores(const float* x, const float* dy, int B, int64_t n_in, int64_t n_out, const uint32_t* bits,
+                       int64_t words, uint32_t* keys, cudaStream_t s) {
+    if (n_in == 0 || n_out == 0) return;
+    dim3 g((unsigned)((n_out + kTN - 1) / kTN), (unsigned)((n_in + kTM - 1) / kTM));
+    k_dyx_scores<<<g, 256, 0, s>>>(x, dy, B, n_in, n_out, bits, words, keys);
+    count_launch();
+}
+
+// radix-select histogram of one 8-bit digit among keys whose higher digits
+// equal `prefix` under `mask`
+__global__ void k_digit_hist(const uint32_t* __restrict__ keys, int64_t n, int shift, uint32_t mask, uint32_t prefix,
+                             unsigned int* __restrict__ hist) {
+    __shared__ unsigned int h[256];
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) h[i] = 0;
+    __syncthreads();
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const uint32_t k = keys[i];
+        if ((k & mask) == prefix) atomicAdd(&h[(k >> shift) & 0xFFu], 1u);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < 256; i += blockDim.x)
+        if (h[i]) atomicAdd(hist + i, h[i]);
+}
+void launch_digit_hist(const uint32_t* keys, int64_t n, int shift, uint32_t mask, uint32_t prefix, unsigned int* hist,
+                       int sms, cudaStream_t s) {
+    const int64_t blocks = std::min<int64_t>((n + 255) / 256, (int64_t)sms * 8);
+    k_digit_hist<<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, s>>>(keys, n, shift, mask, prefix, hist);
+    count_launch();
+}
+
+// prune keys: bits(|w * S(r, c)|) per existing synapse, in export order
+__global__ void k_prune_keys(LayerView L, const float* __restrict__ w, uint32_t* __restrict__ keys,
+                             int* __restrict__ ids) {
+    const int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (r >= L.n_in) return;
+    for (int f = L.rowptr[r] + lane; f < L.rowptr[r + 1]; f += 32) {
+        const int64_t c = L.abs_cols[f];
+        float S = 0.0f;
+        for (int k = 0; k < L.rank; ++k) S = __fmaf_rn(L.vs[r * L.rank + k], L.os[c * L.rank + k], S);
+        keys[f] = __float_as_uint(fabsf(__fmul_rn(w[f], S)));
+        ids[f] = f;
+    }
+}
+void launch_prune_keys(const LayerView& L, const float* w, uint32_t* keys, int* ids, cudaStream_t s) {
+    if (L.n_in == 0) return;
+    k_prune_keys<<<(unsigned)((L.n_in + 7) / 8), 256, 0, s>>>(L, w, keys, ids);
+    count_launch();
+}
+
+// drop flags for the first npr synapses of the sorted order; out_degree -1
+__global__ void k_mark_drop(const int* __restrict__ sorted_ids, int npr, const int* __restrict__ abs_cols,
+                            uint8_t* __restrict__ drop, int* __restrict__ out_degree) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= npr) return;
+    const int f = sorted_ids[i];
+    drop[f] = 1;
+    atomicSub(out_degree + abs_cols[f], 1);
+}
+void launch_mark_drop(const int* sorted_ids, int npr, const int* abs_cols, uint8_t* drop, int* out_degree,
+                      cudaStream_t s) {
+    if (npr <= 0) return;
+    k_mark_drop<<<(unsigned)((npr + 255) / 256), 256, 0, s>>>(sorted_ids, npr, abs_cols, drop, out_degree);
+    count_launch();
+}
+
+// candidate flat indices (sorted) -> per-row pointers over the candidate list
+__global__ void k_cand_rowptr(const int64_t* __restrict__ cand, int nc, int64_t n_out, int64_t n_in,
+                              int* __restrict__ cptr) {
+    const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (r > n_in) return;
+    int lo = 0, hi = nc;
+    while (lo < hi) { const int mid = (lo + hi) >> 1; if (cand[mid] / n_out < r) lo = mid + 1; else hi = mid; }
+    cptr[r] = lo;
+}
+void launch_cand_rowptr(const int64_t* cand, int nc, int64_t n_out, int64_t n_in, int* cptr, cudaStream_t s) {
+    k_cand_rowptr<<<(unsigned)((n_in + 256) / 256), 256, 0, s>>>(cand, nc, n_out, n_in, cptr);
+    count_launch();
+}
+
+// Per row: kept old synapses merged with the row's candidates by column.
+// pass 0 counts into cnt[r]; pass 1 writes at newptr[r].
+__global__ void k_topk_merge(LayerView L, const float* __restrict__ w, const float* __restrict__ imp,
+                             const uint8_t* __restrict__ drop, const int64_t* __restrict__ cand,
+                             const uint32_t* __restrict__ keys, const int* __restrict__ cptr, int pass,
+                             int* __restrict__ cnt, const int* __restrict__ newptr, int* __restrict__ nidx,
+                             float* __restrict__ nw, float* __restrict__ nimp, int* __restrict__ out_degree) {
+    const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= L.n_in) return;
+    int f = L.rowptr[r];
+    const int f1 = L.rowptr[r + 1];
+    int a = cptr[r];
+    const int a1 = cptr[r + 1];
+    int o = pass ? newptr[r] : 0;
+    int n = 0;
+    while (f < f1 || a < a1) {
+        const int64_t cc = a < a1 ? cand[a] % L.n_out : INT64_MAX;
+        const bool take_old = f < f1 && !(a < a1 && cc < L.abs_cols[f]);
+        if (take_old) {
+            if (!drop[f]) {
+                if (pass) { nidx[o] = L.abs_cols[f]; nw[o] = w[f]; nimp[o] = imp[f]; ++o; }
+                ++n;
+            }
+            ++f;
+        } else {
+            if (pass) {
+                const float score = __uint_as_float(keys[cand[a]] - 1u);
+                nidx[o] = (int)cc; nw[o] = 0.0f; nimp[o] = fp4_decode(fp4_encode(score)); ++o;
+                atomicAdd(out_degree + cc, 1);
+            }
+            ++n;
+            ++a;
+        }
+    }
+    if (!pass) cnt[r] = n;
+}
+void launch_topk_merge(const LayerView& L, const float* w, const float* imp, const uint8_t* drop, const int64_t* cand,
+                       const uint32_t* keys, const int* cptr, int pass, int* cnt, const int* newptr, int* nidx,
+                       float* nw, float* nimp, int* out_degree, cudaStream_t s) {
+    if (L.n_in == 0) return;
+    k_topk_merge<<<(unsigned)((L.n_in + 127) / 128), 128, 0, s>>>(L, w, imp, drop, cand, keys, cptr, pass, cnt, newptr,
+                                                                 nidx, nw, nimp, out_degree);
+    count_launch();
+}
+
+}  // namespace sili
