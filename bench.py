@@ -203,6 +203,80 @@ def run_reference_cpu(work, budget_s, threads, max_steps=None):
     return el / n, n, variant
 
 
+def run_folded(args, dev, rank, world, dist, S, torch):
+    """Mistral-Small-24B-shaped folded stack (hidden 5120,
+    32 heads / 8 KV x 128, FFN 32768, 40 layers folded per suffix), every
+    linear pruned to 95 %, random init; one decode step at batch 32 = every
+    suffix's stacked layer once (forward + fold sum), output columns sharded
+    over the ranks with an NCCL all-gather per suffix (strong scaling: the
+    same model whatever the rank count).  Returns the line's folded_stack
+    object (rank 0) or None."""
+    from sili__new_b200 import folded as F
+    cfg = F.MISTRAL_SMALL_24B
+    suffixes = F.mistral_suffixes(cfg)
+    n_folds, B, density = cfg["layers"], 32, 0.05
+    stack = F.FoldedStack(suffixes, n_folds, rank, world,
+                          lambda a, b, c: S.SparseLinearLayer(a, b, c, 1, dev),
+                          group=None)
+    t_build = time.perf_counter()
+    nnz_local = 0
+    for k, (name, (in_dim, out_dim)) in enumerate(suffixes.items()):
+        j0, j1 = F.column_slice(out_dim, rank, world)
+        ptrs, idx, vals, nnz = F.synthetic_shard(in_dim, out_dim, n_folds, density, j0, j1, seed=101 + k,
+                                                 device=f"cuda:{dev}")
+        stack.load(name, ptrs, idx, vals, nnz, F.SYNTHETIC_VALUE_SCALE)
+        nnz_local += nnz
+        del ptrs, idx, vals
+        torch.cuda.empty_cache()
+    build_s = time.perf_counter() - t_build
+    gen = torch.Generator(device=f"cuda:{dev}")
+    gen.manual_seed(7)
+    xs = {name: torch.randn(B, in_dim, generator=gen, device=f"cuda:{dev}") for name, (in_dim, _) in suffixes.items()}
+    stream = torch.cuda.Stream(device=dev)
+
+    def decode_step():
+        outs = []
+        for name in suffixes:
+            outs.append(stack.forward_device(name, xs[name], stream))
+        return outs
+
+    for _ in range(max(args.warmup, 3)):
+        decode_step()
+    torch.cuda.synchronize(dev)
+    steps = max(5, min(args.steps, 50))
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    l0 = S.kernel_launches()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        decode_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / steps
+    launches = S.kernel_launches() - l0
+    nnz_t = torch.tensor([float(nnz_local)], device=f"cuda:{dev}")
+    if dist:
+        t = torch.tensor([ms], device=f"cuda:{dev}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.all_reduce(nnz_t)
+    total_nnz = int(nnz_t.item())
+    flops = 2.0 * total_nnz * B
+    mem_gb = torch.cuda.max_memory_allocated(dev) / 1e9
+    if rank != 0:
+        return None
+    return {"metric": "folded-stack decode tokens/s (Mistral-Small-24B shape, 40 layers folded, 95% pruned, "
+                      "batch 32, linears only)",
+            "value": B / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "scaling": "strong",
+            "ms_per_step": ms, "steps": steps, "nnz": total_nnz,
+            "gflop_per_step": flops / 1e9, "fp32_tflops": flops / (ms * 1e-3) / 1e12,
+            "sharding": f"output columns within each fold over {world} rank(s), NCCL all-gather per suffix",
+            "build_s_rank0": build_s, "torch_mem_gb_rank0": mem_gb, "gpu_launches_rank0": launches,
+            "data": "synthetic: random N(0,0.02) pruned to 5% (Bernoulli), x ~ N(0,1)"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -212,6 +286,7 @@ def main():
     ap.add_argument("--layers", type=int, default=16)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-folded", action="store_true", help="skip the folded-stack (config 5) measurement")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -248,7 +323,7 @@ def main():
         import torch.distributed as dist
         from datetime import timedelta
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300))
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device(f"cuda:{local}"))
     dev = local if world > 1 else 0
     torch.cuda.set_device(dev)
 
@@ -362,6 +437,13 @@ def main():
                    "sample": f"{n} fwd+bwd steps of the full config-2 workload on sili._cpu "
                              f"(reference source built -march={variant}, num_cpus={threads})"}
 
+    # ── folded stack (config 5), sharded over the ranks ─────────────────────
+    folded = None
+    if not args.no_folded:
+        del layers, xs, dys, ys, dxs
+        torch.cuda.empty_cache()
+        folded = run_folded(args, dev, rank, world, dist, S, torch)
+
     if dist:
         dist.barrier()
         dist.destroy_process_group()
@@ -385,6 +467,7 @@ def main():
                 "d2h_bytes_per_step": BATCH * (N_IN + N_OUT) * 4},
         "gpu_launches": launches,
         "clocks": clk,
+        "folded_stack": folded,
     }
     print(json.dumps(line))
     return 0

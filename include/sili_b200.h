@@ -208,6 +208,11 @@ int sili_layer_b4_export(sili_layer* h, int* br, int* bc, uint8_t* slots, uint8_
  * bytes used, tile-slot alloc, tiles (the reference's Block4Store layout) */
 int sili_layer_b4_rows(sili_layer* h, int64_t* out6);
 
+/* ── folded stacks ─────────────────────────────────────────────────────── */
+/* FoldedLayer's fold sum (sili/sparse_rnn.py:1120-1125) on device arrays:
+ * y[b, j] = sum over folds f ascending of raw[b, f*out_dim + j] */
+int sili_fold_sum(const float* raw, int batch, int n_folds, int64_t out_dim, float* y, void* stream);
+
 /* ── module functions (cpu_backend.cpp:3075-3196) ───────────────────────── */
 /* fp4_quantize_array: deterministic FP4 encode, fp4quant.hpp:86-121 */
 int sili_fp4_quantize(const float* vals, uint8_t* codes, int64_t n, void* stream);

@@ -209,6 +209,9 @@ inline int64_t synap_scratch_stride(int64_t m, int64_t p) {
 // ── block4 (csrc/block4.cu) ──────────────────────────────────────────────────
 // load_dense_codes: every tile of the [BR, BC] grid from row-major codes;
 // row_used[br] receives the reference's packed byte length of the row.
+// FoldedLayer fold sum: y[B, out_dim] from raw[B, n_folds*out_dim]
+void launch_fold_sum(const float* raw, int B, int n_folds, int64_t out_dim, float* y, cudaStream_t s);
+
 // ── top-k |dy^T x| growth rule (csrc/topk.cu) ───────────────────────────────
 void launch_exist_bits(const int* rowptr, const int* abs_cols, int64_t n_in, int64_t words, uint32_t* bits,
                        cudaStream_t s);

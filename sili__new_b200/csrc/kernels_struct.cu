@@ -438,3 +438,23 @@ void launch_import_write(const int* ptrs, const int* idx, const float* vals, con
 }
 
 }  // namespace sili
+
+namespace sili {
+// FoldedLayer's fold sum (sili/sparse_rnn.py:1120-1125): y[b, j] = sum over
+// folds f (ascending) of raw[b, f * out_dim + j], raw of width n_folds * out_dim
+__global__ void k_fold_sum(const float* __restrict__ raw, int B, int n_folds, int64_t out_dim, float* __restrict__ y) {
+    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= (int64_t)B * out_dim) return;
+    const int64_t b = t / out_dim, j = t % out_dim;
+    const float* r = raw + b * (int64_t)n_folds * out_dim + j;
+    float acc = 0.0f;
+    for (int f = 0; f < n_folds; ++f) acc = __fadd_rn(acc, r[(int64_t)f * out_dim]);
+    y[t] = acc;
+}
+void launch_fold_sum(const float* raw, int B, int n_folds, int64_t out_dim, float* y, cudaStream_t s) {
+    const int64_t n = (int64_t)B * out_dim;
+    if (n == 0) return;
+    k_fold_sum<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(raw, B, n_folds, out_dim, y);
+    count_launch();
+}
+}  // namespace sili

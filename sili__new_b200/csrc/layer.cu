@@ -2204,6 +2204,15 @@ int sili_layer_b4_rows(sili_layer* h, int64_t* out) {
     return SILI_OK;
 }
 
+// ── folded stacks ───────────────────────────────────────────────────────────
+int sili_fold_sum(const float* raw, int batch, int n_folds, int64_t out_dim, float* y, void* stream) {
+    if (batch < 0 || n_folds < 0 || out_dim < 0 || !raw || !y) return fail(SILI_EINVAL, "fold_sum: bad arguments");
+    if (!is_device_ptr(raw) || !is_device_ptr(y)) return fail(SILI_EINVAL, "fold_sum: device pointers expected");
+    launch_fold_sum(raw, batch, n_folds, out_dim, y, (cudaStream_t)stream);
+    CK(cudaGetLastError());
+    return SILI_OK;
+}
+
 }  // extern "C"
 
 // ── forward_dense with no allocation ────────────────────────────────────────

@@ -432,6 +432,9 @@ void bind_layer(py::module_& m, const char* name) {
             if ((int)p.size() != s.n_in + 1) throw py::value_error("load_weights: ptrs must have n_inputs+1 entries");
             check(sili_layer_load_weights(s.h, p.data(), i.data(), w.data(), (int)i.size()));
         }, py::arg("ptrs"), py::arg("indices"), py::arg("weights"))
+        .def("load_weights_ptr", [](T& s, uintptr_t p, uintptr_t i, uintptr_t w, int nnz) {
+            check(sili_layer_load_weights(s.h, (const int*)p, (const int*)i, (const float*)w, nnz));
+        }, py::arg("ptrs"), py::arg("indices"), py::arg("weights"), py::arg("nnz"))
         .def_property_readonly("out_degree", [](T& s) {
             py::array_t<int> o((py::ssize_t)s.n_out);
             check(sili_layer_out_degree(s.h, o.mutable_data()));
@@ -477,6 +480,9 @@ PYBIND11_MODULE(_cuda, m) {
     m.attr("SCALE_VALUE_MOMENTUM") = SILI_SCALE_VALUE_MOMENTUM;
 
     m.def("device_count", []() { int n = 0; sili_device_count(&n); return n; });
+    m.def("fold_sum_ptr", [](uintptr_t raw, int batch, int n_folds, int64_t out_dim, uintptr_t y, uintptr_t stream) {
+        check(sili_fold_sum((const float*)raw, batch, n_folds, out_dim, (float*)y, (void*)stream));
+    }, py::arg("raw"), py::arg("batch"), py::arg("n_folds"), py::arg("out_dim"), py::arg("y"), py::arg("stream") = 0);
     m.def("kernel_launches", []() { int64_t n = 0; sili_kernel_launches(&n); return n; });
     m.def("dense_to_csr", [](farr x, float thr) {
         auto b = x.request();
