@@ -97,9 +97,10 @@ int sili_layer_rescale_row(sili_layer* h, int kind, int row, float new_scale);
 int sili_layer_forward_dense(sili_layer* h, const float* x, int batch, float* y, void* stream);
 /* forward_dense without any allocation.  No counterpart in the reference:
  * for callers that cannot call cudaMalloc.  x [batch, n_in] and y
- * [batch, n_out] must be device pointers; the transposed-input scratch is a
- * fixed per-device array of SILI_STATIC_FWD_MAX_ELEMS floats (4 MiB), so
- * batch * n_in above that is rejected with SILI_EINVAL.  The column index
+ * [batch, n_out] must be device pointers; the transposed-input scratch (plus
+ * one zero row) is a fixed per-device array of SILI_STATIC_FWD_MAX_ELEMS
+ * floats (4 MiB), so batch * (n_in + 1) above that is rejected with
+ * SILI_EINVAL.  The column index
  * must be current (one forward_dense after load_weights or a structural
  * change), else SILI_EINVAL.  Does not keep x for backward_dense.  The first
  * call on a device looks up the scratch address (cudaGetSymbolAddress); make

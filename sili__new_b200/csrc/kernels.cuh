@@ -32,9 +32,10 @@ struct LayerView {
     // derived index (rebuilt after structural changes)
     const int* rowptr;   // [n_in+1] exclusive scan of row nnz
     const int* abs_cols; // [nnz] absolute column of every live synapse, row-major
-    const int* colptr;   // [n_out+1] CSC shadow: synapses of column c at [colptr[c], colptr[c+1])
-    const int* crow;     // [nnz] their rows, ascending within a column
-    const int* cvpos;    // [nnz] their positions in val[]
+    const int* colptr;   // [n_out+1] CSC shadow, each column padded to a multiple of 8 entries:
+                         // column c at [colptr[c], colptr[c+1])
+    const int* crow;     // their rows, ascending within a column; padding: row n_in (the zero input row)
+    const int* cvpos;    // their positions in val[]; padding: -1 (weight 0)
     const int* b4_nt = nullptr;  // [ceil(n_in/4)] block4 tiles per block-row (null: no block4)
 };
 
@@ -109,8 +110,11 @@ void launch_csr_to_dense_t(const int* ptrs, const int* idx, const float* vals, i
 void launch_row_nnz(const int64_t* es, const int64_t* ee, int64_t n_in, int* rowptr_plus1, cudaStream_t s);
 void launch_decode_rows(const LayerView& L, int* abs_cols, int* frow, int* fvpos, int* colcount,
                         cudaStream_t s);
-void launch_gather_csc(const int* sorted_f, const int* frow, const int* fvpos, int64_t nnz, int* crow,
-                       int* cvpos, cudaStream_t s);
+void launch_gather_csc(const int* sorted_f, const int* sorted_col, const int* frow, const int* fvpos,
+                       const int* colptr, const int* pcolptr, int64_t nnz, int* crow, int* cvpos, cudaStream_t s);
+void launch_pad_csc(const int* colcount, const int* pcolptr, int64_t n_cols, int n_in, int* crow, int* cvpos,
+                    cudaStream_t s);
+void launch_pad_counts(const int* colcount, int64_t n, int* out, cudaStream_t s);
 
 // state helpers
 void launch_fill_f32(float* p, int64_t n, float v, cudaStream_t s);

@@ -109,8 +109,8 @@ __global__ void __launch_bounds__(256) k_forward_gather(LayerView L, const float
             const int kk = kb + lane;
             int r = 0;
             float w = 0.0f, cs = 0.0f;
-            if (kk < k1) {
-                r = L.crow[kk];
+            if (kk < k1) r = L.crow[kk];   // CSC padding: the zero input row, weight 0
+            if (kk < k1 && L.cvpos[kk] >= 0) {
                 const float wq = fp4_decode(L.val[L.cvpos[kk]] >> 4);
                 if (SPARSE) {
                     w = wq;
@@ -161,6 +161,117 @@ __global__ void __launch_bounds__(256) k_forward_gather(LayerView L, const float
     }
 }
 
+// Vectorised gather for batches that are a multiple of 4: each lane carries 4
+// samples (one float4 of the transposed input), LPC lanes cover 4*LPC
+// samples of one column and a warp works 32/LPC columns at once.  Every
+// (column, sample) keeps its own fma chain over the column's synapses in
+// ascending row -- the reference's single-thread order -- so the result is
+// bit-exact.  Columns come padded to a multiple of 8 entries whose row is the
+// all-zero input row n_in and whose weight is 0, so the inner loop has no
+// bounds tests.  The reference skips zero inputs; for a finite weight
+// fma(w, 0, acc) == acc (acc, built from +0, is never -0), so the skip is
+// only applied in a chunk holding a non-finite weight or scale.
+template <int LPC, bool SPARSE>
+__global__ void __launch_bounds__(256) k_forward_vec(LayerView L, const float* __restrict__ xT, int B,
+                                                     float* __restrict__ y) {
+    constexpr int CPW = 32 / LPC;          // columns per warp
+    constexpr int CPB = 8 * CPW;           // columns per block
+    constexpr int SPB = 4 * LPC;           // samples per block
+    __shared__ float ys[CPB][SPB + 1];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int grp = lane / LPC, lid = lane % LPC;
+    const int gbase = grp * LPC;
+    const int64_t cb = (int64_t)blockIdx.x * CPB;
+    const int64_t c = cb + warp * CPW + grp;
+    const int b0 = blockIdx.y * SPB;
+    const int bl = b0 + lid * 4;
+    const bool bok = bl < B;
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    int k0 = 0, len = 0;
+    float osk[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (c < L.n_out) {
+        k0 = L.colptr[c];
+        len = L.colptr[c + 1] - k0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) osk[k] = k < L.rank ? L.os[c * L.rank + k] : 0.0f;
+    }
+    int maxlen = len;
+#pragma unroll
+    for (int o = LPC; o < 32; o <<= 1) maxlen = max(maxlen, __shfl_xor_sync(0xffffffffu, maxlen, o));
+    // lanes past the batch read the zero row: every lane stays on the fast path
+    const float* xb = bok ? xT + bl : xT + (int64_t)L.n_in * B;
+    const int omask = bok ? -1 : 0;
+    for (int kb = 0; kb < maxlen; kb += 8) {
+        // lanes lid < 8 load the chunk's metadata: row offset and weight
+        int off = L.n_in * B;                  // zero row
+        float w = 0.0f, cs = 0.0f;
+        if (lid < 8 && kb < len) {
+            const int kk = k0 + kb + lid;
+            const int vp = L.cvpos[kk];
+            if (vp >= 0) {
+                const int r = L.crow[kk];
+                off = r * B;
+                const float wq = fp4_decode(L.val[vp] >> 4);
+                if (SPARSE) {
+                    w = wq;
+                    cs = __fmul_rn(L.vs[(int64_t)r * L.rank], osk[0]);
+                } else {
+                    float sc = 0.0f;
+                    for (int k = 0; k < L.rank; ++k) sc = __fmaf_rn(L.vs[(int64_t)r * L.rank + k], osk[k], sc);
+                    w = __fmul_rn(wq, sc);
+                }
+            }
+        }
+        const bool careful = __any_sync(0xffffffffu, !isfinite(w) || (SPARSE && !isfinite(cs)));
+        float4 xv[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int o = __shfl_sync(0xffffffffu, off, gbase + u) & omask;
+            xv[u] = __ldg(reinterpret_cast<const float4*>(xb + o));
+        }
+        if (!careful) {
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const float wj = __shfl_sync(0xffffffffu, w, gbase + u);
+                if (SPARSE) {
+                    const float cj = __shfl_sync(0xffffffffu, cs, gbase + u);
+                    acc[0] = __fadd_rn(acc[0], __fmul_rn(__fmul_rn(wj, xv[u].x), cj));
+                    acc[1] = __fadd_rn(acc[1], __fmul_rn(__fmul_rn(wj, xv[u].y), cj));
+                    acc[2] = __fadd_rn(acc[2], __fmul_rn(__fmul_rn(wj, xv[u].z), cj));
+                    acc[3] = __fadd_rn(acc[3], __fmul_rn(__fmul_rn(wj, xv[u].w), cj));
+                } else {
+                    acc[0] = __fmaf_rn(wj, xv[u].x, acc[0]);
+                    acc[1] = __fmaf_rn(wj, xv[u].y, acc[1]);
+                    acc[2] = __fmaf_rn(wj, xv[u].z, acc[2]);
+                    acc[3] = __fmaf_rn(wj, xv[u].w, acc[3]);
+                }
+            }
+        } else {
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const float wj = __shfl_sync(0xffffffffu, w, gbase + u);
+                const float cj = SPARSE ? __shfl_sync(0xffffffffu, cs, gbase + u) : 0.0f;
+                const float xs[4] = {xv[u].x, xv[u].y, xv[u].z, xv[u].w};
+#pragma unroll
+                for (int v = 0; v < 4; ++v) {
+                    if (xs[v] == 0.0f) continue;
+                    acc[v] = SPARSE ? __fadd_rn(acc[v], __fmul_rn(__fmul_rn(wj, xs[v]), cj))
+                                    : __fmaf_rn(wj, xs[v], acc[v]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int v = 0; v < 4; ++v) ys[warp * CPW + grp][lid * 4 + v] = acc[v];
+    __syncthreads();
+    for (int i = threadIdx.x; i < CPB * SPB; i += 256) {
+        const int bi = i / CPB, ci = i % CPB;
+        const int b = b0 + bi;
+        const int64_t cc = cb + ci;
+        if (b < B && cc < L.n_out) y[(int64_t)b * L.n_out + cc] = ys[ci][bi];
+    }
+}
+
 // Small batches: lanes over a column's synapses, per-lane partial sums over
 // the batch, then a fixed warp tree (deterministic; not the reference's
 // sequential order, so equal to it within fp32 rounding).
@@ -178,6 +289,7 @@ __global__ void __launch_bounds__(256) k_forward_small(LayerView L, const float*
     for (int b = 0; b < BMAX; ++b) acc[b] = 0.0f;
     const int k0 = L.colptr[c], k1 = L.colptr[c + 1];
     for (int kk = k0 + lane; kk < k1; kk += 32) {
+        if (L.cvpos[kk] < 0) continue;   // CSC padding
         const int r = L.crow[kk];
         const float wq = fp4_decode(L.val[L.cvpos[kk]] >> 4);
         float w, cs = 0.0f;
@@ -217,7 +329,22 @@ void launch_forward(const LayerView& L, const float* xT, int B, float* y, bool s
         count_launch();
         return;
     }
-    if (B <= 32) {
+    if (B % 4 == 0) {
+        // lanes per column: 4 samples each, up to one warp per column
+        const int lpc = B <= 32 ? 8 : (B <= 64 ? 16 : 32);
+        const int cpb = 8 * (32 / lpc), spb = 4 * lpc;
+        dim3 g((unsigned)((L.n_out + cpb - 1) / cpb), (unsigned)((B + spb - 1) / spb));
+        if (lpc == 8) {
+            if (sparse) k_forward_vec<8, true><<<g, 256, 0, s>>>(L, xT, B, y);
+            else k_forward_vec<8, false><<<g, 256, 0, s>>>(L, xT, B, y);
+        } else if (lpc == 16) {
+            if (sparse) k_forward_vec<16, true><<<g, 256, 0, s>>>(L, xT, B, y);
+            else k_forward_vec<16, false><<<g, 256, 0, s>>>(L, xT, B, y);
+        } else {
+            if (sparse) k_forward_vec<32, true><<<g, 256, 0, s>>>(L, xT, B, y);
+            else k_forward_vec<32, false><<<g, 256, 0, s>>>(L, xT, B, y);
+        }
+    } else if (B <= 32) {
         dim3 g(gx, 1);
         if (sparse) k_forward_gather<1, true><<<g, 256, 0, s>>>(L, xT, B, y);
         else k_forward_gather<1, false><<<g, 256, 0, s>>>(L, xT, B, y);

@@ -50,19 +50,49 @@ void launch_decode_rows(const LayerView& L, int* abs_cols, int* frow, int* fvpos
     k_decode_rows<<<(unsigned)((L.n_in + 7) / 8), 256, 0, s>>>(L, abs_cols, frow, fvpos, colcount); count_launch();
 }
 
-__global__ void k_gather_csc(const int* __restrict__ sorted_f, const int* __restrict__ frow,
-                             const int* __restrict__ fvpos, int64_t nnz, int* __restrict__ crow,
-                             int* __restrict__ cvpos) {
+// CSC shadow with every column padded to a multiple of 8 entries: entry k of
+// the column-sorted order goes to pcolptr[col] + (k - colptr[col]); the
+// padding entries are (row n_in, value position -1), i.e. the zero input row
+// with weight 0, so the forward kernels need no per-element bounds tests.
+__global__ void k_gather_csc(const int* __restrict__ sorted_f, const int* __restrict__ sorted_col,
+                             const int* __restrict__ frow, const int* __restrict__ fvpos,
+                             const int* __restrict__ colptr, const int* __restrict__ pcolptr, int64_t nnz,
+                             int* __restrict__ crow, int* __restrict__ cvpos) {
     const int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (k >= nnz) return;
-    const int f = sorted_f[k];
-    crow[k] = frow[f];
-    cvpos[k] = fvpos[f];
+    const int f = sorted_f[k], c = sorted_col[k];
+    const int64_t o = pcolptr[c] + (k - colptr[c]);
+    crow[o] = frow[f];
+    cvpos[o] = fvpos[f];
 }
-void launch_gather_csc(const int* sorted_f, const int* frow, const int* fvpos, int64_t nnz, int* crow, int* cvpos,
-                       cudaStream_t s) {
+__global__ void k_pad_csc(const int* __restrict__ colcount, const int* __restrict__ pcolptr, int64_t n_cols,
+                          int n_in, int* __restrict__ crow, int* __restrict__ cvpos) {
+    const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= n_cols) return;
+    for (int o = pcolptr[c] + colcount[c]; o < pcolptr[c + 1]; ++o) { crow[o] = n_in; cvpos[o] = -1; }
+}
+// padded column counts: (count + 7) & ~7
+__global__ void k_pad_counts(const int* __restrict__ colcount, int64_t n, int* __restrict__ out) {
+    const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (c < n) out[c] = (colcount[c] + 7) & ~7;
+}
+void launch_gather_csc(const int* sorted_f, const int* sorted_col, const int* frow, const int* fvpos,
+                       const int* colptr, const int* pcolptr, int64_t nnz, int* crow, int* cvpos, cudaStream_t s) {
     if (nnz == 0) return;
-    k_gather_csc<<<(unsigned)((nnz + 255) / 256), 256, 0, s>>>(sorted_f, frow, fvpos, nnz, crow, cvpos); count_launch();
+    k_gather_csc<<<(unsigned)((nnz + 255) / 256), 256, 0, s>>>(sorted_f, sorted_col, frow, fvpos, colptr, pcolptr, nnz,
+                                                               crow, cvpos);
+    count_launch();
+}
+void launch_pad_csc(const int* colcount, const int* pcolptr, int64_t n_cols, int n_in, int* crow, int* cvpos,
+                    cudaStream_t s) {
+    if (n_cols == 0) return;
+    k_pad_csc<<<(unsigned)((n_cols + 255) / 256), 256, 0, s>>>(colcount, pcolptr, n_cols, n_in, crow, cvpos);
+    count_launch();
+}
+void launch_pad_counts(const int* colcount, int64_t n, int* out, cudaStream_t s) {
+    if (n == 0) return;
+    k_pad_counts<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(colcount, n, out);
+    count_launch();
 }
 
 __global__ void k_fill_f32(float* p, int64_t n, float v) {

@@ -131,6 +131,7 @@ struct sili_layer {
     // derived index
     bool aux_dirty = true;
     DBuf<int> rowptr, abs_cols, frow, fvpos, colcount, colptr, crow, cvpos, sort_k, sort_ko, sort_v, sort_vo;
+    DBuf<int> colptr_x, padcnt;   // exact column offsets, padded counts
     DBuf<uint8_t> cub_tmp;
     // scratch
     DBuf<float> xT, dyT, dxT, colg, colc, ytmp, x_stage, dy_stage, dx_stage;
@@ -250,8 +251,11 @@ int stage_in(sili_layer* h, const float* src, size_t n, DBuf<float>& stage, cons
 int stage_transposed(sili_layer* h, const float* src, int64_t rows, int64_t cols, DBuf<float>& dst, cudaStream_t s) {
     const float* d = nullptr;
     RC(stage_in(h, src, (size_t)(rows * cols), h->x_stage, &d, s));
-    RC(dst.reserve(rows * cols + 1));
+    // [cols, rows] plus one zero row (row `cols`), which the forward kernels'
+    // CSC padding entries point at
+    RC(dst.reserve(rows * cols + rows + 1));
     launch_transpose(d, dst.p, rows, cols, s);
+    CK(cudaMemsetAsync(dst.p + rows * cols, 0, (size_t)rows * sizeof(float), s));
     return SILI_OK;
 }
 UpdateParams update_params(sili_layer* h, float lr, unsigned flags, float beta2, float eps) {
@@ -291,8 +295,9 @@ int ensure_aux(sili_layer* h, cudaStream_t s) {
     RC(h->colptr.reserve(C + 1));
     RC(h->colcount.reserve(C + 1));
     const int64_t nz = std::max<int64_t>(nnz, 1);
+    const int64_t nzp = nz + 7 * C + 8;   // padded CSC bound
     RC(h->abs_cols.reserve(nz)); RC(h->frow.reserve(nz)); RC(h->fvpos.reserve(nz));
-    RC(h->crow.reserve(nz)); RC(h->cvpos.reserve(nz));
+    RC(h->crow.reserve(nzp)); RC(h->cvpos.reserve(nzp)); RC(h->colptr_x.reserve(C + 1)); RC(h->padcnt.reserve(C + 1));
     RC(h->sort_k.reserve(nz)); RC(h->sort_ko.reserve(nz)); RC(h->sort_v.reserve(nz)); RC(h->sort_vo.reserve(nz));
     CK(cudaMemsetAsync(h->rowptr.p, 0, sizeof(int), s));
     launch_row_nnz(h->es.p, h->ee.p, R, h->rowptr.p + 1, s);
@@ -311,9 +316,15 @@ int ensure_aux(sili_layer* h, cudaStream_t s) {
         RC(h->cub_tmp.reserve((int64_t)bytes + 1));
         CK(cub::DeviceRadixSort::SortPairs(h->cub_tmp.p, bytes, h->sort_k.p, h->sort_ko.p, h->sort_v.p,
                                            h->sort_vo.p, (int)nnz, 0, bits, s));
-        launch_gather_csc(h->sort_vo.p, h->frow.p, h->fvpos.p, nnz, h->crow.p, h->cvpos.p, s);
     }
-    RC(scan_excl_int(h, h->colcount.p, h->colptr.p, C + 1, s));
+    // exact column offsets, then the padded ones the forward kernels use
+    RC(scan_excl_int(h, h->colcount.p, h->colptr_x.p, C + 1, s));
+    launch_pad_counts(h->colcount.p, C + 1, h->padcnt.p, s);
+    RC(scan_excl_int(h, h->padcnt.p, h->colptr.p, C + 1, s));
+    if (nnz > 0)
+        launch_gather_csc(h->sort_vo.p, h->sort_ko.p, h->frow.p, h->fvpos.p, h->colptr_x.p, h->colptr.p, nnz,
+                          h->crow.p, h->cvpos.p, s);
+    launch_pad_csc(h->colcount.p, h->colptr.p, C, (int)R, h->crow.p, h->cvpos.p, s);
     CK(cudaGetLastError());
     {   // rows with no synapse take the dead-row bootstrap (linear_disldo.hpp:1985-2042)
         std::vector<int> rp((size_t)R + 1);
@@ -1285,8 +1296,8 @@ int sili_layer_forward_sparse(sili_layer* h, const int* ptrs, const int* idx, co
     RC(to_dev(ptrs, dp.p, (size_t)(batch + 1) * 4, s));
     RC(to_dev(idx, di.p, (size_t)nnz * 4, s));
     RC(to_dev(vals, dv.p, (size_t)nnz * 4, s));
-    RC(h->xT.reserve((int64_t)batch * n_in + 1));
-    CK(cudaMemsetAsync(h->xT.p, 0, (size_t)batch * n_in * 4, s));
+    RC(h->xT.reserve((int64_t)batch * (n_in + 1) + 1));
+    CK(cudaMemsetAsync(h->xT.p, 0, (size_t)batch * (n_in + 1) * 4, s));   // + the zero row
     uint8_t* xpres = nullptr;
     if (h->b4_ntiles > 0) {
         RC(h->presX.reserve((int64_t)batch * n_in + 1));
@@ -2231,7 +2242,8 @@ int sili_fold_sum(const float* raw, int batch, int n_folds, int64_t out_dim, flo
 // must be ordered, e.g. issued on one stream.
 //
 // Nothing in the scratch has to start at zero: the transpose writes every
-// element xT[0, n_in * batch) before the gather kernel reads any of it.
+// element xT[0, n_in * batch) and a memset the zero row after it before the
+// gather kernel reads any of it.
 namespace {
 constexpr int64_t kStaticFwdScratch = SILI_STATIC_FWD_MAX_ELEMS;  // floats, 4 MiB
 constexpr int kStaticMaxDevices = 64;
@@ -2261,9 +2273,10 @@ extern "C" int sili_layer_forward_dense_static(sili_layer* h, const float* x, in
     RC(use(h));
     if (batch < 0 || !x || !y) return fail(SILI_EINVAL, "forward_dense_static: bad arguments");
     const int64_t n_in = h->rows;
-    if ((int64_t)batch * n_in > kStaticFwdScratch)
-        return fail(SILI_EINVAL, "forward_dense_static: batch * n_inputs = " + std::to_string((int64_t)batch * n_in) +
-                                     " exceeds the static scratch of " + std::to_string(kStaticFwdScratch) + " floats");
+    if ((int64_t)batch * (n_in + 1) > kStaticFwdScratch)
+        return fail(SILI_EINVAL, "forward_dense_static: batch * (n_inputs + 1) = " +
+                                     std::to_string((int64_t)batch * (n_in + 1)) + " exceeds the static scratch of " +
+                                     std::to_string(kStaticFwdScratch) + " floats");
     if (!is_device_ptr(x) || !is_device_ptr(y))
         return fail(SILI_EINVAL, "forward_dense_static: x and y must be device pointers");
     if (h->aux_dirty)
@@ -2273,6 +2286,7 @@ extern "C" int sili_layer_forward_dense_static(sili_layer* h, const float* x, in
     RC(static_fwd_scratch(h->dev, &xT));
     cudaStream_t s = pick(h, stream);
     launch_transpose(x, xT, batch, n_in, s);
+    CK(cudaMemsetAsync(xT + (int64_t)batch * n_in, 0, (size_t)batch * sizeof(float), s));   // zero row
     launch_forward(h->view(), xT, batch, y, false, s);
     CK(cudaGetLastError());
     return SILI_OK;

@@ -118,7 +118,7 @@ def test_codec_golden(S):
 
 
 # ── larger seeded cases vs the CPU oracle ──────────────────────────────────
-@pytest.mark.parametrize("B", [1, 5, 16, 33, 64])
+@pytest.mark.parametrize("B", [1, 5, 9, 12, 16, 32, 33, 36, 64, 100])
 def test_forward_vs_oracle(S, B):
     n_in, n_out = 300, 500
     p, i, w, vs = random_layer(n_in, n_out, 25, seed=B, empty_rows=(0, 7))
@@ -233,3 +233,15 @@ def test_backward_update_edge_cases(S, case):
     assert np.array_equal(sg["live_val"], so2["live_val"])
     for k in ("sc_value_scale", "sc_value_scale_importance", "sc_value_scale_step"):
         assert np.array_equal(sg[k], so2[k], equal_nan=True), k
+
+
+@pytest.mark.parametrize("B", [12, 32, 64, 68])
+def test_forward_sparse_vec_vs_oracle(S, B):
+    """forward_sparse through the vectorised gather (batch a multiple of 4)."""
+    n_in, n_out = 200, 330
+    p, i, w, vs = random_layer(n_in, n_out, 20, seed=B + 3)
+    g = setup_layer(S.SparseLinearLayerDeterministic(n_in, n_out, len(i) * 2), p, i, w, vs)
+    o = setup_layer(O.OracleLayer(n_in, n_out, len(i) * 2), p, i, w, vs)
+    x = relu_sparse_x(np.random.default_rng(B), B, n_in)
+    px, ix, vx = O.dense_to_csr(x, 0.0)
+    assert np.array_equal(g.forward_sparse(px, ix, vx, B), o.forward_sparse(px, ix, vx, B))

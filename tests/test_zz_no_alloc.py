@@ -45,7 +45,7 @@ def _make(lib, n_in, n_out, per_row, seed):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("n_in,n_out,batch", [(1024, 768, 64), (8192, 4096, 128), (300, 500, 5)])
+@pytest.mark.parametrize("n_in,n_out,batch", [(1024, 768, 64), (8191, 4096, 128), (300, 500, 5)])
 def test_static_forward_matches_forward_dense(n_in, n_out, batch):
     lib = _lib()
     h = _make(lib, n_in, n_out, 41, seed=n_in)
@@ -78,17 +78,17 @@ def test_static_forward_rejects_what_it_cannot_serve():
     n_in, n_out = 4096, 256
     h = _make(lib, n_in, n_out, 9, seed=1)
     try:
-        x = torch.zeros(MAX_ELEMS // n_in + 1, n_in, device="cuda")
+        x = torch.zeros(MAX_ELEMS // (n_in + 1) + 1, n_in, device="cuda")
         y = torch.empty(x.shape[0], n_out, device="cuda")
         # column index not built yet (no forward_dense since load_weights)
         assert lib.sili_layer_forward_dense_static(h, x.data_ptr(), 1, y.data_ptr(), None) == 1
         assert b"column index is stale" in lib.sili_last_error()
         _ok(lib, lib.sili_layer_forward_dense(h, x.data_ptr(), 1, y.data_ptr(), None))
-        # batch * n_in one row above the scratch size
+        # batch * (n_in + 1) one sample above the scratch size
         assert lib.sili_layer_forward_dense_static(h, x.data_ptr(), x.shape[0], y.data_ptr(), None) == 1
         assert b"exceeds the static scratch" in lib.sili_last_error()
         # exactly at the limit is served
-        b = MAX_ELEMS // n_in
+        b = MAX_ELEMS // (n_in + 1)
         _ok(lib, lib.sili_layer_forward_dense_static(h, x.data_ptr(), b, y.data_ptr(), None))
         # host pointers are rejected (they would need staging)
         xh = np.zeros((1, n_in), np.float32)
