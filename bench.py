@@ -411,7 +411,9 @@ def main():
         L.forward_dense_ptr(hx[j % 2].data_ptr(), BATCH, hy[j % 2].data_ptr(), sh)
         L.backward_dense_ptr(hdy[j % 2].data_ptr(), BATCH, LR, True, True, 0.999, 1e-8, hdx[j % 2].data_ptr(), sh, 0)
 
-    for j in range(3):
+    # every layer copy once through the host-buffer path first: its staging
+    # buffers are allocated on first use, outside the timed region
+    for j in range(max(3, len(layers))):
         e2e_step(j)
     torch.cuda.synchronize(dev)
     if dist:
