@@ -74,10 +74,16 @@ struct UpdateParams {
     float* colc;           // [n_out*rank] forward-contribution sums
     double* stats;         // [4] importance l1 new-old, l2 new-old (sums)
     float* stat_max;       // [1] importance max (float bits as uint max)
+    // *dy_flag == dy_tag: this call's dy holds an inf or NaN (null: unknown,
+    // treated as "may hold one")
+    const unsigned long long* dy_flag = nullptr;
+    unsigned long long dy_tag = 0;
 };
 
 void launch_transpose(const float* in, float* out, int64_t R, int64_t C, cudaStream_t s);
-void launch_accum_abs(const float* x, float* acc, int B, int64_t n, cudaStream_t s);
+// nonfinite (optional): set to `tag` when some |x| is inf or NaN
+void launch_accum_abs(const float* x, float* acc, int B, int64_t n, cudaStream_t s,
+                      unsigned long long* nonfinite = nullptr, unsigned long long tag = 0);
 void launch_accum_abs_t(const float* xT, float* acc, int B, int64_t n, cudaStream_t s);
 void launch_accum_abs_csr(const int* ptrs, const int* idx, const float* vals, int rows, int ncols, float* acc,
                           cudaStream_t s);
@@ -91,6 +97,9 @@ void launch_backward_dx(const LayerView& L, const float* dyT, int B, float* dx, 
 // dense backward at lr != 0: fused per-synapse update + dxT [n_in, B]
 void launch_backward_update(const LayerView& L, const float* xT, const float* dyT, int B,
                             const UpdateParams& P, float* dxT, cudaStream_t s);
+// the same for B <= 128 (kernels_update.cu); launch_backward_update calls it
+void launch_backward_update_tiled(const LayerView& L, const float* xT, const float* dyT, int B,
+                                  const UpdateParams& P, float* dxT, cudaStream_t s);
 void launch_output_scale_update(const LayerView& L, const int* out_degree, const UpdateParams& P,
                                 cudaStream_t s);
 void launch_dead_rows(const LayerView& L, const float* xT, const float* dy, int B, double* scratchS,

@@ -41,16 +41,26 @@ void launch_transpose(const float* in, float* out, int64_t R, int64_t C, cudaStr
 }
 
 // neuron_*_accum[j] += |x[b, j]| for b ascending (linear_disldo.hpp:515-520).
-__global__ void k_accum_abs(const float* __restrict__ x, float* __restrict__ acc, int B, int64_t n) {
+// With a flag pointer, a thread that meets an inf or NaN stores `tag` there
+// (the update kernel reads it to choose its exact general path for the call).
+__global__ void k_accum_abs(const float* __restrict__ x, float* __restrict__ acc, int B, int64_t n,
+                            unsigned long long* __restrict__ nonfinite, unsigned long long tag) {
     const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (j >= n) return;
     float a = acc[j];
-    for (int b = 0; b < B; ++b) a = __fadd_rn(a, fabsf(x[(int64_t)b * n + j]));
+    bool bad = false;
+    for (int b = 0; b < B; ++b) {
+        const float v = fabsf(x[(int64_t)b * n + j]);
+        bad |= !(v <= 3.402823466e38f);
+        a = __fadd_rn(a, v);
+    }
     acc[j] = a;
+    if (bad && nonfinite) *nonfinite = tag;
 }
-void launch_accum_abs(const float* x, float* acc, int B, int64_t n, cudaStream_t s) {
+void launch_accum_abs(const float* x, float* acc, int B, int64_t n, cudaStream_t s, unsigned long long* nonfinite,
+                      unsigned long long tag) {
     if (n == 0 || B == 0) return;
-    k_accum_abs<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(x, acc, B, n); count_launch();
+    k_accum_abs<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(x, acc, B, n, nonfinite, tag); count_launch();
 }
 
 // Same accumulation from the transposed input xT [n, B].
@@ -658,6 +668,10 @@ __global__ void __launch_bounds__(kUpdWarps * 32, 6) k_backward_update(LayerView
 void launch_backward_update(const LayerView& L, const float* xT, const float* dyT, int B,
                             const UpdateParams& P, float* dxT, cudaStream_t s) {
     if (L.n_in == 0) return;
+    if (B <= 128) {   // x and dx of a row fit in registers: the tiled two-chain kernel
+        launch_backward_update_tiled(L, xT, dyT, B, P, dxT, s);
+        return;
+    }
     const unsigned g = (unsigned)((L.n_in + kUpdWarps - 1) / kUpdWarps);
 #define SILI_BWD(R)                                                                         \
     if (P.stochastic) k_backward_update<true, R><<<g, kUpdWarps * 32, 0, s>>>(L, xT, dyT, B, P, dxT);  \

@@ -1,0 +1,338 @@
+// The fused dense backward at learning_rate != 0 for batches up to 128:
+// disldo_backward's scattered non-deferred path (linear_disldo.hpp:625-925),
+// with k_backward_update's arithmetic and summation orders (so codes, scales
+// and dx are bit-identical to it), arranged to issue fewer instructions and
+// keep more warps resident.
+//
+//  * One warp per input row, one synapse per lane, 32 synapses at a time.
+//  * The dy tile [32 synapses][32 samples] reaches shared memory by cp.async
+//    16-byte copies, one 128-byte line of dyT per synapse, with no staging
+//    registers (pitch 36 floats keeps the lanes = samples reads of the dx
+//    pass free of bank conflicts).
+//  * x of the row sits in shared memory; dx[b, r] stays in registers for the
+//    whole row (lanes = samples, one register per 32-sample block) and is
+//    stored once, instead of a read-modify-write per tile.
+//  * Whether dy holds an inf or NaN is known per call (a flag written by the
+//    |dy| accumulation), not checked per tile.
+//  * The weight history cw (the weight after every sample that can change
+//    it) is kept for at most kU2K such samples of a 32-sample block; a block
+//    with more is processed as sub-blocks, each followed by the dx pass over
+//    its own samples.  dx sums the synapses in stored order with fmaf, each
+//    sample with the weight its synapse had after that sample.
+//
+// Floating point: compiled with --fmad=false like every kernel file here;
+// each fused multiply-add is an explicit __fmaf_rn placed as the reference's
+// build fuses it.
+#include "common.cuh"
+#include "kernels.cuh"
+#include "update_math.cuh"
+
+namespace sili {
+
+// 2-warp CTAs with 12 KB of shared memory each; 14 resident per SM (28
+// warps, 72 registers) at scale rank 1-2, 10 at rank 3-4 (their per-synapse
+// state needs more registers)
+constexpr int kU2Warps = 2, kU2K = 8, kU2Pitch = 36;
+constexpr int u2_min_ctas(int rank) { return rank <= 2 ? 14 : 10; }
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(d), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+
+// One synapse's running state through the batch.
+template <int RANK>
+struct SynChain {
+    float ci, quant, cw, S, cw_orig;
+    uint32_t byte;   // the stored FP4BiPacked byte at entry
+    int c;           // absolute column
+    bool ok;         // finite S and weight, and the row's parameters allow the x == 0 closed form
+    float osk[RANK], cg[RANK], cc[RANK];
+};
+
+template <bool STOCH, bool OST, int RANK, int NB>
+__global__ void __launch_bounds__(kU2Warps * 32, u2_min_ctas(RANK)) k_backward_update_tiled(LayerView L, const float* __restrict__ xT,
+                                                                             const float* __restrict__ dyT, int B,
+                                                                             UpdateParams P, float* __restrict__ dxT) {
+    __shared__ __align__(16) float dys_s[kU2Warps][32][kU2Pitch];   // [synapse][sample]
+    __shared__ __align__(16) float cws_s[kU2Warps][kU2K + 1][32];   // [segment][synapse]
+    __shared__ float xs_s[kU2Warps][NB * 32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t r = (int64_t)blockIdx.x * kU2Warps + warp;
+    if (r >= L.n_in) return;
+    const int64_t es = L.es[r];
+    const int nnz = (int)(L.ee[r] - es);
+    float* dxr = dxT + r * (int64_t)B;
+    if (nnz == 0) {
+        for (int b = lane; b < B; b += 32) dxr[b] = 0.0f;
+        return;
+    }
+    float (*dys)[kU2Pitch] = dys_s[warp];
+    float (*cws)[32] = cws_s[warp];
+    float* xs = xs_s[warp];
+    const int f0 = L.rowptr[r];
+    const float eff_lr = P.lr_per_row_nnz ? __fdiv_rn(P.lr, (float)nnz) : P.lr;
+    const float beta2 = P.beta2;
+    const float onem = __fsub_rn(1.0f, beta2);
+    const float zterm = __fmul_rn(onem, 0.0f);
+    const bool fast_ok = (!P.damp || P.eps > 0.0f) && isfinite(eff_lr) && beta2 >= 0.0f && beta2 <= 1.0f;
+    const bool dy_finite = P.dy_flag != nullptr && *P.dy_flag != P.dy_tag;
+    const float imp_scale = L.is[r];
+    float vsr[RANK];
+#pragma unroll
+    for (int k = 0; k < RANK; ++k) vsr[k] = L.vs[r * RANK + k];
+    const float* xr = xT + r * (int64_t)B;
+    const bool vec4 = (B & 3) == 0;
+    const int nblk = (B + 31) >> 5;
+    float acc[NB];
+#pragma unroll
+    for (int k = 0; k < NB; ++k) {
+        const int t = k * 32 + lane;
+        xs[t] = t < B ? __ldg(xr + t) : 0.0f;
+        acc[k] = 0.0f;
+    }
+    __syncwarp();
+
+    double sgs[RANK], sgc[RANK];
+#pragma unroll
+    for (int k = 0; k < RANK; ++k) { sgs[k] = 0.0; sgc[k] = 0.0; }
+    // importance statistics: FP4 magnitudes are multiples of 1/2, so the
+    // l1 and l2 changes are exact integers in units of 1/2 and 1/4
+    int l1d = 0, l2d = 0;
+    bool st_nan = false;
+    float mx_new = 0.0f;
+
+    auto init = [&](SynChain<RANK>& C, int e, bool valid) {
+        C.c = 0;
+        C.byte = 0;
+        if (valid) {
+            C.c = L.abs_cols[f0 + e];
+            C.byte = L.val[es + e];
+        }
+        C.cw_orig = fp4_decode(C.byte >> 4);
+#pragma unroll
+        for (int k = 0; k < RANK; ++k) C.osk[k] = valid ? L.os[(int64_t)C.c * RANK + k] : 0.0f;
+        const float cis = valid ? __fmul_rn(imp_scale, L.ois[C.c]) : 1.0f;
+        float S = 0.0f;
+#pragma unroll
+        for (int k = 0; k < RANK; ++k) S = __fmaf_rn(vsr[k], C.osk[k], S);
+        C.S = S;
+        C.ci = __fmul_rn(fp4_decode(C.byte & 15u), cis);
+        C.quant = C.cw_orig;
+        C.cw = __fmul_rn(C.quant, S);
+        C.ok = fast_ok && isfinite(S) && isfinite(C.cw_orig);
+#pragma unroll
+        for (int k = 0; k < RANK; ++k) { C.cg[k] = 0.0f; C.cc[k] = 0.0f; }
+    };
+    // one sample that can change the weight (x != 0, or any sample on the
+    // general path)
+    auto step = [&](SynChain<RANK>& C, float dyv, float iv) {
+        const float g = __fmul_rn(dyv, iv);
+        const float contrib = __fmul_rn(iv, C.cw_orig);
+        C.ci = bounded_ci(C.ci, g, contrib, beta2, onem);
+        const float ngS = __fmul_rn(-g, C.S);
+        float raw = P.damp ? __fdiv_rn(ngS, __fadd_rn(__fsqrt_rn(C.ci), P.eps)) : ngS;
+        if (raw > 2.0f) raw = 2.0f;
+        if (raw < -2.0f) raw = -2.0f;
+        C.quant = __fmaf_rn(eff_lr, raw, C.quant);
+        C.cw = __fmul_rn(C.quant, C.S);
+        const float qf = (C.quant == 0.0f) ? 0.1f : C.quant;
+#pragma unroll
+        for (int k = 0; k < RANK; ++k) {
+            const double qo = (double)qf * (double)C.osk[k];
+            sgs[k] = __fma_rn(qo, (double)g, sgs[k]);
+            sgc[k] = __fma_rn(qo, (double)contrib, sgc[k]);
+            if (OST) {
+                const float qv = __fmul_rn(qf, vsr[k]);
+                C.cg[k] = __fmaf_rn(qv, g, C.cg[k]);
+                C.cc[k] = __fmaf_rn(qv, contrib, C.cc[k]);
+            }
+        }
+    };
+    // dy tile: row l = synapse e0 + l (its n synapses), samples [t0, t0 + nb);
+    // rows of absent synapses read as dy = 0
+    auto stage = [&](const SynChain<RANK>& C, int n, int t0, int nb) {
+        if (vec4) {   // B % 4 == 0: every 16-byte group lies inside or outside [0, nb)
+            const int sub = lane >> 3, m4 = (lane & 7) * 4;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const int l = q * 4 + sub;
+                const int cl = __shfl_sync(0xffffffffu, C.c, l);
+                if (l < n && m4 < nb) cp_async16(&dys[l][m4], dyT + (int64_t)cl * B + t0 + m4);
+            }
+        } else {
+            for (int l = 0; l < n; ++l) {
+                const int cl = __shfl_sync(0xffffffffu, C.c, l);
+                if (lane < nb) cp_async4(&dys[l][lane], dyT + (int64_t)cl * B + t0 + lane);
+            }
+        }
+        for (int l = n; l < 32; ++l) dys[l][lane] = 0.0f;
+    };
+    auto finish = [&](const SynChain<RANK>& C, int e) {
+        const float cis = __fmul_rn(imp_scale, L.ois[C.c]);
+        const float imp_st = __fdiv_rn(C.ci, cis);
+        uint32_t nbyte;
+        if (STOCH) {
+            const uint64_t vp = (uint64_t)(es + e);
+            nbyte = (fp4_quantize_stochastic(C.quant, rng_draw(P.call_key, vp, 0)) << 4) |
+                    fp4_quantize_stochastic(imp_st, rng_draw(P.call_key, vp, 1));
+        } else {
+            nbyte = (fp4_encode(C.quant) << 4) | fp4_encode(imp_st);
+        }
+        L.val[es + e] = (uint8_t)nbyte;
+        const float an = fabsf(fp4_decode(nbyte & 15u)), ao = fabsf(fp4_decode(C.byte & 15u));
+        if (an != an || ao != ao) {
+            st_nan = true;
+        } else {
+            const int hn = (int)(2.0f * an), ho = (int)(2.0f * ao);
+            l1d += hn - ho;
+            l2d += hn * hn - ho * ho;
+        }
+        mx_new = fmaxf(mx_new, an);
+        if (OST) {
+#pragma unroll
+            for (int k = 0; k < RANK; ++k) {
+                atomicAdd(P.colg + (int64_t)C.c * RANK + k, C.cg[k]);
+                atomicAdd(P.colc + (int64_t)C.c * RANK + k, C.cc[k]);
+            }
+        }
+    };
+
+    SynChain<RANK> A;   // synapse e0 + lane
+    for (int e0 = 0; e0 < nnz; e0 += 32) {
+        const int nA = min(32, nnz - e0);
+        init(A, e0 + lane, lane < nA);
+        for (int blk = 0; blk < nblk; ++blk) {
+            const int t0 = blk * 32, nb = min(32, B - t0);
+            float a = acc[0];
+#pragma unroll
+            for (int k = 1; k < NB; ++k)
+                if (blk == k) a = acc[k];
+            __syncwarp();   // the previous tile's readers are done
+            stage(A, nA, t0, nb);
+            const float* xb = xs + t0;
+            const unsigned act = __ballot_sync(0xffffffffu, xb[lane] != 0.0f);   // zero beyond B
+            cp_async_wait_all();
+            __syncwarp();
+            const unsigned full = nb >= 32 ? 0xffffffffu : ((1u << nb) - 1u);
+            const bool fast = A.ok && A.ci >= 0.0f && A.ci <= 100.0f;
+            // samples where some weight may change: x != 0, or all of them
+            // when some lane cannot take the x == 0 closed form
+            const unsigned bnd = (dy_finite && __all_sync(0xffffffffu, fast)) ? act : full;
+            unsigned rem = bnd;
+            int j = 0, s0 = 0;
+            while (s0 < nb) {
+                cws[0][lane] = A.cw;
+                int seg = 0, s1 = nb;
+                while (true) {
+                    const int ja = rem ? (__ffs(rem) - 1) : nb;
+                    for (; j + 4 <= ja; j += 4) {   // x == 0 run: only the importance decays
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) A.ci = __fmaf_rn(beta2, A.ci, zterm);
+                    }
+                    for (; j < ja; ++j) A.ci = __fmaf_rn(beta2, A.ci, zterm);
+                    if (ja >= nb) break;
+                    rem &= rem - 1u;
+                    const float iv = xb[ja];
+                    step(A, dys[lane][ja], iv);
+                    ++seg;
+                    cws[seg][lane] = A.cw;
+                    j = ja + 1;
+                    if (seg == kU2K) { s1 = j; break; }
+                }
+                __syncwarp();
+                // dx over this sub-block's samples, synapses in stored order
+                if (lane >= s0 && lane < s1) {
+                    const unsigned m = bnd & ((2u << lane) - 1u) & ~((1u << s0) - 1u);
+                    const float* cwrow = cws[__popc(m)];
+                    if (nA == 32) {
+#pragma unroll
+                        for (int l = 0; l < 32; l += 4) {
+                            const float4 w = *reinterpret_cast<const float4*>(cwrow + l);
+                            a = __fmaf_rn(w.x, dys[l][lane], a);
+                            a = __fmaf_rn(w.y, dys[l + 1][lane], a);
+                            a = __fmaf_rn(w.z, dys[l + 2][lane], a);
+                            a = __fmaf_rn(w.w, dys[l + 3][lane], a);
+                        }
+                    } else {
+                        for (int l = 0; l < nA; ++l) a = __fmaf_rn(cwrow[l], dys[l][lane], a);
+                    }
+                }
+                __syncwarp();
+                s0 = s1;
+            }
+#pragma unroll
+            for (int k = 0; k < NB; ++k)
+                if (blk == k) acc[k] = a;
+        }
+        if (lane < nA) finish(A, e0 + lane);
+    }
+#pragma unroll
+    for (int k = 0; k < NB; ++k) {
+        const int t = k * 32 + lane;
+        if (t < B) dxr[t] = acc[k];
+    }
+    // value_scale update (linear_disldo.hpp:901-925)
+#pragma unroll
+    for (int k = 0; k < RANK; ++k) {
+        sgs[k] = warp_sum(sgs[k]);
+        sgc[k] = warp_sum(sgc[k]);
+    }
+    if (lane == 0) {
+        const float scale_eff_lr = __fdiv_rn(P.lr, (float)nnz);
+#pragma unroll
+        for (int k = 0; k < RANK; ++k) {
+            const int64_t i = r * RANK + k;
+            rmsprop_scale(L.vs + i, L.vsi + i, (float)sgs[k], scale_eff_lr, (float)sgc[k], L.vstep + i, P);
+        }
+    }
+    l1d = warp_sum(l1d);
+    l2d = warp_sum(l2d);
+    const bool any_nan = __any_sync(0xffffffffu, st_nan);
+    for (int o = 16; o > 0; o >>= 1) mx_new = fmaxf(mx_new, __shfl_xor_sync(0xffffffffu, mx_new, o));
+    if (lane == 0) {
+        const double nan = __longlong_as_double(0x7ff8000000000000LL);
+        atomicAdd(P.stats + 0, any_nan ? nan : 0.5 * (double)l1d);
+        atomicAdd(P.stats + 1, any_nan ? nan : 0.25 * (double)l2d);
+        atomicMax(reinterpret_cast<unsigned int*>(P.stat_max), __float_as_uint(mx_new));
+    }
+}
+
+template <bool STOCH, bool OST, int RANK>
+static void launch_tiled_nb(const LayerView& L, const float* xT, const float* dyT, int B, const UpdateParams& P,
+                            float* dxT, cudaStream_t s) {
+    const unsigned g = (unsigned)((L.n_in + kU2Warps - 1) / kU2Warps);
+    if (B <= 64) k_backward_update_tiled<STOCH, OST, RANK, 2><<<g, kU2Warps * 32, 0, s>>>(L, xT, dyT, B, P, dxT);
+    else k_backward_update_tiled<STOCH, OST, RANK, 4><<<g, kU2Warps * 32, 0, s>>>(L, xT, dyT, B, P, dxT);
+}
+
+template <bool STOCH, bool OST>
+static void launch_tiled_rank(const LayerView& L, const float* xT, const float* dyT, int B, const UpdateParams& P,
+                              float* dxT, cudaStream_t s) {
+    switch (L.rank) {
+    case 1: launch_tiled_nb<STOCH, OST, 1>(L, xT, dyT, B, P, dxT, s); break;
+    case 2: launch_tiled_nb<STOCH, OST, 2>(L, xT, dyT, B, P, dxT, s); break;
+    case 3: launch_tiled_nb<STOCH, OST, 3>(L, xT, dyT, B, P, dxT, s); break;
+    default: launch_tiled_nb<STOCH, OST, 4>(L, xT, dyT, B, P, dxT, s); break;
+    }
+}
+
+void launch_backward_update_tiled(const LayerView& L, const float* xT, const float* dyT, int B, const UpdateParams& P,
+                                  float* dxT, cudaStream_t s) {
+    if (L.n_in == 0) return;
+    if (P.stochastic) {
+        if (P.os_trainable) launch_tiled_rank<true, true>(L, xT, dyT, B, P, dxT, s);
+        else launch_tiled_rank<true, false>(L, xT, dyT, B, P, dxT, s);
+    } else {
+        if (P.os_trainable) launch_tiled_rank<false, true>(L, xT, dyT, B, P, dxT, s);
+        else launch_tiled_rank<false, false>(L, xT, dyT, B, P, dxT, s);
+    }
+    count_launch();
+}
+
+}  // namespace sili

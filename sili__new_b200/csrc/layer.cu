@@ -127,6 +127,7 @@ struct sili_layer {
     float st_vmax = 0.f, st_imax = 0.f, max_abs_decay = 1.f;
     DBuf<double> d_st;             // pending importance l1/l2 deltas
     DBuf<float> d_stmax;
+    DBuf<unsigned long long> d_dyflag;   // = call tag when that call's dy held an inf or NaN
     bool st_pending = false;
     // derived index
     bool aux_dirty = true;
@@ -647,7 +648,7 @@ int make_layer(int n_in, int n_out, int max_weights, int device, int stochastic,
     chk(alloc_scales(h));
     chk(h->is.reserve(n_in + 1)); chk(h->ois.reserve(n_out + 1));
     chk(h->in_acc.reserve(n_in + 1)); chk(h->grad_acc.reserve(n_out + 1)); chk(h->out_degree.reserve(n_out + 1));
-    chk(h->d_st.reserve(2)); chk(h->d_stmax.reserve(1));
+    chk(h->d_st.reserve(2)); chk(h->d_stmax.reserve(1)); chk(h->d_dyflag.reserve(1));
     if (rc) { delete h; return rc; }
     cudaStream_t s = h->stream;
     launch_fill_scale_default(h->vs.p, 0, (int64_t)n_in, 1, s);
@@ -664,6 +665,7 @@ int make_layer(int n_in, int n_out, int max_weights, int device, int stochastic,
     cudaMemsetAsync(h->out_degree.p, 0, (size_t)(n_out + 1) * 4, s);
     cudaMemsetAsync(h->d_st.p, 0, 2 * sizeof(double), s);
     cudaMemsetAsync(h->d_stmax.p, 0, sizeof(float), s);
+    cudaMemsetAsync(h->d_dyflag.p, 0, sizeof(unsigned long long), s);
     // empty delta-CSR with per-row headroom (cpu_backend.cpp:380-389)
     h->idx_budget = (int64_t)max_weights * 8 + 4096;
     h->val_budget = (int64_t)max_weights + 64;
@@ -1231,7 +1233,8 @@ int sili_layer_backward_dense(sili_layer* h, const float* x, const float* dy, in
     launch_transpose(dyd, h->dyT.p, batch, n_out, s);
     // accumulators, linear_disldo.hpp:515-520
     launch_accum_abs_t(h->xT.p, h->in_acc.p, batch, n_in, s);
-    launch_accum_abs(dyd, h->grad_acc.p, batch, n_out, s);
+    const unsigned long long dy_tag = (unsigned long long)h->call + 1;   // never 0, the flag's initial value
+    launch_accum_abs(dyd, h->grad_acc.p, batch, n_out, s, h->d_dyflag.p, dy_tag);
     const bool dev_out = is_device_ptr(dx);
     float* dxd = dx;
     if (!dev_out) {
@@ -1254,6 +1257,8 @@ int sili_layer_backward_dense(sili_layer* h, const float* x, const float* dy, in
         UpdateParams P = update_params(h, lr, flags, beta2, eps);
         P.stochastic = h->stochastic;
         P.os_trainable = h->os_trainable;
+        P.dy_flag = h->d_dyflag.p;
+        P.dy_tag = dy_tag;
         h->call++;
         if (h->os_trainable) {
             CK(cudaMemsetAsync(h->colg.p, 0, (size_t)n_out * h->rank * 4, s));

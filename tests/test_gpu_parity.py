@@ -155,6 +155,32 @@ def test_backward_update_vs_oracle(S, B, lr, flags):
             assert np.array_equal(sg[k], so[k][: len(sg[k])] if k.endswith("_end") else so[k]), f"step {step}: {k}"
 
 
+@pytest.mark.parametrize("B,dense_x", [(128, True), (64, True), (33, True), (64, False), (130, False)])
+def test_backward_update_chunks_and_dense_x(S, B, dense_x):
+    """Rows of 70 synapses (two full 32-synapse chunks and a partial one);
+    dense x makes every sample change every weight, so a 32-sample block
+    holds more weight changes than the kernel keeps history for at once and
+    is processed in parts.  B = 130 takes the kernel for batches above 128."""
+    n_in, n_out = 96, 400
+    p, i, w, vs = random_layer(n_in, n_out, 70, seed=B, empty_rows=(5,))
+    g = setup_layer(S.SparseLinearLayerDeterministic(n_in, n_out, len(i) * 2), p, i, w, vs, imp_scale=0.01 / 6)
+    o = setup_layer(O.OracleLayer(n_in, n_out, len(i) * 2), p, i, w, vs, imp_scale=0.01 / 6)
+    rng = np.random.default_rng(B + dense_x)
+    for step in range(2):
+        x = rng.normal(0, 1, (B, n_in)).astype(np.float32) if dense_x else relu_sparse_x(rng, B, n_in)
+        dy = rng.normal(0, 1, (B, n_out)).astype(np.float32)
+        g.forward_dense(x)
+        o.forward_dense(x)
+        dxg = g.backward_dense(dy, 0.01, True, True)
+        dxo = o.backward_dense(dy, 0.01, True, True)
+        assert np.array_equal(dxg, dxo), f"step {step}: dx differs"
+        sg, so = snapshot(g), snapshot(o)
+        for k in ("live_idx", "live_val", "sc_value_scale", "sc_value_scale_importance", "sc_value_scale_step"):
+            assert np.array_equal(sg[k], so[k]), f"step {step}: {k}"
+        # importance l1 / l2 / max (the value statistics are set at load)
+        assert np.array_equal(sg["stats"].astype(np.float32)[3:], so["stats"].astype(np.float32)[3:]), f"step {step}"
+
+
 def test_stochastic_rounding_unbiased(S):
     """Stochastic layer: codes differ from the deterministic layer only by
     unbiased rounding -- the mean decoded weight over many synapses matches."""
