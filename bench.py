@@ -140,16 +140,17 @@ def peaks():
         return 6650.0, "fallback"
 
 
-def traffic_from_profile():
-    """Per-launch DRAM bytes of the backward update kernel from the committed
-    ncu summary (profiles/*.json written from an ncu capture), or None."""
-    for f in sorted(glob.glob(os.path.join(ROOT, "profiles", "*traffic*.json"))):
-        try:
-            d = json.load(open(f))
-            return d.get("k_backward_update_bytes_per_launch")
-        except (OSError, ValueError):
-            continue
-    return None
+BWD_KERNEL = "k_backward_update_tiled"
+
+
+def kernel_profile():
+    """The committed ncu summary of the backward update kernel
+    (profiles/<kernel>_config2.json, from one ncu capture), or {}."""
+    try:
+        with open(os.path.join(ROOT, "profiles", BWD_KERNEL + "_config2.json")) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return {}
 
 
 # ── CPU reference (the reference's own C++/OpenMP build) ────────────────────
@@ -398,6 +399,13 @@ def main():
     # dominant kernel: the fused backward/update
     bwd_kernel_bytes = bwd_b
     achieved = bwd_kernel_bytes / (bwd_ms * 1e-3) / 1e9
+    prof = kernel_profile()
+    issue = None
+    if prof.get("warp_instructions_per_launch") and clk and clk.get("sm_mhz"):
+        peak_inst = 148 * 4 * clk["sm_mhz"] * 1e6
+        got = prof["warp_instructions_per_launch"] / (bwd_ms * 1e-3)
+        issue = {"achieved_warp_inst_per_s": got, "peak_warp_inst_per_s": peak_inst, "frac": got / peak_inst,
+                 "warp_inst_per_launch": prof["warp_instructions_per_launch"]}
 
     # ── end to end through the public API with pinned host buffers ─────────
     hx = [torch.from_numpy(x_np).pin_memory() for _ in range(2)]
@@ -461,9 +469,13 @@ def main():
                    "layers_rotated": args.layers, "l2": "inputs larger than L2 (16 layer copies rotated)",
                    "parallelism": f"replicas x{world}", "bytes_per_step": step_bytes,
                    "forward_kernel_ms": fwd_ms, "backward_kernel_ms": bwd_ms},
-        "roofline": {"bound": "hbm", "kernel": "k_backward_update", "achieved": achieved, "peak": hbm_peak,
+        "roofline": {"bound": "hbm", "kernel": BWD_KERNEL, "achieved": achieved, "peak": hbm_peak,
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / hbm_peak,
-                     "traffic": traffic_from_profile(), "algorithmic_bytes_per_launch": bwd_kernel_bytes},
+                     "traffic": prof.get("dram_bytes_per_launch"), "algorithmic_bytes_per_launch": bwd_kernel_bytes,
+                     # the kernel is issue-bound (a sequential per-sample recurrence per synapse):
+                     # warp instructions per launch (ncu) / the bench's kernel time, against
+                     # 148 SMs x 4 schedulers x 1 warp instruction per cycle at the sampled clock
+                     "issue": issue},
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": BATCH * (N_IN + N_OUT) * 4,
                 "d2h_bytes_per_step": BATCH * (N_IN + N_OUT) * 4},

@@ -48,14 +48,15 @@ __global__ void k_accum_abs(const float* __restrict__ x, float* __restrict__ acc
     const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (j >= n) return;
     float a = acc[j];
-    bool bad = false;
-    for (int b = 0; b < B; ++b) {
-        const float v = fabsf(x[(int64_t)b * n + j]);
-        bad |= !(v <= 3.402823466e38f);
-        a = __fadd_rn(a, v);
-    }
+    const bool was_finite = isfinite(a);
+    for (int b = 0; b < B; ++b) a = __fadd_rn(a, fabsf(x[(int64_t)b * n + j]));
     acc[j] = a;
-    if (bad && nonfinite) *nonfinite = tag;
+    if (!nonfinite || isfinite(a)) return;   // a finite sum of |x| has only finite terms
+    // a non-finite sum: an inf or NaN term, a sum that was already non-finite,
+    // or an overflow of finite terms (which only costs the update its fast path)
+    bool bad = was_finite;
+    for (int b = 0; b < B && !bad; ++b) bad = !(fabsf(x[(int64_t)b * n + j]) <= 3.402823466e38f);
+    if (bad) *nonfinite = tag;
 }
 void launch_accum_abs(const float* x, float* acc, int B, int64_t n, cudaStream_t s, unsigned long long* nonfinite,
                       unsigned long long tag) {
