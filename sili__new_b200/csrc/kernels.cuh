@@ -37,6 +37,8 @@ struct LayerView {
     const int* crow;     // their rows, ascending within a column; padding: row n_in (the zero input row)
     const int* cvpos;    // their positions in val[]; padding: -1 (weight 0)
     const int* b4_nt = nullptr;  // [ceil(n_in/4)] block4 tiles per block-row (null: no block4)
+    const int* colptr_x = nullptr;  // [n_out+1] exact (unpadded) column offsets of the same CSC
+    const int* cpack = nullptr;     // per padded CSC entry: row << 4 | weight code (padding: n_in << 4)
 };
 
 // One layer's block4 store (4x4 dense FP4 tiles, block4.hpp:1016-1490) on the
@@ -95,6 +97,15 @@ void launch_forward(const LayerView& L, const float* xT, int B, float* y, bool s
 // dense backward at lr == 0: dx [B, n_in] from dyT [n_out, B] (bit-exact order)
 void launch_backward_dx(const LayerView& L, const float* dyT, int B, float* dx, cudaStream_t s);
 // dense backward at lr != 0: fused per-synapse update + dxT [n_in, B]
+// The forward with x rows staged in shared memory per row tile (kernels_forward.cu):
+// needs L.cpack and L.colptr_x; returns false (launching nothing) when the
+// shape is better served by launch_forward.
+bool launch_forward_rows(const LayerView& L, const float* xT, int B, float* y, bool sparse_formula,
+                         cudaStream_t s);
+// whether launch_forward_rows would run for this shape (it needs L.cpack)
+bool forward_rows_applies(const LayerView& L, int B);
+// L.cpack from crow / cvpos / val over the padded CSC (its length is colptr[n_out])
+void launch_pack_csc(const LayerView& L, int64_t bound, int* cpack, cudaStream_t s);
 void launch_backward_update(const LayerView& L, const float* xT, const float* dyT, int B,
                             const UpdateParams& P, float* dxT, cudaStream_t s);
 // the same for B <= 128 (kernels_update.cu); launch_backward_update calls it

@@ -133,6 +133,8 @@ struct sili_layer {
     bool aux_dirty = true;
     DBuf<int> rowptr, abs_cols, frow, fvpos, colcount, colptr, crow, cvpos, sort_k, sort_ko, sort_v, sort_vo;
     DBuf<int> colptr_x, padcnt;   // exact column offsets, padded counts
+    DBuf<int> cpack;              // packed CSC (row << 4 | weight code) for the row-tiled forward
+    bool pack_valid = false;      // cpack matches the current weight codes
     DBuf<uint8_t> cub_tmp;
     // scratch
     DBuf<float> xT, dyT, dxT, colg, colc, ytmp, x_stage, dy_stage, dx_stage;
@@ -335,6 +337,27 @@ int ensure_aux(sili_layer* h, cudaStream_t s) {
         for (int64_t r = 0; r < R; ++r) if (rp[r + 1] == rp[r]) { h->has_dead_rows = true; break; }
     }
     h->aux_dirty = false;
+    h->pack_valid = false;
+    return SILI_OK;
+}
+
+// The dense / sparse-formula forward over xT: the row-tiled kernel (x staged
+// in shared memory, packed column index rebuilt here when the weight codes
+// changed) where its shape rules allow, else the per-synapse gather kernels.
+int forward_columns(sili_layer* h, const float* xT, int batch, float* y, bool sparse, cudaStream_t s) {
+    LayerView v = h->view();
+    if (forward_rows_applies(v, batch)) {
+        const int64_t bound = std::max<int64_t>(h->total_nnz, 1) + 7 * h->cols + 8;   // padded CSC bound
+        if (!h->pack_valid) {
+            RC(h->cpack.reserve(bound));
+            launch_pack_csc(v, bound, h->cpack.p, s);
+            h->pack_valid = true;
+        }
+        v.cpack = h->cpack.p;
+        v.colptr_x = h->colptr_x.p;
+        if (launch_forward_rows(v, xT, batch, y, sparse, s)) return SILI_OK;
+    }
+    launch_forward(v, xT, batch, y, sparse, s);
     return SILI_OK;
 }
 
@@ -1056,6 +1079,7 @@ int sili_layer_set_value_bytes(sili_layer* h, const uint8_t* values, int64_t n) 
     RC(use(h));
     n = std::min<int64_t>(n, h->val_n);
     RC(to_dev(values, h->val.p, (size_t)n, h->stream));
+    h->pack_valid = false;
     CK(cudaStreamSynchronize(h->stream));
     return SILI_OK;
 }
@@ -1179,6 +1203,7 @@ int sili_layer_rescale_row(sili_layer* h, int kind, int row, float new_scale) {
     RC(sili_layer_get_scale(h, kind, row, 0, &old));
     if (new_scale == old) return SILI_OK;
     launch_rescale_row(h->view(), row, old, new_scale, kind == SILI_SCALE_VALUE, h->stream);
+    h->pack_valid = false;
     CK(cudaGetLastError());
     return sili_layer_set_scale(h, kind, row, 0, new_scale);
 }
@@ -1200,7 +1225,7 @@ int sili_layer_forward_dense(sili_layer* h, const float* x, int batch, float* y,
         yd = h->ytmp.p;
     }
     if (h->timing) CK(cudaEventRecord(h->ev[0], s));
-    launch_forward(h->view(), h->xT.p, batch, yd, false, s);
+    RC(forward_columns(h, h->xT.p, batch, yd, false, s));
     if (h->b4_ntiles > 0) {
         RC(ensure_b4_index(h, s));
         launch_b4_forward(h->view(), h->b4view(), h->xT.p, batch, yd, s);
@@ -1260,6 +1285,7 @@ int sili_layer_backward_dense(sili_layer* h, const float* x, const float* dy, in
         P.dy_flag = h->d_dyflag.p;
         P.dy_tag = dy_tag;
         h->call++;
+        h->pack_valid = false;   // the update rewrites weight codes
         if (h->os_trainable) {
             CK(cudaMemsetAsync(h->colg.p, 0, (size_t)n_out * h->rank * 4, s));
             CK(cudaMemsetAsync(h->colc.p, 0, (size_t)n_out * h->rank * 4, s));
@@ -1316,7 +1342,7 @@ int sili_layer_forward_sparse(sili_layer* h, const int* ptrs, const int* idx, co
         RC(h->ytmp.reserve((int64_t)batch * n_out + 1));
         yd = h->ytmp.p;
     }
-    if (h->total_nnz > 0) launch_forward(h->view(), h->xT.p, batch, yd, true, s);
+    if (h->total_nnz > 0) RC(forward_columns(h, h->xT.p, batch, yd, true, s));
     else CK(cudaMemsetAsync(yd, 0, (size_t)batch * n_out * 4, s));
     if (h->b4_ntiles > 0) {
         RC(ensure_b4_index(h, s));
@@ -1363,6 +1389,7 @@ int sili_layer_backward_sparse(sili_layer* h, const float* x, const int* dptrs, 
     RC(ensure_pow_table(h, beta2, (uint32_t)(h->call + 2)));
     UpdateParams P = update_params(h, lr, flags, beta2, eps);
     h->call++;
+    if (lr != 0.0f) h->pack_valid = false;
     LayerView v = h->view();
     if (h->total_nnz > 0) {
         launch_backward_sparse(v, h->xT.p, h->dyT.p, h->presT.p, batch, P, h->sgs.p, h->sgc.p, h->dxT.p, s);

@@ -133,6 +133,43 @@ def test_forward_vs_oracle(S, B):
         assert_close_sum(yg, yo, 1e-5)
 
 
+@pytest.mark.parametrize("n_in,n_out,B", [(700, 40000, 32), (1100, 20000, 64), (1300, 80000, 36),
+                                          (520, 20000, 100)])
+def test_forward_row_tiles_vs_oracle(S, n_in, n_out, B):
+    """Shapes wide enough for the forward that stages x rows in shared memory
+    (tiles of 512 rows, one thread per column): bit-exact, including after a
+    weight update and a row rescale (the packed column index is rebuilt) and
+    with a non-finite weight (x == 0 inputs skipped)."""
+    p, i, w, vs = random_layer(n_in, n_out, 40, seed=n_in + B, empty_rows=(1, n_in - 1))
+    g = setup_layer(S.SparseLinearLayerDeterministic(n_in, n_out, len(i) * 2), p, i, w, vs, imp_scale=0.01 / 6)
+    o = setup_layer(O.OracleLayer(n_in, n_out, len(i) * 2), p, i, w, vs, imp_scale=0.01 / 6)
+    rng = np.random.default_rng(B)
+    x = relu_sparse_x(rng, B, n_in)
+    assert np.array_equal(g.forward_dense(x), o.forward_dense(x)), "forward"
+    dy = rng.normal(0, 1, (B, n_out)).astype(np.float32)
+    assert np.array_equal(g.backward_dense(dy, 0.01, True), o.backward_dense(dy, 0.01, True)), "dx"
+    x = relu_sparse_x(rng, B, n_in)
+    assert np.array_equal(g.forward_dense(x), o.forward_dense(x)), "forward after the update"
+    for L in (g, o):
+        L.rescale_value_row(5, 0.7 * float(vs[5]))
+    assert np.array_equal(g.forward_dense(x), o.forward_dense(x)), "forward after rescale_value_row"
+    for L in (g, o):
+        L.set_value_scale_raw(7, float("inf"))
+    yg, yo = g.forward_dense(x), o.forward_dense(x)
+    assert np.array_equal(yg, yo, equal_nan=True), "forward with an infinite value_scale row"
+
+
+def test_sparse_forward_row_tiles_vs_oracle(S):
+    n_in, n_out, B = 600, 40000, 32
+    p, i, w, vs = random_layer(n_in, n_out, 30, seed=3)
+    g = setup_layer(S.SparseLinearLayerDeterministic(n_in, n_out, len(i) * 2), p, i, w, vs)
+    o = setup_layer(O.OracleLayer(n_in, n_out, len(i) * 2), p, i, w, vs)
+    rng = np.random.default_rng(4)
+    x = relu_sparse_x(rng, B, n_in)
+    px, ix, vx = O.dense_to_csr(x, 0.0)
+    assert np.array_equal(g.forward_sparse(px, ix, vx, B), o.forward_sparse(px, ix, vx, B))
+
+
 @pytest.mark.parametrize("B,lr,flags", [(64, 0.01, (True, True)), (40, 0.05, (False, True)),
                                         (7, 0.02, (True, False)), (96, 0.01, (True, True))])
 def test_backward_update_vs_oracle(S, B, lr, flags):
