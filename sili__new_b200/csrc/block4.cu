@@ -234,10 +234,24 @@ void launch_b4_dx(const LayerView& L, const B4View& V, const float* dyT, int B, 
 }
 
 // Block4Store::merge_row_workspace (block4.hpp:1368-1465) for one block-row,
-// run by its half-warp: while the packed bytes exceed the row's tile
-// allocation, zero the live slot of smallest |importance * importance_scale *
-// output_importance_scale| (first in tile, li, lj order on ties) and repack
-// that tile; then count tiles that still do not fit.
+// run by its half-warp.  The reference, while the packed bytes exceed the
+// row's tile allocation, scans the row in (tile, li, lj) order for the live
+// slot of smallest a = |importance * importance_scale * output_importance_
+// scale| (the first live slot, replaced only by a strictly smaller a), zeroes
+// it and repacks that tile.  Zeroing a slot changes no other slot's a, so
+// without NaN importances the evictions are the live slots in ascending
+// (a, tile, li, lj) order, stopped as soon as the row fits: here they are
+// taken a level (one value of a) at a time, 16 tiles per step with a prefix
+// sum of the tiles' byte savings, which gives the same slots, repacking and
+// counters in O(levels x tiles) instead of O(evictions x tiles).  A NaN
+// importance changes the reference's scan (a NaN first live slot is taken,
+// later ones never are), so a row holding one is evicted one slot at a time
+// exactly as the reference does.  Then tiles that still do not fit are
+// counted.
+__device__ __forceinline__ double b4_abs_imp(const LayerView& L, uint32_t byte, int64_t r, int64_t c) {
+    return fabs((double)fp4_decode(byte >> 4) * (double)L.is[r] * (double)L.ois[c]);
+}
+
 __device__ void b4_evict_row(const LayerView& L, const B4View& V, int64_t br, int64_t base, int nt, int s,
                              unsigned hmask) {
     const int64_t cap = V.alloc[V.BR + br];
@@ -245,41 +259,123 @@ __device__ void b4_evict_row(const LayerView& L, const B4View& V, int64_t br, in
     for (int e = s; e < nt; e += 16) used += tile_len(tile_live(V.tile[base + e]), V.sparse[base + e] != 0);
 #pragma unroll
     for (int o = 8; o > 0; o >>= 1) used += __shfl_xor_sync(hmask, used, o);
-    while (used > cap) {
-        double best = -1.0;
-        long long best_key = -1;
-        for (int e = s; e < nt; e += 16) {
+    if (used > cap) {
+        bool nan_here = false;
+        for (int e = s; e < nt && !nan_here; e += 16) {
             const uint4 tw = V.tile[base + e];
             const int64_t c0 = (int64_t)V.bc[base + e] * 4;
-            for (int l_i = 0; l_i < 4; ++l_i)
-                for (int l_j = 0; l_j < 4; ++l_j) {
-                    const uint32_t byte = tile_byte(tw, l_j * 4 + l_i);
-                    if (byte == 0) continue;
-                    const int64_t r = br * 4 + l_i, c = c0 + l_j;
-                    const double ti = (double)fp4_decode(byte >> 4) * (double)L.is[r] * (double)L.ois[c];
-                    const double a = fabs(ti);
-                    const long long key = (long long)e * 16 + l_i * 4 + l_j;
-                    if (best < 0.0 || a < best) { best = a; best_key = key; }
+            for (int q = 0; q < 16; ++q) {
+                const uint32_t byte = tile_byte(tw, q);
+                if (byte != 0 && isnan(b4_abs_imp(L, byte, br * 4 + (q & 3), c0 + (q >> 2)))) nan_here = true;
+            }
+        }
+        if (__any_sync(hmask, nan_here)) {
+            // the reference's scan, one eviction at a time (lane 0)
+            if (s == 0) {
+                while (used > cap) {
+                    double best = -1.0;
+                    int be = -1, bq = 0;
+                    for (int e = 0; e < nt; ++e) {
+                        const uint4 tw = V.tile[base + e];
+                        const int64_t c0 = (int64_t)V.bc[base + e] * 4;
+                        for (int l_i = 0; l_i < 4; ++l_i)
+                            for (int l_j = 0; l_j < 4; ++l_j) {
+                                const uint32_t byte = tile_byte(tw, l_j * 4 + l_i);
+                                if (byte == 0) continue;
+                                const double av = b4_abs_imp(L, byte, br * 4 + l_i, c0 + l_j);
+                                if (best < 0.0 || av < best) { best = av; be = e; bq = l_j * 4 + l_i; }
+                            }
+                    }
+                    if (be < 0) break;   // nothing live left
+                    uint4 tw = V.tile[base + be];
+                    const int old_len = tile_len(tile_live(tw), V.sparse[base + be] != 0);
+                    set_tile_byte(tw, bq, 0u);
+                    const int live = tile_live(tw);
+                    const bool sp = (uint32_t)live <= V.switch_point;
+                    used -= old_len - tile_len(live, sp);
+                    V.tile[base + be] = tw;
+                    V.sparse[base + be] = sp ? 1 : 0;
                 }
-        }
+            }
+            used = __shfl_sync(hmask, used, (threadIdx.x & 16));
+            __syncwarp(hmask);
+        } else {
+            while (used > cap) {
+                // the smallest a among the live slots
+                double amin = -1.0;
+                for (int e = s; e < nt; e += 16) {
+                    const uint4 tw = V.tile[base + e];
+                    const int64_t c0 = (int64_t)V.bc[base + e] * 4;
+                    for (int q = 0; q < 16; ++q) {
+                        const uint32_t byte = tile_byte(tw, q);
+                        if (byte == 0) continue;
+                        const double av = b4_abs_imp(L, byte, br * 4 + (q & 3), c0 + (q >> 2));
+                        if (amin < 0.0 || av < amin) amin = av;
+                    }
+                }
 #pragma unroll
-        for (int o = 8; o > 0; o >>= 1) {
-            const double ob = __shfl_xor_sync(hmask, best, o);
-            const long long ok = __shfl_xor_sync(hmask, best_key, o);
-            const bool take = ob >= 0.0 && (best < 0.0 || ob < best || (ob == best && ok < best_key));
-            if (take) { best = ob; best_key = ok; }
+                for (int o = 8; o > 0; o >>= 1) {
+                    const double ob = __shfl_xor_sync(hmask, amin, o);
+                    if (ob >= 0.0 && (amin < 0.0 || ob < amin)) amin = ob;
+                }
+                if (amin < 0.0) break;   // nothing live left
+                // its slots in (tile, li, lj) order, 16 tiles per step, while the row does not fit
+                for (int e0 = 0; e0 < nt && used > cap; e0 += 16) {
+                    const int e = e0 + s;
+                    uint4 tw = make_uint4(0u, 0u, 0u, 0u);
+                    int live = 0, k = 0, old_len = 0;
+                    int64_t c0 = 0;
+                    if (e < nt) {
+                        tw = V.tile[base + e];
+                        c0 = (int64_t)V.bc[base + e] * 4;
+                        live = tile_live(tw);
+                        old_len = tile_len(live, V.sparse[base + e] != 0);
+                        for (int q = 0; q < 16; ++q) {
+                            const uint32_t byte = tile_byte(tw, q);
+                            if (byte != 0 && b4_abs_imp(L, byte, br * 4 + (q & 3), c0 + (q >> 2)) == amin) ++k;
+                        }
+                    }
+                    auto saving = [&](int j) {   // bytes saved by evicting j of this tile's level slots
+                        const int lv = live - j;
+                        return (long long)(old_len - tile_len(lv, (uint32_t)lv <= V.switch_point));
+                    };
+                    const long long d = k > 0 ? saving(k) : 0;
+                    long long incl = d;
+#pragma unroll
+                    for (int o = 1; o < 16; o <<= 1) {
+                        const long long t = __shfl_up_sync(hmask, incl, o, 16);
+                        if (s >= o) incl += t;
+                    }
+                    const long long excl = incl - d, need = used - cap;
+                    int take = 0;
+                    if (k > 0 && excl < need) {
+                        take = k;
+                        for (int j = 1; j < k; ++j)
+                            if (excl + saving(j) >= need) { take = j; break; }
+                    }
+                    long long applied = 0;
+                    if (take > 0) {
+                        int left = take;
+                        for (int l_i = 0; l_i < 4 && left > 0; ++l_i)
+                            for (int l_j = 0; l_j < 4 && left > 0; ++l_j) {
+                                const int q = l_j * 4 + l_i;
+                                const uint32_t byte = tile_byte(tw, q);
+                                if (byte != 0 && b4_abs_imp(L, byte, br * 4 + l_i, c0 + l_j) == amin) {
+                                    set_tile_byte(tw, q, 0u);
+                                    --left;
+                                }
+                            }
+                        const int lv = tile_live(tw);
+                        V.tile[base + e] = tw;
+                        V.sparse[base + e] = (uint32_t)lv <= V.switch_point ? 1 : 0;
+                        applied = saving(take);
+                    }
+#pragma unroll
+                    for (int o = 8; o > 0; o >>= 1) applied += __shfl_xor_sync(hmask, applied, o);
+                    used -= applied;
+                }
+            }
         }
-        if (best < 0.0) break;   // nothing live left
-        const int e = (int)(best_key / 16), l_i = (int)((best_key / 4) % 4), l_j = (int)(best_key % 4);
-        const int64_t ti = base + e;
-        uint4 tw = V.tile[ti];
-        const int old_len = tile_len(tile_live(tw), V.sparse[ti] != 0);
-        set_tile_byte(tw, l_j * 4 + l_i, 0u);
-        const int live = tile_live(tw);
-        const bool sp = (uint32_t)live <= V.switch_point;
-        used -= old_len - tile_len(live, sp);
-        __syncwarp(hmask);
-        if (s == 0) { V.tile[ti] = tw; V.sparse[ti] = sp ? 1 : 0; }
         __syncwarp(hmask);
     }
     if (s == 0) {

@@ -120,6 +120,40 @@ def test_block4_eviction_after_compact():
     assert o.b4_view()[1] < live0, "the case evicts"
 
 
+@pytest.mark.parametrize("nan_imp", [False, True])
+def test_block4_mass_eviction(nan_imp):
+    """Sparse tiles that all grow live slots in one update (the config-2
+    matrix loaded as block4): rows of 256 tiles evict thousands of slots over
+    many importance levels (per-row and per-column importance scales), in the
+    reference's order.  With NaN importance codes present the reference's
+    scan rule for NaN decides instead."""
+    n_in, n_out = 64, 1024
+    rng = np.random.default_rng(11 + nan_imp)
+    wc, ic = _codes(rng, n_in, n_out, 0.05, imp_frac=0.0)
+    if nan_imp:
+        nz = np.argwhere(wc > 0)
+        pick = nz[rng.choice(len(nz), 40, replace=False)]
+        ic[pick[:, 0], pick[:, 1]] = 8
+    g, o = _pair(n_in, n_out, wc, ic)
+    for L in (g, o):
+        for r in range(n_in):
+            L.set_importance_scale_raw(r, float(0.01 * (1 + r % 5)))
+        for c in range(n_out):
+            L.set_output_importance_scale_raw(c, float(0.5 + 0.25 * (c % 3)))
+    _check_state(g, o, "load")
+    for step in range(2):
+        x = relu_sparse_x(rng, 32, n_in)
+        dy = rng.normal(0, 1, (32, n_out)).astype(np.float32)
+        assert np.array_equal(g.forward_dense(x), o.forward_dense(x), equal_nan=True), f"step {step}: forward"
+        assert np.array_equal(g.backward_dense(dy, 0.02, True), o.backward_dense(dy, 0.02, True),
+                              equal_nan=True), f"step {step}: dx"
+        _check_state(g, o, f"step {step}")
+    # every row is active in some sample, so without eviction nearly all
+    # 16 slots of every tile would be live after an update
+    tiles, live = o.b4_view()[0], o.b4_view()[1]
+    assert live < 0.2 * 16 * tiles, "the case evicts"
+
+
 def test_block4_stochastic_matches_oracle():
     n_in, n_out = 120, 124
     rng = np.random.default_rng(9)
