@@ -204,6 +204,82 @@ def run_reference_cpu(work, budget_s, threads, max_steps=None):
     return el / n, n, variant
 
 
+def block4_codes(work):
+    """config 2's matrix as dense FP4 codes [n_in, n_out] (the stored weights'
+    codes, importance 0): what load_dense_codes turns into block4 tiles."""
+    from sili__new_b200 import fp4_quantize_array
+    p, i, w = work[0], work[1], work[2]
+    wc = np.zeros((N_IN, N_OUT), np.uint8)
+    wc[np.repeat(np.arange(N_IN), np.diff(p)), i] = fp4_quantize_array(w)
+    return wc, np.zeros_like(wc)
+
+
+def run_block4(args, dev, S, torch, work, cpu_sample):
+    """BASELINE config 2 in the block4 format: load_dense_codes makes a tile
+    for every 4x4 block of the 8192^2 matrix (4.19 M tiles, 95 % of their
+    slots empty), same x and dy; a step is forward_dense +
+    backward_dense(lr=0.01) through the public API, timed with CUDA events.
+    cpu_sample: also time the reference's own block4 CPU path on the first
+    256 input rows (its step cost is per row) and scale to the full matrix."""
+    p, i, w, vs, x, dy = work
+    wc, ic = block4_codes(work)
+    L = S.SparseLinearLayer(N_IN, N_OUT, len(i), 1, dev)
+    L.load_dense_codes(wc, ic)
+    for r in range(N_IN):
+        L.set_value_scale_raw(r, float(vs[r]))
+        L.set_importance_scale_raw(r, LR / 6.0)
+    xs = torch.from_numpy(x).cuda(dev)
+    dys = torch.from_numpy(dy).cuda(dev)
+    y = torch.empty(BATCH, N_OUT, device=f"cuda:{dev}")
+    dx = torch.empty(BATCH, N_IN, device=f"cuda:{dev}")
+    stream = torch.cuda.Stream(device=dev)
+    sh = stream.cuda_stream
+
+    def step():
+        L.forward_dense_ptr(xs.data_ptr(), BATCH, y.data_ptr(), sh)
+        L.backward_dense_ptr(dys.data_ptr(), BATCH, LR, True, True, 0.999, 1e-8, dx.data_ptr(), sh, 0)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize(dev)
+    steps = max(3, min(args.steps, 10))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / steps
+    tiles = int(L.block4.tiles)
+    # 16 B per tile read by the forward, read and written by the update, + activations
+    step_bytes = tiles * 16 * 3 + BATCH * 4 * (2 * N_IN + 2 * N_OUT + N_IN)
+    out = {"metric": "block4 format fwd+bwd effective GB/s (config 2 matrix in 4x4 FP4 tiles, batch 64)",
+           "value": step_bytes / (ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms, "steps": steps,
+           "tiles": tiles, "live_slots_at_load": int(np.count_nonzero(wc)), "bytes_per_step": step_bytes}
+    del L, xs, dys, y, dx
+    torch.cuda.empty_cache()
+    if cpu_sample:
+        mod, variant = reference_module()
+        if mod is not None:
+            rows = 256
+            threads = os.cpu_count() or 1
+            R = mod.SparseLinearLayer(rows, N_OUT, len(i), threads)
+            R.load_dense_codes(np.ascontiguousarray(wc[:rows]), np.ascontiguousarray(ic[:rows]))
+            for r in range(rows):
+                R.set_value_scale_raw(r, float(vs[r]))
+                R.set_importance_scale_raw(r, LR / 6.0)
+            xr = np.ascontiguousarray(x[:, :rows])
+            t0 = time.perf_counter()
+            R.forward_dense(xr)
+            R.backward_dense(dy, LR, lr_per_row_nnz=True)
+            per = (time.perf_counter() - t0) * (N_IN / rows)
+            out["cpu_baseline"] = {"value": step_bytes / per / 1e9, "unit": "GB/s", "ms_per_step": per * 1e3,
+                                   "cores": threads, "kind": "reference",
+                                   "sample": f"one fwd+bwd step on the first {rows} of {N_IN} input rows in block4, "
+                                             f"scaled x{N_IN // rows} (sili._cpu -march={variant})"}
+    return out
+
+
 def run_folded(args, dev, rank, world, dist, S, torch):
     """Mistral-Small-24B-shaped folded stack (hidden 5120,
     32 heads / 8 KV x 128, FFN 32768, 40 layers folded per suffix), every
@@ -288,6 +364,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-folded", action="store_true", help="skip the folded-stack (config 5) measurement")
+    ap.add_argument("--no-block4", action="store_true", help="skip the block4-format (config 2) measurement")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -447,11 +524,15 @@ def main():
                    "sample": f"{n} fwd+bwd steps of the full config-2 workload on sili._cpu "
                              f"(reference source built -march={variant}, num_cpus={threads})"}
 
+    del layers, xs, dys, ys, dxs
+    torch.cuda.empty_cache()
+    # ── the same matrix in the block4 format (config 2) ─────────────────────
+    block4 = None
+    if not args.no_block4 and world == 1:   # one layer: measured on one GPU
+        block4 = run_block4(args, dev, S, torch, work, cpu_sample=not args.no_cpu_baseline)
     # ── folded stack (config 5), sharded over the ranks ─────────────────────
     folded = None
     if not args.no_folded:
-        del layers, xs, dys, ys, dxs
-        torch.cuda.empty_cache()
         folded = run_folded(args, dev, rank, world, dist, S, torch)
 
     if dist:
@@ -481,6 +562,7 @@ def main():
                 "d2h_bytes_per_step": BATCH * (N_IN + N_OUT) * 4},
         "gpu_launches": launches,
         "clocks": clk,
+        "block4": block4,
         "folded_stack": folded,
     }
     print(json.dumps(line))
