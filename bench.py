@@ -280,6 +280,65 @@ def run_block4(args, dev, S, torch, work, cpu_sample):
     return out
 
 
+def run_synaptogenesis(args, dev, S, torch, cpu_sample):
+    """a 16384^2 layer at 98 % sparsity (328 synapses per
+    input row), batch 256, x and dy ~ N(0,1); one step = topk_dyx_step through
+    the public API on device pointers: |dy^T x| scored at all 268 M positions
+    (fp32, ascending-sample fma chains), exact top-k over the non-existing
+    ones with k = 1 % of nnz, as many smallest-|w S| synapses pruned, the
+    delta-CSR and FP4 arrays rebuilt.  The rule has no reference function, so
+    cpu_sample times the CPU restatement (oracle, kind "port") on the first
+    512 input rows and scales to 16384."""
+    from helpers import random_layer
+    n, per, B = 16384, 328, 256
+    p, i, w, vs = random_layer(n, n, per, seed=3)
+    L = S.SparseLinearLayer(n, n, int(len(i) * 1.1), 1, dev)
+    L.load_weights(p, i, w)
+    for r in range(n):
+        L.set_value_scale_raw(r, float(vs[r]))
+        L.set_importance_scale_raw(r, LR / 6.0)
+    gen = torch.Generator(device=f"cuda:{dev}")
+    gen.manual_seed(3)
+    x = torch.randn(B, n, generator=gen, device=f"cuda:{dev}")
+    dy = torch.randn(B, n, generator=gen, device=f"cuda:{dev}")
+    k = len(i) // 100
+    stream = torch.cuda.Stream(device=dev)
+    L.topk_dyx_step_ptr(x.data_ptr(), dy.data_ptr(), B, k, stream.cuda_stream)   # warm-up (first-use buffers)
+    torch.cuda.synchronize(dev)
+    steps = 3
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        L.topk_dyx_step_ptr(x.data_ptr(), dy.data_ptr(), B, k, stream.cuda_stream)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / steps
+    out = {"metric": "synaptogenesis step ms (16384^2, 98% sparse, batch 256, top-k |dy^T x| with k = 1% of nnz)",
+           "value": ms, "unit": "ms", "higher_is_better": False, "steps": steps, "nnz": int(len(i)), "k": int(k),
+           "positions_scored_per_s": n * n / (ms * 1e-3)}
+    del L, x, dy
+    torch.cuda.empty_cache()
+    if cpu_sample:
+        from oracle import oracle as O
+        rows = 512
+        sub = p[: rows + 1]
+        o = O.OracleLayer(rows, n, int(sub[-1] * 1.1))
+        o.load_weights(sub, i[: sub[-1]], w[: sub[-1]])
+        for r in range(rows):
+            o.set_value_scale_raw(r, float(vs[r]))
+            o.set_importance_scale_raw(r, LR / 6.0)
+        rng = np.random.default_rng(3)
+        xs = rng.normal(0, 1, (B, rows)).astype(np.float32)
+        dys = rng.normal(0, 1, (B, n)).astype(np.float32)
+        t0 = time.perf_counter()
+        o.topk_dyx_step(xs, dys, max(1, int(sub[-1]) // 100))
+        per_step = (time.perf_counter() - t0) * (n / rows)
+        out["cpu_baseline"] = {"value": per_step * 1e3, "unit": "ms", "cores": 1, "kind": "port",
+                               "sample": f"the rule's C restatement on the first {rows} of {n} input rows "
+                                         f"(same batch and columns), scaled x{n // rows}"}
+    return out
+
+
 def run_folded(args, dev, rank, world, dist, S, torch):
     """Mistral-Small-24B-shaped folded stack (hidden 5120,
     32 heads / 8 KV x 128, FFN 32768, 40 layers folded per suffix), every
@@ -365,6 +424,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-folded", action="store_true", help="skip the folded-stack (config 5) measurement")
     ap.add_argument("--no-block4", action="store_true", help="skip the block4-format (config 2) measurement")
+    ap.add_argument("--no-synap", action="store_true", help="skip the synaptogenesis (config 3) measurement")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -530,6 +590,10 @@ def main():
     block4 = None
     if not args.no_block4 and world == 1:   # one layer: measured on one GPU
         block4 = run_block4(args, dev, S, torch, work, cpu_sample=not args.no_cpu_baseline)
+    # ── synaptogenesis step (config 3) ──────────────────────────────────────
+    synap = None
+    if not args.no_synap and world == 1:   # one layer: measured on one GPU
+        synap = run_synaptogenesis(args, dev, S, torch, cpu_sample=not args.no_cpu_baseline)
     # ── folded stack (config 5), sharded over the ranks ─────────────────────
     folded = None
     if not args.no_folded:
@@ -563,6 +627,7 @@ def main():
         "gpu_launches": launches,
         "clocks": clk,
         "block4": block4,
+        "synaptogenesis": synap,
         "folded_stack": folded,
     }
     print(json.dumps(line))
