@@ -350,7 +350,7 @@ def run_folded(args, dev, rank, world, dist, S, torch):
     from sili__new_b200 import folded as F
     cfg = F.MISTRAL_SMALL_24B
     suffixes = F.mistral_suffixes(cfg)
-    n_folds, B, density = cfg["layers"], 32, 0.05
+    n_folds, B, density = (args.folded_layers or cfg["layers"]), 32, 0.05
     stack = F.FoldedStack(suffixes, n_folds, rank, world,
                           lambda a, b, c: S.SparseLinearLayer(a, b, c, 1, dev),
                           group=None)
@@ -403,7 +403,7 @@ def run_folded(args, dev, rank, world, dist, S, torch):
     mem_gb = torch.cuda.max_memory_allocated(dev) / 1e9
     if rank != 0:
         return None
-    return {"metric": "folded-stack decode tokens/s (Mistral-Small-24B shape, 40 layers folded, 95% pruned, "
+    return {"metric": f"folded-stack decode tokens/s (Mistral-Small-24B shape, {n_folds} layers folded, 95% pruned, "
                       "batch 32, linears only)",
             "value": B / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "scaling": "strong",
             "ms_per_step": ms, "steps": steps, "nnz": total_nnz,
@@ -425,6 +425,10 @@ def main():
     ap.add_argument("--no-folded", action="store_true", help="skip the folded-stack (config 5) measurement")
     ap.add_argument("--no-block4", action="store_true", help="skip the block4-format (config 2) measurement")
     ap.add_argument("--no-synap", action="store_true", help="skip the synaptogenesis (config 3) measurement")
+    ap.add_argument("--only", choices=["block4", "synap", "folded"],
+                    help="run one secondary measurement alone and print its object (profiling)")
+    ap.add_argument("--folded-layers", type=int, default=None,
+                    help="layers folded per suffix (default: config 5's 40; fewer for small profiling runs)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -464,6 +468,19 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device(f"cuda:{local}"))
     dev = local if world > 1 else 0
     torch.cuda.set_device(dev)
+    if args.only:
+        if args.only == "block4":
+            out = run_block4(args, dev, S, torch, make_workload(), cpu_sample=False)
+        elif args.only == "synap":
+            out = run_synaptogenesis(args, dev, S, torch, cpu_sample=False)
+        else:
+            out = run_folded(args, dev, rank, world, dist, S, torch)
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
+        if rank == 0:
+            print(json.dumps(out))
+        return 0
 
     work = make_workload()
     p, i, w, vs, x_np, dy_np = work

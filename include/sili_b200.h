@@ -17,7 +17,11 @@
  *    Host arrays are copied in / out inside the call and the call returns
  *    after the copy back; device arrays are used in place and the work is
  *    enqueued on `stream` (NULL = the layer's own stream) without a host
- *    synchronisation.
+ *    synchronisation.  Device input arrays must be complete on that stream's
+ *    timeline.  Entry points without a stream argument (setters, getters,
+ *    structural calls) work on the layer's own stream and return after it
+ *    drains; a caller that enqueued work on another stream orders the two
+ *    itself (e.g. synchronises that stream first).
  *  - Activations and gradients are fp32, row-major [batch, features].
  *  - Sizes are C int, as in the reference (S = int, cpu_backend.cpp:353).
  *

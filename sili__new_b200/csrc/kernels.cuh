@@ -241,8 +241,18 @@ void launch_exist_bits(const int* rowptr, const int* abs_cols, int64_t n_in, int
                        cudaStream_t s);
 void launch_dyx_scores(const float* x, const float* dy, int B, int64_t n_in, int64_t n_out, const uint32_t* bits,
                        int64_t words, uint32_t* keys, cudaStream_t s);
-void launch_digit_hist(const uint32_t* keys, int64_t n, int shift, uint32_t mask, uint32_t prefix, unsigned int* hist,
-                       int sms, cudaStream_t s);
+// device-side radix select state (csrc/topk.cu)
+struct SelState {
+    unsigned int prefix, mask;   // the key bits fixed so far
+    long long need;              // keys still to take at or below the prefix
+    long long eq_count;          // keys equal to the final prefix
+};
+void launch_sel_init(SelState* st, int64_t need, cudaStream_t s);
+void launch_digit_hist(const uint32_t* keys, int64_t n, int shift, const SelState* st, unsigned int* hist, int sms,
+                       cudaStream_t s);
+void launch_digit_pick(unsigned int* hist, int shift, SelState* st, cudaStream_t s);
+void launch_select_ge(const uint32_t* keys, int64_t n, const SelState* st, int64_t* out, unsigned long long* count,
+                      int64_t cap, int sms, cudaStream_t s);
 void launch_prune_keys(const LayerView& L, const float* w, uint32_t* keys, int* ids, cudaStream_t s);
 void launch_mark_drop(const int* sorted_ids, int npr, const int* abs_cols, uint8_t* drop, int* out_degree,
                       cudaStream_t s);

@@ -174,7 +174,13 @@ struct sili_layer {
         DBuf<int64_t> cand, cand_o, eq, nsel;
         DBuf<int> pid, pid_o, cptr, cnt, nptr;
         DBuf<uint8_t> drop;
+        DBuf<SelState> sel;
+        DBuf<unsigned long long> nge;
+        DBuf<int> di, nidx;            // kept across calls: no allocation per step
+        DBuf<float> dw, dm, nw, nimp;
     } topk;
+    DBuf<int> imp_len, imp_boff;       // import_csr scratch, kept across rebuilds
+    DBuf<int64_t> imp_rb, imp_rn;
     // optional CUDA-event timing of the main forward / backward kernels
     bool timing = false;
     cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
@@ -458,9 +464,10 @@ int relayout_steps(sili_layer* h, DBuf<uint32_t>& v, int64_t n_entities, int old
 
 // Grows the logical size of value_scale / output_scale to n, filling new
 // entries with `fill` (std::vector::resize semantics of the reference).
-void grow_logical(sili_layer* h, DBuf<float>& v, int64_t& n_logical, int64_t n, float fill) {
+// fills on the stream of the call that grows the vector (its kernels read it next)
+void grow_logical(sili_layer* h, DBuf<float>& v, int64_t& n_logical, int64_t n, float fill, cudaStream_t s = nullptr) {
     if (n <= n_logical) return;
-    launch_fill_f32(v.p + n_logical, n - n_logical, fill, h->stream);
+    launch_fill_f32(v.p + n_logical, n - n_logical, fill, s ? s : h->stream);
     n_logical = n;
 }
 
@@ -530,13 +537,15 @@ int import_csr(sili_layer* h, const int* d_ptrs, const int* d_idx, const float* 
                const float* d_imps = nullptr) {
     cudaStream_t s = h->stream;
     const int R = (int)h->rows;
-    DBuf<int> len, boff;
+    DBuf<int>& len = h->imp_len;
+    DBuf<int>& boff = h->imp_boff;
     RC(len.reserve(nnz + 1));
     RC(boff.reserve(nnz + 1));
     CK(cudaMemsetAsync(len.p, 0, (size_t)(nnz + 1) * sizeof(int), s));
     launch_import_lengths(d_ptrs, d_idx, R, len.p, s);
     RC(scan_excl_int(h, len.p, boff.p, nnz + 1, s));
-    DBuf<int64_t> rb, rn;
+    DBuf<int64_t>& rb = h->imp_rb;
+    DBuf<int64_t>& rn = h->imp_rn;
     RC(rb.reserve(R + 1));
     RC(rn.reserve(R + 1));
     launch_import_rows(d_ptrs, boff.p, R, rb.p, rn.p, s);
@@ -1276,8 +1285,8 @@ int sili_layer_backward_dense(sili_layer* h, const float* x, const float* dy, in
     } else {
         RC(h->dxT.reserve((int64_t)batch * n_in + 1));
         // pre-size the lazily sized scale vectors (linear_disldo.hpp:571-594)
-        grow_logical(h, h->vs, h->n_vs, n_in * h->rank, 1.0f);
-        grow_logical(h, h->os, h->n_os, n_out * h->rank, 1.0f);
+        grow_logical(h, h->vs, h->n_vs, n_in * h->rank, 1.0f, s);
+        grow_logical(h, h->os, h->n_os, n_out * h->rank, 1.0f, s);
         RC(ensure_pow_table(h, beta2, (uint32_t)(h->call + 2)));
         UpdateParams P = update_params(h, lr, flags, beta2, eps);
         P.stochastic = h->stochastic;
@@ -1376,7 +1385,7 @@ int sili_layer_backward_sparse(sili_layer* h, const float* x, const int* dptrs, 
     launch_accum_abs(dxin.p, h->in_acc.p, batch, n_in, s);
     launch_accum_abs_csr(dp.p, di.p, dv.p, batch, (int)n_out, h->grad_acc.p, s);
     // value_scale / value_scale_importance sized to n_in (sisldo_ops.hpp:622-625)
-    grow_logical(h, h->vs, h->n_vs, n_in, 1.0f);
+    grow_logical(h, h->vs, h->n_vs, n_in, 1.0f, s);
     RC(h->xT.reserve((int64_t)batch * n_in + 1));
     launch_transpose(dxin.p, h->xT.p, batch, n_in, s);
     RC(h->dyT.reserve((int64_t)batch * n_out + 1));
@@ -1784,35 +1793,38 @@ int sili_layer_topk_dyx_step(sili_layer* h, const float* x, const float* dy, int
     LayerView v = h->view();
     launch_exist_bits(h->rowptr.p, h->abs_cols.p, R, words, T.bits.p, s);
     launch_dyx_scores(dx_, ddy, batch, R, C, T.bits.p, words, T.keys.p, s);
-    // radix select: the k-th largest key, 8 bits at a time from the top
+    // radix select of the k-th largest key on the device, 8 bits at a time
+    // from the top; one read-back of its result
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, h->dev);
-    RC(T.hist.reserve(256));
-    uint32_t prefix = 0, mask = 0;
-    int64_t need = nc, eq_count = 0;
-    for (int shift = 24; shift >= 0 && nc > 0; shift -= 8) {
+    RC(T.hist.reserve(256)); RC(T.sel.reserve(1)); RC(T.nge.reserve(1));
+    SelState st{0u, 0u, 0, 0};
+    if (nc > 0) {
         CK(cudaMemsetAsync(T.hist.p, 0, 256 * sizeof(unsigned int), s));
-        launch_digit_hist(T.keys.p, n, shift, mask, prefix, T.hist.p, sms, s);
-        unsigned int hh[256];
-        CK(cudaMemcpyAsync(hh, T.hist.p, sizeof(hh), cudaMemcpyDeviceToHost, s));
-        CK(cudaStreamSynchronize(s));
-        int64_t cum = 0;
-        int d = 255;
-        for (; d > 0; --d) {
-            if (cum + (int64_t)hh[d] >= need) break;
-            cum += hh[d];
+        launch_sel_init(T.sel.p, nc, s);
+        for (int shift = 24; shift >= 0; shift -= 8) {
+            launch_digit_hist(T.keys.p, n, shift, T.sel.p, T.hist.p, sms, s);
+            launch_digit_pick(T.hist.p, shift, T.sel.p, s);
         }
-        need -= cum;
-        eq_count = hh[d];
-        prefix |= (uint32_t)d << shift;
-        mask |= 0xFFu << shift;
+        CK(cudaMemcpyAsync(&st, T.sel.p, sizeof st, cudaMemcpyDeviceToHost, s));
+        CK(cudaStreamSynchronize(s));
     }
-    const uint32_t thr = prefix;
+    const uint32_t thr = st.prefix;
+    const int64_t need = st.need, eq_count = st.eq_count;
     // candidates: every key above the threshold, then the first `need` equal
     // keys in (r, c) order; merged into (r, c) order
     RC(T.cand.reserve(nc + 1)); RC(T.cand_o.reserve(nc + 1)); RC(T.nsel.reserve(2));
-    int64_t n_gt = 0;
-    if (nc > 0) {
+    if (nc > 0 && need == eq_count) {
+        // every key equal to the threshold is taken: the candidates are the
+        // keys >= thr, gathered in one pass and sorted into (r, c) order
+        CK(cudaMemsetAsync(T.nge.p, 0, sizeof(unsigned long long), s));
+        launch_select_ge(T.keys.p, n, T.sel.p, T.cand.p, T.nge.p, nc, sms, s);
+        size_t b3 = 0;
+        cub::DeviceRadixSort::SortKeys(nullptr, b3, T.cand.p, T.cand_o.p, (int)nc, 0, 64, s);
+        RC(h->cub_tmp.reserve((int64_t)b3 + 1));
+        CK(cub::DeviceRadixSort::SortKeys(h->cub_tmp.p, b3, T.cand.p, T.cand_o.p, (int)nc, 0, 64, s));
+    } else if (nc > 0) {
+        int64_t n_gt = 0;
         cub::CountingInputIterator<int64_t> it(0);
         RC(T.eq.reserve(eq_count + 1));
         size_t b1 = 0, b2 = 0;
@@ -1835,8 +1847,9 @@ int sili_layer_topk_dyx_step(sili_layer* h, const float* x, const float* dy, int
         CK(cub::DeviceRadixSort::SortKeys(h->cub_tmp.p, b3, T.cand.p, T.cand_o.p, (int)nc, 0, 64, s));
     }
     // prune: the npr existing synapses of smallest |w * S|, ties in (r, c) order
-    DBuf<int> di;
-    DBuf<float> dw, dm;
+    DBuf<int>& di = T.di;
+    DBuf<float>& dw = T.dw;
+    DBuf<float>& dm = T.dm;
     RC(di.reserve(nnz + 1)); RC(dw.reserve(nnz + 1)); RC(dm.reserve(nnz + 1));
     launch_export(v, di.p, dw.p, dm.p, s);
     RC(T.pk.reserve(nnz + 1)); RC(T.pk_o.reserve(nnz + 1)); RC(T.pid.reserve(nnz + 1)); RC(T.pid_o.reserve(nnz + 1));
@@ -1857,12 +1870,16 @@ int sili_layer_topk_dyx_step(sili_layer* h, const float* x, const float* dy, int
     launch_topk_merge(v, dw.p, dm.p, T.drop.p, T.cand_o.p, T.keys.p, T.cptr.p, 0, T.cnt.p, nullptr, nullptr, nullptr,
                       nullptr, h->out_degree.p, s);
     RC(scan_excl_int(h, T.cnt.p, T.nptr.p, R + 1, s));
-    DBuf<int> nidx;
-    DBuf<float> nw, nimp;
+    DBuf<int>& nidx = T.nidx;
+    DBuf<float>& nw = T.nw;
+    DBuf<float>& nimp = T.nimp;
     RC(nidx.reserve(nn + 1)); RC(nw.reserve(nn + 1)); RC(nimp.reserve(nn + 1));
     launch_topk_merge(v, dw.p, dm.p, T.drop.p, T.cand_o.p, T.keys.p, T.cptr.p, 1, T.cnt.p, T.nptr.p, nidx.p, nw.p,
                       nimp.p, h->out_degree.p, s);
     CK(cudaGetLastError());
+    // the rebuild runs on the layer's own stream: its inputs, written above on
+    // the caller's stream, must be complete first
+    CK(cudaStreamSynchronize(s));
     RC(import_csr(h, T.nptr.p, nidx.p, nw.p, (int)nn, nimp.p));
     CK(cudaStreamSynchronize(s));
     return SILI_OK;

@@ -31,14 +31,15 @@ void launch_exist_bits(const int* rowptr, const int* abs_cols, int64_t n_in, int
 
 // Scores as 32-bit keys: 0 for an existing synapse, bits(|s|) + 1 otherwise
 // (|s| >= 0, so key order is score order).  128 x 128 output tile per block,
-// 8 x 8 per thread, samples staged 16 at a time; each output accumulates its
-// fma chain over b in ascending order, as the rule defines.
+// 8 x 8 per thread (rows ty*8.., columns tx*8..: both read from shared memory
+// as two 16-byte loads), samples staged 16 at a time; each output
+// accumulates its fma chain over b in ascending order, as the rule defines.
 constexpr int kTM = 128, kTN = 128, kTK = 16;
 __global__ void __launch_bounds__(256) k_dyx_scores(const float* __restrict__ x, const float* __restrict__ dy, int B,
                                                     int64_t n_in, int64_t n_out, const uint32_t* __restrict__ bits,
                                                     int64_t words, uint32_t* __restrict__ keys) {
-    __shared__ float xs[kTK][kTM];
-    __shared__ float ds[kTK][kTN];
+    __shared__ __align__(16) float xs[kTK][kTM];
+    __shared__ __align__(16) float ds[kTK][kTN];
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
     const int64_t r0 = (int64_t)blockIdx.y * kTM, c0 = (int64_t)blockIdx.x * kTN;
     float acc[8][8];
@@ -56,11 +57,12 @@ __global__ void __launch_bounds__(256) k_dyx_scores(const float* __restrict__ x,
         __syncthreads();
         const int kn = min(kTK, B - b0);
         for (int k = 0; k < kn; ++k) {
-            float xv[8], dv[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) xv[i] = xs[k][ty * 8 + i];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) dv[j] = ds[k][tx + 16 * j];
+            const float4 xa = *reinterpret_cast<const float4*>(&xs[k][ty * 8]);
+            const float4 xb = *reinterpret_cast<const float4*>(&xs[k][ty * 8 + 4]);
+            const float4 da = *reinterpret_cast<const float4*>(&ds[k][tx * 8]);
+            const float4 db = *reinterpret_cast<const float4*>(&ds[k][tx * 8 + 4]);
+            const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+            const float dv[8] = {da.x, da.y, da.z, da.w, db.x, db.y, db.z, db.w};
 #pragma unroll
             for (int i = 0; i < 8; ++i)
 #pragma unroll
@@ -74,7 +76,7 @@ __global__ void __launch_bounds__(256) k_dyx_scores(const float* __restrict__ x,
         if (r >= n_in) continue;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            const int64_t c = c0 + tx + 16 * j;
+            const int64_t c = c0 + tx * 8 + j;
             if (c >= n_out) continue;
             const bool ex = (bits[r * words + (c >> 5)] >> (c & 31)) & 1u;
             keys[r * n_out + c] = ex ? 0u : __float_as_uint(fabsf(acc[i][j])) + 1u;
@@ -89,11 +91,26 @@ void launch_dyx_scores(const float* x, const float* dy, int B, int64_t n_in, int
     count_launch();
 }
 
-// radix-select histogram of one 8-bit digit among keys whose higher digits
-// equal `prefix` under `mask`
-__global__ void k_digit_hist(const uint32_t* __restrict__ keys, int64_t n, int shift, uint32_t mask, uint32_t prefix,
+// Radix select of the k-th largest key, 8 bits at a time from the top, with
+// its state on the device (no host round trip per digit):
+// k_sel_init -> 4 x (histogram of the digit among keys matching the prefix so
+// far, k_digit_pick) -> prefix = the k-th largest key, need = how many keys
+// equal to it are taken, eq_count = how many there are.
+__global__ void k_sel_init(SelState* st, int64_t need) {
+    st->prefix = 0u;
+    st->mask = 0u;
+    st->need = need;
+    st->eq_count = 0;
+}
+void launch_sel_init(SelState* st, int64_t need, cudaStream_t s) {
+    k_sel_init<<<1, 1, 0, s>>>(st, need);
+    count_launch();
+}
+
+__global__ void k_digit_hist(const uint32_t* __restrict__ keys, int64_t n, int shift, const SelState* __restrict__ st,
                              unsigned int* __restrict__ hist) {
     __shared__ unsigned int h[256];
+    const uint32_t mask = st->mask, prefix = st->prefix;
     for (int i = threadIdx.x; i < 256; i += blockDim.x) h[i] = 0;
     __syncthreads();
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
@@ -104,10 +121,61 @@ __global__ void k_digit_hist(const uint32_t* __restrict__ keys, int64_t n, int s
     for (int i = threadIdx.x; i < 256; i += blockDim.x)
         if (h[i]) atomicAdd(hist + i, h[i]);
 }
-void launch_digit_hist(const uint32_t* keys, int64_t n, int shift, uint32_t mask, uint32_t prefix, unsigned int* hist,
-                       int sms, cudaStream_t s) {
+void launch_digit_hist(const uint32_t* keys, int64_t n, int shift, const SelState* st, unsigned int* hist, int sms,
+                       cudaStream_t s) {
     const int64_t blocks = std::min<int64_t>((n + 255) / 256, (int64_t)sms * 8);
-    k_digit_hist<<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, s>>>(keys, n, shift, mask, prefix, hist);
+    k_digit_hist<<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, s>>>(keys, n, shift, st, hist);
+    count_launch();
+}
+
+// the digit holding the need-th largest key; clears the histogram for the next pass
+__global__ void k_digit_pick(unsigned int* __restrict__ hist, int shift, SelState* __restrict__ st) {
+    if (threadIdx.x == 0) {
+        int64_t cum = 0;
+        int d = 255;
+        for (; d > 0; --d) {
+            if (cum + (int64_t)hist[d] >= st->need) break;
+            cum += hist[d];
+        }
+        st->need -= cum;
+        st->eq_count = hist[d];
+        st->prefix |= (uint32_t)d << shift;
+        st->mask |= 0xFFu << shift;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+}
+void launch_digit_pick(unsigned int* hist, int shift, SelState* st, cudaStream_t s) {
+    k_digit_pick<<<1, 256, 0, s>>>(hist, shift, st);
+    count_launch();
+}
+
+// flat indices of every key >= thr (the caller has checked that this is
+// exactly the k wanted: every key equal to the threshold is taken), appended
+// in arbitrary order with one atomic per warp; the caller sorts them
+__global__ void k_select_ge(const uint32_t* __restrict__ keys, int64_t n, const SelState* __restrict__ st,
+                            int64_t* __restrict__ out, unsigned long long* __restrict__ count, int64_t cap) {
+    const uint32_t thr = st->prefix;
+    const int lane = threadIdx.x & 31;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i0 = (int64_t)blockIdx.x * blockDim.x; i0 < n; i0 += stride) {   // warp-uniform trip count
+        const int64_t i = i0 + threadIdx.x;
+        const bool sel = i < n && keys[i] >= thr;
+        const unsigned m = __ballot_sync(0xffffffffu, sel);
+        if (m == 0u) continue;
+        unsigned long long base = 0;
+        if (lane == 0) base = atomicAdd(count, (unsigned long long)__popc(m));
+        base = __shfl_sync(0xffffffffu, base, 0);
+        if (sel) {
+            const int64_t slot = (int64_t)base + __popc(m & ((1u << lane) - 1u));
+            if (slot < cap) out[slot] = i;
+        }
+    }
+}
+void launch_select_ge(const uint32_t* keys, int64_t n, const SelState* st, int64_t* out, unsigned long long* count,
+                      int64_t cap, int sms, cudaStream_t s) {
+    const int64_t blocks = std::min<int64_t>((n + 255) / 256, (int64_t)sms * 8);
+    k_select_ge<<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, s>>>(keys, n, st, out, count, cap);
     count_launch();
 }
 
