@@ -181,6 +181,7 @@ struct sili_layer {
     } topk;
     DBuf<int> imp_len, imp_boff;       // import_csr scratch, kept across rebuilds
     DBuf<int64_t> imp_rb, imp_rn;
+    DBuf<uint8_t> idx_spare, val_spare;  // the arrays the last rebuild replaced
     // optional CUDA-event timing of the main forward / backward kernels
     bool timing = false;
     cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
@@ -566,11 +567,14 @@ int import_csr(sili_layer* h, const int* d_ptrs, const int* d_idx, const float* 
     }
     RC(put_layout(h, N));
     const int64_t ib = N.bs[R], vb = N.es[R];
-    DBuf<uint8_t> nidx, nval;
+    // the previous rebuild's arrays are the spares: a rebuild of the same
+    // size (a synaptogenesis step) allocates and frees nothing
+    DBuf<uint8_t>& nidx = h->idx_spare;
+    DBuf<uint8_t>& nval = h->val_spare;
     RC(nidx.reserve(ib + 64));
     RC(nval.reserve(vb + 64));
-    CK(cudaMemsetAsync(nidx.p, 0, (size_t)nidx.cap, s));
-    CK(cudaMemsetAsync(nval.p, 0, (size_t)nval.cap, s));
+    CK(cudaMemsetAsync(nidx.p, 0, (size_t)(ib + 64), s));
+    CK(cudaMemsetAsync(nval.p, 0, (size_t)(vb + 64), s));
     launch_import_write(d_ptrs, d_idx, d_vals, d_imps, boff.p, R, h->bs.p, h->es.p, nidx.p, nval.p, s);
     CK(cudaGetLastError());
     CK(cudaStreamSynchronize(s));

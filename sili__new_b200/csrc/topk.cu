@@ -157,19 +157,33 @@ __global__ void k_select_ge(const uint32_t* __restrict__ keys, int64_t n, const 
                             int64_t* __restrict__ out, unsigned long long* __restrict__ count, int64_t cap) {
     const uint32_t thr = st->prefix;
     const int lane = threadIdx.x & 31;
+    const int64_t n4 = n >> 2;   // whole 16-byte groups; the tail below
+    const uint4* k4 = reinterpret_cast<const uint4*>(keys);
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t i0 = (int64_t)blockIdx.x * blockDim.x; i0 < n; i0 += stride) {   // warp-uniform trip count
-        const int64_t i = i0 + threadIdx.x;
-        const bool sel = i < n && keys[i] >= thr;
+    auto emit = [&](bool sel, int64_t i) {   // warp-wide: one atomic per warp
         const unsigned m = __ballot_sync(0xffffffffu, sel);
-        if (m == 0u) continue;
-        unsigned long long base = 0;
-        if (lane == 0) base = atomicAdd(count, (unsigned long long)__popc(m));
-        base = __shfl_sync(0xffffffffu, base, 0);
+        if (m == 0u) return;
+        unsigned long long b = 0;
+        if (lane == 0) b = atomicAdd(count, (unsigned long long)__popc(m));
+        b = __shfl_sync(0xffffffffu, b, 0);
         if (sel) {
-            const int64_t slot = (int64_t)base + __popc(m & ((1u << lane) - 1u));
+            const int64_t slot = (int64_t)b + __popc(m & ((1u << lane) - 1u));
             if (slot < cap) out[slot] = i;
         }
+    };
+    for (int64_t g0 = (int64_t)blockIdx.x * blockDim.x; g0 < n4; g0 += stride) {   // warp-uniform trip count
+        const int64_t g = g0 + threadIdx.x;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        const bool ok = g < n4;
+        if (ok) v = __ldg(k4 + g);
+        emit(ok && v.x >= thr, 4 * g + 0);
+        emit(ok && v.y >= thr, 4 * g + 1);
+        emit(ok && v.z >= thr, 4 * g + 2);
+        emit(ok && v.w >= thr, 4 * g + 3);
+    }
+    if (blockIdx.x == 0 && threadIdx.x < 32) {
+        const int64_t i = 4 * n4 + threadIdx.x;
+        emit(i < n && keys[i] >= thr, i);
     }
 }
 void launch_select_ge(const uint32_t* keys, int64_t n, const SelState* st, int64_t* out, unsigned long long* count,
@@ -229,48 +243,72 @@ void launch_cand_rowptr(const int64_t* cand, int nc, int64_t n_out, int64_t n_in
     count_launch();
 }
 
-// Per row: kept old synapses merged with the row's candidates by column.
-// pass 0 counts into cnt[r]; pass 1 writes at newptr[r].
+// Per row: kept old synapses merged with the row's candidates by column
+// (candidates are non-existing positions, so no column appears twice).
+// One warp per row.  pass 0 counts into cnt[r]; pass 1 writes at newptr[r]:
+// a kept old synapse at (kept synapses before it) + (candidates of smaller
+// column, binary search in the row's few candidates); a candidate at (its
+// index among the row's candidates) + (kept synapses of smaller column:
+// lower bound in the row's ascending columns minus the dropped ones before).
 __global__ void k_topk_merge(LayerView L, const float* __restrict__ w, const float* __restrict__ imp,
                              const uint8_t* __restrict__ drop, const int64_t* __restrict__ cand,
                              const uint32_t* __restrict__ keys, const int* __restrict__ cptr, int pass,
                              int* __restrict__ cnt, const int* __restrict__ newptr, int* __restrict__ nidx,
                              float* __restrict__ nw, float* __restrict__ nimp, int* __restrict__ out_degree) {
-    const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
     if (r >= L.n_in) return;
-    int f = L.rowptr[r];
-    const int f1 = L.rowptr[r + 1];
-    int a = cptr[r];
-    const int a1 = cptr[r + 1];
-    int o = pass ? newptr[r] : 0;
-    int n = 0;
-    while (f < f1 || a < a1) {
-        const int64_t cc = a < a1 ? cand[a] % L.n_out : INT64_MAX;
-        const bool take_old = f < f1 && !(a < a1 && cc < L.abs_cols[f]);
-        if (take_old) {
-            if (!drop[f]) {
-                if (pass) { nidx[o] = L.abs_cols[f]; nw[o] = w[f]; nimp[o] = imp[f]; ++o; }
-                ++n;
-            }
-            ++f;
-        } else {
-            if (pass) {
-                const float score = __uint_as_float(keys[cand[a]] - 1u);
-                nidx[o] = (int)cc; nw[o] = 0.0f; nimp[o] = fp4_decode(fp4_encode(score)); ++o;
-                atomicAdd(out_degree + cc, 1);
-            }
-            ++n;
-            ++a;
-        }
+    const int f0 = L.rowptr[r], f1 = L.rowptr[r + 1];
+    const int a0 = cptr[r], a1 = cptr[r + 1];
+    if (pass == 0) {
+        int kept = 0;
+        for (int f = f0 + lane; f < f1; f += 32) kept += drop[f] ? 0 : 1;
+        for (int o = 16; o > 0; o >>= 1) kept += __shfl_xor_sync(0xffffffffu, kept, o);
+        if (lane == 0) cnt[r] = kept + (a1 - a0);
+        return;
     }
-    if (!pass) cnt[r] = n;
+    const int base = newptr[r];
+    // kept old synapses
+    int carry = 0;
+    for (int c0 = f0; c0 < f1; c0 += 32) {
+        const int f = c0 + lane;
+        const bool valid = f < f1;
+        const bool keep = valid && !drop[f];
+        const unsigned m = __ballot_sync(0xffffffffu, keep);
+        if (keep) {
+            const int col = L.abs_cols[f];
+            int lo = a0, hi = a1;   // candidates with column < col
+            while (lo < hi) {
+                const int mid = (lo + hi) >> 1;
+                if (cand[mid] % L.n_out < col) lo = mid + 1; else hi = mid;
+            }
+            const int o = base + carry + __popc(m & ((1u << lane) - 1u)) + (lo - a0);
+            nidx[o] = col; nw[o] = w[f]; nimp[o] = imp[f];
+        }
+        carry += __popc(m);
+    }
+    // candidates
+    for (int a = a0 + lane; a < a1; a += 32) {
+        const int64_t cc = cand[a] % L.n_out;
+        int lo = f0, hi = f1;        // first old synapse with column > cc
+        while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if (L.abs_cols[mid] < cc) lo = mid + 1; else hi = mid;
+        }
+        int dropped = 0;
+        for (int f = f0; f < lo; ++f) dropped += drop[f] ? 1 : 0;
+        const int o = base + (a - a0) + (lo - f0 - dropped);
+        const float score = __uint_as_float(keys[cand[a]] - 1u);
+        nidx[o] = (int)cc; nw[o] = 0.0f; nimp[o] = fp4_decode(fp4_encode(score));
+        atomicAdd(out_degree + cc, 1);
+    }
 }
 void launch_topk_merge(const LayerView& L, const float* w, const float* imp, const uint8_t* drop, const int64_t* cand,
                        const uint32_t* keys, const int* cptr, int pass, int* cnt, const int* newptr, int* nidx,
                        float* nw, float* nimp, int* out_degree, cudaStream_t s) {
     if (L.n_in == 0) return;
-    k_topk_merge<<<(unsigned)((L.n_in + 127) / 128), 128, 0, s>>>(L, w, imp, drop, cand, keys, cptr, pass, cnt, newptr,
-                                                                 nidx, nw, nimp, out_degree);
+    k_topk_merge<<<(unsigned)((L.n_in + 7) / 8), 256, 0, s>>>(L, w, imp, drop, cand, keys, cptr, pass, cnt, newptr,
+                                                             nidx, nw, nimp, out_degree);
     count_launch();
 }
 
