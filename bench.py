@@ -303,9 +303,10 @@ def run_synaptogenesis(args, dev, S, torch, cpu_sample):
     dy = torch.randn(B, n, generator=gen, device=f"cuda:{dev}")
     k = len(i) // 100
     stream = torch.cuda.Stream(device=dev)
-    L.topk_dyx_step_ptr(x.data_ptr(), dy.data_ptr(), B, k, stream.cuda_stream)   # warm-up (first-use buffers)
+    for _ in range(3):   # warm-up: first-use buffers, and clocks up after the CPU-only samples before
+        L.topk_dyx_step_ptr(x.data_ptr(), dy.data_ptr(), B, k, stream.cuda_stream)
     torch.cuda.synchronize(dev)
-    steps = 3
+    steps = 8
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(steps):
@@ -339,18 +340,34 @@ def run_synaptogenesis(args, dev, S, torch, cpu_sample):
     return out
 
 
-def run_folded(args, dev, rank, world, dist, S, torch):
-    """Mistral-Small-24B-shaped folded stack (hidden 5120,
-    32 heads / 8 KV x 128, FFN 32768, 40 layers folded per suffix), every
-    linear pruned to 95 %, random init; one decode step at batch 32 = every
-    suffix's stacked layer once (forward + fold sum), output columns sharded
-    over the ranks with an NCCL all-gather per suffix (strong scaling: the
-    same model whatever the rank count).  Returns the line's folded_stack
-    object (rank 0) or None."""
+FOLDED = {
+    # Mistral-Small-24B shape (hidden 5120, 32 heads / 8 KV
+    # x 128, FFN 32768, 40 layers), every linear pruned to 95 %, decode batch 32
+    "config5": dict(shape="MISTRAL_SMALL_24B", batch=32, density=0.05, kind="decode",
+                    label="Mistral-Small-24B shape, {L} layers folded, 95% pruned, batch 32"),
+    # toy Mistral shape (hidden 4096, 32 heads / 8 KV x 128,
+    # FFN 14336, 32 layers), magnitude-pruned to 90 %, seq 512 x batch 8
+    # tokens in one pass
+    "config4": dict(shape="TOY_MISTRAL", batch=512 * 8, density=0.10, kind="prefill",
+                    label="toy Mistral shape, {L} layers folded, 90% pruned, seq 512 x batch 8"),
+}
+
+
+def run_folded(args, dev, rank, world, dist, S, torch, which="config5"):
+    """A folded multi-layer stack (FoldedLayer: per weight suffix one stacked
+    layer of all layers' matrices, then the fold sum), random init: one step =
+    every suffix's stacked layer once (forward + fold sum) on the config's
+    token batch, output columns sharded over the ranks with an NCCL
+    all-gather per suffix (strong scaling: the same model whatever the rank
+    count).  Pruning keeps a uniformly random pattern at the config's density
+    (magnitude pruning of i.i.d. initial weights keeps exactly such a
+    pattern); config 4's attention band mask belongs to attention, which is
+    not on this path.  Returns the line's object (rank 0) or None."""
     from sili__new_b200 import folded as F
-    cfg = F.MISTRAL_SMALL_24B
+    fc = FOLDED[which]
+    cfg = getattr(F, fc["shape"])
     suffixes = F.mistral_suffixes(cfg)
-    n_folds, B, density = (args.folded_layers or cfg["layers"]), 32, 0.05
+    n_folds, B, density = (args.folded_layers or cfg["layers"]), fc["batch"], fc["density"]
     stack = F.FoldedStack(suffixes, n_folds, rank, world,
                           lambda a, b, c: S.SparseLinearLayer(a, b, c, 1, dev),
                           group=None)
@@ -376,10 +393,11 @@ def run_folded(args, dev, rank, world, dist, S, torch):
             outs.append(stack.forward_device(name, xs[name], stream))
         return outs
 
-    for _ in range(max(args.warmup, 3)):
+    prefill = fc["kind"] == "prefill"   # a step of 4096 tokens: fewer, longer steps
+    for _ in range(3 if prefill else max(args.warmup, 3)):
         decode_step()
     torch.cuda.synchronize(dev)
-    steps = max(5, min(args.steps, 50))
+    steps = max(3, min(args.steps, 5)) if prefill else max(5, min(args.steps, 50))
     if dist:
         dist.barrier()
     torch.cuda.synchronize(dev)
@@ -403,14 +421,13 @@ def run_folded(args, dev, rank, world, dist, S, torch):
     mem_gb = torch.cuda.max_memory_allocated(dev) / 1e9
     if rank != 0:
         return None
-    return {"metric": f"folded-stack decode tokens/s (Mistral-Small-24B shape, {n_folds} layers folded, 95% pruned, "
-                      "batch 32, linears only)",
+    return {"metric": f"folded-stack {fc['kind']} tokens/s ({fc['label'].format(L=n_folds)}, linears only)",
             "value": B / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "scaling": "strong",
             "ms_per_step": ms, "steps": steps, "nnz": total_nnz,
             "gflop_per_step": flops / 1e9, "fp32_tflops": flops / (ms * 1e-3) / 1e12,
             "sharding": f"output columns within each fold over {world} rank(s), NCCL all-gather per suffix",
             "build_s_rank0": build_s, "torch_mem_gb_rank0": mem_gb, "gpu_launches_rank0": launches,
-            "data": "synthetic: random N(0,0.02) pruned to 5% (Bernoulli), x ~ N(0,1)"}
+            "data": f"synthetic: random N(0,0.02) pruned to {density * 100:g}% (uniform pattern), x ~ N(0,1)"}
 
 
 def main():
@@ -425,7 +442,7 @@ def main():
     ap.add_argument("--no-folded", action="store_true", help="skip the folded-stack (config 5) measurement")
     ap.add_argument("--no-block4", action="store_true", help="skip the block4-format (config 2) measurement")
     ap.add_argument("--no-synap", action="store_true", help="skip the synaptogenesis (config 3) measurement")
-    ap.add_argument("--only", choices=["block4", "synap", "folded"],
+    ap.add_argument("--only", choices=["block4", "synap", "folded", "folded4"],
                     help="run one secondary measurement alone and print its object (profiling)")
     ap.add_argument("--folded-layers", type=int, default=None,
                     help="layers folded per suffix (default: config 5's 40; fewer for small profiling runs)")
@@ -474,7 +491,8 @@ def main():
         elif args.only == "synap":
             out = run_synaptogenesis(args, dev, S, torch, cpu_sample=False)
         else:
-            out = run_folded(args, dev, rank, world, dist, S, torch)
+            out = run_folded(args, dev, rank, world, dist, S, torch,
+                             which="config4" if args.only == "folded4" else "config5")
         if dist:
             dist.barrier()
             dist.destroy_process_group()
@@ -612,9 +630,11 @@ def main():
     if not args.no_synap and world == 1:   # one layer: measured on one GPU
         synap = run_synaptogenesis(args, dev, S, torch, cpu_sample=not args.no_cpu_baseline)
     # ── folded stack (config 5), sharded over the ranks ─────────────────────
-    folded = None
+    folded = folded4 = None
     if not args.no_folded:
         folded = run_folded(args, dev, rank, world, dist, S, torch)
+        torch.cuda.empty_cache()
+        folded4 = run_folded(args, dev, rank, world, dist, S, torch, which="config4")
 
     if dist:
         dist.barrier()
@@ -646,6 +666,7 @@ def main():
         "block4": block4,
         "synaptogenesis": synap,
         "folded_stack": folded,
+        "folded_prefill": folded4,
     }
     print(json.dumps(line))
     return 0
