@@ -340,6 +340,182 @@ def run_synaptogenesis(args, dev, S, torch, cpu_sample):
     return out
 
 
+def run_sparse_variants(layers, S, torch, dev, work, cpu_sample):
+    """BASELINE config 2's sparse-input forward (x as dense_to_csr(x, 0),
+    ~20 % of it non-zero) and sparse-gradient backward (dy as
+    dense_to_top_k_csr(dy, 0.03 B n), lr 0.01), on the config-2 layer copies
+    (rotated), through the public API with device-resident CSR arrays."""
+    p, i, w, vs, x, dy = work
+    px, ix, vx = S.dense_to_csr(x, 0.0)
+    kd = int(0.03 * BATCH * N_OUT)
+    pd, idd, vd = S.dense_to_top_k_csr(dy, kd)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda(dev)
+    dpx, dix, dvx, dpd, did, dvd = t(px), t(ix), t(vx), t(pd), t(idd), t(vd)
+    xs = t(x)
+    y = torch.empty(BATCH, N_OUT, device=f"cuda:{dev}")
+    dx = torch.empty(BATCH, N_IN, device=f"cuda:{dev}")
+    stream = torch.cuda.Stream(device=dev)
+    sh = stream.cuda_stream
+    n = len(layers)
+
+    def fwd(j):
+        layers[j % n].forward_sparse_ptr(dpx.data_ptr(), dix.data_ptr(), dvx.data_ptr(), len(ix), BATCH, y.data_ptr(), sh)
+
+    def bwd(j):
+        layers[j % n].backward_sparse_ptr(xs.data_ptr(), dpd.data_ptr(), did.data_ptr(), dvd.data_ptr(), len(idd), BATCH,
+                                          LR, True, True, 0.999, 1e-8, dx.data_ptr(), sh)
+
+    out = {"metric": "config 2 sparse variants: forward_sparse and backward_sparse ms per call",
+           "unit": "ms", "higher_is_better": False, "x_nnz": int(len(ix)), "dy_nnz": int(len(idd))}
+    for name, fn in (("forward_sparse", fwd), ("backward_sparse", bwd)):
+        for j in range(n):
+            fn(j)
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        steps = 2 * n
+        for j in range(steps):
+            fn(j)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        out[name + "_ms"] = e0.elapsed_time(e1) / steps
+    out["value"] = out["forward_sparse_ms"] + out["backward_sparse_ms"]
+    if cpu_sample:
+        mod, variant = reference_module()
+        if mod is not None:
+            threads = os.cpu_count() or 1
+            R = mod.SparseLinearLayer(N_IN, N_OUT, int(len(i) * 1.25), threads)
+            R.load_weights(p, i, w)
+            for r in range(N_IN):
+                R.set_value_scale_raw(r, float(vs[r]))
+                R.set_importance_scale_raw(r, LR / 6.0)
+            t0 = time.perf_counter()
+            R.forward_sparse(px, ix, vx, BATCH)
+            t1 = time.perf_counter()
+            R.backward_sparse(x, pd, idd, vd, BATCH, LR, lr_per_row_nnz=True)
+            t2 = time.perf_counter()
+            out["cpu_baseline"] = {"value": (t2 - t0) * 1e3, "unit": "ms", "forward_sparse_ms": (t1 - t0) * 1e3,
+                                   "backward_sparse_ms": (t2 - t1) * 1e3, "cores": threads, "kind": "reference",
+                                   "sample": f"one call each on the full config-2 layer (sili._cpu -march={variant})"}
+    return out
+
+
+def run_reference_rule(args, dev, S, torch, cpu_sample):
+    """BASELINE config 3 with the reference's own grow/prune rule (A11/A12):
+    on the 16384^2 98 % layer (deterministic rounding), after one
+    backward_dense(dy, lr=0.01) (non-zero importances) and one
+    backward_dense(dy, lr=0) (the neuron accumulators), time build_probes(232)
+    and a full synap_step sweep (importance_cutoff 1e30, max_row_weights =
+    row nnz, max_prune_per_step 3) as one synap_rows call.  cpu_sample: the
+    reference's build_probes + synap_step loop on a 512-row slice, scaled."""
+    from helpers import random_layer
+    n, per, B, kp = 16384, 328, 256, 232
+    p, i, w, vs = random_layer(n, n, per, seed=3)
+    rng = np.random.default_rng(0)
+    x = rng.normal(0, 1, (B, n)).astype(np.float32)
+    dy = np.random.default_rng(1).normal(0, 1, (B, n)).astype(np.float32)
+    L = S.SparseLinearLayerDeterministic(n, n, int(len(i) * 1.25), 1, dev)
+    L.load_weights(p, i, w)
+    for r in range(n):
+        L.set_value_scale_raw(r, float(vs[r]))
+        L.set_importance_scale_raw(r, LR / 6.0)
+    L.forward_dense(x)
+    L.backward_dense(dy, LR, True)
+    L.zero_accum()
+    L.backward_dense(dy, 0.0)
+    L.sync()
+    t0 = time.perf_counter()
+    L.build_probes(kp)
+    L.sync()
+    t1 = time.perf_counter()
+    L.synap_rows(0, n, 1e30, per, 3)
+    L.sync()
+    t2 = time.perf_counter()
+    out = {"metric": "config 3, reference rule: build_probes(232) + full synap_step sweep, ms",
+           "value": (t2 - t0) * 1e3, "unit": "ms", "higher_is_better": False,
+           "build_probes_ms": (t1 - t0) * 1e3, "sweep_ms": (t2 - t1) * 1e3, "timing": "host wall clock, synchronised"}
+    del L
+    torch.cuda.empty_cache()
+    if cpu_sample:
+        mod, variant = reference_module()
+        if mod is not None:
+            rows = 512
+            threads = os.cpu_count() or 1
+            sub = p[: rows + 1]
+            R = mod.SparseLinearLayerDeterministic(rows, n, int(sub[-1] * 1.25), threads)
+            R.load_weights(sub, i[: sub[-1]], w[: sub[-1]])
+            for r in range(rows):
+                R.set_value_scale_raw(r, float(vs[r]))
+                R.set_importance_scale_raw(r, LR / 6.0)
+            xr = np.ascontiguousarray(x[:, :rows])
+            R.forward_dense(xr)
+            R.backward_dense(dy, LR, lr_per_row_nnz=True)
+            R.zero_accum()
+            R.backward_dense(dy, 0.0)
+            t0 = time.perf_counter()
+            R.build_probes(kp)
+            for _ in range(rows):
+                R.synap_step(1e30, per, 3)
+            per_run = (time.perf_counter() - t0) * (n / rows)
+            out["cpu_baseline"] = {"value": per_run * 1e3, "unit": "ms", "cores": threads, "kind": "reference",
+                                   "sample": f"build_probes + synap_step over a {rows}-row slice (same columns, "
+                                             f"batch and probe count), scaled x{n // rows} (sili._cpu -march={variant})"}
+    return out
+
+
+def run_spmv(S, torch, dev, cpu_sample):
+    """forward_dense at batch 1 on a 4096^2 layer at 90 %
+    (410 synapses per row), x ~ N(0,1), seed 0; rotated over 48 layer copies
+    (163 MB of weight streams, above L2), device pointers, CUDA events."""
+    from helpers import random_layer
+    n, per = 4096, 410
+    p, i, w, vs = random_layer(n, n, per, seed=0)
+    x = np.random.default_rng(0).normal(0, 1, (1, n)).astype(np.float32)
+    copies = 48
+    layers = []
+    for _ in range(copies):
+        L = S.SparseLinearLayer(n, n, int(len(i) * 1.25), 1, dev)
+        L.load_weights(p, i, w)
+        for r in range(n):
+            L.set_value_scale_raw(r, float(vs[r]))
+        layers.append(L)
+    xs = torch.from_numpy(x).cuda(dev)
+    y = torch.empty(1, n, device=f"cuda:{dev}")
+    stream = torch.cuda.Stream(device=dev)
+    for L in layers:
+        L.forward_dense_ptr(xs.data_ptr(), 1, y.data_ptr(), stream.cuda_stream)
+    torch.cuda.synchronize(dev)
+    steps = 4 * copies
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for j in range(steps):
+        layers[j % copies].forward_dense_ptr(xs.data_ptr(), 1, y.data_ptr(), stream.cuda_stream)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    us = e0.elapsed_time(e1) / steps * 1e3
+    out = {"metric": "config 1 SpMV (4096^2, 90% sparse, batch 1) us per forward_dense", "value": us, "unit": "us",
+           "higher_is_better": False, "nnz": int(len(i)), "launches_per_call": 3,
+           "timing": "CUDA events over 192 calls rotating 48 layer copies, no CUDA graph"}
+    del layers
+    torch.cuda.empty_cache()
+    if cpu_sample:
+        mod, variant = reference_module()
+        if mod is not None:
+            threads = os.cpu_count() or 1
+            R = mod.SparseLinearLayer(n, n, int(len(i) * 1.25), threads)
+            R.load_weights(p, i, w)
+            for r in range(n):
+                R.set_value_scale_raw(r, float(vs[r]))
+            R.forward_dense(x)
+            t0 = time.perf_counter()
+            reps = 200
+            for _ in range(reps):
+                R.forward_dense(x)
+            out["cpu_baseline"] = {"value": (time.perf_counter() - t0) / reps * 1e6, "unit": "us", "cores": threads,
+                                   "kind": "reference", "sample": f"{reps} calls (sili._cpu -march={variant})"}
+    return out
+
+
 FOLDED = {
     # BASELINE config 5: Mistral-Small-24B shape (hidden 5120, 32 heads / 8 KV
     # x 128, FFN 32768, 40 layers), every linear pruned to 95 %, decode batch 32
@@ -442,7 +618,9 @@ def main():
     ap.add_argument("--no-folded", action="store_true", help="skip the folded-stack (config 5) measurement")
     ap.add_argument("--no-block4", action="store_true", help="skip the block4-format (config 2) measurement")
     ap.add_argument("--no-synap", action="store_true", help="skip the synaptogenesis (config 3) measurement")
-    ap.add_argument("--only", choices=["block4", "synap", "folded", "folded4"],
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the sparse-variant, reference-rule and SpMV measurements")
+    ap.add_argument("--only", choices=["block4", "synap", "folded", "folded4", "rule", "spmv"],
                     help="run one secondary measurement alone and print its object (profiling)")
     ap.add_argument("--folded-layers", type=int, default=None,
                     help="layers folded per suffix (default: config 5's 40; fewer for small profiling runs)")
@@ -490,6 +668,10 @@ def main():
             out = run_block4(args, dev, S, torch, make_workload(), cpu_sample=False)
         elif args.only == "synap":
             out = run_synaptogenesis(args, dev, S, torch, cpu_sample=False)
+        elif args.only == "rule":
+            out = run_reference_rule(args, dev, S, torch, cpu_sample=False)
+        elif args.only == "spmv":
+            out = run_spmv(S, torch, dev, cpu_sample=False)
         else:
             out = run_folded(args, dev, rank, world, dist, S, torch,
                              which="config4" if args.only == "folded4" else "config5")
@@ -619,6 +801,10 @@ def main():
                    "sample": f"{n} fwd+bwd steps of the full config-2 workload on sili._cpu "
                              f"(reference source built -march={variant}, num_cpus={threads})"}
 
+    # ── config 2's sparse-input / sparse-gradient variants ─────────────────
+    sparse_v = None
+    if world == 1 and not args.no_extras:
+        sparse_v = run_sparse_variants(layers, S, torch, dev, work, cpu_sample=not args.no_cpu_baseline)
     del layers, xs, dys, ys, dxs
     torch.cuda.empty_cache()
     # ── the same matrix in the block4 format (config 2) ─────────────────────
@@ -629,6 +815,11 @@ def main():
     synap = None
     if not args.no_synap and world == 1:   # one layer: measured on one GPU
         synap = run_synaptogenesis(args, dev, S, torch, cpu_sample=not args.no_cpu_baseline)
+    # ── config 3 with the reference's grow/prune rule; config 1 SpMV ─────────
+    rule = spmv = None
+    if world == 1 and not args.no_extras:
+        rule = run_reference_rule(args, dev, S, torch, cpu_sample=not args.no_cpu_baseline)
+        spmv = run_spmv(S, torch, dev, cpu_sample=not args.no_cpu_baseline)
     # ── folded stack (config 5), sharded over the ranks ─────────────────────
     folded = folded4 = None
     if not args.no_folded:
@@ -665,6 +856,9 @@ def main():
         "clocks": clk,
         "block4": block4,
         "synaptogenesis": synap,
+        "synaptogenesis_reference_rule": rule,
+        "sparse_variants": sparse_v,
+        "spmv": spmv,
         "folded_stack": folded,
         "folded_prefill": folded4,
     }

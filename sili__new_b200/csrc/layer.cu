@@ -182,6 +182,8 @@ struct sili_layer {
     DBuf<int> imp_len, imp_boff;       // import_csr scratch, kept across rebuilds
     DBuf<int64_t> imp_rb, imp_rn;
     DBuf<uint8_t> idx_spare, val_spare;  // the arrays the last rebuild replaced
+    DBuf<int> csr_p, csr_i;               // staging of host CSR arguments
+    DBuf<float> csr_v;
     // optional CUDA-event timing of the main forward / backward kernels
     bool timing = false;
     cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
@@ -255,6 +257,19 @@ int stage_in(sili_layer* h, const float* src, size_t n, DBuf<float>& stage, cons
     RC(stage.reserve((int64_t)n + 1));
     CK(cudaMemcpyAsync(stage.p, src, n * 4, cudaMemcpyHostToDevice, s));
     *out = stage.p;
+    return SILI_OK;
+}
+// Device views of a CSR argument (row pointers, indices, values): the arrays
+// themselves when they are device memory, else copies in the layer's staging
+// buffers (kept across calls).
+int stage_csr(sili_layer* h, const int* ptrs, const int* idx, const float* vals, int rows, int nnz, const int** dp,
+              const int** di, const float** dv, cudaStream_t s) {
+    if (is_device_ptr(ptrs)) { *dp = ptrs; }
+    else { RC(h->csr_p.reserve(rows + 1)); RC(to_dev(ptrs, h->csr_p.p, (size_t)(rows + 1) * 4, s)); *dp = h->csr_p.p; }
+    if (nnz == 0 || is_device_ptr(idx)) { *di = idx; }
+    else { RC(h->csr_i.reserve(nnz + 1)); RC(to_dev(idx, h->csr_i.p, (size_t)nnz * 4, s)); *di = h->csr_i.p; }
+    if (nnz == 0 || is_device_ptr(vals)) { *dv = vals; }
+    else { RC(h->csr_v.reserve(nnz + 1)); RC(to_dev(vals, h->csr_v.p, (size_t)nnz * 4, s)); *dv = h->csr_v.p; }
     return SILI_OK;
 }
 // dst = transpose of the row-major [rows, cols] array src (host or device).
@@ -1334,12 +1349,10 @@ int sili_layer_forward_sparse(sili_layer* h, const int* ptrs, const int* idx, co
     const int64_t n_in = h->rows, n_out = h->cols;
     RC(check_csr(ptrs, idx, batch, nnz, n_in, "forward_sparse"));
     RC(ensure_aux(h, s));
-    DBuf<int> dp, di;
-    DBuf<float> dv;
-    RC(dp.reserve(batch + 1)); RC(di.reserve(nnz + 1)); RC(dv.reserve(nnz + 1));
-    RC(to_dev(ptrs, dp.p, (size_t)(batch + 1) * 4, s));
-    RC(to_dev(idx, di.p, (size_t)nnz * 4, s));
-    RC(to_dev(vals, dv.p, (size_t)nnz * 4, s));
+    const int* dp = nullptr;
+    const int* di = nullptr;
+    const float* dv = nullptr;
+    RC(stage_csr(h, ptrs, idx, vals, batch, nnz, &dp, &di, &dv, s));
     RC(h->xT.reserve((int64_t)batch * (n_in + 1) + 1));
     CK(cudaMemsetAsync(h->xT.p, 0, (size_t)batch * (n_in + 1) * 4, s));   // + the zero row
     uint8_t* xpres = nullptr;
@@ -1348,7 +1361,7 @@ int sili_layer_forward_sparse(sili_layer* h, const int* ptrs, const int* idx, co
         CK(cudaMemsetAsync(h->presX.p, 0, (size_t)batch * n_in, s));
         xpres = h->presX.p;
     }
-    launch_csr_to_dense_t(dp.p, di.p, dv.p, batch, (int)n_in, h->xT.p, xpres, s);
+    launch_csr_to_dense_t(dp, di, dv, batch, (int)n_in, h->xT.p, xpres, s);
     const bool dev_out = is_device_ptr(y);
     float* yd = y;
     if (!dev_out) {
@@ -1376,27 +1389,24 @@ int sili_layer_backward_sparse(sili_layer* h, const float* x, const int* dptrs, 
     const int64_t n_in = h->rows, n_out = h->cols;
     RC(check_csr(dptrs, didx, batch, dnnz, n_out, "backward_sparse"));
     RC(ensure_aux(h, s));
-    DBuf<float> dxin;
-    RC(dxin.reserve((int64_t)batch * n_in + 1));
-    RC(to_dev(x, dxin.p, (size_t)batch * n_in * 4, s));
-    DBuf<int> dp, di;
-    DBuf<float> dv;
-    RC(dp.reserve(batch + 1)); RC(di.reserve(dnnz + 1)); RC(dv.reserve(dnnz + 1));
-    RC(to_dev(dptrs, dp.p, (size_t)(batch + 1) * 4, s));
-    RC(to_dev(didx, di.p, (size_t)dnnz * 4, s));
-    RC(to_dev(dvals, dv.p, (size_t)dnnz * 4, s));
+    const float* dxin = nullptr;
+    RC(stage_in(h, x, (size_t)batch * n_in, h->x_stage, &dxin, s));
+    const int* dp = nullptr;
+    const int* di = nullptr;
+    const float* dv = nullptr;
+    RC(stage_csr(h, dptrs, didx, dvals, batch, dnnz, &dp, &di, &dv, s));
     // accumulators, sisldo_ops.hpp:611-617
-    launch_accum_abs(dxin.p, h->in_acc.p, batch, n_in, s);
-    launch_accum_abs_csr(dp.p, di.p, dv.p, batch, (int)n_out, h->grad_acc.p, s);
+    launch_accum_abs(dxin, h->in_acc.p, batch, n_in, s);
+    launch_accum_abs_csr(dp, di, dv, batch, (int)n_out, h->grad_acc.p, s);
     // value_scale / value_scale_importance sized to n_in (sisldo_ops.hpp:622-625)
     grow_logical(h, h->vs, h->n_vs, n_in, 1.0f, s);
     RC(h->xT.reserve((int64_t)batch * n_in + 1));
-    launch_transpose(dxin.p, h->xT.p, batch, n_in, s);
+    launch_transpose(dxin, h->xT.p, batch, n_in, s);
     RC(h->dyT.reserve((int64_t)batch * n_out + 1));
     RC(h->presT.reserve((int64_t)batch * n_out + 1));
     CK(cudaMemsetAsync(h->dyT.p, 0, (size_t)batch * n_out * 4, s));
     CK(cudaMemsetAsync(h->presT.p, 0, (size_t)batch * n_out, s));
-    launch_csr_to_dense_t(dp.p, di.p, dv.p, batch, (int)n_out, h->dyT.p, h->presT.p, s);
+    launch_csr_to_dense_t(dp, di, dv, batch, (int)n_out, h->dyT.p, h->presT.p, s);
     RC(h->dxT.reserve((int64_t)batch * n_in + 1));
     RC(h->sgs.reserve(n_in + 1)); RC(h->sgc.reserve(n_in + 1));
     RC(ensure_pow_table(h, beta2, (uint32_t)(h->call + 2)));

@@ -156,6 +156,20 @@ public:
         check(sili_layer_backward_dense(h, (const float*)x, (const float*)dy, batch, lr, flags, beta2, eps, (float*)dx,
                                         (void*)stream));
     }
+    // device-resident variants of forward_sparse / backward_sparse (pointers
+    // to CUDA memory, e.g. torch tensors' data_ptr(); no copies)
+    void forward_sparse_ptr(uintptr_t ptrs, uintptr_t idx, uintptr_t vals, int nnz, int batch, uintptr_t y,
+                            uintptr_t stream) {
+        check(sili_layer_forward_sparse(h, (const int*)ptrs, (const int*)idx, (const float*)vals, nnz, batch,
+                                        (float*)y, (void*)stream));
+    }
+    void backward_sparse_ptr(uintptr_t x, uintptr_t dptrs, uintptr_t didx, uintptr_t dvals, int dnnz, int batch,
+                             float lr, bool lr_per_row_nnz, bool damp, float beta2, float eps, uintptr_t dx,
+                             uintptr_t stream) {
+        unsigned flags = (lr_per_row_nnz ? SILI_LR_PER_ROW_NNZ : 0u) | (damp ? SILI_DAMP_BY_IMPORTANCE : 0u);
+        check(sili_layer_backward_sparse(h, (const float*)x, (const int*)dptrs, (const int*)didx, (const float*)dvals,
+                                         dnnz, batch, lr, flags, beta2, eps, (float*)dx, (void*)stream));
+    }
     void sync() { check(sili_layer_sync(h)); }
     void set_kernel_timing(bool on) { check(sili_layer_set_kernel_timing(h, on ? 1 : 0)); }
     py::tuple kernel_ms() {
@@ -352,6 +366,12 @@ void bind_layer(py::module_& m, const char* name) {
              py::arg("lr_per_row_nnz") = false, py::arg("damp_by_importance") = true, py::arg("beta2") = 0.999f,
              py::arg("eps") = 1e-8f)
         .def("forward_sparse", &T::forward_sparse, py::arg("ptrs"), py::arg("indices"), py::arg("values"), py::arg("batch"))
+        .def("forward_sparse_ptr", &T::forward_sparse_ptr, py::arg("ptrs"), py::arg("indices"), py::arg("values"),
+             py::arg("nnz"), py::arg("batch"), py::arg("y"), py::arg("stream") = 0)
+        .def("backward_sparse_ptr", &T::backward_sparse_ptr, py::arg("x"), py::arg("dy_ptrs"), py::arg("dy_indices"),
+             py::arg("dy_values"), py::arg("dnnz"), py::arg("batch"), py::arg("learning_rate") = 0.01f,
+             py::arg("lr_per_row_nnz") = false, py::arg("damp_by_importance") = true, py::arg("beta2") = 0.999f,
+             py::arg("eps") = 1e-8f, py::arg("dx") = 0, py::arg("stream") = 0)
         .def("backward_sparse", &T::backward_sparse, py::arg("x"), py::arg("dy_ptrs"), py::arg("dy_indices"),
              py::arg("dy_values"), py::arg("batch"), py::arg("learning_rate") = 0.01f, py::arg("lr_per_row_nnz") = false,
              py::arg("damp_by_importance") = true, py::arg("beta2") = 0.999f, py::arg("eps") = 1e-8f)
