@@ -620,7 +620,7 @@ def main():
     ap.add_argument("--no-synap", action="store_true", help="skip the synaptogenesis (config 3) measurement")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the sparse-variant, reference-rule and SpMV measurements")
-    ap.add_argument("--only", choices=["block4", "synap", "folded", "folded4", "rule", "spmv"],
+    ap.add_argument("--only", choices=["block4", "synap", "folded", "folded4", "rule", "spmv", "sparse"],
                     help="run one secondary measurement alone and print its object (profiling)")
     ap.add_argument("--folded-layers", type=int, default=None,
                     help="layers folded per suffix (default: config 5's 40; fewer for small profiling runs)")
@@ -672,6 +672,10 @@ def main():
             out = run_reference_rule(args, dev, S, torch, cpu_sample=False)
         elif args.only == "spmv":
             out = run_spmv(S, torch, dev, cpu_sample=False)
+        elif args.only == "sparse":
+            w0 = make_workload()
+            out = run_sparse_variants([load_layer(S.SparseLinearLayer, *w0[:4], device=dev) for _ in range(4)], S, torch,
+                                      dev, w0, cpu_sample=False)
         else:
             out = run_folded(args, dev, rank, world, dist, S, torch,
                              which="config4" if args.only == "folded4" else "config5")

@@ -87,9 +87,6 @@ void launch_transpose(const float* in, float* out, int64_t R, int64_t C, cudaStr
 void launch_accum_abs(const float* x, float* acc, int B, int64_t n, cudaStream_t s,
                       unsigned long long* nonfinite = nullptr, unsigned long long tag = 0);
 void launch_accum_abs_t(const float* xT, float* acc, int B, int64_t n, cudaStream_t s);
-void launch_accum_abs_csr(const int* ptrs, const int* idx, const float* vals, int rows, int ncols, float* acc,
-                          cudaStream_t s);
-
 // forward: y[B, n_out] from xT [n_in, B]; sparse_formula selects the
 // sisldo_forward arithmetic (sisldo_ops.hpp:289-308) over disldo_forward's.
 void launch_forward(const LayerView& L, const float* xT, int B, float* y, bool sparse_formula,

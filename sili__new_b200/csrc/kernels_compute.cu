@@ -78,23 +78,6 @@ void launch_accum_abs_t(const float* xT, float* acc, int B, int64_t n, cudaStrea
     k_accum_abs_t<<<(unsigned)((n + 127) / 128), 128, 0, s>>>(xT, acc, B, n); count_launch();
 }
 
-// neuron_grad_accum[idx] += |v| over a CSR in entry order (sisldo_ops.hpp:614-617):
-// one thread per batch row would race on shared columns, so a single warp
-// walks the entries in order (the CSR gradient is small: a top-k of dy).
-__global__ void k_accum_abs_csr(const int* __restrict__ ptrs, const int* __restrict__ idx,
-                                const float* __restrict__ vals, int rows, int ncols, float* __restrict__ acc) {
-    if (threadIdx.x != 0) return;
-    const int n = ptrs[rows];
-    for (int j = ptrs[0]; j < n; ++j) {
-        const int c = idx[j];
-        if (c >= 0 && c < ncols) acc[c] = __fadd_rn(acc[c], fabsf(vals[j]));
-    }
-}
-void launch_accum_abs_csr(const int* ptrs, const int* idx, const float* vals, int rows, int ncols, float* acc,
-                          cudaStream_t s) {
-    k_accum_abs_csr<<<1, 32, 0, s>>>(ptrs, idx, vals, rows, ncols, acc); count_launch();
-}
-
 // ── forward ────────────────────────────────────────────────────────────────
 // Output-stationary gather over the CSC shadow: one warp per output column,
 // lanes over batch samples, rows visited in ascending order.  This is the
@@ -839,10 +822,137 @@ __global__ void __launch_bounds__(256) k_backward_sparse(LayerView L, const floa
         }
     }
 }
+// The same for B <= 64, arranged around dy's sparsity: a lane keeps its
+// synapse's column, scales and current byte in registers across the samples,
+// reads its 64 presence flags once as a bit mask and visits only its own
+// present samples (about 3 % of them at a 3 % top-k dy).  Each
+// (synapse, sample) step is k_backward_sparse's, in the same sample order; a
+// lane's dx partial for sample b accumulates over its synapses in the same
+// order (shared memory, [sample][lane]) and the per-sample warp tree is the
+// same, so dx and every code and sum match k_backward_sparse.
+constexpr int kBs64Warps = 4;
+__global__ void __launch_bounds__(kBs64Warps * 32) k_backward_sparse64(LayerView L, const float* __restrict__ xT,
+                                                                      const float* __restrict__ dyT,
+                                                                      const uint8_t* __restrict__ presT, int B,
+                                                                      UpdateParams P, double* __restrict__ sgs_out,
+                                                                      double* __restrict__ sgc_out,
+                                                                      float* __restrict__ dxT) {
+    __shared__ float dxa_s[kBs64Warps][64][32];
+    __shared__ float xs_s[kBs64Warps][64];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t r = (int64_t)blockIdx.x * kBs64Warps + warp;
+    if (r >= L.n_in) return;
+    const int64_t es = L.es[r];
+    const int nnz = (int)(L.ee[r] - es);
+    float* dxr = dxT + r * (int64_t)B;
+    if (nnz == 0) {
+        for (int b = lane; b < B; b += 32) dxr[b] = 0.0f;
+        return;
+    }
+    float (*dxa)[32] = dxa_s[warp];
+    float* xs = xs_s[warp];
+    for (int b = 0; b < 64; ++b) dxa[b][lane] = 0.0f;
+    for (int b = lane; b < 64; b += 32) xs[b] = b < B ? xT[r * B + b] : 0.0f;
+    __syncwarp();
+    const int f0 = L.rowptr[r];
+    const float eff_lr = P.lr_per_row_nnz ? __fdiv_rn(P.lr, (float)nnz) : P.lr;
+    const float onem = __fsub_rn(1.0f, P.beta2);
+    const float imp_scale = L.is[r];
+    const float val_scale = L.vs[r * L.rank];
+    const bool train = P.lr != 0.0f;
+    double sgs = 0.0, sgc = 0.0, sa_new = 0.0, sa_old = 0.0, sq_new = 0.0, sq_old = 0.0;
+    float mx_new = 0.0f;
+    for (int e0 = 0; e0 < nnz; e0 += 32) {
+        const int e = e0 + lane;
+        const bool valid = e < nnz;
+        int c = 0;
+        uint32_t byte = 0;
+        unsigned long long mask = 0ull;
+        float out_scale = 0.0f, cs = 0.0f, cis = 0.0f;
+        if (valid) {
+            c = L.abs_cols[f0 + e];
+            byte = L.val[es + e];
+            out_scale = L.os[(int64_t)c * L.rank];
+            cs = __fmul_rn(val_scale, out_scale);
+            cis = __fmul_rn(imp_scale, L.ois[c]);
+            const uint8_t* pr = presT + (int64_t)c * B;
+            if (B == 64) {
+                const uint4* p4 = reinterpret_cast<const uint4*>(pr);   // c * 64 bytes: 16-byte aligned
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const uint4 v = __ldg(p4 + q);
+                    const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+#pragma unroll
+                        for (int t = 0; t < 4; ++t)
+                            if ((wv[k] >> (8 * t)) & 0xFFu) mask |= 1ull << (q * 16 + k * 4 + t);
+                }
+            } else {
+                for (int b = 0; b < B; ++b)
+                    if (pr[b]) mask |= 1ull << b;
+            }
+        }
+        // this synapse's present samples, in order (lanes independent)
+        while (mask) {
+            const int b = __ffsll((long long)mask) - 1;
+            mask &= mask - 1ull;
+            const float in_val = xs[b];
+            const float w_stored = fp4_decode(byte >> 4);
+            const float w = __fmul_rn(w_stored, cs);
+            const float dyv = dyT[(int64_t)c * B + b];
+            dxa[b][lane] = __fmaf_rn(w, dyv, dxa[b][lane]);
+            if (train) {
+                const float grad = __fmul_rn(dyv, in_val);
+                const float stored_imp = fp4_decode(byte & 15u);
+                float imp = __fmul_rn(stored_imp, cis);
+                const float contrib = __fmul_rn(in_val, w);
+                imp = __fmaf_rn(P.beta2, imp, __fmul_rn(onem, __fmaf_rn(grad, grad, __fmul_rn(contrib, contrib))));
+                const float num = __fmul_rn(-eff_lr, grad);
+                const float step = P.damp ? __fdiv_rn(num, __fadd_rn(__fsqrt_rn(imp), P.eps)) : num;
+                const float new_w = __fadd_rn(w, step);
+                const uint32_t nbyte = (fp4_encode(__fdiv_rn(new_w, cs)) << 4) | fp4_encode(__fdiv_rn(imp, cis));
+                const float ai = fp4_decode(nbyte & 15u);
+                sa_new += fabs((double)ai); sa_old += fabs((double)stored_imp);
+                sq_new += (double)ai * (double)ai; sq_old += (double)stored_imp * (double)stored_imp;
+                mx_new = fmaxf(mx_new, fabsf(ai));
+                sgs += (double)w_stored * (double)out_scale * (double)grad;
+                sgc += (double)w_stored * (double)out_scale * (double)contrib;
+                byte = nbyte;
+            }
+        }
+        if (valid && train) L.val[es + e] = (uint8_t)byte;
+    }
+    __syncwarp();
+    for (int b = 0; b < B; ++b) {
+        const float v = warp_sum(dxa[b][lane]);
+        if (lane == 0) dxr[b] = v;
+    }
+    sgs = warp_sum(sgs); sgc = warp_sum(sgc);
+    sa_new = warp_sum(sa_new); sa_old = warp_sum(sa_old);
+    sq_new = warp_sum(sq_new); sq_old = warp_sum(sq_old);
+    for (int o = 16; o > 0; o >>= 1) mx_new = fmaxf(mx_new, __shfl_xor_sync(0xffffffffu, mx_new, o));
+    if (lane == 0) {
+        sgs_out[r] = sgs;
+        sgc_out[r] = sgc;
+        if (train) {
+            atomicAdd(P.stats + 0, sa_new - sa_old);
+            atomicAdd(P.stats + 1, sq_new - sq_old);
+            atomicMax(reinterpret_cast<unsigned int*>(P.stat_max), __float_as_uint(mx_new));
+        }
+    }
+}
+
 void launch_backward_sparse(const LayerView& L, const float* xT, const float* dyT, const uint8_t* presT, int B,
                             const UpdateParams& P, double* sgs, double* sgc, float* dxT, cudaStream_t s) {
     if (L.n_in == 0) return;
-    k_backward_sparse<<<(unsigned)((L.n_in + 7) / 8), 256, 0, s>>>(L, xT, dyT, presT, B, P, sgs, sgc, dxT); count_launch();
+    if (B <= 64) {
+        k_backward_sparse64<<<(unsigned)((L.n_in + kBs64Warps - 1) / kBs64Warps), kBs64Warps * 32, 0, s>>>(
+            L, xT, dyT, presT, B, P, sgs, sgc, dxT);
+    } else {
+        k_backward_sparse<<<(unsigned)((L.n_in + 7) / 8), 256, 0, s>>>(L, xT, dyT, presT, B, P, sgs, sgc, dxT);
+    }
+    count_launch();
 }
 
 // value_scale after all samples, sisldo_ops.hpp:772-797 (no finiteness guards there).

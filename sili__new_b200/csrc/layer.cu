@@ -1395,9 +1395,8 @@ int sili_layer_backward_sparse(sili_layer* h, const float* x, const int* dptrs, 
     const int* di = nullptr;
     const float* dv = nullptr;
     RC(stage_csr(h, dptrs, didx, dvals, batch, dnnz, &dp, &di, &dv, s));
-    // accumulators, sisldo_ops.hpp:611-617
+    // accumulators, sisldo_ops.hpp:611-617 (the dy part below, from dyT)
     launch_accum_abs(dxin, h->in_acc.p, batch, n_in, s);
-    launch_accum_abs_csr(dp, di, dv, batch, (int)n_out, h->grad_acc.p, s);
     // value_scale / value_scale_importance sized to n_in (sisldo_ops.hpp:622-625)
     grow_logical(h, h->vs, h->n_vs, n_in, 1.0f, s);
     RC(h->xT.reserve((int64_t)batch * n_in + 1));
@@ -1407,6 +1406,10 @@ int sili_layer_backward_sparse(sili_layer* h, const float* x, const int* dptrs, 
     CK(cudaMemsetAsync(h->dyT.p, 0, (size_t)batch * n_out * 4, s));
     CK(cudaMemsetAsync(h->presT.p, 0, (size_t)batch * n_out, s));
     launch_csr_to_dense_t(dp, di, dv, batch, (int)n_out, h->dyT.p, h->presT.p, s);
+    // neuron_grad_accum[c] += |v| over dy's entries in CSR order: per column
+    // that is its samples in order, and an absent entry (0 in dyT) adds +0 to
+    // a non-negative sum, so the per-column sum over dyT is the same sum
+    launch_accum_abs_t(h->dyT.p, h->grad_acc.p, batch, n_out, s);
     RC(h->dxT.reserve((int64_t)batch * n_in + 1));
     RC(h->sgs.reserve(n_in + 1)); RC(h->sgc.reserve(n_in + 1));
     RC(ensure_pow_table(h, beta2, (uint32_t)(h->call + 2)));

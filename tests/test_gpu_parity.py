@@ -159,6 +159,18 @@ def test_forward_row_tiles_vs_oracle(S, n_in, n_out, B):
     assert np.array_equal(yg, yo, equal_nan=True), "forward with an infinite value_scale row"
 
 
+def test_config1_spmv_vs_oracle(S):
+    """4096^2 at 90 % (410 synapses per row), batch 1,
+    x ~ N(0,1), seed 0 (fp32 tolerance at batch <= 8)."""
+    n = 4096
+    p, i, w, vs = random_layer(n, n, 410, seed=0)
+    g = setup_layer(S.SparseLinearLayerDeterministic(n, n, len(i) * 2), p, i, w, vs)
+    o = setup_layer(O.OracleLayer(n, n, len(i) * 2), p, i, w, vs)
+    x = np.random.default_rng(0).normal(0, 1, (1, n)).astype(np.float32)
+    assert_close_sum(g.forward_dense(x), o.forward_dense(x), 1e-5)
+    assert_close_sum(g.forward_dense(x[0]), o.forward_dense(x[0]), 1e-5)   # 1-D input as in the reference
+
+
 def test_sparse_forward_row_tiles_vs_oracle(S):
     n_in, n_out, B = 600, 40000, 32
     p, i, w, vs = random_layer(n_in, n_out, 30, seed=3)
@@ -216,6 +228,28 @@ def test_backward_update_chunks_and_dense_x(S, B, dense_x):
             assert np.array_equal(sg[k], so[k]), f"step {step}: {k}"
         # importance l1 / l2 / max (the value statistics are set at load)
         assert np.array_equal(sg["stats"].astype(np.float32)[3:], so["stats"].astype(np.float32)[3:]), f"step {step}"
+
+
+@pytest.mark.parametrize("B", [64, 33, 100])
+def test_backward_sparse_vs_oracle(S, B):
+    """Sparse-gradient backward (dy as a global top-k CSR, 3 %) over three
+    steps: codes and value scales bit-exact, dx within fp32 tolerance.
+    B = 100 takes the kernel for batches above 64."""
+    n_in, n_out = 400, 700
+    p, i, w, vs = random_layer(n_in, n_out, 40, seed=B, empty_rows=(2,))
+    g = setup_layer(S.SparseLinearLayerDeterministic(n_in, n_out, len(i) * 2), p, i, w, vs, imp_scale=0.02 / 6)
+    o = setup_layer(O.OracleLayer(n_in, n_out, len(i) * 2), p, i, w, vs, imp_scale=0.02 / 6)
+    rng = np.random.default_rng(B + 7)
+    for step in range(3):
+        x = relu_sparse_x(rng, B, n_in)
+        dy = rng.normal(0, 1, (B, n_out)).astype(np.float32)
+        pd, idd, vd = S.dense_to_top_k_csr(dy, int(0.03 * B * n_out))
+        dxg = g.backward_sparse(x, pd, idd, vd, B, 0.02, True)
+        dxo = o.backward_sparse(x, pd, idd, vd, B, 0.02, True)
+        assert_close_sum(dxg, dxo, 1e-5)
+        sg, so = snapshot(g), snapshot(o)
+        for k in ("live_idx", "live_val", "sc_value_scale", "sc_value_scale_importance", "sc_value_scale_step"):
+            assert np.array_equal(sg[k], so[k]), f"step {step}: {k}"
 
 
 def test_stochastic_rounding_unbiased(S):
