@@ -1,6 +1,6 @@
 """Benchmark: FP4 delta-CSR sparse layer, forward + fused backward/update.
 
-Workload: one 8192 x 8192 layer at 95 % sparsity
+Workload (benchmark configuration 2): one 8192 x 8192 layer at 95 % sparsity
 (410 synapses per input row, columns uniform without replacement), batch 64,
 x = ReLU(N(0,1)) with a further 60 % zeroed (~80 % zeros), dy ~ N(0,1); a
 step is forward_dense + backward_dense(learning_rate=0.01, lr_per_row_nnz)
@@ -215,7 +215,7 @@ def block4_codes(work):
 
 
 def run_block4(args, dev, S, torch, work, cpu_sample):
-    """BASELINE config 2 in the block4 format: load_dense_codes makes a tile
+    """Configuration 2 in the block4 format: load_dense_codes makes a tile
     for every 4x4 block of the 8192^2 matrix (4.19 M tiles, 95 % of their
     slots empty), same x and dy; a step is forward_dense +
     backward_dense(lr=0.01) through the public API, timed with CUDA events.
@@ -281,7 +281,7 @@ def run_block4(args, dev, S, torch, work, cpu_sample):
 
 
 def run_synaptogenesis(args, dev, S, torch, cpu_sample):
-    """a 16384^2 layer at 98 % sparsity (328 synapses per
+    """Configuration 3: a 16384^2 layer at 98 % sparsity (328 synapses per
     input row), batch 256, x and dy ~ N(0,1); one step = topk_dyx_step through
     the public API on device pointers: |dy^T x| scored at all 268 M positions
     (fp32, ascending-sample fma chains), exact top-k over the non-existing
@@ -341,7 +341,7 @@ def run_synaptogenesis(args, dev, S, torch, cpu_sample):
 
 
 def run_sparse_variants(layers, S, torch, dev, work, cpu_sample):
-    """BASELINE config 2's sparse-input forward (x as dense_to_csr(x, 0),
+    """Configuration 2's sparse-input forward (x as dense_to_csr(x, 0),
     ~20 % of it non-zero) and sparse-gradient backward (dy as
     dense_to_top_k_csr(dy, 0.03 B n), lr 0.01), on the config-2 layer copies
     (rotated), through the public API with device-resident CSR arrays."""
@@ -401,7 +401,7 @@ def run_sparse_variants(layers, S, torch, dev, work, cpu_sample):
 
 
 def run_reference_rule(args, dev, S, torch, cpu_sample):
-    """BASELINE config 3 with the reference's own grow/prune rule (A11/A12):
+    """Configuration 3 with the reference's own grow/prune rule (A11/A12):
     on the 16384^2 98 % layer (deterministic rounding), after one
     backward_dense(dy, lr=0.01) (non-zero importances) and one
     backward_dense(dy, lr=0) (the neuron accumulators), time build_probes(232)
@@ -464,7 +464,7 @@ def run_reference_rule(args, dev, S, torch, cpu_sample):
 
 
 def run_spmv(S, torch, dev, cpu_sample):
-    """forward_dense at batch 1 on a 4096^2 layer at 90 %
+    """Configuration 1: forward_dense at batch 1 on a 4096^2 layer at 90 %
     (410 synapses per row), x ~ N(0,1), seed 0; rotated over 48 layer copies
     (163 MB of weight streams, above L2), device pointers, CUDA events."""
     from helpers import random_layer
@@ -517,11 +517,11 @@ def run_spmv(S, torch, dev, cpu_sample):
 
 
 FOLDED = {
-    # Mistral-Small-24B shape (hidden 5120, 32 heads / 8 KV
+    # configuration 5: Mistral-Small-24B shape (hidden 5120, 32 heads / 8 KV
     # x 128, FFN 32768, 40 layers), every linear pruned to 95 %, decode batch 32
     "config5": dict(shape="MISTRAL_SMALL_24B", batch=32, density=0.05, kind="decode",
                     label="Mistral-Small-24B shape, {L} layers folded, 95% pruned, batch 32"),
-    # toy Mistral shape (hidden 4096, 32 heads / 8 KV x 128,
+    # configuration 4: toy Mistral shape (hidden 4096, 32 heads / 8 KV x 128,
     # FFN 14336, 32 layers), magnitude-pruned to 90 %, seq 512 x batch 8
     # tokens in one pass
     "config4": dict(shape="TOY_MISTRAL", batch=512 * 8, density=0.10, kind="prefill",

@@ -156,7 +156,7 @@ int sili_layer_expand_headroom(sili_layer* h, float blank_fraction);
 int sili_layer_expand_headroom_to(sili_layer* h, int min_nnz_per_row, float blank_fraction);
 /* zero_accum(), cpu_backend.cpp:851-854 */
 int sili_layer_zero_accum(sili_layer* h);
-/* BASELINE config-3 rule (no reference function): exact top-k of
+/* the top-k growth rule (no reference function): exact top-k of
  * |sum_b x[b,r]*dy[b,c]| over non-existing (r,c), prune the same number of
  * smallest |FP4(w)*S(r,c)|, rebuild the arrays.  x [batch,n_in], dy [batch,n_out]. */
 int sili_layer_topk_dyx_step(sili_layer* h, const float* x, const float* dy, int batch, int64_t k,

@@ -1127,7 +1127,7 @@ int64_t o_top_k_csr(const float* x, int rows, int cols, int64_t k, int* ptrs, in
     return k;
 }
 
-/* ── BASELINE config-3 rule: exact top-k of |sum_b x[b,r] dy[b,c]| ─────── */
+/* ── the top-k growth rule: exact top-k of |sum_b x[b,r] dy[b,c]| ─────── */
 /* Defined here (no reference function exists): score[r,c] = |s| with
  * s = fmaf(x[b,r], dy[b,c], s) for b = 0..B-1 in order from s = 0; candidates
  * are the non-existing (r,c) with the k largest scores, ties toward lower

@@ -113,7 +113,7 @@ void    o_std_sort_keys(const float* keys, int64_t n, int desc, int64_t* perm);
 int64_t o_dense_to_csr(const float* x, int rows, int cols, float threshold, int* ptrs, int* idx, float* vals);
 int64_t o_top_k_csr(const float* x, int rows, int cols, int64_t k, int* ptrs, int* idx, float* vals);
 
-/* BASELINE config-3 rule (no reference function): exact top-k of |dy^T x| */
+/* the top-k growth rule (no reference function): exact top-k of |dy^T x| */
 int64_t o_topk_dyx_candidates(const OLayer* L, const float* x, const float* dy, int batch, int64_t k,
                               int* rows, int* cols, float* scores);
 int     o_topk_dyx_step(OLayer* L, const float* x, const float* dy, int batch, int64_t k);

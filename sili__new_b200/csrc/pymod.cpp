@@ -192,7 +192,7 @@ public:
         check(sili_layer_synap_rows(h, row, 1, cutoff, max_rw, max_prune, eps, &did));
         return did != 0;
     }
-    // BASELINE config-3 growth rule: exact top-k of |dy^T x| over non-existing
+    // The top-k growth rule (benchmark configuration 3): exact top-k of |dy^T x| over non-existing
     // synapses, prune as many smallest |w*S|, rebuild (host or device arrays)
     void topk_dyx_step(farr x, farr dy, int64_t k) {
         if (x.ndim() != 2 || dy.ndim() != 2 || x.shape(0) != dy.shape(0) || x.shape(1) != n_in || dy.shape(1) != n_out)

@@ -1,4 +1,4 @@
-// BASELINE config-3 growth rule on the device: exact top-k of
+// The top-k |dy^T x| growth rule on the device: exact top-k of
 // |sum_b x[b,r] dy[b,c]| over non-existing (r, c), prune as many existing
 // synapses of smallest |w * S(r,c)|, rebuild the delta-CSR.  No reference
 // function exists; the rule is defined (and restated on the CPU by

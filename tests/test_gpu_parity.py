@@ -160,7 +160,7 @@ def test_forward_row_tiles_vs_oracle(S, n_in, n_out, B):
 
 
 def test_config1_spmv_vs_oracle(S):
-    """4096^2 at 90 % (410 synapses per row), batch 1,
+    """Benchmark configuration 1: 4096^2 at 90 % (410 synapses per row), batch 1,
     x ~ N(0,1), seed 0 (fp32 tolerance at batch <= 8)."""
     n = 4096
     p, i, w, vs = random_layer(n, n, 410, seed=0)

@@ -1,4 +1,4 @@
-"""The BASELINE config-3 growth rule (exact top-k of |dy^T x|, prune, rebuild)
+"""The top-k growth rule of benchmark configuration 3 (exact top-k of |dy^T x|, prune, rebuild)
 on the GPU against the CPU oracle's restatement: bit-exact layout, ULEB128
 bytes, codes, out_degree and export."""
 import numpy as np
