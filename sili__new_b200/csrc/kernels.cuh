@@ -39,6 +39,10 @@ struct LayerView {
     const int* b4_nt = nullptr;  // [ceil(n_in/4)] block4 tiles per block-row (null: no block4)
     const int* colptr_x = nullptr;  // [n_out+1] exact (unpadded) column offsets of the same CSC
     const int* cpack = nullptr;     // per padded CSC entry: row << 4 | weight code (padding: n_in << 4)
+    // when set, kernels that rewrite weight codes also rewrite their packed
+    // words: fcpos[f] = the padded CSC position of synapse f (row-major order)
+    int* cpack_upd = nullptr;
+    const int* fcpos = nullptr;
 };
 
 // One layer's block4 store (4x4 dense FP4 tiles, block4.hpp:1016-1490) on the
@@ -128,7 +132,8 @@ void launch_row_nnz(const int64_t* es, const int64_t* ee, int64_t n_in, int* row
 void launch_decode_rows(const LayerView& L, int* abs_cols, int* frow, int* fvpos, int* colcount,
                         cudaStream_t s);
 void launch_gather_csc(const int* sorted_f, const int* sorted_col, const int* frow, const int* fvpos,
-                       const int* colptr, const int* pcolptr, int64_t nnz, int* crow, int* cvpos, cudaStream_t s);
+                       const int* colptr, const int* pcolptr, int64_t nnz, int* crow, int* cvpos, int* fcpos,
+                       cudaStream_t s);
 void launch_pad_csc(const int* colcount, const int* pcolptr, int64_t n_cols, int n_in, int* crow, int* cvpos,
                     cudaStream_t s);
 void launch_pad_counts(const int* colcount, int64_t n, int* out, cudaStream_t s);

@@ -201,11 +201,22 @@ __global__ void __launch_bounds__(256) k_forward_vec(LayerView L, const float* _
         float w = 0.0f, cs = 0.0f;
         if (lid < 8 && kb < len) {
             const int kk = k0 + kb + lid;
-            const int vp = L.cvpos[kk];
-            if (vp >= 0) {
-                const int r = L.crow[kk];
+            // packed word (row << 4 | weight code; padding = row n_in) when
+            // present, else the row and value position separately
+            int r;
+            uint32_t code;
+            if (L.cpack) {
+                const int pk = L.cpack[kk];
+                r = pk >> 4;
+                code = (uint32_t)pk & 15u;
+            } else {
+                const int vp = L.cvpos[kk];
+                r = vp >= 0 ? L.crow[kk] : L.n_in;
+                code = vp >= 0 ? (uint32_t)(L.val[vp] >> 4) : 0u;
+            }
+            if (r < L.n_in) {
                 off = r * B;
-                const float wq = fp4_decode(L.val[vp] >> 4);
+                const float wq = fp4_decode(code);
                 if (SPARSE) {
                     w = wq;
                     cs = __fmul_rn(L.vs[(int64_t)r * L.rank], osk[0]);
@@ -611,6 +622,7 @@ __global__ void __launch_bounds__(kUpdWarps * 32, 6) k_backward_update(LayerView
                 nbyte = (fp4_encode(quant) << 4) | fp4_encode(imp_st);
             }
             L.val[es + e] = (uint8_t)nbyte;
+            if (L.cpack_upd) L.cpack_upd[L.fcpos[f0 + e]] = (int)(((uint32_t)r << 4) | (nbyte >> 4));
             const float ai = fp4_decode(nbyte & 15u);
             sa_new += fabs((double)ai);
             sa_old += fabs((double)ci_orig);
@@ -796,6 +808,7 @@ __global__ void __launch_bounds__(256) k_backward_sparse(LayerView L, const floa
                 const float new_w = __fadd_rn(w, step);
                 const uint32_t nbyte = (fp4_encode(__fdiv_rn(new_w, cs)) << 4) | fp4_encode(__fdiv_rn(imp, cis));
                 L.val[es + e] = (uint8_t)nbyte;
+                if (L.cpack_upd) L.cpack_upd[L.fcpos[f0 + e]] = (int)(((uint32_t)r << 4) | (nbyte >> 4));
                 const float ai = fp4_decode(nbyte & 15u);
                 sa_new += fabs((double)ai); sa_old += fabs((double)stored_imp);
                 sq_new += (double)ai * (double)ai; sq_old += (double)stored_imp * (double)stored_imp;

@@ -57,13 +57,14 @@ void launch_decode_rows(const LayerView& L, int* abs_cols, int* frow, int* fvpos
 __global__ void k_gather_csc(const int* __restrict__ sorted_f, const int* __restrict__ sorted_col,
                              const int* __restrict__ frow, const int* __restrict__ fvpos,
                              const int* __restrict__ colptr, const int* __restrict__ pcolptr, int64_t nnz,
-                             int* __restrict__ crow, int* __restrict__ cvpos) {
+                             int* __restrict__ crow, int* __restrict__ cvpos, int* __restrict__ fcpos) {
     const int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (k >= nnz) return;
     const int f = sorted_f[k], c = sorted_col[k];
     const int64_t o = pcolptr[c] + (k - colptr[c]);
     crow[o] = frow[f];
     cvpos[o] = fvpos[f];
+    fcpos[f] = (int)o;   // where synapse f (row-major order) sits in the padded CSC
 }
 __global__ void k_pad_csc(const int* __restrict__ colcount, const int* __restrict__ pcolptr, int64_t n_cols,
                           int n_in, int* __restrict__ crow, int* __restrict__ cvpos) {
@@ -77,10 +78,11 @@ __global__ void k_pad_counts(const int* __restrict__ colcount, int64_t n, int* _
     if (c < n) out[c] = (colcount[c] + 7) & ~7;
 }
 void launch_gather_csc(const int* sorted_f, const int* sorted_col, const int* frow, const int* fvpos,
-                       const int* colptr, const int* pcolptr, int64_t nnz, int* crow, int* cvpos, cudaStream_t s) {
+                       const int* colptr, const int* pcolptr, int64_t nnz, int* crow, int* cvpos, int* fcpos,
+                       cudaStream_t s) {
     if (nnz == 0) return;
     k_gather_csc<<<(unsigned)((nnz + 255) / 256), 256, 0, s>>>(sorted_f, sorted_col, frow, fvpos, colptr, pcolptr, nnz,
-                                                               crow, cvpos);
+                                                               crow, cvpos, fcpos);
     count_launch();
 }
 void launch_pad_csc(const int* colcount, const int* pcolptr, int64_t n_cols, int n_in, int* crow, int* cvpos,

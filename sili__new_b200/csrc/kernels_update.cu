@@ -185,6 +185,7 @@ __global__ void __launch_bounds__(kU2Warps * 32, u2_min_ctas(RANK)) k_backward_u
             nbyte = (fp4_encode(C.quant) << 4) | fp4_encode(imp_st);
         }
         L.val[es + e] = (uint8_t)nbyte;
+        if (L.cpack_upd) L.cpack_upd[L.fcpos[f0 + e]] = (int)(((uint32_t)r << 4) | (nbyte >> 4));
         const float an = fabsf(fp4_decode(nbyte & 15u)), ao = fabsf(fp4_decode(C.byte & 15u));
         if (an != an || ao != ao) {
             st_nan = true;

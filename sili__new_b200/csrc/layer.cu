@@ -133,6 +133,7 @@ struct sili_layer {
     bool aux_dirty = true;
     DBuf<int> rowptr, abs_cols, frow, fvpos, colcount, colptr, crow, cvpos, sort_k, sort_ko, sort_v, sort_vo;
     DBuf<int> colptr_x, padcnt;   // exact column offsets, padded counts
+    DBuf<int> fcpos;              // padded CSC position of each synapse (row-major order)
     DBuf<int> cpack;              // packed CSC (row << 4 | weight code) for the row-tiled forward
     bool pack_valid = false;      // cpack matches the current weight codes
     DBuf<uint8_t> cub_tmp;
@@ -323,6 +324,7 @@ int ensure_aux(sili_layer* h, cudaStream_t s) {
     const int64_t nzp = nz + 7 * C + 8;   // padded CSC bound
     RC(h->abs_cols.reserve(nz)); RC(h->frow.reserve(nz)); RC(h->fvpos.reserve(nz));
     RC(h->crow.reserve(nzp)); RC(h->cvpos.reserve(nzp)); RC(h->colptr_x.reserve(C + 1)); RC(h->padcnt.reserve(C + 1));
+    RC(h->fcpos.reserve(nz));
     RC(h->sort_k.reserve(nz)); RC(h->sort_ko.reserve(nz)); RC(h->sort_v.reserve(nz)); RC(h->sort_vo.reserve(nz));
     CK(cudaMemsetAsync(h->rowptr.p, 0, sizeof(int), s));
     launch_row_nnz(h->es.p, h->ee.p, R, h->rowptr.p + 1, s);
@@ -348,7 +350,7 @@ int ensure_aux(sili_layer* h, cudaStream_t s) {
     RC(scan_excl_int(h, h->padcnt.p, h->colptr.p, C + 1, s));
     if (nnz > 0)
         launch_gather_csc(h->sort_vo.p, h->sort_ko.p, h->frow.p, h->fvpos.p, h->colptr_x.p, h->colptr.p, nnz,
-                          h->crow.p, h->cvpos.p, s);
+                          h->crow.p, h->cvpos.p, h->fcpos.p, s);
     launch_pad_csc(h->colcount.p, h->colptr.p, C, (int)R, h->crow.p, h->cvpos.p, s);
     CK(cudaGetLastError());
     {   // rows with no synapse take the dead-row bootstrap (linear_disldo.hpp:1985-2042)
@@ -368,7 +370,9 @@ int ensure_aux(sili_layer* h, cudaStream_t s) {
 // changed) where its shape rules allow, else the per-synapse gather kernels.
 int forward_columns(sili_layer* h, const float* xT, int batch, float* y, bool sparse, cudaStream_t s) {
     LayerView v = h->view();
-    if (forward_rows_applies(v, batch)) {
+    if (h->total_nnz > 0 && batch > 8) {
+        // the packed column index: rebuilt here after a change of the weight
+        // codes that did not keep it current (the dense update keeps it)
         const int64_t bound = std::max<int64_t>(h->total_nnz, 1) + 7 * h->cols + 8;   // padded CSC bound
         if (!h->pack_valid) {
             RC(h->cpack.reserve(bound));
@@ -377,7 +381,7 @@ int forward_columns(sili_layer* h, const float* xT, int batch, float* y, bool sp
         }
         v.cpack = h->cpack.p;
         v.colptr_x = h->colptr_x.p;
-        if (launch_forward_rows(v, xT, batch, y, sparse, s)) return SILI_OK;
+        if (forward_rows_applies(v, batch) && launch_forward_rows(v, xT, batch, y, sparse, s)) return SILI_OK;
     }
     launch_forward(v, xT, batch, y, sparse, s);
     return SILI_OK;
@@ -1313,7 +1317,11 @@ int sili_layer_backward_dense(sili_layer* h, const float* x, const float* dy, in
         P.dy_flag = h->d_dyflag.p;
         P.dy_tag = dy_tag;
         h->call++;
-        h->pack_valid = false;   // the update rewrites weight codes
+        if (h->pack_valid) {
+            // the update kernels rewrite the packed words of the codes they rewrite
+            v.cpack_upd = h->cpack.p;
+            v.fcpos = h->fcpos.p;
+        }
         if (h->os_trainable) {
             CK(cudaMemsetAsync(h->colg.p, 0, (size_t)n_out * h->rank * 4, s));
             CK(cudaMemsetAsync(h->colc.p, 0, (size_t)n_out * h->rank * 4, s));

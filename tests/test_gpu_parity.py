@@ -230,6 +230,26 @@ def test_backward_update_chunks_and_dense_x(S, B, dense_x):
         assert np.array_equal(sg["stats"].astype(np.float32)[3:], so["stats"].astype(np.float32)[3:]), f"step {step}"
 
 
+@pytest.mark.parametrize("n_in,n_out,B", [(256, 384, 64), (256, 384, 36), (700, 40000, 32)])
+def test_forward_after_updates_vs_oracle(S, n_in, n_out, B):
+    """The packed column index (row and weight code in one word) is written
+    by the update kernels as they rewrite codes; forwards between training
+    steps must see the new codes (bit-exact y at every step).  The last case
+    takes the lane-per-column forward, the others the per-column gather."""
+    p, i, w, vs = random_layer(n_in, n_out, 30, seed=n_out + B, empty_rows=(3,))
+    g = setup_layer(S.SparseLinearLayerDeterministic(n_in, n_out, len(i) * 2), p, i, w, vs, imp_scale=0.05 / 6)
+    o = setup_layer(O.OracleLayer(n_in, n_out, len(i) * 2), p, i, w, vs, imp_scale=0.05 / 6)
+    rng = np.random.default_rng(B)
+    for step in range(4):
+        x = relu_sparse_x(rng, B, n_in)
+        dy = rng.normal(0, 1, (B, n_out)).astype(np.float32)
+        yg, yo = g.forward_dense(x), o.forward_dense(x)
+        assert np.array_equal(yg, yo), f"step {step}: y differs"
+        g.backward_dense(dy, 0.05, True, True)
+        o.backward_dense(dy, 0.05, True, True)
+    assert np.array_equal(g.forward_dense(x), o.forward_dense(x))
+
+
 @pytest.mark.parametrize("B", [64, 33, 100])
 def test_backward_sparse_vs_oracle(S, B):
     """Sparse-gradient backward (dy as a global top-k CSR, 3 %) over three
