@@ -217,6 +217,37 @@ int sili_layer_b4_rows(sili_layer* h, int64_t* out6);
 /* FoldedLayer's fold sum (sili/sparse_rnn.py:1120-1125) on device arrays:
  * y[b, j] = sum over folds f ascending of raw[b, f*out_dim + j] */
 int sili_fold_sum(const float* raw, int batch, int n_folds, int64_t out_dim, float* y, void* stream);
+/* The backward of the fold sum for one rank's column slice (the np.tile of
+ * FoldedLayer's backward, sili/sparse_rnn.py:1144-1148, restricted to output
+ * columns [j0, j0 + width)): raw[b, f*width + j] = dy[b, j0 + j], dy being
+ * [batch, out_dim] and raw [batch, n_folds * width]; device arrays. */
+int sili_fold_broadcast(const float* dy, int batch, int64_t out_dim, int64_t j0, int64_t width, int n_folds,
+                        float* raw, void* stream);
+
+/* Column shards of one layer.  A folded stack split by output column over
+ * ranks gives each rank every row of the stack but only some columns.  The
+ * synapse updates of disldo_backward (linear_disldo.hpp:790-925) are local
+ * to their (row, column); three things couple a row's columns: the
+ * learning rate lr / nnz_row, the row's value_scale step from sums over all
+ * its synapses (:901-925) and the dead-row bootstrap from sums over all
+ * columns (:1985-2042).  After sili_layer_set_row_shard(global synapse count
+ * per row, global column count) a shard's backward is
+ *   sili_layer_backward_dense_shard(...)  -> partial dx over its columns and
+ *                                            `part` (its part of the row sums)
+ *   sum dx and part over the ranks (e.g. two NCCL all-reduces)
+ *   sili_layer_apply_row_part(summed part) -> the row steps, same on every rank
+ * so every rank's value_scale stays equal to the unsharded layer's (up to
+ * the order of the double sums).  part holds sili_layer_row_part_len
+ * doubles: (value-gradient, contribution) sums per (row, rank-k), then the
+ * dead-row S[batch, rank].  Host or device part arrays; no other forward or
+ * backward of the layer between the two calls.  Not for layers with block4
+ * tiles (SILI_EINVAL).  n = 0 switches sharding off. */
+int sili_layer_set_row_shard(sili_layer* h, const int* global_row_nnz, int64_t n, int64_t global_n_out);
+int sili_layer_row_part_len(sili_layer* h, int batch, int64_t* n);
+int sili_layer_backward_dense_shard(sili_layer* h, const float* x, const float* dy, int batch, float lr,
+                                    unsigned flags, float beta2, float eps, float* dx, double* part,
+                                    void* stream);
+int sili_layer_apply_row_part(sili_layer* h, const double* part, void* stream);
 
 /* ── module functions (cpu_backend.cpp:3075-3196) ───────────────────────── */
 /* fp4_quantize_array: deterministic FP4 encode, fp4quant.hpp:86-121 */

@@ -80,6 +80,10 @@ def lib():
             ("o_output_scale_trainable", _I, [_P]),
             ("o_forward_dense", None, [_P, _P, _I, _P]),
             ("o_backward_dense", None, [_P, _P, _P, _I, _F, _I, _I, _F, _F, _P]),
+            ("o_set_row_shard", _I, [_P, _P, _I64, _I64]),
+            ("o_row_part_len", _I64, [_P, _I]),
+            ("o_backward_dense_shard", _I, [_P, _P, _P, _I, _F, _I, _I, _F, _F, _P, _P]),
+            ("o_apply_row_part", None, [_P, _P, _I, _F, _F, _F, _P]),
             ("o_forward_sparse", None, [_P, _P, _P, _P, _I, _P]),
             ("o_backward_sparse", None, [_P, _P, _P, _P, _P, _I, _F, _I, _I, _F, _F, _P]),
             ("o_build_probes", None, [_P, _I, _I]),
@@ -407,6 +411,35 @@ class OracleLayer(_LayerBase):
         self.L.o_backward_sparse(self.h, _ptr(x), _ptr(p), _ptr(i), _ptr(v), batch, learning_rate,
                                  int(lr_per_row_nnz), int(damp_by_importance), beta2, eps, _ptr(dx))
         return dx
+
+    # column shards (sili_oracle.c, o_set_row_shard): a layer holding some
+    # columns of every row, its row-scale sums returned as parts
+    def set_row_shard(self, global_row_nnz, global_n_out):
+        g = np.ascontiguousarray(global_row_nnz, np.int32)
+        if self.L.o_set_row_shard(self.h, _ptr(g), len(g), int(global_n_out)):
+            raise ValueError("set_row_shard: one count per input row")
+
+    def row_part_len(self, batch):
+        return int(self.L.o_row_part_len(self.h, batch))
+
+    def backward_dense_shard(self, dy, learning_rate, lr_per_row_nnz=False, damp_by_importance=True,
+                             beta2=0.999, eps=1e-8):
+        """Returns (partial dx over this shard's columns, row-sum parts)."""
+        x = self._last
+        dy = np.ascontiguousarray(dy, np.float32).reshape(x.shape[0], self.n_outputs)
+        dx = np.zeros_like(x)
+        part = np.zeros(self.row_part_len(x.shape[0]), np.float64)
+        if self.L.o_backward_dense_shard(self.h, _ptr(x), _ptr(dy), x.shape[0], learning_rate, int(lr_per_row_nnz),
+                                         int(damp_by_importance), beta2, eps, _ptr(dx), _ptr(part)):
+            raise ValueError("backward_dense_shard: no row shard set, or block4 tiles present")
+        self._shard_args = (learning_rate, beta2, eps)
+        return dx, part
+
+    def apply_row_part(self, part):
+        """The row steps with the arguments of the last backward_dense_shard."""
+        part = np.ascontiguousarray(part, np.float64)
+        lr, beta2, eps = self._shard_args
+        self.L.o_apply_row_part(self.h, _ptr(self._last), self._last.shape[0], lr, beta2, eps, _ptr(part))
 
     def build_probes(self, k, per_row=False):
         self.L.o_build_probes(self.h, k, int(per_row))

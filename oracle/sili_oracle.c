@@ -65,6 +65,11 @@ struct OLayer {
      * draws (o_rng_draw, the CUDA path's), 1 = the reference's xorshift64*
      * stream (fp4quant.hpp:170-190) for pinning against its build */
     int ref_stream; uint64_t ref_state;
+    /* column-sharded rows (a layer holding some of the columns of every
+     * row): global synapse count per row and the global column count; during
+     * o_backward_dense_shard the row-scale sums go to shard_part instead of
+     * being applied */
+    int* shard_nnz; int64_t shard_n_out; double* shard_part;
 };
 
 #define NO_LIMIT INT64_MAX
@@ -349,6 +354,7 @@ void o_destroy(OLayer* L) {
     free(L->value_scale_step.d); free(L->output_scale_step.d);
     free(L->in_acc); free(L->grad_acc); free(L->out_degree);
     free(L->prow); free(L->pcol); free(L->pval);
+    free(L->shard_nnz);
     b4_free(L);
     free(L);
 }
@@ -464,8 +470,10 @@ void o_backward_dense(OLayer* L, const float* x, const float* dy, int batch, flo
         for (int64_t r = 0; r < n_in; ++r) {
             const int64_t nnz = row_nnz(L, r);
             if (nnz == 0) continue;
-            const float eff_lr = lr_per_row_nnz ? lr / (float)nnz : lr;
-            const float scale_eff_lr = lr / (float)nnz;
+            /* a column shard divides by the row's global synapse count */
+            const int64_t gnnz = L->shard_part ? (int64_t)L->shard_nnz[r] : nnz;
+            const float eff_lr = lr_per_row_nnz ? lr / (float)gnnz : lr;
+            const float scale_eff_lr = lr / (float)gnnz;
             const float imp_scale = o_get_importance_scale(L, (int)r);
             double sgs[4] = {0, 0, 0, 0}, sgc[4] = {0, 0, 0, 0};
             int64_t pos = L->byte_start[r]; uint32_t col = 0;
@@ -518,6 +526,11 @@ void o_backward_dense(OLayer* L, const float* x, const float* dy, int batch, flo
             if (lr != 0.0f) {
                 for (int64_t k = 0; k < rank; ++k) {
                     const int64_t i = r * rank + k;
+                    if (L->shard_part) {   /* this shard's part of the row sums */
+                        L->shard_part[2 * i] = sgs[k];
+                        L->shard_part[2 * i + 1] = sgc[k];
+                        continue;
+                    }
                     rmsprop_scale_update(&L->value_scale.d[i], &L->value_scale_importance.d[i],
                                          (float)sgs[k], scale_eff_lr, beta2, eps, (float)sgc[k],
                                          &L->value_scale_step.d[i]);
@@ -532,8 +545,21 @@ void o_backward_dense(OLayer* L, const float* x, const float* dy, int batch, flo
         }
     }
     b4_backward(L, x, dy, batch, lr, lr_per_row_nnz, damp, beta2, eps, dx, colg, colc, call);
-    /* dead-row bootstrap, linear_disldo.hpp:1985-2042 */
-    if (lr != 0.0f) {
+    /* dead-row bootstrap, linear_disldo.hpp:1985-2042; a column shard only
+     * sums its columns' part of S (rows dead on every shard take the step in
+     * o_apply_row_part) */
+    if (lr != 0.0f && L->shard_part) {
+        int any_dead = 0;
+        for (int64_t r = 0; r < n_in; ++r) if (L->shard_nnz[r] == 0) { any_dead = 1; break; }
+        double* S = L->shard_part + 2 * n_in * rank;
+        for (int b = 0; b < batch && any_dead; ++b)
+            for (int64_t k = 0; k < rank; ++k) {
+                double sum = 0.0;
+                for (int64_t c = 0; c < n_out; ++c)
+                    sum += (double)o_get_output_scale_k(L, (int)c, (int)k) * (double)dy[(int64_t)b * n_out + c];
+                S[b * rank + k] = sum;
+            }
+    } else if (lr != 0.0f) {
         int any_dead = 0;
         for (int64_t r = 0; r < n_in; ++r) if (row_nnz(L, r) == 0 && b4_row_live(L, r) == 0) { any_dead = 1; break; }
         if (any_dead) {
@@ -589,6 +615,71 @@ void o_backward_dense(OLayer* L, const float* x, const float* dy, int batch, flo
         }
     }
     free(colg); free(colc);
+}
+
+/* ── column shards of one layer (a folded stack split by output column) ──
+ * Every synapse update of disldo_backward is local to its (row, column); what
+ * couples the columns of a row is (a) lr / nnz_row, (b) the row's value_scale
+ * step from sums over all its synapses (linear_disldo.hpp:901-925) and (c) the
+ * dead-row bootstrap's S over all columns (:1985-2042).  A shard takes the
+ * global row counts for (a), returns its part of (b) and (c), and after the
+ * parts are summed over the shards applies the row steps with the totals. */
+int o_set_row_shard(OLayer* L, const int* global_row_nnz, int64_t n, int64_t global_n_out) {
+    free(L->shard_nnz);
+    L->shard_nnz = NULL;
+    if (n == 0) return 0;
+    if (n != L->rows) return 1;
+    L->shard_nnz = (int*)malloc((size_t)n * sizeof(int));
+    memcpy(L->shard_nnz, global_row_nnz, (size_t)n * sizeof(int));
+    L->shard_n_out = global_n_out;
+    return 0;
+}
+int64_t o_row_part_len(const OLayer* L, int batch) { return 2 * L->rows * L->rank + (int64_t)batch * L->rank; }
+
+int o_backward_dense_shard(OLayer* L, const float* x, const float* dy, int batch, float lr, int lr_per_row_nnz,
+                           int damp, float beta2, float eps, float* dx, double* part) {
+    if (!L->shard_nnz || o_b4_ntiles(L) > 0) return 1;   /* block4 tiles: not sharded */
+    memset(part, 0, (size_t)o_row_part_len(L, batch) * sizeof(double));
+    L->shard_part = part;
+    o_backward_dense(L, x, dy, batch, lr, lr_per_row_nnz, damp, beta2, eps, dx);
+    L->shard_part = NULL;
+    return 0;
+}
+
+void o_apply_row_part(OLayer* L, const float* x, int batch, float lr, float beta2, float eps, const double* part) {
+    const int64_t n_in = L->rows, rank = L->rank;
+    if (lr == 0.0f || !L->shard_nnz) return;
+    const double* S = part + 2 * n_in * rank;
+    const float dead_lr = lr / (float)L->shard_n_out;
+    for (int64_t r = 0; r < n_in; ++r) {
+        const int64_t gnnz = L->shard_nnz[r];
+        for (int64_t k = 0; k < rank; ++k) {
+            const int64_t i = r * rank + k;
+            if (gnnz > 0) {
+                rmsprop_scale_update(&L->value_scale.d[i], &L->value_scale_importance.d[i], (float)part[2 * i],
+                                     lr / (float)gnnz, beta2, eps, (float)part[2 * i + 1], &L->value_scale_step.d[i]);
+                continue;
+            }
+            double sum = 0.0;
+            for (int b = 0; b < batch; ++b) {
+                const float iv = x[(int64_t)b * n_in + r];
+                if (iv == 0.0f) continue;
+                sum += (double)iv * S[b * rank + k];
+            }
+            if (sum == 0.0) continue;
+            const float g = (float)sum;
+            if (!isfinite(g)) continue;
+            float* m = &L->value_scale_momentum.d[i];
+            float* v = &L->value_scale_importance.d[i];
+            const float nm = fmaf(0.9f, *m, (1.0f - 0.9f) * g);
+            const float nv = fmaf(beta2, *v, (1.0f - beta2) * (g * g));
+            if (!isfinite(nm) || !isfinite(nv)) continue;
+            const float nvs = L->value_scale.d[i] - dead_lr * nm / (sqrtf(nv) + eps);
+            if (!isfinite(nvs)) continue;
+            *m = nm; *v = nv;
+            L->value_scale.d[i] = nvs;
+        }
+    }
 }
 
 /* ── sisldo_forward, sisldo_ops.hpp:198-340 (scattered part, num_cpus = 1) ─ */

@@ -63,6 +63,14 @@ int     o_output_scale_trainable(const OLayer* L);
 void    o_forward_dense(OLayer* L, const float* x, int batch, float* y);
 void    o_backward_dense(OLayer* L, const float* x, const float* dy, int batch, float lr,
                          int lr_per_row_nnz, int damp, float beta2, float eps, float* dx);
+/* column shards: global row synapse counts, this shard's part of the row
+ * sums ([2*rows*rank] (sgs, sgc) pairs then [batch*rank] dead-row S), the
+ * row steps from the summed parts */
+int     o_set_row_shard(OLayer* L, const int* global_row_nnz, int64_t n, int64_t global_n_out);
+int64_t o_row_part_len(const OLayer* L, int batch);
+int     o_backward_dense_shard(OLayer* L, const float* x, const float* dy, int batch, float lr, int lr_per_row_nnz,
+                               int damp, float beta2, float eps, float* dx, double* part);
+void    o_apply_row_part(OLayer* L, const float* x, int batch, float lr, float beta2, float eps, const double* part);
 void    o_forward_sparse(OLayer* L, const int* ptrs, const int* idx, const float* vals, int batch, float* y);
 void    o_backward_sparse(OLayer* L, const float* x, const int* dptrs, const int* didx, const float* dvals,
                           int batch, float lr, int lr_per_row_nnz, int damp, float beta2, float eps, float* dx);

@@ -84,6 +84,11 @@ struct UpdateParams {
     // treated as "may hold one")
     const unsigned long long* dy_flag = nullptr;
     unsigned long long dy_tag = 0;
+    // column shard of a layer (dense update only): the rows' global synapse
+    // counts divide the learning rate, and each row's value_scale sums go to
+    // row_part[2*(r*rank+k) + {0,1}] instead of being applied
+    const int* row_nnz_g = nullptr;
+    double* row_part = nullptr;
 };
 
 void launch_transpose(const float* in, float* out, int64_t R, int64_t C, cudaStream_t s);
@@ -114,6 +119,11 @@ void launch_backward_update_tiled(const LayerView& L, const float* xT, const flo
                                   const UpdateParams& P, float* dxT, cudaStream_t s);
 void launch_output_scale_update(const LayerView& L, const int* out_degree, const UpdateParams& P,
                                 cudaStream_t s);
+// column shards: this shard's part of the dead-row sums S[b,k] (over its
+// columns), and the row steps from the parts summed over every shard
+void launch_dead_S(const LayerView& L, const float* dy, int B, double* S, cudaStream_t s);
+void launch_apply_row_part(const LayerView& L, const int* row_nnz_g, int64_t g_n_out, const double* part,
+                           const float* xT, int B, const UpdateParams& P, cudaStream_t s);
 void launch_dead_rows(const LayerView& L, const float* xT, const float* dy, int B, double* scratchS,
                       const UpdateParams& P, cudaStream_t s);
 // sparse-gradient backward: dyT/presT dense [n_out, B] with a presence mask
@@ -237,6 +247,8 @@ inline int64_t synap_scratch_stride(int64_t m, int64_t p) {
 // row_used[br] receives the reference's packed byte length of the row.
 // FoldedLayer fold sum: y[B, out_dim] from raw[B, n_folds*out_dim]
 void launch_fold_sum(const float* raw, int B, int n_folds, int64_t out_dim, float* y, cudaStream_t s);
+void launch_fold_broadcast(const float* dy, int B, int64_t out_dim, int64_t j0, int64_t w, int n_folds, float* raw,
+                           cudaStream_t s);
 
 // ── top-k |dy^T x| growth rule (csrc/topk.cu) ───────────────────────────────
 void launch_exist_bits(const int* rowptr, const int* abs_cols, int64_t n_in, int64_t words, uint32_t* bits,

@@ -475,8 +475,9 @@ __global__ void __launch_bounds__(kUpdWarps * 32, 6) k_backward_update(LayerView
     float (*cws)[33] = cws_s[warp];
     float* xs = xs_s[warp];
     const int f0 = L.rowptr[r];
-    const float eff_lr = P.lr_per_row_nnz ? __fdiv_rn(P.lr, (float)nnz) : P.lr;
-    const float scale_eff_lr = __fdiv_rn(P.lr, (float)nnz);
+    const int gnnz = P.row_nnz_g ? P.row_nnz_g[r] : nnz;   // a column shard divides by the global count
+    const float eff_lr = P.lr_per_row_nnz ? __fdiv_rn(P.lr, (float)gnnz) : P.lr;
+    const float scale_eff_lr = __fdiv_rn(P.lr, (float)gnnz);
     const float onem = __fsub_rn(1.0f, P.beta2);
     const float zterm = __fmul_rn(onem, 0.0f);
     const bool fast_ok = (!P.damp || P.eps > 0.0f) && isfinite(eff_lr) && P.beta2 >= 0.0f && P.beta2 <= 1.0f;
@@ -648,7 +649,12 @@ __global__ void __launch_bounds__(kUpdWarps * 32, 6) k_backward_update(LayerView
 #pragma unroll
         for (int k = 0; k < RANK; ++k) {
             const int64_t i = r * RANK + k;
-            rmsprop_scale(L.vs + i, L.vsi + i, (float)sgs[k], scale_eff_lr, (float)sgc[k], L.vstep + i, P);
+            if (P.row_part) {   // a column shard: its part of the row sums
+                P.row_part[2 * i] = sgs[k];
+                P.row_part[2 * i + 1] = sgc[k];
+            } else {
+                rmsprop_scale(L.vs + i, L.vsi + i, (float)sgs[k], scale_eff_lr, (float)sgc[k], L.vstep + i, P);
+            }
         }
     }
     sa_new = warp_sum(sa_new); sa_old = warp_sum(sa_old);
@@ -717,13 +723,9 @@ __global__ void k_dead_S(LayerView L, const float* __restrict__ dy, int B, doubl
         S[(int64_t)b * L.rank + k] = t;
     }
 }
-__global__ void k_dead_rows(LayerView L, const float* __restrict__ xT, int B, const double* __restrict__ S,
-                            UpdateParams P) {
-    const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (r >= L.n_in) return;
-    if (L.ee[r] != L.es[r]) return;
-    if (L.b4_nt && L.b4_nt[r >> 2] > 0) return;   // block4 slots make the row live (:1961-1967)
-    const float dead_lr = __fdiv_rn(P.lr, (float)L.n_out);
+// the Adam step of one dead row from S (linear_disldo.hpp:2000-2040)
+__device__ void dead_row_step(const LayerView& L, const float* __restrict__ xT, int B, const double* __restrict__ S,
+                              int64_t r, float dead_lr, const UpdateParams& P) {
     const float onem = __fsub_rn(1.0f, P.beta2);
     for (int k = 0; k < L.rank; ++k) {
         double sum = 0.0;
@@ -747,11 +749,51 @@ __global__ void k_dead_rows(LayerView L, const float* __restrict__ xT, int B, co
         L.vs[i] = nvs;
     }
 }
+__global__ void k_dead_rows(LayerView L, const float* __restrict__ xT, int B, const double* __restrict__ S,
+                            UpdateParams P) {
+    const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= L.n_in) return;
+    if (L.ee[r] != L.es[r]) return;
+    if (L.b4_nt && L.b4_nt[r >> 2] > 0) return;   // block4 slots make the row live (:1961-1967)
+    dead_row_step(L, xT, B, S, r, __fdiv_rn(P.lr, (float)L.n_out), P);
+}
 void launch_dead_rows(const LayerView& L, const float* xT, const float* dy, int B, double* S,
                       const UpdateParams& P, cudaStream_t s) {
     if (L.n_in == 0 || B == 0) return;
     k_dead_S<<<dim3((unsigned)B, (unsigned)L.rank), 256, 0, s>>>(L, dy, B, S); count_launch();
     k_dead_rows<<<(unsigned)((L.n_in + 127) / 128), 128, 0, s>>>(L, xT, B, S, P); count_launch();
+}
+void launch_dead_S(const LayerView& L, const float* dy, int B, double* S, cudaStream_t s) {
+    if (B == 0) return;
+    k_dead_S<<<dim3((unsigned)B, (unsigned)L.rank), 256, 0, s>>>(L, dy, B, S); count_launch();
+}
+
+// Column shards: the row steps every shard takes after the parts are summed,
+// the value_scale step of a row with synapses on some shard (the row sums of
+// linear_disldo.hpp:901-925 over all its synapses) and the dead-row step of a
+// row with none on any shard (S over every column, lr / global n_out).
+__global__ void k_apply_row_part(LayerView L, const int* __restrict__ row_nnz_g, float dead_lr,
+                                 const double* __restrict__ part, const float* __restrict__ xT, int B,
+                                 UpdateParams P) {
+    const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= L.n_in) return;
+    const int gnnz = row_nnz_g[r];
+    if (gnnz == 0) {
+        dead_row_step(L, xT, B, part + 2 * L.n_in * L.rank, r, dead_lr, P);
+        return;
+    }
+    const float se = __fdiv_rn(P.lr, (float)gnnz);
+    for (int k = 0; k < L.rank; ++k) {
+        const int64_t i = r * L.rank + k;
+        rmsprop_scale(L.vs + i, L.vsi + i, (float)part[2 * i], se, (float)part[2 * i + 1], L.vstep + i, P);
+    }
+}
+void launch_apply_row_part(const LayerView& L, const int* row_nnz_g, int64_t g_n_out, const double* part,
+                           const float* xT, int B, const UpdateParams& P, cudaStream_t s) {
+    if (L.n_in == 0) return;
+    const float dead_lr = P.lr / (float)g_n_out;   // IEEE division, as __fdiv_rn
+    k_apply_row_part<<<(unsigned)((L.n_in + 127) / 128), 128, 0, s>>>(L, row_nnz_g, dead_lr, part, xT, B, P);
+    count_launch();
 }
 
 // ── sparse-gradient backward (disldo_backward_sparse_grad, sisldo_ops.hpp:589-799) ──

@@ -489,4 +489,21 @@ void launch_fold_sum(const float* raw, int B, int n_folds, int64_t out_dim, floa
     k_fold_sum<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(raw, B, n_folds, out_dim, y);
     count_launch();
 }
+// its backward for one column slice: raw[b, f * w + j] = dy[b, j0 + j]
+// (the np.tile of sili/sparse_rnn.py:1144-1148), one thread per output float
+__global__ void k_fold_broadcast(const float* __restrict__ dy, int B, int64_t out_dim, int64_t j0, int64_t w,
+                                 int n_folds, float* __restrict__ raw) {
+    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t row = (int64_t)n_folds * w;
+    if (t >= (int64_t)B * row) return;
+    const int64_t b = t / row, j = (t % row) % w;
+    raw[t] = dy[b * out_dim + j0 + j];
+}
+void launch_fold_broadcast(const float* dy, int B, int64_t out_dim, int64_t j0, int64_t w, int n_folds, float* raw,
+                           cudaStream_t s) {
+    const int64_t n = (int64_t)B * n_folds * w;
+    if (n == 0) return;
+    k_fold_broadcast<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(dy, B, out_dim, j0, w, n_folds, raw);
+    count_launch();
+}
 }  // namespace sili

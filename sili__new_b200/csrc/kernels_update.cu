@@ -76,7 +76,8 @@ __global__ void __launch_bounds__(kU2Warps * 32, u2_min_ctas(RANK)) k_backward_u
     float (*cws)[32] = cws_s[warp];
     float* xs = xs_s[warp];
     const int f0 = L.rowptr[r];
-    const float eff_lr = P.lr_per_row_nnz ? __fdiv_rn(P.lr, (float)nnz) : P.lr;
+    const int gnnz = P.row_nnz_g ? P.row_nnz_g[r] : nnz;   // a column shard divides by the global count
+    const float eff_lr = P.lr_per_row_nnz ? __fdiv_rn(P.lr, (float)gnnz) : P.lr;
     const float beta2 = P.beta2;
     const float onem = __fsub_rn(1.0f, beta2);
     const float zterm = __fmul_rn(onem, 0.0f);
@@ -285,11 +286,16 @@ __global__ void __launch_bounds__(kU2Warps * 32, u2_min_ctas(RANK)) k_backward_u
         sgc[k] = warp_sum(sgc[k]);
     }
     if (lane == 0) {
-        const float scale_eff_lr = __fdiv_rn(P.lr, (float)nnz);
+        const float scale_eff_lr = __fdiv_rn(P.lr, (float)gnnz);
 #pragma unroll
         for (int k = 0; k < RANK; ++k) {
             const int64_t i = r * RANK + k;
-            rmsprop_scale(L.vs + i, L.vsi + i, (float)sgs[k], scale_eff_lr, (float)sgc[k], L.vstep + i, P);
+            if (P.row_part) {   // a column shard: its part of the row sums
+                P.row_part[2 * i] = sgs[k];
+                P.row_part[2 * i + 1] = sgc[k];
+            } else {
+                rmsprop_scale(L.vs + i, L.vsi + i, (float)sgs[k], scale_eff_lr, (float)sgc[k], L.vstep + i, P);
+            }
         }
     }
     l1d = warp_sum(l1d);

@@ -140,6 +140,16 @@ struct sili_layer {
     // scratch
     DBuf<float> xT, dyT, dxT, colg, colc, ytmp, x_stage, dy_stage, dx_stage;
     bool has_dead_rows = false;
+    // column shard (sili_layer_set_row_shard): global synapse count per row,
+    // global column count, whether some row has none anywhere; the
+    // arguments of the last shard backward, which its row steps reuse
+    DBuf<int> shard_nnz;
+    int64_t shard_n_out = 0;
+    bool shard_on = false, shard_any_dead = false;
+    DBuf<double> rpart;
+    float sh_lr = 0.f, sh_beta2 = 0.f, sh_eps = 0.f;
+    unsigned sh_flags = 0;
+    int sh_batch = -1;
     DBuf<uint8_t> presT, presX;
     DBuf<double> dS, sgs, sgc;
     DBuf<int> i_tmp0, i_tmp1, i_tmp2;
@@ -1271,11 +1281,11 @@ int sili_layer_forward_dense(sili_layer* h, const float* x, int batch, float* y,
     return SILI_OK;
 }
 
-int sili_layer_backward_dense(sili_layer* h, const float* x, const float* dy, int batch, float lr, unsigned flags,
-                              float beta2, float eps, float* dx, void* stream) {
-    RC(use(h));
-    if (batch < 0 || !dy || !dx) return fail(SILI_EINVAL, "backward_dense: bad arguments");
-    cudaStream_t s = pick(h, stream);
+// part != nullptr: a column shard's backward (device array of
+// sili_layer_row_part_len doubles, zeroed here; the row steps wait for
+// sili_layer_apply_row_part)
+static int backward_dense_impl(sili_layer* h, const float* x, const float* dy, int batch, float lr, unsigned flags,
+                               float beta2, float eps, float* dx, cudaStream_t s, double* part) {
     const int64_t n_in = h->rows, n_out = h->cols;
     if (x) {
         RC(stage_transposed(h, x, batch, n_in, h->xT, s));
@@ -1316,6 +1326,10 @@ int sili_layer_backward_dense(sili_layer* h, const float* x, const float* dy, in
         P.os_trainable = h->os_trainable;
         P.dy_flag = h->d_dyflag.p;
         P.dy_tag = dy_tag;
+        if (part) {
+            P.row_nnz_g = h->shard_nnz.p;
+            P.row_part = part;
+        }
         h->call++;
         if (h->pack_valid) {
             // the update kernels rewrite the packed words of the codes they rewrite
@@ -1336,7 +1350,10 @@ int sili_layer_backward_dense(sili_layer* h, const float* x, const float* dy, in
         }
         // block4 part after the scattered one (linear_disldo.hpp:939-1951)
         if (h->b4_ntiles > 0) launch_b4_update(v, h->b4view(), h->xT.p, h->dyT.p, batch, P, h->dxT.p, s);
-        if (h->has_dead_rows) {
+        if (part) {
+            // rows with no synapse on any shard: this shard's columns' part of S
+            if (h->shard_any_dead) launch_dead_S(v, dyd, batch, part + 2 * n_in * h->rank, s);
+        } else if (h->has_dead_rows) {
             RC(h->dS.reserve((int64_t)batch * h->rank + 1));
             launch_dead_rows(v, h->xT.p, dyd, batch, h->dS.p, P, s);
         }
@@ -1346,6 +1363,95 @@ int sili_layer_backward_dense(sili_layer* h, const float* x, const float* dy, in
     CK(cudaGetLastError());
     if (!dev_out) CK(cudaMemcpyAsync(dx, dxd, (size_t)batch * n_in * 4, cudaMemcpyDeviceToHost, s));
     if (!dev_out || !is_device_ptr(dy) || (x && !is_device_ptr(x))) CK(cudaStreamSynchronize(s));
+    return SILI_OK;
+}
+
+int sili_layer_backward_dense(sili_layer* h, const float* x, const float* dy, int batch, float lr, unsigned flags,
+                              float beta2, float eps, float* dx, void* stream) {
+    RC(use(h));
+    if (batch < 0 || !dy || !dx) return fail(SILI_EINVAL, "backward_dense: bad arguments");
+    return backward_dense_impl(h, x, dy, batch, lr, flags, beta2, eps, dx, pick(h, stream), nullptr);
+}
+
+// ── column shards (a folded stack split by output column over ranks) ──────
+// Each synapse update is local to its (row, column); lr / nnz_row, the row's
+// value_scale step (sums over all its synapses, linear_disldo.hpp:901-925)
+// and the dead-row bootstrap (S over all columns, :1985-2042) couple a row's
+// columns.  A shard divides by the global counts, hands out its part of the
+// row sums, and applies the row steps once the parts are summed.
+int sili_layer_set_row_shard(sili_layer* h, const int* global_row_nnz, int64_t n, int64_t global_n_out) {
+    RC(use(h));
+    if (n == 0) { h->shard_on = false; return SILI_OK; }
+    if (n != h->rows || !global_row_nnz || global_n_out <= 0)
+        return fail(SILI_EINVAL, "set_row_shard: one global count per input row and a positive column count");
+    if (h->b4_ntiles > 0) return fail(SILI_EINVAL, "set_row_shard: a layer with block4 tiles is not column-sharded");
+    std::vector<int> g((size_t)n);
+    if (is_device_ptr(global_row_nnz)) CK(cudaMemcpy(g.data(), global_row_nnz, (size_t)n * 4, cudaMemcpyDeviceToHost));
+    else std::memcpy(g.data(), global_row_nnz, (size_t)n * 4);
+    bool any_dead = false;
+    for (int64_t r = 0; r < n; ++r) {
+        if (g[r] < 0) return fail(SILI_EINVAL, "set_row_shard: negative synapse count");
+        any_dead |= g[r] == 0;
+    }
+    RC(h->shard_nnz.reserve(n));
+    CK(cudaMemcpy(h->shard_nnz.p, g.data(), (size_t)n * 4, cudaMemcpyHostToDevice));
+    h->shard_n_out = global_n_out;
+    h->shard_any_dead = any_dead;
+    h->shard_on = true;
+    return SILI_OK;
+}
+
+int sili_layer_row_part_len(sili_layer* h, int batch, int64_t* n) {
+    RC(use(h));
+    if (!n || batch < 0) return fail(SILI_EINVAL, "row_part_len: bad arguments");
+    *n = 2 * h->rows * h->rank + (int64_t)batch * h->rank;
+    return SILI_OK;
+}
+
+int sili_layer_backward_dense_shard(sili_layer* h, const float* x, const float* dy, int batch, float lr,
+                                    unsigned flags, float beta2, float eps, float* dx, double* part, void* stream) {
+    RC(use(h));
+    if (batch < 0 || !dy || !dx || !part) return fail(SILI_EINVAL, "backward_dense_shard: bad arguments");
+    if (!h->shard_on) return fail(SILI_EINVAL, "backward_dense_shard: no row shard set (sili_layer_set_row_shard)");
+    if (h->b4_ntiles > 0) return fail(SILI_EINVAL, "backward_dense_shard: a layer with block4 tiles is not column-sharded");
+    cudaStream_t s = pick(h, stream);
+    const int64_t len = 2 * h->rows * h->rank + (int64_t)batch * h->rank;
+    double* pd = part;
+    const bool dev_part = is_device_ptr(part);
+    if (!dev_part) {
+        RC(h->rpart.reserve(len + 1));
+        pd = h->rpart.p;
+    }
+    CK(cudaMemsetAsync(pd, 0, (size_t)len * sizeof(double), s));
+    RC(backward_dense_impl(h, x, dy, batch, lr, flags, beta2, eps, dx, s, pd));
+    h->sh_lr = lr; h->sh_beta2 = beta2; h->sh_eps = eps; h->sh_flags = flags; h->sh_batch = batch;
+    if (!dev_part) {
+        CK(cudaMemcpyAsync(part, pd, (size_t)len * sizeof(double), cudaMemcpyDeviceToHost, s));
+        CK(cudaStreamSynchronize(s));
+    }
+    return SILI_OK;
+}
+
+int sili_layer_apply_row_part(sili_layer* h, const double* part, void* stream) {
+    RC(use(h));
+    if (!part) return fail(SILI_EINVAL, "apply_row_part: bad arguments");
+    if (!h->shard_on || h->sh_batch < 0)
+        return fail(SILI_EINVAL, "apply_row_part: no shard backward to complete (sili_layer_backward_dense_shard)");
+    const int batch = h->sh_batch;
+    h->sh_batch = -1;
+    if (h->sh_lr == 0.0f) return SILI_OK;
+    cudaStream_t s = pick(h, stream);
+    const int64_t len = 2 * h->rows * h->rank + (int64_t)batch * h->rank;
+    const double* pd = part;
+    if (!is_device_ptr(part)) {
+        RC(h->rpart.reserve(len + 1));
+        CK(cudaMemcpyAsync(h->rpart.p, part, (size_t)len * sizeof(double), cudaMemcpyHostToDevice, s));
+        pd = h->rpart.p;
+    }
+    UpdateParams P = update_params(h, h->sh_lr, h->sh_flags, h->sh_beta2, h->sh_eps);
+    launch_apply_row_part(h->view(), h->shard_nnz.p, h->shard_n_out, pd, h->xT.p, batch, P, s);
+    CK(cudaGetLastError());
+    if (!is_device_ptr(part)) CK(cudaStreamSynchronize(s));
     return SILI_OK;
 }
 
@@ -2294,6 +2400,15 @@ int sili_fold_sum(const float* raw, int batch, int n_folds, int64_t out_dim, flo
     if (batch < 0 || n_folds < 0 || out_dim < 0 || !raw || !y) return fail(SILI_EINVAL, "fold_sum: bad arguments");
     if (!is_device_ptr(raw) || !is_device_ptr(y)) return fail(SILI_EINVAL, "fold_sum: device pointers expected");
     launch_fold_sum(raw, batch, n_folds, out_dim, y, (cudaStream_t)stream);
+    CK(cudaGetLastError());
+    return SILI_OK;
+}
+int sili_fold_broadcast(const float* dy, int batch, int64_t out_dim, int64_t j0, int64_t width, int n_folds,
+                        float* raw, void* stream) {
+    if (batch < 0 || n_folds < 0 || out_dim < 0 || j0 < 0 || width < 0 || j0 + width > out_dim || !dy || !raw)
+        return fail(SILI_EINVAL, "fold_broadcast: bad arguments");
+    if (!is_device_ptr(dy) || !is_device_ptr(raw)) return fail(SILI_EINVAL, "fold_broadcast: device pointers expected");
+    launch_fold_broadcast(dy, batch, out_dim, j0, width, n_folds, raw, (cudaStream_t)stream);
     CK(cudaGetLastError());
     return SILI_OK;
 }

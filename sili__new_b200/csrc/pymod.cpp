@@ -37,6 +37,7 @@ void check(int rc) {
 using farr = py::array_t<float, py::array::c_style | py::array::forcecast>;
 using iarr = py::array_t<int, py::array::c_style | py::array::forcecast>;
 using u8arr = py::array_t<uint8_t, py::array::c_style | py::array::forcecast>;
+using darr = py::array_t<double, py::array::c_style | py::array::forcecast>;
 
 std::mutex g_live_mu;
 std::set<sili_layer*> g_live;
@@ -114,6 +115,40 @@ public:
         check(sili_layer_backward_dense(h, nullptr, (const float*)b.ptr, batch, lr, flags, beta2, eps,
                                         dx.mutable_data(), nullptr));
         return dx;
+    }
+
+    // column shards (sili_layer_set_row_shard): host-array variants
+    void set_row_shard(iarr global_row_nnz, int64_t global_n_out) {
+        check(sili_layer_set_row_shard(h, global_row_nnz.data(), (int64_t)global_row_nnz.size(), global_n_out));
+    }
+    int64_t row_part_len(int batch) {
+        int64_t n = 0;
+        check(sili_layer_row_part_len(h, batch, &n));
+        return n;
+    }
+    py::tuple backward_dense_shard(farr dy, float lr, bool lr_per_row_nnz, bool damp, float beta2, float eps) {
+        auto b = dy.request();
+        int batch = 0, cols = 0;
+        check(sili_layer_last_input(h, nullptr, &batch, &cols));
+        if (batch == 0) throw std::runtime_error("backward_dense_shard: no forward_dense input to differentiate");
+        if ((int64_t)b.size != (int64_t)batch * n_out) throw py::value_error("backward_dense_shard: dy shape does not match the last forward");
+        warn_lr(lr);
+        py::array_t<float> dx({(py::ssize_t)batch, (py::ssize_t)n_in});
+        py::array_t<double> part((py::ssize_t)row_part_len(batch));
+        unsigned flags = (lr_per_row_nnz ? SILI_LR_PER_ROW_NNZ : 0u) | (damp ? SILI_DAMP_BY_IMPORTANCE : 0u);
+        check(sili_layer_backward_dense_shard(h, nullptr, (const float*)b.ptr, batch, lr, flags, beta2, eps,
+                                              dx.mutable_data(), part.mutable_data(), nullptr));
+        return py::make_tuple(dx, part);
+    }
+    void apply_row_part(darr part) { check(sili_layer_apply_row_part(h, part.data(), nullptr)); }
+    void backward_dense_shard_ptr(uintptr_t dy, int batch, float lr, bool lr_per_row_nnz, bool damp, float beta2,
+                                  float eps, uintptr_t dx, uintptr_t part, uintptr_t stream) {
+        unsigned flags = (lr_per_row_nnz ? SILI_LR_PER_ROW_NNZ : 0u) | (damp ? SILI_DAMP_BY_IMPORTANCE : 0u);
+        check(sili_layer_backward_dense_shard(h, nullptr, (const float*)dy, batch, lr, flags, beta2, eps, (float*)dx,
+                                              (double*)part, (void*)stream));
+    }
+    void apply_row_part_ptr(uintptr_t part, uintptr_t stream) {
+        check(sili_layer_apply_row_part(h, (const double*)part, (void*)stream));
     }
 
     // cpu_backend.cpp:28-41: one-time warning above the validated lr range.
@@ -380,6 +415,17 @@ void bind_layer(py::module_& m, const char* name) {
         .def("backward_dense_ptr", &T::backward_dense_ptr, py::arg("dy_ptr"), py::arg("batch"), py::arg("learning_rate"),
              py::arg("lr_per_row_nnz") = false, py::arg("damp_by_importance") = true, py::arg("beta2") = 0.999f,
              py::arg("eps") = 1e-8f, py::arg("dx_ptr") = 0, py::arg("stream") = 0, py::arg("x_ptr") = 0)
+        .def("set_row_shard", &T::set_row_shard, py::arg("global_row_nnz"), py::arg("global_n_outputs"))
+        .def("row_part_len", &T::row_part_len, py::arg("batch"))
+        .def("backward_dense_shard", &T::backward_dense_shard, py::arg("dy"), py::arg("learning_rate"),
+             py::arg("lr_per_row_nnz") = false, py::arg("damp_by_importance") = true, py::arg("beta2") = 0.999f,
+             py::arg("eps") = 1e-8f)
+        .def("apply_row_part", &T::apply_row_part, py::arg("part"))
+        .def("backward_dense_shard_ptr", &T::backward_dense_shard_ptr, py::arg("dy_ptr"), py::arg("batch"),
+             py::arg("learning_rate"), py::arg("lr_per_row_nnz") = false, py::arg("damp_by_importance") = true,
+             py::arg("beta2") = 0.999f, py::arg("eps") = 1e-8f, py::arg("dx_ptr") = 0, py::arg("part_ptr") = 0,
+             py::arg("stream") = 0)
+        .def("apply_row_part_ptr", &T::apply_row_part_ptr, py::arg("part_ptr"), py::arg("stream") = 0)
         .def("sync", &T::sync)
         .def("set_kernel_timing", &T::set_kernel_timing, py::arg("enable"))
         .def("kernel_ms", &T::kernel_ms)
@@ -503,6 +549,11 @@ PYBIND11_MODULE(_cuda, m) {
     m.def("fold_sum_ptr", [](uintptr_t raw, int batch, int n_folds, int64_t out_dim, uintptr_t y, uintptr_t stream) {
         check(sili_fold_sum((const float*)raw, batch, n_folds, out_dim, (float*)y, (void*)stream));
     }, py::arg("raw"), py::arg("batch"), py::arg("n_folds"), py::arg("out_dim"), py::arg("y"), py::arg("stream") = 0);
+    m.def("fold_broadcast_ptr", [](uintptr_t dy, int batch, int64_t out_dim, int64_t j0, int64_t width, int n_folds,
+                                   uintptr_t raw, uintptr_t stream) {
+        check(sili_fold_broadcast((const float*)dy, batch, out_dim, j0, width, n_folds, (float*)raw, (void*)stream));
+    }, py::arg("dy"), py::arg("batch"), py::arg("out_dim"), py::arg("j0"), py::arg("width"), py::arg("n_folds"),
+       py::arg("raw"), py::arg("stream") = 0);
     m.def("kernel_launches", []() { int64_t n = 0; sili_kernel_launches(&n); return n; });
     m.def("dense_to_csr", [](farr x, float thr) {
         auto b = x.request();

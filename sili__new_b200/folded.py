@@ -13,8 +13,17 @@ slice of the fold-summed output (the fold sum stays local because every fold
 of a column lives on the same rank) and the slices are all-gathered over
 NCCL into the full ``[B, out_dim]``.  Per-rank work is 1/w of the stack.
 
-The compute is the library's own (``forward_dense_ptr`` and the fold-sum
-kernel); torch provides device memory, streams and torch.distributed.
+Training (FoldedLayer's backward, sili/sparse_rnn.py:1135-1157): dy
+``[B, out_dim]`` is broadcast to every fold of the rank's columns, the local
+layer runs the fused update as a column shard of the whole stack (global
+synapse counts per row; its part of the rows' value_scale sums handed out),
+and two all-reduces sum the partial dx ``[B, in_dim]`` and the row parts,
+after which every rank applies the same row steps, so value_scale stays
+replicated.
+
+The compute is the library's own (``forward_dense_ptr``, the fused update,
+the fold-sum and fold-broadcast kernels); torch provides device memory,
+streams and torch.distributed.
 """
 from __future__ import annotations
 
@@ -72,6 +81,9 @@ class Suffix:
     raw: object = None      # device scratch [B, n_folds * width]
     part: object = None     # device slice of the output [B, width]
     gathered: object = None  # device [world, B, slice]
+    dyraw: object = None    # device [B, n_folds * width]: dy broadcast over the folds
+    dx: object = None       # device [B, in_dim]
+    rpart: object = None    # device float64: this rank's part of the row sums
 
 
 @dataclass
@@ -110,14 +122,60 @@ class FoldedStack:
             p.layer.load_weights(ptrs, idx, vals)
         for r in range(p.in_dim):
             p.layer.set_value_scale_raw(r, float(value_scale))
+        if self.world > 1:
+            # the rows' synapse counts over the whole stack (every rank holds
+            # every row): the learning-rate divisor and the dead-row test
+            if hasattr(ptrs, "data_ptr"):
+                cnt = (ptrs[1:] - ptrs[:-1]).to("cpu").numpy().astype(np.int32)
+            else:
+                cnt = np.diff(np.asarray(ptrs, np.int64)).astype(np.int32)
+            p.layer.set_row_shard(self._sum_over_ranks(cnt), self.n_folds * p.out_dim)
+
+    def _sum_over_ranks(self, a: np.ndarray) -> np.ndarray:
+        import torch
+        import torch.distributed as dist
+        t = torch.from_numpy(np.ascontiguousarray(a))
+        if dist.get_backend(self.group) == "nccl":
+            t = t.cuda()
+        dist.all_reduce(t, group=self.group)
+        return t.cpu().numpy()
+
+    def _broadcast_host(self, name: str, dy: np.ndarray) -> np.ndarray:
+        """dy [B, out_dim] -> [B, n_folds * width] over this rank's columns
+        (the np.tile of sili/sparse_rnn.py:1144-1148); a rank with no columns
+        gets the one zero column its placeholder layer has."""
+        p = self.parts[name]
+        w = self.width(name)
+        dy = np.asarray(dy, np.float32).reshape(-1, p.out_dim)
+        if w == 0:
+            return np.zeros((dy.shape[0], 1), np.float32)
+        return np.ascontiguousarray(np.tile(dy[:, None, p.j0:p.j1], (1, self.n_folds, 1)).reshape(dy.shape[0], -1))
+
+    def backward_host(self, name: str, dy: np.ndarray, lr: float, lr_per_row_nnz: bool = True,
+                      damp_by_importance: bool = True, beta2: float = 0.999, eps: float = 1e-8) -> np.ndarray:
+        """FoldedLayer's backward for one suffix (lr_per_row_nnz=True as
+        sili/sparse_rnn.py:1152 passes): returns dx [B, in_dim] and updates
+        the rank's synapses and (replicated) row scales."""
+        import torch
+        p = self.parts[name]
+        raw = self._broadcast_host(name, dy)
+        if self.world == 1:
+            return p.layer.backward_dense(raw, lr, lr_per_row_nnz, damp_by_importance, beta2, eps)
+        import torch.distributed as dist
+        dx, part = p.layer.backward_dense_shard(raw, lr, lr_per_row_nnz, damp_by_importance, beta2, eps)
+        t_dx, t_part = torch.from_numpy(np.ascontiguousarray(dx)), torch.from_numpy(np.ascontiguousarray(part))
+        dist.all_reduce(t_dx, group=self.group)
+        dist.all_reduce(t_part, group=self.group)
+        p.layer.apply_row_part(t_part.numpy())
+        return t_dx.numpy()
 
     # ── host path (any layer object with forward_dense; CPU ranks use gloo) ──
     def forward_host(self, name: str, x: np.ndarray) -> np.ndarray:
         import torch
         p = self.parts[name]
         w = self.width(name)
-        raw = p.layer.forward_dense(x) if w > 0 else np.zeros((x.shape[0], 0), np.float32)
-        part = fold_sum_host(raw, self.n_folds, w)
+        raw = p.layer.forward_dense(x)     # a rank with no columns: one zero column, ignored
+        part = fold_sum_host(raw[:, : self.n_folds * w], self.n_folds, w)
         if self.world == 1:
             return part
         import torch.distributed as dist
@@ -141,8 +199,10 @@ class FoldedStack:
             p.raw = torch.empty(b, max(self.n_folds * w, 1), device=x.device)
             p.part = torch.zeros(b, s, device=x.device)
             p.gathered = torch.empty(self.world, b, s, device=x.device)
+        # a rank with no columns still runs its placeholder layer (one zero
+        # column) so that it holds the input its backward needs
+        p.layer.forward_dense_ptr(x.data_ptr(), b, p.raw.data_ptr(), stream.cuda_stream)
         if w > 0:
-            p.layer.forward_dense_ptr(x.data_ptr(), b, p.raw.data_ptr(), stream.cuda_stream)
             if w == s:
                 _cuda.fold_sum_ptr(p.raw.data_ptr(), b, self.n_folds, w, p.part.data_ptr(), stream.cuda_stream)
             else:
@@ -155,6 +215,40 @@ class FoldedStack:
         with torch.cuda.stream(stream):
             dist.all_gather_into_tensor(p.gathered, p.part, group=self.group)
         return p.gathered.permute(1, 0, 2).reshape(b, self.world * s)[:, : p.out_dim]
+
+    def backward_device(self, name: str, dy, lr: float, stream, lr_per_row_nnz: bool = True,
+                        damp_by_importance: bool = True, beta2: float = 0.999, eps: float = 1e-8):
+        """dy: torch CUDA tensor [B, out_dim] on `stream` (the gradient of the
+        last forward_device output); returns dx [B, in_dim] (a buffer reused
+        by the next call) and updates the rank's synapses and row scales:
+        fold-broadcast kernel, fused update as a column shard, NCCL
+        all-reduces of dx and of the row parts, then the row steps."""
+        import torch
+        from . import _cuda
+        p = self.parts[name]
+        b = dy.shape[0]
+        w = self.width(name)
+        dy = dy.contiguous()
+        if p.dyraw is None or p.dyraw.shape[0] != b:
+            p.dyraw = torch.zeros(b, max(self.n_folds * w, 1), device=dy.device)
+            p.dx = torch.empty(b, p.in_dim, device=dy.device)
+            if self.world > 1:
+                p.rpart = torch.empty(p.layer.row_part_len(b), dtype=torch.float64, device=dy.device)
+        if w > 0:
+            _cuda.fold_broadcast_ptr(dy.data_ptr(), b, p.out_dim, p.j0, w, self.n_folds, p.dyraw.data_ptr(),
+                                     stream.cuda_stream)
+        if self.world == 1:
+            p.layer.backward_dense_ptr(p.dyraw.data_ptr(), b, lr, lr_per_row_nnz, damp_by_importance, beta2, eps,
+                                       p.dx.data_ptr(), stream.cuda_stream)
+            return p.dx
+        import torch.distributed as dist
+        p.layer.backward_dense_shard_ptr(p.dyraw.data_ptr(), b, lr, lr_per_row_nnz, damp_by_importance, beta2, eps,
+                                         p.dx.data_ptr(), p.rpart.data_ptr(), stream.cuda_stream)
+        with torch.cuda.stream(stream):
+            dist.all_reduce(p.dx, group=self.group)
+            dist.all_reduce(p.rpart, group=self.group)
+        p.layer.apply_row_part_ptr(p.rpart.data_ptr(), stream.cuda_stream)
+        return p.dx
 
 
 # ── synthetic stacks (random init, magnitude-pruned shape) ───────────────────

@@ -2,8 +2,11 @@
 
 CPU: two gloo ranks, each with its column slice of every fold (the oracle
 layer as the rank-local compute), reproduce the unsharded fold-summed output
-bit for bit.  GPU: the device path (forward_dense_ptr + fold-sum kernel)
-against the host path on the same CUDA layers."""
+bit for bit, and the sharded training step (column-shard backward, summed
+row parts, row steps) reproduces the unsharded layer's update: synapse codes
+bit for bit, dx and value_scale to fp32/fp64 summation-order tolerance.
+GPU: the device path (forward_dense_ptr + fold-sum kernel, fold-broadcast +
+column-shard update) against the host path and the oracle."""
 import os
 import socket
 
@@ -99,3 +102,191 @@ def test_device_path_matches_host_path():
         yd = st.forward_device(name, xd, stream)
         stream.synchronize()
         assert np.array_equal(yd.cpu().numpy(), st.forward_host(name, x)), name
+
+
+# ── training: column-shard backward ─────────────────────────────────────────
+TRAIN = {"a": SUFFIXES["a"]}
+LR = 0.05
+
+
+def _train_csr():
+    """Stacked CSR of suffix "a" with a row that has no synapse anywhere
+    (row 5: the dead-row bootstrap) and a row whose synapses all lie in
+    columns j < 11, i.e. on rank 0 of two (row 7: dead on rank 1 only)."""
+    rng = np.random.default_rng(5)
+    in_dim, out_dim = TRAIN["a"]
+    n_cols = N_FOLDS * out_dim
+    ptrs, idx, vals = [0], [], []
+    for r in range(in_dim):
+        if r == 5:
+            cols = np.zeros(0, np.int64)
+        elif r == 7:
+            allowed = np.array([f * out_dim + j for f in range(N_FOLDS) for j in range(11)])
+            cols = np.sort(rng.choice(allowed, 6, replace=False))
+        else:
+            cols = np.sort(rng.choice(n_cols, 9, replace=False))
+        idx += list(cols)
+        vals += list(rng.normal(0.0, 1.5, len(cols)))
+        ptrs.append(len(idx))
+    return np.array(ptrs, np.int32), np.array(idx, np.int32), np.array(vals, np.float32)
+
+
+def _train_data(step):
+    rng = np.random.default_rng(100 + step)
+    x = np.maximum(rng.normal(0, 1, (12, TRAIN["a"][0])), 0).astype(np.float32)
+    dy = rng.normal(0, 1, (12, TRAIN["a"][1])).astype(np.float32)
+    return x, dy
+
+
+def _unsharded(factory, steps):
+    st = FoldedStack(dict(TRAIN), N_FOLDS, 0, 1, factory)
+    p, i, w = _train_csr()
+    st.load("a", p, i, w, len(i), 0.01)
+    dxs = []
+    for step in range(steps):
+        x, dy = _train_data(step)
+        st.forward_host("a", x)
+        dxs.append(st.backward_host("a", dy, LR))
+    return st.parts["a"].layer, dxs
+
+
+def _layer_state(layer, in_dim):
+    ptrs, idx, wv, imp = layer.export()[:4]
+    vs = np.array([layer.get_value_scale(r) for r in range(in_dim)], np.float32)
+    vsi = np.array([layer.get_value_scale_importance(r) for r in range(in_dim)], np.float32)
+    return dict(ptrs=np.asarray(ptrs), idx=np.asarray(idx), w=np.asarray(wv), imp=np.asarray(imp), vs=vs, vsi=vsi)
+
+
+def _check_shard(want_layer, got, rank, world):
+    """A rank's local layer state against the unsharded layer's columns."""
+    in_dim, out_dim = TRAIN["a"]
+    ref = _layer_state(want_layer, in_dim)
+    j0, j1 = column_slice(out_dim, rank, world)
+    lp, li, lw = shard_csr(ref["ptrs"], ref["idx"], ref["w"], N_FOLDS, out_dim, j0, j1)
+    _, _, lm = shard_csr(ref["ptrs"], ref["idx"], ref["imp"], N_FOLDS, out_dim, j0, j1)
+    assert np.array_equal(got["ptrs"], lp) and np.array_equal(got["idx"], li)
+    assert np.array_equal(got["w"], lw), f"rank {rank}: weight codes"
+    assert np.array_equal(got["imp"], lm), f"rank {rank}: importance codes"
+    np.testing.assert_allclose(got["vs"], ref["vs"], rtol=1e-6, err_msg=f"rank {rank}: value_scale")
+    np.testing.assert_allclose(got["vsi"], ref["vsi"], rtol=1e-5, atol=1e-30, err_msg=f"rank {rank}: importance")
+
+
+def _shard_layers(factory, world):
+    """Column-shard layers of the training stack built directly (no
+    process group): global row counts from the unsharded CSR."""
+    in_dim, out_dim = TRAIN["a"]
+    p, i, w = _train_csr()
+    layers = []
+    for rank in range(world):
+        j0, j1 = column_slice(out_dim, rank, world)
+        lp, li, lw = shard_csr(p, i, w, N_FOLDS, out_dim, j0, j1)
+        L = factory(in_dim, max(N_FOLDS * (j1 - j0), 1), max(len(li), 1))
+        L.load_weights(lp, li, lw)
+        for r in range(in_dim):
+            L.set_value_scale_raw(r, 0.01)
+        L.set_row_shard(np.diff(p).astype(np.int32), N_FOLDS * out_dim)
+        layers.append((L, j0, j1))
+    return layers
+
+
+def _sharded_steps(layers, steps):
+    out_dim = TRAIN["a"][1]
+    dxs = []
+    for step in range(steps):
+        x, dy = _train_data(step)
+        parts, dx = [], 0
+        for L, j0, j1 in layers:
+            L.forward_dense(x)
+            raw = np.ascontiguousarray(np.tile(dy[:, None, j0:j1], (1, N_FOLDS, 1)).reshape(len(dy), -1))
+            d, part = L.backward_dense_shard(raw, LR, True)
+            dx = dx + d
+            parts.append(part)
+        total = np.sum(parts, axis=0)
+        for L, _, _ in layers:
+            L.apply_row_part(total)
+        dxs.append(dx)
+    return dxs
+
+
+def test_row_shard_parts_reproduce_unsharded_update():
+    """The split of disldo_backward into column shards (global row counts,
+    summed row parts, row steps) against the unsharded oracle layer."""
+    want, want_dx = _unsharded(_oracle, 3)
+    layers = _shard_layers(_oracle, 2)
+    got_dx = _sharded_steps(layers, 3)
+    for a, b in zip(got_dx, want_dx):
+        np.testing.assert_allclose(a, b, rtol=1e-5, atol=1e-6)
+    in_dim = TRAIN["a"][0]
+    for rank, (L, _, _) in enumerate(layers):
+        _check_shard(want, _layer_state(L, in_dim), rank, 2)
+    # the dead row took the bootstrap step, identically on both ranks
+    vs5 = [L.get_value_scale(5) for L, _, _ in layers]
+    assert vs5[0] == vs5[1] == want.get_value_scale(5) != np.float32(0.01)
+
+
+def _train_rank_main(rank, world, port, out):
+    import torch.distributed as dist
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    st = FoldedStack(dict(TRAIN), N_FOLDS, rank, world, _oracle)
+    p, i, w = _train_csr()
+    j0, j1 = column_slice(TRAIN["a"][1], rank, world)
+    lp, li, lw = shard_csr(p, i, w, N_FOLDS, TRAIN["a"][1], j0, j1)
+    st.load("a", lp, li, lw, len(li), 0.01)
+    dxs = []
+    for step in range(2):
+        x, dy = _train_data(step)
+        st.forward_host("a", x)
+        dxs.append(st.backward_host("a", dy, LR))
+    state = _layer_state(st.parts["a"].layer, TRAIN["a"][0])
+    np.savez(out + f".{rank}.npz", dx=np.stack(dxs), **state)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_sharded_training_two_gloo_ranks(tmp_path):
+    want, want_dx = _unsharded(_oracle, 2)
+    out = str(tmp_path / "train")
+    mp.start_processes(_train_rank_main, args=(2, _free_port(), out), nprocs=2, start_method="spawn")
+    for rank in range(2):
+        got = dict(np.load(out + f".{rank}.npz"))
+        np.testing.assert_allclose(got["dx"], np.stack(want_dx), rtol=1e-5, atol=1e-6)
+        _check_shard(want, got, rank, 2)
+
+
+@pytest.mark.gpu
+def test_column_shard_update_vs_oracle():
+    """The CUDA column-shard update (two shards on one GPU, parts summed on
+    the host) against the unsharded oracle layer."""
+    import sili__new_b200 as S
+    want, want_dx = _unsharded(_oracle, 3)
+    layers = _shard_layers(lambda a, b, c: S.SparseLinearLayerDeterministic(a, b, c), 2)
+    got_dx = _sharded_steps(layers, 3)
+    for a, b in zip(got_dx, want_dx):
+        np.testing.assert_allclose(a, b, rtol=1e-5, atol=1e-6)
+    for rank, (L, _, _) in enumerate(layers):
+        _check_shard(want, _layer_state(L, TRAIN["a"][0]), rank, 2)
+
+
+@pytest.mark.gpu
+def test_device_backward_matches_host_backward():
+    """backward_device (fold-broadcast kernel + fused update) against
+    backward_host on twin CUDA stacks, world 1."""
+    import torch
+    import sili__new_b200 as S
+    fac = lambda a, b, c: S.SparseLinearLayerDeterministic(a, b, c)   # noqa: E731
+    host, dev = FoldedStack(dict(TRAIN), N_FOLDS, 0, 1, fac), FoldedStack(dict(TRAIN), N_FOLDS, 0, 1, fac)
+    p, i, w = _train_csr()
+    host.load("a", p, i, w, len(i), 0.01)
+    dev.load("a", p, i, w, len(i), 0.01)
+    stream = torch.cuda.Stream()
+    for step in range(2):
+        x, dy = _train_data(step)
+        host.forward_host("a", x)
+        dev.forward_device("a", torch.from_numpy(x).cuda(), stream)
+        dxh = host.backward_host("a", dy, LR)
+        dxd = dev.backward_device("a", torch.from_numpy(dy).cuda(), LR, stream)
+        stream.synchronize()
+        assert np.array_equal(dxd.cpu().numpy(), dxh), f"step {step}"
+    sh, sd = _layer_state(host.parts["a"].layer, TRAIN["a"][0]), _layer_state(dev.parts["a"].layer, TRAIN["a"][0])
+    for k in sh:
+        assert np.array_equal(sh[k], sd[k]), k
