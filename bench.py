@@ -586,6 +586,9 @@ def run_folded(args, dev, rank, world, dist, S, torch, which="config5"):
     torch.cuda.synchronize(dev)
     ms = e0.elapsed_time(e1) / steps
     launches = S.kernel_launches() - l0
+    train = None
+    if not prefill:
+        train = folded_train_leg(args, dev, dist, S, torch, stack, suffixes, xs, stream, B)
     nnz_t = torch.tensor([float(nnz_local)], device=f"cuda:{dev}")
     if dist:
         t = torch.tensor([ms], device=f"cuda:{dev}")
@@ -603,7 +606,51 @@ def run_folded(args, dev, rank, world, dist, S, torch, which="config5"):
             "gflop_per_step": flops / 1e9, "fp32_tflops": flops / (ms * 1e-3) / 1e12,
             "sharding": f"output columns within each fold over {world} rank(s), NCCL all-gather per suffix",
             "build_s_rank0": build_s, "torch_mem_gb_rank0": mem_gb, "gpu_launches_rank0": launches,
-            "data": f"synthetic: random N(0,0.02) pruned to {density * 100:g}% (uniform pattern), x ~ N(0,1)"}
+            "data": f"synthetic: random N(0,0.02) pruned to {density * 100:g}% (uniform pattern), x ~ N(0,1)",
+            "train": train}
+
+
+def folded_train_leg(args, dev, dist, S, torch, stack, suffixes, xs, stream, B):
+    """Training steps through the sharded stack (FoldedLayer's forward +
+    backward, sili/sparse_rnn.py:1095-1157, lr 0.01, lr_per_row_nnz): per
+    suffix forward_device, then backward_device -- fold broadcast, fused
+    update as a column shard, NCCL all-reduces of dx and of the rows'
+    value_scale parts, row steps.  Timed on the device, max over ranks."""
+    gen = torch.Generator(device=f"cuda:{dev}")
+    gen.manual_seed(11)
+    dys = {name: torch.randn(B, out_dim, generator=gen, device=f"cuda:{dev}")
+           for name, (_, out_dim) in suffixes.items()}
+
+    def train_step():
+        for name in suffixes:
+            stack.forward_device(name, xs[name], stream)
+            stack.backward_device(name, dys[name], 0.01, stream)
+
+    for _ in range(2):
+        train_step()
+    torch.cuda.synchronize(dev)
+    steps = max(3, min(args.steps, 8))
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    l0 = S.kernel_launches()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        train_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / steps
+    launches = S.kernel_launches() - l0
+    if dist:
+        t = torch.tensor([ms], device=f"cuda:{dev}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    world = dist.get_world_size() if dist else 1
+    return {"metric": "folded-stack training tokens/s (forward + backward with the fused update, lr 0.01)",
+            "value": B / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms, "steps": steps,
+            "collectives_per_step": len(suffixes) * (3 if world > 1 else 0),
+            "gpu_launches_rank0": launches}
 
 
 def main():

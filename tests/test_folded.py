@@ -290,3 +290,46 @@ def test_device_backward_matches_host_backward():
     sh, sd = _layer_state(host.parts["a"].layer, TRAIN["a"][0]), _layer_state(dev.parts["a"].layer, TRAIN["a"][0])
     for k in sh:
         assert np.array_equal(sh[k], sd[k]), k
+
+
+def _nccl_rank_main(rank, world, port, out):
+    import torch
+    import torch.distributed as dist
+    import datetime
+    import sili__new_b200 as S
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    st = FoldedStack(dict(TRAIN), N_FOLDS, rank, world,
+                     lambda a, b, c: S.SparseLinearLayerDeterministic(a, b, c, 1, rank))
+    p, i, w = _train_csr()
+    j0, j1 = column_slice(TRAIN["a"][1], rank, world)
+    lp, li, lw = shard_csr(p, i, w, N_FOLDS, TRAIN["a"][1], j0, j1)
+    st.load("a", lp, li, lw, len(li), 0.01)
+    stream = torch.cuda.Stream()
+    dxs = []
+    for step in range(2):
+        x, dy = _train_data(step)
+        st.forward_device("a", torch.from_numpy(x).cuda(), stream)
+        dxs.append(st.backward_device("a", torch.from_numpy(dy).cuda(), LR, stream).cpu().numpy().copy())
+    stream.synchronize()
+    state = _layer_state(st.parts["a"].layer, TRAIN["a"][0])
+    np.savez(out + f".{rank}.npz", dx=np.stack(dxs), **state)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_sharded_training_two_nccl_ranks(tmp_path):
+    """backward_device over NCCL on two GPUs against the unsharded oracle
+    (runs where the box has two GPUs)."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    want, want_dx = _unsharded(_oracle, 2)
+    out = str(tmp_path / "nccl")
+    mp.start_processes(_nccl_rank_main, args=(2, _free_port(), out), nprocs=2, start_method="spawn")
+    for rank in range(2):
+        got = dict(np.load(out + f".{rank}.npz"))
+        np.testing.assert_allclose(got["dx"], np.stack(want_dx), rtol=1e-5, atol=1e-6)
+        _check_shard(want, got, rank, 2)
