@@ -174,6 +174,20 @@ int sili_layer_raw(sili_layer* h, int64_t* byte_start, int64_t* byte_end, int64_
                    int64_t* elem_end, uint8_t* indices, uint8_t* values);
 /* overwrite the stored value bytes (weight code << 4 | importance code) */
 int sili_layer_set_value_bytes(sili_layer* h, const uint8_t* values, int64_t n);
+/* Checkpoint image: the layer's whole training state in one flat buffer
+ * (host or device memory), written by one copy per state array.  It holds
+ * what the reference's state dict (sili/sparse_rnn.py:817-851: weights,
+ * value_scale, importance_scale) holds and what it cannot restore: the
+ * importance codes, the delta-CSR layout with its headroom, every scale
+ * optimiser vector and step counter, the accumulators, out_degree, the
+ * running statistics and the stochastic-rounding seed and call counter, so a
+ * layer loaded from it continues training bit for bit.  load_state needs a
+ * layer of the same n_inputs x n_outputs (its scale rank follows the image)
+ * and drops the last forward input.  Layers holding block4 tiles:
+ * SILI_EINVAL. */
+int sili_layer_state_size(sili_layer* h, int64_t* bytes);
+int sili_layer_save_state(sili_layer* h, void* buf, int64_t bytes, void* stream);
+int sili_layer_load_state(sili_layer* h, const void* buf, int64_t bytes, void* stream);
 int sili_layer_accums(sili_layer* h, float* input_accum, float* grad_accum);
 int sili_layer_set_accums(sili_layer* h, const float* input_accum, const float* grad_accum);
 int sili_layer_out_degree(sili_layer* h, int* out);

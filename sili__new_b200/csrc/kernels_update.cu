@@ -39,6 +39,13 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
     const unsigned d = (unsigned)__cvta_generic_to_shared(smem);
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(gmem) : "memory");
 }
+// 16 bytes, or (take == false) 16 zero bytes without reading global memory
+// (src-size 0; gmem must still be a valid address)
+__device__ __forceinline__ void cp_async16_or_zero(void* smem, const void* gmem, bool take) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(gmem), "r"(take ? 16 : 0)
+                 : "memory");
+}
 __device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
     const unsigned d = (unsigned)__cvta_generic_to_shared(smem);
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(d), "l"(gmem) : "memory");
@@ -60,7 +67,9 @@ __global__ void __launch_bounds__(kU2Warps * 32, u2_min_ctas(RANK)) k_backward_u
                                                                              const float* __restrict__ dyT, int B,
                                                                              UpdateParams P, float* __restrict__ dxT) {
     __shared__ __align__(16) float dys_s[kU2Warps][32][kU2Pitch];   // [synapse][sample]
-    __shared__ __align__(16) float cws_s[kU2Warps][kU2K + 1][32];   // [segment][synapse]
+    // [segment][synapse]; pitch 36 puts the rows of different segments,
+    // which the lanes (samples) of the dx pass read at once, in different banks
+    __shared__ __align__(16) float cws_s[kU2Warps][kU2K + 1][kU2Pitch];
     __shared__ float xs_s[kU2Warps][NB * 32];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t r = (int64_t)blockIdx.x * kU2Warps + warp;
@@ -73,7 +82,7 @@ __global__ void __launch_bounds__(kU2Warps * 32, u2_min_ctas(RANK)) k_backward_u
         return;
     }
     float (*dys)[kU2Pitch] = dys_s[warp];
-    float (*cws)[32] = cws_s[warp];
+    float (*cws)[kU2Pitch] = cws_s[warp];
     float* xs = xs_s[warp];
     const int f0 = L.rowptr[r];
     const int gnnz = P.row_nnz_g ? P.row_nnz_g[r] : nnz;   // a column shard divides by the global count
@@ -159,13 +168,17 @@ __global__ void __launch_bounds__(kU2Warps * 32, u2_min_ctas(RANK)) k_backward_u
     // rows of absent synapses read as dy = 0
     auto stage = [&](const SynChain<RANK>& C, int n, int t0, int nb) {
         if (vec4) {   // B % 4 == 0: every 16-byte group lies inside or outside [0, nb)
+            // groups outside the tile are zero-filled by the copy itself (no
+            // branch around the asm, no separate fill of absent rows)
             const int sub = lane >> 3, m4 = (lane & 7) * 4;
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
                 const int l = q * 4 + sub;
                 const int cl = __shfl_sync(0xffffffffu, C.c, l);
-                if (l < n && m4 < nb) cp_async16(&dys[l][m4], dyT + (int64_t)cl * B + t0 + m4);
+                const bool take = l < n && m4 < nb;
+                cp_async16_or_zero(&dys[l][m4], take ? dyT + (int64_t)cl * B + t0 + m4 : dyT, take);
             }
+            return;
         } else {
             for (int l = 0; l < n; ++l) {
                 const int cl = __shfl_sync(0xffffffffu, C.c, l);

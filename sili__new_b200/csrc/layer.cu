@@ -2058,6 +2058,129 @@ int sili_layer_raw(sili_layer* h, int64_t* bs, int64_t* be, int64_t* es, int64_t
     return SILI_OK;
 }
 
+// ── checkpoint: the whole training state as one flat image ─────────────────
+// The reference's state dict (sili/sparse_rnn.py:817-851) carries weights and
+// the per-row scales only; importance cannot be restored there.  The image
+// holds everything a training run reads: the delta-CSR layout with its
+// headroom (value positions key the stochastic rounding draws), the value
+// bytes (weight and importance codes), every scale / optimiser vector and
+// step counter, the accumulators, out_degree, the running statistics and the
+// RNG seed and call counter.  A layer loaded from it continues bit for bit.
+// Layout: CkptHead, then each section in ckpt_sections() order at a 16-byte
+// aligned offset.  Block4 tiles are not part of it.
+struct CkptHead {
+    uint64_t magic;
+    uint32_t version, rank;
+    int64_t rows, cols;
+    uint64_t seed, call;
+    int64_t idx_n, val_n, total_nnz, max_idx_bytes, max_val_bytes, idx_budget, val_budget, n_vs, n_os;
+    double st[4];
+    float st_vmax, st_imax, max_abs_decay;
+    int32_t os_trainable, stochastic, reserved;
+};
+constexpr uint64_t kCkptMagic = 0x3130434B42494C53ULL;   // "SLIBKC01"
+constexpr uint32_t kCkptVersion = 1;
+static size_t ckpt_align(size_t n) { return (n + 15) & ~(size_t)15; }
+
+struct CkptSec { void* dev; size_t bytes; };
+static std::vector<CkptSec> ckpt_sections(sili_layer* h) {
+    const size_t R = (size_t)h->rows, C = (size_t)h->cols, k = (size_t)h->rank;
+    return {{h->bs.p, (R + 1) * 8}, {h->be.p, R * 8}, {h->es.p, (R + 1) * 8}, {h->ee.p, R * 8},
+            {h->idx.p, (size_t)h->idx_n}, {h->val.p, (size_t)h->val_n},
+            {h->vs.p, R * k * 4}, {h->os.p, C * k * 4}, {h->vsi.p, R * k * 4}, {h->osi.p, C * k * 4},
+            {h->vsm.p, R * k * 4}, {h->is.p, R * 4}, {h->ois.p, C * 4},
+            {h->vstep.p, R * k * 4}, {h->ostep.p, C * k * 4},
+            {h->in_acc.p, R * 4}, {h->grad_acc.p, C * 4}, {h->out_degree.p, C * 4}};
+}
+static int64_t ckpt_bytes(sili_layer* h) {
+    size_t n = ckpt_align(sizeof(CkptHead));
+    for (const auto& sec : ckpt_sections(h)) n += ckpt_align(sec.bytes);
+    return (int64_t)n;
+}
+
+int sili_layer_state_size(sili_layer* h, int64_t* bytes) {
+    RC(use(h));
+    if (!bytes) return fail(SILI_EINVAL, "state_size: bad arguments");
+    *bytes = ckpt_bytes(h);
+    return SILI_OK;
+}
+
+int sili_layer_save_state(sili_layer* h, void* buf, int64_t bytes, void* stream) {
+    RC(use(h));
+    if (!buf) return fail(SILI_EINVAL, "save_state: bad arguments");
+    if (h->b4_ntiles > 0) return fail(SILI_EINVAL, "save_state: block4 tiles are not part of the checkpoint image");
+    if (bytes < ckpt_bytes(h)) return fail(SILI_EINVAL, "save_state: buffer smaller than sili_layer_state_size");
+    cudaStream_t s = pick(h, stream);
+    CK(cudaStreamSynchronize(s));
+    CK(cudaStreamSynchronize(h->stream));
+    RC(flush_stats(h));
+    CkptHead hd{};
+    hd.magic = kCkptMagic; hd.version = kCkptVersion; hd.rank = (uint32_t)h->rank;
+    hd.rows = h->rows; hd.cols = h->cols; hd.seed = h->seed; hd.call = h->call;
+    hd.idx_n = h->idx_n; hd.val_n = h->val_n; hd.total_nnz = h->total_nnz;
+    hd.max_idx_bytes = h->max_idx_bytes; hd.max_val_bytes = h->max_val_bytes;
+    hd.idx_budget = h->idx_budget; hd.val_budget = h->val_budget; hd.n_vs = h->n_vs; hd.n_os = h->n_os;
+    for (int i = 0; i < 4; ++i) hd.st[i] = h->st[i];
+    hd.st_vmax = h->st_vmax; hd.st_imax = h->st_imax; hd.max_abs_decay = h->max_abs_decay;
+    hd.os_trainable = h->os_trainable ? 1 : 0; hd.stochastic = h->stochastic ? 1 : 0;
+    uint8_t* out = (uint8_t*)buf;
+    CK(cudaMemcpyAsync(out, &hd, sizeof hd, cudaMemcpyDefault, s));
+    size_t off = ckpt_align(sizeof hd);
+    for (const auto& sec : ckpt_sections(h)) {
+        if (sec.bytes) CK(cudaMemcpyAsync(out + off, sec.dev, sec.bytes, cudaMemcpyDefault, s));
+        off += ckpt_align(sec.bytes);
+    }
+    CK(cudaStreamSynchronize(s));   // hd lives on this frame
+    return SILI_OK;
+}
+
+int sili_layer_load_state(sili_layer* h, const void* buf, int64_t bytes, void* stream) {
+    RC(use(h));
+    if (!buf || bytes < (int64_t)sizeof(CkptHead)) return fail(SILI_EINVAL, "load_state: bad arguments");
+    if (h->b4_ntiles > 0) return fail(SILI_EINVAL, "load_state: the layer holds block4 tiles");
+    cudaStream_t s = pick(h, stream);
+    CK(cudaStreamSynchronize(s));
+    CK(cudaStreamSynchronize(h->stream));
+    CkptHead hd;
+    CK(cudaMemcpy(&hd, buf, sizeof hd, cudaMemcpyDefault));
+    if (hd.magic != kCkptMagic || hd.version != kCkptVersion)
+        return fail(SILI_EINVAL, "load_state: not a checkpoint image of this library version");
+    if (hd.rows != h->rows || hd.cols != h->cols)
+        return fail(SILI_EINVAL, "load_state: image of a " + std::to_string(hd.rows) + "x" + std::to_string(hd.cols) +
+                                     " layer, this layer is " + std::to_string(h->rows) + "x" + std::to_string(h->cols));
+    if (hd.rank < 1 || hd.rank > 4 || hd.idx_n < 0 || hd.val_n < 0 || hd.total_nnz < 0)
+        return fail(SILI_EINVAL, "load_state: corrupt header");
+    RC(sili_layer_set_scale_rank(h, (int)hd.rank));
+    const int64_t R = h->rows;
+    RC(h->bs.reserve(R + 1)); RC(h->be.reserve(R + 1)); RC(h->es.reserve(R + 1)); RC(h->ee.reserve(R + 1));
+    RC(h->idx.reserve(hd.idx_n + 64));
+    RC(h->val.reserve(hd.val_n + 64));
+    h->idx_n = hd.idx_n; h->val_n = hd.val_n;
+    if (bytes < ckpt_bytes(h)) return fail(SILI_EINVAL, "load_state: image shorter than its header says");
+    CK(cudaMemsetAsync(h->idx.p + hd.idx_n, 0, 64, s));
+    CK(cudaMemsetAsync(h->val.p + hd.val_n, 0, 64, s));
+    const uint8_t* in = (const uint8_t*)buf;
+    size_t off = ckpt_align(sizeof hd);
+    for (const auto& sec : ckpt_sections(h)) {
+        if (sec.bytes) CK(cudaMemcpyAsync(sec.dev, in + off, sec.bytes, cudaMemcpyDefault, s));
+        off += ckpt_align(sec.bytes);
+    }
+    CK(cudaStreamSynchronize(s));
+    h->seed = hd.seed; h->call = hd.call; h->total_nnz = hd.total_nnz;
+    h->max_idx_bytes = hd.max_idx_bytes; h->max_val_bytes = hd.max_val_bytes;
+    h->idx_budget = hd.idx_budget; h->val_budget = hd.val_budget; h->n_vs = hd.n_vs; h->n_os = hd.n_os;
+    for (int i = 0; i < 4; ++i) h->st[i] = hd.st[i];
+    h->st_vmax = hd.st_vmax; h->st_imax = hd.st_imax; h->max_abs_decay = hd.max_abs_decay;
+    h->os_trainable = hd.os_trainable != 0;
+    h->st_pending = false;
+    CK(cudaMemset(h->d_st.p, 0, 2 * sizeof(double)));
+    CK(cudaMemset(h->d_stmax.p, 0, sizeof(float)));
+    h->aux_dirty = true;      // column index and dead-row set follow the new layout
+    h->pack_valid = false;
+    h->last_batch = 0;        // the image carries no forward input
+    return SILI_OK;
+}
+
 int sili_layer_accums(sili_layer* h, float* a, float* g) {
     RC(use(h));
     RC(from_dev(h->in_acc.p, a, (size_t)h->rows * 4, h->stream));

@@ -117,6 +117,26 @@ public:
         return dx;
     }
 
+    // checkpoint image (sili_layer_save_state / sili_layer_load_state)
+    int64_t state_size() {
+        int64_t n = 0;
+        check(sili_layer_state_size(h, &n));
+        return n;
+    }
+    py::array_t<uint8_t> save_state() {
+        const int64_t n = state_size();
+        py::array_t<uint8_t> out((py::ssize_t)n);
+        check(sili_layer_save_state(h, out.mutable_data(), n, nullptr));
+        return out;
+    }
+    void load_state(u8arr image) { check(sili_layer_load_state(h, image.data(), (int64_t)image.size(), nullptr)); }
+    void save_state_ptr(uintptr_t buf, int64_t bytes, uintptr_t stream) {
+        check(sili_layer_save_state(h, (void*)buf, bytes, (void*)stream));
+    }
+    void load_state_ptr(uintptr_t buf, int64_t bytes, uintptr_t stream) {
+        check(sili_layer_load_state(h, (const void*)buf, bytes, (void*)stream));
+    }
+
     // column shards (sili_layer_set_row_shard): host-array variants
     void set_row_shard(iarr global_row_nnz, int64_t global_n_out) {
         check(sili_layer_set_row_shard(h, global_row_nnz.data(), (int64_t)global_row_nnz.size(), global_n_out));
@@ -415,6 +435,11 @@ void bind_layer(py::module_& m, const char* name) {
         .def("backward_dense_ptr", &T::backward_dense_ptr, py::arg("dy_ptr"), py::arg("batch"), py::arg("learning_rate"),
              py::arg("lr_per_row_nnz") = false, py::arg("damp_by_importance") = true, py::arg("beta2") = 0.999f,
              py::arg("eps") = 1e-8f, py::arg("dx_ptr") = 0, py::arg("stream") = 0, py::arg("x_ptr") = 0)
+        .def("state_size", &T::state_size)
+        .def("save_state", &T::save_state)
+        .def("load_state", &T::load_state, py::arg("image"))
+        .def("save_state_ptr", &T::save_state_ptr, py::arg("buf"), py::arg("bytes"), py::arg("stream") = 0)
+        .def("load_state_ptr", &T::load_state_ptr, py::arg("buf"), py::arg("bytes"), py::arg("stream") = 0)
         .def("set_row_shard", &T::set_row_shard, py::arg("global_row_nnz"), py::arg("global_n_outputs"))
         .def("row_part_len", &T::row_part_len, py::arg("batch"))
         .def("backward_dense_shard", &T::backward_dense_shard, py::arg("dy"), py::arg("learning_rate"),

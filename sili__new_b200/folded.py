@@ -131,6 +131,30 @@ class FoldedStack:
                 cnt = np.diff(np.asarray(ptrs, np.int64)).astype(np.int32)
             p.layer.set_row_shard(self._sum_over_ranks(cnt), self.n_folds * p.out_dim)
 
+    def state_dict(self) -> dict:
+        """Per suffix: this rank's layer state (sili__new_b200.checkpoint,
+        the reference's keys plus the checkpoint image) and the stack's
+        shape, as FoldedLayer.state_dict (sili/sparse_rnn.py:1212-1221)."""
+        from .checkpoint import state_dict
+        out = {}
+        for name, p in self.parts.items():
+            d = state_dict(p.layer)
+            d["n_folds"] = np.array([self.n_folds])
+            d["out_dim"] = np.array([p.out_dim])
+            d["columns"] = np.array([p.j0, p.j1])
+            out[name] = d
+        return out
+
+    def load_state_dict(self, d: dict) -> None:
+        """Restores every suffix's rank-local layer (loaded shards of the
+        same column slices; the row-shard counts set at load stay)."""
+        from .checkpoint import load_state_dict
+        for name, sub in d.items():
+            p = self.parts[name]
+            if int(sub["n_folds"][0]) != self.n_folds or list(sub["columns"]) != [p.j0, p.j1]:
+                raise ValueError(f"load_state_dict: {name} was saved for other folds or columns")
+            load_state_dict(p.layer, sub)
+
     def _sum_over_ranks(self, a: np.ndarray) -> np.ndarray:
         import torch
         import torch.distributed as dist

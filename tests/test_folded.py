@@ -333,3 +333,32 @@ def test_sharded_training_two_nccl_ranks(tmp_path):
         got = dict(np.load(out + f".{rank}.npz"))
         np.testing.assert_allclose(got["dx"], np.stack(want_dx), rtol=1e-5, atol=1e-6)
         _check_shard(want, got, rank, 2)
+
+
+@pytest.mark.gpu
+def test_folded_state_dict_round_trip():
+    """FoldedStack.state_dict / load_state_dict: a restored stack trains on
+    bit for bit (device path, world 1)."""
+    import torch
+    import sili__new_b200 as S
+    fac = lambda a, b, c: S.SparseLinearLayer(a, b, c)   # noqa: E731  (stochastic rounding)
+    p, i, w = _train_csr()
+    a, b = FoldedStack(dict(TRAIN), N_FOLDS, 0, 1, fac), FoldedStack(dict(TRAIN), N_FOLDS, 0, 1, fac)
+    a.load("a", p, i, w, len(i), 0.01)
+    b.load("a", p, i, w, len(i), 0.01)
+    stream = torch.cuda.Stream()
+    x, dy = _train_data(0)
+    a.forward_device("a", torch.from_numpy(x).cuda(), stream)
+    a.backward_device("a", torch.from_numpy(dy).cuda(), LR, stream)
+    stream.synchronize()
+    b.load_state_dict(a.state_dict())
+    for step in (1, 2):
+        x, dy = _train_data(step)
+        outs = []
+        for st in (a, b):
+            y = st.forward_device("a", torch.from_numpy(x).cuda(), stream).clone()
+            dx = st.backward_device("a", torch.from_numpy(dy).cuda(), LR, stream).clone()
+            outs.append((y, dx))
+        stream.synchronize()
+        assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1]), step
+    assert np.array_equal(a.parts["a"].layer.save_state(), b.parts["a"].layer.save_state())
