@@ -42,23 +42,38 @@ void launch_pack_csc(const LayerView& L, int64_t bound, int* cpack, cudaStream_t
 // ── lane-per-column forward ───────────────────────────────────────────────
 // One thread per output column, 32 samples per CTA (acc[32] in registers).
 // Per tile of RT input rows the CTA stages x[rows][32 samples] into shared
-// memory (8 float4 chunks of 128-byte rows); each thread then consumes its
+// memory (8 float4 chunks of a 128-byte row); each thread then consumes its
 // column's entries whose row lies in the tile, in ascending row order, 32
 // fmas per entry, the next entry's packed word loaded ahead.  Lane l reads
-// chunk (q + l) mod 8 at step q (its accumulator k holds sample
-// (k + 4l) mod 32): the 8 lanes of a quarter-warp then always touch 8
-// different bank groups, whatever rows they read.
+// chunk q ^ (l mod 8) at step q (its accumulator 4q + v holds sample
+// 4 (q ^ (l mod 8)) + v): the 8 lanes of a quarter-warp then always touch 8
+// different bank groups, whatever rows they read, and with the tile 128-byte
+// aligned the chunk address is one xor of the row address.  Weight codes are
+// decoded through a 16-entry table in shared memory.
 constexpr int kFcSg = 32;   // samples per CTA
 
+__device__ __forceinline__ float4 lds128(uint32_t a) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a));
+    return v;
+}
+
 template <bool SPARSE>
-__global__ void __launch_bounds__(256) k_forward_cols(LayerView L, const float* __restrict__ xT, int B, int RT,
+__global__ void __launch_bounds__(256, 3) k_forward_cols(LayerView L, const float* __restrict__ xT, int B, int RT,
                                                       float* __restrict__ y) {
-    extern __shared__ __align__(16) float4 xs4[];   // [RT][8] chunks of 4 samples, then vs of the RT rows
+    // [pad to 128 B][RT][8] chunks of 4 samples, then vs of the RT rows, then the code table
+    extern __shared__ __align__(16) unsigned char fc_smem[];
+    const uint32_t raw32 = (uint32_t)__cvta_generic_to_shared(fc_smem);
+    const uint32_t pad = (128u - (raw32 & 127u)) & 127u;
+    float4* xs4 = reinterpret_cast<float4*>(fc_smem + pad);
+    const uint32_t xs32 = raw32 + pad;
     float* vs_t = reinterpret_cast<float*>(xs4 + RT * 8);
+    float* ftab = vs_t + RT;
+    if (threadIdx.x < 16) ftab[threadIdx.x] = fp4_decode(threadIdx.x);
     const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int b0 = blockIdx.y * kFcSg;
     const int n_in = (int)L.n_in;
-    const int rot = threadIdx.x & 7;
+    const uint32_t rot16 = (threadIdx.x & 7) << 4;
     int cur = 0, end = 0;
     float oc = 0.0f;
     if (c < L.n_out) {
@@ -93,7 +108,7 @@ __global__ void __launch_bounds__(256) k_forward_cols(LayerView L, const float* 
         for (int i = threadIdx.x; i < nr; i += blockDim.x) vs_t[i] = __ldg(L.vs + R0 + i);
         __syncthreads();
         while (cur < end && (pk >> 4) < R1) {
-            const int r = pk >> 4, code = pk & 15;
+            const int ri = (pk >> 4) - R0, code = pk & 15;
             ++cur;
             // the next entry's word, ahead of this one's fmas
             if ((cur & 3) == 0) {
@@ -101,8 +116,8 @@ __global__ void __launch_bounds__(256) k_forward_cols(LayerView L, const float* 
                 nb2 = cur + 4 < end ? __ldg(cp4 + (cur >> 2) + 1) : none;
             }
             pk = cur < end ? word(cur & 3) : (n_in << 4);
-            const float wq = fp4_decode((uint32_t)code);
-            const float vr = vs_t[r - R0];
+            const float wq = ftab[code];
+            const float vr = vs_t[ri];
             float w, cs = 0.0f;
             if (SPARSE) {
                 w = wq;
@@ -110,11 +125,11 @@ __global__ void __launch_bounds__(256) k_forward_cols(LayerView L, const float* 
             } else {
                 w = __fmul_rn(wq, __fmaf_rn(vr, oc, 0.0f));
             }
-            const float4* row = xs4 + (r - R0) * 8;
+            const uint32_t rowa = (xs32 + ((uint32_t)ri << 7)) ^ rot16;
             if (isfinite(w) && (!SPARSE || isfinite(cs))) {
 #pragma unroll
                 for (int q = 0; q < 8; ++q) {
-                    const float4 xv = row[(q + rot) & 7];
+                    const float4 xv = lds128(rowa ^ ((uint32_t)q << 4));
                     if (SPARSE) {
                         acc[4 * q + 0] = __fadd_rn(acc[4 * q + 0], __fmul_rn(__fmul_rn(w, xv.x), cs));
                         acc[4 * q + 1] = __fadd_rn(acc[4 * q + 1], __fmul_rn(__fmul_rn(w, xv.y), cs));
@@ -132,7 +147,7 @@ __global__ void __launch_bounds__(256) k_forward_cols(LayerView L, const float* 
                 // 0 * inf never reaches the sum
 #pragma unroll
                 for (int q = 0; q < 8; ++q) {
-                    const float4 xv = row[(q + rot) & 7];
+                    const float4 xv = lds128(rowa ^ ((uint32_t)q << 4));
                     const float xq[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
                     for (int v = 0; v < 4; ++v) {
@@ -145,9 +160,10 @@ __global__ void __launch_bounds__(256) k_forward_cols(LayerView L, const float* 
         }
     }
     if (c < L.n_out) {
+        const int rot = threadIdx.x & 7;
 #pragma unroll
         for (int k = 0; k < kFcSg; ++k) {
-            const int b = b0 + ((k + 4 * rot) & (kFcSg - 1));
+            const int b = b0 + 4 * ((k >> 2) ^ rot) + (k & 3);
             if (b < B) y[(int64_t)b * L.n_out + c] = acc[k];
         }
     }
@@ -179,7 +195,7 @@ bool forward_rows_applies(const LayerView& L, int B) { return cols_plan(L, B).th
 bool launch_forward_rows(const LayerView& L, const float* xT, int B, float* y, bool sparse, cudaStream_t s) {
     const ColsPlan p = cols_plan(L, B);
     if (p.threads == 0 || !L.cpack || !L.colptr_x) return false;
-    const size_t smem = (size_t)p.rt * (8 * sizeof(float4) + sizeof(float));
+    const size_t smem = 128 + (size_t)p.rt * (8 * sizeof(float4) + sizeof(float)) + 16 * sizeof(float);
     static unsigned long long attr_devices = 0;   // the attribute is per device and kernel
     int dev = 0;
     cudaGetDevice(&dev);

@@ -2124,6 +2124,10 @@ int sili_layer_save_state(sili_layer* h, void* buf, int64_t bytes, void* stream)
     hd.st_vmax = h->st_vmax; hd.st_imax = h->st_imax; hd.max_abs_decay = h->max_abs_decay;
     hd.os_trainable = h->os_trainable ? 1 : 0; hd.stochastic = h->stochastic ? 1 : 0;
     uint8_t* out = (uint8_t*)buf;
+    // the alignment gaps between sections are zero, so equal states give equal images
+    const int64_t total = ckpt_bytes(h);
+    if (is_device_ptr(buf)) CK(cudaMemsetAsync(out, 0, (size_t)total, s));
+    else std::memset(out, 0, (size_t)total);
     CK(cudaMemcpyAsync(out, &hd, sizeof hd, cudaMemcpyDefault, s));
     size_t off = ckpt_align(sizeof hd);
     for (const auto& sec : ckpt_sections(h)) {

@@ -506,14 +506,16 @@ void bind_layer(py::module_& m, const char* name) {
         .def("hoyer_importance", [](T& s) { auto st = s.stats(); return s.hoyer(st[3], st[4]); })
         .def("recompute_stats", [](T& s) { check(sili_layer_recompute_stats(s.h)); })
         .def("zero_accum", [](T& s) { check(sili_layer_zero_accum(s.h)); })
-        .def_property_readonly("neuron_input_accum", [](T& s) { return s.accums()[0]; })
-        .def_property_readonly("neuron_grad_accum", [](T& s) { return s.accums()[1]; })
+        .def_property_readonly("neuron_input_accum", [](T& s) { py::tuple t = s.accums(); return py::object(t[0]); })
+        .def_property_readonly("neuron_grad_accum", [](T& s) { py::tuple t = s.accums(); return py::object(t[1]); })
         .def("accums", &T::accums)
         .def("set_accums", &T::set_accums, py::arg("input_accum"), py::arg("grad_accum"))
-        .def_property_readonly("weights_vals", [](T& s) { return s.export_csr()[2]; })
-        .def_property_readonly("importance", [](T& s) { return s.export_csr()[3]; })
-        .def_property_readonly("indices", [](T& s) { return s.export_csr()[1]; })
-        .def_property_readonly("ptrs", [](T& s) { return s.export_csr()[0]; })
+        // (the element is taken as an owning object while the tuple is alive:
+        // an accessor returned past the tuple's lifetime would dangle)
+        .def_property_readonly("weights_vals", [](T& s) { py::tuple t = s.export_csr(); return py::object(t[2]); })
+        .def_property_readonly("importance", [](T& s) { py::tuple t = s.export_csr(); return py::object(t[3]); })
+        .def_property_readonly("indices", [](T& s) { py::tuple t = s.export_csr(); return py::object(t[1]); })
+        .def_property_readonly("ptrs", [](T& s) { py::tuple t = s.export_csr(); return py::object(t[0]); })
         .def("export", &T::export_csr)
         .def("raw_state", &T::raw_state)
         .def("scales", &T::scales, py::arg("kind"))
