@@ -92,6 +92,8 @@ struct UpdateParams {
 };
 
 void launch_transpose(const float* in, float* out, int64_t R, int64_t C, cudaStream_t s);
+// out[0..C) = in[0..C), out[C] = 0 (a one-row input and its zero row)
+void launch_copy_pad(const float* in, float* out, int64_t C, cudaStream_t s);
 // nonfinite (optional): set to `tag` when some |x| is inf or NaN
 void launch_accum_abs(const float* x, float* acc, int B, int64_t n, cudaStream_t s,
                       unsigned long long* nonfinite = nullptr, unsigned long long tag = 0);

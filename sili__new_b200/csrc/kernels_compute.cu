@@ -40,6 +40,17 @@ void launch_transpose(const float* in, float* out, int64_t R, int64_t C, cudaStr
     k_transpose<<<grid, block, 0, s>>>(in, out, R, C); count_launch();
 }
 
+// A single row [1, C] is its own transpose: copy it and append the zero row
+// (one element) in one launch.
+__global__ void k_copy_pad(const float* __restrict__ in, float* __restrict__ out, int64_t C) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < C) out[i] = in[i];
+    else if (i == C) out[i] = 0.0f;
+}
+void launch_copy_pad(const float* in, float* out, int64_t C, cudaStream_t s) {
+    k_copy_pad<<<(unsigned)((C + 1 + 255) / 256), 256, 0, s>>>(in, out, C); count_launch();
+}
+
 // neuron_*_accum[j] += |x[b, j]| for b ascending (linear_disldo.hpp:515-520).
 // With a flag pointer, a thread that meets an inf or NaN stores `tag` there
 // (the update kernel reads it to choose its exact general path for the call).
@@ -280,7 +291,7 @@ __global__ void __launch_bounds__(256) k_forward_vec(LayerView L, const float* _
 // Small batches: lanes over a column's synapses, per-lane partial sums over
 // the batch, then a fixed warp tree (deterministic; not the reference's
 // sequential order, so equal to it within fp32 rounding).
-template <int BMAX, bool SPARSE>
+template <int BMAX, int U, bool SPARSE>
 __global__ void __launch_bounds__(256) k_forward_small(LayerView L, const float* __restrict__ xT, int B,
                                                        float* __restrict__ y) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -293,27 +304,62 @@ __global__ void __launch_bounds__(256) k_forward_small(LayerView L, const float*
 #pragma unroll
     for (int b = 0; b < BMAX; ++b) acc[b] = 0.0f;
     const int k0 = L.colptr[c], k1 = L.colptr[c + 1];
-    for (int kk = k0 + lane; kk < k1; kk += 32) {
-        if (L.cvpos[kk] < 0) continue;   // CSC padding
-        const int r = L.crow[kk];
-        const float wq = fp4_decode(L.val[L.cvpos[kk]] >> 4);
+    // one entry's contribution to the lane's sums (entries in ascending
+    // position per lane: lane, lane + 32, ...)
+    // vs0: the row's first value_scale component (the others, rank > 1,
+    // are read here)
+    auto add = [&](float wq, int r, float vs0, const float* xv) {
         float w, cs = 0.0f;
         if (SPARSE) {
             w = wq;
-            cs = __fmul_rn(L.vs[(int64_t)r * L.rank], osk[0]);
+            cs = __fmul_rn(vs0, osk[0]);
         } else {
-            float sc = 0.0f;
-            for (int k = 0; k < L.rank; ++k) sc = __fmaf_rn(L.vs[(int64_t)r * L.rank + k], osk[k], sc);
+            float sc = __fmaf_rn(vs0, osk[0], 0.0f);
+            for (int k = 1; k < L.rank; ++k) sc = __fmaf_rn(L.vs[(int64_t)r * L.rank + k], osk[k], sc);
             w = __fmul_rn(wq, sc);
         }
-        const float* xr = xT + (int64_t)r * B;
 #pragma unroll
         for (int b = 0; b < BMAX; ++b) {
-            if (b < B) {
-                const float xv = __ldg(xr + b);
-                if (xv != 0.0f)
-                    acc[b] = SPARSE ? __fadd_rn(acc[b], __fmul_rn(__fmul_rn(w, xv), cs)) : __fmaf_rn(w, xv, acc[b]);
+            if (b < B && xv[b] != 0.0f)
+                acc[b] = SPARSE ? __fadd_rn(acc[b], __fmul_rn(__fmul_rn(w, xv[b]), cs)) : __fmaf_rn(w, xv[b], acc[b]);
+        }
+    };
+    if (L.cpack) {
+        // the packed column index (row << 4 | weight code, one coalesced word
+        // per entry): U entries per lane in flight at once, their words
+        // first, then their x values and row scales, then the sums in entry
+        // order
+        for (int kb = k0 + lane; kb < k1; kb += 32 * U) {
+            int rr[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int kk = kb + 32 * u;
+                rr[u] = kk < k1 ? __ldg(L.cpack + kk) : (L.n_in << 4);
             }
+            float xv[U][BMAX], vs0[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int r = rr[u] >> 4;
+                const bool live = r < L.n_in;   // not CSC padding
+#pragma unroll
+                for (int b = 0; b < BMAX; ++b) xv[u][b] = (live && b < B) ? __ldg(xT + (int64_t)r * B + b) : 0.0f;
+                vs0[u] = live ? __ldg(L.vs + (int64_t)r * L.rank) : 0.0f;
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int r = rr[u] >> 4;
+                if (r < L.n_in) add(fp4_decode((uint32_t)rr[u] & 15u), r, vs0[u], xv[u]);
+            }
+        }
+    } else {
+        for (int kk = k0 + lane; kk < k1; kk += 32) {
+            const int vp = L.cvpos[kk];
+            if (vp < 0) continue;        // CSC padding
+            const int r = L.crow[kk];
+            float xv[BMAX];
+#pragma unroll
+            for (int b = 0; b < BMAX; ++b) xv[b] = b < B ? __ldg(xT + (int64_t)r * B + b) : 0.0f;
+            add(fp4_decode(L.val[vp] >> 4), r, L.vs[(int64_t)r * L.rank], xv);
         }
     }
 #pragma unroll
@@ -328,9 +374,15 @@ __global__ void __launch_bounds__(256) k_forward_small(LayerView L, const float*
 void launch_forward(const LayerView& L, const float* xT, int B, float* y, bool sparse, cudaStream_t s) {
     if (L.n_out == 0 || B == 0) return;
     const unsigned gx = (unsigned)((L.n_out + 7) / 8);
+    if (B == 1) {   // a vector: 8 entries per lane in flight
+        if (sparse) k_forward_small<1, 8, true><<<gx, 256, 0, s>>>(L, xT, B, y);
+        else k_forward_small<1, 8, false><<<gx, 256, 0, s>>>(L, xT, B, y);
+        count_launch();
+        return;
+    }
     if (B <= 8) {
-        if (sparse) k_forward_small<8, true><<<gx, 256, 0, s>>>(L, xT, B, y);
-        else k_forward_small<8, false><<<gx, 256, 0, s>>>(L, xT, B, y);
+        if (sparse) k_forward_small<8, 4, true><<<gx, 256, 0, s>>>(L, xT, B, y);
+        else k_forward_small<8, 4, false><<<gx, 256, 0, s>>>(L, xT, B, y);
         count_launch();
         return;
     }

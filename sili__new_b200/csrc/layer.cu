@@ -290,6 +290,10 @@ int stage_transposed(sili_layer* h, const float* src, int64_t rows, int64_t cols
     // [cols, rows] plus one zero row (row `cols`), which the forward kernels'
     // CSC padding entries point at
     RC(dst.reserve(rows * cols + rows + 1));
+    if (rows == 1) {   // a single sample: one launch
+        launch_copy_pad(d, dst.p, cols, s);
+        return SILI_OK;
+    }
     launch_transpose(d, dst.p, rows, cols, s);
     CK(cudaMemsetAsync(dst.p + rows * cols, 0, (size_t)rows * sizeof(float), s));
     return SILI_OK;
@@ -380,7 +384,7 @@ int ensure_aux(sili_layer* h, cudaStream_t s) {
 // changed) where its shape rules allow, else the per-synapse gather kernels.
 int forward_columns(sili_layer* h, const float* xT, int batch, float* y, bool sparse, cudaStream_t s) {
     LayerView v = h->view();
-    if (h->total_nnz > 0 && batch > 8) {
+    if (h->total_nnz > 0) {
         // the packed column index: rebuilt here after a change of the weight
         // codes that did not keep it current (the dense update keeps it)
         const int64_t bound = std::max<int64_t>(h->total_nnz, 1) + 7 * h->cols + 8;   // padded CSC bound

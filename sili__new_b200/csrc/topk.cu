@@ -34,12 +34,23 @@ void launch_exist_bits(const int* rowptr, const int* abs_cols, int64_t n_in, int
 // 8 x 8 per thread (rows ty*8.., columns tx*8..: both read from shared memory
 // as two 16-byte loads), samples staged 16 at a time; each output
 // accumulates its fma chain over b in ascending order, as the rule defines.
+// With row lengths that are multiples of 4 floats (ASYNC), the next 16
+// samples' x and dy tiles are copied by cp.async into the second of two
+// buffers while the current ones are consumed.
 constexpr int kTM = 128, kTN = 128, kTK = 16;
+
+__device__ __forceinline__ void sc_cp16(float* smem, const float* gmem, bool take) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(gmem), "r"(take ? 16 : 0)
+                 : "memory");
+}
+
+template <bool ASYNC>
 __global__ void __launch_bounds__(256) k_dyx_scores(const float* __restrict__ x, const float* __restrict__ dy, int B,
                                                     int64_t n_in, int64_t n_out, const uint32_t* __restrict__ bits,
                                                     int64_t words, uint32_t* __restrict__ keys) {
-    __shared__ __align__(16) float xs[kTK][kTM];
-    __shared__ __align__(16) float ds[kTK][kTN];
+    __shared__ __align__(16) float xs[ASYNC ? 2 : 1][kTK][kTM];
+    __shared__ __align__(16) float ds[ASYNC ? 2 : 1][kTK][kTN];
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
     const int64_t r0 = (int64_t)blockIdx.y * kTM, c0 = (int64_t)blockIdx.x * kTN;
     float acc[8][8];
@@ -47,20 +58,27 @@ __global__ void __launch_bounds__(256) k_dyx_scores(const float* __restrict__ x,
     for (int i = 0; i < 8; ++i)
 #pragma unroll
         for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
-    for (int b0 = 0; b0 < B; b0 += kTK) {
-        for (int t = threadIdx.x; t < kTK * kTM; t += 256) {
-            const int k = t / kTM, i = t % kTM;
+    // 16 samples x 128 floats of x and of dy: 512 16-byte groups each, two
+    // per thread; groups past B or past the matrix edge are zero-filled
+    auto stage_async = [&](int buf, int b0) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int t = threadIdx.x + h * 256;
+            const int k = t >> 5, i4 = (t & 31) * 4;
             const int b = b0 + k;
-            xs[k][i] = (b < B && r0 + i < n_in) ? x[(int64_t)b * n_in + r0 + i] : 0.0f;
-            ds[k][i] = (b < B && c0 + i < n_out) ? dy[(int64_t)b * n_out + c0 + i] : 0.0f;
+            const bool tx_ = b < B && r0 + i4 < n_in;
+            const bool td = b < B && c0 + i4 < n_out;
+            sc_cp16(&xs[buf][k][i4], tx_ ? x + (int64_t)b * n_in + r0 + i4 : x, tx_);
+            sc_cp16(&ds[buf][k][i4], td ? dy + (int64_t)b * n_out + c0 + i4 : dy, td);
         }
-        __syncthreads();
-        const int kn = min(kTK, B - b0);
+        asm volatile("cp.async.commit_group;\n" ::: "memory");
+    };
+    auto compute = [&](int buf, int kn) {
         for (int k = 0; k < kn; ++k) {
-            const float4 xa = *reinterpret_cast<const float4*>(&xs[k][ty * 8]);
-            const float4 xb = *reinterpret_cast<const float4*>(&xs[k][ty * 8 + 4]);
-            const float4 da = *reinterpret_cast<const float4*>(&ds[k][tx * 8]);
-            const float4 db = *reinterpret_cast<const float4*>(&ds[k][tx * 8 + 4]);
+            const float4 xa = *reinterpret_cast<const float4*>(&xs[buf][k][ty * 8]);
+            const float4 xb = *reinterpret_cast<const float4*>(&xs[buf][k][ty * 8 + 4]);
+            const float4 da = *reinterpret_cast<const float4*>(&ds[buf][k][tx * 8]);
+            const float4 db = *reinterpret_cast<const float4*>(&ds[buf][k][tx * 8 + 4]);
             const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
             const float dv[8] = {da.x, da.y, da.z, da.w, db.x, db.y, db.z, db.w};
 #pragma unroll
@@ -68,7 +86,34 @@ __global__ void __launch_bounds__(256) k_dyx_scores(const float* __restrict__ x,
 #pragma unroll
                 for (int j = 0; j < 8; ++j) acc[i][j] = __fmaf_rn(xv[i], dv[j], acc[i][j]);
         }
-        __syncthreads();
+    };
+    if (ASYNC) {
+        int buf = 0;
+        if (B > 0) stage_async(0, 0);
+        for (int b0 = 0; b0 < B; b0 += kTK) {
+            if (b0 + kTK < B) {
+                stage_async(buf ^ 1, b0 + kTK);
+                asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+            } else {
+                asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+            }
+            __syncthreads();
+            compute(buf, min(kTK, B - b0));
+            __syncthreads();   // the buffer is refilled two tiles on
+            buf ^= 1;
+        }
+    } else {
+        for (int b0 = 0; b0 < B; b0 += kTK) {
+            for (int t = threadIdx.x; t < kTK * kTM; t += 256) {
+                const int k = t / kTM, i = t % kTM;
+                const int b = b0 + k;
+                xs[0][k][i] = (b < B && r0 + i < n_in) ? x[(int64_t)b * n_in + r0 + i] : 0.0f;
+                ds[0][k][i] = (b < B && c0 + i < n_out) ? dy[(int64_t)b * n_out + c0 + i] : 0.0f;
+            }
+            __syncthreads();
+            compute(0, min(kTK, B - b0));
+            __syncthreads();
+        }
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -87,7 +132,10 @@ void launch_dyx_scores(const float* x, const float* dy, int B, int64_t n_in, int
                        int64_t words, uint32_t* keys, cudaStream_t s) {
     if (n_in == 0 || n_out == 0) return;
     dim3 g((unsigned)((n_out + kTN - 1) / kTN), (unsigned)((n_in + kTM - 1) / kTM));
-    k_dyx_scores<<<g, 256, 0, s>>>(x, dy, B, n_in, n_out, bits, words, keys);
+    // 16-byte copies need 16-byte aligned rows and bases
+    const bool async = (n_in % 4 == 0) && (n_out % 4 == 0) && ((uintptr_t)x % 16 == 0) && ((uintptr_t)dy % 16 == 0);
+    if (async) k_dyx_scores<true><<<g, 256, 0, s>>>(x, dy, B, n_in, n_out, bits, words, keys);
+    else k_dyx_scores<false><<<g, 256, 0, s>>>(x, dy, B, n_in, n_out, bits, words, keys);
     count_launch();
 }
 
