@@ -130,16 +130,35 @@ __global__ void __launch_bounds__(128) k_b4_forward(LayerView L, B4View V, const
     const bool bok = b < B;
     float mo[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     const int64_t col0 = bcol * 4;
-    for (int t = V.cptr[bcol]; t < V.cptr[bcol + 1]; ++t) {
-        const int64_t br = V.cbr[t];
-        const uint4 tw = V.tile[V.ctile[t]];
-        float x[4];
+    // the block-column's output scales, read once (S = sum_k vs_k * os_k as a
+    // fused chain from 0, scale_of's arithmetic)
+    float os[4][4];
+#pragma unroll
+    for (int lj = 0; lj < 4; ++lj)
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            os[lj][k] = (col0 + lj < L.n_out && k < L.rank) ? L.os[(col0 + lj) * L.rank + k] : 0.0f;
+    const int t0 = V.cptr[bcol], t1 = V.cptr[bcol + 1];
+    // the next tile's block-row and slot bytes are loaded a tile ahead
+    int64_t nbr = t0 < t1 ? V.cbr[t0] : 0;
+    uint4 ntw = t0 < t1 ? V.tile[V.ctile[t0]] : make_uint4(0, 0, 0, 0);
+    for (int t = t0; t < t1; ++t) {
+        const int64_t br = nbr;
+        const uint4 tw = ntw;
+        if (t + 1 < t1) {
+            nbr = V.cbr[t + 1];
+            ntw = V.tile[V.ctile[t + 1]];
+        }
+        float x[4], vs[4][4];
         int64_t rows[4];
 #pragma unroll
         for (int li = 0; li < 4; ++li) {
             const int64_t row = br * 4 + li;
             rows[li] = row;
-            x[li] = bok ? xT[(row < L.n_in ? row : 0) * B + b] : 0.0f;
+            const bool rok = row < L.n_in;
+            x[li] = bok ? xT[(rok ? row : 0) * B + b] : 0.0f;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) vs[li][k] = (rok && k < L.rank) ? L.vs[row * L.rank + k] : 0.0f;
         }
 #pragma unroll
         for (int lj = 0; lj < 4; ++lj) {
@@ -147,10 +166,13 @@ __global__ void __launch_bounds__(128) k_b4_forward(LayerView L, B4View V, const
             if (col >= L.n_out) continue;
             float w[4];
 #pragma unroll
-            for (int li = 0; li < 4; ++li)
-                w[li] = rows[li] < L.n_in
-                    ? __fmul_rn(fp4_decode(tile_byte(tw, lj * 4 + li) & 0xFu), scale_of(L, rows[li], col))
-                    : 0.0f;
+            for (int li = 0; li < 4; ++li) {
+                float sc = 0.0f;
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    if (k < L.rank) sc = __fmaf_rn(vs[li][k], os[lj][k], sc);
+                w[li] = rows[li] < L.n_in ? __fmul_rn(fp4_decode(tile_byte(tw, lj * 4 + li) & 0xFu), sc) : 0.0f;
+            }
             const float acc = __fadd_rn(__fmaf_rn(w[0], x[0], __fmul_rn(w[1], x[1])),
                                         __fmaf_rn(w[2], x[2], __fmul_rn(w[3], x[3])));
             mo[lj] = __fadd_rn(mo[lj], acc);
@@ -591,6 +613,282 @@ __global__ void __launch_bounds__(128) k_b4_update(LayerView L, B4View V, const 
         if (use_smem)
             for (int b = 0; b < B; ++b) dxT[row * B + b] = dbuf[b];
     }
+}
+
+// ── the same update with tiles in parallel (every tile full: n_out % 4 == 0) ─
+// Within a block-row only two things chain the tiles: the row's dx, an
+// ordered fadd over its tiles' per-sample sums hs = (p0 + p1) + (p2 + p3),
+// and the row's value_scale sums, an ordered dadd over the tiles' per-tile
+// double sums.  Each tile's own recurrence (its 16 slots over the samples)
+// depends on nothing outside it.  So the update runs as
+//   k_b4_update_tiles: a half-warp per tile, 8 per block-row at a time,
+//     writing the tile's new bytes, its hs[4 rows][B] and its per-row
+//     double sums to scratch;
+//   k_b4_rows_chain: a warp per row, the ordered chains over the tiles
+//     (dx in place, then the value_scale step from the totals);
+//   k_b4_evict_rows: a half-warp per block-row, the eviction.
+// Same values, same order of every sum as k_b4_update, with all tiles of
+// the layer's block-rows in flight instead of one half-warp per block-row.
+constexpr int kB4Group = 64;   // tiles per block of k_b4_update_tiles
+template <int RANK, bool STOCH>
+__global__ void __launch_bounds__(128) k_b4_update_tiles(LayerView L, B4View V, const float* __restrict__ xT,
+                                                         const float* __restrict__ dyT, int B, UpdateParams P,
+                                                         int64_t br0, int64_t part_base, float* __restrict__ hsb,
+                                                         double* __restrict__ mrb, float* __restrict__ mcb) {
+    const int lane = threadIdx.x & 31, half = lane >> 4, s = lane & 15;
+    const int hw = threadIdx.x >> 4;                     // 8 half-warps per block
+    const int64_t br = br0 + blockIdx.y;                 // blockIdx.x: a group of kB4Group tiles
+    const unsigned hmask = half ? 0xFFFF0000u : 0x0000FFFFu;
+    if (br >= V.BR) return;
+    const int nt = min(V.nt[br], (int)(blockIdx.x + 1) * kB4Group);
+    const int li = s & 3, lj = s >> 2;
+    const int64_t row = br * 4 + li;
+    const bool row_ok = row < L.n_in;
+    const bool leader = lj == 0;
+    const uint32_t nnz_row = (uint32_t)V.nt[br] * 4u;
+    const float eff_lr = P.lr_per_row_nnz ? __fdiv_rn(P.lr, (float)nnz_row) : P.lr;
+    const float onem = __fsub_rn(1.0f, P.beta2);
+    float vsk[RANK];
+#pragma unroll
+    for (int k = 0; k < RANK; ++k) vsk[k] = row_ok ? L.vs[row * RANK + k] : 0.0f;
+    const float isr = row_ok ? L.is[row] : 0.0f;
+    const int64_t base = V.es[br];
+    for (int e = (int)blockIdx.x * kB4Group + hw; e < nt; e += 8) {
+        const int64_t ti = base + e;
+        const int64_t loc = ti - part_base;
+        uint4 tw = V.tile[ti];
+        const int64_t col = (int64_t)V.bc[ti] * 4 + lj;
+        const bool act = row_ok;                         // every column of a full tile exists
+        const uint32_t byte = tile_byte(tw, s);
+        float osk[RANK];
+        float S = 0.0f;
+#pragma unroll
+        for (int k = 0; k < RANK; ++k) {
+            osk[k] = L.os[col * RANK + k];
+            S = __fmaf_rn(vsk[k], osk[k], S);
+        }
+        if (!act) S = 0.0f;
+        const float cis = act ? __fmul_rn(isr, L.ois[col]) : 0.0f;
+        const float qorig = act ? fp4_decode(byte & 0xFu) : 0.0f;
+        float quant = qorig;
+        float ci = act ? __fmul_rn(fp4_decode(byte >> 4), cis) : 0.0f;
+        float mcol[RANK], mcolc[RANK];
+        double mrow[RANK], mrowc[RANK];
+#pragma unroll
+        for (int k = 0; k < RANK; ++k) { mcol[k] = mcolc[k] = 0.0f; mrow[k] = mrowc[k] = 0.0; }
+        float* hrow = hsb + (loc * 4 + li) * (int64_t)B;
+#pragma unroll 4
+        for (int b = 0; b < B; ++b) {
+            const float x = row_ok ? xT[row * B + b] : 0.0f;
+            const float dy = dyT[col * B + b];
+            const float g = __fmul_rn(dy, x);
+            float cb = 0.0f, qf = 0.0f;
+            if (act) {
+                cb = __fmul_rn(qorig, x);
+                ci = bounded_ci(ci, g, cb, P.beta2, onem);
+                const float ngS = __fmul_rn(-g, S);
+                float raw = P.damp ? __fdiv_rn(ngS, __fadd_rn(__fsqrt_rn(ci), P.eps)) : ngS;
+                if (raw > 2.0f) raw = 2.0f;
+                if (raw < -2.0f) raw = -2.0f;
+                quant = __fmaf_rn(eff_lr, raw, quant);
+                qf = (quant == 0.0f) ? 0.1f : quant;
+            }
+            const float sdy = __fmul_rn(S, dy);
+#pragma unroll
+            for (int k = 0; k < RANK; ++k) {
+                const float qo = __fmul_rn(qf, osk[k]);
+                const float pg = __fmul_rn(qo, g), pc = __fmul_rn(qo, cb);
+                const float ag = __fadd_rn(pg, __shfl_xor_sync(hmask, pg, 8));
+                const float ac = __fadd_rn(pc, __shfl_xor_sync(hmask, pc, 8));
+                const float hg = __fadd_rn(ag, __shfl_xor_sync(hmask, ag, 4));
+                const float hc = __fadd_rn(ac, __shfl_xor_sync(hmask, ac, 4));
+                mrow[k] = __dadd_rn(mrow[k], (double)hg);
+                mrowc[k] = __dadd_rn(mrowc[k], (double)hc);
+                mcol[k] = __fmaf_rn(__fmul_rn(qf, vsk[k]), g, mcol[k]);
+                mcolc[k] = __fmaf_rn(__fmul_rn(qf, vsk[k]), cb, mcolc[k]);
+            }
+            const float p = __fmul_rn(quant, sdy);
+            const float a = __fadd_rn(p, __shfl_xor_sync(hmask, p, 4));
+            const float hs = __fadd_rn(a, __shfl_xor_sync(hmask, a, 8));
+            if (leader) hrow[b] = hs;
+        }
+        if (leader) {
+#pragma unroll
+            for (int k = 0; k < RANK; ++k) {
+                mrb[((loc * 4 + li) * RANK + k) * 2] = mrow[k];
+                mrb[((loc * 4 + li) * RANK + k) * 2 + 1] = mrowc[k];
+            }
+        }
+        if (P.os_trainable) {   // the slot's column sums, added in order by k_b4_col_sums
+#pragma unroll
+            for (int k = 0; k < RANK; ++k) {
+                mcb[((loc * 16 + s) * RANK + k) * 2] = act ? mcol[k] : 0.0f;
+                mcb[((loc * 16 + s) * RANK + k) * 2 + 1] = act ? mcolc[k] : 0.0f;
+            }
+        }
+        if (act) {
+            const float imp_ratio = __fdiv_rn(ci, cis);
+            uint32_t wq, iq;
+            if (STOCH) {
+                const uint64_t el = (1ULL << 61) | ((uint64_t)row * (uint64_t)L.n_out + (uint64_t)col);
+                wq = fp4_quantize_stochastic(quant, rng_draw(P.call_key, el, 0));
+                iq = fp4_quantize_stochastic(imp_ratio, rng_draw(P.call_key, el, 1));
+            } else {
+                wq = fp4_encode(quant);
+                iq = fp4_encode(imp_ratio);
+            }
+            set_tile_byte(tw, s, (iq << 4) | wq);
+        }
+        const uint32_t mine = tile_byte(tw, s);
+        uint32_t words[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            uint32_t w = 0;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) w |= __shfl_sync(hmask, mine, (lane & 16) | (q * 4 + k)) << (8 * k);
+            words[q] = w;
+        }
+        if (s == 0) {
+            const uint4 nw = make_uint4(words[0], words[1], words[2], words[3]);
+            V.tile[ti] = nw;
+            V.sparse[ti] = (uint32_t)tile_live(nw) <= V.switch_point ? 1 : 0;
+        }
+    }
+}
+
+// output_scale gradient sums of the chunk's tiles, one thread per column, in
+// the reference's order: block-rows ascending (the tile column index lists
+// each block-column's tiles so), rows li ascending within a tile
+template <int RANK>
+__global__ void k_b4_col_sums(LayerView L, B4View V, int64_t br0, int64_t br1, int64_t part_base,
+                              const float* __restrict__ mcb, float* __restrict__ colg, float* __restrict__ colc) {
+    const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= L.n_out) return;
+    const int64_t bcol = c >> 2;
+    const int lj = (int)(c & 3);
+    float g[RANK], h[RANK];
+#pragma unroll
+    for (int k = 0; k < RANK; ++k) { g[k] = colg[c * RANK + k]; h[k] = colc[c * RANK + k]; }
+    for (int t = V.cptr[bcol]; t < V.cptr[bcol + 1]; ++t) {
+        const int64_t br = V.cbr[t];
+        if (br < br0) continue;
+        if (br >= br1) break;
+        const int64_t loc = (int64_t)V.ctile[t] - part_base;
+        for (int li = 0; li < 4; ++li) {
+            if (br * 4 + li >= L.n_in) break;
+            const float* m = mcb + ((loc * 16 + lj * 4 + li) * RANK) * 2;
+#pragma unroll
+            for (int k = 0; k < RANK; ++k) {
+                g[k] = __fadd_rn(g[k], m[2 * k]);
+                h[k] = __fadd_rn(h[k], m[2 * k + 1]);
+            }
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < RANK; ++k) { colg[c * RANK + k] = g[k]; colc[c * RANK + k] = h[k]; }
+}
+
+// the ordered chains of one row over its block-row's tiles (a warp per row):
+// dx[b] = ((dx[b] + hs_0[b]) + hs_1[b]) + ..., the value_scale totals
+// likewise in double, then the block4 value_scale step (linear_disldo.hpp:1882-1950)
+template <int RANK>
+__global__ void __launch_bounds__(128) k_b4_rows_chain(LayerView L, B4View V, int B, UpdateParams P, int64_t br0,
+                                                       int64_t br1, int64_t part_base,
+                                                       const float* __restrict__ hsb, const double* __restrict__ mrb,
+                                                       float* __restrict__ dxT) {
+    const int lane = threadIdx.x & 31;
+    const int64_t row = br0 * 4 + (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
+    const int64_t br = row >> 2;
+    const int li = (int)(row & 3);
+    if (br >= br1 || row >= L.n_in) return;
+    const int nt = V.nt[br];
+    if (nt == 0) return;
+    const int64_t loc0 = V.es[br] - part_base;
+    const int64_t stride = (int64_t)4 * B;
+    for (int b = lane; b < B; b += 32) {
+        float acc = dxT[row * B + b];
+        const float* h = hsb + (loc0 * 4 + li) * (int64_t)B + b;
+        int e = 0;
+        for (; e + 8 <= nt; e += 8) {   // eight loads in flight, then the ordered adds
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v[u] = h[(int64_t)(e + u) * stride];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) acc = __fadd_rn(acc, v[u]);
+        }
+        for (; e < nt; ++e) acc = __fadd_rn(acc, h[(int64_t)e * stride]);
+        dxT[row * B + b] = acc;
+    }
+    if (lane < RANK) {
+        const int k = lane;
+        double trg = 0.0, trc = 0.0;
+        const double* m = mrb + ((loc0 * 4 + li) * RANK + k) * 2;
+        for (int e = 0; e < nt; ++e) {
+            trg = __dadd_rn(trg, m[(int64_t)e * 4 * RANK * 2]);
+            trc = __dadd_rn(trc, m[(int64_t)e * 4 * RANK * 2 + 1]);
+        }
+        if (trg != 0.0 || trc != 0.0) {
+            const float scale_eff_lr = __fdiv_rn(P.lr, (float)((uint32_t)nt * 4u));
+            const int64_t i = row * RANK + k;
+            rmsprop_scale(L.vs + i, L.vsi + i, (float)trg, scale_eff_lr, (float)trc, L.vstep + i, P);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(128) k_b4_evict_rows(LayerView L, B4View V, int64_t br0, int64_t br1) {
+    const int lane = threadIdx.x & 31, half = lane >> 4, s = lane & 15;
+    const int64_t br = br0 + (int64_t)blockIdx.x * 8 + (threadIdx.x >> 4);
+    const unsigned hmask = half ? 0xFFFF0000u : 0x0000FFFFu;
+    if (br >= br1) return;
+    const int nt = V.nt[br];
+    if (nt == 0) return;
+    b4_evict_row(L, V, br, V.es[br], nt, s, hmask);
+}
+
+bool b4_update_split_applies(const LayerView& L) { return L.n_out % 4 == 0; }
+
+void launch_b4_update_split(const LayerView& L, const B4View& V, const float* xT, const float* dyT, int B,
+                            const UpdateParams& P, float* dxT, int64_t br0, int64_t br1, int64_t part_base,
+                            float* hsb, double* mrb, float* mcb, cudaStream_t s) {
+    if (br1 <= br0 || B == 0) return;
+    const unsigned nbr = (unsigned)(br1 - br0);
+    const dim3 tg((unsigned)((V.BC + kB4Group - 1) / kB4Group), nbr);   // a row holds at most BC tiles
+#define SILI_B4S(R, ST) \
+    k_b4_update_tiles<R, ST><<<tg, 128, 0, s>>>(L, V, xT, dyT, B, P, br0, part_base, hsb, mrb, mcb)
+    switch (L.rank * 2 + (P.stochastic ? 1 : 0)) {
+        case 2: SILI_B4S(1, false); break;
+        case 3: SILI_B4S(1, true); break;
+        case 4: SILI_B4S(2, false); break;
+        case 5: SILI_B4S(2, true); break;
+        case 6: SILI_B4S(3, false); break;
+        case 7: SILI_B4S(3, true); break;
+        case 8: SILI_B4S(4, false); break;
+        default: SILI_B4S(4, true); break;
+    }
+#undef SILI_B4S
+    count_launch();
+    if (P.os_trainable) {
+        const unsigned cg = (unsigned)((L.n_out + 255) / 256);
+        switch (L.rank) {
+            case 1: k_b4_col_sums<1><<<cg, 256, 0, s>>>(L, V, br0, br1, part_base, mcb, P.colg, P.colc); break;
+            case 2: k_b4_col_sums<2><<<cg, 256, 0, s>>>(L, V, br0, br1, part_base, mcb, P.colg, P.colc); break;
+            case 3: k_b4_col_sums<3><<<cg, 256, 0, s>>>(L, V, br0, br1, part_base, mcb, P.colg, P.colc); break;
+            default: k_b4_col_sums<4><<<cg, 256, 0, s>>>(L, V, br0, br1, part_base, mcb, P.colg, P.colc); break;
+        }
+        count_launch();
+    }
+    switch (L.rank) {
+        case 1: k_b4_rows_chain<1><<<nbr, 128, 0, s>>>(L, V, B, P, br0, br1, part_base, hsb, mrb, dxT); break;
+        case 2: k_b4_rows_chain<2><<<nbr, 128, 0, s>>>(L, V, B, P, br0, br1, part_base, hsb, mrb, dxT); break;
+        case 3: k_b4_rows_chain<3><<<nbr, 128, 0, s>>>(L, V, B, P, br0, br1, part_base, hsb, mrb, dxT); break;
+        default: k_b4_rows_chain<4><<<nbr, 128, 0, s>>>(L, V, B, P, br0, br1, part_base, hsb, mrb, dxT); break;
+    }
+    count_launch();
+}
+void launch_b4_evict_rows(const LayerView& L, const B4View& V, cudaStream_t s) {
+    if (V.BR == 0) return;
+    k_b4_evict_rows<<<(unsigned)((V.BR + 7) / 8), 128, 0, s>>>(L, V, 0, V.BR);
+    count_launch();
 }
 
 void launch_b4_update(const LayerView& L, const B4View& V, const float* xT, const float* dyT, int B,

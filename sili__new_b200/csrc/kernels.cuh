@@ -289,6 +289,16 @@ void launch_b4_dx(const LayerView& L, const B4View& V, const float* dyT, int B, 
 // then merge_row_workspace's eviction and the block4 value_scale step
 void launch_b4_update(const LayerView& L, const B4View& V, const float* xT, const float* dyT, int B,
                       const UpdateParams& P, float* dxT, cudaStream_t s);
+// the same update as passes with every tile in parallel (block-rows
+// [br0, br1); scratch hsb: 4*B floats, mrb: 4*rank*2 doubles, mcb (when the
+// output scale trains): 16*rank*2 floats per tile slot from part_base =
+// es[br0] to es[br1]; needs the tile column index); only when n_out % 4 == 0
+bool b4_update_split_applies(const LayerView& L);
+void launch_b4_update_split(const LayerView& L, const B4View& V, const float* xT, const float* dyT, int B,
+                            const UpdateParams& P, float* dxT, int64_t br0, int64_t br1, int64_t part_base,
+                            float* hsb, double* mrb, float* mcb, cudaStream_t s);
+// the eviction pass after every chunk's update (a half-warp per block-row)
+void launch_b4_evict_rows(const LayerView& L, const B4View& V, cudaStream_t s);
 // sparse-input forward block4 windows: y[B, n_out] += (xT/presT [n_in, B])
 void launch_b4_forward_sparse(const LayerView& L, const B4View& V, const float* xT, const uint8_t* presT, int B,
                               float* y, cudaStream_t s);

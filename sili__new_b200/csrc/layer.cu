@@ -165,6 +165,9 @@ struct sili_layer {
     DBuf<uint4> b4_tile;
     DBuf<uint8_t> b4_sparse;
     DBuf<unsigned long long> b4_cnt;
+    DBuf<float> b4_hs;       // per-tile dx sums of the tile-parallel update
+    DBuf<double> b4_mr;      // per-tile value_scale sums of the tile-parallel update
+    DBuf<float> b4_mc;       // per-slot output_scale sums of the tile-parallel update
     DBuf<int> b4_cptr, b4_ctile, b4_cbr, b4_keys, b4_keys_o, b4_perm, b4_perm_o, b4_slots, b4_brs, b4_off;
     int64_t b4_ntiles = 0;                 // live tiles (host mirror)
     int64_t b4_max_idx = INT64_MAX, b4_max_tile = INT64_MAX;
@@ -1285,6 +1288,42 @@ int sili_layer_forward_dense(sili_layer* h, const float* x, int batch, float* y,
     return SILI_OK;
 }
 
+// The block4 part of the fused update: tiles in parallel (passes over chunks
+// of block-rows whose per-tile scratch stays within 4 GiB, then the eviction
+// of every block-row) when every tile is full width, else one half-warp per
+// block-row.
+static int b4_update(sili_layer* h, const LayerView& v, int batch, const UpdateParams& P, cudaStream_t s) {
+    const B4View V = h->b4view();
+    if (!b4_update_split_applies(v)) {
+        launch_b4_update(v, V, h->xT.p, h->dyT.p, batch, P, h->dxT.p, s);
+        return SILI_OK;
+    }
+    if (P.os_trainable) RC(ensure_b4_index(h, s));   // the column sums walk it
+    const int64_t BR = h->b4_BR;
+    std::vector<int64_t> es((size_t)BR + 1);
+    CK(cudaMemcpyAsync(es.data(), h->b4_es.p, (size_t)(BR + 1) * 8, cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    const int64_t per_tile = (int64_t)4 * batch * 4 + (int64_t)4 * h->rank * 2 * 8 + (int64_t)16 * h->rank * 2 * 4;
+    const int64_t limit = std::max<int64_t>(1, ((int64_t)4 << 30) / per_tile);   // 4 GiB
+    std::vector<std::pair<int64_t, int64_t>> chunks;
+    int64_t most = 1;
+    for (int64_t br0 = 0; br0 < BR;) {
+        int64_t br1 = br0 + 1;
+        while (br1 < BR && es[br1 + 1] - es[br0] <= limit) ++br1;
+        chunks.emplace_back(br0, br1);
+        most = std::max(most, es[br1] - es[br0]);
+        br0 = br1;
+    }
+    RC(h->b4_hs.reserve(most * 4 * batch + 1));
+    RC(h->b4_mr.reserve(most * 4 * h->rank * 2 + 1));
+    if (P.os_trainable) RC(h->b4_mc.reserve(most * 16 * h->rank * 2 + 1));
+    for (const auto& c : chunks)
+        launch_b4_update_split(v, V, h->xT.p, h->dyT.p, batch, P, h->dxT.p, c.first, c.second, es[c.first],
+                               h->b4_hs.p, h->b4_mr.p, h->b4_mc.p, s);
+    launch_b4_evict_rows(v, V, s);
+    return SILI_OK;
+}
+
 // part != nullptr: a column shard's backward (device array of
 // sili_layer_row_part_len doubles, zeroed here; the row steps wait for
 // sili_layer_apply_row_part)
@@ -1353,7 +1392,7 @@ static int backward_dense_impl(sili_layer* h, const float* x, const float* dy, i
             CK(cudaMemsetAsync(h->dxT.p, 0, (size_t)batch * n_in * 4, s));
         }
         // block4 part after the scattered one (linear_disldo.hpp:939-1951)
-        if (h->b4_ntiles > 0) launch_b4_update(v, h->b4view(), h->xT.p, h->dyT.p, batch, P, h->dxT.p, s);
+        if (h->b4_ntiles > 0) RC(b4_update(h, v, batch, P, s));
         if (part) {
             // rows with no synapse on any shard: this shard's columns' part of S
             if (h->shard_any_dead) launch_dead_S(v, dyd, batch, part + 2 * n_in * h->rank, s);
