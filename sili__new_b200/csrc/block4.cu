@@ -139,43 +139,53 @@ __global__ void __launch_bounds__(128) k_b4_forward(LayerView L, B4View V, const
         for (int k = 0; k < 4; ++k)
             os[lj][k] = (col0 + lj < L.n_out && k < L.rank) ? L.os[(col0 + lj) * L.rank + k] : 0.0f;
     const int t0 = V.cptr[bcol], t1 = V.cptr[bcol + 1];
-    // the next tile's block-row and slot bytes are loaded a tile ahead
-    int64_t nbr = t0 < t1 ? V.cbr[t0] : 0;
-    uint4 ntw = t0 < t1 ? V.tile[V.ctile[t0]] : make_uint4(0, 0, 0, 0);
-    for (int t = t0; t < t1; ++t) {
-        const int64_t br = nbr;
-        const uint4 tw = ntw;
-        if (t + 1 < t1) {
-            nbr = V.cbr[t + 1];
-            ntw = V.tile[V.ctile[t + 1]];
+    // four tiles at a time: their indices, then their slot bytes, x values
+    // and row scales are all in flight before the first tile's sums, which
+    // then run in tile order
+    constexpr int G = 4;
+    for (int t = t0; t < t1; t += G) {
+        int64_t br[G];
+        int ct[G];
+#pragma unroll
+        for (int u = 0; u < G; ++u) {
+            const bool ok = t + u < t1;
+            ct[u] = ok ? V.ctile[t + u] : -1;
+            br[u] = ok ? V.cbr[t + u] : 0;
         }
-        float x[4], vs[4][4];
-        int64_t rows[4];
+        uint4 tw[G];
+        float x[G][4], vs[G][4];
 #pragma unroll
-        for (int li = 0; li < 4; ++li) {
-            const int64_t row = br * 4 + li;
-            rows[li] = row;
-            const bool rok = row < L.n_in;
-            x[li] = bok ? xT[(rok ? row : 0) * B + b] : 0.0f;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) vs[li][k] = (rok && k < L.rank) ? L.vs[row * L.rank + k] : 0.0f;
-        }
-#pragma unroll
-        for (int lj = 0; lj < 4; ++lj) {
-            const int64_t col = col0 + lj;
-            if (col >= L.n_out) continue;
-            float w[4];
+        for (int u = 0; u < G; ++u) {
+            tw[u] = ct[u] >= 0 ? V.tile[ct[u]] : make_uint4(0, 0, 0, 0);
 #pragma unroll
             for (int li = 0; li < 4; ++li) {
-                float sc = 0.0f;
-#pragma unroll
-                for (int k = 0; k < 4; ++k)
-                    if (k < L.rank) sc = __fmaf_rn(vs[li][k], os[lj][k], sc);
-                w[li] = rows[li] < L.n_in ? __fmul_rn(fp4_decode(tile_byte(tw, lj * 4 + li) & 0xFu), sc) : 0.0f;
+                const int64_t row = br[u] * 4 + li;
+                const bool rok = ct[u] >= 0 && row < L.n_in;
+                x[u][li] = (bok && rok) ? xT[row * B + b] : 0.0f;
+                vs[u][li] = rok ? L.vs[row * L.rank] : 0.0f;   // component 0; the others below
             }
-            const float acc = __fadd_rn(__fmaf_rn(w[0], x[0], __fmul_rn(w[1], x[1])),
-                                        __fmaf_rn(w[2], x[2], __fmul_rn(w[3], x[3])));
-            mo[lj] = __fadd_rn(mo[lj], acc);
+        }
+#pragma unroll
+        for (int u = 0; u < G; ++u) {
+            if (ct[u] < 0) break;
+#pragma unroll
+            for (int lj = 0; lj < 4; ++lj) {
+                const int64_t col = col0 + lj;
+                if (col >= L.n_out) continue;
+                float w[4];
+#pragma unroll
+                for (int li = 0; li < 4; ++li) {
+                    const int64_t row = br[u] * 4 + li;
+                    float sc = __fmaf_rn(vs[u][li], os[lj][0], 0.0f);
+#pragma unroll
+                    for (int k = 1; k < 4; ++k)
+                        if (k < L.rank) sc = __fmaf_rn(L.vs[row * L.rank + k], os[lj][k], sc);
+                    w[li] = row < L.n_in ? __fmul_rn(fp4_decode(tile_byte(tw[u], lj * 4 + li) & 0xFu), sc) : 0.0f;
+                }
+                const float acc = __fadd_rn(__fmaf_rn(w[0], x[u][0], __fmul_rn(w[1], x[u][1])),
+                                            __fmaf_rn(w[2], x[u][2], __fmul_rn(w[3], x[u][3])));
+                mo[lj] = __fadd_rn(mo[lj], acc);
+            }
         }
     }
     if (!bok) return;
