@@ -273,7 +273,7 @@ void launch_b4_dx(const LayerView& L, const B4View& V, const float* dyT, int B, 
 // it and repacks that tile.  Zeroing a slot changes no other slot's a, so
 // without NaN importances the evictions are the live slots in ascending
 // (a, tile, li, lj) order, stopped as soon as the row fits: here they are
-// taken a level (one value of a) at a time, 16 tiles per step with a prefix
+// taken a level (one value of a) at a time, one tile per lane per step with a prefix
 // sum of the tiles' byte savings, which gives the same slots, repacking and
 // counters in O(levels x tiles) instead of O(evictions x tiles).  A NaN
 // importance changes the reference's scan (a NaN first live slot is taken,
@@ -284,16 +284,17 @@ __device__ __forceinline__ double b4_abs_imp(const LayerView& L, uint32_t byte, 
     return fabs((double)fp4_decode(byte >> 4) * (double)L.is[r] * (double)L.ois[c]);
 }
 
+template <int W>   // lanes per block-row: 16 (a half-warp) or 32
 __device__ void b4_evict_row(const LayerView& L, const B4View& V, int64_t br, int64_t base, int nt, int s,
                              unsigned hmask) {
     const int64_t cap = V.alloc[V.BR + br];
     long long used = 0;
-    for (int e = s; e < nt; e += 16) used += tile_len(tile_live(V.tile[base + e]), V.sparse[base + e] != 0);
+    for (int e = s; e < nt; e += W) used += tile_len(tile_live(V.tile[base + e]), V.sparse[base + e] != 0);
 #pragma unroll
-    for (int o = 8; o > 0; o >>= 1) used += __shfl_xor_sync(hmask, used, o);
+    for (int o = W / 2; o > 0; o >>= 1) used += __shfl_xor_sync(hmask, used, o);
     if (used > cap) {
         bool nan_here = false;
-        for (int e = s; e < nt && !nan_here; e += 16) {
+        for (int e = s; e < nt && !nan_here; e += W) {
             const uint4 tw = V.tile[base + e];
             const int64_t c0 = (int64_t)V.bc[base + e] * 4;
             for (int q = 0; q < 16; ++q) {
@@ -329,13 +330,13 @@ __device__ void b4_evict_row(const LayerView& L, const B4View& V, int64_t br, in
                     V.sparse[base + be] = sp ? 1 : 0;
                 }
             }
-            used = __shfl_sync(hmask, used, (threadIdx.x & 16));
+            used = __shfl_sync(hmask, used, W == 32 ? 0 : (int)(threadIdx.x & 16));
             __syncwarp(hmask);
         } else {
             while (used > cap) {
                 // the smallest a among the live slots
                 double amin = -1.0;
-                for (int e = s; e < nt; e += 16) {
+                for (int e = s; e < nt; e += W) {
                     const uint4 tw = V.tile[base + e];
                     const int64_t c0 = (int64_t)V.bc[base + e] * 4;
                     for (int q = 0; q < 16; ++q) {
@@ -346,13 +347,13 @@ __device__ void b4_evict_row(const LayerView& L, const B4View& V, int64_t br, in
                     }
                 }
 #pragma unroll
-                for (int o = 8; o > 0; o >>= 1) {
+                for (int o = W / 2; o > 0; o >>= 1) {
                     const double ob = __shfl_xor_sync(hmask, amin, o);
                     if (ob >= 0.0 && (amin < 0.0 || ob < amin)) amin = ob;
                 }
                 if (amin < 0.0) break;   // nothing live left
-                // its slots in (tile, li, lj) order, 16 tiles per step, while the row does not fit
-                for (int e0 = 0; e0 < nt && used > cap; e0 += 16) {
+                // its slots in (tile, li, lj) order, W tiles per step, while the row does not fit
+                for (int e0 = 0; e0 < nt && used > cap; e0 += W) {
                     const int e = e0 + s;
                     uint4 tw = make_uint4(0u, 0u, 0u, 0u);
                     int live = 0, k = 0, old_len = 0;
@@ -374,8 +375,8 @@ __device__ void b4_evict_row(const LayerView& L, const B4View& V, int64_t br, in
                     const long long d = k > 0 ? saving(k) : 0;
                     long long incl = d;
 #pragma unroll
-                    for (int o = 1; o < 16; o <<= 1) {
-                        const long long t = __shfl_up_sync(hmask, incl, o, 16);
+                    for (int o = 1; o < W; o <<= 1) {
+                        const long long t = __shfl_up_sync(hmask, incl, o, W);
                         if (s >= o) incl += t;
                     }
                     const long long excl = incl - d, need = used - cap;
@@ -403,7 +404,7 @@ __device__ void b4_evict_row(const LayerView& L, const B4View& V, int64_t br, in
                         applied = saving(take);
                     }
 #pragma unroll
-                    for (int o = 8; o > 0; o >>= 1) applied += __shfl_xor_sync(hmask, applied, o);
+                    for (int o = W / 2; o > 0; o >>= 1) applied += __shfl_xor_sync(hmask, applied, o);
                     used -= applied;
                 }
             }
@@ -610,7 +611,7 @@ __global__ void __launch_bounds__(128) k_b4_update(LayerView L, B4View V, const 
         }
         __syncwarp(hmask);
     }
-    b4_evict_row(L, V, br, base, nt, s, hmask);
+    b4_evict_row<16>(L, V, br, base, nt, s, hmask);
     // ── block4 value_scale step and dx write-back (leader lane of each row) ──
     if (leader && row_ok) {
         const float scale_eff_lr = __fdiv_rn(P.lr, (float)nnz_row);
@@ -636,7 +637,7 @@ __global__ void __launch_bounds__(128) k_b4_update(LayerView L, B4View V, const 
 //     double sums to scratch;
 //   k_b4_rows_chain: a warp per row, the ordered chains over the tiles
 //     (dx in place, then the value_scale step from the totals);
-//   k_b4_evict_rows: a half-warp per block-row, the eviction.
+//   k_b4_evict_rows: a warp per block-row, the eviction.
 // Same values, same order of every sum as k_b4_update, with all tiles of
 // the layer's block-rows in flight instead of one half-warp per block-row.
 constexpr int kB4Group = 64;   // tiles per block of k_b4_update_tiles
@@ -845,14 +846,14 @@ __global__ void __launch_bounds__(128) k_b4_rows_chain(LayerView L, B4View V, in
     }
 }
 
+// a warp per block-row (the update kernel's own eviction uses its half-warp)
 __global__ void __launch_bounds__(128) k_b4_evict_rows(LayerView L, B4View V, int64_t br0, int64_t br1) {
-    const int lane = threadIdx.x & 31, half = lane >> 4, s = lane & 15;
-    const int64_t br = br0 + (int64_t)blockIdx.x * 8 + (threadIdx.x >> 4);
-    const unsigned hmask = half ? 0xFFFF0000u : 0x0000FFFFu;
+    const int lane = threadIdx.x & 31;
+    const int64_t br = br0 + (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
     if (br >= br1) return;
     const int nt = V.nt[br];
     if (nt == 0) return;
-    b4_evict_row(L, V, br, V.es[br], nt, s, hmask);
+    b4_evict_row<32>(L, V, br, V.es[br], nt, lane, 0xFFFFFFFFu);
 }
 
 bool b4_update_split_applies(const LayerView& L) { return L.n_out % 4 == 0; }
@@ -897,7 +898,7 @@ void launch_b4_update_split(const LayerView& L, const B4View& V, const float* xT
 }
 void launch_b4_evict_rows(const LayerView& L, const B4View& V, cudaStream_t s) {
     if (V.BR == 0) return;
-    k_b4_evict_rows<<<(unsigned)((V.BR + 7) / 8), 128, 0, s>>>(L, V, 0, V.BR);
+    k_b4_evict_rows<<<(unsigned)((V.BR + 3) / 4), 128, 0, s>>>(L, V, 0, V.BR);
     count_launch();
 }
 
@@ -1105,7 +1106,7 @@ __global__ void __launch_bounds__(128) k_b4_backward_sparse(LayerView L, B4View 
                 __syncwarp(hmask);
             }
         }
-        if (training) b4_evict_row(L, V, br, base, nt, s, hmask);
+        if (training) b4_evict_row<16>(L, V, br, base, nt, s, hmask);
         if (leader && row_ok) {
             float* d = dxT + row * B + b;
             *d = __fadd_rn(*d, dxa);
