@@ -130,18 +130,18 @@ __global__ void __launch_bounds__(128) k_b4_forward(LayerView L, B4View V, const
     const bool bok = b < B;
     float mo[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     const int64_t col0 = bcol * 4;
-    // the block-column's output scales, read once (S = sum_k vs_k * os_k as a
-    // fused chain from 0, scale_of's arithmetic)
-    float os[4][4];
+    // The slot weights w = fp4(code) * S(row, col) are the same for every
+    // sample, so each is computed once per warp: lane l holds slot l & 15
+    // (li = l & 3, lj = (l >> 2) & 3) of one of two tiles (l >> 4), and the
+    // sums fetch them by shuffle.  S is scale_of's fused chain from 0.
+    const int q = lane & 15, qli = q & 3, qlj = q >> 2;
+    const bool qcol = col0 + qlj < L.n_out;
+    float osq[4];
 #pragma unroll
-    for (int lj = 0; lj < 4; ++lj)
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-            os[lj][k] = (col0 + lj < L.n_out && k < L.rank) ? L.os[(col0 + lj) * L.rank + k] : 0.0f;
+    for (int k = 0; k < 4; ++k) osq[k] = (qcol && k < L.rank) ? L.os[(col0 + qlj) * L.rank + k] : 0.0f;
     const int t0 = V.cptr[bcol], t1 = V.cptr[bcol + 1];
-    // four tiles at a time: their indices, then their slot bytes, x values
-    // and row scales are all in flight before the first tile's sums, which
-    // then run in tile order
+    // four tiles at a time: their indices, bytes, x values and weights are
+    // all in flight before the first tile's sums, which run in tile order
     constexpr int G = 4;
     for (int t = t0; t < t1; t += G) {
         int64_t br[G];
@@ -152,36 +152,42 @@ __global__ void __launch_bounds__(128) k_b4_forward(LayerView L, B4View V, const
             ct[u] = ok ? V.ctile[t + u] : -1;
             br[u] = ok ? V.cbr[t + u] : 0;
         }
-        uint4 tw[G];
-        float x[G][4], vs[G][4];
+        float x[G][4], wl[G / 2];
 #pragma unroll
-        for (int u = 0; u < G; ++u) {
-            tw[u] = ct[u] >= 0 ? V.tile[ct[u]] : make_uint4(0, 0, 0, 0);
+        for (int u = 0; u < G; ++u)
 #pragma unroll
             for (int li = 0; li < 4; ++li) {
                 const int64_t row = br[u] * 4 + li;
-                const bool rok = ct[u] >= 0 && row < L.n_in;
-                x[u][li] = (bok && rok) ? xT[row * B + b] : 0.0f;
-                vs[u][li] = rok ? L.vs[row * L.rank] : 0.0f;   // component 0; the others below
+                x[u][li] = (bok && ct[u] >= 0 && row < L.n_in) ? xT[row * B + b] : 0.0f;
             }
+#pragma unroll
+        for (int pr = 0; pr < G / 2; ++pr) {
+            const int u = 2 * pr + (lane >> 4);
+            const int cu = (lane >> 4) ? ct[2 * pr + 1] : ct[2 * pr];
+            const int64_t bru = (lane >> 4) ? br[2 * pr + 1] : br[2 * pr];
+            const int64_t row = bru * 4 + qli;
+            float w = 0.0f;
+            if (cu >= 0 && row < L.n_in) {
+                const uint4 tw = V.tile[cu];
+                float sc = 0.0f;
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    if (k < L.rank) sc = __fmaf_rn(L.vs[row * L.rank + k], osq[k], sc);
+                w = __fmul_rn(fp4_decode(tile_byte(tw, q) & 0xFu), sc);
+            }
+            wl[pr] = w;
+            (void)u;
         }
 #pragma unroll
         for (int u = 0; u < G; ++u) {
             if (ct[u] < 0) break;
+            const int src = (u & 1) << 4;
 #pragma unroll
             for (int lj = 0; lj < 4; ++lj) {
-                const int64_t col = col0 + lj;
-                if (col >= L.n_out) continue;
                 float w[4];
 #pragma unroll
-                for (int li = 0; li < 4; ++li) {
-                    const int64_t row = br[u] * 4 + li;
-                    float sc = __fmaf_rn(vs[u][li], os[lj][0], 0.0f);
-#pragma unroll
-                    for (int k = 1; k < 4; ++k)
-                        if (k < L.rank) sc = __fmaf_rn(L.vs[row * L.rank + k], os[lj][k], sc);
-                    w[li] = row < L.n_in ? __fmul_rn(fp4_decode(tile_byte(tw[u], lj * 4 + li) & 0xFu), sc) : 0.0f;
-                }
+                for (int li = 0; li < 4; ++li) w[li] = __shfl_sync(0xffffffffu, wl[u >> 1], src | (lj * 4 + li));
+                if (col0 + lj >= L.n_out) continue;
                 const float acc = __fadd_rn(__fmaf_rn(w[0], x[u][0], __fmul_rn(w[1], x[u][1])),
                                             __fmaf_rn(w[2], x[u][2], __fmul_rn(w[3], x[u][3])));
                 mo[lj] = __fadd_rn(mo[lj], acc);
