@@ -1309,7 +1309,8 @@ static int b4_update(sili_layer* h, const LayerView& v, int batch, const UpdateP
     int64_t most = 1;
     for (int64_t br0 = 0; br0 < BR;) {
         int64_t br1 = br0 + 1;
-        while (br1 < BR && es[br1 + 1] - es[br0] <= limit) ++br1;
+        // (at most 65535 block-rows: the tile pass puts them on the grid's y axis)
+        while (br1 < BR && br1 - br0 < 65535 && es[br1 + 1] - es[br0] <= limit) ++br1;
         chunks.emplace_back(br0, br1);
         most = std::max(most, es[br1] - es[br0]);
         br0 = br1;
