@@ -221,43 +221,69 @@ __global__ void __launch_bounds__(128) k_b4_dx(LayerView L, B4View V, const floa
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t br = (int64_t)blockIdx.x * 4 + warp;
     const int b = blockIdx.y * 32 + lane;
-    if (br >= V.BR || b >= B) return;
+    if (br >= V.BR) return;
+    const bool bok = b < B;
     const int nt = V.nt[br];
     if (nt == 0) return;
+    // each slot's weight code and scale S are the same for every sample:
+    // lane l computes them for slot l & 15 of one of two tiles (l >> 4) and
+    // the sample lanes fetch them by shuffle
+    const int q = lane & 15, qli = q & 3, qlj = q >> 2;
+    const int64_t es = V.es[br];
     float d[4];
 #pragma unroll
     for (int li = 0; li < 4; ++li) {
         const int64_t row = br * 4 + li;
-        d[li] = row < L.n_in ? dx[(int64_t)b * L.n_in + row] : 0.0f;
+        d[li] = (bok && row < L.n_in) ? dx[(int64_t)b * L.n_in + row] : 0.0f;
     }
-    for (int e = 0; e < nt; ++e) {
-        const int64_t ti = V.es[br] + e;
-        const uint4 tw = V.tile[ti];
-        const int64_t col0 = (int64_t)V.bc[ti] * 4;
-        const bool full = col0 + 4 <= L.n_out;
-        float dyv[4];
+    for (int e = 0; e < nt; e += 2) {
+        float qv = 0.0f, sv = 0.0f;
+        {
+            const int eu = e + (lane >> 4);
+            if (eu < nt) {
+                const int64_t tu = es + eu;
+                const int64_t row = br * 4 + qli, col = (int64_t)V.bc[tu] * 4 + qlj;
+                if (row < L.n_in && col < L.n_out) {
+                    qv = fp4_decode(tile_byte(V.tile[tu], q) & 0xFu);
+                    sv = scale_of(L, row, col);
+                }
+            }
+        }
 #pragma unroll
-        for (int lj = 0; lj < 4; ++lj) dyv[lj] = col0 + lj < L.n_out ? dyT[(col0 + lj) * B + b] : 0.0f;
+        for (int u = 0; u < 2; ++u) {
+            if (e + u >= nt) break;
+            const int64_t ti = es + e + u;
+            const int64_t col0 = (int64_t)V.bc[ti] * 4;
+            const bool full = col0 + 4 <= L.n_out;
+            const int src = u << 4;
+            float dyv[4];
 #pragma unroll
-        for (int li = 0; li < 4; ++li) {
-            const int64_t row = br * 4 + li;
-            if (row >= L.n_in) continue;
-            if (full) {
-                float p[4];
+            for (int lj = 0; lj < 4; ++lj) dyv[lj] = (bok && col0 + lj < L.n_out) ? dyT[(col0 + lj) * B + b] : 0.0f;
 #pragma unroll
-                for (int lj = 0; lj < 4; ++lj)
-                    p[lj] = __fmul_rn(fp4_decode(tile_byte(tw, lj * 4 + li) & 0xFu),
-                                      __fmul_rn(scale_of(L, row, col0 + lj), dyv[lj]));
-                d[li] = __fadd_rn(d[li], __fadd_rn(__fadd_rn(p[0], p[1]), __fadd_rn(p[2], p[3])));
-            } else {
-                for (int lj = 0; lj < 4; ++lj) {
-                    if (col0 + lj >= L.n_out) continue;
-                    d[li] = __fmaf_rn(fp4_decode(tile_byte(tw, lj * 4 + li) & 0xFu),
-                                      __fmul_rn(scale_of(L, row, col0 + lj), dyv[lj]), d[li]);
+            for (int li = 0; li < 4; ++li) {
+                const int64_t row = br * 4 + li;
+                if (row >= L.n_in) continue;
+                if (full) {
+                    float p[4];
+#pragma unroll
+                    for (int lj = 0; lj < 4; ++lj) {
+                        const float qq = __shfl_sync(0xffffffffu, qv, src | (lj * 4 + li));
+                        const float ss = __shfl_sync(0xffffffffu, sv, src | (lj * 4 + li));
+                        p[lj] = __fmul_rn(qq, __fmul_rn(ss, dyv[lj]));
+                    }
+                    d[li] = __fadd_rn(d[li], __fadd_rn(__fadd_rn(p[0], p[1]), __fadd_rn(p[2], p[3])));
+                } else {
+                    for (int lj = 0; lj < 4; ++lj) {
+                        if (col0 + lj >= L.n_out) continue;
+                        const float qq = __shfl_sync(0xffffffffu, qv, src | (lj * 4 + li));
+                        const float ss = __shfl_sync(0xffffffffu, sv, src | (lj * 4 + li));
+                        d[li] = __fmaf_rn(qq, __fmul_rn(ss, dyv[lj]), d[li]);
+                    }
                 }
             }
         }
     }
+    if (!bok) return;
 #pragma unroll
     for (int li = 0; li < 4; ++li) {
         const int64_t row = br * 4 + li;
