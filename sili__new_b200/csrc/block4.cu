@@ -673,7 +673,8 @@ __global__ void __launch_bounds__(128) k_b4_update(LayerView L, B4View V, const 
 // Same values, same order of every sum as k_b4_update, with all tiles of
 // the layer's block-rows in flight instead of one half-warp per block-row.
 constexpr int kB4Group = 64;   // tiles per block of k_b4_update_tiles
-template <int RANK, bool STOCH>
+// OST: the output scale trains (per-slot column sums are kept)
+template <int RANK, bool STOCH, bool OST>
 __global__ void __launch_bounds__(128) k_b4_update_tiles(LayerView L, B4View V, const float* __restrict__ xT,
                                                          const float* __restrict__ dyT, int B, UpdateParams P,
                                                          int64_t br0, int64_t part_base, float* __restrict__ hsb,
@@ -747,8 +748,10 @@ __global__ void __launch_bounds__(128) k_b4_update_tiles(LayerView L, B4View V, 
                 const float hc = __fadd_rn(ac, __shfl_xor_sync(hmask, ac, 4));
                 mrow[k] = __dadd_rn(mrow[k], (double)hg);
                 mrowc[k] = __dadd_rn(mrowc[k], (double)hc);
-                mcol[k] = __fmaf_rn(__fmul_rn(qf, vsk[k]), g, mcol[k]);
-                mcolc[k] = __fmaf_rn(__fmul_rn(qf, vsk[k]), cb, mcolc[k]);
+                if (OST) {
+                    mcol[k] = __fmaf_rn(__fmul_rn(qf, vsk[k]), g, mcol[k]);
+                    mcolc[k] = __fmaf_rn(__fmul_rn(qf, vsk[k]), cb, mcolc[k]);
+                }
             }
             const float p = __fmul_rn(quant, sdy);
             const float a = __fadd_rn(p, __shfl_xor_sync(hmask, p, 4));
@@ -762,7 +765,7 @@ __global__ void __launch_bounds__(128) k_b4_update_tiles(LayerView L, B4View V, 
                 mrb[((loc * 4 + li) * RANK + k) * 2 + 1] = mrowc[k];
             }
         }
-        if (P.os_trainable) {   // the slot's column sums, added in order by k_b4_col_sums
+        if (OST) {   // the slot's column sums, added in order by k_b4_col_sums
 #pragma unroll
             for (int k = 0; k < RANK; ++k) {
                 mcb[((loc * 16 + s) * RANK + k) * 2] = act ? mcol[k] : 0.0f;
@@ -896,8 +899,13 @@ void launch_b4_update_split(const LayerView& L, const B4View& V, const float* xT
     if (br1 <= br0 || B == 0) return;
     const unsigned nbr = (unsigned)(br1 - br0);
     const dim3 tg((unsigned)((V.BC + kB4Group - 1) / kB4Group), nbr);   // a row holds at most BC tiles
-#define SILI_B4S(R, ST) \
-    k_b4_update_tiles<R, ST><<<tg, 128, 0, s>>>(L, V, xT, dyT, B, P, br0, part_base, hsb, mrb, mcb)
+#define SILI_B4S(R, ST)                                                                                     \
+    do {                                                                                                   \
+        if (P.os_trainable)                                                                                \
+            k_b4_update_tiles<R, ST, true><<<tg, 128, 0, s>>>(L, V, xT, dyT, B, P, br0, part_base, hsb, mrb, mcb); \
+        else                                                                                               \
+            k_b4_update_tiles<R, ST, false><<<tg, 128, 0, s>>>(L, V, xT, dyT, B, P, br0, part_base, hsb, mrb, mcb); \
+    } while (0)
     switch (L.rank * 2 + (P.stochastic ? 1 : 0)) {
         case 2: SILI_B4S(1, false); break;
         case 3: SILI_B4S(1, true); break;
