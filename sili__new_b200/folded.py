@@ -212,7 +212,10 @@ class FoldedStack:
 
     # ── device path: forward_dense_ptr + fold sum + NCCL all-gather ──
     def forward_device(self, name: str, x, stream):
-        """x: torch CUDA tensor [B, in_dim] on `stream`; returns [B, out_dim]."""
+        """x: torch CUDA tensor [B, in_dim] on `stream`; returns [B, out_dim].
+        The caller makes x ready on `stream` (and keeps it alive until the
+        stream has used it): create it under ``torch.cuda.stream(stream)``
+        or make `stream` wait for the stream that wrote it."""
         import torch
         from . import _cuda
         p = self.parts[name]
@@ -243,7 +246,8 @@ class FoldedStack:
     def backward_device(self, name: str, dy, lr: float, stream, lr_per_row_nnz: bool = True,
                         damp_by_importance: bool = True, beta2: float = 0.999, eps: float = 1e-8):
         """dy: torch CUDA tensor [B, out_dim] on `stream` (the gradient of the
-        last forward_device output); returns dx [B, in_dim] (a buffer reused
+        last forward_device output, ready on `stream` as forward_device's x
+        must be); returns dx [B, in_dim] (a buffer reused
         by the next call) and updates the rank's synapses and row scales:
         fold-broadcast kernel, fused update as a column shard, NCCL
         all-reduces of dx and of the row parts, then the row steps."""

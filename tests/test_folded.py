@@ -97,11 +97,12 @@ def test_device_path_matches_host_path():
     st = _stack(0, 1, lambda a, b, c: S.SparseLinearLayerDeterministic(a, b, c))
     x = _x()
     stream = torch.cuda.Stream()
-    xd = torch.from_numpy(x).cuda()
-    for name in SUFFIXES:
-        yd = st.forward_device(name, xd, stream)
-        stream.synchronize()
-        assert np.array_equal(yd.cpu().numpy(), st.forward_host(name, x)), name
+    # device tensors made, read and freed on the stream the stack runs on
+    with torch.cuda.stream(stream):
+        xd = torch.from_numpy(x).cuda()
+        for name in SUFFIXES:
+            yd = st.forward_device(name, xd, stream).cpu().numpy()
+            assert np.array_equal(yd, st.forward_host(name, x)), name
 
 
 # ── training: column-shard backward ─────────────────────────────────────────
@@ -282,11 +283,11 @@ def test_device_backward_matches_host_backward():
     for step in range(2):
         x, dy = _train_data(step)
         host.forward_host("a", x)
-        dev.forward_device("a", torch.from_numpy(x).cuda(), stream)
         dxh = host.backward_host("a", dy, LR)
-        dxd = dev.backward_device("a", torch.from_numpy(dy).cuda(), LR, stream)
-        stream.synchronize()
-        assert np.array_equal(dxd.cpu().numpy(), dxh), f"step {step}"
+        with torch.cuda.stream(stream):   # inputs made and freed on the stack's stream
+            dev.forward_device("a", torch.from_numpy(x).cuda(), stream)
+            dxd = dev.backward_device("a", torch.from_numpy(dy).cuda(), LR, stream).cpu().numpy()
+        assert np.array_equal(dxd, dxh), f"step {step}"
     sh, sd = _layer_state(host.parts["a"].layer, TRAIN["a"][0]), _layer_state(dev.parts["a"].layer, TRAIN["a"][0])
     for k in sh:
         assert np.array_equal(sh[k], sd[k]), k
@@ -308,10 +309,11 @@ def _nccl_rank_main(rank, world, port, out):
     st.load("a", lp, li, lw, len(li), 0.01)
     stream = torch.cuda.Stream()
     dxs = []
-    for step in range(2):
-        x, dy = _train_data(step)
-        st.forward_device("a", torch.from_numpy(x).cuda(), stream)
-        dxs.append(st.backward_device("a", torch.from_numpy(dy).cuda(), LR, stream).cpu().numpy().copy())
+    with torch.cuda.stream(stream):   # inputs made and freed on the stack's stream
+        for step in range(2):
+            x, dy = _train_data(step)
+            st.forward_device("a", torch.from_numpy(x).cuda(), stream)
+            dxs.append(st.backward_device("a", torch.from_numpy(dy).cuda(), LR, stream).cpu().numpy().copy())
     stream.synchronize()
     state = _layer_state(st.parts["a"].layer, TRAIN["a"][0])
     np.savez(out + f".{rank}.npz", dx=np.stack(dxs), **state)
@@ -348,17 +350,19 @@ def test_folded_state_dict_round_trip():
     b.load("a", p, i, w, len(i), 0.01)
     stream = torch.cuda.Stream()
     x, dy = _train_data(0)
-    a.forward_device("a", torch.from_numpy(x).cuda(), stream)
-    a.backward_device("a", torch.from_numpy(dy).cuda(), LR, stream)
+    with torch.cuda.stream(stream):   # inputs made and freed on the stacks' stream
+        a.forward_device("a", torch.from_numpy(x).cuda(), stream)
+        a.backward_device("a", torch.from_numpy(dy).cuda(), LR, stream)
     stream.synchronize()
     b.load_state_dict(a.state_dict())
     for step in (1, 2):
         x, dy = _train_data(step)
         outs = []
-        for st in (a, b):
-            y = st.forward_device("a", torch.from_numpy(x).cuda(), stream).clone()
-            dx = st.backward_device("a", torch.from_numpy(dy).cuda(), LR, stream).clone()
-            outs.append((y, dx))
+        with torch.cuda.stream(stream):
+            for st in (a, b):
+                y = st.forward_device("a", torch.from_numpy(x).cuda(), stream).clone()
+                dx = st.backward_device("a", torch.from_numpy(dy).cuda(), LR, stream).clone()
+                outs.append((y, dx))
         stream.synchronize()
         assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1]), step
     assert np.array_equal(a.parts["a"].layer.save_state(), b.parts["a"].layer.save_state())

@@ -133,7 +133,7 @@ def test_forward_vs_oracle(S, B):
         assert_close_sum(yg, yo, 1e-5)
 
 
-@pytest.mark.parametrize("n_in,n_out,B", [(700, 40000, 32), (1100, 20000, 64), (1300, 80000, 36),
+@pytest.mark.parametrize("n_in,n_out,B", [(700, 40000, 32), (1100, 20000, 64), (1300, 80000, 36), (1100, 160000, 32),
                                           (520, 20000, 100)])
 def test_forward_row_tiles_vs_oracle(S, n_in, n_out, B):
     """Shapes wide enough for the forward that stages x rows in shared memory
