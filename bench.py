@@ -592,6 +592,7 @@ def run_folded(args, dev, rank, world, dist, S, torch, which="config5"):
     gen.manual_seed(7)
     xs = {name: torch.randn(B, in_dim, generator=gen, device=f"cuda:{dev}") for name, (in_dim, _) in suffixes.items()}
     stream = torch.cuda.Stream(device=dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))   # the inputs are written on the current stream
 
     def decode_step():
         outs = []
@@ -650,6 +651,7 @@ def folded_train_leg(args, dev, dist, S, torch, stack, suffixes, xs, stream, B):
     gen.manual_seed(11)
     dys = {name: torch.randn(B, out_dim, generator=gen, device=f"cuda:{dev}")
            for name, (_, out_dim) in suffixes.items()}
+    stream.wait_stream(torch.cuda.current_stream(dev))   # written on the current stream
 
     def train_step():
         for name in suffixes:
