@@ -61,6 +61,12 @@ int sili_kernel_launches(int64_t* count);
  * kernels' durations in milliseconds (synchronising the layer's stream). */
 int sili_layer_set_kernel_timing(sili_layer* h, int enable);
 int sili_layer_kernel_ms(sili_layer* h, float* forward_ms, float* backward_ms);
+/* Measurement utility, no counterpart in the reference: the device's FP32
+ * FMA throughput (16 independent fma chains per thread, every SM full, best
+ * of 4 timed launches of `iters` iterations), the denominator of the FP32
+ * fraction reported for the issue-bound kernels.  ms (may be NULL) gets the
+ * best launch's duration. */
+int sili_fp32_fma_peak(int device, int iters, double* tflops, double* ms);
 
 /* ── lifetime / loading ──────────────────────────────────────────────────── */
 /* SparseLinearLayerImpl(n_inputs, n_outputs, max_weights, num_cpus),
@@ -106,7 +112,13 @@ int sili_layer_forward_dense(sili_layer* h, const float* x, int batch, float* y,
  * floats (4 MiB), so batch * (n_in + 1) above that is rejected with
  * SILI_EINVAL.  The column index
  * must be current (one forward_dense after load_weights or a structural
- * change), else SILI_EINVAL.  Does not keep x for backward_dense.  The first
+ * change), else SILI_EINVAL; so must the block4 tile index when the layer
+ * holds block4 tiles (their part is added as forward_dense adds it).  The
+ * scattered part always runs the per-synapse gather kernels, never the
+ * row-tiled one forward_dense picks for wide rank-1 layers (its packed
+ * column index is a rebuildable buffer), so on wide layers this entry point
+ * is slower than forward_dense; results are equal.  Does not keep x for
+ * backward_dense.  The first
  * call on a device looks up the scratch address (cudaGetSymbolAddress); make
  * it before work that must see only launches.  Calls on one device share the
  * scratch: overlapping calls race, so order them (one stream). */

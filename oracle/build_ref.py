@@ -23,7 +23,8 @@ What it builds (outputs go to ``oracle/_ref/`` only, which git ignores):
   reference's internal delta-CSR state (ULEB128 bytes, FP4 value bytes,
   per-row offsets) through a small C ABI, which the pybind module does not.
 
-Run: ``python oracle/build_ref.py [--variant native|x86-64-v3|all]``.
+Run: ``python oracle/build_ref.py --reference <checkout> [--variant native|x86-64-v3|all]``
+(or set ``SILI_REFERENCE_DIR``).
 Does nothing (and says so) when the reference sources are absent, which is
 the case on the GPU box: there the prebuilt files travel with the repo.
 """
@@ -40,7 +41,10 @@ import tempfile
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "_ref")
-REFERENCE_DIR = os.environ.get("SILI_REFERENCE_DIR", "/root/reference")
+# The reference checkout to build from: the SILI_REFERENCE_DIR environment
+# variable or --reference; there is no default, and without either nothing
+# is built (the prebuilt files under _ref/ are used as they are).
+REFERENCE_DIR = os.environ.get("SILI_REFERENCE_DIR", "")
 
 # setup.py:41-60 of the reference (minus -march, chosen per variant).
 REF_FLAGS = ["-O3", "-std=c++20", "-shared", "-fPIC", "-fopenmp",
@@ -58,7 +62,7 @@ _ISA_FLAGS = ("sse4_2", "avx", "avx2", "fma", "bmi1", "bmi2", "f16c", "movbe",
 
 
 def reference_present() -> bool:
-    return os.path.isfile(os.path.join(REFERENCE_DIR, "sili", "cpu_backend.cpp"))
+    return bool(REFERENCE_DIR) and os.path.isfile(os.path.join(REFERENCE_DIR, "sili", "cpu_backend.cpp"))
 
 
 def _pybind_includes() -> list[str]:
@@ -113,7 +117,11 @@ def build_variant(variant: str) -> None:
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--variant", default="all", choices=["all"] + list(VARIANTS))
+    ap.add_argument("--reference", default=None, help="reference checkout (else $SILI_REFERENCE_DIR)")
     args = ap.parse_args(argv)
+    global REFERENCE_DIR
+    if args.reference:
+        REFERENCE_DIR = args.reference
     if not reference_present():
         print("oracle/build_ref.py: reference sources not present; using prebuilt oracle/_ref")
         return 0

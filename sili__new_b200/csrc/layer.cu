@@ -1020,6 +1020,11 @@ SynView synap_view(sili_layer* h) {
 }
 
 // ═══════════════════════════════════════════════════════════════════════════
+// the error slot sili_last_error reads, for the library's other files
+namespace sili {
+int set_error(int code, const std::string& msg) { return fail(code, msg); }
+}
+
 extern "C" {
 
 const char* sili_last_error(void) { return g_err.c_str(); }
@@ -2642,12 +2647,18 @@ extern "C" int sili_layer_forward_dense_static(sili_layer* h, const float* x, in
     if (h->aux_dirty)
         return fail(SILI_EINVAL, "forward_dense_static: the column index is stale (load_weights or a structural "
                                  "change since the last forward_dense); call forward_dense once to rebuild it");
+    // block4 tiles add their part through the tile column index, which only
+    // forward_dense (re)builds: a stale one would need an allocation
+    if (h->b4_ntiles > 0 && h->b4_dirty)
+        return fail(SILI_EINVAL, "forward_dense_static: the block4 tile index is stale (tiles changed since the "
+                                 "last forward_dense); call forward_dense once to rebuild it");
     float* xT = nullptr;
     RC(static_fwd_scratch(h->dev, &xT));
     cudaStream_t s = pick(h, stream);
     launch_transpose(x, xT, batch, n_in, s);
     CK(cudaMemsetAsync(xT + (int64_t)batch * n_in, 0, (size_t)batch * sizeof(float), s));   // zero row
     launch_forward(h->view(), xT, batch, y, false, s);
+    if (h->b4_ntiles > 0) launch_b4_forward(h->view(), h->b4view(), xT, batch, y, s);
     CK(cudaGetLastError());
     return SILI_OK;
 }

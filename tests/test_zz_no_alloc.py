@@ -24,6 +24,7 @@ def _lib():
         getattr(lib, name).argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]
     lib.sili_layer_create.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_void_p)]
     lib.sili_layer_load_weights.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]
+    lib.sili_layer_load_dense_codes.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p]
     lib.sili_layer_set_scale.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_float]
     lib.sili_layer_destroy.argtypes = [C.c_void_p]
     lib.sili_layer_sync.argtypes = [C.c_void_p]
@@ -34,10 +35,19 @@ def _ok(lib, rc):
     assert rc == 0, lib.sili_last_error().decode()
 
 
-def _make(lib, n_in, n_out, per_row, seed):
+def _make(lib, n_in, n_out, per_row, seed, block4_density=0.0):
     p, i, w, vs = random_layer(n_in, n_out, per_row, seed=seed)
     h = C.c_void_p()
-    _ok(lib, lib.sili_layer_create(n_in, n_out, len(i) * 2, 0, 1, C.byref(h)))
+    _ok(lib, lib.sili_layer_create(n_in, n_out, len(i) * 2 + n_in * n_out, 0, 1, C.byref(h)))
+    if block4_density > 0:
+        # block4 tiles beside the scattered synapses (load_dense_codes first,
+        # as the reference's callers do)
+        rng = np.random.default_rng(seed + 7)
+        mask = rng.random((n_in, n_out)) < block4_density
+        wc = np.where(mask, rng.integers(1, 16, (n_in, n_out)), 0).astype(np.uint8)
+        wc[wc == 8] = 1
+        ic = np.zeros((n_in, n_out), np.uint8)
+        _ok(lib, lib.sili_layer_load_dense_codes(h, wc.ctypes.data, ic.ctypes.data))
     _ok(lib, lib.sili_layer_load_weights(h, p.ctypes.data, i.ctypes.data, w.ctypes.data, len(i)))
     for r in range(n_in):
         _ok(lib, lib.sili_layer_set_scale(h, 0, r, 0, float(vs[r])))  # SILI_SCALE_VALUE
@@ -45,10 +55,11 @@ def _make(lib, n_in, n_out, per_row, seed):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("n_in,n_out,batch", [(1024, 768, 64), (8191, 4096, 128), (300, 500, 5)])
-def test_static_forward_matches_forward_dense(n_in, n_out, batch):
+@pytest.mark.parametrize("n_in,n_out,batch,b4", [(1024, 768, 64, 0.0), (8191, 4096, 128, 0.0), (300, 500, 5, 0.0),
+                                                 (256, 512, 64, 0.05), (130, 98, 7, 0.2)])
+def test_static_forward_matches_forward_dense(n_in, n_out, batch, b4):
     lib = _lib()
-    h = _make(lib, n_in, n_out, 41, seed=n_in)
+    h = _make(lib, n_in, n_out, 41, seed=n_in, block4_density=b4)
     try:
         rng = np.random.default_rng(batch)
         stream = torch.cuda.Stream()
@@ -56,6 +67,7 @@ def test_static_forward_matches_forward_dense(n_in, n_out, batch):
         # the regular entry point once: it also builds the column index
         warm = torch.from_numpy(relu_sparse_x(rng, batch, n_in)).cuda()
         y_ref = torch.empty(batch, n_out, device="cuda")
+        stream.wait_stream(torch.cuda.current_stream())
         _ok(lib, lib.sili_layer_forward_dense(h, warm.data_ptr(), batch, y_ref.data_ptr(), sh))
         # two consecutive calls on different inputs: the second must not see
         # anything the first left in the shared scratch
@@ -63,6 +75,9 @@ def test_static_forward_matches_forward_dense(n_in, n_out, batch):
             x = torch.from_numpy(relu_sparse_x(rng, batch, n_in)).cuda()
             y_static = torch.full((batch, n_out), float("nan"), device="cuda")
             y_ref = torch.empty(batch, n_out, device="cuda")
+            # x and the NaN fill were written on torch's current stream: the
+            # layer's calls on `stream` must come after them
+            stream.wait_stream(torch.cuda.current_stream())
             _ok(lib, lib.sili_layer_forward_dense_static(h, x.data_ptr(), batch, y_static.data_ptr(), sh))
             _ok(lib, lib.sili_layer_forward_dense(h, x.data_ptr(), batch, y_ref.data_ptr(), sh))
             stream.synchronize()
