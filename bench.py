@@ -143,6 +143,13 @@ def peaks():
 BWD_KERNEL = "k_backward_update_tiled"
 
 
+def update_flops(nnz):
+    """Algorithmic FP32 operations of one fused update at config 2: 25 per
+    (synapse, sample) pair -- the recurrence's arithmetic and the dx fma --
+    for every pair (the square root and the division are not counted)."""
+    return nnz * BATCH * 25.0
+
+
 def kernel_profile():
     """The committed ncu summary of the backward update kernel
     (profiles/<kernel>_config2.json, from one ncu capture), or {}."""
@@ -701,6 +708,7 @@ def main():
                     help="skip the sparse-variant, reference-rule and SpMV measurements")
     ap.add_argument("--only", choices=["block4", "synap", "folded", "folded4", "rule", "spmv", "sparse"],
                     help="run one secondary measurement alone and print its object (profiling)")
+    ap.add_argument("--detail", default=None, help="write every measurement's full object to this JSON file")
     ap.add_argument("--folded-layers", type=int, default=None,
                     help="layers folded per suffix (default: config 5's 40; fewer for small profiling runs)")
     args = ap.parse_args()
@@ -833,6 +841,8 @@ def main():
         L.set_kernel_timing(False)
     fwd_ms, bwd_ms = float(np.mean(fw)), float(np.mean(bw))
     hbm_peak, peak_kind = peaks()
+    # the FP32 FMA peak, measured now on this GPU (the update is issue-bound)
+    fp32_peak = float(S._cuda.fp32_fma_peak(dev)[0])
     # dominant kernel: the fused backward/update
     bwd_kernel_bytes = bwd_b
     achieved = bwd_kernel_bytes / (bwd_ms * 1e-3) / 1e9
@@ -915,38 +925,90 @@ def main():
         dist.destroy_process_group()
     if rank != 0:
         return 0
+    detail = {"block4": block4, "synaptogenesis": synap, "synaptogenesis_reference_rule": rule,
+              "sparse_variants": sparse_v, "spmv": spmv, "folded_stack": folded, "folded_prefill": folded4,
+              "issue": issue}
+    if args.detail:
+        with open(args.detail, "w") as f:
+            json.dump(detail, f, indent=1)
+    fp32 = None
+    if fp32_peak:
+        fl = update_flops(len(i))
+        fp32 = {"achieved_tflops": fl / (bwd_ms * 1e-3) / 1e12, "peak_tflops": fp32_peak,
+                "frac": fl / (bwd_ms * 1e-3) / 1e12 / fp32_peak}
     line = {
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": per_step_ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "fp32 activations, FP4 (E2M1-with-NaN) weights",
-        "data": "synthetic",
-        "config": {"workload": "config2: 8192x8192, 95% sparse (410/row), batch 64, forward_dense + "
-                               "backward_dense(lr=0.01, lr_per_row_nnz) on FP4 delta-CSR",
-                   "layers_rotated": args.layers, "l2": "inputs larger than L2 (16 layer copies rotated)",
-                   "parallelism": f"replicas x{world}", "bytes_per_step": step_bytes,
-                   "forward_kernel_ms": fwd_ms, "backward_kernel_ms": bwd_ms},
-        "roofline": {"bound": "hbm", "kernel": BWD_KERNEL, "achieved": achieved, "peak": hbm_peak,
-                     "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / hbm_peak,
-                     "traffic": prof.get("dram_bytes_per_launch"), "algorithmic_bytes_per_launch": bwd_kernel_bytes,
-                     # the kernel is issue-bound (a sequential per-sample recurrence per synapse):
-                     # warp instructions per launch (ncu) / the bench's kernel time, against
-                     # 148 SMs x 4 schedulers x 1 warp instruction per cycle at the sampled clock
-                     "issue": issue},
+        "vs_baseline": None, "dtype": "fp32 act, FP4 weights", "data": "synthetic",
+        "config": {"workload": "config2 8192^2 95% B64 fwd+bwd(lr .01) FP4 delta-CSR",
+                   "l2": f"inputs > L2 ({args.layers} layer copies rotated)", "parallelism": f"replicas x{world}",
+                   "bytes_per_step": step_bytes, "fwd_kernel_ms": _r(fwd_ms), "bwd_kernel_ms": _r(bwd_ms)},
+        "roofline": {"bound": "hbm", "kernel": BWD_KERNEL, "achieved": _r(achieved), "peak": hbm_peak,
+                     "unit": "GB/s", "frac": _r(achieved / hbm_peak, 5), "traffic": prof.get("dram_bytes_per_launch"),
+                     "peak_kind": peak_kind, "fp32": _rd(fp32),
+                     "issue_frac": _r(issue["frac"]) if issue else None},
         "cpu_baseline": cpu,
-        "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": BATCH * (N_IN + N_OUT) * 4,
+        "e2e": {"value": _r(e2e_value), "unit": "GB/s", "h2d_bytes_per_step": BATCH * (N_IN + N_OUT) * 4,
                 "d2h_bytes_per_step": BATCH * (N_IN + N_OUT) * 4},
         "gpu_launches": launches,
         "clocks": clk,
-        "block4": block4,
-        "synaptogenesis": synap,
-        "synaptogenesis_reference_rule": rule,
-        "sparse_variants": sparse_v,
-        "spmv": spmv,
-        "folded_stack": folded,
-        "folded_prefill": folded4,
+        "folded_decode": _leg_folded(folded),
+        "legs": compact_legs(block4, synap, rule, sparse_v, spmv, folded4),
     }
-    print(json.dumps(line))
+    print(json.dumps(line, separators=(",", ":")))
     return 0
+
+
+def _r(v, nd=4):
+    """Round for the one-line summary (None passes through)."""
+    if v is None:
+        return None
+    return float(f"{v:.{nd}g}")
+
+
+def _rd(d):
+    return {k: (_r(v) if isinstance(v, float) else v) for k, v in d.items()} if d else d
+
+
+def _cpu_short(o):
+    c = (o or {}).get("cpu_baseline")
+    return {"v": _r(c["value"]), "u": c["unit"], "cores": c["cores"], "kind": c["kind"]} if c else None
+
+
+def _leg_folded(f):
+    if not f:
+        return None
+    out = {"tok_s": _r(f["value"]), "ms": _r(f["ms_per_step"]), "n_gpus": f["n_gpus"], "tflops": _r(f["fp32_tflops"])}
+    if f.get("train"):
+        out["train_tok_s"] = _r(f["train"]["value"])
+    if f.get("parts_ms"):
+        out["parts_ms"] = {k: _r(v, 3) for k, v in f["parts_ms"].items()}
+    return out
+
+
+def compact_legs(block4, synap, rule, sparse_v, spmv, folded4):
+    """The secondary measurements, numbers only, so the whole line stays short
+    (the full objects go to --detail)."""
+    legs = {}
+    if block4:
+        legs["block4"] = {"ms": _r(block4["ms_per_step"]), "gbs": _r(block4["value"]), "cpu": _cpu_short(block4)}
+        for k in ("fwd_ms", "fwd_tc_ms"):
+            if block4.get(k) is not None:
+                legs["block4"][k] = _r(block4[k])
+    if synap:
+        legs["synap_topk"] = {"ms": _r(synap["value"]), "cpu": _cpu_short(synap)}
+    if rule:
+        legs["synap_rule"] = {"ms": _r(rule["value"]), "probes_ms": _r(rule["build_probes_ms"]),
+                              "sweep_ms": _r(rule["sweep_ms"]), "cpu": _cpu_short(rule)}
+    if sparse_v:
+        legs["sparse"] = {"fwd_ms": _r(sparse_v["forward_sparse_ms"]), "bwd_ms": _r(sparse_v["backward_sparse_ms"]),
+                          "cpu": _cpu_short(sparse_v)}
+    if spmv:
+        legs["spmv"] = {"us": _r(spmv["value"]), "eager_us": _r(spmv["eager_us"]), "cpu": _cpu_short(spmv)}
+    if folded4:
+        legs["prefill"] = {"tok_s": _r(folded4["value"]), "ms": _r(folded4["ms_per_step"]),
+                           "tflops": _r(folded4["fp32_tflops"])}
+    return legs
 
 
 def _uleb_bytes(work):

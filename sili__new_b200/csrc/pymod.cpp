@@ -582,6 +582,11 @@ PYBIND11_MODULE(_cuda, m) {
     }, py::arg("dy"), py::arg("batch"), py::arg("out_dim"), py::arg("j0"), py::arg("width"), py::arg("n_folds"),
        py::arg("raw"), py::arg("stream") = 0);
     m.def("kernel_launches", []() { int64_t n = 0; sili_kernel_launches(&n); return n; });
+    m.def("fp32_fma_peak", [](int device, int iters) {
+        double tf = 0, ms = 0;
+        check(sili_fp32_fma_peak(device, iters, &tf, &ms));
+        return py::make_tuple(tf, ms);
+    }, py::arg("device") = 0, py::arg("iters") = 4096);
     m.def("dense_to_csr", [](farr x, float thr) {
         auto b = x.request();
         const int rows = b.ndim == 2 ? (int)b.shape[0] : 1;
