@@ -114,6 +114,8 @@ def lib():
             ("o_top_k_csr", _I64, [_P, _I, _I, _I64, _P, _P, _P]),
             ("o_topk_dyx_candidates", _I64, [_P, _P, _P, _I, _I64, _P, _P, _P]),
             ("o_topk_dyx_step", _I, [_P, _P, _P, _I, _I64]),
+            ("o_topk_apply", _I, [_P, _P, _P, _P, _I64]),
+            ("o_dyx_scores_at", None, [_P, _P, _I, _I64, _I64, _P, _P, _I64, _P]),
             ("o_load_dense_codes", _I, [_P, _P, _P]),
             ("o_b4_expand_headroom", _I, [_P, _F, _I64]),
             ("o_b4_equalize_step", _I, [_P, _I64]),
@@ -536,8 +538,40 @@ class OracleLayer(_LayerBase):
         if self.L.o_topk_dyx_step(self.h, _ptr(x), _ptr(dy), x.shape[0], k):
             raise MemoryError("topk_dyx_step: budget exceeded")
 
+    def topk_apply(self, rows, cols, scores):
+        """The rule's prune + add + rebuild for a given candidate list."""
+        r = np.ascontiguousarray(rows, np.int32); c = np.ascontiguousarray(cols, np.int32)
+        s = np.ascontiguousarray(scores, np.float32)
+        if self.L.o_topk_apply(self.h, _ptr(r), _ptr(c), _ptr(s), len(r)):
+            raise MemoryError("topk_apply: budget exceeded")
+
+
+def dyx_scores_at(x, dy, rows, cols):
+    """|sum_b x[b,r] dy[b,c]| by the top-k rule's ascending-b fma chain."""
+    x = np.ascontiguousarray(x, np.float32); dy = np.ascontiguousarray(dy, np.float32)
+    r = np.ascontiguousarray(rows, np.int32); c = np.ascontiguousarray(cols, np.int32)
+    out = np.zeros(len(r), np.float32)
+    lib().o_dyx_scores_at(_ptr(x), _ptr(dy), x.shape[0], x.shape[1], dy.shape[1], _ptr(r), _ptr(c), len(r), _ptr(out))
+    return out
+
 
 # ── the reference itself, through oracle/ref_shim.cpp ───────────────────────
+def host_variant() -> str:
+    """The reference build this host can run: "native" when it has every ISA
+    extension the native build was compiled for (cpu_flags.txt), else
+    "x86-64-v3"."""
+    try:
+        need = set(open(os.path.join(HERE, "_ref", "native", "cpu_flags.txt")).read().split())
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("flags"):
+                if need and need <= set(line.split(":", 1)[1].split()):
+                    return "native"
+                break
+    except OSError:
+        pass
+    return "x86-64-v3"
+
+
 def ref_available(variant: str = "native") -> bool:
     return os.path.exists(os.path.join(HERE, "_ref", variant, "libref_shim.so"))
 

@@ -1278,18 +1278,38 @@ static int cmp_ex(const void* a, const void* b) {
     return (x->c > y->c) - (x->c < y->c);
 }
 int o_topk_dyx_step(OLayer* L, const float* x, const float* dy, int batch, int64_t k) {
-    const int64_t nnz = L->total_nnz;
     if (o_b4_ntiles(L) > 0) return O_EINVAL;   /* defined on the scattered store */
     int* cr = (int*)malloc((size_t)(k + 1) * sizeof(int));
     int* cc = (int*)malloc((size_t)(k + 1) * sizeof(int));
     float* cs = (float*)malloc((size_t)(k + 1) * sizeof(float));
     const int64_t nc = o_topk_dyx_candidates(L, x, dy, batch, k, cr, cc, cs);
+    const int rc = o_topk_apply(L, cr, cc, cs, nc);
+    free(cr); free(cc); free(cs);
+    return rc;
+}
+
+/* |sum_b x[b,r] * dy[b,c]| by the rule's ascending-b fma chain, at n given
+ * positions: the scores o_topk_dyx_candidates ranks, for checking a chosen
+ * set without scoring every position. */
+void o_dyx_scores_at(const float* x, const float* dy, int batch, int64_t n_in, int64_t n_out, const int* rows,
+                     const int* cols, int64_t n, float* out) {
+    for (int64_t i = 0; i < n; ++i) {
+        float s = 0.0f;
+        for (int b = 0; b < batch; ++b)
+            s = fmaf(x[(int64_t)b * n_in + rows[i]], dy[(int64_t)b * n_out + cols[i]], s);
+        out[i] = fabsf(s);
+    }
+}
+
+/* The rule's second half for a given candidate list (rows / cols ascending by
+ * (row, col), scores = their |dy^T x|): prune as many smallest |FP4(w) S|,
+ * add the candidates, rebuild (o_topk_dyx_step = candidates + this). */
+int o_topk_apply(OLayer* L, const int* cr, const int* cc, const float* cs, int64_t nc) {
+    const int64_t nnz = L->total_nnz;
+    if (o_b4_ntiles(L) > 0) return O_EINVAL;
     {   /* the rebuild's reserve requests against the hard limits, before any change */
         const int64_t nn0 = nnz - (nc < nnz ? nc : nnz) + nc;
-        if (nn0 + 64 > L->max_val_bytes || nn0 * 8 + 4096 > L->max_idx_bytes) {
-            free(cr); free(cc); free(cs);
-            return O_ENOMEM;
-        }
+        if (nn0 + 64 > L->max_val_bytes || nn0 * 8 + 4096 > L->max_idx_bytes) return O_ENOMEM;
     }
     int* p = (int*)malloc((size_t)(L->rows + 1) * sizeof(int));
     int* ix = (int*)malloc((size_t)(nnz + 1) * sizeof(int));
@@ -1329,7 +1349,7 @@ int o_topk_dyx_step(OLayer* L, const float* x, const float* dy, int batch, int64
     }
     const int rc = from_absolute(L, np_, nix, nw, nim, L->rows, L->cols,
                                  (int64_t)nn * 8 + 4096, (int64_t)nn + 64, 0.2f, L->max_idx_bytes, L->max_val_bytes);
-    free(cr); free(cc); free(cs); free(p); free(ix); free(w); free(im); free(e); free(drop);
+    free(p); free(ix); free(w); free(im); free(e); free(drop);
     free(np_); free(nix); free(nw); free(nim);
     return rc;
 }

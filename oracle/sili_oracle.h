@@ -125,6 +125,11 @@ int64_t o_top_k_csr(const float* x, int rows, int cols, int64_t k, int* ptrs, in
 int64_t o_topk_dyx_candidates(const OLayer* L, const float* x, const float* dy, int batch, int64_t k,
                               int* rows, int* cols, float* scores);
 int     o_topk_dyx_step(OLayer* L, const float* x, const float* dy, int batch, int64_t k);
+/* its second half for a given candidate list (ascending (row, col)) */
+int     o_topk_apply(OLayer* L, const int* rows, const int* cols, const float* scores, int64_t n);
+/* the rule's score at given positions */
+void    o_dyx_scores_at(const float* x, const float* dy, int batch, int64_t n_in, int64_t n_out, const int* rows,
+                        const int* cols, int64_t n, float* out);
 
 #ifdef __cplusplus
 }

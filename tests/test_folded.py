@@ -366,3 +366,63 @@ def test_folded_state_dict_round_trip():
         stream.synchronize()
         assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1]), step
     assert np.array_equal(a.parts["a"].layer.save_state(), b.parts["a"].layer.save_state())
+
+
+# ── config 5 decode, sharded over NCCL ranks ───────────────────────────────
+DECODE_FOLDS, DECODE_B = 2, 32
+
+
+def _decode_outputs(rank, world, dev):
+    """Every suffix of the config-5 shape (Mistral-Small-24B: hidden 5120,
+    FFN 32768), 2 layers folded at 5 % density, forward_device on one
+    decode batch; returns {suffix: y [B, out_dim]} (host)."""
+    import torch
+    import sili__new_b200 as S
+    from sili__new_b200 import folded as F
+    suffixes = F.mistral_suffixes(F.MISTRAL_SMALL_24B)
+    st = FoldedStack(dict(suffixes), DECODE_FOLDS, rank, world,
+                     lambda a, b, c: S.SparseLinearLayer(a, b, c, 1, dev))
+    for k, (name, (in_dim, out_dim)) in enumerate(suffixes.items()):
+        j0, j1 = column_slice(out_dim, rank, world)
+        ptrs, idx, vals, nnz = F.synthetic_shard(in_dim, out_dim, DECODE_FOLDS, 0.05, j0, j1, seed=101 + k,
+                                                 device=f"cuda:{dev}")
+        st.load(name, ptrs, idx, vals, nnz, F.SYNTHETIC_VALUE_SCALE)
+    stream = torch.cuda.Stream(device=dev)
+    out = {}
+    with torch.cuda.stream(stream):
+        for name, (in_dim, _) in suffixes.items():
+            x = torch.from_numpy(np.random.default_rng(in_dim).normal(0, 1, (DECODE_B, in_dim)).astype(np.float32))
+            out[name] = st.forward_device(name, x.cuda(dev), stream).cpu().numpy().copy()
+    stream.synchronize()
+    return out
+
+
+def _decode_rank_main(rank, world, port, out):
+    import datetime
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120))
+    res = _decode_outputs(rank, world, rank)
+    if rank == 0:
+        np.savez(out, **res)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_sharded_decode_two_nccl_ranks(tmp_path):
+    """Config 5's decode forward column-sharded over two NCCL ranks equals
+    the unsharded stack bit for bit (column sharding does not reorder any
+    sum: each output column's rows are summed in ascending order, the folds
+    in ascending order, on whichever rank holds the column)."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    out = str(tmp_path / "decode.npz")
+    mp.start_processes(_decode_rank_main, args=(2, _free_port(), out), nprocs=2, start_method="spawn")
+    got = np.load(out)
+    want = _decode_outputs(0, 1, 0)
+    for name, y in want.items():
+        assert np.array_equal(got[name], y), name
