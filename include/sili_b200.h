@@ -209,6 +209,12 @@ int sili_layer_stats(sili_layer* h, double* stats);
 int sili_layer_recompute_stats(sili_layer* h);
 /* last forward input [batch, n_in] (NULL out -> only batch/cols) */
 int sili_layer_last_input(sili_layer* h, float* out, int* batch, int* cols);
+/* the last forward_sparse input as a dense [batch, n_in] array (NULL out ->
+ * only batch/cols).  No reference counterpart: the reference's SISLDOLayer
+ * (sili/sparse_rnn.py:764-810) hands backward_sparse the layer's last_input,
+ * meaning the dense form of its forward_sparse input, which the reference's
+ * module never stores; the pybind layer passes this one for x = None. */
+int sili_layer_last_sparse_input(sili_layer* h, float* out, int* batch, int* cols);
 
 /* ── block4 tiles (4x4 dense FP4 tiles beside the scattered synapses) ───── */
 /* synapses in the combined export (scattered + live block4 slots) -- the
@@ -286,6 +292,38 @@ int sili_dense_to_csr(const float* x, int rows, int cols, float threshold, int* 
  * ascending columns; ties at the k-th magnitude go to the lower flat index. */
 int sili_dense_to_top_k_csr(const float* x, int rows, int cols, int64_t k, int* ptrs, int* idx,
                             float* vals, void* stream);
+
+/* csr_union(ptrs_a, idx_a, vals_a, ptrs_b, idx_b, vals_b, n_rows, prefer),
+ * cpu_backend.cpp:3200-3238 -> csr_union (csr.hpp:505-580): per row the
+ * two-pointer merge of A's and B's column lists; prefer 0 keeps A's value on
+ * an overlap, 1 B's, 2 their sum (anything else: SILI_EINVAL).  Host or
+ * device arrays.  Two-phase like sili_dense_to_csr: out_idx / out_vals NULL
+ * gives out_ptrs[n_rows+1] and *nnz_out only. */
+int sili_csr_union(const int* ptrs_a, const int* idx_a, const float* vals_a, const int* ptrs_b, const int* idx_b,
+                   const float* vals_b, int n_rows, int prefer, int* out_ptrs, int* out_idx, float* out_vals,
+                   int64_t* nnz_out, void* stream);
+
+/* ── attention (sili/lib/headers/attention.hpp) ────────────────────────── */
+/* banded_attention_forward (:39-96) and, for inner_k > 0,
+ * sparse_banded_attention_forward (:121-197; the inner_k band keys of largest
+ * L2 norm, ties to the lower key) over `groups` query matrices [T, d] and
+ * `kv_groups` key / value matrices [K, d] (query group g reads key group
+ * g / (groups / kv_groups)); out [groups, T, d].  Host or device arrays.
+ * The bindings banded_attention / sparse_banded_attention of
+ * cpu_backend.cpp:3404-3443 are groups = kv_groups = 1.  d <= 256. */
+int sili_banded_attention(const float* q, const float* k, const float* v, float* out, int64_t groups,
+                          int64_t kv_groups, int64_t T, int64_t K, int64_t d, int64_t half_bandwidth,
+                          int64_t inner_k, int causal, void* stream);
+/* sparse_attention_forward (:228-333, binding cpu_backend.cpp:3384-3402):
+ * q, k, v, out [T, d]; top_k = 0 -> floor(sqrt(T)); rows of unselected
+ * queries are zero. */
+int sili_sparse_attention(const float* q, const float* k, const float* v, float* out, int64_t T, int64_t d,
+                          int64_t top_k, int causal, void* stream);
+/* banded_attention_backward (:354-442, binding cpu_backend.cpp:3445-3468):
+ * dQ [groups, T, d], dK / dV [kv_groups, K, d] (written, not accumulated). */
+int sili_banded_attention_backward(const float* q, const float* k, const float* v, const float* dO, float* dQ,
+                                   float* dK, float* dV, int64_t groups, int64_t kv_groups, int64_t T, int64_t K,
+                                   int64_t d, int64_t half_bandwidth, int causal, void* stream);
 
 #ifdef __cplusplus
 }

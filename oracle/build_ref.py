@@ -18,6 +18,8 @@ What it builds (outputs go to ``oracle/_ref/`` only, which git ignores):
   3.0.2) is patched there: ``py::keep_alive<0, 1>()`` is removed from the
   ``def_property_readonly`` bindings, which pybind11 3.1 rejects.  The
   reference tree itself is read-only and is never modified.
+* ``_ref/py/`` -- the reference's pure-Python package ``sili`` and the Python
+  tests of its sparse-layer callers, copied unchanged, for the drop-in tests.
 * ``_ref/<variant>/libref_shim.so`` -- ``oracle/ref_shim.cpp`` (this repo's
   own harness code) compiled against the reference headers.  It exposes the
   reference's internal delta-CSR state (ULEB128 bytes, FP4 value bytes,
@@ -94,6 +96,33 @@ def _cpu_flags() -> list[str]:
     return []
 
 
+# The reference's pure-Python package and the Python tests of its
+# sparse-layer callers, copied as they are (outputs under _ref/py only):
+# the drop-in tests import the reference's own FoldedLayer / SparseRNNCell /
+# DISLDO / SISLDO classes from here and run them on this library's module.
+PY_TESTS = ["tests/unit/python/test_sparse_rnn_cell.py", "tests/unit/python/test_forward_output_not_aliased.py",
+            "tests/unit/python/test_stochastic_rounding.py", "tests/unit/python/gen_toy_mistral.py",
+            "tests/integration/test_toy_mistral.py", "tests/integration/test_folded_column_layer.py"]
+
+
+def copy_python() -> None:
+    dst = os.path.join(OUT, "py")
+    if os.path.isdir(dst):
+        shutil.rmtree(dst)
+    src_pkg = os.path.join(REFERENCE_DIR, "sili")
+    for root, _dirs, files in os.walk(src_pkg):
+        rel = os.path.relpath(root, src_pkg)
+        if rel.startswith("lib"):
+            continue
+        for f in files:
+            if f.endswith(".py"):
+                os.makedirs(os.path.join(dst, "sili", rel), exist_ok=True)
+                shutil.copy2(os.path.join(root, f), os.path.join(dst, "sili", rel, f))
+    os.makedirs(os.path.join(dst, "reftests"), exist_ok=True)
+    for t in PY_TESTS:
+        shutil.copy2(os.path.join(REFERENCE_DIR, t), os.path.join(dst, "reftests", os.path.basename(t)))
+
+
 def build_variant(variant: str) -> None:
     march = VARIANTS[variant]
     out_dir = os.path.join(OUT, variant)
@@ -132,6 +161,8 @@ def main(argv=None) -> int:
     for v in names:
         build_variant(v)
         print(f"built oracle/_ref/{v}")
+    copy_python()
+    print("copied the reference's Python package and caller tests to oracle/_ref/py")
     return 0
 
 

@@ -3,7 +3,8 @@
 A drop-in for the reference's ``sili._cpu`` sparse-layer module
 (sili/cpu_backend.cpp): ``SparseLinearLayer`` / ``SparseLinearLayerDeterministic``
 with the same method surface, plus the module functions ``dense_to_csr``,
-``dense_to_top_k_csr``, ``fp4_quantize_array`` and ``seed_fp4_stochastic_rng``.
+``dense_to_top_k_csr``, ``fp4_quantize_array``, ``seed_fp4_stochastic_rng``,
+``csr_union`` and the banded / sparse attention functions.
 All compute runs in ``libsili_b200.so`` (CUDA kernels behind the C ABI of
 ``include/sili_b200.h``); there is no CPU path.  Importing fails loudly when
 the extension has not been built (``python -m sili__new_b200.build``).
@@ -31,9 +32,15 @@ from ._cuda import (  # noqa: E402,F401
     seed_fp4_stochastic_rng,
     device_count,
     kernel_launches,
+    csr_union,
+    banded_attention,
+    sparse_banded_attention,
+    sparse_attention,
+    banded_attention_backward,
 )
 from .backend import CudaBackend, install_as_sili_cuda, register  # noqa: E402,F401
 
 __all__ = ["SparseLinearLayer", "SparseLinearLayerDeterministic", "dense_to_csr", "dense_to_top_k_csr",
-           "fp4_quantize_array", "seed_fp4_stochastic_rng", "device_count", "kernel_launches", "CudaBackend", "register",
-           "install_as_sili_cuda", "LIBRARY_PATH"]
+           "fp4_quantize_array", "seed_fp4_stochastic_rng", "device_count", "kernel_launches", "csr_union",
+           "banded_attention", "sparse_banded_attention", "sparse_attention", "banded_attention_backward",
+           "CudaBackend", "register", "install_as_sili_cuda", "LIBRARY_PATH"]

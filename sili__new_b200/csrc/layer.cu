@@ -139,6 +139,8 @@ struct sili_layer {
     DBuf<uint8_t> cub_tmp;
     // scratch
     DBuf<float> xT, dyT, dxT, colg, colc, ytmp, x_stage, dy_stage, dx_stage;
+    DBuf<float> xsT;              // the last forward_sparse input, densified and transposed
+    int sparse_batch = 0;
     bool has_dead_rows = false;
     // column shard (sili_layer_set_row_shard): global synapse count per row,
     // global column count, whether some row has none anywhere; the
@@ -1105,15 +1107,16 @@ int sili_layer_load_weights(sili_layer* h, const int* ptrs, const int* idx, cons
     CK(cudaMemcpyAsync(dp.p, hp.data(), (R + 1) * 4, cudaMemcpyHostToDevice, s));
     RC(to_dev(idx, di.p, (size_t)nnz * 4, s));
     RC(to_dev(vals, dv.p, (size_t)nnz * 4, s));
-    // column range / ordering check on the host copy (the reference assumes sorted input)
+    // column range check on the host copy.  Columns need not ascend within a
+    // row: like delta_csr_from_absolute (delta_csr_memory.hpp:16-93) a
+    // descending step is stored as the wrapped 32-bit delta (a 5-byte
+    // ULEB128) and decodes back to the same column, so such rows load,
+    // forward and train in their given order as in the reference.
     std::vector<int> hi(nnz);
     if (nnz) CK(cudaMemcpyAsync(hi.data(), di.p, (size_t)nnz * 4, cudaMemcpyDeviceToHost, s));
     CK(cudaStreamSynchronize(s));
-    for (int r = 0; r < R; ++r)
-        for (int f = hp[r]; f < hp[r + 1]; ++f) {
-            if (hi[f] < 0 || hi[f] >= h->cols) return fail(SILI_EINVAL, "load_weights: column index out of range");
-            if (f > hp[r] && hi[f] < hi[f - 1]) return fail(SILI_EINVAL, "load_weights: columns must be sorted within a row");
-        }
+    for (int f = 0; f < nnz; ++f)
+        if (hi[f] < 0 || hi[f] >= h->cols) return fail(SILI_EINVAL, "load_weights: column index out of range");
     RC(import_csr(h, dp.p, di.p, dv.p, nnz));
     h->idx_budget = std::max<int64_t>(h->idx_budget, (int64_t)nnz * 8 + 4096);
     h->val_budget = std::max<int64_t>(h->val_budget, (int64_t)nnz + 64);
@@ -1516,26 +1519,30 @@ int sili_layer_forward_sparse(sili_layer* h, const int* ptrs, const int* idx, co
     const int* di = nullptr;
     const float* dv = nullptr;
     RC(stage_csr(h, ptrs, idx, vals, batch, nnz, &dp, &di, &dv, s));
-    RC(h->xT.reserve((int64_t)batch * (n_in + 1) + 1));
-    CK(cudaMemsetAsync(h->xT.p, 0, (size_t)batch * (n_in + 1) * 4, s));   // + the zero row
+    // the densified input goes to its own buffer: forward_sparse leaves the
+    // last forward_dense input (which backward_dense uses) alone, as the
+    // reference's does (cpu_backend.cpp:571-585 never touches _last_input)
+    RC(h->xsT.reserve((int64_t)batch * (n_in + 1) + 1));
+    CK(cudaMemsetAsync(h->xsT.p, 0, (size_t)batch * (n_in + 1) * 4, s));   // + the zero row
     uint8_t* xpres = nullptr;
     if (h->b4_ntiles > 0) {
         RC(h->presX.reserve((int64_t)batch * n_in + 1));
         CK(cudaMemsetAsync(h->presX.p, 0, (size_t)batch * n_in, s));
         xpres = h->presX.p;
     }
-    launch_csr_to_dense_t(dp, di, dv, batch, (int)n_in, h->xT.p, xpres, s);
+    launch_csr_to_dense_t(dp, di, dv, batch, (int)n_in, h->xsT.p, xpres, s);
+    h->sparse_batch = batch;
     const bool dev_out = is_device_ptr(y);
     float* yd = y;
     if (!dev_out) {
         RC(h->ytmp.reserve((int64_t)batch * n_out + 1));
         yd = h->ytmp.p;
     }
-    if (h->total_nnz > 0) RC(forward_columns(h, h->xT.p, batch, yd, true, s));
+    if (h->total_nnz > 0) RC(forward_columns(h, h->xsT.p, batch, yd, true, s));
     else CK(cudaMemsetAsync(yd, 0, (size_t)batch * n_out * 4, s));
     if (h->b4_ntiles > 0) {
         RC(ensure_b4_index(h, s));
-        launch_b4_forward_sparse(h->view(), h->b4view(), h->xT.p, xpres, batch, yd, s);
+        launch_b4_forward_sparse(h->view(), h->b4view(), h->xsT.p, xpres, batch, yd, s);
     }
     CK(cudaGetLastError());
     if (!dev_out) CK(cudaMemcpyAsync(y, yd, (size_t)batch * n_out * 4, cudaMemcpyDeviceToHost, s));
@@ -2269,6 +2276,20 @@ int sili_layer_stats(sili_layer* h, double* stats) {
 int sili_layer_recompute_stats(sili_layer* h) {
     RC(use(h));
     return recompute_stats(h);
+}
+
+int sili_layer_last_sparse_input(sili_layer* h, float* out, int* batch, int* cols) {
+    RC(use(h));
+    if (batch) *batch = h->sparse_batch;
+    if (cols) *cols = (int)h->rows;
+    if (out && h->sparse_batch > 0) {
+        DBuf<float> t;
+        RC(t.reserve((int64_t)h->sparse_batch * h->rows + 1));
+        launch_transpose(h->xsT.p, t.p, h->rows, h->sparse_batch, h->stream);
+        RC(from_dev(t.p, out, (size_t)h->sparse_batch * h->rows * 4, h->stream));
+        CK(cudaStreamSynchronize(h->stream));
+    }
+    return SILI_OK;
 }
 
 int sili_layer_last_input(sili_layer* h, float* out, int* batch, int* cols) {

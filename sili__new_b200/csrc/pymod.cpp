@@ -191,8 +191,21 @@ public:
         return y;
     }
 
-    py::array_t<float> backward_sparse(farr x, iarr dptrs, iarr didx, farr dvals, int batch, float lr,
+    py::array_t<float> backward_sparse(py::object xo, iarr dptrs, iarr didx, farr dvals, int batch, float lr,
                                        bool lr_per_row_nnz, bool damp, float beta2, float eps) {
+        farr x;
+        if (xo.is_none()) {
+            // the reference's SISLDOLayer passes last_input, which its module
+            // leaves unset after forward_sparse: the dense form of the last
+            // forward_sparse input is what that caller means
+            int sb = 0, sc = 0;
+            check(sili_layer_last_sparse_input(h, nullptr, &sb, &sc));
+            if (sb != batch) throw py::value_error("backward_sparse: x is None and the last forward_sparse batch differs");
+            x = farr({(py::ssize_t)sb, (py::ssize_t)sc});
+            check(sili_layer_last_sparse_input(h, x.mutable_data(), &sb, &sc));
+        } else {
+            x = xo.cast<farr>();
+        }
         if ((int64_t)x.size() != (int64_t)batch * n_in) throw py::value_error("backward_sparse: x must be [batch, n_inputs]");
         py::array_t<float> dx({(py::ssize_t)batch, (py::ssize_t)n_in});
         unsigned flags = (lr_per_row_nnz ? SILI_LR_PER_ROW_NNZ : 0u) | (damp ? SILI_DAMP_BY_IMPORTANCE : 0u);
@@ -582,6 +595,87 @@ PYBIND11_MODULE(_cuda, m) {
     }, py::arg("dy"), py::arg("batch"), py::arg("out_dim"), py::arg("j0"), py::arg("width"), py::arg("n_folds"),
        py::arg("raw"), py::arg("stream") = 0);
     m.def("kernel_launches", []() { int64_t n = 0; sili_kernel_launches(&n); return n; });
+    m.def("csr_union", [](iarr pa, iarr ia, farr va, iarr pb, iarr ib, farr vb, int n_rows, std::string prefer,
+                          int num_cpus) {
+        (void)num_cpus;
+        const int code = prefer == "a" ? 0 : prefer == "b" ? 1 : prefer == "sum" ? 2 : -1;
+        if (code < 0) throw py::value_error("prefer must be 'a', 'b', or 'sum'");
+        if (pa.size() < (py::ssize_t)n_rows + 1 || pb.size() < (py::ssize_t)n_rows + 1)
+            throw py::value_error("csr_union: ptrs shorter than n_rows + 1");
+        const int na = pa.data()[n_rows], nb = pb.data()[n_rows];
+        if (ia.size() < na || va.size() < na || ib.size() < nb || vb.size() < nb)
+            throw py::value_error("csr_union: idx/vals shorter than ptrs[n_rows]");
+        py::array_t<int> p((py::ssize_t)n_rows + 1);
+        int64_t n = 0;
+        check(sili_csr_union(pa.data(), ia.data(), va.data(), pb.data(), ib.data(), vb.data(), n_rows, code,
+                             p.mutable_data(), nullptr, nullptr, &n, nullptr));
+        py::array_t<int> i((py::ssize_t)n);
+        py::array_t<float> v((py::ssize_t)n);
+        check(sili_csr_union(pa.data(), ia.data(), va.data(), pb.data(), ib.data(), vb.data(), n_rows, code,
+                             p.mutable_data(), i.mutable_data(), v.mutable_data(), &n, nullptr));
+        return py::make_tuple(p, i, v);
+    }, py::arg("ptrs_a"), py::arg("idx_a"), py::arg("vals_a"), py::arg("ptrs_b"), py::arg("idx_b"), py::arg("vals_b"),
+       py::arg("n_rows"), py::arg("prefer") = "a", py::arg("num_cpus") = 4);
+    // attention.hpp's kernels with the reference's signatures (cpu_backend.cpp:3384-3468)
+    auto td = [](const farr& a, const char* who) {
+        auto b = a.request();
+        if (b.ndim != 2) throw py::value_error(std::string(who) + ": q, k, v must be [T, d]");
+        return std::make_pair((int64_t)b.shape[0], (int64_t)b.shape[1]);
+    };
+    m.def("banded_attention", [td](farr q, farr k, farr v, int64_t hbw, int num_cpus, bool causal) {
+        (void)num_cpus;
+        auto [T, d] = td(q, "banded_attention");
+        auto [K, dk] = td(k, "banded_attention");
+        if (dk != d || v.size() != K * d) throw py::value_error("banded_attention: k, v must be [K, d]");
+        py::array_t<float> out({(py::ssize_t)T, (py::ssize_t)d});
+        check(sili_banded_attention(q.data(), k.data(), v.data(), out.mutable_data(), 1, 1, T, K, d, hbw, 0, causal,
+                                    nullptr));
+        return out;
+    }, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("half_bandwidth"), py::arg("num_cpus") = 4,
+       py::arg("causal") = false);
+    m.def("sparse_banded_attention", [td](farr q, farr k, farr v, int64_t hbw, int64_t inner_k, int num_cpus,
+                                          bool causal) {
+        (void)num_cpus;
+        auto [T, d] = td(q, "sparse_banded_attention");
+        auto [K, dk] = td(k, "sparse_banded_attention");
+        if (dk != d || v.size() != K * d) throw py::value_error("sparse_banded_attention: k, v must be [K, d]");
+        py::array_t<float> out({(py::ssize_t)T, (py::ssize_t)d});
+        check(sili_banded_attention(q.data(), k.data(), v.data(), out.mutable_data(), 1, 1, T, K, d, hbw, inner_k,
+                                    causal, nullptr));
+        return out;
+    }, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("half_bandwidth"), py::arg("inner_k") = 0,
+       py::arg("num_cpus") = 4, py::arg("causal") = false);
+    m.def("sparse_attention", [td](farr q, farr k, farr v, int64_t top_k, int num_cpus, bool causal) {
+        (void)num_cpus;
+        auto [T, d] = td(q, "sparse_attention");
+        if (k.size() != T * d || v.size() != T * d) throw py::value_error("sparse_attention: q, k, v must be [T, d]");
+        py::array_t<float> out({(py::ssize_t)T, (py::ssize_t)d});
+        check(sili_sparse_attention(q.data(), k.data(), v.data(), out.mutable_data(), T, d, top_k, causal, nullptr));
+        return out;
+    }, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("top_k") = 0, py::arg("num_cpus") = 4,
+       py::arg("causal") = false);
+    m.def("banded_attention_backward", [td](farr q, farr k, farr v, farr dO, int64_t hbw, int num_cpus, bool causal) {
+        (void)num_cpus;
+        auto [T, d] = td(q, "banded_attention_backward");
+        auto [K, dk] = td(k, "banded_attention_backward");
+        if (dk != d || v.size() != K * d || dO.size() != T * d)
+            throw py::value_error("banded_attention_backward: k, v [K, d] and dO [T, d] expected");
+        py::array_t<float> dQ({(py::ssize_t)T, (py::ssize_t)d}), dK({(py::ssize_t)K, (py::ssize_t)d}),
+            dV({(py::ssize_t)K, (py::ssize_t)d});
+        check(sili_banded_attention_backward(q.data(), k.data(), v.data(), dO.data(), dQ.mutable_data(),
+                                             dK.mutable_data(), dV.mutable_data(), 1, 1, T, K, d, hbw, causal, nullptr));
+        return py::make_tuple(dQ, dK, dV);
+    }, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("dO"), py::arg("half_bandwidth"), py::arg("num_cpus") = 4,
+       py::arg("causal") = false);
+    // device-pointer form over groups (heads x sequences), grouped-query KV
+    m.def("banded_attention_ptr", [](uintptr_t q, uintptr_t k, uintptr_t v, uintptr_t out, int64_t groups,
+                                     int64_t kv_groups, int64_t T, int64_t K, int64_t d, int64_t hbw, int64_t inner_k,
+                                     bool causal, uintptr_t stream) {
+        check(sili_banded_attention((const float*)q, (const float*)k, (const float*)v, (float*)out, groups, kv_groups,
+                                    T, K, d, hbw, inner_k, causal, (void*)stream));
+    }, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("out"), py::arg("groups"), py::arg("kv_groups"),
+       py::arg("T"), py::arg("K"), py::arg("d"), py::arg("half_bandwidth"), py::arg("inner_k") = 0,
+       py::arg("causal") = false, py::arg("stream") = 0);
     m.def("fp32_fma_peak", [](int device, int iters) {
         double tf = 0, ms = 0;
         check(sili_fp32_fma_peak(device, iters, &tf, &ms));

@@ -59,3 +59,20 @@ def test_backend_registration_protocol():
     be = S.CudaBackend()
     assert be.name == "cuda" and be.mod is S._cuda
     assert be.dense_to_csr is S._cuda.dense_to_csr
+
+
+def test_path_module_serves_the_path_names_only():
+    """PathModule (the drop-in for sili._cpu) resolves the sparse-layer names
+    to this library and every other name to the module it wraps."""
+    import types
+    import sili__new_b200 as S
+    from sili__new_b200.backend import PATH_NAMES, PathModule
+    base = types.SimpleNamespace(__name__="sili._cpu", SparseLinearLayer=object, DISLDOLayerV="ref-fp32",
+                                 gaussian_attention="ref-attn", csr_union="ref-union")
+    pm = PathModule(base)
+    assert pm.SparseLinearLayer is S._cuda.SparseLinearLayer
+    assert pm.csr_union is S._cuda.csr_union
+    assert pm.DISLDOLayerV == "ref-fp32" and pm.gaussian_attention == "ref-attn"
+    assert pm.banded_attention is S._cuda.banded_attention
+    for name in PATH_NAMES:
+        assert getattr(pm, name) is getattr(S._cuda, name), name
