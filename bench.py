@@ -257,11 +257,41 @@ def run_block4(args, dev, S, torch, work, cpu_sample):
     e1.record(stream)
     torch.cuda.synchronize(dev)
     ms = e0.elapsed_time(e1) / steps
+
+    def fwd_ms(tc):
+        # the forward alone, exact CUDA-core path or tensor cores (tcgen05)
+        L.set_block4_tensor_cores(tc)
+        for _ in range(3):
+            L.forward_dense_ptr(xs.data_ptr(), BATCH, y.data_ptr(), sh)
+        e0.record(stream)
+        for _ in range(steps):
+            L.forward_dense_ptr(xs.data_ptr(), BATCH, y.data_ptr(), sh)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / steps
+
+    f_exact, f_tc = fwd_ms(False), fwd_ms(True)
+    # the training step with the tensor-core forward (the update is the same)
+    L.set_block4_tensor_cores(True)
+    for _ in range(2):
+        step()
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms_tc = e0.elapsed_time(e1) / steps
+    L.set_block4_tensor_cores(False)
     tiles = int(L.block4.tiles)
     # 16 B per tile read by the forward, read and written by the update, + activations
     step_bytes = tiles * 16 * 3 + BATCH * 4 * (2 * N_IN + 2 * N_OUT + N_IN)
+    # the forward as a product: 2 * 16 FLOP per tile per sample (x3 for the
+    # split activations on the tensor cores)
+    fwd_flop = 2.0 * 16 * tiles * BATCH
     out = {"metric": "block4 format fwd+bwd effective GB/s (config 2 matrix in 4x4 FP4 tiles, batch 64)",
            "value": step_bytes / (ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms, "steps": steps,
+           "ms_per_step_tc_forward": ms_tc, "fwd_ms": f_exact, "fwd_tc_ms": f_tc,
+           "fwd_tc_tflops": 3 * fwd_flop / (f_tc * 1e-3) / 1e12,
            "tiles": tiles, "live_slots_at_load": int(np.count_nonzero(wc)), "bytes_per_step": step_bytes}
     del L, xs, dys, y, dx
     torch.cuda.empty_cache()
@@ -601,11 +631,14 @@ def run_folded(args, dev, rank, world, dist, S, torch, which="config5"):
     stream = torch.cuda.Stream(device=dev)
     stream.wait_stream(torch.cuda.current_stream(dev))   # the inputs are written on the current stream
 
+    # one all-gather per group of suffixes (q/k/v, o, gate/up, down) instead
+    # of one per suffix
+    groups = [[n for n in ("q_proj", "k_proj", "v_proj") if n in suffixes], ["o_proj"],
+              ["gate_proj", "up_proj"], ["down_proj"]]
+    groups = [g for g in groups if g and all(n in suffixes for n in g)]
+
     def decode_step():
-        outs = []
-        for name in suffixes:
-            outs.append(stack.forward_device(name, xs[name], stream))
-        return outs
+        return [stack.forward_group(g, xs, stream) for g in groups]
 
     prefill = fc["kind"] == "prefill"   # a step of 4096 tokens: fewer, longer steps
     for _ in range(3 if prefill else max(args.warmup, 3)):
@@ -642,10 +675,72 @@ def run_folded(args, dev, rank, world, dist, S, torch, which="config5"):
             "value": B / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "scaling": "strong",
             "ms_per_step": ms, "steps": steps, "nnz": total_nnz,
             "gflop_per_step": flops / 1e9, "fp32_tflops": flops / (ms * 1e-3) / 1e12,
-            "sharding": f"output columns within each fold over {world} rank(s), NCCL all-gather per suffix",
+            "sharding": f"output columns within each fold over {world} rank(s), "
+                        f"{len(groups)} NCCL all-gathers per step (suffix groups)",
+            "collectives_per_step": len(groups) if world > 1 else 0,
             "build_s_rank0": build_s, "torch_mem_gb_rank0": mem_gb, "gpu_launches_rank0": launches,
             "data": f"synthetic: random N(0,0.02) pruned to {density * 100:g}% (uniform pattern), x ~ N(0,1)",
             "train": train}
+
+
+def run_shards(args, dev, S, torch, worlds=(1, 2, 4, 8)):
+    """Per-rank forward work of config 5's column-sharded stack, emulated on
+    one GPU: for each rank count N, rank 0's shard of every suffix (40 folds,
+    its 1/N of the output columns), timed with CUDA events per call (the
+    x transpose and the one-launch forward + fold sum of
+    sili_folded_forward), each suffix alone.  The collectives are not in
+    this number; the multi-GPU run measures them."""
+    from sili__new_b200 import folded as F
+    cfg = F.MISTRAL_SMALL_24B
+    suffixes = F.mistral_suffixes(cfg)
+    n_folds, B = (args.folded_layers or cfg["layers"]), 32
+    out = {}
+    stream = torch.cuda.Stream(device=dev)
+    for N in worlds:
+        rows = {}
+        for k, (name, (in_dim, out_dim)) in enumerate(suffixes.items()):
+            j0, j1 = F.column_slice(out_dim, 0, N)
+            w = j1 - j0
+            ptrs, idx, vals, nnz = F.synthetic_shard(in_dim, out_dim, n_folds, 0.05, j0, j1, seed=101 + k,
+                                                     device=f"cuda:{dev}")
+            L = S.SparseLinearLayer(in_dim, n_folds * w, nnz, 1, dev)
+            L.load_weights_ptr(ptrs.data_ptr(), idx.data_ptr(), vals.data_ptr(), nnz)
+            L.set_scales(S._cuda.SCALE_VALUE, np.full(in_dim, np.float32(F.SYNTHETIC_VALUE_SCALE), np.float32))
+            del ptrs, idx, vals
+            gen = torch.Generator(device=f"cuda:{dev}")
+            gen.manual_seed(7)
+            x = torch.randn(B, in_dim, generator=gen, device=f"cuda:{dev}")
+            y = torch.empty(B, w, device=f"cuda:{dev}")
+            stream.wait_stream(torch.cuda.current_stream(dev))
+            call = lambda: S._cuda.folded_forward_ptr([L], x.data_ptr(), B, n_folds, w, True,  # noqa: E731
+                                                      y.data_ptr(), stream.cuda_stream)
+            raw = torch.empty(B, n_folds * w, device=f"cuda:{dev}")
+
+            def unfused():
+                # the two-launch form: the stacked layer's forward, then the fold sum
+                L.forward_dense_ptr(x.data_ptr(), B, raw.data_ptr(), stream.cuda_stream)
+                S._cuda.fold_sum_ptr(raw.data_ptr(), B, n_folds, w, y.data_ptr(), stream.cuda_stream)
+
+            def timed(fn, reps=20):
+                for _ in range(3):
+                    fn()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                for _ in range(reps):
+                    fn()
+                e1.record(stream)
+                torch.cuda.synchronize(dev)
+                return e0.elapsed_time(e1) / reps
+
+            ms = timed(call)
+            ms_u = timed(unfused)
+            rows[name] = {"ms": round(ms, 4), "ms_unfused": round(ms_u, 4), "cols": n_folds * w, "nnz": nnz,
+                          "gflops": round(2.0 * nnz * B / (ms * 1e-3) / 1e9, 1)}
+            del L, x, y, raw
+            torch.cuda.empty_cache()
+        out[str(N)] = {"suffixes": rows, "step_ms": round(sum(r["ms"] for r in rows.values()), 4),
+                       "step_ms_unfused": round(sum(r["ms_unfused"] for r in rows.values()), 4)}
+    return out
 
 
 def folded_train_leg(args, dev, dist, S, torch, stack, suffixes, xs, stream, B):
@@ -706,7 +801,7 @@ def main():
     ap.add_argument("--no-synap", action="store_true", help="skip the synaptogenesis (config 3) measurement")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the sparse-variant, reference-rule and SpMV measurements")
-    ap.add_argument("--only", choices=["block4", "synap", "folded", "folded4", "rule", "spmv", "sparse"],
+    ap.add_argument("--only", choices=["block4", "synap", "folded", "folded4", "rule", "spmv", "sparse", "shards"],
                     help="run one secondary measurement alone and print its object (profiling)")
     ap.add_argument("--detail", default=None, help="write every measurement's full object to this JSON file")
     ap.add_argument("--folded-layers", type=int, default=None,
@@ -759,6 +854,8 @@ def main():
             out = run_reference_rule(args, dev, S, torch, cpu_sample=False)
         elif args.only == "spmv":
             out = run_spmv(S, torch, dev, cpu_sample=False)
+        elif args.only == "shards":
+            out = run_shards(args, dev, S, torch)
         elif args.only == "sparse":
             w0 = make_workload()
             out = run_sparse_variants([load_layer(S.SparseLinearLayer, *w0[:4], device=dev) for _ in range(4)], S, torch,
@@ -992,7 +1089,7 @@ def compact_legs(block4, synap, rule, sparse_v, spmv, folded4):
     legs = {}
     if block4:
         legs["block4"] = {"ms": _r(block4["ms_per_step"]), "gbs": _r(block4["value"]), "cpu": _cpu_short(block4)}
-        for k in ("fwd_ms", "fwd_tc_ms"):
+        for k in ("ms_per_step_tc_forward", "fwd_ms", "fwd_tc_ms", "fwd_tc_tflops"):
             if block4.get(k) is not None:
                 legs["block4"][k] = _r(block4[k])
     if synap:

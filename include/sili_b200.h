@@ -94,6 +94,12 @@ int sili_layer_get_scale_rank(sili_layer* h, int* rank);
 /* set_*_scale_raw(_k): kind SILI_SCALE_VALUE/OUTPUT/IMPORTANCE/OUTPUT_IMPORTANCE */
 int sili_layer_set_scale(sili_layer* h, int kind, int index, int k, float v);
 int sili_layer_get_scale(sili_layer* h, int kind, int index, int k, float* v);
+/* bulk write of entries [0, n) of a scale vector's [n_rows_or_cols * rank]
+ * view (kind VALUE / OUTPUT / IMPORTANCE / OUTPUT_IMPORTANCE; host or device
+ * array): n calls of set_*_scale_raw(_k) in one copy, with their effects
+ * (the vector's logical size grows to n; setting output scales makes them
+ * trainable, cpu_backend.cpp:792-829) */
+int sili_layer_set_scales(sili_layer* h, int kind, const float* v, int n);
 /* bulk read of a whole scale vector (n entries of the [n_rows_or_cols * rank] view) */
 int sili_layer_get_scales(sili_layer* h, int kind, float* out, int n);
 /* value_scale_step / output_scale_step counters (bias correction) */
@@ -231,6 +237,15 @@ int sili_layer_b4_expand_headroom(sili_layer* h, float blank_fraction, int64_t m
 /* the block4 half of equalizer_step (Block4Store::equalize_step,
  * block4.hpp:1208-1221); row is the block-row cursor */
 int sili_layer_b4_equalize_row(sili_layer* h, int64_t row);
+/* The block4 forward on the tensor cores (no counterpart in the reference,
+ * whose block4 forward is linear_disldo.hpp:128-339): enable = 1 runs the
+ * block4 part of forward_dense for rank-1 layers at batch >= 16 as
+ * tcgen05 MMAs (FP4 codes exact in bf16, x * value_scale split into three
+ * bf16 terms, fp32 accumulation) -- within fp32 summation tolerance of the
+ * exact CUDA-core path, which is the default (enable = 0).  A bounded
+ * device-side wait that gives up is reported as SILI_ETIMEOUT by the next
+ * synchronising call (sili_layer_sync, or a forward with host arrays). */
+int sili_layer_set_b4_tensor_cores(sili_layer* h, int enable);
 /* Block4View.switch_point setter (cpu_backend.cpp:61-62) */
 int sili_layer_b4_set_switch_point(sili_layer* h, uint32_t v);
 /* Block4View counters, cpu_backend.cpp:51-98: tiles, synapses, switch_point,
@@ -249,6 +264,19 @@ int sili_layer_b4_rows(sili_layer* h, int64_t* out6);
 /* FoldedLayer's fold sum (sili/sparse_rnn.py:1120-1125) on device arrays:
  * y[b, j] = sum over folds f ascending of raw[b, f*out_dim + j] */
 int sili_fold_sum(const float* raw, int batch, int n_folds, int64_t out_dim, float* y, void* stream);
+/* FoldedLayer.forward (sili/sparse_rnn.py:1096-1125) in one call: every
+ * suffix layer (each n_in -> n_folds * out_dim, one device) on the same x
+ * [batch, n_in], their outputs summed in suffix order and, with fold_sum,
+ * the folds summed: y [batch, out_dim]; without fold_sum (FoldedColumnLayer.
+ * in_proj, :1340-1362) y is the suffix sum [batch, n_folds * out_dim].  One
+ * transposed copy of x serves every layer and stays each layer's last input
+ * (backward_dense works as after forward_dense).  Two to four rank-1 suffix
+ * layers without block4 tiles, at batch >= 16 and a multiple of 4, run as
+ * one kernel launch that sums in shared memory; a single suffix runs its
+ * layer's forward and the fold sum (two launches, measured faster).  Host or
+ * device x / y. */
+int sili_folded_forward(sili_layer* const* layers, int n_layers, const float* x, int batch, int n_folds,
+                        int64_t out_dim, int fold_sum, float* y, void* stream);
 /* The backward of the fold sum for one rank's column slice (the np.tile of
  * FoldedLayer's backward, sili/sparse_rnn.py:1144-1148, restricted to output
  * columns [j0, j0 + width)): raw[b, f*width + j] = dy[b, j0 + j], dy being
@@ -302,6 +330,35 @@ int sili_dense_to_top_k_csr(const float* x, int rows, int cols, int64_t k, int* 
 int sili_csr_union(const int* ptrs_a, const int* idx_a, const float* vals_a, const int* ptrs_b, const int* idx_b,
                    const float* vals_b, int n_rows, int prefer, int* out_ptrs, int* out_idx, float* out_vals,
                    int64_t* nnz_out, void* stream);
+
+/* ── conversion-time CSR operations (device arrays) ─────────────────────
+ * What the reference's conversion path does in torch / numpy on the host:
+ * prune_to_csr     to_sparse_csr (sili/conversion/sparse_prune.py:466-482):
+ *                  w [rows, cols] -> row-major CSR of the entries with
+ *                  |w| >= min_abs and w != 0; two-phase (idx / vals NULL ->
+ *                  ptrs and *nnz_out only)
+ * csr_transpose    csr.t().to_sparse_csr() (sili/sparse_rnn.py:1002): rows
+ *                  of the result ascend in column order
+ * csr_stack_vertical  stack_csr_vertical (sili/conversion/rnn_fold.py:259-320):
+ *                  parts [rows_p, cols] -> [sum rows_p, cols]; out_ptrs has
+ *                  sum rows_p + 1 entries
+ * fit_rank1_envelope  fit_rank1_scale_envelope (sili/sparse_rnn.py:854-882) on
+ *                  the |vals| of a CSR, n_iters alternating max-fits
+ * fp4_row_rescale  FoldedLayer.from_descriptor's FP4 preparation
+ *                  (sili/sparse_rnn.py:1005-1037): mode 0 per_row (row_scale
+ *                  out = max|row| / 6, 1 for empty / zero rows), mode 1 rank1
+ *                  (row_scale in = the envelope's rows, out = them / 6);
+ *                  vals divided in place */
+int sili_prune_to_csr(const float* w, int64_t rows, int64_t cols, float min_abs, int* ptrs, int* idx, float* vals,
+                      int64_t* nnz_out, void* stream);
+int sili_csr_transpose(const int* ptrs, const int* idx, const float* vals, int n_rows, int n_cols, int* out_ptrs,
+                       int* out_idx, float* out_vals, void* stream);
+int sili_csr_stack_vertical(int n_parts, const int* const* ptrs, const int* const* idx, const float* const* vals,
+                            const int* rows, int* out_ptrs, int* out_idx, float* out_vals, void* stream);
+int sili_fit_rank1_envelope(const int* ptrs, const int* idx, const float* vals, int n_rows, int n_cols, int n_iters,
+                            float* row_scale, float* col_scale, void* stream);
+int sili_fp4_row_rescale(const int* ptrs, const int* idx, float* vals, int n_rows, int mode, const float* col_scale,
+                         float* row_scale, void* stream);
 
 /* ── attention (sili/lib/headers/attention.hpp) ────────────────────────── */
 /* banded_attention_forward (:39-96) and, for inner_k > 0,

@@ -21,7 +21,7 @@ BUILD = os.path.join(HERE, "_build")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 NVCC = os.environ.get("NVCC", "nvcc")
 
-CU_SOURCES = ["kernels_compute.cu", "kernels_update.cu", "kernels_forward.cu", "kernels_struct.cu", "block4.cu", "synap.cu", "topk.cu", "peak.cu", "csr_ops.cu", "attention.cu", "layer.cu"]
+CU_SOURCES = ["kernels_compute.cu", "kernels_update.cu", "kernels_forward.cu", "kernels_struct.cu", "block4.cu", "block4_tc.cu", "synap.cu", "topk.cu", "peak.cu", "csr_ops.cu", "attention.cu", "layer.cu"]
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "--fmad=false",
               "-std=c++17", "-Xcompiler", "-fPIC", "-I" + INCLUDE]
 LIB = os.path.join(HERE, "libsili_b200.so")

@@ -3,6 +3,7 @@
 
 #include <cstdint>
 #include <cuda_runtime.h>
+#include <string>
 
 namespace sili {
 
@@ -112,6 +113,43 @@ bool launch_forward_rows(const LayerView& L, const float* xT, int B, float* y, b
                          cudaStream_t s);
 // whether launch_forward_rows would run for this shape (it needs L.cpack)
 bool forward_rows_applies(const LayerView& L, int B);
+
+// The suffix layers of one folded layer (same n_in, n_out = n_folds *
+// out_dim, scale rank 1), for the one-launch FoldedLayer forward.
+constexpr int kFoldedMaxSuffixes = 4;
+struct FoldedView {
+    int ns = 0;
+    int n_in = 0;
+    int64_t n_cols = 0, out_dim = 0;
+    int n_folds = 0;
+    bool fold_sum = true;
+    int J = 1;   // output columns per CTA (set by the launcher)
+    const int* colptr[kFoldedMaxSuffixes] = {};
+    const int* colptr_x[kFoldedMaxSuffixes] = {};
+    const int* cpack[kFoldedMaxSuffixes] = {};
+    const float* vs[kFoldedMaxSuffixes] = {};
+    const float* os[kFoldedMaxSuffixes] = {};
+};
+bool folded_forward_applies(const FoldedView& F, int B);
+// The block4 forward on the tensor cores (block4_tc.cu): rank 1, B >= 16.
+// Scratch: the split activations (b4_tc_xsplit_elems bf16) and the partial
+// sums (b4_tc_scratch_floats, which also picks the input-row slices).
+bool b4_tc_applies(const LayerView& L, const B4View& V, int B);
+int64_t b4_tc_scratch_floats(const LayerView& L, int B, int* kslices);
+int64_t b4_tc_xsplit_elems(const LayerView& L, int B);
+// the panel map (tile slot per 32-block-column x 16-block-row cell), rebuilt
+// when the tile layout changes
+int64_t b4_tc_pmap_elems(const LayerView& L);
+void launch_b4_panel_map(const LayerView& L, const B4View& V, int* pmap, cudaStream_t s);
+int launch_b4_forward_tc(const LayerView& L, const B4View& V, const float* xT, int B, float* y, uint16_t* xsplit,
+                         float* part, int kslices, const int* pmap, unsigned int* err, cudaStream_t s);
+int set_error(int code, const std::string& msg);
+
+// y = [B, out_dim] (fold_sum) or [B, n_cols]; false when the shape rules
+// (folded_forward_applies) do not hold
+bool launch_folded_forward(FoldedView F, const float* xT, int B, float* y, cudaStream_t s);
+// y[b, c] = 0 + raw_0[b, c] + raw_1[b, c] + ... (n raws of [B, n_cols])
+void launch_suffix_sum(const float* const* raws, int n, int64_t count, float* y, cudaStream_t s);
 // L.cpack from crow / cvpos / val over the padded CSC (its length is colptr[n_out])
 void launch_pack_csc(const LayerView& L, int64_t bound, int* cpack, cudaStream_t s);
 void launch_backward_update(const LayerView& L, const float* xT, const float* dyT, int B,

@@ -140,6 +140,7 @@ struct sili_layer {
     // scratch
     DBuf<float> xT, dyT, dxT, colg, colc, ytmp, x_stage, dy_stage, dx_stage;
     DBuf<float> xsT;              // the last forward_sparse input, densified and transposed
+    DBuf<float> fold_raw;         // sili_folded_forward's per-suffix outputs before the sums
     int sparse_batch = 0;
     bool has_dead_rows = false;
     // column shard (sili_layer_set_row_shard): global synapse count per row,
@@ -175,6 +176,12 @@ struct sili_layer {
     int64_t b4_max_idx = INT64_MAX, b4_max_tile = INT64_MAX;
     uint32_t b4_switch = 10;
     bool b4_dirty = true;                  // tile column index stale
+    bool b4_tc = false;                    // block4 forward on the tensor cores (tolerance contract)
+    DBuf<uint16_t> b4_xs;                  // its split activations
+    DBuf<float> b4_part;                   // its per-slice partial sums
+    DBuf<unsigned int> tc_err;             // set by a tensor-core kernel whose bounded wait gave up
+    DBuf<int> b4_pmap;                     // its panel map (tile slot per 32 x 16 block cell)
+    bool b4_pmap_dirty = true;             // the tile layout changed since the map was built
     // synaptogenesis working set (probe-by-row index, scratch, snapshot)
     struct SynStateT {
         DBuf<int> pr_ptr, keys, keys_o, ids, ids_o, od0, od_decs;
@@ -644,6 +651,7 @@ int b4_init(sili_layer* h, int64_t cap, cudaStream_t s) {
     CK(cudaStreamSynchronize(s));
     h->b4_ntiles = 0;
     h->b4_dirty = true;
+    h->b4_pmap_dirty = true;
     return SILI_OK;
 }
 
@@ -722,7 +730,7 @@ int make_layer(int n_in, int n_out, int max_weights, int device, int stochastic,
     chk(alloc_scales(h));
     chk(h->is.reserve(n_in + 1)); chk(h->ois.reserve(n_out + 1));
     chk(h->in_acc.reserve(n_in + 1)); chk(h->grad_acc.reserve(n_out + 1)); chk(h->out_degree.reserve(n_out + 1));
-    chk(h->d_st.reserve(2)); chk(h->d_stmax.reserve(1)); chk(h->d_dyflag.reserve(1));
+    chk(h->d_st.reserve(2)); chk(h->d_stmax.reserve(1)); chk(h->d_dyflag.reserve(1)); chk(h->tc_err.reserve(1));
     if (rc) { delete h; return rc; }
     cudaStream_t s = h->stream;
     launch_fill_scale_default(h->vs.p, 0, (int64_t)n_in, 1, s);
@@ -740,6 +748,7 @@ int make_layer(int n_in, int n_out, int max_weights, int device, int stochastic,
     cudaMemsetAsync(h->d_st.p, 0, 2 * sizeof(double), s);
     cudaMemsetAsync(h->d_stmax.p, 0, sizeof(float), s);
     cudaMemsetAsync(h->d_dyflag.p, 0, sizeof(unsigned long long), s);
+    cudaMemsetAsync(h->tc_err.p, 0, sizeof(unsigned int), s);
     // empty delta-CSR with per-row headroom (cpu_backend.cpp:380-389)
     h->idx_budget = (int64_t)max_weights * 8 + 4096;
     h->val_budget = (int64_t)max_weights + 64;
@@ -888,6 +897,7 @@ int b4_relayout(sili_layer* h, const std::vector<int64_t>& newcap, cudaStream_t 
     CK(cudaStreamSynchronize(s));
     h->b4_bc.swap(nbc); h->b4_tile.swap(ntile); h->b4_sparse.swap(nsp);
     h->b4_dirty = true;
+    h->b4_pmap_dirty = true;
     return SILI_OK;
 }
 
@@ -1077,10 +1087,12 @@ int sili_layer_destroy(sili_layer* h) {
     return SILI_OK;
 }
 
+static int check_tc_err(sili_layer* h);
+
 int sili_layer_sync(sili_layer* h) {
     RC(use(h));
     CK(cudaStreamSynchronize(h->stream));
-    return SILI_OK;
+    return check_tc_err(h);
 }
 
 int sili_layer_seed_rng(sili_layer* h, uint64_t seed) {
@@ -1202,6 +1214,29 @@ int sili_layer_set_scale(sili_layer* h, int kind, int index, int k, float v) {
     return SILI_OK;
 }
 
+static float* scale_ptr(sili_layer* h, int kind, int64_t* n_entities, int* stride);
+
+int sili_layer_set_scales(sili_layer* h, int kind, const float* v, int n) {
+    RC(use(h));
+    if (n < 0 || (n > 0 && !v)) return fail(SILI_EINVAL, "set_scales: bad arguments");
+    if (kind != SILI_SCALE_VALUE && kind != SILI_SCALE_OUTPUT && kind != SILI_SCALE_IMPORTANCE &&
+        kind != SILI_SCALE_OUTPUT_IMPORTANCE)
+        return fail(SILI_EINVAL, "set_scales: kind must be value, output, importance or output importance");
+    int64_t ents;
+    int stride;
+    float* p = scale_ptr(h, kind, &ents, &stride);
+    if (n > ents * stride) return fail(SILI_EINVAL, "set_scales: more entries than the vector holds");
+    CK(cudaStreamSynchronize(h->stream));
+    if (kind == SILI_SCALE_VALUE) grow_logical(h, h->vs, h->n_vs, n, 1.0f);
+    if (kind == SILI_SCALE_OUTPUT) {
+        grow_logical(h, h->os, h->n_os, n, 1.0f);
+        if (n > 0) h->os_trainable = true;
+    }
+    if (n > 0) RC(to_dev(v, p, (size_t)n * 4, h->stream));
+    CK(cudaStreamSynchronize(h->stream));
+    return SILI_OK;
+}
+
 static float* scale_ptr(sili_layer* h, int kind, int64_t* n_entities, int* stride) {
     *stride = h->rank;
     switch (kind) {
@@ -1266,6 +1301,50 @@ int sili_layer_rescale_row(sili_layer* h, int kind, int row, float new_scale) {
 }
 
 // ── compute ─────────────────────────────────────────────────────────────────
+// A tensor-core kernel's bounded wait that gave up (the word it sets),
+// reported once as SILI_ETIMEOUT at the next synchronising call.
+static int check_tc_err(sili_layer* h) {
+    unsigned int e = 0;
+    CK(cudaMemcpy(&e, h->tc_err.p, sizeof(e), cudaMemcpyDeviceToHost));
+    if (e) {
+        CK(cudaMemset(h->tc_err.p, 0, sizeof(e)));
+        return fail(SILI_ETIMEOUT, "block4 tensor-core forward: a bounded device-side wait gave up");
+    }
+    return SILI_OK;
+}
+
+// The panel map costs n_in * n_out / 4 bytes; past this many entries (1 GiB)
+// the tensor-core forward is not taken.
+constexpr int64_t kB4PanelMapMax = (int64_t)1 << 28;
+
+// The block4 part of forward_dense: on the tensor cores when the layer asks
+// for it and the shape allows (rank 1, batch >= 16), else the exact
+// CUDA-core kernel.
+static int b4_forward(sili_layer* h, const float* xT, int batch, float* y, cudaStream_t s) {
+    const LayerView v = h->view();
+    const B4View V = h->b4view();
+    if (h->b4_tc && b4_tc_applies(v, V, batch) && b4_tc_pmap_elems(v) <= kB4PanelMapMax) {
+        if (h->b4_pmap_dirty) {
+            RC(h->b4_pmap.reserve(b4_tc_pmap_elems(v) + 1));
+            launch_b4_panel_map(v, V, h->b4_pmap.p, s);
+            h->b4_pmap_dirty = false;
+        }
+        int ks = 1;
+        const int64_t nf = b4_tc_scratch_floats(v, batch, &ks);
+        RC(h->b4_part.reserve(nf + 1));
+        RC(h->b4_xs.reserve(b4_tc_xsplit_elems(v, batch) + 8));
+        return launch_b4_forward_tc(v, V, xT, batch, y, h->b4_xs.p, h->b4_part.p, ks, h->b4_pmap.p, h->tc_err.p, s);
+    }
+    launch_b4_forward(v, V, xT, batch, y, s);
+    return SILI_OK;
+}
+
+int sili_layer_set_b4_tensor_cores(sili_layer* h, int enable) {
+    RC(use(h));
+    h->b4_tc = enable != 0;
+    return SILI_OK;
+}
+
 int sili_layer_forward_dense(sili_layer* h, const float* x, int batch, float* y, void* stream) {
     RC(use(h));
     if (batch < 0 || !x || !y) return fail(SILI_EINVAL, "forward_dense: bad arguments");
@@ -1285,13 +1364,112 @@ int sili_layer_forward_dense(sili_layer* h, const float* x, int batch, float* y,
     RC(forward_columns(h, h->xT.p, batch, yd, false, s));
     if (h->b4_ntiles > 0) {
         RC(ensure_b4_index(h, s));
-        launch_b4_forward(h->view(), h->b4view(), h->xT.p, batch, yd, s);
+        RC(b4_forward(h, h->xT.p, batch, yd, s));
     }
     if (h->timing) { CK(cudaEventRecord(h->ev[1], s)); h->ev_fwd = true; }
     CK(cudaGetLastError());
     if (!dev_out) {
         CK(cudaMemcpyAsync(y, yd, (size_t)batch * n_out * 4, cudaMemcpyDeviceToHost, s));
     }
+    if (!dev_out || !is_device_ptr(x)) {
+        CK(cudaStreamSynchronize(s));
+        RC(check_tc_err(h));
+    }
+    return SILI_OK;
+}
+
+// FoldedLayer.forward (sili/sparse_rnn.py:1096-1125) over its suffix layers:
+// one transposed copy of x for all of them (every layer keeps it as its
+// last input, as each layer's forward_dense would), then one launch of
+// k_folded_cols where its shape rules hold, else each layer's forward into
+// a raw buffer, the suffix sum and the fold sum.  The sums are the
+// reference's: raw = 0 + raw_0 + raw_1 + ... (Python's sum), y[b, j] = raw
+// folds added in ascending order (numpy's reduction over the fold axis).
+int sili_folded_forward(sili_layer* const* layers, int n_layers, const float* x, int batch, int n_folds,
+                        int64_t out_dim, int fold_sum, float* y, void* stream) {
+    if (!layers || n_layers < 1 || batch < 0 || n_folds < 1 || out_dim < 1 || !x || !y)
+        return fail(SILI_EINVAL, "folded_forward: bad arguments");
+    sili_layer* h0 = layers[0];
+    RC(use(h0));
+    for (int k = 0; k < n_layers; ++k) {
+        sili_layer* h = layers[k];
+        if (!h) return fail(SILI_EINVAL, "folded_forward: null layer");
+        if (h->dev != h0->dev || h->rows != h0->rows || h->cols != (int64_t)n_folds * out_dim)
+            return fail(SILI_EINVAL, "folded_forward: every suffix layer must be n_in -> n_folds * out_dim on one device");
+    }
+    cudaStream_t s = pick(h0, stream);
+    const int64_t n_in = h0->rows, n_cols = h0->cols;
+    for (int k = 0; k < n_layers; ++k) RC(ensure_aux(layers[k], s));
+    RC(stage_transposed(h0, x, batch, n_in, h0->xT, s));
+    h0->last_batch = batch;
+    for (int k = 1; k < n_layers; ++k) {
+        sili_layer* h = layers[k];
+        RC(h->xT.reserve((int64_t)batch * n_in + batch + 1));
+        CK(cudaMemcpyAsync(h->xT.p, h0->xT.p, (size_t)(batch * n_in + batch) * 4, cudaMemcpyDeviceToDevice, s));
+        h->last_batch = batch;
+    }
+    const int64_t y_count = (int64_t)batch * (fold_sum ? out_dim : n_cols);
+    const bool dev_out = is_device_ptr(y);
+    float* yd = y;
+    if (!dev_out) {
+        RC(h0->ytmp.reserve(y_count + 1));
+        yd = h0->ytmp.p;
+    }
+    FoldedView F;
+    F.ns = n_layers;
+    F.n_in = (int)n_in;
+    F.n_cols = n_cols;
+    F.out_dim = out_dim;
+    F.n_folds = n_folds;
+    F.fold_sum = fold_sum != 0;
+    // one suffix: the stacked layer's own forward and the fold sum in two
+    // launches measured faster than the one-launch kernel on config 5's
+    // shards at 1-8 ranks (the row-tiled forward keeps three 256-thread CTAs
+    // per SM; the fold-grouped CTAs of k_folded_cols fewer); two to four
+    // suffixes share one x staging in k_folded_cols
+    bool fused = n_layers >= 2 && n_layers <= kFoldedMaxSuffixes && batch > 0;
+    for (int k = 0; k < n_layers && fused; ++k) {
+        sili_layer* h = layers[k];
+        if (h->rank != 1 || h->b4_ntiles > 0 || h->total_nnz == 0) { fused = false; break; }
+        const int64_t bound = std::max<int64_t>(h->total_nnz, 1) + 7 * h->cols + 8;
+        if (!h->pack_valid) {
+            RC(h->cpack.reserve(bound));
+            launch_pack_csc(h->view(), bound, h->cpack.p, s);
+            h->pack_valid = true;
+        }
+        F.colptr[k] = h->colptr.p; F.colptr_x[k] = h->colptr_x.p; F.cpack[k] = h->cpack.p;
+        F.vs[k] = h->vs.p; F.os[k] = h->os.p;
+    }
+    if (h0->timing) CK(cudaEventRecord(h0->ev[0], s));
+    if (!(fused && launch_folded_forward(F, h0->xT.p, batch, yd, s))) {
+        // each layer's own forward into raw, then the sums
+        const int64_t raw_count = (int64_t)batch * n_cols;
+        DBuf<float>& raws = h0->fold_raw;   // kept across calls (no allocation per step)
+        RC(raws.reserve(raw_count * n_layers + 1));
+        std::vector<const float*> rp((size_t)n_layers);
+        for (int k = 0; k < n_layers; ++k) {
+            sili_layer* h = layers[k];
+            float* rk = raws.p + raw_count * k;
+            RC(forward_columns(h, h0->xT.p, batch, rk, false, s));
+            if (h->b4_ntiles > 0) {
+                RC(ensure_b4_index(h, s));
+                launch_b4_forward(h->view(), h->b4view(), h0->xT.p, batch, rk, s);
+            }
+            rp[(size_t)k] = rk;
+        }
+        float* sum = fold_sum ? raws.p : yd;   // the suffix sum in place over raw_0 when folding after
+        launch_suffix_sum(rp.data(), std::min(n_layers, kFoldedMaxSuffixes), raw_count, sum, s);
+        for (int k0 = kFoldedMaxSuffixes; k0 < n_layers; k0 += kFoldedMaxSuffixes - 1) {
+            std::vector<const float*> more = {sum};
+            for (int k = k0; k < std::min(n_layers, k0 + kFoldedMaxSuffixes - 1); ++k) more.push_back(rp[(size_t)k]);
+            launch_suffix_sum(more.data(), (int)more.size(), raw_count, sum, s);
+        }
+        if (fold_sum) launch_fold_sum(sum, batch, n_folds, out_dim, yd, s);
+        CK(cudaGetLastError());
+    }
+    if (h0->timing) { CK(cudaEventRecord(h0->ev[1], s)); h0->ev_fwd = true; }
+    CK(cudaGetLastError());
+    if (!dev_out) CK(cudaMemcpyAsync(y, yd, (size_t)y_count * 4, cudaMemcpyDeviceToHost, s));
     if (!dev_out || !is_device_ptr(x)) CK(cudaStreamSynchronize(s));
     return SILI_OK;
 }
@@ -1750,6 +1928,7 @@ int sili_layer_synap_rows(sili_layer* h, int row0, int nrows, float importance_c
         h->total_nnz += (int64_t)res[2];
         h->aux_dirty = true;
         h->b4_dirty = true;
+    h->b4_pmap_dirty = true;
         std::vector<int> nt((size_t)BR + 1, 0);
         if (BR > 0) CK(cudaMemcpyAsync(nt.data(), h->b4_nt.p, (size_t)BR * 4, cudaMemcpyDeviceToHost, s));
         CK(cudaStreamSynchronize(s));
@@ -2475,6 +2654,7 @@ int sili_layer_load_dense_codes(sili_layer* h, const uint8_t* wc, const uint8_t*
     RC(b4_put_allocs(h, a, s));
     h->b4_ntiles = BR * BC;
     h->b4_dirty = true;
+    h->b4_pmap_dirty = true;
     // out_degree[c] = n_in for every column (cpu_backend.cpp:916-920)
     std::vector<int> od((size_t)h->cols + 1, (int)h->rows);
     if (h->cols > 0) CK(cudaMemcpyAsync(h->out_degree.p, od.data(), (size_t)h->cols * 4, cudaMemcpyHostToDevice, s));

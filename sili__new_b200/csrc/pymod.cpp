@@ -7,6 +7,7 @@
 // The *_ptr methods take device pointers (e.g. torch CUDA tensors'
 // data_ptr()) and enqueue work on a CUDA stream without copies.
 #include <pybind11/numpy.h>
+#include <pybind11/stl.h>
 #include <pybind11/pybind11.h>
 
 #include <cmath>
@@ -494,6 +495,15 @@ void bind_layer(py::module_& m, const char* name) {
              py::arg("col"), py::arg("k"), py::arg("v"))
         .def("get_scale", &T::get_scale, py::arg("row"), py::arg("col"))
         .def("set_value_scale_raw", [](T& s, int r, float v) { s.ss(SILI_SCALE_VALUE, r, 0, v); }, py::arg("row"), py::arg("scale"))
+        .def("set_block4_tensor_cores", [](T& s, bool enable) {
+            check(sili_layer_set_b4_tensor_cores(s.h, enable ? 1 : 0));
+        }, py::arg("enable"))
+        .def("set_scales", [](T& s, int kind, farr v) {
+            check(sili_layer_set_scales(s.h, kind, v.data(), (int)v.size()));
+        }, py::arg("kind"), py::arg("values"))
+        .def("set_scales_ptr", [](T& s, int kind, uintptr_t v, int n) {
+            check(sili_layer_set_scales(s.h, kind, (const float*)v, n));
+        }, py::arg("kind"), py::arg("values_ptr"), py::arg("n"))
         .def("set_importance_scale_raw", [](T& s, int r, float v) { s.ss(SILI_SCALE_IMPORTANCE, r, 0, v); },
              py::arg("row"), py::arg("scale"))
         .def("get_output_scale", [](T& s, int c) { return s.gs(SILI_SCALE_OUTPUT, c, 0); }, py::arg("col"))
@@ -616,6 +626,75 @@ PYBIND11_MODULE(_cuda, m) {
         return py::make_tuple(p, i, v);
     }, py::arg("ptrs_a"), py::arg("idx_a"), py::arg("vals_a"), py::arg("ptrs_b"), py::arg("idx_b"), py::arg("vals_b"),
        py::arg("n_rows"), py::arg("prefer") = "a", py::arg("num_cpus") = 4);
+    // FoldedLayer.forward over its suffix layers in one call
+    auto handles = [](py::list layers) {
+        std::vector<sili_layer*> hs;
+        for (auto o : layers) {
+            if (py::isinstance<LayerT<true>>(o)) hs.push_back(o.cast<LayerT<true>&>().h);
+            else if (py::isinstance<LayerT<false>>(o)) hs.push_back(o.cast<LayerT<false>&>().h);
+            else throw py::type_error("folded_forward: layers must be this module's SparseLinearLayer objects");
+        }
+        if (hs.empty()) throw py::value_error("folded_forward: no layers");
+        return hs;
+    };
+    m.def("folded_forward", [handles](py::list layers, farr x, int n_folds, int64_t out_dim, bool fold_sum) {
+        auto hs = handles(layers);
+        auto b = x.request();
+        const int batch = b.ndim == 2 ? (int)b.shape[0] : 1;
+        int64_t n_in = 0;
+        {
+            int64_t sz[6];
+            check(sili_layer_sizes(hs[0], sz));
+            n_in = sz[0];
+        }
+        if ((int64_t)b.size != (int64_t)batch * n_in) throw py::value_error("folded_forward: x must be [batch, n_inputs]");
+        const int64_t w = fold_sum ? out_dim : (int64_t)n_folds * out_dim;
+        py::array_t<float> y({(py::ssize_t)batch, (py::ssize_t)w});
+        check(sili_folded_forward(hs.data(), (int)hs.size(), x.data(), batch, n_folds, out_dim, fold_sum ? 1 : 0,
+                                  y.mutable_data(), nullptr));
+        return y;
+    }, py::arg("layers"), py::arg("x"), py::arg("n_folds"), py::arg("out_dim"), py::arg("fold_sum") = true);
+    m.def("folded_forward_ptr", [handles](py::list layers, uintptr_t x, int batch, int n_folds, int64_t out_dim,
+                                          bool fold_sum, uintptr_t y, uintptr_t stream) {
+        auto hs = handles(layers);
+        check(sili_folded_forward(hs.data(), (int)hs.size(), (const float*)x, batch, n_folds, out_dim,
+                                  fold_sum ? 1 : 0, (float*)y, (void*)stream));
+    }, py::arg("layers"), py::arg("x"), py::arg("batch"), py::arg("n_folds"), py::arg("out_dim"), py::arg("fold_sum"),
+       py::arg("y"), py::arg("stream") = 0);
+    // conversion-time CSR operations on device arrays (sili__new_b200.convert)
+    m.def("prune_to_csr_ptr", [](uintptr_t w, int64_t rows, int64_t cols, float min_abs, uintptr_t ptrs, uintptr_t idx,
+                                 uintptr_t vals, uintptr_t stream) {
+        int64_t n = 0;
+        check(sili_prune_to_csr((const float*)w, rows, cols, min_abs, (int*)ptrs, (int*)idx, (float*)vals, &n,
+                                (void*)stream));
+        return n;
+    }, py::arg("w"), py::arg("rows"), py::arg("cols"), py::arg("min_abs"), py::arg("ptrs"), py::arg("idx") = 0,
+       py::arg("vals") = 0, py::arg("stream") = 0);
+    m.def("csr_transpose_ptr", [](uintptr_t p, uintptr_t i, uintptr_t v, int n_rows, int n_cols, uintptr_t op,
+                                  uintptr_t oi, uintptr_t ov, uintptr_t stream) {
+        check(sili_csr_transpose((const int*)p, (const int*)i, (const float*)v, n_rows, n_cols, (int*)op, (int*)oi,
+                                 (float*)ov, (void*)stream));
+    });
+    m.def("csr_stack_vertical_ptr", [](std::vector<uintptr_t> p, std::vector<uintptr_t> i, std::vector<uintptr_t> v,
+                                       std::vector<int> rows, uintptr_t op, uintptr_t oi, uintptr_t ov, uintptr_t stream) {
+        if (p.size() != i.size() || p.size() != v.size() || p.size() != rows.size())
+            throw py::value_error("csr_stack_vertical: one ptrs / idx / vals / rows entry per part");
+        std::vector<const int*> pp(p.size()), ii(p.size());
+        std::vector<const float*> vv(p.size());
+        for (size_t k = 0; k < p.size(); ++k) { pp[k] = (const int*)p[k]; ii[k] = (const int*)i[k]; vv[k] = (const float*)v[k]; }
+        check(sili_csr_stack_vertical((int)p.size(), pp.data(), ii.data(), vv.data(), rows.data(), (int*)op, (int*)oi,
+                                      (float*)ov, (void*)stream));
+    });
+    m.def("fit_rank1_envelope_ptr", [](uintptr_t p, uintptr_t i, uintptr_t v, int n_rows, int n_cols, int n_iters,
+                                       uintptr_t rs, uintptr_t cs, uintptr_t stream) {
+        check(sili_fit_rank1_envelope((const int*)p, (const int*)i, (const float*)v, n_rows, n_cols, n_iters,
+                                      (float*)rs, (float*)cs, (void*)stream));
+    });
+    m.def("fp4_row_rescale_ptr", [](uintptr_t p, uintptr_t i, uintptr_t v, int n_rows, int mode, uintptr_t cs,
+                                    uintptr_t rs, uintptr_t stream) {
+        check(sili_fp4_row_rescale((const int*)p, (const int*)i, (float*)v, n_rows, mode, (const float*)cs,
+                                   (float*)rs, (void*)stream));
+    });
     // attention.hpp's kernels with the reference's signatures (cpu_backend.cpp:3384-3468)
     auto td = [](const farr& a, const char* who) {
         auto b = a.request();
