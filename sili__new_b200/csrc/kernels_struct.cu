@@ -489,6 +489,24 @@ void launch_fold_sum(const float* raw, int B, int n_folds, int64_t out_dim, floa
     k_fold_sum<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(raw, B, n_folds, out_dim, y);
     count_launch();
 }
+// FoldedLayer's suffix sum (Python's sum over the suffix outputs,
+// sili/sparse_rnn.py:1120-1122): y = 0 + raw_0 + raw_1 + ..., elementwise
+struct RawPtrs { const float* p[kFoldedMaxSuffixes]; };
+__global__ void k_suffix_sum(RawPtrs R, int n, int64_t count, float* __restrict__ y) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= count) return;
+    float a = 0.0f;
+    for (int k = 0; k < n; ++k) a = __fadd_rn(a, R.p[k][i]);
+    y[i] = a;
+}
+void launch_suffix_sum(const float* const* raws, int n, int64_t count, float* y, cudaStream_t s) {
+    if (count == 0 || n <= 0) return;
+    RawPtrs R{};
+    for (int k = 0; k < n && k < kFoldedMaxSuffixes; ++k) R.p[k] = raws[k];
+    k_suffix_sum<<<(unsigned)((count + 255) / 256), 256, 0, s>>>(R, n < kFoldedMaxSuffixes ? n : kFoldedMaxSuffixes,
+                                                                 count, y);
+    count_launch();
+}
 // its backward for one column slice: raw[b, f * w + j] = dy[b, j0 + j]
 // (the np.tile of sili/sparse_rnn.py:1144-1148), one thread per output float
 __global__ void k_fold_broadcast(const float* __restrict__ dy, int B, int64_t out_dim, int64_t j0, int64_t w,

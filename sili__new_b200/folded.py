@@ -33,6 +33,11 @@ from dataclasses import dataclass, field
 import numpy as np
 
 
+def _scale_kind_value():
+    from . import _cuda
+    return _cuda.SCALE_VALUE
+
+
 def column_slice(out_dim: int, rank: int, world: int) -> tuple[int, int]:
     """Output columns [j0, j1) of one rank; slices are equal width (the last
     may be short or empty) so the gather is a plain all_gather."""
@@ -78,7 +83,7 @@ class Suffix:
     j0: int = 0
     j1: int = 0
     layer: object = None
-    raw: object = None      # device scratch [B, n_folds * width]
+    raw: object = None      # device scratch [B, width] (fold-summed slice) or the placeholder's output
     part: object = None     # device slice of the output [B, width]
     gathered: object = None  # device [world, B, slice]
     dyraw: object = None    # device [B, n_folds * width]: dy broadcast over the folds
@@ -120,8 +125,12 @@ class FoldedStack:
             p.layer.load_weights_ptr(ptrs.data_ptr(), idx.data_ptr(), vals.data_ptr(), int(nnz))
         else:
             p.layer.load_weights(ptrs, idx, vals)
-        for r in range(p.in_dim):
-            p.layer.set_value_scale_raw(r, float(value_scale))
+        if hasattr(p.layer, "set_scales"):
+            # every row's value_scale in one copy (set_value_scale_raw per row, in bulk)
+            p.layer.set_scales(_scale_kind_value(), np.full(p.in_dim, np.float32(value_scale), np.float32))
+        else:
+            for r in range(p.in_dim):
+                p.layer.set_value_scale_raw(r, float(value_scale))
         if self.world > 1:
             # the rows' synapse counts over the whole stack (every rank holds
             # every row): the learning-rate divisor and the dead-row test
@@ -220,28 +229,76 @@ class FoldedStack:
         from . import _cuda
         p = self.parts[name]
         b = x.shape[0]
-        w = self.width(name)
         s = -(-p.out_dim // self.world)
-        if p.raw is None or p.raw.shape[0] != b:
-            p.raw = torch.empty(b, max(self.n_folds * w, 1), device=x.device)
+        if p.part is None or p.part.shape[0] != b:
             p.part = torch.zeros(b, s, device=x.device)
             p.gathered = torch.empty(self.world, b, s, device=x.device)
-        # a rank with no columns still runs its placeholder layer (one zero
-        # column) so that it holds the input its backward needs
-        p.layer.forward_dense_ptr(x.data_ptr(), b, p.raw.data_ptr(), stream.cuda_stream)
-        if w > 0:
-            if w == s:
-                _cuda.fold_sum_ptr(p.raw.data_ptr(), b, self.n_folds, w, p.part.data_ptr(), stream.cuda_stream)
-            else:
-                tmp = torch.empty(b, w, device=x.device)
-                _cuda.fold_sum_ptr(p.raw.data_ptr(), b, self.n_folds, w, tmp.data_ptr(), stream.cuda_stream)
-                p.part[:, :w].copy_(tmp)
+        self._forward_part(name, x, p.part, stream)
         if self.world == 1:
             return p.part[:, : p.out_dim]
         import torch.distributed as dist
         with torch.cuda.stream(stream):
             dist.all_gather_into_tensor(p.gathered, p.part, group=self.group)
         return p.gathered.permute(1, 0, 2).reshape(b, self.world * s)[:, : p.out_dim]
+
+    def _forward_part(self, name: str, x, part, stream):
+        """This rank's slice of the fold-summed output of one suffix into
+        part [B, s] (columns past the rank's width stay zero): the stacked
+        layer's forward and the fold sum in one call (sili_folded_forward)."""
+        import torch
+        from . import _cuda
+        p = self.parts[name]
+        b = x.shape[0]
+        w = self.width(name)
+        s = part.shape[1]
+        if w == 0:
+            # a rank with no columns still runs its placeholder layer (one
+            # zero column) so that it holds the input its backward needs
+            if p.raw is None or p.raw.shape[0] != b:
+                p.raw = torch.empty(b, 1, device=x.device)
+            p.layer.forward_dense_ptr(x.data_ptr(), b, p.raw.data_ptr(), stream.cuda_stream)
+            return
+        if w == s and part.is_contiguous():
+            _cuda.folded_forward_ptr([p.layer], x.data_ptr(), b, self.n_folds, w, True, part.data_ptr(),
+                                     stream.cuda_stream)
+        else:
+            if p.raw is None or p.raw.shape != (b, w):
+                p.raw = torch.empty(b, w, device=x.device)
+            _cuda.folded_forward_ptr([p.layer], x.data_ptr(), b, self.n_folds, w, True, p.raw.data_ptr(),
+                                     stream.cuda_stream)
+            with torch.cuda.stream(stream):
+                part[:, :w].copy_(p.raw)
+
+    def forward_group(self, names, xs: dict, stream) -> dict:
+        """forward_device of several suffixes with ONE all-gather: each
+        suffix's slice [B, s_i] is written to its block of one buffer
+        (blocks back to back), the buffer is gathered once and split.
+        xs: {name: x [B, in_dim] on `stream`}; returns {name: [B, out_dim]}."""
+        import torch
+        names = list(names)
+        b = xs[names[0]].shape[0]
+        sl = [-(-self.parts[n].out_dim // self.world) for n in names]
+        total = sum(b * si for si in sl)
+        key = (tuple(names), b)
+        bufs = self._group_bufs = getattr(self, "_group_bufs", {})
+        if key not in bufs:
+            dev = xs[names[0]].device
+            bufs[key] = (torch.zeros(total, device=dev), torch.empty(self.world, total, device=dev))
+        flat, gathered = bufs[key]
+        off = 0
+        views = []
+        for n, si in zip(names, sl):
+            part = flat[off: off + b * si].view(b, si)
+            self._forward_part(n, xs[n], part, stream)
+            views.append((n, off, si))
+            off += b * si
+        if self.world == 1:
+            return {n: flat[o: o + b * si].view(b, si)[:, : self.parts[n].out_dim] for n, o, si in views}
+        import torch.distributed as dist
+        with torch.cuda.stream(stream):
+            dist.all_gather_into_tensor(gathered, flat, group=self.group)
+        return {n: gathered[:, o: o + b * si].reshape(self.world, b, si).permute(1, 0, 2).reshape(b, self.world * si)
+                [:, : self.parts[n].out_dim] for n, o, si in views}
 
     def backward_device(self, name: str, dy, lr: float, stream, lr_per_row_nnz: bool = True,
                         damp_by_importance: bool = True, beta2: float = 0.999, eps: float = 1e-8):

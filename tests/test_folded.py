@@ -390,9 +390,14 @@ def _decode_outputs(rank, world, dev):
     stream = torch.cuda.Stream(device=dev)
     out = {}
     with torch.cuda.stream(stream):
-        for name, (in_dim, _) in suffixes.items():
-            x = torch.from_numpy(np.random.default_rng(in_dim).normal(0, 1, (DECODE_B, in_dim)).astype(np.float32))
-            out[name] = st.forward_device(name, x.cuda(dev), stream).cpu().numpy().copy()
+        xs = {name: torch.from_numpy(np.random.default_rng(in_dim).normal(0, 1, (DECODE_B, in_dim))
+                                     .astype(np.float32)).cuda(dev) for name, (in_dim, _) in suffixes.items()}
+        for name in suffixes:
+            out[name] = st.forward_device(name, xs[name], stream).cpu().numpy().copy()
+        # the same outputs with one all-gather per suffix group
+        for group in (["q_proj", "k_proj", "v_proj"], ["o_proj"], ["gate_proj", "up_proj"], ["down_proj"]):
+            for name, y in st.forward_group(group, xs, stream).items():
+                out["grouped_" + name] = y.cpu().numpy().copy()
     stream.synchronize()
     return out
 
@@ -416,7 +421,8 @@ def test_sharded_decode_two_nccl_ranks(tmp_path):
     """Config 5's decode forward column-sharded over two NCCL ranks equals
     the unsharded stack bit for bit (column sharding does not reorder any
     sum: each output column's rows are summed in ascending order, the folds
-    in ascending order, on whichever rank holds the column)."""
+    in ascending order, on whichever rank holds the column), with one
+    all-gather per suffix and with one per suffix group."""
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
@@ -426,3 +432,52 @@ def test_sharded_decode_two_nccl_ranks(tmp_path):
     want = _decode_outputs(0, 1, 0)
     for name, y in want.items():
         assert np.array_equal(got[name], y), name
+        if name.startswith("grouped_"):
+            assert np.array_equal(y, want[name[len("grouped_"):]]), name
+
+
+# ── FoldedLayer.forward in one call (sili_folded_forward) ──────────────────
+@pytest.mark.gpu
+@pytest.mark.parametrize("ns,n_folds,out_dim,B,fold_sum", [(1, 40, 24, 32, True), (2, 3, 200, 64, True),
+                                                           (3, 7, 50, 16, True), (2, 5, 60, 32, False),
+                                                           (1, 300, 2, 32, True), (2, 4, 30, 7, True),
+                                                           (5, 3, 20, 32, True)])
+def test_folded_forward_matches_reference_sums(ns, n_folds, out_dim, B, fold_sum):
+    """The fused FoldedLayer forward equals the reference's composition --
+    each suffix layer's forward_dense, Python's sum over the suffixes, numpy's
+    sum over the fold axis (sili/sparse_rnn.py:1116-1125) -- bit for bit
+    (batch >= 9), both through the one-launch kernel (up to four suffixes,
+    batch a multiple of 4 and >= 16, at most 256 folds) and the fallback."""
+    import sili__new_b200 as S
+    n_in = 96
+    layers = []
+    for k in range(ns):
+        p, i, w, vs = random_layer(n_in, n_folds * out_dim, 20, seed=10 * k + n_folds)
+        L = S.SparseLinearLayerDeterministic(n_in, n_folds * out_dim, len(i) * 2)
+        L.load_weights(p, i, w)
+        for r in range(n_in):
+            L.set_value_scale_raw(r, float(vs[r]))
+        layers.append(L)
+    x = np.random.default_rng(ns + B).normal(0, 1, (B, n_in)).astype(np.float32)
+    raw = sum(L.forward_dense(x) for L in layers)
+    want = raw.reshape(B, n_folds, out_dim).sum(axis=1) if fold_sum else raw
+    got = S._cuda.folded_forward(layers, x, n_folds, out_dim, fold_sum)
+    if B >= 9:
+        assert np.array_equal(got, want)
+    else:
+        np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-6)
+    # every layer keeps x as its last input: backward_dense works after it
+    dy = np.ones((B, n_folds * out_dim), np.float32)
+    for L in layers:
+        assert L.last_input.shape == (B, n_in)
+        L.backward_dense(dy, 0.0)
+
+
+@pytest.mark.gpu
+def test_forward_group_matches_forward_device():
+    """forward_group (one gather buffer for several suffixes) equals
+    forward_device per suffix, world 1."""
+    r = _decode_outputs(0, 1, 0)
+    for name in list(r):
+        if name.startswith("grouped_"):
+            assert np.array_equal(r[name], r[name[len("grouped_"):]]), name
