@@ -204,9 +204,12 @@ const PlanOverride& plan_override() {
     return o;
 }
 
-// 32 samples per thread; 256-thread CTAs when that still gives every SM two
-// CTAs, else 128; no plan (threads 0) for narrower layers, where the
-// per-synapse gathers of k_forward_vec win (a CTA re-reads all of x).
+// 32 samples per thread in 256-thread CTAs when that gives every SM two CTAs;
+// no plan (threads 0) for narrower layers, where the per-synapse gathers of
+// k_forward_vec win (a CTA re-reads all of x).  128-thread CTAs for layers
+// between 148 and 296 CTAs wide measured slower than k_forward_vec on every
+// config-5 shard they served (q / o / down at 4 ranks: 0.213 / 0.178 / 1.736
+// ms against about 0.18 / 0.17 / 1.13).
 ColsPlan cols_plan(const LayerView& L, int B) {
     ColsPlan p;
     if (L.rank != 1 || B < 16 || (B & 3) != 0 || L.n_in >= (1 << 27) || L.n_out == 0 || L.n_in == 0) return p;
@@ -219,14 +222,11 @@ ColsPlan cols_plan(const LayerView& L, int B) {
     }
     const int sg = 32;
     const int64_t sgroups = (B + sg - 1) / sg;
-    int t = 256;
-    if (((L.n_out + t - 1) / t) * sgroups < 2 * 148) t = 128;
+    const int t = 256;
     if (((L.n_out + t - 1) / t) * sgroups < 2 * 148) return p;
     p.threads = t;
     p.sg = sg;
-    // x tile: 128 bytes per row, 64 KB (3 CTAs per SM).  Smaller tiles for
-    // 128-thread CTAs (more CTAs per SM) measured no faster: the per-tile
-    // maximum of the lanes' entry counts grows relative to the mean.
+    // x tile: 128 bytes per row, 64 KB (3 CTAs per SM)
     p.rt = (int)std::min<int64_t>(L.n_in, 512);
     return p;
 }
