@@ -73,6 +73,11 @@ struct DBuf {
         return SILI_OK;
     }
     void swap(DBuf& o) { std::swap(p, o.p); std::swap(cap, o.cap); }
+    void release() {                    // frees the memory (waits for its users, as cudaFree does)
+        if (p) cudaFree(p);
+        p = nullptr;
+        cap = 0;
+    }
 };
 
 // FP4_TABLE (fp4quant.hpp:16-33), code 8 = NaN
@@ -340,6 +345,10 @@ int check_csr(const int* ptrs, const int* idx, int rows, int nnz, int64_t cols, 
 }
 
 // ── derived index: flat decode + CSC shadow ─────────────────────────────────
+// Rebuild scratch kept between rebuilds up to this size (smaller layers
+// rebuild often -- synaptogenesis steps -- and should not allocate each time).
+constexpr int64_t kRebuildKeepBytes = (int64_t)256 << 20;
+
 int ensure_aux(sili_layer* h, cudaStream_t s) {
     if (!h->aux_dirty) return SILI_OK;
     const int64_t R = h->rows, C = h->cols, nnz = h->total_nnz;
@@ -379,6 +388,14 @@ int ensure_aux(sili_layer* h, cudaStream_t s) {
                           h->crow.p, h->cvpos.p, h->fcpos.p, s);
     launch_pad_csc(h->colcount.p, h->colptr.p, C, (int)R, h->crow.p, h->cvpos.p, s);
     CK(cudaGetLastError());
+    // the rebuild's own arrays (24 bytes per synapse: the row and value
+    // position of every synapse, the sort's keys and values) are not read
+    // again until the next rebuild: a large layer gives them back, keeping
+    // only abs_cols, crow, cvpos, fcpos and cpack (20 bytes per synapse)
+    if ((int64_t)nz * 24 > kRebuildKeepBytes) {
+        h->frow.release(); h->fvpos.release();
+        h->sort_k.release(); h->sort_ko.release(); h->sort_v.release(); h->sort_vo.release();
+    }
     {   // rows with no synapse take the dead-row bootstrap (linear_disldo.hpp:1985-2042)
         std::vector<int> rp((size_t)R + 1);
         CK(cudaMemcpyAsync(rp.data(), h->rowptr.p, (size_t)(R + 1) * 4, cudaMemcpyDeviceToHost, s));
