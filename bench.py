@@ -271,6 +271,21 @@ def run_block4(args, dev, S, torch, work, cpu_sample):
         return e0.elapsed_time(e1) / steps
 
     f_exact, f_tc = fwd_ms(False), fwd_ms(True)
+
+    def dx_ms(tc):
+        # backward_dense at learning rate 0: dx alone (plus the accumulators)
+        L.set_block4_tensor_cores(tc)
+        L.forward_dense_ptr(xs.data_ptr(), BATCH, y.data_ptr(), sh)
+        for _ in range(3):
+            L.backward_dense_ptr(dys.data_ptr(), BATCH, 0.0, True, True, 0.999, 1e-8, dx.data_ptr(), sh, 0)
+        e0.record(stream)
+        for _ in range(steps):
+            L.backward_dense_ptr(dys.data_ptr(), BATCH, 0.0, True, True, 0.999, 1e-8, dx.data_ptr(), sh, 0)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / steps
+
+    d_exact, d_tc = dx_ms(False), dx_ms(True)
     # the training step with the tensor-core forward (the update is the same)
     L.set_block4_tensor_cores(True)
     for _ in range(2):
@@ -291,7 +306,7 @@ def run_block4(args, dev, S, torch, work, cpu_sample):
     out = {"metric": "block4 format fwd+bwd effective GB/s (config 2 matrix in 4x4 FP4 tiles, batch 64)",
            "value": step_bytes / (ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms, "steps": steps,
            "ms_per_step_tc_forward": ms_tc, "fwd_ms": f_exact, "fwd_tc_ms": f_tc,
-           "fwd_tc_tflops": 3 * fwd_flop / (f_tc * 1e-3) / 1e12,
+           "fwd_tc_tflops": 3 * fwd_flop / (f_tc * 1e-3) / 1e12, "dx_lr0_ms": d_exact, "dx_lr0_tc_ms": d_tc,
            "tiles": tiles, "live_slots_at_load": int(np.count_nonzero(wc)), "bytes_per_step": step_bytes}
     del L, xs, dys, y, dx
     torch.cuda.empty_cache()
@@ -804,6 +819,7 @@ def main():
     ap.add_argument("--only", choices=["block4", "synap", "folded", "folded4", "rule", "spmv", "sparse", "shards"],
                     help="run one secondary measurement alone and print its object (profiling)")
     ap.add_argument("--detail", default=None, help="write every measurement's full object to this JSON file")
+    ap.add_argument("--shard-worlds", default="1,2,4,8", help="rank counts for --only shards")
     ap.add_argument("--folded-layers", type=int, default=None,
                     help="layers folded per suffix (default: config 5's 40; fewer for small profiling runs)")
     args = ap.parse_args()
@@ -855,7 +871,7 @@ def main():
         elif args.only == "spmv":
             out = run_spmv(S, torch, dev, cpu_sample=False)
         elif args.only == "shards":
-            out = run_shards(args, dev, S, torch)
+            out = run_shards(args, dev, S, torch, worlds=tuple(int(w) for w in args.shard_worlds.split(",")))
         elif args.only == "sparse":
             w0 = make_workload()
             out = run_sparse_variants([load_layer(S.SparseLinearLayer, *w0[:4], device=dev) for _ in range(4)], S, torch,
@@ -1089,7 +1105,7 @@ def compact_legs(block4, synap, rule, sparse_v, spmv, folded4):
     legs = {}
     if block4:
         legs["block4"] = {"ms": _r(block4["ms_per_step"]), "gbs": _r(block4["value"]), "cpu": _cpu_short(block4)}
-        for k in ("ms_per_step_tc_forward", "fwd_ms", "fwd_tc_ms", "fwd_tc_tflops"):
+        for k in ("ms_per_step_tc_forward", "fwd_ms", "fwd_tc_ms", "fwd_tc_tflops", "dx_lr0_ms", "dx_lr0_tc_ms"):
             if block4.get(k) is not None:
                 legs["block4"][k] = _r(block4[k])
     if synap:

@@ -237,12 +237,14 @@ int sili_layer_b4_expand_headroom(sili_layer* h, float blank_fraction, int64_t m
 /* the block4 half of equalizer_step (Block4Store::equalize_step,
  * block4.hpp:1208-1221); row is the block-row cursor */
 int sili_layer_b4_equalize_row(sili_layer* h, int64_t row);
-/* The block4 forward on the tensor cores (no counterpart in the reference,
- * whose block4 forward is linear_disldo.hpp:128-339): enable = 1 runs the
- * block4 part of forward_dense for rank-1 layers at batch >= 16 as
- * tcgen05 MMAs (FP4 codes exact in bf16, x * value_scale split into three
- * bf16 terms, fp32 accumulation) -- within fp32 summation tolerance of the
- * exact CUDA-core path, which is the default (enable = 0).  A bounded
+/* The block4 forward and lr = 0 dx on the tensor cores (no counterpart in
+ * the reference, whose block4 forward is linear_disldo.hpp:128-339 and
+ * block4 dx :1512-1703): enable = 1 runs the block4 part of forward_dense,
+ * and of backward_dense's dx at learning_rate 0, for rank-1 layers at batch
+ * >= 16 as tcgen05 MMAs (FP4 codes exact in bf16, x * value_scale or
+ * dy * output_scale split into three bf16 terms, fp32 accumulation) --
+ * within fp32 summation tolerance of the exact CUDA-core path, which is the
+ * default (enable = 0).  A bounded
  * device-side wait that gives up is reported as SILI_ETIMEOUT by the next
  * synchronising call (sili_layer_sync, or a forward with host arrays). */
 int sili_layer_set_b4_tensor_cores(sili_layer* h, int enable);

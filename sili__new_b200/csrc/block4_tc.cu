@@ -1,4 +1,9 @@
-// The block4 forward on the tensor cores (tcgen05, sm_100a).
+// The block4 forward and the lr = 0 block4 dx on the tensor cores (tcgen05,
+// sm_100a).  The text below speaks of the forward; the dx is the same
+// product transposed (linear_disldo.hpp:1512-1703 at lr = 0: dx[b, r] +=
+// vs[r] * sum_c fp4(w[r, c]) * (dy[b, c] * os[c])): panels over input rows,
+// chunks over output columns, the tile rows as the A operand's rows,
+// dy * os split into the three bf16 terms.
 //
 // disldo_forward's block4 part (linear_disldo.hpp:128-339) is, for scale
 // rank 1, y[b, c] += os[c] * sum_r (x[b, r] * vs[r]) * fp4(w[r, c]) over the
@@ -152,23 +157,23 @@ __device__ __forceinline__ uint32_t sw128_off(int m, int k) {
     return (uint32_t)((m >> 3) * 1024 + r * 128 + ((((k >> 3) ^ r) & 7) << 4) + (k & 7) * 2);
 }
 
+// The product D[m, n] = sum_k A[m, k] * B'[n, k] in either orientation: the
+// forward (m = output column, k = input row) or the lr = 0 dx (m = input row,
+// k = output column).
 struct TcArgs {
-    int64_t n_in, n_out;
+    int64_t M, K;           // output rows (columns of y, or rows of dx) and the summed dimension
     int B, groups;          // batch, batch groups of 64
-    int kslices;            // input-row slices (grid.y)
+    int kslices;            // slices of the summed dimension (grid.y)
     int chunks_per_slice;
-    int64_t BC;             // block-columns
-    const int* cptr;        // tile column index
-    const int* ctile;
-    const int* cbr;
     const uint4* tile;
-    const int* pmap;        // [panels][chunks][16 block-rows][32 block-columns] tile slot or -1
-    int64_t chunks;         // chunks of the input rows in all
-    float* part;            // [kslices][B][n_out] partial sums
+    const int* pmap;        // [panels][chunks][16 k-blocks][32 m-blocks] tile slot or -1
+    int64_t chunks;         // chunks of the summed dimension in all
+    float* part;            // [kslices][B][M] partial sums
     unsigned int* err;      // set when a wait gave up
 };
 
-__global__ void __launch_bounds__(128, 1) k_b4_forward_tc(const __grid_constant__ CUtensorMap xmap, TcArgs P) {
+template <bool DX>
+__global__ void __launch_bounds__(128, 1) k_b4_tc(const __grid_constant__ CUtensorMap xmap, TcArgs P) {
     extern __shared__ unsigned char tc_raw[];
     TcSmem& S = *reinterpret_cast<TcSmem*>((reinterpret_cast<uintptr_t>(tc_raw) + 1023) & ~(uintptr_t)1023);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -196,9 +201,9 @@ __global__ void __launch_bounds__(128, 1) k_b4_forward_tc(const __grid_constant_
     const uint32_t tmem = S.tmem_base;
 
     const int chunk0 = slice * P.chunks_per_slice;
-    // this thread's four tiles of a chunk: block-column panel * 32 + lane,
-    // block-rows 4 warp .. 4 warp + 3 of the chunk, through the panel map;
-    // the next chunk's are loaded while the current one is built
+    // this thread's four tiles of a chunk: m-block panel * 32 + lane, k-blocks
+    // 4 warp .. 4 warp + 3 of the chunk, through the panel map; the next
+    // chunk's are loaded while the current one is built
     const int* pm = P.pmap + ((int64_t)panel * P.chunks + chunk0) * 512 + warp * 128 + lane;
     uint4 nt[4];
     auto fetch = [&](int i) {
@@ -208,12 +213,14 @@ __global__ void __launch_bounds__(128, 1) k_b4_forward_tc(const __grid_constant_
 #pragma unroll
         for (int j = 0; j < 4; ++j) nt[j] = id[j] >= 0 ? P.tile[id[j]] : make_uint4(0, 0, 0, 0);
     };
-    const int64_t left = (P.n_in + kChunk - 1) / kChunk - chunk0;
+    const int64_t left = (P.K + kChunk - 1) / kChunk - chunk0;
     const int nchunks = (int)(left < P.chunks_per_slice ? left : P.chunks_per_slice);
     constexpr uint32_t idesc = idesc_bf16(kPanel, kN);
     bool ok = true;
-    uint32_t tma_phase[2] = {0, 0}, mma_phase[2] = {0, 0};
-    int issued[2] = {0, 0};   // MMA groups committed to each buffer and not yet waited for
+    // per buffer s, bit s: the barriers' phase parities and whether MMAs
+    // committed to the buffer are not yet waited for (bit masks, not arrays,
+    // so that they stay in registers)
+    uint32_t tma_phase = 0, mma_phase = 0, issued = 0;
     // Waits on the barriers are thread 0's; the other threads learn the
     // outcome at the next __syncthreads_and, so all threads leave the loop
     // together.
@@ -225,10 +232,10 @@ __global__ void __launch_bounds__(128, 1) k_b4_forward_tc(const __grid_constant_
         for (int j = 0; j < 4; ++j) ct[j] = nt[j];
         if (i + 1 < nchunks) fetch(i + 1);
         // the MMAs that read this buffer two chunks ago must be done
-        if (issued[s]) {
-            if (threadIdx.x == 0 && !mbar_wait(&S.mma_bar[s], mma_phase[s])) ok = false;
-            mma_phase[s] ^= 1;
-            issued[s] = 0;
+        if ((issued >> s) & 1u) {
+            if (threadIdx.x == 0 && !mbar_wait(&S.mma_bar[s], (mma_phase >> s) & 1u)) ok = false;
+            mma_phase ^= 1u << s;
+            issued &= ~(1u << s);
             ok = __syncthreads_and(ok ? 1 : 0) != 0;
             if (!ok) break;
         }
@@ -241,22 +248,29 @@ __global__ void __launch_bounds__(128, 1) k_b4_forward_tc(const __grid_constant_
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const uint4 t = ct[j];
-            const int k0 = 4 * (4 * warp + j);   // the tile's first row within the chunk
-            const uint32_t words[4] = {t.x, t.y, t.z, t.w};
+            const int k0 = 4 * (4 * warp + j);   // the tile's first k within the chunk
+            const uint32_t words[4] = {t.x, t.y, t.z, t.w};   // word lj holds slots lj*4 + li (bytes li)
 #pragma unroll
-            for (int lj = 0; lj < 4; ++lj) {
-                const uint32_t wd = words[lj];   // slots lj*4 + li, li = 0..3 (bytes)
-                const uint32_t h0 = S.ftab[wd & 0xFu], h1 = S.ftab[(wd >> 8) & 0xFu];
-                const uint32_t h2 = S.ftab[(wd >> 16) & 0xFu], h3 = S.ftab[(wd >> 24) & 0xFu];
-                const uint2 v = make_uint2(h0 | (h1 << 16), h2 | (h3 << 16));
-                *reinterpret_cast<uint2*>(A + sw128_off(lane * 4 + lj, k0)) = v;
+            for (int q = 0; q < 4; ++q) {
+                uint32_t h[4];
+                if (!DX) {
+                    // row m = column lj = q of the tile, k = its rows li = 0..3
+#pragma unroll
+                    for (int li = 0; li < 4; ++li) h[li] = S.ftab[(words[q] >> (8 * li)) & 0xFu];
+                } else {
+                    // row m = row li = q of the tile, k = its columns lj = 0..3
+#pragma unroll
+                    for (int lj = 0; lj < 4; ++lj) h[lj] = S.ftab[(words[lj] >> (8 * q)) & 0xFu];
+                }
+                const uint2 v = make_uint2(h[0] | (h[1] << 16), h[2] | (h[3] << 16));
+                *reinterpret_cast<uint2*>(A + sw128_off(lane * 4 + q, k0)) = v;
             }
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncthreads();
         bool mma_started = false;
         if (threadIdx.x == 0) {
-            if (!mbar_wait(&S.tma_bar[s], tma_phase[s])) {
+            if (!mbar_wait(&S.tma_bar[s], (tma_phase >> s) & 1u)) {
                 ok = false;
             } else {
                 asm volatile("tcgen05.fence::after_thread_sync;");
@@ -268,8 +282,8 @@ __global__ void __launch_bounds__(128, 1) k_b4_forward_tc(const __grid_constant_
                 mma_started = true;
             }
         }
-        tma_phase[s] ^= 1;
-        issued[s] = __syncthreads_or(mma_started ? 1 : 0);
+        tma_phase ^= 1u << s;
+        if (__syncthreads_or(mma_started ? 1 : 0)) issued |= 1u << s;
         // every thread learns whether thread 0's wait gave up
         ok = __syncthreads_and(ok ? 1 : 0) != 0;
     }
@@ -277,17 +291,17 @@ __global__ void __launch_bounds__(128, 1) k_b4_forward_tc(const __grid_constant_
     bool fin = true;
     if (threadIdx.x == 0) {
         for (int s = 0; s < 2; ++s)
-            if (issued[s] && !mbar_wait(&S.mma_bar[s], mma_phase[s])) fin = false;
+            if (((issued >> s) & 1u) && !mbar_wait(&S.mma_bar[s], (mma_phase >> s) & 1u)) fin = false;
     }
     ok = __syncthreads_and((ok && fin) ? 1 : 0) != 0;
     if (!ok && threadIdx.x == 0) atomicOr(P.err, 1u);
     asm volatile("tcgen05.fence::after_thread_sync;");
     __syncthreads();
     if (ok && nchunks > 0) {
-        // D row = output column panel * 128 + 32 warp + lane; columns p * 64 + b
+        // D row m = panel * 128 + 32 warp + lane; columns p * 64 + b
         const int64_t col = (int64_t)panel * kPanel + warp * 32 + lane;
         const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
-        float* out = P.part + (int64_t)slice * P.B * P.n_out;
+        float* out = P.part + (int64_t)slice * P.B * P.M;
         for (int c16 = 0; c16 < kBatch / 16; ++c16) {
             float hi[16], mi[16], lo[16];
             tmem_ld16(lane_addr + c16 * 16, hi);
@@ -297,15 +311,15 @@ __global__ void __launch_bounds__(128, 1) k_b4_forward_tc(const __grid_constant_
 #pragma unroll
             for (int v = 0; v < 16; ++v) {
                 const int b = group * kBatch + c16 * 16 + v;
-                if (b < P.B && col < P.n_out) out[(int64_t)b * P.n_out + col] = hi[v] + mi[v] + lo[v];
+                if (b < P.B && col < P.M) out[(int64_t)b * P.M + col] = hi[v] + mi[v] + lo[v];
             }
         }
     } else if (nchunks <= 0) {
         const int64_t col = (int64_t)panel * kPanel + warp * 32 + lane;
-        float* out = P.part + (int64_t)slice * P.B * P.n_out;
+        float* out = P.part + (int64_t)slice * P.B * P.M;
         for (int v = 0; v < kBatch; ++v) {
             const int b = group * kBatch + v;
-            if (b < P.B && col < P.n_out) out[(int64_t)b * P.n_out + col] = 0.0f;
+            if (b < P.B && col < P.M) out[(int64_t)b * P.M + col] = 0.0f;
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;");
@@ -314,9 +328,11 @@ __global__ void __launch_bounds__(128, 1) k_b4_forward_tc(const __grid_constant_
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
 }
 
-// The panel map: for every tile, its slot at [bc / 32][br / 16][br % 16][bc % 32]
-// (a warp per block-row, lanes over its tiles); the map starts all -1.
-__global__ void k_b4_panel_map(B4View V, int64_t chunks, int* __restrict__ pmap) {
+// The panel maps: for every tile (br, bc), its slot at
+// [m-block / 32][k-block / 16][k-block % 16][m-block % 32] with m = bc, k = br
+// for the forward and m = br, k = bc for the dx (a warp per block-row, lanes
+// over its tiles); the map starts all -1.
+__global__ void k_b4_panel_map(B4View V, int dx, int64_t chunks, int* __restrict__ pmap) {
     const int lane = threadIdx.x & 31;
     const int64_t br = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (br >= V.BR) return;
@@ -325,21 +341,22 @@ __global__ void k_b4_panel_map(B4View V, int64_t chunks, int* __restrict__ pmap)
     for (int k = lane; k < n; k += 32) {
         const int64_t slot = es + k;
         const int64_t bc = V.bc[slot];
-        pmap[((bc >> 5) * chunks + (br >> 4)) * 512 + (br & 15) * 32 + (bc & 31)] = (int)slot;
+        const int64_t mb = dx ? br : bc, kb = dx ? bc : br;
+        pmap[((mb >> 5) * chunks + (kb >> 4)) * 512 + (kb & 15) * 32 + (mb & 31)] = (int)slot;
     }
 }
 
-// x' = x * vs split into bf16 hi, mid, lo: row
-// (group * 192 + p * 64 + b), column r of a [groups * 192, K_pad] array;
-// samples past B and rows past n_in are 0
-__global__ void k_b4_xsplit(const float* __restrict__ xT, const float* __restrict__ vs, int64_t n_in, int B,
+// act' = act * kscale split into bf16 hi, mid, lo: row (group * 192 + p * 64
+// + b), column k of a [groups * 192, K_pad] array; act is [K (+1), B] (the
+// transposed x or dy); samples past B and k past K are 0
+__global__ void k_b4_xsplit(const float* __restrict__ actT, const float* __restrict__ kscale, int64_t K, int B,
                             int groups, int64_t kpad, uint16_t* __restrict__ xs) {
     const int64_t total = (int64_t)groups * kBatch * kpad;
     for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
         const int64_t r = t % kpad, gb = t / kpad;
         const int g = (int)(gb / kBatch), bl = (int)(gb % kBatch);
         const int b = g * kBatch + bl;
-        const float v = (r < n_in && b < B) ? __fmul_rn(xT[r * B + b], vs[r]) : 0.0f;
+        const float v = (r < K && b < B) ? __fmul_rn(actT[r * B + b], kscale[r]) : 0.0f;
         const __nv_bfloat16 h = __float2bfloat16_rn(v);
         const float r1 = __fsub_rn(v, __bfloat162float(h));
         const __nv_bfloat16 m = __float2bfloat16_rn(r1);
@@ -352,36 +369,54 @@ __global__ void k_b4_xsplit(const float* __restrict__ xT, const float* __restric
     }
 }
 
-// y[b, c] += os[c] * (partials summed in slice order); a non-finite result is
-// recomputed term by term over the column's tiles in the reference's form
-// x * (fp4(w) * S) (no zero-input skip in the block4 forward), so that a NaN
-// or an infinity comes out as the exact path gives it
-__global__ void k_b4_tc_reduce(const float* __restrict__ part, int kslices, int B, int64_t n_out,
-                               const float* __restrict__ os, const float* __restrict__ vs, const float* __restrict__ xT,
-                               int64_t n_in, const int* __restrict__ cptr, const int* __restrict__ ctile,
-                               const int* __restrict__ cbr, const uint4* __restrict__ tile, float* __restrict__ y) {
+// out[b, m] += mscale[m] * (partials summed in slice order).  A non-finite
+// result is recomputed term by term over the tiles in the reference's form,
+// so that a NaN or an infinity comes out as the exact path gives it:
+//   forward (linear_disldo.hpp:128-339, no zero-input skip):
+//     y[b, c]  = sum over the column's tiles and rows of x * (fp4(w) * S)
+//   dx at lr = 0 (:1512-1703): dx[b, r] = sum over the row's tiles and
+//     columns of fp4(w) * (S * dy)
+template <bool DX>
+__global__ void k_b4_tc_reduce(const float* __restrict__ part, int kslices, int B, LayerView L, B4View V,
+                               const float* __restrict__ actT, float* __restrict__ out) {
+    const int64_t M = DX ? L.n_in : L.n_out;
     const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (t >= (int64_t)B * n_out) return;
-    const int64_t b = t / n_out, c = t % n_out;
+    if (t >= (int64_t)B * M) return;
+    const int64_t b = t / M, m = t % M;
     float v = 0.0f;
-    for (int k = 0; k < kslices; ++k) v += part[(int64_t)k * B * n_out + t];
-    float add = v * os[c];
+    for (int k = 0; k < kslices; ++k) v += part[(int64_t)k * B * M + t];
+    float add = v * (DX ? L.vs[m] : L.os[m]);
     if (!isfinite(add)) {
-        const int64_t bc = c >> 2;
-        const int lj = (int)(c & 3);
         float acc = 0.0f;
-        for (int q = cptr[bc]; q < cptr[bc + 1]; ++q) {
-            const uint4 tw = tile[ctile[q]];
-            const uint32_t word = lj == 0 ? tw.x : lj == 1 ? tw.y : lj == 2 ? tw.z : tw.w;
-            for (int li = 0; li < 4; ++li) {
-                const int64_t r = (int64_t)cbr[q] * 4 + li;
-                if (r >= n_in) break;
-                acc += xT[r * B + b] * (fp4_decode((word >> (8 * li)) & 0xFu) * (vs[r] * os[c]));
+        if (!DX) {
+            const int64_t bc = m >> 2;
+            const int lj = (int)(m & 3);
+            for (int q = V.cptr[bc]; q < V.cptr[bc + 1]; ++q) {
+                const uint4 tw = V.tile[V.ctile[q]];
+                const uint32_t word = lj == 0 ? tw.x : lj == 1 ? tw.y : lj == 2 ? tw.z : tw.w;
+                for (int li = 0; li < 4; ++li) {
+                    const int64_t r = (int64_t)V.cbr[q] * 4 + li;
+                    if (r >= L.n_in) break;
+                    acc += actT[r * B + b] * (fp4_decode((word >> (8 * li)) & 0xFu) * (L.vs[r] * L.os[m]));
+                }
+            }
+        } else {
+            const int64_t br = m >> 2;
+            const int li = (int)(m & 3);
+            const int64_t es = V.es[br];
+            for (int q = 0; q < V.nt[br]; ++q) {
+                const uint4 tw = V.tile[es + q];
+                const uint32_t words[4] = {tw.x, tw.y, tw.z, tw.w};
+                for (int lj = 0; lj < 4; ++lj) {
+                    const int64_t c = (int64_t)V.bc[es + q] * 4 + lj;
+                    if (c >= L.n_out) break;
+                    acc += fp4_decode((words[lj] >> (8 * li)) & 0xFu) * ((L.vs[m] * L.os[c]) * actT[c * B + b]);
+                }
             }
         }
         add = acc;
     }
-    y[t] += add;
+    out[t] += add;
 }
 
 using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -401,55 +436,60 @@ EncodeTiled encode_fn() {
     return fn;
 }
 
+int64_t dims_m(const LayerView& L, bool dx) { return dx ? L.n_in : L.n_out; }
+int64_t dims_k(const LayerView& L, bool dx) { return dx ? L.n_out : L.n_in; }
+
 }  // namespace
 
 bool b4_tc_applies(const LayerView& L, const B4View& V, int B) {
-    return L.rank == 1 && V.BC > 0 && B >= 16 && L.n_in > 0 && V.cptr != nullptr;
+    return L.rank == 1 && V.BC > 0 && B >= 16 && L.n_in > 0 && L.n_out > 0 && V.cptr != nullptr;
 }
 
-int64_t b4_tc_scratch_floats(const LayerView& L, int B, int* kslices) {
-    const int64_t panels = (L.n_out + kPanel - 1) / kPanel;
+int64_t b4_tc_scratch_floats(const LayerView& L, int B, bool dx, int* kslices) {
+    const int64_t panels = (dims_m(L, dx) + kPanel - 1) / kPanel;
     const int groups = (B + kBatch - 1) / kBatch;
-    const int64_t chunks = (L.n_in + kChunk - 1) / kChunk;
-    // slices of the input rows so that panels x groups x slices fill the
-    // SMs about twice (two CTAs fit per SM: 88 KB of shared memory, 256
+    const int64_t chunks = (dims_k(L, dx) + kChunk - 1) / kChunk;
+    // slices of the summed dimension so that panels x groups x slices fill the
+    // SMs about twice (two CTAs fit per SM: 84 KB of shared memory, 256
     // tensor-memory columns each), at least 4 chunks per slice
     int64_t k = std::max<int64_t>(1, (2 * 148) / std::max<int64_t>(1, panels * groups));
     k = std::min<int64_t>(k, std::max<int64_t>(1, chunks / 4));
     *kslices = (int)k;
-    return k * (int64_t)B * L.n_out;
+    return k * (int64_t)B * dims_m(L, dx);
 }
 
-int64_t b4_tc_pmap_elems(const LayerView& L) {
-    const int64_t panels = (L.n_out + kPanel - 1) / kPanel;
-    const int64_t chunks = (L.n_in + kChunk - 1) / kChunk;
+int64_t b4_tc_pmap_elems(const LayerView& L, bool dx) {
+    const int64_t panels = (dims_m(L, dx) + kPanel - 1) / kPanel;
+    const int64_t chunks = (dims_k(L, dx) + kChunk - 1) / kChunk;
     return panels * chunks * 512;
 }
 
-void launch_b4_panel_map(const LayerView& L, const B4View& V, int* pmap, cudaStream_t s) {
-    const int64_t chunks = (L.n_in + kChunk - 1) / kChunk;
-    cudaMemsetAsync(pmap, 0xFF, (size_t)b4_tc_pmap_elems(L) * sizeof(int), s);
+void launch_b4_panel_map(const LayerView& L, const B4View& V, bool dx, int* pmap, cudaStream_t s) {
+    const int64_t chunks = (dims_k(L, dx) + kChunk - 1) / kChunk;
+    cudaMemsetAsync(pmap, 0xFF, (size_t)b4_tc_pmap_elems(L, dx) * sizeof(int), s);
     if (V.BR > 0) {
-        k_b4_panel_map<<<(unsigned)((V.BR + 7) / 8), 256, 0, s>>>(V, chunks, pmap);
+        k_b4_panel_map<<<(unsigned)((V.BR + 7) / 8), 256, 0, s>>>(V, dx ? 1 : 0, chunks, pmap);
         count_launch();
     }
 }
 
-int64_t b4_tc_xsplit_elems(const LayerView& L, int B) {
+int64_t b4_tc_xsplit_elems(const LayerView& L, int B, bool dx) {
     const int groups = (B + kBatch - 1) / kBatch;
-    const int64_t kpad = (L.n_in + kChunk - 1) / kChunk * kChunk;
+    const int64_t kpad = (dims_k(L, dx) + kChunk - 1) / kChunk * kChunk;
     return (int64_t)groups * kN * kpad;
 }
 
-int launch_b4_forward_tc(const LayerView& L, const B4View& V, const float* xT, int B, float* y, uint16_t* xsplit,
-                         float* part, int kslices, const int* pmap, unsigned int* err, cudaStream_t s) {
+template <bool DX>
+static int launch_tc(const LayerView& L, const B4View& V, const float* actT, int B, float* out, uint16_t* xsplit,
+                     float* part, int kslices, const int* pmap, unsigned int* err, cudaStream_t s) {
     EncodeTiled enc = encode_fn();
-    if (!enc) return set_error(SILI_ECUDA, "block4 tensor-core forward: cuTensorMapEncodeTiled unavailable");
+    if (!enc) return set_error(SILI_ECUDA, "block4 tensor-core kernel: cuTensorMapEncodeTiled unavailable");
+    const int64_t M = dims_m(L, DX), K = dims_k(L, DX);
     const int groups = (B + kBatch - 1) / kBatch;
-    const int64_t kpad = (L.n_in + kChunk - 1) / kChunk * kChunk;
+    const int64_t kpad = (K + kChunk - 1) / kChunk * kChunk;
     const int64_t chunks = kpad / kChunk;
     k_b4_xsplit<<<(unsigned)std::min<int64_t>((groups * kBatch * kpad + 255) / 256, 148 * 32), 256, 0, s>>>(
-        xT, L.vs, L.n_in, B, groups, kpad, xsplit);
+        actT, DX ? L.os : L.vs, K, B, groups, kpad, xsplit);
     count_launch();
     CUtensorMap map;
     std::memset(&map, 0, sizeof(map));
@@ -460,28 +500,36 @@ int launch_b4_forward_tc(const LayerView& L, const B4View& V, const float* xT, i
     const CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, xsplit, dims, strides, box, estr,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return set_error(SILI_ECUDA, "block4 tensor-core forward: tensor map encoding failed");
+    if (r != CUDA_SUCCESS) return set_error(SILI_ECUDA, "block4 tensor-core kernel: tensor map encoding failed");
     TcArgs P;
-    P.n_in = L.n_in; P.n_out = L.n_out; P.B = B; P.groups = groups; P.kslices = kslices;
+    P.M = M; P.K = K; P.B = B; P.groups = groups; P.kslices = kslices;
     P.chunks_per_slice = (int)((chunks + kslices - 1) / kslices);
-    P.BC = V.BC; P.cptr = V.cptr; P.ctile = V.ctile; P.cbr = V.cbr; P.tile = V.tile;
-    P.pmap = pmap; P.chunks = chunks;
+    P.tile = V.tile; P.pmap = pmap; P.chunks = chunks;
     P.part = part; P.err = err;
     const size_t smem = sizeof(TcSmem) + 1024;
     static unsigned long long attr_devices = 0;
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 64 && !(attr_devices & (1ull << dev))) {
-        cudaFuncSetAttribute(k_b4_forward_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(k_b4_tc<DX>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         attr_devices |= 1ull << dev;
     }
-    dim3 g((unsigned)((L.n_out + kPanel - 1) / kPanel), (unsigned)kslices, (unsigned)groups);
-    k_b4_forward_tc<<<g, 128, smem, s>>>(map, P);
-    const int64_t n = (int64_t)B * L.n_out;
-    k_b4_tc_reduce<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(part, kslices, B, L.n_out, L.os, L.vs, xT, L.n_in,
-                                                              V.cptr, V.ctile, V.cbr, V.tile, y);
+    dim3 g((unsigned)((M + kPanel - 1) / kPanel), (unsigned)kslices, (unsigned)groups);
+    k_b4_tc<DX><<<g, 128, smem, s>>>(map, P);
+    const int64_t n = (int64_t)B * M;
+    k_b4_tc_reduce<DX><<<(unsigned)((n + 255) / 256), 256, 0, s>>>(part, kslices, B, L, V, actT, out);
     count_launch(2);
     return SILI_OK;
+}
+
+int launch_b4_forward_tc(const LayerView& L, const B4View& V, const float* xT, int B, float* y, uint16_t* xsplit,
+                         float* part, int kslices, const int* pmap, unsigned int* err, cudaStream_t s) {
+    return launch_tc<false>(L, V, xT, B, y, xsplit, part, kslices, pmap, err, s);
+}
+
+int launch_b4_dx_tc(const LayerView& L, const B4View& V, const float* dyT, int B, float* dx, uint16_t* xsplit,
+                    float* part, int kslices, const int* pmap, unsigned int* err, cudaStream_t s) {
+    return launch_tc<true>(L, V, dyT, B, dx, xsplit, part, kslices, pmap, err, s);
 }
 
 }  // namespace sili

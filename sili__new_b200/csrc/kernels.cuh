@@ -134,15 +134,19 @@ bool folded_forward_applies(const FoldedView& F, int B);
 // The block4 forward on the tensor cores (block4_tc.cu): rank 1, B >= 16.
 // Scratch: the split activations (b4_tc_xsplit_elems bf16) and the partial
 // sums (b4_tc_scratch_floats, which also picks the input-row slices).
+// dx = false: the forward (y [B, n_out] += ...), true: the lr = 0 dx
+// (dx [B, n_in] += ...).
 bool b4_tc_applies(const LayerView& L, const B4View& V, int B);
-int64_t b4_tc_scratch_floats(const LayerView& L, int B, int* kslices);
-int64_t b4_tc_xsplit_elems(const LayerView& L, int B);
-// the panel map (tile slot per 32-block-column x 16-block-row cell), rebuilt
-// when the tile layout changes
-int64_t b4_tc_pmap_elems(const LayerView& L);
-void launch_b4_panel_map(const LayerView& L, const B4View& V, int* pmap, cudaStream_t s);
+int64_t b4_tc_scratch_floats(const LayerView& L, int B, bool dx, int* kslices);
+int64_t b4_tc_xsplit_elems(const LayerView& L, int B, bool dx);
+// the panel map (tile slot per 32 x 16 block cell), rebuilt when the tile
+// layout changes
+int64_t b4_tc_pmap_elems(const LayerView& L, bool dx);
+void launch_b4_panel_map(const LayerView& L, const B4View& V, bool dx, int* pmap, cudaStream_t s);
 int launch_b4_forward_tc(const LayerView& L, const B4View& V, const float* xT, int B, float* y, uint16_t* xsplit,
                          float* part, int kslices, const int* pmap, unsigned int* err, cudaStream_t s);
+int launch_b4_dx_tc(const LayerView& L, const B4View& V, const float* dyT, int B, float* dx, uint16_t* xsplit,
+                    float* part, int kslices, const int* pmap, unsigned int* err, cudaStream_t s);
 int set_error(int code, const std::string& msg);
 
 // y = [B, out_dim] (fold_sum) or [B, n_cols]; false when the shape rules

@@ -223,7 +223,13 @@ ColsPlan cols_plan(const LayerView& L, int B) {
     const int sg = 32;
     const int64_t sgroups = (B + sg - 1) / sg;
     const int t = 256;
-    if (((L.n_out + t - 1) / t) * sgroups < 2 * 148) return p;
+    // 3 CTAs fit per SM (64 KB x tile each): a grid whose last wave is
+    // mostly empty loses to the per-synapse kernel (measured on the 8-way
+    // shard of a 163840-column gate projection: 640 CTAs, 1.44 waves, 9 %
+    // slower; the 4-way shard's 1280 CTAs, 2.9 waves, 13 % faster)
+    const int64_t ctas = ((L.n_out + t - 1) / t) * sgroups;
+    const int64_t wave = 3 * 148;
+    if (ctas < 2 * 148 || ctas * 10 < ((ctas + wave - 1) / wave) * wave * 8) return p;
     p.threads = t;
     p.sg = sg;
     // x tile: 128 bytes per row, 64 KB (3 CTAs per SM)

@@ -187,6 +187,8 @@ struct sili_layer {
     DBuf<unsigned int> tc_err;             // set by a tensor-core kernel whose bounded wait gave up
     DBuf<int> b4_pmap;                     // its panel map (tile slot per 32 x 16 block cell)
     bool b4_pmap_dirty = true;             // the tile layout changed since the map was built
+    DBuf<int> b4_pmapT;                    // the lr = 0 dx's panel map (block-rows along the panel)
+    bool b4_pmapT_dirty = true;
     // synaptogenesis working set (probe-by-row index, scratch, snapshot)
     struct SynStateT {
         DBuf<int> pr_ptr, keys, keys_o, ids, ids_o, od0, od_decs;
@@ -668,7 +670,7 @@ int b4_init(sili_layer* h, int64_t cap, cudaStream_t s) {
     CK(cudaStreamSynchronize(s));
     h->b4_ntiles = 0;
     h->b4_dirty = true;
-    h->b4_pmap_dirty = true;
+    h->b4_pmap_dirty = h->b4_pmapT_dirty = true;
     return SILI_OK;
 }
 
@@ -914,7 +916,7 @@ int b4_relayout(sili_layer* h, const std::vector<int64_t>& newcap, cudaStream_t 
     CK(cudaStreamSynchronize(s));
     h->b4_bc.swap(nbc); h->b4_tile.swap(ntile); h->b4_sparse.swap(nsp);
     h->b4_dirty = true;
-    h->b4_pmap_dirty = true;
+    h->b4_pmap_dirty = h->b4_pmapT_dirty = true;
     return SILI_OK;
 }
 
@@ -1334,26 +1336,34 @@ static int check_tc_err(sili_layer* h) {
 // the tensor-core forward is not taken.
 constexpr int64_t kB4PanelMapMax = (int64_t)1 << 28;
 
-// The block4 part of forward_dense: on the tensor cores when the layer asks
-// for it and the shape allows (rank 1, batch >= 16), else the exact
-// CUDA-core kernel.
-static int b4_forward(sili_layer* h, const float* xT, int batch, float* y, cudaStream_t s) {
+// The block4 part of forward_dense (dx = false) and of the lr = 0 backward's
+// dx (dx = true): on the tensor cores when the layer asks for it and the
+// shape allows (rank 1, batch >= 16), else the exact CUDA-core kernels.
+static int b4_tc_or_exact(sili_layer* h, bool dx, const float* actT, int batch, float* out, cudaStream_t s) {
     const LayerView v = h->view();
     const B4View V = h->b4view();
-    if (h->b4_tc && b4_tc_applies(v, V, batch) && b4_tc_pmap_elems(v) <= kB4PanelMapMax) {
-        if (h->b4_pmap_dirty) {
-            RC(h->b4_pmap.reserve(b4_tc_pmap_elems(v) + 1));
-            launch_b4_panel_map(v, V, h->b4_pmap.p, s);
-            h->b4_pmap_dirty = false;
+    if (h->b4_tc && b4_tc_applies(v, V, batch) && b4_tc_pmap_elems(v, dx) <= kB4PanelMapMax) {
+        DBuf<int>& map = dx ? h->b4_pmapT : h->b4_pmap;
+        bool& dirty = dx ? h->b4_pmapT_dirty : h->b4_pmap_dirty;
+        if (dirty) {
+            RC(map.reserve(b4_tc_pmap_elems(v, dx) + 1));
+            launch_b4_panel_map(v, V, dx, map.p, s);
+            dirty = false;
         }
         int ks = 1;
-        const int64_t nf = b4_tc_scratch_floats(v, batch, &ks);
+        const int64_t nf = b4_tc_scratch_floats(v, batch, dx, &ks);
         RC(h->b4_part.reserve(nf + 1));
-        RC(h->b4_xs.reserve(b4_tc_xsplit_elems(v, batch) + 8));
-        return launch_b4_forward_tc(v, V, xT, batch, y, h->b4_xs.p, h->b4_part.p, ks, h->b4_pmap.p, h->tc_err.p, s);
+        RC(h->b4_xs.reserve(b4_tc_xsplit_elems(v, batch, dx) + 8));
+        return dx ? launch_b4_dx_tc(v, V, actT, batch, out, h->b4_xs.p, h->b4_part.p, ks, map.p, h->tc_err.p, s)
+                  : launch_b4_forward_tc(v, V, actT, batch, out, h->b4_xs.p, h->b4_part.p, ks, map.p, h->tc_err.p, s);
     }
-    launch_b4_forward(v, V, xT, batch, y, s);
+    if (dx) launch_b4_dx(v, V, actT, batch, out, s);
+    else launch_b4_forward(v, V, actT, batch, out, s);
     return SILI_OK;
+}
+
+static int b4_forward(sili_layer* h, const float* xT, int batch, float* y, cudaStream_t s) {
+    return b4_tc_or_exact(h, false, xT, batch, y, s);
 }
 
 int sili_layer_set_b4_tensor_cores(sili_layer* h, int enable) {
@@ -1559,7 +1569,7 @@ static int backward_dense_impl(sili_layer* h, const float* x, const float* dy, i
     if (lr == 0.0f) {
         if (h->timing) CK(cudaEventRecord(h->ev[2], s));
         launch_backward_dx(v, h->dyT.p, batch, dxd, s);
-        if (h->b4_ntiles > 0) launch_b4_dx(v, h->b4view(), h->dyT.p, batch, dxd, s);
+        if (h->b4_ntiles > 0) RC(b4_tc_or_exact(h, true, h->dyT.p, batch, dxd, s));
         if (h->timing) { CK(cudaEventRecord(h->ev[3], s)); h->ev_bwd = true; }
         h->call++;   // every backward call advances the stochastic-rounding counter
     } else {
@@ -1945,7 +1955,7 @@ int sili_layer_synap_rows(sili_layer* h, int row0, int nrows, float importance_c
         h->total_nnz += (int64_t)res[2];
         h->aux_dirty = true;
         h->b4_dirty = true;
-    h->b4_pmap_dirty = true;
+    h->b4_pmap_dirty = h->b4_pmapT_dirty = true;
         std::vector<int> nt((size_t)BR + 1, 0);
         if (BR > 0) CK(cudaMemcpyAsync(nt.data(), h->b4_nt.p, (size_t)BR * 4, cudaMemcpyDeviceToHost, s));
         CK(cudaStreamSynchronize(s));
@@ -2671,7 +2681,7 @@ int sili_layer_load_dense_codes(sili_layer* h, const uint8_t* wc, const uint8_t*
     RC(b4_put_allocs(h, a, s));
     h->b4_ntiles = BR * BC;
     h->b4_dirty = true;
-    h->b4_pmap_dirty = true;
+    h->b4_pmap_dirty = h->b4_pmapT_dirty = true;
     // out_degree[c] = n_in for every column (cpu_backend.cpp:916-920)
     std::vector<int> od((size_t)h->cols + 1, (int)h->rows);
     if (h->cols > 0) CK(cudaMemcpyAsync(h->out_degree.p, od.data(), (size_t)h->cols * 4, cudaMemcpyHostToDevice, s));

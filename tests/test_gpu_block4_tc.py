@@ -1,5 +1,6 @@
-"""The block4 forward on the tensor cores (tcgen05 MMA, TMA-staged
-activations) against the exact CUDA-core block4 forward and the CPU oracle.
+"""The block4 forward and the lr = 0 dx on the tensor cores (tcgen05 MMA,
+TMA-staged activations) against the exact CUDA-core block4 kernels and the
+CPU oracle.
 
 Contract: fp32 summation tolerance, 1e-5 relative (replay.assert_close_sum:
 |got - want| <= 1e-5 (|want| + mean |want|)).  The FP4 codes are exact in
@@ -128,3 +129,53 @@ def test_tc_forward_config2_full_grid():
         ys.append(L.forward_dense(x))
         del L
     assert_close_sum(ys[1], ys[0], 1e-5)
+
+
+@pytest.mark.parametrize("n_in,n_out,B,dens", [(256, 256, 64, 0.3), (200, 300, 16, 0.5), (512, 1024, 130, 0.05),
+                                               (384, 512, 64, 1.0)])
+def test_tc_dx_matches_exact(n_in, n_out, B, dens):
+    """backward_dense(dy, 0.0): dx = dy W^T with W's block4 part on the
+    tensor cores (dy * output_scale split in three bf16 terms)."""
+    (ex, tc), _, _, _ = _layers(n_in, n_out, dens, seed=n_in + 3 * B)
+    rng = np.random.default_rng(B + 1)
+    for call in range(3):
+        x = rng.normal(0, 1, (B, n_in)).astype(np.float32)
+        dy = rng.normal(0, 1, (B, n_out)).astype(np.float32)
+        if call == 2:
+            dy[:, ::3] = 0.0
+        for L in (ex, tc):
+            L.forward_dense(x)
+        assert_close_sum(tc.backward_dense(dy, 0.0), ex.backward_dense(dy, 0.0), 1e-5)
+    tc.sync()
+
+
+def test_tc_dx_vs_oracle_and_nan():
+    import sili__new_b200 as S
+    n_in, n_out, B = 256, 192, 32
+    rng = np.random.default_rng(9)
+    wc, ic = _codes(rng, n_in, n_out, 0.4)
+    g = S.SparseLinearLayerDeterministic(n_in, n_out, n_in * n_out)
+    o = O.OracleLayer(n_in, n_out, n_in * n_out)
+    for L in (g, o):
+        L.load_dense_codes(wc, ic)
+        for r in range(n_in):
+            L.set_value_scale_raw(r, float(0.01 + 0.001 * (r % 7)))
+    g.set_block4_tensor_cores(True)
+    x = rng.normal(0, 1, (B, n_in)).astype(np.float32)
+    dy = rng.normal(0, 1, (B, n_out)).astype(np.float32)
+    g.forward_dense(x)
+    o.forward_dense(x)
+    assert_close_sum(g.backward_dense(dy, 0.0), o.backward_dense(dy, 0.0), 1e-5)
+    # a NaN weight code: its row of dx is NaN on both paths
+    wc[7, 11] = 8
+    dxs = []
+    for tc in (False, True):
+        L = S.SparseLinearLayerDeterministic(n_in, n_out, n_in * n_out)
+        L.load_dense_codes(wc, ic)
+        L.set_block4_tensor_cores(tc)
+        L.forward_dense(x)
+        dxs.append(L.backward_dense(dy, 0.0))
+    want, got = dxs
+    assert np.array_equal(np.isnan(got), np.isnan(want))
+    m = ~np.isnan(want)
+    assert_close_sum(got[m], want[m], 1e-5)
