@@ -881,6 +881,167 @@ __global__ void __launch_bounds__(128) k_b4_rows_chain(LayerView L, B4View V, in
     }
 }
 
+// The importance magnitudes a of a tile's 16 slots, indexed li * 4 + lj (the
+// eviction's scan order), -1 for empty slots.  a = |dec(imp)| * m[li][lj]
+// with m = |is[r]| * |ois[c]| in double: every factor has at most 24
+// significant bits (dec at most 2), so each product is exact and equals
+// b4_abs_imp's, which multiplies in another order; it is NaN exactly when
+// b4_abs_imp's is (a NaN factor, or 0 times infinity in either order).
+__device__ __forceinline__ void b4_tile_levels(const uint4& tw, const double isd[4], const double oisd[4],
+                                               double a[16]) {
+    const uint32_t wd[4] = {tw.x, tw.y, tw.z, tw.w};
+#pragma unroll
+    for (int li = 0; li < 4; ++li)
+#pragma unroll
+        for (int lj = 0; lj < 4; ++lj) {
+            const uint32_t byte = (wd[lj] >> (8 * li)) & 0xFFu;
+            const double mag = (double)fabsf(fp4_decode(byte >> 4));
+            a[li * 4 + lj] = byte ? mag * (isd[li] * oisd[lj]) : -1.0;
+        }
+}
+// the smaller of two levels, -1 meaning none
+__device__ __forceinline__ double b4_lvl_min(double m, double a) { return (a >= 0.0 && (m < 0.0 || a < m)) ? a : m; }
+
+// The eviction of one block-row by a full warp: the same evictions, repacking
+// and counters as b4_evict_row, organised for rows of many tiles:
+//   * the packed flags are first refreshed from the tiles' live counts (the
+//     warp-per-row update writes slot bytes only; for tiles whose flags are
+//     current this rewrites the same values);
+//   * each slot's a is computed from registers (b4_tile_levels) instead of
+//     two global loads per slot;
+//   * one walk per importance level, which also finds the next level (the
+//     smallest a above the current one; every slot at the current level has
+//     been evicted when a walk ends with the row still too long);
+//   * the fit count at the end by a warp prefix sum over the tiles.
+// A row holding a NaN importance takes b4_evict_row's one-at-a-time path.
+__device__ void b4_evict_row_warp(const LayerView& L, const B4View& V, int64_t br, int64_t base, int nt, int lane) {
+    const unsigned full = 0xFFFFFFFFu;
+    const int64_t cap = V.alloc[V.BR + br];
+    double isd[4];
+#pragma unroll
+    for (int li = 0; li < 4; ++li) {
+        const int64_t r = br * 4 + li;
+        isd[li] = r < L.n_in ? fabs((double)L.is[r]) : 0.0;
+    }
+    auto ois_of = [&](int64_t c0, double oisd[4]) {
+#pragma unroll
+        for (int lj = 0; lj < 4; ++lj) oisd[lj] = c0 + lj < L.n_out ? fabs((double)L.ois[c0 + lj]) : 0.0;
+    };
+    long long used = 0;
+    bool nan_here = false;
+    double amin = -1.0;
+    for (int e = lane; e < nt; e += 32) {
+        const uint4 tw = V.tile[base + e];
+        const int live = tile_live(tw);
+        const bool sp = (uint32_t)live <= V.switch_point;
+        V.sparse[base + e] = sp ? 1 : 0;
+        used += tile_len(live, sp);
+        double oisd[4], a[16];
+        ois_of((int64_t)V.bc[base + e] * 4, oisd);
+        b4_tile_levels(tw, isd, oisd, a);
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+            if (isnan(a[q])) nan_here = true;
+            amin = b4_lvl_min(amin, a[q]);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) used += __shfl_xor_sync(full, used, o);
+    if (used <= cap) return;   // every tile fits
+    if (__any_sync(full, nan_here)) {
+        b4_evict_row<32>(L, V, br, base, nt, lane, full);
+        return;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amin = b4_lvl_min(amin, __shfl_xor_sync(full, amin, o));
+    while (used > cap && amin >= 0.0) {
+        double nxt = -1.0;
+        for (int e0 = 0; e0 < nt && used > cap; e0 += 32) {
+            const int e = e0 + lane;
+            uint4 tw = make_uint4(0u, 0u, 0u, 0u);
+            int live = 0, k = 0, old_len = 0;
+            uint32_t lvl = 0;   // this level's slots, bit li * 4 + lj
+            if (e < nt) {
+                tw = V.tile[base + e];
+                double oisd[4], a[16];
+                ois_of((int64_t)V.bc[base + e] * 4, oisd);
+                b4_tile_levels(tw, isd, oisd, a);
+#pragma unroll
+                for (int q = 0; q < 16; ++q) {
+                    if (a[q] == amin) lvl |= 1u << q;
+                    else if (a[q] > amin) nxt = b4_lvl_min(nxt, a[q]);
+                }
+                live = tile_live(tw);
+                old_len = tile_len(live, V.sparse[base + e] != 0);
+                k = __popc(lvl);
+            }
+            auto saving = [&](int j) {   // bytes saved by evicting j of this tile's level slots
+                const int lv = live - j;
+                return (long long)(old_len - tile_len(lv, (uint32_t)lv <= V.switch_point));
+            };
+            const long long d = k > 0 ? saving(k) : 0;
+            long long incl = d;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const long long t = __shfl_up_sync(full, incl, o);
+                if (lane >= o) incl += t;
+            }
+            const long long excl = incl - d, need = used - cap;
+            int take = 0;
+            if (k > 0 && excl < need) {
+                take = k;
+                for (int j = 1; j < k; ++j)
+                    if (excl + saving(j) >= need) { take = j; break; }
+            }
+            long long applied = 0;
+            if (take > 0) {
+                uint32_t m = lvl;
+                for (int j = 0; j < take; ++j) {
+                    const int bit = __ffs(m) - 1;
+                    m &= m - 1u;
+                    set_tile_byte(tw, (bit & 3) * 4 + (bit >> 2), 0u);   // slot lj * 4 + li
+                }
+                const int lv = tile_live(tw);
+                V.tile[base + e] = tw;
+                V.sparse[base + e] = (uint32_t)lv <= V.switch_point ? 1 : 0;
+                applied = saving(take);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) applied += __shfl_xor_sync(full, applied, o);
+            used -= applied;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) nxt = b4_lvl_min(nxt, __shfl_xor_sync(full, nxt, o));
+        amin = nxt;
+    }
+    // tiles that do not fit even after eviction (the reference counts them):
+    // the first tile whose running length passes the allocation
+    long long fit = 0;
+    int fitted = nt;
+    for (int e0 = 0; e0 < nt; e0 += 32) {
+        const int e = e0 + lane;
+        const long long tl = e < nt ? tile_len(tile_live(V.tile[base + e]), V.sparse[base + e] != 0) : 0;
+        long long incl = tl;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const long long t = __shfl_up_sync(full, incl, o);
+            if (lane >= o) incl += t;
+        }
+        const unsigned over = __ballot_sync(full, e < nt && fit + incl > cap);
+        if (over) {
+            const int first = __ffs(over) - 1;
+            fit += __shfl_sync(full, incl - tl, first);
+            fitted = e0 + first;
+            break;
+        }
+        fit += __shfl_sync(full, incl, 31);
+    }
+    if (lane == 0 && fitted < nt) {
+        atomicAdd(V.counters + 1, 1ull);
+        atomicAdd(V.counters + 2, (unsigned long long)(used - fit));
+    }
+}
+
 // a warp per block-row (the update kernel's own eviction uses its half-warp)
 __global__ void __launch_bounds__(128) k_b4_evict_rows(LayerView L, B4View V, int64_t br0, int64_t br1) {
     const int lane = threadIdx.x & 31;
@@ -888,7 +1049,254 @@ __global__ void __launch_bounds__(128) k_b4_evict_rows(LayerView L, B4View V, in
     if (br >= br1) return;
     const int nt = V.nt[br];
     if (nt == 0) return;
-    b4_evict_row<32>(L, V, br, V.es[br], nt, lane, 0xFFFFFFFFu);
+    b4_evict_row_warp(L, V, br, V.es[br], nt, lane);
+}
+
+// ── the same update, a warp per row (every tile full, B % 4 == 0, B <= 128) ─
+// The row's dx chain ((dx + hs_0) + hs_1) + ... runs in tile order for every
+// sample, and each slot's recurrence runs in sample order; a warp that owns
+// one row and walks its tiles 32 at a time (lane = tile, the thread holding
+// the tile's 4 slots of that row) keeps both chains in registers, so the
+// per-(tile, row, sample) sums hs never leave the SM and the tile passes need
+// no scratch.  Per sample, with x[row, b] the same for the whole warp:
+//   * x == 0 (and every slot of the warp in the range where the step reduces
+//     to it -- finite scale, weight and importance state, ci in [0, 100],
+//     dy finite, eps > 0): the step leaves quant and the value_scale sums
+//     unchanged and ci = fma(beta2, ci, (1 - beta2) * 0), exactly as the
+//     full step evaluates it (the same closed form as the scattered update);
+//   * otherwise the full step, as k_b4_update_tiles;
+//   * hs = (p0 + p1) + (p2 + p3), p = quant * (S * dy), goes to shared
+//     memory, and after 32 samples the lanes (= samples) add the 32 tiles'
+//     hs in tile order to the row's dx.
+// The 4 warps of a CTA are the 4 rows of one block-row: they share a dy panel
+// (the chunk's 128 columns x 32 samples) staged in shared memory by cp.async.
+// The tile bytes are written a byte per slot; the packed flags are refreshed
+// by k_b4_evict_rows.  Same values and the same order of every sum as
+// k_b4_update_tiles + k_b4_rows_chain.
+constexpr int kB4RowsPitch = 4 * 32 + 4;   // panel floats per tile (16-byte bank stagger)
+
+__device__ __forceinline__ void b4_cp_async16(void* smem, const void* gmem) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(gmem) : "memory");
+}
+
+// 6 blocks per SM at scale rank 1 (80 registers), 4 above (the per-slot
+// state grows with the rank)
+template <int RANK, bool STOCH, bool OST, int NB>
+__global__ void __launch_bounds__(128, RANK == 1 ? 6 : 4) k_b4_update_rows(LayerView L, B4View V, const float* __restrict__ xT,
+                                                           const float* __restrict__ dyT, int B, UpdateParams P,
+                                                           int64_t br0, int64_t part_base, float* __restrict__ mcb,
+                                                           float* __restrict__ dxT) {
+    __shared__ __align__(16) float dyp[32 * kB4RowsPitch];   // [tile][column j][sample]
+    __shared__ float hs_s[4][32][33];                          // [row][tile][sample]
+    __shared__ __align__(16) float xs_s[4][NB * 32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t br = br0 + blockIdx.x;
+    const int li = warp;
+    const int64_t row = br * 4 + li;
+    const bool row_ok = row < L.n_in;   // warp-uniform; such warps only help stage the panels
+    const int nt = V.nt[br];
+    if (nt == 0) return;                // the whole block
+    const float eff_lr = P.lr_per_row_nnz ? __fdiv_rn(P.lr, (float)((uint32_t)nt * 4u)) : P.lr;
+    const float beta2 = P.beta2;
+    const float onem = __fsub_rn(1.0f, beta2);
+    const float zterm = __fmul_rn(onem, 0.0f);
+    const bool fast_ok = (!P.damp || P.eps > 0.0f) && isfinite(eff_lr) && beta2 >= 0.0f && beta2 <= 1.0f &&
+                         P.dy_flag != nullptr && *P.dy_flag != P.dy_tag;
+    float vsk[RANK];
+#pragma unroll
+    for (int k = 0; k < RANK; ++k) vsk[k] = row_ok ? L.vs[row * RANK + k] : 0.0f;
+    const float isr = row_ok ? L.is[row] : 0.0f;
+    float* xs = xs_s[warp];
+    for (int t = lane; t < NB * 32; t += 32) xs[t] = (row_ok && t < B) ? xT[row * B + t] : 0.0f;
+    float acc[NB];
+#pragma unroll
+    for (int k = 0; k < NB; ++k) {
+        const int b = k * 32 + lane;
+        acc[k] = (row_ok && b < B) ? dxT[row * B + b] : 0.0f;
+    }
+    double tg[RANK], tc[RANK];
+#pragma unroll
+    for (int k = 0; k < RANK; ++k) { tg[k] = 0.0; tc[k] = 0.0; }
+    const int64_t base = V.es[br];
+    const int nblk = (B + 31) >> 5;
+    for (int e0 = 0; e0 < nt; e0 += 32) {
+        const int n = min(32, nt - e0);
+        const bool have = lane < n;
+        const int64_t ti = base + e0 + (have ? lane : 0);
+        const uint4 tw = V.tile[ti];
+        const int64_t col0 = (int64_t)V.bc[ti] * 4;
+        const uint32_t wd[4] = {tw.x, tw.y, tw.z, tw.w};   // word j: column j, byte li: row li
+        float quant[4], ci[4], qo0[4], S[4], osk[4][RANK];
+        float mc[4][RANK], mcc[4][RANK];
+        bool fin0 = true;   // finite S and weight: the part of the fast condition fixed per chunk
+        bool fin = true;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t byte = (wd[j] >> (8 * li)) & 0xFFu;
+            const int64_t col = col0 + j;
+            float sc = 0.0f;
+#pragma unroll
+            for (int k = 0; k < RANK; ++k) {
+                osk[j][k] = L.os[col * RANK + k];
+                sc = __fmaf_rn(vsk[k], osk[j][k], sc);
+                mc[j][k] = 0.0f;
+                mcc[j][k] = 0.0f;
+            }
+            S[j] = sc;
+            const float cis = __fmul_rn(isr, L.ois[col]);
+            qo0[j] = fp4_decode(byte & 0xFu);
+            quant[j] = qo0[j];
+            ci[j] = __fmul_rn(fp4_decode(byte >> 4), cis);
+            fin0 = fin0 && isfinite(sc) && isfinite(qo0[j]);
+            const float qf = (quant[j] == 0.0f) ? 0.1f : quant[j];
+            fin = fin && ci[j] >= 0.0f && ci[j] <= 100.0f;
+#pragma unroll
+            for (int k = 0; k < RANK; ++k) {
+                fin = fin && isfinite(__fmul_rn(qf, osk[j][k]));
+                if (OST) fin = fin && isfinite(__fmul_rn(qf, vsk[k]));
+            }
+        }
+        double mr[RANK], mrc[RANK];
+#pragma unroll
+        for (int k = 0; k < RANK; ++k) { mr[k] = 0.0; mrc[k] = 0.0; }
+        bool wfast = fast_ok && __all_sync(0xffffffffu, !have || (fin0 && fin));
+        for (int sb = 0; sb < nblk; ++sb) {
+            const int t0 = sb * 32, nb = min(32, B - t0);
+            __syncthreads();   // the previous panel's readers are done
+            for (int q = threadIdx.x; q < 32 * 4 * 8; q += 128) {
+                const int t = q >> 5, j = (q >> 3) & 3, g = q & 7;
+                if (t < n && g * 4 < nb) {
+                    const int64_t c = (int64_t)V.bc[base + e0 + t] * 4 + j;
+                    b4_cp_async16(&dyp[t * kB4RowsPitch + j * 32 + g * 4], dyT + c * B + t0 + g * 4);
+                }
+            }
+            asm volatile("cp.async.wait_all;\n" ::: "memory");
+            __syncthreads();
+            if (!row_ok) continue;
+            float a = acc[0];
+#pragma unroll
+            for (int k = 1; k < NB; ++k)
+                if (sb == k) a = acc[k];
+            const float* dp = dyp + lane * kB4RowsPitch;
+            float* hrow = hs_s[warp][lane];
+            for (int u0 = 0; u0 < nb; u0 += 4) {
+                const float4 x4 = *reinterpret_cast<const float4*>(xs + t0 + u0);
+                float4 d4[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) d4[j] = *reinterpret_cast<const float4*>(dp + j * 32 + u0);
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const float x = u == 0 ? x4.x : u == 1 ? x4.y : u == 2 ? x4.z : x4.w;
+                    float dy[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) dy[j] = u == 0 ? d4[j].x : u == 1 ? d4[j].y : u == 2 ? d4[j].z : d4[j].w;
+                    if (x == 0.0f && wfast) {
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) ci[j] = __fmaf_rn(beta2, ci[j], zterm);
+                    } else {
+                        float pg[4][RANK], pc[4][RANK];
+                        bool f = fin0;
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const float g = __fmul_rn(dy[j], x);
+                            const float cb = __fmul_rn(qo0[j], x);
+                            ci[j] = bounded_ci(ci[j], g, cb, beta2, onem);
+                            const float ngS = __fmul_rn(-g, S[j]);
+                            float raw = P.damp ? __fdiv_rn(ngS, __fadd_rn(__fsqrt_rn(ci[j]), P.eps)) : ngS;
+                            if (raw > 2.0f) raw = 2.0f;
+                            if (raw < -2.0f) raw = -2.0f;
+                            quant[j] = __fmaf_rn(eff_lr, raw, quant[j]);
+                            const float qf = (quant[j] == 0.0f) ? 0.1f : quant[j];
+                            f = f && ci[j] >= 0.0f && ci[j] <= 100.0f;
+#pragma unroll
+                            for (int k = 0; k < RANK; ++k) {
+                                const float qo = __fmul_rn(qf, osk[j][k]);
+                                pg[j][k] = __fmul_rn(qo, g);
+                                pc[j][k] = __fmul_rn(qo, cb);
+                                f = f && isfinite(qo);
+                                if (OST) {
+                                    const float qv = __fmul_rn(qf, vsk[k]);
+                                    mc[j][k] = __fmaf_rn(qv, g, mc[j][k]);
+                                    mcc[j][k] = __fmaf_rn(qv, cb, mcc[j][k]);
+                                    f = f && isfinite(qv);
+                                }
+                            }
+                        }
+#pragma unroll
+                        for (int k = 0; k < RANK; ++k) {
+                            const float hg = __fadd_rn(__fadd_rn(pg[0][k], pg[2][k]), __fadd_rn(pg[1][k], pg[3][k]));
+                            const float hc = __fadd_rn(__fadd_rn(pc[0][k], pc[2][k]), __fadd_rn(pc[1][k], pc[3][k]));
+                            mr[k] = __dadd_rn(mr[k], (double)hg);
+                            mrc[k] = __dadd_rn(mrc[k], (double)hc);
+                        }
+                        wfast = fast_ok && __all_sync(0xffffffffu, !have || f);
+                    }
+                    float p[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) p[j] = __fmul_rn(quant[j], __fmul_rn(S[j], dy[j]));
+                    hrow[u0 + u] = __fadd_rn(__fadd_rn(p[0], p[1]), __fadd_rn(p[2], p[3]));
+                }
+            }
+            __syncwarp();
+            // dx: lanes = samples, the chunk's tiles in stored order
+            if (lane < nb)
+                for (int l = 0; l < n; ++l) a = __fadd_rn(a, hs_s[warp][l][lane]);
+#pragma unroll
+            for (int k = 0; k < NB; ++k)
+                if (sb == k) acc[k] = a;
+            __syncwarp();
+        }
+        if (!row_ok) continue;
+        if (have) {
+            uint8_t* tb = reinterpret_cast<uint8_t*>(V.tile + ti);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int64_t col = col0 + j;
+                const float imp_ratio = __fdiv_rn(ci[j], __fmul_rn(isr, L.ois[col]));
+                uint32_t wq, iq;
+                if (STOCH) {
+                    const uint64_t el = (1ULL << 61) | ((uint64_t)row * (uint64_t)L.n_out + (uint64_t)col);
+                    wq = fp4_quantize_stochastic(quant[j], rng_draw(P.call_key, el, 0));
+                    iq = fp4_quantize_stochastic(imp_ratio, rng_draw(P.call_key, el, 1));
+                } else {
+                    wq = fp4_encode(quant[j]);
+                    iq = fp4_encode(imp_ratio);
+                }
+                tb[j * 4 + li] = (uint8_t)((iq << 4) | wq);
+                if (OST) {
+                    const int64_t loc = ti - part_base;
+#pragma unroll
+                    for (int k = 0; k < RANK; ++k) {
+                        mcb[((loc * 16 + j * 4 + li) * RANK + k) * 2] = mc[j][k];
+                        mcb[((loc * 16 + j * 4 + li) * RANK + k) * 2 + 1] = mcc[j][k];
+                    }
+                }
+            }
+        }
+        // the row's value_scale totals: the tiles' double sums in stored order
+#pragma unroll
+        for (int k = 0; k < RANK; ++k)
+            for (int l = 0; l < n; ++l) {
+                tg[k] = __dadd_rn(tg[k], __shfl_sync(0xffffffffu, mr[k], l));
+                tc[k] = __dadd_rn(tc[k], __shfl_sync(0xffffffffu, mrc[k], l));
+            }
+    }
+    if (!row_ok) return;
+#pragma unroll
+    for (int k = 0; k < NB; ++k) {
+        const int b = k * 32 + lane;
+        if (b < B) dxT[row * B + b] = acc[k];
+    }
+    if (lane == 0) {
+        const float scale_eff_lr = __fdiv_rn(P.lr, (float)((uint32_t)nt * 4u));
+#pragma unroll
+        for (int k = 0; k < RANK; ++k)
+            if (tg[k] != 0.0 || tc[k] != 0.0) {
+                const int64_t i = row * RANK + k;
+                rmsprop_scale(L.vs + i, L.vsi + i, (float)tg[k], scale_eff_lr, (float)tc[k], L.vstep + i, P);
+            }
+    }
 }
 
 bool b4_update_split_applies(const LayerView& L) { return L.n_out % 4 == 0; }
@@ -936,6 +1344,50 @@ void launch_b4_update_split(const LayerView& L, const B4View& V, const float* xT
     }
     count_launch();
 }
+bool b4_update_rows_applies(const LayerView& L, int B) { return L.n_out % 4 == 0 && B > 0 && B <= 128 && B % 4 == 0; }
+
+void launch_b4_update_rows(const LayerView& L, const B4View& V, const float* xT, const float* dyT, int B,
+                           const UpdateParams& P, float* dxT, int64_t br0, int64_t br1, int64_t part_base,
+                           float* mcb, cudaStream_t s) {
+    if (br1 <= br0 || B == 0) return;
+    const unsigned nbr = (unsigned)(br1 - br0);
+#define SILI_B4R(R, ST, NBV)                                                                                \
+    do {                                                                                                   \
+        if (P.os_trainable)                                                                                \
+            k_b4_update_rows<R, ST, true, NBV><<<nbr, 128, 0, s>>>(L, V, xT, dyT, B, P, br0, part_base, mcb, dxT); \
+        else                                                                                               \
+            k_b4_update_rows<R, ST, false, NBV><<<nbr, 128, 0, s>>>(L, V, xT, dyT, B, P, br0, part_base, mcb, dxT); \
+    } while (0)
+#define SILI_B4R_NB(R, ST)              \
+    do {                                \
+        if (B <= 64) SILI_B4R(R, ST, 2); \
+        else SILI_B4R(R, ST, 4);         \
+    } while (0)
+    switch (L.rank * 2 + (P.stochastic ? 1 : 0)) {
+        case 2: SILI_B4R_NB(1, false); break;
+        case 3: SILI_B4R_NB(1, true); break;
+        case 4: SILI_B4R_NB(2, false); break;
+        case 5: SILI_B4R_NB(2, true); break;
+        case 6: SILI_B4R_NB(3, false); break;
+        case 7: SILI_B4R_NB(3, true); break;
+        case 8: SILI_B4R_NB(4, false); break;
+        default: SILI_B4R_NB(4, true); break;
+    }
+#undef SILI_B4R_NB
+#undef SILI_B4R
+    count_launch();
+    if (P.os_trainable) {
+        const unsigned cg = (unsigned)((L.n_out + 255) / 256);
+        switch (L.rank) {
+            case 1: k_b4_col_sums<1><<<cg, 256, 0, s>>>(L, V, br0, br1, part_base, mcb, P.colg, P.colc); break;
+            case 2: k_b4_col_sums<2><<<cg, 256, 0, s>>>(L, V, br0, br1, part_base, mcb, P.colg, P.colc); break;
+            case 3: k_b4_col_sums<3><<<cg, 256, 0, s>>>(L, V, br0, br1, part_base, mcb, P.colg, P.colc); break;
+            default: k_b4_col_sums<4><<<cg, 256, 0, s>>>(L, V, br0, br1, part_base, mcb, P.colg, P.colc); break;
+        }
+        count_launch();
+    }
+}
+
 void launch_b4_evict_rows(const LayerView& L, const B4View& V, cudaStream_t s) {
     if (V.BR == 0) return;
     k_b4_evict_rows<<<(unsigned)((V.BR + 3) / 4), 128, 0, s>>>(L, V, 0, V.BR);

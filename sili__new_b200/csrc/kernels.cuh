@@ -340,6 +340,12 @@ void launch_b4_update_split(const LayerView& L, const B4View& V, const float* xT
                             const UpdateParams& P, float* dxT, int64_t br0, int64_t br1, int64_t part_base,
                             float* hsb, double* mrb, float* mcb, cudaStream_t s);
 // the eviction pass after every chunk's update (a half-warp per block-row)
+// the warp-per-row update (no per-tile scratch; the packed flags are left to
+// launch_b4_evict_rows, which refreshes them)
+bool b4_update_rows_applies(const LayerView& L, int B);
+void launch_b4_update_rows(const LayerView& L, const B4View& V, const float* xT, const float* dyT, int B,
+                           const UpdateParams& P, float* dxT, int64_t br0, int64_t br1, int64_t part_base,
+                           float* mcb, cudaStream_t s);
 void launch_b4_evict_rows(const LayerView& L, const B4View& V, cudaStream_t s);
 // sparse-input forward block4 windows: y[B, n_out] += (xT/presT [n_in, B])
 void launch_b4_forward_sparse(const LayerView& L, const B4View& V, const float* xT, const uint8_t* presT, int B,

@@ -1513,9 +1513,35 @@ static int b4_update(sili_layer* h, const LayerView& v, int batch, const UpdateP
     }
     if (P.os_trainable) RC(ensure_b4_index(h, s));   // the column sums walk it
     const int64_t BR = h->b4_BR;
+    if (b4_update_rows_applies(v, batch) && !P.os_trainable) {
+        // a warp per row: no per-tile scratch
+        launch_b4_update_rows(v, V, h->xT.p, h->dyT.p, batch, P, h->dxT.p, 0, BR, 0, nullptr, s);
+        launch_b4_evict_rows(v, V, s);
+        return SILI_OK;
+    }
     std::vector<int64_t> es((size_t)BR + 1);
     CK(cudaMemcpyAsync(es.data(), h->b4_es.p, (size_t)(BR + 1) * 8, cudaMemcpyDeviceToHost, s));
     CK(cudaStreamSynchronize(s));
+    if (b4_update_rows_applies(v, batch)) {
+        // the output scale trains: per-slot column sums in parts of at most 4 GiB
+        const int64_t per_tile = (int64_t)16 * h->rank * 2 * 4;
+        const int64_t limit = std::max<int64_t>(1, ((int64_t)4 << 30) / per_tile);
+        std::vector<std::pair<int64_t, int64_t>> parts;
+        int64_t most = 1;
+        for (int64_t br0 = 0; br0 < BR;) {
+            int64_t br1 = br0 + 1;
+            while (br1 < BR && es[br1 + 1] - es[br0] <= limit) ++br1;
+            parts.emplace_back(br0, br1);
+            most = std::max(most, es[br1] - es[br0]);
+            br0 = br1;
+        }
+        RC(h->b4_mc.reserve(most * 16 * h->rank * 2 + 1));
+        for (const auto& c : parts)
+            launch_b4_update_rows(v, V, h->xT.p, h->dyT.p, batch, P, h->dxT.p, c.first, c.second, es[c.first],
+                                  h->b4_mc.p, s);
+        launch_b4_evict_rows(v, V, s);
+        return SILI_OK;
+    }
     const int64_t per_tile = (int64_t)4 * batch * 4 + (int64_t)4 * h->rank * 2 * 8 + (int64_t)16 * h->rank * 2 * 4;
     const int64_t limit = std::max<int64_t>(1, ((int64_t)4 << 30) / per_tile);   // 4 GiB
     std::vector<std::pair<int64_t, int64_t>> chunks;

@@ -566,10 +566,15 @@ __device__ int synap_row(Ctx& c, int64_t r, const SynParams& P, uint32_t* ecol, 
 
 // One thread per block-row (or one thread for the whole sweep when
 // sequential).  Sweep position i covers row (row0 + i) % R; rows at
-// positions > limit are left alone.
+// positions > limit are left alone.  The block-row's thread is lane 0 of its
+// own warp: the row steps branch on the data (sorts, searches, row
+// rewrites), and lanes of one warp on different block-rows would run those
+// branches one after another; one working lane per warp lets the scheduler
+// interleave the block-rows instead.
 __global__ void k_synap(SynView V, SynParams P, int sequential) {
     const int64_t R = V.n_in, BR = (R + 3) / 4;
-    const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if ((threadIdx.x & 31) != 0) return;
+    const int64_t tid = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (sequential ? tid != 0 : tid >= BR) return;
     Ctx c;
     c.V = V;
@@ -635,9 +640,9 @@ __global__ void k_synap(SynView V, SynParams P, int sequential) {
 void launch_synap(const SynView& V, const SynParams& P, bool sequential, cudaStream_t s) {
     const int64_t BR = (V.n_in + 3) / 4;
     if (sequential) {
-        k_synap<<<1, 1, 0, s>>>(V, P, 1);
+        k_synap<<<1, 32, 0, s>>>(V, P, 1);
     } else {
-        k_synap<<<(unsigned)((BR + 63) / 64), 64, 0, s>>>(V, P, 0);
+        k_synap<<<(unsigned)((BR + 3) / 4), 128, 0, s>>>(V, P, 0);
     }
     count_launch();
 }

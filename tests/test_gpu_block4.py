@@ -87,7 +87,8 @@ def _check_state(g, o, tag):
 
 @pytest.mark.parametrize("n_in,n_out,dens,rank,B", [(258, 301, 0.15, 1, 64), (64, 96, 0.5, 2, 40),
                                                     (130, 70, 0.05, 1, 9), (130, 72, 0.1, 1, 20),
-                                                    (44, 400, 0.3, 3, 33), (44, 401, 0.3, 3, 33)])
+                                                    (44, 400, 0.3, 3, 33), (44, 401, 0.3, 3, 33),
+                                                    (256, 512, 0.05, 1, 128), (96, 200, 0.2, 2, 100)])
 def test_block4_vs_oracle(n_in, n_out, dens, rank, B):
     rng = np.random.default_rng(n_in)
     wc, ic = _codes(rng, n_in, n_out, dens)
