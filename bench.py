@@ -232,9 +232,8 @@ def run_block4(args, dev, S, torch, work, cpu_sample):
     wc, ic = block4_codes(work)
     L = S.SparseLinearLayer(N_IN, N_OUT, len(i), 1, dev)
     L.load_dense_codes(wc, ic)
-    for r in range(N_IN):
-        L.set_value_scale_raw(r, float(vs[r]))
-        L.set_importance_scale_raw(r, LR / 6.0)
+    L.set_scales(S._cuda.SCALE_VALUE, np.ascontiguousarray(vs, np.float32))
+    L.set_scales(S._cuda.SCALE_IMPORTANCE, np.full(N_IN, LR / 6.0, np.float32))
     xs = torch.from_numpy(x).cuda(dev)
     dys = torch.from_numpy(dy).cuda(dev)
     y = torch.empty(BATCH, N_OUT, device=f"cuda:{dev}")

@@ -93,52 +93,93 @@ __device__ void ss_insertion(int* f, int* l, const SortKeys& K) {
         }
     }
 }
-// Partitions of disjoint ranges do not interact, so the explicit stack may
-// visit them in any order and still give std::sort's permutation.
-__device__ void std_sort(int* a, int n, const SortKeys& K) {
-    if (n <= 1) return;
-    int lg = 0;
-    while ((1 << (lg + 1)) <= n) ++lg;
-    struct Frame { int* f; int* l; int depth; };
-    Frame st[64];
-    int sp = 0;
-    st[sp++] = {a, a + n, 2 * lg};
-    while (sp > 0) {
-        Frame fr = st[--sp];
-        int* f = fr.f;
-        int* l = fr.l;
-        int depth = fr.depth;
-        while (l - f > 16) {
-            if (depth == 0) { ss_heapsort(f, (int)(l - f), K); break; }
-            --depth;
-            int *x = f + 1, *y = f + (l - f) / 2, *z = l - 1;
-            if (K.lt(*x, *y)) {
-                if (K.lt(*y, *z)) ss_swap(f, y);
-                else if (K.lt(*x, *z)) ss_swap(f, z);
-                else ss_swap(f, x);
-            } else if (K.lt(*x, *z)) ss_swap(f, x);
-            else if (K.lt(*y, *z)) ss_swap(f, z);
-            else ss_swap(f, y);
-            int *lo = f + 1, *hi = l;
-            for (;;) {
-                while (K.lt(*lo, *f)) ++lo;
-                --hi;
-                while (K.lt(*f, *hi)) --hi;
-                if (!(lo < hi)) break;
-                ss_swap(lo, hi);
-                ++lo;
-            }
-            if (sp < 64) st[sp++] = {lo, l, depth};
-            l = lo;
-        }
+// __unguarded_partition_pivot: median of three moved to f, Hoare partition
+// of [f + 1, l) around it; returns the cut
+__device__ int* ss_partition(int* f, int* l, const SortKeys& K) {
+    int *x = f + 1, *y = f + (l - f) / 2, *z = l - 1;
+    if (K.lt(*x, *y)) {
+        if (K.lt(*y, *z)) ss_swap(f, y);
+        else if (K.lt(*x, *z)) ss_swap(f, z);
+        else ss_swap(f, x);
+    } else if (K.lt(*x, *z)) ss_swap(f, x);
+    else if (K.lt(*y, *z)) ss_swap(f, z);
+    else ss_swap(f, y);
+    int *lo = f + 1, *hi = l;
+    for (;;) {
+        while (K.lt(*lo, *f)) ++lo;
+        --hi;
+        while (K.lt(*f, *hi)) --hi;
+        if (!(lo < hi)) break;
+        ss_swap(lo, hi);
+        ++lo;
     }
-    if (n > 16) {
-        ss_insertion(a, a + 16, K);
-        for (int* i = a + 16; i != a + n; ++i) ss_linear_insert(i, K);
-    } else {
-        ss_insertion(a, a + n, K);
-    }
+    return lo;
 }
+// std::sort's permutation (GCC's introsort: ranges of more than 16 are
+// partitioned, depth-limited to 2 log2 n with heapsort beyond, then one
+// insertion pass), produced front to back on demand: extend(m) makes
+// positions [0, m) final, extend(n) is the whole std::sort.  Ranges are kept
+// on an explicit stack: partitions of disjoint ranges do not interact, so
+// they may be visited in any order.  Partial extension is valid for keys in
+// a strict weak order (no NaN): after a partition every element right of the cut is not less than every
+// element left of it, and the final insertion passes move an element only
+// leftwards past strictly greater ones, so no element ever crosses a cut.
+// Hence the prefix [0, P) -- P the start of the leftmost range not yet
+// partitioned -- is final once every range starting below P is partitioned
+// and the insertion passes of std::sort have run over [0, P); ranges starting
+// at or beyond the requested end are left for later calls.  Each range is
+// partitioned from the same contents as in std::sort (nothing else touches
+// it first), so the permutation is std::sort's.
+struct LazySort {
+    struct Frame { int* f; int* l; int depth; };
+    int* a;
+    int n;
+    int done;   // [0, done) final
+    int sp;
+    Frame st[64];
+    __device__ void init(int* arr, int len) {
+        a = arr; n = len; done = 0; sp = 0;
+        if (n <= 1) { done = n; return; }
+        int lg = 0;
+        while ((1 << (lg + 1)) <= n) ++lg;
+        st[sp++] = {a, a + n, 2 * lg};
+    }
+    __device__ void extend(int m, const SortKeys& K) {
+        if (m <= done) return;
+        m = m < 16 ? 16 : m;
+        if (m > n) m = n;
+        // partition every pending range that starts below m
+        for (;;) {
+            int pick = -1;
+            for (int i = 0; i < sp; ++i)
+                if (st[i].f - a < m) { pick = i; break; }
+            if (pick < 0) break;
+            const Frame fr = st[pick];
+            st[pick] = st[--sp];
+            int* f = fr.f;
+            int* l = fr.l;
+            int depth = fr.depth;
+            while (l - f > 16) {
+                if (depth == 0) { ss_heapsort(f, (int)(l - f), K); break; }
+                --depth;
+                int* lo = ss_partition(f, l, K);
+                if (sp < 64) st[sp++] = {lo, l, depth};
+                l = lo;
+            }
+        }
+        int P = n;
+        for (int i = 0; i < sp; ++i)
+            if ((int)(st[i].f - a) < P) P = (int)(st[i].f - a);
+        // std::sort's insertion passes over [done, P)
+        int i0 = done;
+        if (done == 0) {
+            ss_insertion(a, a + (n > 16 ? 16 : n), K);
+            i0 = 16;
+        }
+        for (int i = i0; i < P; ++i) ss_linear_insert(a + i, K);
+        done = P > done ? P : done;
+    }
+};
 
 __device__ __forceinline__ int uleb_len(uint32_t v) { int n = 0; do { v >>= 7; ++n; } while (v); return n; }
 __device__ __forceinline__ int uleb_put(uint32_t v, uint8_t* p) {
@@ -502,25 +543,52 @@ __device__ int synap_row(Ctx& c, int64_t r, const SynParams& P, uint32_t* ecol, 
         pss[np] = c.V.pval[p];
         ++np;
     }
-    // removals by stored importance ascending (:1147-1167)
+    // removals by stored importance ascending (:1147-1167).  Without a NaN
+    // key the removals are a prefix of the sorted order (the clamped
+    // importance only grows along it and keep only shrinks, so the first
+    // position not taken ends the scan), and only that prefix is sorted.
     for (int i = 0; i < n_exist; ++i) by[i] = i;
-    std_sort(by, n_exist, SortKeys{eimp, nullptr, 0});
+    const SortKeys K0{eimp, nullptr, 0};
+    bool key_nan = false;
+    for (int i = 0; i < n_exist; ++i) key_nan = key_nan || isnan(eimp[i]);
+    LazySort ls;   // one frame stack for the three sorts (extend(n) is std::sort)
     int nrm = 0;
-    for (int a = 0; a < n_exist && nrm < P.max_prune; ++a) {
-        const int k = by[a];
-        const int keep = n_exist - nrm;
-        const float fl = (eimp[k] < P.eps) ? P.eps : eimp[k];
-        if (fl < P.cutoff || keep > P.max_rw) { rmc[nrm] = ecol[k]; rmb[nrm] = eb4[k]; ++nrm; }
+    if (key_nan) {
+        ls.init(by, n_exist);
+        ls.extend(n_exist, K0);
+        for (int a = 0; a < n_exist && nrm < P.max_prune; ++a) {
+            const int k = by[a];
+            const int keep = n_exist - nrm;
+            const float fl = (eimp[k] < P.eps) ? P.eps : eimp[k];
+            if (fl < P.cutoff || keep > P.max_rw) { rmc[nrm] = ecol[k]; rmb[nrm] = eb4[k]; ++nrm; }
+        }
+    } else {
+        ls.init(by, n_exist);
+        for (int a = 0; a < n_exist && nrm < P.max_prune; ++a) {
+            ls.extend(a + 1, K0);
+            const int k = by[a];
+            const int keep = n_exist - nrm;
+            const float fl = (eimp[k] < P.eps) ? P.eps : eimp[k];
+            if (!(fl < P.cutoff || keep > P.max_rw)) break;
+            rmc[nrm] = ecol[k]; rmb[nrm] = eb4[k]; ++nrm;
+        }
     }
     for (int i = 0; i < nrm; ++i) rperm[i] = i;
-    std_sort(rperm, nrm, SortKeys{nullptr, rmc, 2});
-    // adds by score descending (:1171-1201)
+    ls.init(rperm, nrm);
+    ls.extend(nrm, SortKeys{nullptr, rmc, 2});
+    // adds by score descending (:1171-1201), the sorted order produced as far
+    // as the scan reads it
     for (int i = 0; i < np; ++i) pidx[i] = i;
-    std_sort(pidx, np, SortKeys{pss, nullptr, 1});
+    const SortKeys K1{pss, nullptr, 1};
+    bool score_nan = false;
+    for (int i = 0; i < np; ++i) score_nan = score_nan || isnan(pss[i]);
+    ls.init(pidx, np);
+    if (score_nan) ls.extend(np, K1);
     const unsigned long long slots = (unsigned long long)((long long)P.max_rw - (long long)(n_exist - nrm));
     int nadd = 0;
     for (int a = 0; a < np; ++a) {
         if ((unsigned long long)nadd >= slots) break;
+        if (!score_nan) ls.extend(a + 1, K1);
         const uint32_t col = pcs[pidx[a]];
         bool exists = false;
         for (int i = 0; i < n_exist; ++i) if (ecol[i] == col) { exists = true; break; }

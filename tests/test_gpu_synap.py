@@ -63,6 +63,10 @@ def _train(layers, rng, n_in, n_out, steps, B=16, lr=0.01):
     (256, 256, 24, 0.05, 3, 0.002, 2),
     (130, 301, 40, 0.2, 8, 1e30, 1),      # cutoff above everything: prune max_prune per row
     (64, 64, 10, 0.5, 2, 0.002, 3),       # dense-ish: many promotions and demotions
+    # long removal and add scans: the sorted orders are produced past their
+    # first 16 positions, in several extensions
+    (160, 400, 60, 0.5, 40, 1e30, 1),
+    (96, 200, 48, 0.3, 30, 0.002, 2),
 ])
 def test_synap_vs_oracle(n_in, n_out, per, k_frac, max_prune, cut, sweeps):
     p, i, w, vs = random_layer(n_in, n_out, per, seed=n_in + per)
