@@ -1344,6 +1344,28 @@ void launch_b4_update_split(const LayerView& L, const B4View& V, const float* xT
     }
     count_launch();
 }
+// b4_relayout's move: block-row br's nt[br] tiles from old_es[br] to
+// new_es[br] in the new arrays (a warp per block-row)
+__global__ void k_b4_move(int64_t BR, const int64_t* __restrict__ old_es, const int64_t* __restrict__ new_es,
+                          const int* __restrict__ nt, const int* __restrict__ bc, const uint4* __restrict__ tile,
+                          const uint8_t* __restrict__ sp, int* __restrict__ nbc, uint4* __restrict__ ntile,
+                          uint8_t* __restrict__ nsp) {
+    const int64_t br = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (br >= BR) return;
+    const int64_t o = old_es[br], d = new_es[br];
+    for (int e = threadIdx.x & 31; e < nt[br]; e += 32) {
+        nbc[d + e] = bc[o + e];
+        ntile[d + e] = tile[o + e];
+        nsp[d + e] = sp[o + e];
+    }
+}
+void launch_b4_move(int64_t BR, const int64_t* old_es, const int64_t* new_es, const int* nt, const int* bc,
+                    const uint4* tile, const uint8_t* sp, int* nbc, uint4* ntile, uint8_t* nsp, cudaStream_t s) {
+    if (BR <= 0) return;
+    k_b4_move<<<(unsigned)((BR + 7) / 8), 256, 0, s>>>(BR, old_es, new_es, nt, bc, tile, sp, nbc, ntile, nsp);
+    count_launch();
+}
+
 bool b4_update_rows_applies(const LayerView& L, int B) { return L.n_out % 4 == 0 && B > 0 && B <= 128 && B % 4 == 0; }
 
 void launch_b4_update_rows(const LayerView& L, const B4View& V, const float* xT, const float* dyT, int B,

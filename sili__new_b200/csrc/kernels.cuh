@@ -347,6 +347,9 @@ void launch_b4_update_rows(const LayerView& L, const B4View& V, const float* xT,
                            const UpdateParams& P, float* dxT, int64_t br0, int64_t br1, int64_t part_base,
                            float* mcb, cudaStream_t s);
 void launch_b4_evict_rows(const LayerView& L, const B4View& V, cudaStream_t s);
+// the tiles of every block-row moved to new offsets (new arrays)
+void launch_b4_move(int64_t BR, const int64_t* old_es, const int64_t* new_es, const int* nt, const int* bc,
+                    const uint4* tile, const uint8_t* sp, int* nbc, uint4* ntile, uint8_t* nsp, cudaStream_t s);
 // sparse-input forward block4 windows: y[B, n_out] += (xT/presT [n_in, B])
 void launch_b4_forward_sparse(const LayerView& L, const B4View& V, const float* xT, const uint8_t* presT, int B,
                               float* y, cudaStream_t s);

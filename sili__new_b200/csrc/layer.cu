@@ -126,6 +126,11 @@ struct sili_layer {
     DBuf<int> out_degree;
     DBuf<int> prow, pcol;
     DBuf<float> pval;
+    // build_probes' scratch, kept between calls (allocating it per call cost
+    // more than the probe kernels)
+    DBuf<float> pb_keys;
+    DBuf<int> pb_iota, pb_in, pb_out, pb_flags, pb_pos, pb_tr, pb_tc, pb_counts;
+    DBuf<float> pb_tv;
     int64_t n_probes = 0;
     // running stats (delta_csr_types.hpp:1265-1281)
     double st[4] = {0, 0, 0, 0};   // value_l1, value_l2_sq, importance_l1, importance_l2_sq
@@ -893,9 +898,7 @@ int64_t b4_live_total(sili_layer* h, cudaStream_t s) {
 // Re-lay the block4 store out so block-row br has newcap[br] tile slots.
 int b4_relayout(sili_layer* h, const std::vector<int64_t>& newcap, cudaStream_t s) {
     const int64_t BR = h->b4_BR;
-    std::vector<int64_t> es((size_t)BR + 1);
     std::vector<int> nt((size_t)BR + 1);
-    CK(cudaMemcpyAsync(es.data(), h->b4_es.p, (size_t)(BR + 1) * 8, cudaMemcpyDeviceToHost, s));
     CK(cudaMemcpyAsync(nt.data(), h->b4_nt.p, (size_t)BR * 4, cudaMemcpyDeviceToHost, s));
     CK(cudaStreamSynchronize(s));
     std::vector<int64_t> ne((size_t)BR + 1, 0);
@@ -904,15 +907,11 @@ int b4_relayout(sili_layer* h, const std::vector<int64_t>& newcap, cudaStream_t 
     DBuf<int> nbc;
     DBuf<uint4> ntile;
     DBuf<uint8_t> nsp;
-    RC(nbc.reserve(total)); RC(ntile.reserve(total)); RC(nsp.reserve(total));
-    for (int64_t br = 0; br < BR; ++br) {
-        const int n = nt[(size_t)br];
-        if (!n) continue;
-        CK(cudaMemcpyAsync(nbc.p + ne[(size_t)br], h->b4_bc.p + es[(size_t)br], (size_t)n * 4, cudaMemcpyDeviceToDevice, s));
-        CK(cudaMemcpyAsync(ntile.p + ne[(size_t)br], h->b4_tile.p + es[(size_t)br], (size_t)n * 16, cudaMemcpyDeviceToDevice, s));
-        CK(cudaMemcpyAsync(nsp.p + ne[(size_t)br], h->b4_sparse.p + es[(size_t)br], (size_t)n, cudaMemcpyDeviceToDevice, s));
-    }
-    CK(cudaMemcpyAsync(h->b4_es.p, ne.data(), (size_t)(BR + 1) * 8, cudaMemcpyHostToDevice, s));
+    DBuf<int64_t> nes;
+    RC(nbc.reserve(total)); RC(ntile.reserve(total)); RC(nsp.reserve(total)); RC(nes.reserve(BR + 1));
+    CK(cudaMemcpyAsync(nes.p, ne.data(), (size_t)(BR + 1) * 8, cudaMemcpyHostToDevice, s));
+    launch_b4_move(BR, h->b4_es.p, nes.p, h->b4_nt.p, h->b4_bc.p, h->b4_tile.p, h->b4_sparse.p, nbc.p, ntile.p, nsp.p, s);
+    CK(cudaMemcpyAsync(h->b4_es.p, nes.p, (size_t)(BR + 1) * 8, cudaMemcpyDeviceToDevice, s));
     CK(cudaStreamSynchronize(s));
     h->b4_bc.swap(nbc); h->b4_tile.swap(ntile); h->b4_sparse.swap(nsp);
     h->b4_dirty = true;
@@ -966,8 +965,11 @@ int synap_prepare(sili_layer* h, int64_t nrows, cudaStream_t s) {
         if (need[(size_t)br] > es4[(size_t)br + 1] - es4[(size_t)br]) grow = true;
     }
     if (grow) {
+        // a quarter more than this sweep can need, so that the tiles created
+        // by the next sweeps' promotions rarely force another relayout
         for (int64_t br = 0; br < BR; ++br)
-            need[(size_t)br] = std::max(need[(size_t)br] + 8, es4[(size_t)br + 1] - es4[(size_t)br]);
+            need[(size_t)br] = std::max(need[(size_t)br] + std::max<int64_t>(8, need[(size_t)br] / 4),
+                                        es4[(size_t)br + 1] - es4[(size_t)br]);
         RC(b4_relayout(h, need, s));
     }
     for (int64_t br = 0; br < BR; ++br)
@@ -1852,8 +1854,8 @@ int sili_layer_backward_sparse(sili_layer* h, const float* x, const int* dptrs, 
 // partial_sort leaves tie order unspecified).
 static int sorted_desc(sili_layer* h, const float* keys, int64_t n, DBuf<int>& out_idx) {
     cudaStream_t s = h->stream;
-    DBuf<float> ko;
-    DBuf<int> vin;
+    DBuf<float>& ko = h->pb_keys;
+    DBuf<int>& vin = h->pb_iota;
     RC(ko.reserve(n + 1)); RC(vin.reserve(n + 1)); RC(out_idx.reserve(n + 1));
     launch_iota(vin.p, n, s);
     size_t bytes = 0;
@@ -1873,14 +1875,16 @@ int sili_layer_build_probes(sili_layer* h, int k, int per_row) {
     if (R == 0 || C == 0 || k <= 0) return SILI_OK;
     RC(ensure_aux(h, s));
     const int kin = (int)std::min<int64_t>(k, R);
-    DBuf<int> in_sorted, out_sorted;
+    DBuf<int>& in_sorted = h->pb_in;
+    DBuf<int>& out_sorted = h->pb_out;
     RC(sorted_desc(h, h->in_acc.p, R, in_sorted));
     RC(sorted_desc(h, h->grad_acc.p, C, out_sorted));
     LayerView v = h->view();
     if (!per_row) {
         const int kout = (int)std::min<int64_t>(k, C);
         const int64_t n = (int64_t)kin * kout;
-        DBuf<int> flags, pos;
+        DBuf<int>& flags = h->pb_flags;
+        DBuf<int>& pos = h->pb_pos;
         RC(flags.reserve(n + 1)); RC(pos.reserve(n + 1));
         CK(cudaMemsetAsync(flags.p, 0, (size_t)(n + 1) * 4, s));
         launch_probe_flags(v, in_sorted.p, kin, out_sorted.p, kout, flags.p, s);
@@ -1894,8 +1898,10 @@ int sili_layer_build_probes(sili_layer* h, int k, int per_row) {
         h->n_probes = total;
     } else {
         const int64_t cap = (int64_t)kin * k;
-        DBuf<int> tr, tc, counts;
-        DBuf<float> tv;
+        DBuf<int>& tr = h->pb_tr;
+        DBuf<int>& tc = h->pb_tc;
+        DBuf<int>& counts = h->pb_counts;
+        DBuf<float>& tv = h->pb_tv;
         RC(tr.reserve(cap + 1)); RC(tc.reserve(cap + 1)); RC(tv.reserve(cap + 1)); RC(counts.reserve(kin + 1));
         launch_probe_per_row(v, in_sorted.p, kin, out_sorted.p, C, k, h->in_acc.p, h->grad_acc.p, tr.p, tc.p, tv.p,
                              counts.p, s);

@@ -10,7 +10,7 @@
 // block4 byte budgets (the reference throws / drops when a running total
 // would pass them), out_degree's clamp at zero, and the first row that runs
 // out of blank space (the reference stops the sweep there).  The kernel runs
-// one thread per block-row, each taking its rows in sweep order; the host
+// one warp per block-row, taking its rows in sweep order; the host
 // checks afterwards whether any of the three could have depended on the
 // order and, if so, restores the snapshot and re-runs exactly: truncated at
 // the first failing row, or in one thread over the whole sweep in order.
@@ -215,48 +215,168 @@ __device__ __forceinline__ int64_t tlen(const uint4& t, uint8_t sp) {
 
 constexpr int kOK = 0, kENOMEM = 2, kEHEADROOM = 3;
 
-// Per-thread context: the layer state plus this thread's scratch.
+// The block-row's context: the layer state plus its scratch.  All 32 lanes
+// of the block-row's warp run the row step together: the scalar logic on
+// every lane from the same data (so control flow stays uniform), the scans
+// over a row's entries (ULEB128 decode, rewrite, searches, filters) spread
+// over the lanes, and every write of layer state or scratch that the lanes
+// do not split among themselves -- the block4 store, the counters, the
+// sorted orders -- by lane 0, followed by __syncwarp before the lanes read
+// it again.
 struct Ctx {
     SynView V;
     int64_t R, C, BR;
-    // scratch (per thread)
+    // scratch (per block-row)
     uint32_t* rc;   // row-op columns [M]
     uint8_t* rv;    // row-op values  [M]
-    // block4 running totals (sequential mode only)
+    // block4 running totals (sequential mode only; lane 0's copy is the one used)
     int64_t tot_idx, tot_tile;
     bool seq;
+    int lane;
 };
+constexpr unsigned kFull = 0xffffffffu;
 
 // ── scattered rows ──
 __device__ int row_nnz(const Ctx& c, int64_t r) { return (int)(c.V.ee[r] - c.V.es[r]); }
+// the row's absolute columns into cols (all lanes).  Each step reads the next
+// 32 bytes; the bytes without a continuation bit end the entries; a lane
+// ending an entry gathers its 7-bit groups (at most 5 count: uleb_get's
+// shifts past 31 bits drop the rest) and a warp scan of the deltas gives the
+// columns.  An entry longer than 32 bytes (never written by this library)
+// is decoded by lane 0 alone.
 __device__ int decode_row(const Ctx& c, int64_t r, uint32_t* cols) {
     const int n = row_nnz(c, r);
+    const int lane = c.lane;
     int64_t pos = c.V.bs[r];
-    uint32_t col = 0;
-    for (int k = 0; k < n; ++k) { col += uleb_get(c.V.idx, pos); cols[k] = col; }
+    const int64_t cap_end = c.V.bs[r + 1];
+    uint32_t carry = 0;
+    int k = 0;
+    while (k < n) {
+        const uint32_t b = pos + lane < cap_end ? (uint32_t)c.V.idx[pos + lane] : 0u;
+        const unsigned T = __ballot_sync(kFull, (b & 0x80u) == 0u);
+        const int m = min(__popc(T), n - k);
+        if (m == 0) {
+            if (lane == 0) {
+                int64_t p = pos;
+                uint32_t col = carry;
+                for (int q = k; q < n; ++q) { col += uleb_get(c.V.idx, p); cols[q] = col; }
+            }
+            break;
+        }
+        const unsigned below = T & ((1u << lane) - 1u);
+        const int rank = __popc(below);
+        const bool take = ((T >> lane) & 1u) && rank < m;
+        const int S = below ? 32 - __clz(below) : 0;   // this lane's entry starts after the previous end
+        uint32_t v = 0;
+#pragma unroll
+        for (int t = 0; t < 5; ++t) {
+            const uint32_t bj = __shfl_sync(kFull, b, min(S + t, 31));
+            if (S + t <= lane) v |= (bj & 0x7Fu) << (7 * t);
+        }
+        uint32_t d = take ? v : 0u;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t t = __shfl_up_sync(kFull, d, o);
+            if (lane >= o) d += t;
+        }
+        if (take) cols[k + rank] = carry + d;
+        const int last = __ffs(__ballot_sync(kFull, take && rank == m - 1)) - 1;
+        carry += __shfl_sync(kFull, d, last);
+        pos += last + 1;
+        k += m;
+    }
+    __syncwarp();
     return n;
 }
+// first index in [0, n) whose column satisfies the test (eq: == col, else
+// >= col), or n; all lanes
+__device__ int find_col(const Ctx& c, const uint32_t* cols, int n, uint32_t col, bool eq) {
+    for (int k0 = 0; k0 < n; k0 += 32) {
+        const int k = k0 + c.lane;
+        const bool hit = k < n && (eq ? cols[k] == col : cols[k] >= col);
+        const unsigned m = __ballot_sync(kFull, hit);
+        if (m) return k0 + __ffs(m) - 1;
+    }
+    return n;
+}
+// The new row of n entries, entry k being (as is) k, (drop) k < i ? k : k + 1,
+// or (insert) k < i ? k : k == i ? (col, val) : k - 1 of the scratch row
+// rc / rv.
+struct RowMap {
+    int mode;   // 0 as is, 1 drop entry i, 2 insert (col, val) at i
+    int i;
+    uint32_t col;
+    uint8_t val;
+    __device__ __forceinline__ void get(const Ctx& c, int k, uint32_t& col_k, uint8_t& v_k) const {
+        if (mode == 1) {
+            const int s = k < i ? k : k + 1;
+            col_k = c.rc[s]; v_k = c.rv[s];
+        } else if (mode == 2 && k >= i) {
+            if (k == i) { col_k = col; v_k = val; }
+            else { col_k = c.rc[k - 1]; v_k = c.rv[k - 1]; }
+        } else {
+            col_k = c.rc[k]; v_k = c.rv[k];
+        }
+    }
+};
 // rewrite the live part of row r (the state delta_csr_row_remove_col /
-// _insert_col leave behind, delta_csr_memory.hpp:429-585)
-__device__ int row_write(Ctx& c, int64_t r, const uint32_t* cols, const uint8_t* vals, int n) {
-    int64_t nb = 0;
-    uint32_t prev = 0;
-    for (int i = 0; i < n; ++i) { nb += uleb_len(cols[i] - prev); prev = cols[i]; }
+// _insert_col leave behind, delta_csr_memory.hpp:429-585), all lanes: each
+// lane encodes its entries at offsets from a warp scan of the encoded lengths
+__device__ int row_write(Ctx& c, int64_t r, const RowMap& M, int n) {
+    const int lane = c.lane;
+    long long nb = 0;
+    for (int k0 = 0; k0 < n; k0 += 32) {
+        const int k = k0 + lane;
+        if (k < n) {
+            uint32_t ck, cp = 0;
+            uint8_t v;
+            M.get(c, k, ck, v);
+            if (k > 0) M.get(c, k - 1, cp, v);
+            nb += uleb_len(ck - cp);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) nb += __shfl_xor_sync(kFull, nb, o);
     if (nb > c.V.bs[r + 1] - c.V.bs[r]) return kEHEADROOM;
     if (n > c.V.es[r + 1] - c.V.es[r]) return kEHEADROOM;
     int64_t bp = c.V.bs[r];
-    prev = 0;
-    for (int i = 0; i < n; ++i) { bp += uleb_put(cols[i] - prev, c.V.idx + bp); prev = cols[i]; }
-    c.V.be[r] = bp;
-    for (int i = 0; i < n; ++i) c.V.val[c.V.es[r] + i] = vals[i];
-    atomicAdd(c.V.nnz_delta, (unsigned long long)(long long)(n - row_nnz(c, r)));
-    c.V.ee[r] = c.V.es[r] + n;
+    for (int k0 = 0; k0 < n; k0 += 32) {
+        const int k = k0 + lane;
+        uint32_t ck = 0, cp = 0;
+        uint8_t v = 0, vp;
+        int len = 0;
+        if (k < n) {
+            M.get(c, k, ck, v);
+            if (k > 0) M.get(c, k - 1, cp, vp);
+            len = uleb_len(ck - cp);
+        }
+        int incl = len;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int t = __shfl_up_sync(kFull, incl, o);
+            if (lane >= o) incl += t;
+        }
+        if (k < n) {
+            uleb_put(ck - cp, c.V.idx + bp + (incl - len));
+            c.V.val[c.V.es[r] + k] = v;
+        }
+        bp += __shfl_sync(kFull, incl, 31);
+    }
+    if (lane == 0) {
+        c.V.be[r] = c.V.bs[r] + nb;
+        atomicAdd(c.V.nnz_delta, (unsigned long long)(long long)(n - row_nnz(c, r)));
+        c.V.ee[r] = c.V.es[r] + n;
+    }
+    __syncwarp();
     return kOK;
 }
-__device__ bool insert_fits(const Ctx& c, int64_t r, const uint32_t* cols, int n, uint32_t col) {
-    int i = 0;
-    uint32_t prev = 0;
-    while (i < n && cols[i] < col) { prev = cols[i]; ++i; }
+// the row's value bytes into rv (all lanes)
+__device__ void load_vals(Ctx& c, int64_t r, int n) {
+    for (int k = c.lane; k < n; k += 32) c.rv[k] = c.V.val[c.V.es[r] + k];
+    __syncwarp();
+}
+__device__ bool insert_fits(const Ctx& c, int64_t r, const uint32_t* cols, int n, int i, uint32_t col) {
+    const uint32_t prev = i > 0 ? cols[i - 1] : 0u;
     int64_t delta = uleb_len(col - prev);
     if (i < n) delta += uleb_len(cols[i] - col) - uleb_len(cols[i] - prev);
     const int64_t used = c.V.be[r] - c.V.bs[r];
@@ -266,26 +386,20 @@ __device__ bool insert_fits(const Ctx& c, int64_t r, const uint32_t* cols, int n
 }
 __device__ bool sc_remove_col(Ctx& c, int64_t r, uint32_t col) {
     const int n = decode_row(c, r, c.rc);
-    int i = 0;
-    while (i < n && c.rc[i] != col) ++i;
+    const int i = find_col(c, c.rc, n, col, true);
     if (i == n) return false;
-    for (int k = 0; k < n; ++k) c.rv[k] = c.V.val[c.V.es[r] + k];
-    for (int k = i; k + 1 < n; ++k) { c.rc[k] = c.rc[k + 1]; c.rv[k] = c.rv[k + 1]; }
-    row_write(c, r, c.rc, c.rv, n - 1);
+    load_vals(c, r, n);
+    row_write(c, r, RowMap{1, i, 0u, 0}, n - 1);
     return true;
 }
 // delta_csr_row_insert_col with ValueAccessor::set (deterministic codes)
 __device__ bool sc_insert_col(Ctx& c, int64_t r, uint32_t col, float w, float imp) {
     const int n = decode_row(c, r, c.rc);
-    int i = 0;
-    while (i < n && c.rc[i] < col) ++i;
+    const int i = find_col(c, c.rc, n, col, false);
     if (i < n && c.rc[i] == col) return false;
-    if (!insert_fits(c, r, c.rc, n, col)) return false;
-    for (int k = 0; k < n; ++k) c.rv[k] = c.V.val[c.V.es[r] + k];
-    for (int k = n; k > i; --k) { c.rc[k] = c.rc[k - 1]; c.rv[k] = c.rv[k - 1]; }
-    c.rc[i] = col;
-    c.rv[i] = (uint8_t)((fp4_encode(w) << 4) | fp4_encode(imp));
-    row_write(c, r, c.rc, c.rv, n + 1);
+    if (!insert_fits(c, r, c.rc, n, i, col)) return false;
+    load_vals(c, r, n);
+    row_write(c, r, RowMap{2, i, col, (uint8_t)((fp4_encode(w) << 4) | fp4_encode(imp))}, n + 1);
     return true;
 }
 
@@ -444,27 +558,33 @@ __device__ int b4_demote(Ctx& c, int64_t br, int bc) {
             if (!sc_insert_col(c, row, (uint32_t)col, fp4_decode(byte & 0xFu), fp4_decode(byte >> 4))) return kEHEADROOM;
         }
     }
-    b4_erase(c, br, bc);
+    if (c.lane == 0) b4_erase(c, br, bc);
+    __syncwarp();
     return kOK;
 }
 // block4_maybe_promote (delta_csr_memory.hpp:593-702)
 __device__ int b4_maybe_promote(Ctx& c, int64_t row, uint32_t col) {
     const int64_t br = row / 4;
     const int bc = (int)(col / 4), li = (int)(row % 4), lj = (int)(col % 4);
+    const int lane = c.lane;
     int e = b4_find(c, br, bc);
     if (e >= 0) {
         const int n = decode_row(c, row, c.rc);
-        int k = 0;
-        while (k < n && c.rc[k] != col) ++k;
+        const int k = find_col(c, c.rc, n, col, true);
         if (k == n) return kOK;
-        const uint8_t v = c.V.val[c.V.es[row] + k];
-        uint4 t = c.V.b4_tile[c.V.b4_es[br] + e];
-        set_tb(t, lj * 4 + li, fp4_encode(fp4_decode(v >> 4)) | (fp4_encode(fp4_decode(v & 0xFu)) << 4));
-        b4_write(c, br, e, t);
-        b4_maybe_compress(c, br, e);
+        if (lane == 0) {
+            const uint8_t v = c.V.val[c.V.es[row] + k];
+            uint4 t = c.V.b4_tile[c.V.b4_es[br] + e];
+            set_tb(t, lj * 4 + li, fp4_encode(fp4_decode(v >> 4)) | (fp4_encode(fp4_decode(v & 0xFu)) << 4));
+            b4_write(c, br, e, t);
+            b4_maybe_compress(c, br, e);
+        }
+        __syncwarp();
         sc_remove_col(c, row, col);
         return kOK;
     }
+    // the block's scattered entries, rows ascending, each row's entries in
+    // stored order, at most 16 (every lane keeps the list)
     const int64_t row_lo = br * 4, row_hi = min(row_lo + 4, c.R);
     const int64_t col_lo = (int64_t)bc * 4, col_hi = min(col_lo + 4, c.C);
     int fr[16], fcol[16];
@@ -472,143 +592,205 @@ __device__ int b4_maybe_promote(Ctx& c, int64_t row, uint32_t col) {
     int nf = 0;
     for (int64_t r = row_lo; r < row_hi; ++r) {
         const int n = decode_row(c, r, c.rc);
-        for (int k = 0; k < n; ++k)
-            if ((int64_t)c.rc[k] >= col_lo && (int64_t)c.rc[k] < col_hi && nf < 16) {
-                fr[nf] = (int)r; fcol[nf] = (int)c.rc[k]; fv[nf] = c.V.val[c.V.es[r] + k]; ++nf;
+        for (int k0 = 0; k0 < n && nf < 16; k0 += 32) {
+            const int k = k0 + lane;
+            uint32_t ck = 0;
+            uint8_t vk = 0;
+            bool hit = false;
+            if (k < n) {
+                ck = c.rc[k];
+                hit = (int64_t)ck >= col_lo && (int64_t)ck < col_hi;
+                if (hit) vk = c.V.val[c.V.es[r] + k];
             }
+            unsigned m = __ballot_sync(kFull, hit);
+            while (m && nf < 16) {
+                const int src = __ffs(m) - 1;
+                m &= m - 1u;
+                fr[nf] = (int)r;
+                fcol[nf] = (int)__shfl_sync(kFull, ck, src);
+                fv[nf] = (uint8_t)__shfl_sync(kFull, (uint32_t)vk, src);
+                ++nf;
+            }
+        }
     }
     if (nf < 2) return kOK;
-    // Block4Store::get_or_create (block4.hpp:1168-1184)
-    if (!b4_insert_tile(c, br, bc)) {
-        if (*c.V.flags & 4) return kOK;
-        const int rc = b4_ensure_headroom(c, br);
-        if (rc) return rc;
-        b4_insert_tile(c, br, bc);
-        if (*c.V.flags & 4) return kOK;
+    // Block4Store::get_or_create (block4.hpp:1168-1184), by lane 0
+    int rc = kOK;
+    bool stop = false;
+    if (lane == 0) {
+        if (!b4_insert_tile(c, br, bc)) {
+            if (*c.V.flags & 4) {
+                stop = true;
+            } else {
+                rc = b4_ensure_headroom(c, br);
+                if (rc) {
+                    stop = true;
+                } else {
+                    b4_insert_tile(c, br, bc);
+                    if (*c.V.flags & 4) stop = true;
+                }
+            }
+        }
+        if (!stop) e = b4_find(c, br, bc);
+        if (!stop && e >= 0) {
+            uint4 t = c.V.b4_tile[c.V.b4_es[br] + e];
+            for (int f = 0; f < nf; ++f)
+                set_tb(t, (fcol[f] - (int)col_lo) * 4 + (fr[f] - (int)row_lo),
+                       fp4_encode(fp4_decode(fv[f] >> 4)) | (fp4_encode(fp4_decode(fv[f] & 0xFu)) << 4));
+            b4_write(c, br, e, t);
+            b4_maybe_compress(c, br, e);
+        }
     }
-    e = b4_find(c, br, bc);
-    uint4 t = c.V.b4_tile[c.V.b4_es[br] + e];
-    for (int f = 0; f < nf; ++f)
-        set_tb(t, (fcol[f] - (int)col_lo) * 4 + (fr[f] - (int)row_lo),
-               fp4_encode(fp4_decode(fv[f] >> 4)) | (fp4_encode(fp4_decode(fv[f] & 0xFu)) << 4));
-    b4_write(c, br, e, t);
-    b4_maybe_compress(c, br, e);
+    rc = __shfl_sync(kFull, rc, 0);
+    stop = __shfl_sync(kFull, stop ? 1 : 0, 0) != 0;
+    __syncwarp();
+    if (stop) return rc;
     for (int f = 0; f < nf; ++f) sc_remove_col(c, fr[f], (uint32_t)fcol[f]);
     return kOK;
 }
 
-// out_degree decrement with the reference's clamp (if > 0)
+// out_degree decrement with the reference's clamp (if > 0), by lane 0
 __device__ void od_dec(Ctx& c, uint32_t col) {
-    atomicAdd(c.V.od_decs + col, 1);
-    int cur = c.V.out_degree[col];
-    while (cur > 0) {
-        const int prev = atomicCAS(c.V.out_degree + col, cur, cur - 1);
-        if (prev == cur) break;
-        cur = prev;
+    if (c.lane == 0) {
+        atomicAdd(c.V.od_decs + col, 1);
+        int cur = c.V.out_degree[col];
+        while (cur > 0) {
+            const int prev = atomicCAS(c.V.out_degree + col, cur, cur - 1);
+            if (prev == cur) break;
+            cur = prev;
+        }
     }
+    __syncwarp();
 }
 
-// delta_csr_synap_row_step for one row (oracle: o_synap_row_step)
+// delta_csr_synap_row_step for one row (oracle: o_synap_row_step), all lanes
 __device__ int synap_row(Ctx& c, int64_t r, const SynParams& P, uint32_t* ecol, float* eimp, uint8_t* eb4, int* by,
                          uint32_t* pcs, float* pss, int* pidx, uint32_t* rmc, uint8_t* rmb, int* rperm, uint32_t* addc,
                          float* adds, bool* did) {
     *did = false;
+    const int lane = c.lane;
     const int n_sc = row_nnz(c, r);
     const bool has_probes = c.V.n_probes > 0;
     const int64_t br = r / 4;
     const int li = (int)(r % 4);
     const int nt = c.V.nt[br];
+    // the existing synapses: the scattered row, then the row's tile slots in
+    // tile order
     decode_row(c, r, ecol);
-    for (int k = 0; k < n_sc; ++k) { eimp[k] = fp4_decode(c.V.val[c.V.es[r] + k] & 0xFu); eb4[k] = 0; }
+    for (int k = lane; k < n_sc; k += 32) { eimp[k] = fp4_decode(c.V.val[c.V.es[r] + k] & 0xFu); eb4[k] = 0; }
     int n_exist = n_sc;
     const int64_t base = c.V.b4_es[br];
-    for (int e = 0; e < nt; ++e) {
-        const uint4 t = c.V.b4_tile[base + e];
-        const int64_t c0 = (int64_t)c.V.b4_bc[base + e] * 4;
-        for (int lj = 0; lj < 4; ++lj) {
+    for (int e0 = 0; e0 < nt; e0 += 32) {
+        const int e = e0 + lane;
+        uint4 t = make_uint4(0u, 0u, 0u, 0u);
+        int64_t c0 = 0;
+        int cnt = 0;
+        if (e < nt) {
+            t = c.V.b4_tile[base + e];
+            c0 = (int64_t)c.V.b4_bc[base + e] * 4;
+            for (int lj = 0; lj < 4; ++lj) cnt += (tb(t, lj * 4 + li) != 0 && c0 + lj < c.C) ? 1 : 0;
+        }
+        int incl = cnt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(kFull, incl, o);
+            if (lane >= o) incl += v;
+        }
+        int q = n_exist + incl - cnt;
+        for (int lj = 0; lj < 4 && e < nt; ++lj) {
             const uint32_t byte = tb(t, lj * 4 + li);
             if (byte == 0 || c0 + lj >= c.C) continue;
-            ecol[n_exist] = (uint32_t)(c0 + lj);
-            eimp[n_exist] = fp4_decode(byte >> 4);
-            eb4[n_exist] = 1;
-            ++n_exist;
+            ecol[q] = (uint32_t)(c0 + lj);
+            eimp[q] = fp4_decode(byte >> 4);
+            eb4[q] = 1;
+            ++q;
         }
+        n_exist += __shfl_sync(kFull, incl, 31);
     }
+    __syncwarp();
     if (n_exist == 0 && !has_probes) return kOK;
     // probes of this row, COO order
-    int np = 0;
-    for (int q = c.V.pr_ptr[r]; q < c.V.pr_ptr[r + 1]; ++q) {
-        const int p = c.V.pr_idx[q];
-        pcs[np] = (uint32_t)c.V.pcol[p];
-        pss[np] = c.V.pval[p];
-        ++np;
+    const int q0 = c.V.pr_ptr[r];
+    const int np = c.V.pr_ptr[r + 1] - q0;
+    for (int q = lane; q < np; q += 32) {
+        const int p = c.V.pr_idx[q0 + q];
+        pcs[q] = (uint32_t)c.V.pcol[p];
+        pss[q] = c.V.pval[p];
     }
-    // removals by stored importance ascending (:1147-1167).  Without a NaN
-    // key the removals are a prefix of the sorted order (the clamped
+    for (int i = lane; i < n_exist; i += 32) by[i] = i;
+    for (int i = lane; i < np; i += 32) pidx[i] = i;
+    bool key_nan = false, score_nan = false;
+    for (int i = lane; i < n_exist; i += 32) key_nan = key_nan || isnan(eimp[i]);
+    for (int i = lane; i < np; i += 32) score_nan = score_nan || isnan(pss[i]);
+    key_nan = __any_sync(kFull, key_nan);
+    score_nan = __any_sync(kFull, score_nan);
+    __syncwarp();
+    // removals by stored importance ascending (:1147-1167), lane 0.  Without
+    // a NaN key the removals are a prefix of the sorted order (the clamped
     // importance only grows along it and keep only shrinks, so the first
     // position not taken ends the scan), and only that prefix is sorted.
-    for (int i = 0; i < n_exist; ++i) by[i] = i;
-    const SortKeys K0{eimp, nullptr, 0};
-    bool key_nan = false;
-    for (int i = 0; i < n_exist; ++i) key_nan = key_nan || isnan(eimp[i]);
-    LazySort ls;   // one frame stack for the three sorts (extend(n) is std::sort)
+    LazySort ls;   // lane 0's; one frame stack for the three sorts (extend(n) is std::sort)
     int nrm = 0;
-    if (key_nan) {
+    if (lane == 0) {
+        const SortKeys K0{eimp, nullptr, 0};
         ls.init(by, n_exist);
-        ls.extend(n_exist, K0);
+        if (key_nan) ls.extend(n_exist, K0);
         for (int a = 0; a < n_exist && nrm < P.max_prune; ++a) {
+            if (!key_nan) ls.extend(a + 1, K0);
             const int k = by[a];
             const int keep = n_exist - nrm;
             const float fl = (eimp[k] < P.eps) ? P.eps : eimp[k];
-            if (fl < P.cutoff || keep > P.max_rw) { rmc[nrm] = ecol[k]; rmb[nrm] = eb4[k]; ++nrm; }
+            if (fl < P.cutoff || keep > P.max_rw) {
+                rmc[nrm] = ecol[k]; rmb[nrm] = eb4[k]; ++nrm;
+            } else if (!key_nan) {
+                break;
+            }
         }
-    } else {
-        ls.init(by, n_exist);
-        for (int a = 0; a < n_exist && nrm < P.max_prune; ++a) {
-            ls.extend(a + 1, K0);
-            const int k = by[a];
-            const int keep = n_exist - nrm;
-            const float fl = (eimp[k] < P.eps) ? P.eps : eimp[k];
-            if (!(fl < P.cutoff || keep > P.max_rw)) break;
-            rmc[nrm] = ecol[k]; rmb[nrm] = eb4[k]; ++nrm;
-        }
+        for (int i = 0; i < nrm; ++i) rperm[i] = i;
+        ls.init(rperm, nrm);
+        ls.extend(nrm, SortKeys{nullptr, rmc, 2});
+        // adds by score descending (:1171-1201), produced as far as the scan reads it
+        ls.init(pidx, np);
+        if (score_nan) ls.extend(np, SortKeys{pss, nullptr, 1});
     }
-    for (int i = 0; i < nrm; ++i) rperm[i] = i;
-    ls.init(rperm, nrm);
-    ls.extend(nrm, SortKeys{nullptr, rmc, 2});
-    // adds by score descending (:1171-1201), the sorted order produced as far
-    // as the scan reads it
-    for (int i = 0; i < np; ++i) pidx[i] = i;
-    const SortKeys K1{pss, nullptr, 1};
-    bool score_nan = false;
-    for (int i = 0; i < np; ++i) score_nan = score_nan || isnan(pss[i]);
-    ls.init(pidx, np);
-    if (score_nan) ls.extend(np, K1);
+    nrm = __shfl_sync(kFull, nrm, 0);
+    __syncwarp();
     const unsigned long long slots = (unsigned long long)((long long)P.max_rw - (long long)(n_exist - nrm));
     int nadd = 0;
     for (int a = 0; a < np; ++a) {
         if ((unsigned long long)nadd >= slots) break;
-        if (!score_nan) ls.extend(a + 1, K1);
-        const uint32_t col = pcs[pidx[a]];
-        bool exists = false;
-        for (int i = 0; i < n_exist; ++i) if (ecol[i] == col) { exists = true; break; }
-        if (!exists) { addc[nadd] = col; adds[nadd] = pss[pidx[a]]; ++nadd; }
+        int cand = 0;
+        if (lane == 0) {
+            if (!score_nan) ls.extend(a + 1, SortKeys{pss, nullptr, 1});
+            cand = pidx[a];
+        }
+        cand = __shfl_sync(kFull, cand, 0);
+        const uint32_t col = pcs[cand];
+        if (find_col(c, ecol, n_exist, col, true) == n_exist) {
+            if (lane == 0) { addc[nadd] = col; adds[nadd] = pss[cand]; }
+            ++nadd;
+        }
     }
+    __syncwarp();
     // removals, highest column first (:1203-1233)
     for (int q = 0; q < nrm; ++q) {
         const uint32_t col = rmc[rperm[q]];
         if (rmb[rperm[q]]) {
             const int bc = (int)(col / 4), lj = (int)(col % 4);
-            const int e = b4_find(c, br, bc);
             bool demote = false;
-            if (e >= 0) {
-                uint4 t = c.V.b4_tile[base + e];
-                if (tb(t, lj * 4 + li) != 0) {
-                    set_tb(t, lj * 4 + li, 0u);
-                    demote = live_of(t) < 2;
-                    b4_write(c, br, e, t);
+            if (lane == 0) {
+                const int e = b4_find(c, br, bc);
+                if (e >= 0) {
+                    uint4 t = c.V.b4_tile[base + e];
+                    if (tb(t, lj * 4 + li) != 0) {
+                        set_tb(t, lj * 4 + li, 0u);
+                        demote = live_of(t) < 2;
+                        b4_write(c, br, e, t);
+                    }
                 }
             }
+            demote = __shfl_sync(kFull, demote ? 1 : 0, 0) != 0;
+            __syncwarp();
             if (demote) {
                 const int rc = b4_demote(c, br, bc);
                 if (rc) return rc;
@@ -621,7 +803,8 @@ __device__ int synap_row(Ctx& c, int64_t r, const SynParams& P, uint32_t* ecol, 
     // inserts in score order, each followed by the block4 promotion (:1235-1255)
     for (int a = 0; a < nadd; ++a) {
         if (!sc_insert_col(c, r, addc[a], 0.0f, adds[a])) return kEHEADROOM;
-        atomicAdd(c.V.out_degree + addc[a], 1);
+        if (lane == 0) atomicAdd(c.V.out_degree + addc[a], 1);
+        __syncwarp();
         const int rc = b4_maybe_promote(c, r, addc[a]);
         if (rc) return rc;
         if (*c.V.flags & 4) return kOK;
@@ -632,16 +815,12 @@ __device__ int synap_row(Ctx& c, int64_t r, const SynParams& P, uint32_t* ecol, 
 
 }  // namespace
 
-// One thread per block-row (or one thread for the whole sweep when
-// sequential).  Sweep position i covers row (row0 + i) % R; rows at
-// positions > limit are left alone.  The block-row's thread is lane 0 of its
-// own warp: the row steps branch on the data (sorts, searches, row
-// rewrites), and lanes of one warp on different block-rows would run those
-// branches one after another; one working lane per warp lets the scheduler
-// interleave the block-rows instead.
+// One warp per block-row (or one warp for the whole sweep when sequential).
+// Sweep position i covers row (row0 + i) % R; rows at positions > limit are
+// left alone.
 __global__ void k_synap(SynView V, SynParams P, int sequential) {
     const int64_t R = V.n_in, BR = (R + 3) / 4;
-    if ((threadIdx.x & 31) != 0) return;
+    const int lane = threadIdx.x & 31;
     const int64_t tid = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (sequential ? tid != 0 : tid >= BR) return;
     Ctx c;
@@ -649,9 +828,10 @@ __global__ void k_synap(SynView V, SynParams P, int sequential) {
     c.R = R; c.C = V.n_out; c.BR = BR;
     c.seq = sequential != 0;
     c.tot_idx = V.tot_idx0; c.tot_tile = V.tot_tile0;
+    c.lane = lane;
     const int64_t M = V.scratch_m, PM = V.scratch_p;
     uint8_t* sb = V.scratch + (size_t)(sequential ? 0 : tid) * (size_t)V.scratch_stride;
-    // carve the thread's scratch: row ops, exist lists, probe lists
+    // carve the block-row's scratch: row ops, exist lists, probe lists
     auto take = [&](size_t bytes) { uint8_t* p = sb; sb += (bytes + 15) & ~(size_t)15; return p; };
     c.rc = (uint32_t*)take((size_t)M * 4);
     c.rv = take((size_t)M);
@@ -674,9 +854,10 @@ __global__ void k_synap(SynView V, SynParams P, int sequential) {
             const int64_t r = (row0 + i) % R;
             bool did = false;
             const int rc = synap_row(c, r, P, ecol, eimp, eb4, by, pcs, pss, pidx, rmc, rmb, rperm, addc, adds, &did);
-            if (V.did) V.did[i] = did ? 1 : 0;
+            if (lane == 0 && V.did) V.did[i] = did ? 1 : 0;
+            __syncwarp();
             if (rc || (*V.flags & 4)) {
-                if (rc) { atomicMin(V.err_i, (long long)i); atomicMax(V.err_code, rc); }
+                if (rc && lane == 0) { atomicMin(V.err_i, (long long)i); atomicMax(V.err_code, rc); }
                 return;
             }
         }
@@ -699,8 +880,12 @@ __global__ void k_synap(SynView V, SynParams P, int sequential) {
         bool did = false;
         const int rc = synap_row(c, br * 4 + best, P, ecol, eimp, eb4, by, pcs, pss, pidx, rmc, rmb, rperm, addc,
                                  adds, &did);
-        if (V.did) V.did[i] = did ? 1 : 0;
-        if (rc) { atomicMin(V.err_i, (long long)i); atomicMax(V.err_code, rc); return; }
+        if (lane == 0 && V.did) V.did[i] = did ? 1 : 0;
+        __syncwarp();
+        if (rc) {
+            if (lane == 0) { atomicMin(V.err_i, (long long)i); atomicMax(V.err_code, rc); }
+            return;
+        }
         if (*V.flags & 4) return;
     }
 }
