@@ -248,6 +248,26 @@ int sili_layer_b4_equalize_row(sili_layer* h, int64_t row);
  * device-side wait that gives up is reported as SILI_ETIMEOUT by the next
  * synchronising call (sili_layer_sync, or a forward with host arrays). */
 int sili_layer_set_b4_tensor_cores(sili_layer* h, int enable);
+
+/* The layer's scale policy, the ScalePolicy template argument of the
+ * reference's classes (cpu_backend.cpp:993-1013):
+ *   SILI_SCALE_POLICY_RMSPROP  SparseLinearLayer{,Deterministic} (default)
+ *   SILI_SCALE_POLICY_NONE     SparseLinearLayerNoScale{,Deterministic}:
+ *                              NoScalePolicy (delta_csr_types.hpp:528-537),
+ *                              whose update does nothing -- the dense
+ *                              backward's value_scale step
+ *                              (linear_disldo.hpp:901-925) and output_scale
+ *                              step (:2051-2080) are skipped, their step
+ *                              counters and importance states untouched; the
+ *                              block4 value_scale step, the dead-row
+ *                              bootstrap and the sparse-gradient backward's
+ *                              steps, written inline in the reference rather
+ *                              than through the policy, still run.
+ * The stochastic / deterministic rounding choice stays with
+ * sili_layer_create. */
+#define SILI_SCALE_POLICY_RMSPROP 0
+#define SILI_SCALE_POLICY_NONE 1
+int sili_layer_set_scale_policy(sili_layer* h, int policy);
 /* Block4View.switch_point setter (cpu_backend.cpp:61-62) */
 int sili_layer_b4_set_switch_point(sili_layer* h, uint32_t v);
 /* Block4View counters, cpu_backend.cpp:51-98: tiles, synapses, switch_point,

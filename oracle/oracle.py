@@ -61,6 +61,7 @@ def lib():
             ("o_load_weights", _I, [_P, _P, _P, _P, _I]),
             ("o_set_value_bytes", None, [_P, _P, _I64]),
             ("o_set_stochastic", None, [_P, _I, C.c_uint64]),
+            ("o_set_scale_policy", None, [_P, _I]),
             ("o_set_scale_rank", _I, [_P, _I]),
             ("o_get_scale_rank", _I, [_P]),
             ("o_set_value_scale_raw_k", None, [_P, _I, _I, _F]),
@@ -329,13 +330,15 @@ class OracleLayer(_LayerBase):
     ``stochastic=False`` mirrors SparseLinearLayerDeterministic
     (cpu_backend.cpp:1007); ``stochastic=True`` uses this build's
     counter-based draw (o_rng_draw) in place of the reference's xorshift64*.
+    ``scale_policy=1`` mirrors the NoScale siblings (cpu_backend.cpp:998, 1013).
     """
 
-    def __init__(self, n_inputs, n_outputs, max_weights, num_cpus=1, stochastic=False, seed=0):
+    def __init__(self, n_inputs, n_outputs, max_weights, num_cpus=1, stochastic=False, seed=0, scale_policy=0):
         self.L = lib()
         self.h = self.L.o_create(n_inputs, n_outputs, max_weights)
         self.n_inputs, self.n_outputs, self.num_cpus = n_inputs, n_outputs, num_cpus
         self.L.o_set_stochastic(self.h, int(stochastic), seed)
+        self.L.o_set_scale_policy(self.h, int(scale_policy))
         self._last = None
         self._synap_row = 0
         self._eq_row = 0
@@ -600,7 +603,7 @@ def ref_lib(variant: str = "native"):
             ("ref_get_output_scale_step_k", C.c_uint32, [_P, _I, _I]),
             ("ref_seed_rng", None, [C.c_uint64]),
             ("ref_forward_dense", None, [_P, _P, _I, _P]),
-            ("ref_backward_dense", None, [_P, _P, _P, _I, _F, _I, _I, _F, _F, _I, _P]),
+            ("ref_backward_dense", None, [_P, _P, _P, _I, _F, _I, _I, _F, _F, _I, _I, _P]),
             ("ref_forward_sparse", None, [_P, _P, _P, _P, _I, _P]),
             ("ref_backward_sparse", None, [_P, _P, _P, _P, _P, _I, _F, _I, _I, _F, _F, _P]),
             ("ref_build_probes", None, [_P, _I, _I]),
@@ -639,11 +642,12 @@ def ref_lib(variant: str = "native"):
 class RefLayer(_LayerBase):
     """The reference's own code (num_cpus = 1) behind the same method names."""
 
-    def __init__(self, n_inputs, n_outputs, max_weights, stochastic=False, variant="native"):
+    def __init__(self, n_inputs, n_outputs, max_weights, stochastic=False, variant="native", scale_policy=0):
         self.L = ref_lib(variant)
         self.h = self.L.ref_create(n_inputs, n_outputs, max_weights)
         self.n_inputs, self.n_outputs = n_inputs, n_outputs
         self.stochastic = stochastic
+        self.scale_policy = scale_policy
         self._last = None
         self._synap_row = 0
 
@@ -697,7 +701,8 @@ class RefLayer(_LayerBase):
         dy = np.ascontiguousarray(dy, np.float32).reshape(x.shape[0], self.n_outputs)
         dx = np.zeros_like(x)
         self.L.ref_backward_dense(self.h, _ptr(x), _ptr(dy), x.shape[0], learning_rate, int(lr_per_row_nnz),
-                                  int(damp_by_importance), beta2, eps, int(self.stochastic), _ptr(dx))
+                                  int(damp_by_importance), beta2, eps, int(self.stochastic), int(self.scale_policy),
+                                  _ptr(dx))
         return dx
 
     def forward_sparse(self, ptrs, indices, values, batch):

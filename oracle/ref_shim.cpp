@@ -116,21 +116,25 @@ void ref_forward_dense(void* h, const float* x, int batch, float* y) {
     disldo_forward<S, FP4BiPacked, COL>(x, batch, static_cast<S>(L->w.connections.layout.rows), L->w, y, 1);
 }
 
-// cpu_backend.cpp:496-529 (SparseLinearLayer / SparseLinearLayerDeterministic), num_cpus = 1.
+// cpu_backend.cpp:496-529 (SparseLinearLayer / SparseLinearLayerDeterministic; policy 1:
+// SparseLinearLayerNoScale / SparseLinearLayerNoScaleDeterministic, :998, :1013), num_cpus = 1.
 void ref_backward_dense(void* h, const float* x, const float* dy, int batch, float lr,
-                        int lr_per_row_nnz, int damp, float beta2, float eps, int stochastic, float* dx) {
+                        int lr_per_row_nnz, int damp, float beta2, float eps, int stochastic, int policy, float* dx) {
     auto* L = static_cast<RefLayer*>(h);
     const S n_in = static_cast<S>(L->w.connections.layout.rows);
     std::fill(dx, dx + static_cast<std::size_t>(batch) * n_in, 0.f);
-    if (stochastic) {
-        disldo_backward<S, FP4BiPacked, COL, RMSpropScalePolicy<float>, false, true>(
-            x, batch, n_in, dy, L->w, dx, L->in_acc.data(), L->grad_acc.data(), lr, 1,
-            lr_per_row_nnz != 0, damp != 0, beta2, eps, 0.9f, 0.0f, 2.0f, 100.0f);
+#define REF_BWD(POLICY, STOCH)                                                                   \
+    disldo_backward<S, FP4BiPacked, COL, POLICY, false, STOCH>(                                   \
+        x, batch, n_in, dy, L->w, dx, L->in_acc.data(), L->grad_acc.data(), lr, 1,                \
+        lr_per_row_nnz != 0, damp != 0, beta2, eps, 0.9f, 0.0f, 2.0f, 100.0f)
+    if (policy == 1) {
+        if (stochastic) REF_BWD(NoScalePolicy<float>, true);
+        else REF_BWD(NoScalePolicy<float>, false);
     } else {
-        disldo_backward<S, FP4BiPacked, COL, RMSpropScalePolicy<float>, false, false>(
-            x, batch, n_in, dy, L->w, dx, L->in_acc.data(), L->grad_acc.data(), lr, 1,
-            lr_per_row_nnz != 0, damp != 0, beta2, eps, 0.9f, 0.0f, 2.0f, 100.0f);
+        if (stochastic) REF_BWD(RMSpropScalePolicy<float>, true);
+        else REF_BWD(RMSpropScalePolicy<float>, false);
     }
+#undef REF_BWD
 }
 
 static CSRInput<S, V> make_csr(const int* ptrs, const int* idx, const float* vals, int rows, int cols) {

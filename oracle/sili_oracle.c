@@ -52,6 +52,7 @@ struct OLayer {
     double importance_l1, importance_l2_sq, value_l1, value_l2_sq;
     float importance_max_abs, value_max_abs, max_abs_decay;
     int stochastic; uint64_t seed; uint64_t call;
+    int scale_noop;   /* NoScalePolicy (delta_csr_types.hpp:528-537): ScalePolicy::update does nothing */
     /* block4 store (block4.hpp:1016-1490): per block-row tile lists plus the
      * reference's per-block-row allocations (index bytes, tile bytes, tile
      * slots), which decide headroom growth, eviction and budget errors. */
@@ -380,6 +381,9 @@ void o_set_value_bytes(OLayer* L, const uint8_t* bytes, int64_t n) {
     for (int64_t i = 0; i < n && i < L->val_n; ++i) L->val[i] = bytes[i];
 }
 void o_set_stochastic(OLayer* L, int stochastic, uint64_t seed) { L->stochastic = stochastic; L->seed = seed; L->call = 0; }
+/* 0: RMSpropScalePolicy (SparseLinearLayer{,Deterministic}), 1: NoScalePolicy
+ * (SparseLinearLayerNoScale{,Deterministic}, cpu_backend.cpp:998, 1013) */
+void o_set_scale_policy(OLayer* L, int policy) { L->scale_noop = policy == 1; }
 
 /* ── forward, linear_disldo.hpp:68-126 (scattered part) ─────────────────── */
 void o_forward_dense(OLayer* L, const float* x, int batch, float* y) {
@@ -531,6 +535,7 @@ void o_backward_dense(OLayer* L, const float* x, const float* dy, int batch, flo
                         L->shard_part[2 * i + 1] = sgc[k];
                         continue;
                     }
+                    if (L->scale_noop) continue;   /* ScalePolicy::update, linear_disldo.hpp:914-925 */
                     rmsprop_scale_update(&L->value_scale.d[i], &L->value_scale_importance.d[i],
                                          (float)sgs[k], scale_eff_lr, beta2, eps, (float)sgc[k],
                                          &L->value_scale_step.d[i]);
@@ -599,8 +604,8 @@ void o_backward_dense(OLayer* L, const float* x, const float* dy, int batch, flo
             free(S);
         }
     }
-    /* output_scale update, linear_disldo.hpp:2051-2080 */
-    if (lr != 0.0f && os_train) {
+    /* output_scale update, linear_disldo.hpp:2051-2080 (ScalePolicy::update at :2075) */
+    if (lr != 0.0f && os_train && !L->scale_noop) {
         if (L->output_scale_step.n < n_out * rank) uvec_resize(&L->output_scale_step, n_out * rank, 0u);
         for (int64_t c = 0; c < n_out; ++c) {
             const int deg = L->out_degree[c];
@@ -656,8 +661,10 @@ void o_apply_row_part(OLayer* L, const float* x, int batch, float lr, float beta
         for (int64_t k = 0; k < rank; ++k) {
             const int64_t i = r * rank + k;
             if (gnnz > 0) {
-                rmsprop_scale_update(&L->value_scale.d[i], &L->value_scale_importance.d[i], (float)part[2 * i],
-                                     lr / (float)gnnz, beta2, eps, (float)part[2 * i + 1], &L->value_scale_step.d[i]);
+                if (!L->scale_noop)
+                    rmsprop_scale_update(&L->value_scale.d[i], &L->value_scale_importance.d[i], (float)part[2 * i],
+                                         lr / (float)gnnz, beta2, eps, (float)part[2 * i + 1],
+                                         &L->value_scale_step.d[i]);
                 continue;
             }
             double sum = 0.0;

@@ -42,6 +42,7 @@ void    o_destroy(OLayer* L);
 int     o_load_weights(OLayer* L, const int* ptrs, const int* idx, const float* vals, int nnz);
 void    o_set_value_bytes(OLayer* L, const uint8_t* bytes, int64_t n);
 void    o_set_stochastic(OLayer* L, int stochastic, uint64_t seed);
+void    o_set_scale_policy(OLayer* L, int policy);
 int     o_set_scale_rank(OLayer* L, int rank);
 int     o_get_scale_rank(const OLayer* L);
 void    o_set_value_scale_raw_k(OLayer* L, int row, int k, float v);

@@ -90,6 +90,10 @@ struct UpdateParams {
     // row_part[2*(r*rank+k) + {0,1}] instead of being applied
     const int* row_nnz_g = nullptr;
     double* row_part = nullptr;
+    // NoScalePolicy (delta_csr_types.hpp:528-537): the dense backward's
+    // value_scale and output_scale steps (ScalePolicy::update,
+    // linear_disldo.hpp:914-925, 2075) do nothing
+    bool scale_noop = false;
 };
 
 void launch_transpose(const float* in, float* out, int64_t R, int64_t C, cudaStream_t s);

@@ -704,7 +704,7 @@ __global__ void __launch_bounds__(kUpdWarps * 32, 6) k_backward_update(LayerView
             if (P.row_part) {   // a column shard: its part of the row sums
                 P.row_part[2 * i] = sgs[k];
                 P.row_part[2 * i + 1] = sgc[k];
-            } else {
+            } else if (!P.scale_noop) {
                 rmsprop_scale(L.vs + i, L.vsi + i, (float)sgs[k], scale_eff_lr, (float)sgc[k], L.vstep + i, P);
             }
         }
@@ -754,7 +754,7 @@ __global__ void k_output_scale_update(LayerView L, const int* __restrict__ out_d
 }
 void launch_output_scale_update(const LayerView& L, const int* out_degree, const UpdateParams& P,
                                 cudaStream_t s) {
-    if (L.n_out == 0) return;
+    if (L.n_out == 0 || P.scale_noop) return;
     k_output_scale_update<<<(unsigned)((L.n_out + 255) / 256), 256, 0, s>>>(L, out_degree, P); count_launch();
 }
 
@@ -834,6 +834,7 @@ __global__ void k_apply_row_part(LayerView L, const int* __restrict__ row_nnz_g,
         dead_row_step(L, xT, B, part + 2 * L.n_in * L.rank, r, dead_lr, P);
         return;
     }
+    if (P.scale_noop) return;
     const float se = __fdiv_rn(P.lr, (float)gnnz);
     for (int k = 0; k < L.rank; ++k) {
         const int64_t i = r * L.rank + k;

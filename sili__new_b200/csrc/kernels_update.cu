@@ -306,7 +306,7 @@ __global__ void __launch_bounds__(kU2Warps * 32, u2_min_ctas(RANK)) k_backward_u
             if (P.row_part) {   // a column shard: its part of the row sums
                 P.row_part[2 * i] = sgs[k];
                 P.row_part[2 * i + 1] = sgc[k];
-            } else {
+            } else if (!P.scale_noop) {
                 rmsprop_scale(L.vs + i, L.vsi + i, (float)sgs[k], scale_eff_lr, (float)sgc[k], L.vstep + i, P);
             }
         }

@@ -122,6 +122,7 @@ struct sili_layer {
     DBuf<uint32_t> vstep, ostep;
     int64_t n_vs = 0, n_os = 0;
     bool os_trainable = false;
+    int scale_policy = SILI_SCALE_POLICY_RMSPROP;   // the class's ScalePolicy (cpu_backend.cpp:993-1013)
     DBuf<float> in_acc, grad_acc;
     DBuf<int> out_degree;
     DBuf<int> prow, pcol;
@@ -333,6 +334,7 @@ UpdateParams update_params(sili_layer* h, float lr, unsigned flags, float beta2,
     P.pow_tab = h->pow_tab.p; P.pow_n = h->pow_n;
     P.colg = h->colg.p; P.colc = h->colc.p;
     P.stats = h->d_st.p; P.stat_max = h->d_stmax.p;
+    P.scale_noop = h->scale_policy == SILI_SCALE_POLICY_NONE;
     return P;
 }
 
@@ -1366,6 +1368,14 @@ static int b4_tc_or_exact(sili_layer* h, bool dx, const float* actT, int batch, 
 
 static int b4_forward(sili_layer* h, const float* xT, int batch, float* y, cudaStream_t s) {
     return b4_tc_or_exact(h, false, xT, batch, y, s);
+}
+
+int sili_layer_set_scale_policy(sili_layer* h, int policy) {
+    RC(use(h));
+    if (policy != SILI_SCALE_POLICY_RMSPROP && policy != SILI_SCALE_POLICY_NONE)
+        return fail(SILI_EINVAL, "set_scale_policy: policy must be SILI_SCALE_POLICY_RMSPROP or SILI_SCALE_POLICY_NONE");
+    h->scale_policy = policy;
+    return SILI_OK;
 }
 
 int sili_layer_set_b4_tensor_cores(sili_layer* h, int enable) {

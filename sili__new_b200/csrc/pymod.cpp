@@ -418,9 +418,13 @@ public:
     }
 };
 
-template <bool STOCH>
+// STOCH: stochastic rounding (SparseLinearLayer) or nearest (…Deterministic);
+// POLICY: the scale policy (SILI_SCALE_POLICY_*, …NoScale…)
+template <bool STOCH, int POLICY = SILI_SCALE_POLICY_RMSPROP>
 struct LayerT : Layer {
-    LayerT(int a, int b, int c, int d, int dev) : Layer(a, b, c, d, STOCH, dev) {}
+    LayerT(int a, int b, int c, int d, int dev) : Layer(a, b, c, d, STOCH, dev) {
+        if (POLICY != SILI_SCALE_POLICY_RMSPROP) check(sili_layer_set_scale_policy(h, POLICY));
+    }
 };
 
 template <typename T>
@@ -587,6 +591,8 @@ PYBIND11_MODULE(_cuda, m) {
         .def_property_readonly("alloc_bytes", &Block4View::alloc_bytes);
     bind_layer<LayerT<true>>(m, "SparseLinearLayer");
     bind_layer<LayerT<false>>(m, "SparseLinearLayerDeterministic");
+    bind_layer<LayerT<true, SILI_SCALE_POLICY_NONE>>(m, "SparseLinearLayerNoScale");
+    bind_layer<LayerT<false, SILI_SCALE_POLICY_NONE>>(m, "SparseLinearLayerNoScaleDeterministic");
     m.attr("SCALE_VALUE") = SILI_SCALE_VALUE;
     m.attr("SCALE_OUTPUT") = SILI_SCALE_OUTPUT;
     m.attr("SCALE_IMPORTANCE") = SILI_SCALE_IMPORTANCE;
@@ -632,6 +638,10 @@ PYBIND11_MODULE(_cuda, m) {
         for (auto o : layers) {
             if (py::isinstance<LayerT<true>>(o)) hs.push_back(o.cast<LayerT<true>&>().h);
             else if (py::isinstance<LayerT<false>>(o)) hs.push_back(o.cast<LayerT<false>&>().h);
+            else if (py::isinstance<LayerT<true, SILI_SCALE_POLICY_NONE>>(o))
+                hs.push_back(o.cast<LayerT<true, SILI_SCALE_POLICY_NONE>&>().h);
+            else if (py::isinstance<LayerT<false, SILI_SCALE_POLICY_NONE>>(o))
+                hs.push_back(o.cast<LayerT<false, SILI_SCALE_POLICY_NONE>&>().h);
             else throw py::type_error("folded_forward: layers must be this module's SparseLinearLayer objects");
         }
         if (hs.empty()) throw py::value_error("folded_forward: no layers");
