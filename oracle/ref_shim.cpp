@@ -117,22 +117,26 @@ void ref_forward_dense(void* h, const float* x, int batch, float* y) {
 }
 
 // cpu_backend.cpp:496-529 (SparseLinearLayer / SparseLinearLayerDeterministic; policy 1:
-// SparseLinearLayerNoScale / SparseLinearLayerNoScaleDeterministic, :998, :1013), num_cpus = 1.
+// SparseLinearLayerNoScale / SparseLinearLayerNoScaleDeterministic, :998, :1013; policy 2:
+// SparseLinearLayerResync / SparseLinearLayerResyncDeterministic, :993, :1012), num_cpus = 1.
 void ref_backward_dense(void* h, const float* x, const float* dy, int batch, float lr,
                         int lr_per_row_nnz, int damp, float beta2, float eps, int stochastic, int policy, float* dx) {
     auto* L = static_cast<RefLayer*>(h);
     const S n_in = static_cast<S>(L->w.connections.layout.rows);
     std::fill(dx, dx + static_cast<std::size_t>(batch) * n_in, 0.f);
-#define REF_BWD(POLICY, STOCH)                                                                   \
-    disldo_backward<S, FP4BiPacked, COL, POLICY, false, STOCH>(                                   \
+#define REF_BWD(POLICY, DEFER, STOCH)                                                            \
+    disldo_backward<S, FP4BiPacked, COL, POLICY, DEFER, STOCH>(                                   \
         x, batch, n_in, dy, L->w, dx, L->in_acc.data(), L->grad_acc.data(), lr, 1,                \
         lr_per_row_nnz != 0, damp != 0, beta2, eps, 0.9f, 0.0f, 2.0f, 100.0f)
     if (policy == 1) {
-        if (stochastic) REF_BWD(NoScalePolicy<float>, true);
-        else REF_BWD(NoScalePolicy<float>, false);
+        if (stochastic) REF_BWD(NoScalePolicy<float>, false, true);
+        else REF_BWD(NoScalePolicy<float>, false, false);
+    } else if (policy == 2) {
+        if (stochastic) REF_BWD(RMSpropScalePolicy<float>, true, true);
+        else REF_BWD(RMSpropScalePolicy<float>, true, false);
     } else {
-        if (stochastic) REF_BWD(RMSpropScalePolicy<float>, true);
-        else REF_BWD(RMSpropScalePolicy<float>, false);
+        if (stochastic) REF_BWD(RMSpropScalePolicy<float>, false, true);
+        else REF_BWD(RMSpropScalePolicy<float>, false, false);
     }
 #undef REF_BWD
 }

@@ -53,6 +53,7 @@ struct OLayer {
     float importance_max_abs, value_max_abs, max_abs_decay;
     int stochastic; uint64_t seed; uint64_t call;
     int scale_noop;   /* NoScalePolicy (delta_csr_types.hpp:528-537): ScalePolicy::update does nothing */
+    int resync;       /* DeferredScaleWrite = true (SparseLinearLayerResync{,Deterministic}) */
     /* block4 store (block4.hpp:1016-1490): per block-row tile lists plus the
      * reference's per-block-row allocations (index bytes, tile bytes, tile
      * slots), which decide headroom growth, eviction and budget errors. */
@@ -382,8 +383,10 @@ void o_set_value_bytes(OLayer* L, const uint8_t* bytes, int64_t n) {
 }
 void o_set_stochastic(OLayer* L, int stochastic, uint64_t seed) { L->stochastic = stochastic; L->seed = seed; L->call = 0; }
 /* 0: RMSpropScalePolicy (SparseLinearLayer{,Deterministic}), 1: NoScalePolicy
- * (SparseLinearLayerNoScale{,Deterministic}, cpu_backend.cpp:998, 1013) */
-void o_set_scale_policy(OLayer* L, int policy) { L->scale_noop = policy == 1; }
+ * (SparseLinearLayerNoScale{,Deterministic}, cpu_backend.cpp:998, 1013),
+ * 2: RMSpropScalePolicy with DeferredScaleWrite (SparseLinearLayerResync
+ * {,Deterministic}, :993, :1012) */
+void o_set_scale_policy(OLayer* L, int policy) { L->scale_noop = policy == 1; L->resync = policy == 2; }
 
 /* ── forward, linear_disldo.hpp:68-126 (scattered part) ─────────────────── */
 void o_forward_dense(OLayer* L, const float* x, int batch, float* y) {
@@ -470,6 +473,14 @@ void o_backward_dense(OLayer* L, const float* x, const float* dy, int batch, flo
     presize_scales(L);
     const uint64_t call = L->call++;
     double sa_new = 0, sa_old = 0, sq_new = 0, sq_old = 0; float mx_new = 0.0f;
+    /* DeferredScaleWrite's buffered stores: (value position, cw, ci, row, col) */
+    int64_t n_def = 0;
+    int64_t* def_vb = NULL; float* def_cw = NULL; float* def_ci = NULL; int64_t* def_r = NULL; int64_t* def_c = NULL;
+    if (L->resync && lr != 0.0f && L->total_nnz > 0) {
+        def_vb = (int64_t*)malloc((size_t)L->total_nnz * 8); def_r = (int64_t*)malloc((size_t)L->total_nnz * 8);
+        def_c = (int64_t*)malloc((size_t)L->total_nnz * 8);
+        def_cw = (float*)malloc((size_t)L->total_nnz * 4); def_ci = (float*)malloc((size_t)L->total_nnz * 4);
+    }
     if (L->total_nnz > 0) {
         for (int64_t r = 0; r < n_in; ++r) {
             const int64_t nnz = row_nnz(L, r);
@@ -486,6 +497,41 @@ void o_backward_dense(OLayer* L, const float* x, const float* dy, int batch, flo
                 const float cw_orig = get_w(L, vb), ci_orig = get_imp(L, vb);
                 const float cis = imp_scale * o_get_output_importance_scale(L, (int)col);
                 float ci = ci_orig * cis;
+                if (L->resync) {
+                    /* the DeferredScaleWrite branch, linear_disldo.hpp:686-790: the
+                     * old true-units step (cw += update_cw(g, ci, 1, ...)),
+                     * component-0 scale sums from the stored code, the store
+                     * buffered until the scales are final */
+                    const float vs0 = o_get_value_scale_k(L, (int)r, 0), os0 = o_get_output_scale_k(L, (int)col, 0);
+                    float cw = (cw_orig * vs0) * os0;
+                    for (int b = 0; b < batch; ++b) {
+                        const float iv = x[(int64_t)b * n_in + r];
+                        const float dyv = dy[(int64_t)b * n_out + col];
+                        const float g = dyv * iv;
+                        if (lr != 0.0f) {
+                            const float contrib = iv * cw_orig;
+                            ci = bounded_ci(ci, g, contrib, beta2);
+                            cw = fmaf(eff_lr, bounded_raw(g, ci, 1.0f, eps, damp), cw);
+                            sgs[0] = fma((double)cw_orig * (double)os0, (double)g, sgs[0]);
+                            sgc[0] = fma((double)cw_orig * (double)os0, (double)contrib, sgc[0]);
+                            if (os_train) {
+                                colg[col * rank] = fmaf(cw_orig * vs0, g, colg[col * rank]);
+                                colc[col * rank] = fmaf(cw_orig * vs0, contrib, colc[col * rank]);
+                            }
+                        }
+                        float* d = &dx[(int64_t)b * n_in + r];
+                        *d = fmaf(cw, dyv, *d);
+                    }
+                    if (lr != 0.0f) {
+                        def_vb[n_def] = vb; def_cw[n_def] = cw; def_ci[n_def] = ci;
+                        def_r[n_def] = r; def_c[n_def] = col; ++n_def;
+                        /* stats from the true-units ci, as the reference's stand-in */
+                        sa_new += fabs((double)ci); sa_old += fabs((double)ci_orig);
+                        sq_new += (double)ci * ci; sq_old += (double)ci_orig * ci_orig;
+                        if (fabsf(ci) > mx_new) mx_new = fabsf(ci);
+                    }
+                    continue;
+                }
                 const float S = o_get_scale(L, (int)r, (int)col);
                 float quant = cw_orig, cw = quant * S;
                 for (int b = 0; b < batch; ++b) {
@@ -527,7 +573,13 @@ void o_backward_dense(OLayer* L, const float* x, const float* dy, int batch, flo
                     if (fabsf(ai) > mx_new) mx_new = fabsf(ai);
                 }
             }
-            if (lr != 0.0f) {
+            if (lr != 0.0f && L->resync) {
+                /* component 0 only, through value_scale[r] / value_scale_importance[r]
+                 * (flat index r) and the step counter of (r, 0),
+                 * linear_disldo.hpp:918-923 */
+                rmsprop_scale_update(&L->value_scale.d[r], &L->value_scale_importance.d[r], (float)sgs[0],
+                                     scale_eff_lr, beta2, eps, (float)sgc[0], &L->value_scale_step.d[r * rank]);
+            } else if (lr != 0.0f) {
                 for (int64_t k = 0; k < rank; ++k) {
                     const int64_t i = r * rank + k;
                     if (L->shard_part) {   /* this shard's part of the row sums */
@@ -593,7 +645,7 @@ void o_backward_dense(OLayer* L, const float* x, const float* dy, int batch, flo
                     float* m = &L->value_scale_momentum.d[i];
                     float* v = &L->value_scale_importance.d[i];
                     const float nm = fmaf(0.9f, *m, (1.0f - 0.9f) * g);
-                    const float nv = fmaf(beta2, *v, (1.0f - beta2) * (g * g));
+                    const float nv = fmaf(1.0f - beta2, g * g, beta2 * *v);
                     if (!isfinite(nm) || !isfinite(nv)) continue;
                     const float nvs = L->value_scale.d[i] - dead_lr * nm / (sqrtf(nv) + eps);
                     if (!isfinite(nvs)) continue;
@@ -619,6 +671,21 @@ void o_backward_dense(OLayer* L, const float* x, const float* dy, int batch, flo
             }
         }
     }
+    /* the deferred stores under the final scales, linear_disldo.hpp:2090-2112 */
+    for (int64_t q = 0; q < n_def; ++q) {
+        const int r = (int)def_r[q], c = (int)def_c[q];
+        const float comb = o_get_value_scale_k(L, r, 0) * o_get_output_scale_k(L, c, 0);
+        const float combi = o_get_importance_scale(L, r) * o_get_output_importance_scale(L, c);
+        const float w = def_cw[q] / comb, imp = def_ci[q] / combi;
+        if (L->stochastic) {
+            const uint8_t wq = o_fp4_quantize_stochastic_r(w, o_rng_draw(L->seed, call, (uint64_t)def_vb[q], 0));
+            const uint8_t iq = o_fp4_quantize_stochastic_r(imp, o_rng_draw(L->seed, call, (uint64_t)def_vb[q], 1));
+            L->val[def_vb[q]] = (uint8_t)((wq << 4) | iq);
+        } else {
+            set_wi(L, def_vb[q], w, imp);
+        }
+    }
+    free(def_vb); free(def_cw); free(def_ci); free(def_r); free(def_c);
     free(colg); free(colc);
 }
 
@@ -679,7 +746,7 @@ void o_apply_row_part(OLayer* L, const float* x, int batch, float lr, float beta
             float* m = &L->value_scale_momentum.d[i];
             float* v = &L->value_scale_importance.d[i];
             const float nm = fmaf(0.9f, *m, (1.0f - 0.9f) * g);
-            const float nv = fmaf(beta2, *v, (1.0f - beta2) * (g * g));
+            const float nv = fmaf(1.0f - beta2, g * g, beta2 * *v);
             if (!isfinite(nm) || !isfinite(nv)) continue;
             const float nvs = L->value_scale.d[i] - dead_lr * nm / (sqrtf(nv) + eps);
             if (!isfinite(nvs)) continue;

@@ -760,20 +760,26 @@ void launch_output_scale_update(const LayerView& L, const int* out_degree, const
 
 // Dead-row bootstrap, linear_disldo.hpp:1985-2042: S[b,k] = sum_c os[c,k]*dy[b,c]
 // in double, then an Adam step on value_scale of every row with no synapse.
+// The sum runs over the columns in order, each term a rounded double product
+// then a rounded add (the reference build's evaluation, pinned through the
+// oracle): a thread per (b, k), the loads of the next columns in flight
+// while the chain adds.
 __global__ void k_dead_S(LayerView L, const float* __restrict__ dy, int B, double* __restrict__ S) {
-    const int b = blockIdx.x, k = blockIdx.y;
+    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= (int64_t)B * L.rank) return;
+    const int b = (int)(t / L.rank), k = (int)(t % L.rank);
+    const float* d = dy + (int64_t)b * L.n_out;
     double s = 0.0;
-    for (int64_t c = threadIdx.x; c < L.n_out; c += blockDim.x)
-        s = __fma_rn((double)L.os[c * L.rank + k], (double)dy[(int64_t)b * L.n_out + c], s);
-    __shared__ double red[8];
-    s = warp_sum(s);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        double t = 0.0;
-        for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += red[i];
-        S[(int64_t)b * L.rank + k] = t;
+    int64_t c = 0;
+    for (; c + 4 <= L.n_out; c += 4) {
+        double p[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) p[u] = __dmul_rn((double)L.os[(c + u) * L.rank + k], (double)d[c + u]);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) s = __dadd_rn(s, p[u]);
     }
+    for (; c < L.n_out; ++c) s = __dadd_rn(s, __dmul_rn((double)L.os[c * L.rank + k], (double)d[c]));
+    S[t] = s;
 }
 // the Adam step of one dead row from S (linear_disldo.hpp:2000-2040)
 __device__ void dead_row_step(const LayerView& L, const float* __restrict__ xT, int B, const double* __restrict__ S,
@@ -784,7 +790,7 @@ __device__ void dead_row_step(const LayerView& L, const float* __restrict__ xT, 
         for (int b = 0; b < B; ++b) {
             const float iv = xT[r * B + b];
             if (iv == 0.0f) continue;
-            sum = __fma_rn((double)iv, S[(int64_t)b * L.rank + k], sum);
+            sum = __dadd_rn(sum, __dmul_rn((double)iv, S[(int64_t)b * L.rank + k]));
         }
         if (sum == 0.0) continue;
         const float g = (float)sum;
@@ -792,7 +798,9 @@ __device__ void dead_row_step(const LayerView& L, const float* __restrict__ xT, 
         const int64_t i = r * L.rank + k;
         const float m = L.vsm[i], v = L.vsi[i];
         const float nm = __fmaf_rn(0.9f, m, __fmul_rn(__fsub_rn(1.0f, 0.9f), g));
-        const float nv = __fmaf_rn(P.beta2, v, __fmul_rn(onem, __fmul_rn(g, g)));
+        // new_v = beta2 * v + (1 - beta2) * g * g as the reference build
+        // evaluates it: fma(1 - beta2, g * g, beta2 * v)
+        const float nv = __fmaf_rn(onem, __fmul_rn(g, g), __fmul_rn(P.beta2, v));
         if (!isfinite(nm) || !isfinite(nv)) continue;
         const float nvs = __fsub_rn(L.vs[i], __fdiv_rn(__fmul_rn(dead_lr, nm), __fadd_rn(__fsqrt_rn(nv), P.eps)));
         if (!isfinite(nvs)) continue;
@@ -812,12 +820,12 @@ __global__ void k_dead_rows(LayerView L, const float* __restrict__ xT, int B, co
 void launch_dead_rows(const LayerView& L, const float* xT, const float* dy, int B, double* S,
                       const UpdateParams& P, cudaStream_t s) {
     if (L.n_in == 0 || B == 0) return;
-    k_dead_S<<<dim3((unsigned)B, (unsigned)L.rank), 256, 0, s>>>(L, dy, B, S); count_launch();
+    k_dead_S<<<(unsigned)(((int64_t)B * L.rank + 127) / 128), 128, 0, s>>>(L, dy, B, S); count_launch();
     k_dead_rows<<<(unsigned)((L.n_in + 127) / 128), 128, 0, s>>>(L, xT, B, S, P); count_launch();
 }
 void launch_dead_S(const LayerView& L, const float* dy, int B, double* S, cudaStream_t s) {
     if (B == 0) return;
-    k_dead_S<<<dim3((unsigned)B, (unsigned)L.rank), 256, 0, s>>>(L, dy, B, S); count_launch();
+    k_dead_S<<<(unsigned)(((int64_t)B * L.rank + 127) / 128), 128, 0, s>>>(L, dy, B, S); count_launch();
 }
 
 // Column shards: the row steps every shard takes after the parts are summed,

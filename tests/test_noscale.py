@@ -81,3 +81,28 @@ def test_oracle_noscale_differs_from_rmsprop():
 def test_cabi_exports_scale_policy():
     lib = ctypes.CDLL(os.path.join(ROOT, "sili__new_b200", "libsili_b200.so"))
     assert hasattr(lib, "sili_layer_set_scale_policy")
+
+
+@pytest.mark.parametrize("rank,train_os,dead_rows", [(1, False, ()), (1, True, (3, 17)), (2, True, ())])
+def test_oracle_resync_matches_reference(rank, train_os, dead_rows):
+    """The Resync siblings (SparseLinearLayerResync{,Deterministic},
+    cpu_backend.cpp:993, 1012: DeferredScaleWrite, linear_disldo.hpp:686-790,
+    918-923, 2083-2112) -- the oracle's restatement against the reference."""
+    _ref_or_skip()
+    n_in, n_out, B = 96, 80, 16
+    p, i, w, vs = random_layer(n_in, n_out, 12, seed=rank + 11, empty_rows=dead_rows)
+    rng = np.random.default_rng(rank + 5)
+    os_ = (0.5 + rng.random(n_out)).astype(np.float32) if train_os else None
+    vs2 = (0.01 + 0.01 * rng.random(n_in)).astype(np.float32) if rank > 1 else None
+    os2 = (0.5 + rng.random(n_out)).astype(np.float32) if rank > 1 else None
+    layers = [setup_layer(cls(n_in, n_out, len(i) * 3, scale_policy=2), p, i, w, vs, imp_scale=0.01 / 6, os=os_,
+                          rank=rank, vs2=vs2, os2=os2)
+              for cls in (O.OracleLayer, O.RefLayer)]
+    for step in range(3):
+        x = relu_sparse_x(rng, B, n_in)
+        dy = rng.normal(0, 1, (B, n_out)).astype(np.float32)
+        ys = [L.forward_dense(x) for L in layers]
+        assert np.array_equal(ys[0], ys[1]), f"step {step}: forward differs"
+        dxs = [L.backward_dense(dy, 0.03, True) for L in layers]
+        assert np.array_equal(dxs[0], dxs[1]), f"step {step}: dx differs"
+        _same(snapshot(layers[0]), snapshot(layers[1]), f"step {step}")
