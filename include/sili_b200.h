@@ -263,10 +263,23 @@ int sili_layer_set_b4_tensor_cores(sili_layer* h, int enable);
  *                              bootstrap and the sparse-gradient backward's
  *                              steps, written inline in the reference rather
  *                              than through the policy, still run.
+ *   SILI_SCALE_POLICY_RESYNC   SparseLinearLayerResync{,Deterministic}:
+ *                              RMSpropScalePolicy with DeferredScaleWrite
+ *                              (linear_disldo.hpp:686-790, 918-923,
+ *                              2083-2112): the scattered update runs the old
+ *                              true-units step, its component-0 scale sums
+ *                              come from the stored code, and the new codes
+ *                              are stored after the value_scale and
+ *                              output_scale steps, under the final scales.
+ *                              Here: scale rank 1 (set_scale_rank(k > 1)
+ *                              and this call at rank > 1 give SILI_EINVAL)
+ *                              and batches of at most 128 for a learning
+ *                              rate != 0; not column-sharded.
  * The stochastic / deterministic rounding choice stays with
  * sili_layer_create. */
 #define SILI_SCALE_POLICY_RMSPROP 0
 #define SILI_SCALE_POLICY_NONE 1
+#define SILI_SCALE_POLICY_RESYNC 2
 int sili_layer_set_scale_policy(sili_layer* h, int policy);
 /* Block4View.switch_point setter (cpu_backend.cpp:61-62) */
 int sili_layer_b4_set_switch_point(sili_layer* h, uint32_t v);

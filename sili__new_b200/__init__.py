@@ -2,8 +2,9 @@
 
 A drop-in for the reference's ``sili._cpu`` sparse-layer module
 (sili/cpu_backend.cpp): ``SparseLinearLayer`` / ``SparseLinearLayerDeterministic``
-and the NoScale policy siblings ``SparseLinearLayerNoScale`` /
-``SparseLinearLayerNoScaleDeterministic``, with the same method surface, plus the module functions ``dense_to_csr``,
+and the policy siblings ``SparseLinearLayerNoScale`` /
+``SparseLinearLayerNoScaleDeterministic`` / ``SparseLinearLayerResync`` /
+``SparseLinearLayerResyncDeterministic``, with the same method surface, plus the module functions ``dense_to_csr``,
 ``dense_to_top_k_csr``, ``fp4_quantize_array``, ``seed_fp4_stochastic_rng``,
 ``csr_union`` and the banded / sparse attention functions.
 All compute runs in ``libsili_b200.so`` (CUDA kernels behind the C ABI of
@@ -29,6 +30,8 @@ from ._cuda import (  # noqa: E402,F401
     SparseLinearLayerDeterministic,
     SparseLinearLayerNoScale,
     SparseLinearLayerNoScaleDeterministic,
+    SparseLinearLayerResync,
+    SparseLinearLayerResyncDeterministic,
     dense_to_csr,
     dense_to_top_k_csr,
     fp4_quantize_array,
@@ -44,7 +47,8 @@ from ._cuda import (  # noqa: E402,F401
 from .backend import CudaBackend, install_as_sili_cuda, register  # noqa: E402,F401
 
 __all__ = ["SparseLinearLayer", "SparseLinearLayerDeterministic", "SparseLinearLayerNoScale",
-           "SparseLinearLayerNoScaleDeterministic", "dense_to_csr", "dense_to_top_k_csr",
+           "SparseLinearLayerNoScaleDeterministic", "SparseLinearLayerResync", "SparseLinearLayerResyncDeterministic",
+           "dense_to_csr", "dense_to_top_k_csr",
            "fp4_quantize_array", "seed_fp4_stochastic_rng", "device_count", "kernel_launches", "csr_union",
            "banded_attention", "sparse_banded_attention", "sparse_attention", "banded_attention_backward",
            "CudaBackend", "register", "install_as_sili_cuda", "LIBRARY_PATH"]

@@ -61,14 +61,15 @@ def register(registry_module: str = "sili.backend"):
 
 
 # The names of sili._cpu that this library serves: the FP4 delta-CSR / block4
-# sparse layer classes (the RMSprop and NoScale scale policies, stochastic and
-# deterministic rounding) and the module functions their callers use
-# (sili/cpu_backend.cpp:992-1013, :1506-1738, :3075-3238), and the folded
-# stack's banded / sparse attention (:3384-3468).  Everything else in
-# sili._cpu (the Tensor ops, the FP8 and fp32 layer classes, the Resync
-# policy siblings) is not this library's and stays the reference's own.
+# sparse layer classes (the RMSprop, NoScale and Resync scale policies,
+# stochastic and deterministic rounding) and the module functions their
+# callers use (sili/cpu_backend.cpp:992-1013, :1506-1738, :3075-3238), and the
+# folded stack's banded / sparse attention (:3384-3468).  Everything else in
+# sili._cpu (the Tensor ops, the FP8 and fp32 layer classes) is not this
+# library's and stays the reference's own.
 PATH_NAMES = ("SparseLinearLayer", "SparseLinearLayerDeterministic", "SparseLinearLayerNoScale",
-              "SparseLinearLayerNoScaleDeterministic", "dense_to_csr", "dense_to_top_k_csr",
+              "SparseLinearLayerNoScaleDeterministic", "SparseLinearLayerResync",
+              "SparseLinearLayerResyncDeterministic", "dense_to_csr", "dense_to_top_k_csr",
               "fp4_quantize_array", "seed_fp4_stochastic_rng", "csr_union", "banded_attention",
               "sparse_banded_attention", "sparse_attention", "banded_attention_backward")
 

@@ -43,6 +43,10 @@ struct LayerView {
     // when set, kernels that rewrite weight codes also rewrite their packed
     // words: fcpos[f] = the padded CSC position of synapse f (row-major order)
     int* cpack_upd = nullptr;
+    // the Resync classes' true-units weight for dx at learning rate 0:
+    // (w * vs) * os of component 0, the reference build's association
+    // (linear_disldo.hpp:702), instead of w * S
+    bool true_units = false;
     const int* fcpos = nullptr;
 };
 
@@ -94,6 +98,13 @@ struct UpdateParams {
     // value_scale and output_scale steps (ScalePolicy::update,
     // linear_disldo.hpp:914-925, 2075) do nothing
     bool scale_noop = false;
+    // DeferredScaleWrite (the Resync classes, linear_disldo.hpp:686-790):
+    // the update keeps each synapse's true-units (cw, ci) in def_cw / def_ci
+    // at its value position, stored as codes by launch_resync_store once the
+    // scales are final
+    bool resync = false;
+    float* def_cw = nullptr;
+    float* def_ci = nullptr;
 };
 
 void launch_transpose(const float* in, float* out, int64_t R, int64_t C, cudaStream_t s);
@@ -165,6 +176,9 @@ void launch_backward_update(const LayerView& L, const float* xT, const float* dy
 // the same for B <= 128 (kernels_update.cu); launch_backward_update calls it
 void launch_backward_update_tiled(const LayerView& L, const float* xT, const float* dyT, int B,
                                   const UpdateParams& P, float* dxT, cudaStream_t s);
+// the deferred stores of a Resync update under the final scales
+// (linear_disldo.hpp:2083-2112)
+void launch_resync_store(const LayerView& L, const UpdateParams& P, cudaStream_t s);
 void launch_output_scale_update(const LayerView& L, const int* out_degree, const UpdateParams& P,
                                 cudaStream_t s);
 // column shards: this shard's part of the dead-row sums S[b,k] (over its

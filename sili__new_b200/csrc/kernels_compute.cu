@@ -441,9 +441,13 @@ __global__ void __launch_bounds__(256) k_backward_dx(LayerView L, const float* _
             if (e < nnz) {
                 c = L.abs_cols[f0 + e];
                 const float wq = fp4_decode(L.val[es + e] >> 4);
-                float sc = 0.0f;
-                for (int k = 0; k < L.rank; ++k) sc = __fmaf_rn(vsk[k], L.os[(int64_t)c * L.rank + k], sc);
-                cw = __fmul_rn(wq, sc);
+                if (L.true_units) {
+                    cw = __fmul_rn(__fmul_rn(wq, vsk[0]), L.os[(int64_t)c * L.rank]);
+                } else {
+                    float sc = 0.0f;
+                    for (int k = 0; k < L.rank; ++k) sc = __fmaf_rn(vsk[k], L.os[(int64_t)c * L.rank + k], sc);
+                    cw = __fmul_rn(wq, sc);
+                }
             }
             const int n = min(32, nnz - eb);
             for (int j0 = 0; j0 < n; j0 += 8) {

@@ -62,7 +62,12 @@ struct SynChain {
     float osk[RANK], cg[RANK], cc[RANK];
 };
 
-template <bool STOCH, bool OST, int RANK, int NB>
+// RESYNC: the DeferredScaleWrite update of the Resync classes (scale rank 1):
+// the old true-units step cw += update_cw(g, ci, 1, ...) from
+// cw = (cw_orig * vs) * os, component-0 scale sums from the stored code, the
+// store deferred (def_cw / def_ci) and the importance statistics taken from
+// the true-units ci (linear_disldo.hpp:686-790, 918-923).
+template <bool STOCH, bool OST, int RANK, int NB, bool RESYNC>
 __global__ void __launch_bounds__(kU2Warps * 32, u2_min_ctas(RANK)) k_backward_update_tiled(LayerView L, const float* __restrict__ xT,
                                                                              const float* __restrict__ dyT, int B,
                                                                              UpdateParams P, float* __restrict__ dxT) {
@@ -116,6 +121,7 @@ __global__ void __launch_bounds__(kU2Warps * 32, u2_min_ctas(RANK)) k_backward_u
     int l1d = 0, l2d = 0;
     bool st_nan = false;
     float mx_new = 0.0f;
+    double dsa = 0.0, dsq = 0.0;   // RESYNC: |ci| and ci^2 changes in true units
 
     auto init = [&](SynChain<RANK>& C, int e, bool valid) {
         C.c = 0;
@@ -134,8 +140,18 @@ __global__ void __launch_bounds__(kU2Warps * 32, u2_min_ctas(RANK)) k_backward_u
         C.S = S;
         C.ci = __fmul_rn(fp4_decode(C.byte & 15u), cis);
         C.quant = C.cw_orig;
-        C.cw = __fmul_rn(C.quant, S);
-        C.ok = fast_ok && isfinite(S) && isfinite(C.cw_orig);
+        if (RESYNC) {
+            // true units in the reference build's association; an absent
+            // lane holds +0 so that it never blocks the x == 0 closed form
+            C.S = 1.0f;
+            C.cw = valid ? __fmul_rn(__fmul_rn(C.cw_orig, vsr[0]), C.osk[0]) : 0.0f;
+            // the closed form leaves cw as is only when cw is not -0
+            C.ok = fast_ok && isfinite(S) && isfinite(C.cw_orig) && isfinite(vsr[0]) && isfinite(C.osk[0]) &&
+                   !(C.cw == 0.0f && signbit(C.cw));
+        } else {
+            C.cw = __fmul_rn(C.quant, S);
+            C.ok = fast_ok && isfinite(S) && isfinite(C.cw_orig);
+        }
 #pragma unroll
         for (int k = 0; k < RANK; ++k) { C.cg[k] = 0.0f; C.cc[k] = 0.0f; }
     };
@@ -145,6 +161,21 @@ __global__ void __launch_bounds__(kU2Warps * 32, u2_min_ctas(RANK)) k_backward_u
         const float g = __fmul_rn(dyv, iv);
         const float contrib = __fmul_rn(iv, C.cw_orig);
         C.ci = bounded_ci(C.ci, g, contrib, beta2, onem);
+        if (RESYNC) {
+            float raw = P.damp ? __fdiv_rn(-g, __fadd_rn(__fsqrt_rn(C.ci), P.eps)) : -g;
+            if (raw > 2.0f) raw = 2.0f;
+            if (raw < -2.0f) raw = -2.0f;
+            C.cw = __fmaf_rn(eff_lr, raw, C.cw);
+            const double qo = (double)C.cw_orig * (double)C.osk[0];
+            sgs[0] = __fma_rn(qo, (double)g, sgs[0]);
+            sgc[0] = __fma_rn(qo, (double)contrib, sgc[0]);
+            if (OST) {
+                const float qv = __fmul_rn(C.cw_orig, vsr[0]);
+                C.cg[0] = __fmaf_rn(qv, g, C.cg[0]);
+                C.cc[0] = __fmaf_rn(qv, contrib, C.cc[0]);
+            }
+            return;
+        }
         const float ngS = __fmul_rn(-g, C.S);
         float raw = P.damp ? __fdiv_rn(ngS, __fadd_rn(__fsqrt_rn(C.ci), P.eps)) : ngS;
         if (raw > 2.0f) raw = 2.0f;
@@ -188,6 +219,20 @@ __global__ void __launch_bounds__(kU2Warps * 32, u2_min_ctas(RANK)) k_backward_u
         for (int l = n; l < 32; ++l) dys[l][lane] = 0.0f;
     };
     auto finish = [&](const SynChain<RANK>& C, int e) {
+        if (RESYNC) {
+            // deferred: the true-units state, stored by launch_resync_store
+            P.def_cw[es + e] = C.cw;
+            P.def_ci[es + e] = C.ci;
+            const float ao = fp4_decode(C.byte & 15u);
+            dsa += fabs((double)C.ci) - fabs((double)ao);
+            dsq += (double)C.ci * C.ci - (double)ao * ao;
+            mx_new = fmaxf(mx_new, fabsf(C.ci));
+            if (OST) {
+                atomicAdd(P.colg + (int64_t)C.c * RANK, C.cg[0]);
+                atomicAdd(P.colc + (int64_t)C.c * RANK, C.cc[0]);
+            }
+            return;
+        }
         const float cis = __fmul_rn(imp_scale, L.ois[C.c]);
         const float imp_st = __fdiv_rn(C.ci, cis);
         uint32_t nbyte;
@@ -303,7 +348,12 @@ __global__ void __launch_bounds__(kU2Warps * 32, u2_min_ctas(RANK)) k_backward_u
 #pragma unroll
         for (int k = 0; k < RANK; ++k) {
             const int64_t i = r * RANK + k;
-            if (P.row_part) {   // a column shard: its part of the row sums
+            if (RESYNC) {
+                // component 0 through value_scale[r] / value_scale_importance[r]
+                // and the step counter of (r, 0), linear_disldo.hpp:918-923
+                if (k == 0 && !P.scale_noop)
+                    rmsprop_scale(L.vs + r, L.vsi + r, (float)sgs[0], scale_eff_lr, (float)sgc[0], L.vstep + r * RANK, P);
+            } else if (P.row_part) {   // a column shard: its part of the row sums
                 P.row_part[2 * i] = sgs[k];
                 P.row_part[2 * i + 1] = sgc[k];
             } else if (!P.scale_noop) {
@@ -311,10 +361,20 @@ __global__ void __launch_bounds__(kU2Warps * 32, u2_min_ctas(RANK)) k_backward_u
             }
         }
     }
+    for (int o = 16; o > 0; o >>= 1) mx_new = fmaxf(mx_new, __shfl_xor_sync(0xffffffffu, mx_new, o));
+    if (RESYNC) {
+        dsa = warp_sum(dsa);
+        dsq = warp_sum(dsq);
+        if (lane == 0) {
+            atomicAdd(P.stats + 0, dsa);
+            atomicAdd(P.stats + 1, dsq);
+            atomicMax(reinterpret_cast<unsigned int*>(P.stat_max), __float_as_uint(mx_new));
+        }
+        return;
+    }
     l1d = warp_sum(l1d);
     l2d = warp_sum(l2d);
     const bool any_nan = __any_sync(0xffffffffu, st_nan);
-    for (int o = 16; o > 0; o >>= 1) mx_new = fmaxf(mx_new, __shfl_xor_sync(0xffffffffu, mx_new, o));
     if (lane == 0) {
         const double nan = __longlong_as_double(0x7ff8000000000000LL);
         atomicAdd(P.stats + 0, any_nan ? nan : 0.5 * (double)l1d);
@@ -323,17 +383,21 @@ __global__ void __launch_bounds__(kU2Warps * 32, u2_min_ctas(RANK)) k_backward_u
     }
 }
 
-template <bool STOCH, bool OST, int RANK>
+template <bool STOCH, bool OST, int RANK, bool RESYNC = false>
 static void launch_tiled_nb(const LayerView& L, const float* xT, const float* dyT, int B, const UpdateParams& P,
                             float* dxT, cudaStream_t s) {
     const unsigned g = (unsigned)((L.n_in + kU2Warps - 1) / kU2Warps);
-    if (B <= 64) k_backward_update_tiled<STOCH, OST, RANK, 2><<<g, kU2Warps * 32, 0, s>>>(L, xT, dyT, B, P, dxT);
-    else k_backward_update_tiled<STOCH, OST, RANK, 4><<<g, kU2Warps * 32, 0, s>>>(L, xT, dyT, B, P, dxT);
+    if (B <= 64) k_backward_update_tiled<STOCH, OST, RANK, 2, RESYNC><<<g, kU2Warps * 32, 0, s>>>(L, xT, dyT, B, P, dxT);
+    else k_backward_update_tiled<STOCH, OST, RANK, 4, RESYNC><<<g, kU2Warps * 32, 0, s>>>(L, xT, dyT, B, P, dxT);
 }
 
 template <bool STOCH, bool OST>
 static void launch_tiled_rank(const LayerView& L, const float* xT, const float* dyT, int B, const UpdateParams& P,
                               float* dxT, cudaStream_t s) {
+    if (P.resync) {   // scale rank 1 only (the host enforces it)
+        launch_tiled_nb<STOCH, OST, 1, true>(L, xT, dyT, B, P, dxT, s);
+        return;
+    }
     switch (L.rank) {
     case 1: launch_tiled_nb<STOCH, OST, 1>(L, xT, dyT, B, P, dxT, s); break;
     case 2: launch_tiled_nb<STOCH, OST, 2>(L, xT, dyT, B, P, dxT, s); break;
@@ -352,6 +416,43 @@ void launch_backward_update_tiled(const LayerView& L, const float* xT, const flo
         if (P.os_trainable) launch_tiled_rank<false, true>(L, xT, dyT, B, P, dxT, s);
         else launch_tiled_rank<false, false>(L, xT, dyT, B, P, dxT, s);
     }
+    count_launch();
+}
+
+// The deferred stores of a Resync update (linear_disldo.hpp:2083-2112): every
+// synapse of a row the update visited, under the scales now in effect --
+// w = cw / (vs * os), imp = ci / (is * ois) -- stochastically or to nearest,
+// with the same per-position draws as the immediate store.  A warp per row.
+template <bool STOCH>
+__global__ void k_resync_store(LayerView L, UpdateParams P) {
+    const int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (r >= L.n_in) return;
+    const int64_t es = L.es[r];
+    const int nnz = (int)(L.ee[r] - es);
+    const int f0 = L.rowptr[r];
+    const float vs0 = L.vs[r * L.rank], isr = L.is[r];
+    for (int e = threadIdx.x & 31; e < nnz; e += 32) {
+        const int c = L.abs_cols[f0 + e];
+        const float w = __fdiv_rn(P.def_cw[es + e], __fmul_rn(vs0, L.os[(int64_t)c * L.rank]));
+        const float imp = __fdiv_rn(P.def_ci[es + e], __fmul_rn(isr, L.ois[c]));
+        uint32_t nbyte;
+        if (STOCH) {
+            const uint64_t vp = (uint64_t)(es + e);
+            nbyte = (fp4_quantize_stochastic(w, rng_draw(P.call_key, vp, 0)) << 4) |
+                    fp4_quantize_stochastic(imp, rng_draw(P.call_key, vp, 1));
+        } else {
+            nbyte = (fp4_encode(w) << 4) | fp4_encode(imp);
+        }
+        L.val[es + e] = (uint8_t)nbyte;
+        if (L.cpack_upd) L.cpack_upd[L.fcpos[f0 + e]] = (int)(((uint32_t)r << 4) | (nbyte >> 4));
+    }
+}
+
+void launch_resync_store(const LayerView& L, const UpdateParams& P, cudaStream_t s) {
+    if (L.n_in == 0) return;
+    const unsigned g = (unsigned)((L.n_in + 7) / 8);
+    if (P.stochastic) k_resync_store<true><<<g, 256, 0, s>>>(L, P);
+    else k_resync_store<false><<<g, 256, 0, s>>>(L, P);
     count_launch();
 }
 

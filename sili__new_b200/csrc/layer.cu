@@ -123,6 +123,7 @@ struct sili_layer {
     int64_t n_vs = 0, n_os = 0;
     bool os_trainable = false;
     int scale_policy = SILI_SCALE_POLICY_RMSPROP;   // the class's ScalePolicy (cpu_backend.cpp:993-1013)
+    DBuf<float> def_cw, def_ci;   // a Resync update's deferred true-units state, by value position
     DBuf<float> in_acc, grad_acc;
     DBuf<int> out_degree;
     DBuf<int> prow, pcol;
@@ -234,6 +235,7 @@ struct sili_layer {
         v.vstep = vstep.p; v.ostep = ostep.p; v.is = is.p; v.ois = ois.p;
         v.rowptr = rowptr.p; v.abs_cols = abs_cols.p; v.colptr = colptr.p; v.crow = crow.p; v.cvpos = cvpos.p;
         v.b4_nt = b4_ntiles > 0 ? b4_nt.p : nullptr;
+        v.true_units = scale_policy == SILI_SCALE_POLICY_RESYNC;
         return v;
     }
     B4View b4view() const {
@@ -335,6 +337,7 @@ UpdateParams update_params(sili_layer* h, float lr, unsigned flags, float beta2,
     P.colg = h->colg.p; P.colc = h->colc.p;
     P.stats = h->d_st.p; P.stat_max = h->d_stmax.p;
     P.scale_noop = h->scale_policy == SILI_SCALE_POLICY_NONE;
+    P.resync = h->scale_policy == SILI_SCALE_POLICY_RESYNC;
     return P;
 }
 
@@ -1182,6 +1185,8 @@ int sili_layer_set_scale_rank(sili_layer* h, int rank) {
     if (rank < 1) return fail(SILI_EINVAL, "scale_rank must be >= 1");
     if (rank > 4) return fail(SILI_EINVAL, "scale_rank exceeds SCALE_RANK_MAX (4)");
     if (rank == h->rank) return SILI_OK;
+    if (h->scale_policy == SILI_SCALE_POLICY_RESYNC && rank != 1)
+        return fail(SILI_EINVAL, "set_scale_rank: a Resync layer keeps scale rank 1 on this library");
     const int old = h->rank;
     CK(cudaStreamSynchronize(h->stream));
     RC(relayout_scale(h, h->vs, h->rows, old, rank, h->n_vs, true));
@@ -1372,8 +1377,10 @@ static int b4_forward(sili_layer* h, const float* xT, int batch, float* y, cudaS
 
 int sili_layer_set_scale_policy(sili_layer* h, int policy) {
     RC(use(h));
-    if (policy != SILI_SCALE_POLICY_RMSPROP && policy != SILI_SCALE_POLICY_NONE)
-        return fail(SILI_EINVAL, "set_scale_policy: policy must be SILI_SCALE_POLICY_RMSPROP or SILI_SCALE_POLICY_NONE");
+    if (policy != SILI_SCALE_POLICY_RMSPROP && policy != SILI_SCALE_POLICY_NONE && policy != SILI_SCALE_POLICY_RESYNC)
+        return fail(SILI_EINVAL, "set_scale_policy: unknown policy");
+    if (policy == SILI_SCALE_POLICY_RESYNC && h->rank != 1)
+        return fail(SILI_EINVAL, "set_scale_policy: the Resync policy needs scale rank 1 on this library");
     h->scale_policy = policy;
     return SILI_OK;
 }
@@ -1622,8 +1629,17 @@ static int backward_dense_impl(sili_layer* h, const float* x, const float* dy, i
         P.dy_flag = h->d_dyflag.p;
         P.dy_tag = dy_tag;
         if (part) {
+            if (P.resync) return fail(SILI_EINVAL, "backward_dense_shard: Resync layers are not column-sharded");
             P.row_nnz_g = h->shard_nnz.p;
             P.row_part = part;
+        }
+        if (P.resync) {
+            if (batch > 128)
+                return fail(SILI_EINVAL, "backward_dense: a Resync layer's update takes batches of at most 128 here");
+            RC(h->def_cw.reserve(h->val_n + 1));
+            RC(h->def_ci.reserve(h->val_n + 1));
+            P.def_cw = h->def_cw.p;
+            P.def_ci = h->def_ci.p;
         }
         h->call++;
         if (h->pack_valid) {
@@ -1653,6 +1669,8 @@ static int backward_dense_impl(sili_layer* h, const float* x, const float* dy, i
             launch_dead_rows(v, h->xT.p, dyd, batch, h->dS.p, P, s);
         }
         if (h->os_trainable) launch_output_scale_update(v, h->out_degree.p, P, s);
+        // the Resync classes store their codes only now, under the final scales
+        if (P.resync && h->total_nnz > 0) launch_resync_store(v, P, s);
         launch_transpose(h->dxT.p, dxd, n_in, batch, s);
     }
     CK(cudaGetLastError());

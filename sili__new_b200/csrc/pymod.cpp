@@ -593,6 +593,8 @@ PYBIND11_MODULE(_cuda, m) {
     bind_layer<LayerT<false>>(m, "SparseLinearLayerDeterministic");
     bind_layer<LayerT<true, SILI_SCALE_POLICY_NONE>>(m, "SparseLinearLayerNoScale");
     bind_layer<LayerT<false, SILI_SCALE_POLICY_NONE>>(m, "SparseLinearLayerNoScaleDeterministic");
+    bind_layer<LayerT<true, SILI_SCALE_POLICY_RESYNC>>(m, "SparseLinearLayerResync");
+    bind_layer<LayerT<false, SILI_SCALE_POLICY_RESYNC>>(m, "SparseLinearLayerResyncDeterministic");
     m.attr("SCALE_VALUE") = SILI_SCALE_VALUE;
     m.attr("SCALE_OUTPUT") = SILI_SCALE_OUTPUT;
     m.attr("SCALE_IMPORTANCE") = SILI_SCALE_IMPORTANCE;
@@ -642,6 +644,10 @@ PYBIND11_MODULE(_cuda, m) {
                 hs.push_back(o.cast<LayerT<true, SILI_SCALE_POLICY_NONE>&>().h);
             else if (py::isinstance<LayerT<false, SILI_SCALE_POLICY_NONE>>(o))
                 hs.push_back(o.cast<LayerT<false, SILI_SCALE_POLICY_NONE>&>().h);
+            else if (py::isinstance<LayerT<true, SILI_SCALE_POLICY_RESYNC>>(o))
+                hs.push_back(o.cast<LayerT<true, SILI_SCALE_POLICY_RESYNC>&>().h);
+            else if (py::isinstance<LayerT<false, SILI_SCALE_POLICY_RESYNC>>(o))
+                hs.push_back(o.cast<LayerT<false, SILI_SCALE_POLICY_RESYNC>&>().h);
             else throw py::type_error("folded_forward: layers must be this module's SparseLinearLayer objects");
         }
         if (hs.empty()) throw py::value_error("folded_forward: no layers");

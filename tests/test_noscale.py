@@ -103,6 +103,8 @@ def test_oracle_resync_matches_reference(rank, train_os, dead_rows):
         dy = rng.normal(0, 1, (B, n_out)).astype(np.float32)
         ys = [L.forward_dense(x) for L in layers]
         assert np.array_equal(ys[0], ys[1]), f"step {step}: forward differs"
+        dx0 = [L.backward_dense(dy, 0.0, True) for L in layers]
+        assert np.array_equal(dx0[0], dx0[1]), f"step {step}: dx at learning rate 0 differs"
         dxs = [L.backward_dense(dy, 0.03, True) for L in layers]
         assert np.array_equal(dxs[0], dxs[1]), f"step {step}: dx differs"
         _same(snapshot(layers[0]), snapshot(layers[1]), f"step {step}")
