@@ -44,6 +44,7 @@ __device__ __forceinline__ uint32_t fp4_encode(float v) {
 
 // fp4_quantize_stochastic (fp4quant.hpp:238-273) with the 64-bit draw passed
 // in: top 24 bits give the uniform for |v| < 1, low 22 bits the dither above.
+// The uniform (24-bit integer) * 2^-24 is exact in float.
 __device__ __forceinline__ uint32_t fp4_quantize_stochastic(float v, uint64_t r) {
     const uint32_t bits = f2u(v), sign = bits >> 31, a = bits & 0x7FFFFFFFu;
     uint32_t mag;
@@ -51,11 +52,11 @@ __device__ __forceinline__ uint32_t fp4_quantize_stochastic(float v, uint64_t r)
     if (a >= 0x40C00000u) mag = 7;
     else if (a < 0x3F000000u) {
         const float p = u2f(a) * 2.0f;
-        const float u = (float)((double)(r >> 40) * (1.0 / 16777216.0));
+        const float u = (float)(uint32_t)(r >> 40) * 0x1p-24f;
         mag = (u < p) ? 1u : 0u;
     } else if (a < 0x3F800000u) {
         const float p = __fsub_rn(u2f(a) * 2.0f, 1.0f);
-        const float u = (float)((double)(r >> 40) * (1.0 / 16777216.0));
+        const float u = (float)(uint32_t)(r >> 40) * 0x1p-24f;
         mag = (u < p) ? 2u : 1u;
     } else {
         uint32_t rr = a + (uint32_t)(r & 0x3FFFFFu);

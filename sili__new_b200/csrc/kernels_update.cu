@@ -14,6 +14,8 @@
 //    stored once, instead of a read-modify-write per tile.
 //  * Whether dy holds an inf or NaN is known per call (a flag written by the
 //    |dy| accumulation), not checked per tile.
+//  * FP4 codes decode through a 16-entry shared table, and each run of
+//    x == 0 samples decays the importance in binary-sized unrolled runs.
 //  * The weight history cw (the weight after every sample that can change
 //    it) is kept for at most kU2K such samples of a 32-sample block; a block
 //    with more is processed as sub-blocks, each followed by the dx pass over
@@ -56,6 +58,7 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 template <int RANK>
 struct SynChain {
     float ci, quant, cw, S, cw_orig;
+    float cis;       // importance_scale[row] * output_importance_scale[column]
     uint32_t byte;   // the stored FP4BiPacked byte at entry
     int c;           // absolute column
     bool ok;         // finite S and weight, and the row's parameters allow the x == 0 closed form
@@ -76,6 +79,9 @@ __global__ void __launch_bounds__(kU2Warps * 32, u2_min_ctas(RANK)) k_backward_u
     // which the lanes (samples) of the dx pass read at once, in different banks
     __shared__ __align__(16) float cws_s[kU2Warps][kU2K + 1][kU2Pitch];
     __shared__ float xs_s[kU2Warps][NB * 32];
+    __shared__ float ftab[16];   // fp4_decode of every code
+    if (threadIdx.x < 16) ftab[threadIdx.x] = fp4_decode(threadIdx.x);
+    __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t r = (int64_t)blockIdx.x * kU2Warps + warp;
     if (r >= L.n_in) return;
@@ -130,15 +136,16 @@ __global__ void __launch_bounds__(kU2Warps * 32, u2_min_ctas(RANK)) k_backward_u
             C.c = L.abs_cols[f0 + e];
             C.byte = L.val[es + e];
         }
-        C.cw_orig = fp4_decode(C.byte >> 4);
+        C.cw_orig = ftab[C.byte >> 4];
 #pragma unroll
         for (int k = 0; k < RANK; ++k) C.osk[k] = valid ? L.os[(int64_t)C.c * RANK + k] : 0.0f;
         const float cis = valid ? __fmul_rn(imp_scale, L.ois[C.c]) : 1.0f;
+        C.cis = cis;
         float S = 0.0f;
 #pragma unroll
         for (int k = 0; k < RANK; ++k) S = __fmaf_rn(vsr[k], C.osk[k], S);
         C.S = S;
-        C.ci = __fmul_rn(fp4_decode(C.byte & 15u), cis);
+        C.ci = __fmul_rn(ftab[C.byte & 15u], cis);
         C.quant = C.cw_orig;
         if (RESYNC) {
             // true units in the reference build's association; an absent
@@ -223,7 +230,7 @@ __global__ void __launch_bounds__(kU2Warps * 32, u2_min_ctas(RANK)) k_backward_u
             // deferred: the true-units state, stored by launch_resync_store
             P.def_cw[es + e] = C.cw;
             P.def_ci[es + e] = C.ci;
-            const float ao = fp4_decode(C.byte & 15u);
+            const float ao = ftab[C.byte & 15u];
             dsa += fabs((double)C.ci) - fabs((double)ao);
             dsq += (double)C.ci * C.ci - (double)ao * ao;
             mx_new = fmaxf(mx_new, fabsf(C.ci));
@@ -233,8 +240,7 @@ __global__ void __launch_bounds__(kU2Warps * 32, u2_min_ctas(RANK)) k_backward_u
             }
             return;
         }
-        const float cis = __fmul_rn(imp_scale, L.ois[C.c]);
-        const float imp_st = __fdiv_rn(C.ci, cis);
+        const float imp_st = __fdiv_rn(C.ci, C.cis);
         uint32_t nbyte;
         if (STOCH) {
             const uint64_t vp = (uint64_t)(es + e);
@@ -245,7 +251,7 @@ __global__ void __launch_bounds__(kU2Warps * 32, u2_min_ctas(RANK)) k_backward_u
         }
         L.val[es + e] = (uint8_t)nbyte;
         if (L.cpack_upd) L.cpack_upd[L.fcpos[f0 + e]] = (int)(((uint32_t)r << 4) | (nbyte >> 4));
-        const float an = fabsf(fp4_decode(nbyte & 15u)), ao = fabsf(fp4_decode(C.byte & 15u));
+        const float an = fabsf(ftab[nbyte & 15u]), ao = fabsf(ftab[C.byte & 15u]);
         if (an != an || ao != ao) {
             st_nan = true;
         } else {
@@ -291,11 +297,8 @@ __global__ void __launch_bounds__(kU2Warps * 32, u2_min_ctas(RANK)) k_backward_u
                 int seg = 0, s1 = nb;
                 while (true) {
                     const int ja = rem ? (__ffs(rem) - 1) : nb;
-                    for (; j + 4 <= ja; j += 4) {   // x == 0 run: only the importance decays
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) A.ci = __fmaf_rn(beta2, A.ci, zterm);
-                    }
-                    for (; j < ja; ++j) A.ci = __fmaf_rn(beta2, A.ci, zterm);
+                    A.ci = decay_run(A.ci, ja - j, beta2, zterm);   // x == 0 run: only the importance decays
+                    j = ja;
                     if (ja >= nb) break;
                     rem &= rem - 1u;
                     const float iv = xb[ja];

@@ -191,7 +191,7 @@ struct sili_layer {
     bool b4_tc = false;                    // block4 forward on the tensor cores (tolerance contract)
     DBuf<uint16_t> b4_xs;                  // its split activations
     DBuf<float> b4_part;                   // its per-slice partial sums
-    DBuf<unsigned int> tc_err;             // set by a tensor-core kernel whose bounded wait gave up
+    DBuf<unsigned int> tc_err;             // set by a kernel whose bounded device-side wait gave up
     DBuf<int> b4_pmap;                     // its panel map (tile slot per 32 x 16 block cell)
     bool b4_pmap_dirty = true;             // the tile layout changed since the map was built
     DBuf<int> b4_pmapT;                    // the lr = 0 dx's panel map (block-rows along the panel)
@@ -1329,14 +1329,15 @@ int sili_layer_rescale_row(sili_layer* h, int kind, int row, float new_scale) {
 }
 
 // ── compute ─────────────────────────────────────────────────────────────────
-// A tensor-core kernel's bounded wait that gave up (the word it sets),
-// reported once as SILI_ETIMEOUT at the next synchronising call.
+// A kernel's bounded device-side wait that gave up (the word the block4
+// tensor-core forward / dx set), reported once as SILI_ETIMEOUT at the next
+// synchronising call.
 static int check_tc_err(sili_layer* h) {
     unsigned int e = 0;
     CK(cudaMemcpy(&e, h->tc_err.p, sizeof(e), cudaMemcpyDeviceToHost));
     if (e) {
         CK(cudaMemset(h->tc_err.p, 0, sizeof(e)));
-        return fail(SILI_ETIMEOUT, "block4 tensor-core forward: a bounded device-side wait gave up");
+        return fail(SILI_ETIMEOUT, "block4 tensor cores: a bounded device-side wait gave up");
     }
     return SILI_OK;
 }
@@ -1675,7 +1676,10 @@ static int backward_dense_impl(sili_layer* h, const float* x, const float* dy, i
     }
     CK(cudaGetLastError());
     if (!dev_out) CK(cudaMemcpyAsync(dx, dxd, (size_t)batch * n_in * 4, cudaMemcpyDeviceToHost, s));
-    if (!dev_out || !is_device_ptr(dy) || (x && !is_device_ptr(x))) CK(cudaStreamSynchronize(s));
+    if (!dev_out || !is_device_ptr(dy) || (x && !is_device_ptr(x))) {
+        CK(cudaStreamSynchronize(s));
+        RC(check_tc_err(h));
+    }
     return SILI_OK;
 }
 

@@ -41,4 +41,33 @@ __device__ __forceinline__ float bounded_ci(float ci, float g, float contrib, fl
     return (100.0f < r) ? 100.0f : r;
 }
 
+// n steps of the x == 0 closed form of the importance update (ci = fma(beta2,
+// ci, zterm), n < 64), as n sequential fmas in binary-sized runs: the runs
+// between a row's non-zero inputs are short and vary, and warp-uniform tests
+// of n's bits cost less than a counted loop
+__device__ __forceinline__ float decay_run(float ci, int n, float beta2, float zterm) {
+    if (n & 32) {
+#pragma unroll
+        for (int u = 0; u < 32; ++u) ci = __fmaf_rn(beta2, ci, zterm);
+    }
+    if (n & 16) {
+#pragma unroll
+        for (int u = 0; u < 16; ++u) ci = __fmaf_rn(beta2, ci, zterm);
+    }
+    if (n & 8) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) ci = __fmaf_rn(beta2, ci, zterm);
+    }
+    if (n & 4) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) ci = __fmaf_rn(beta2, ci, zterm);
+    }
+    if (n & 2) {
+        ci = __fmaf_rn(beta2, ci, zterm);
+        ci = __fmaf_rn(beta2, ci, zterm);
+    }
+    if (n & 1) ci = __fmaf_rn(beta2, ci, zterm);
+    return ci;
+}
+
 }  // namespace sili
