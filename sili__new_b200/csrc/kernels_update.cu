@@ -31,10 +31,12 @@
 
 namespace sili {
 
-// 2-warp CTAs with 12 KB of shared memory each; 14 resident per SM (28
+// 2-warp CTAs with 13.5 KB of shared memory each; 14 resident per SM (28
 // warps, 72 registers) at scale rank 1-2, 10 at rank 3-4 (their per-synapse
-// state needs more registers)
-constexpr int kU2Warps = 2, kU2K = 8, kU2Pitch = 36;
+// state needs more registers).  12 weight-history segments: a 32-sample
+// block of 20 %-dense inputs almost never needs a second dx pass (8
+// segments: 0.356 -> 0.344 ms at config 2)
+constexpr int kU2Warps = 2, kU2K = 12, kU2Pitch = 36;
 constexpr int u2_min_ctas(int rank) { return rank <= 2 ? 14 : 10; }
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
