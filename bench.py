@@ -660,8 +660,13 @@ def run_folded(args, dev, rank, world, dist, S, torch, which="config5"):
               ["gate_proj", "up_proj"], ["down_proj"]]
     groups = [g for g in groups if g and all(n in suffixes for n in g)]
 
+    # each group's all-gather on its own stream, overlapped with the next
+    # group's forwards; a group's suffixes run concurrently on side streams
+    comm = torch.cuda.Stream(device=dev) if world > 1 else None
+    sides = [torch.cuda.Stream(device=dev) for _ in range(3)]
+
     def decode_step():
-        return [stack.forward_group(g, xs, stream) for g in groups]
+        return stack.forward_groups(groups, xs, stream, comm, sides)
 
     prefill = fc["kind"] == "prefill"   # a step of 4096 tokens: fewer, longer steps
     for _ in range(3 if prefill else max(args.warmup, 3)):
@@ -699,7 +704,8 @@ def run_folded(args, dev, rank, world, dist, S, torch, which="config5"):
             "ms_per_step": ms, "steps": steps, "nnz": total_nnz,
             "gflop_per_step": flops / 1e9, "fp32_tflops": flops / (ms * 1e-3) / 1e12,
             "sharding": f"output columns within each fold over {world} rank(s), "
-                        f"{len(groups)} NCCL all-gathers per step (suffix groups)",
+                        f"{len(groups)} NCCL all-gathers per step (suffix groups, each overlapped "
+                        f"with the next group's forwards; a group's suffixes on concurrent streams)",
             "collectives_per_step": len(groups) if world > 1 else 0,
             "build_s_rank0": build_s, "torch_mem_gb_rank0": mem_gb, "gpu_launches_rank0": launches,
             "data": f"synthetic: random N(0,0.02) pruned to {density * 100:g}% (uniform pattern), x ~ N(0,1)",

@@ -239,7 +239,8 @@ class FoldedStack:
         import torch.distributed as dist
         with torch.cuda.stream(stream):
             dist.all_gather_into_tensor(p.gathered, p.part, group=self.group)
-        return p.gathered.permute(1, 0, 2).reshape(b, self.world * s)[:, : p.out_dim]
+            # the column interleave copies on `stream`, after the gather
+            return p.gathered.permute(1, 0, 2).reshape(b, self.world * s)[:, : p.out_dim]
 
     def _forward_part(self, name: str, x, part, stream):
         """This rank's slice of the fold-summed output of one suffix into
@@ -269,11 +270,50 @@ class FoldedStack:
             with torch.cuda.stream(stream):
                 part[:, :w].copy_(p.raw)
 
-    def forward_group(self, names, xs: dict, stream) -> dict:
+    def forward_groups(self, groups, xs: dict, stream, comm_stream=None, side_streams=()) -> list:
+        """forward_group of several suffix groups whose inputs are all ready
+        (a decode step's q/k/v, o, gate/up, down with their inputs given),
+        arranged so the exchange hides behind the compute: each group's
+        all-gather runs on `comm_stream` while `stream` goes on with the next
+        group's forward, and the suffixes of one group run concurrently on
+        `side_streams` (narrow column shards fill few SMs each).  Every rank
+        issues the same gathers in the same order.  Returns one dict per
+        group, ready on `stream` (which waits for the last gather, so the
+        next call's forwards are ordered after this call's gathers)."""
+        import torch
+        if comm_stream is None or self.world == 1:
+            return [self.forward_group(g, xs, stream, side_streams) for g in groups]
+        import torch.distributed as dist
+        done = []
+        for g in groups:
+            views, flat, gathered = self._group_compute(g, xs, stream, side_streams)
+            comm_stream.wait_stream(stream)
+            with torch.cuda.stream(comm_stream):
+                dist.all_gather_into_tensor(gathered, flat, group=self.group)
+            done.append((views, flat, gathered))
+        stream.wait_stream(comm_stream)
+        with torch.cuda.stream(stream):
+            return [self._group_results(*d) for d in done]
+
+    def forward_group(self, names, xs: dict, stream, side_streams=()) -> dict:
         """forward_device of several suffixes with ONE all-gather: each
         suffix's slice [B, s_i] is written to its block of one buffer
         (blocks back to back), the buffer is gathered once and split.
-        xs: {name: x [B, in_dim] on `stream`}; returns {name: [B, out_dim]}."""
+        xs: {name: x [B, in_dim] on `stream`}; returns {name: [B, out_dim]}.
+        With `side_streams` the suffixes' forwards run concurrently on them
+        (each waits for `stream`, and `stream` waits for them)."""
+        import torch
+        views, flat, gathered = self._group_compute(names, xs, stream, side_streams)
+        with torch.cuda.stream(stream):
+            if self.world > 1:
+                import torch.distributed as dist
+                dist.all_gather_into_tensor(gathered, flat, group=self.group)
+            return self._group_results(views, flat, gathered)
+
+    def _group_compute(self, names, xs: dict, stream, side_streams=()):
+        """The forwards of one suffix group into its gather buffer; returns
+        (the output views, valid once the buffer is gathered, the buffer,
+        the gather target)."""
         import torch
         names = list(names)
         b = xs[names[0]].shape[0]
@@ -287,16 +327,27 @@ class FoldedStack:
         flat, gathered = bufs[key]
         off = 0
         views = []
-        for n, si in zip(names, sl):
+        sides = list(side_streams) if len(names) > 1 else []
+        for k, (n, si) in enumerate(zip(names, sl)):
             part = flat[off: off + b * si].view(b, si)
-            self._forward_part(n, xs[n], part, stream)
+            st = stream
+            if sides:
+                st = sides[k % len(sides)]
+                st.wait_stream(stream)   # inputs ready, the buffer's last readers done
+            self._forward_part(n, xs[n], part, st)
             views.append((n, off, si))
             off += b * si
+        for st in sides[: len(names)]:
+            stream.wait_stream(st)
+        return (views, b), flat, gathered
+
+    def _group_results(self, views, flat, gathered) -> dict:
+        """{name: [B, out_dim]} from a group's buffer (world 1) or its
+        gather target; the caller runs this on the stream that the gather is
+        ordered on (the column interleave copies)."""
+        views, b = views
         if self.world == 1:
             return {n: flat[o: o + b * si].view(b, si)[:, : self.parts[n].out_dim] for n, o, si in views}
-        import torch.distributed as dist
-        with torch.cuda.stream(stream):
-            dist.all_gather_into_tensor(gathered, flat, group=self.group)
         return {n: gathered[:, o: o + b * si].reshape(self.world, b, si).permute(1, 0, 2).reshape(b, self.world * si)
                 [:, : self.parts[n].out_dim] for n, o, si in views}
 

@@ -395,9 +395,20 @@ def _decode_outputs(rank, world, dev):
         for name in suffixes:
             out[name] = st.forward_device(name, xs[name], stream).cpu().numpy().copy()
         # the same outputs with one all-gather per suffix group
-        for group in (["q_proj", "k_proj", "v_proj"], ["o_proj"], ["gate_proj", "up_proj"], ["down_proj"]):
+        groups = (["q_proj", "k_proj", "v_proj"], ["o_proj"], ["gate_proj", "up_proj"], ["down_proj"])
+        for group in groups:
             for name, y in st.forward_group(group, xs, stream).items():
                 out["grouped_" + name] = y.cpu().numpy().copy()
+        # and with each gather overlapped with the next group's forwards and a
+        # group's suffixes on concurrent streams; twice, so the second call
+        # rewrites the buffers the first one gathered from
+        comm = torch.cuda.Stream(device=dev)
+        sides = [torch.cuda.Stream(device=dev) for _ in range(3)]
+        for _ in range(2):
+            res = st.forward_groups(groups, xs, stream, comm, sides)
+        for d in res:
+            for name, y in d.items():
+                out["overlap_" + name] = y.cpu().numpy().copy()
     stream.synchronize()
     return out
 
@@ -422,7 +433,8 @@ def test_sharded_decode_two_nccl_ranks(tmp_path):
     the unsharded stack bit for bit (column sharding does not reorder any
     sum: each output column's rows are summed in ascending order, the folds
     in ascending order, on whichever rank holds the column), with one
-    all-gather per suffix and with one per suffix group."""
+    all-gather per suffix, with one per suffix group, and with the group
+    gathers overlapped with the next group's forwards."""
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
@@ -432,8 +444,9 @@ def test_sharded_decode_two_nccl_ranks(tmp_path):
     want = _decode_outputs(0, 1, 0)
     for name, y in want.items():
         assert np.array_equal(got[name], y), name
-        if name.startswith("grouped_"):
-            assert np.array_equal(y, want[name[len("grouped_"):]]), name
+        for pre in ("grouped_", "overlap_"):
+            if name.startswith(pre):
+                assert np.array_equal(y, want[name[len(pre):]]), name
 
 
 # ── FoldedLayer.forward in one call (sili_folded_forward) ──────────────────
@@ -475,9 +488,11 @@ def test_folded_forward_matches_reference_sums(ns, n_folds, out_dim, B, fold_sum
 
 @pytest.mark.gpu
 def test_forward_group_matches_forward_device():
-    """forward_group (one gather buffer for several suffixes) equals
-    forward_device per suffix, world 1."""
+    """forward_group (one gather buffer for several suffixes) and
+    forward_groups (suffixes on concurrent streams) equal forward_device per
+    suffix, world 1."""
     r = _decode_outputs(0, 1, 0)
     for name in list(r):
-        if name.startswith("grouped_"):
-            assert np.array_equal(r[name], r[name[len("grouped_"):]]), name
+        for pre in ("grouped_", "overlap_"):
+            if name.startswith(pre):
+                assert np.array_equal(r[name], r[name[len(pre):]]), name
