@@ -114,6 +114,9 @@ void launch_copy_pad(const float* in, float* out, int64_t C, cudaStream_t s);
 void launch_accum_abs(const float* x, float* acc, int B, int64_t n, cudaStream_t s,
                       unsigned long long* nonfinite = nullptr, unsigned long long tag = 0);
 void launch_accum_abs_t(const float* xT, float* acc, int B, int64_t n, cudaStream_t s);
+// out = in^T ([R, C] -> [C, R]) with launch_accum_abs(in, acc, R, C, nonfinite, tag) fused
+void launch_transpose_accum(const float* in, float* out, int64_t R, int64_t C, float* acc,
+                            unsigned long long* nonfinite, unsigned long long tag, cudaStream_t s);
 // forward: y[B, n_out] from xT [n_in, B]; sparse_formula selects the
 // sisldo_forward arithmetic (sisldo_ops.hpp:289-308) over disldo_forward's.
 void launch_forward(const LayerView& L, const float* xT, int B, float* y, bool sparse_formula,

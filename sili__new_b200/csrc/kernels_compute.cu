@@ -75,6 +75,53 @@ void launch_accum_abs(const float* x, float* acc, int B, int64_t n, cudaStream_t
     k_accum_abs<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(x, acc, B, n, nonfinite, tag); count_launch();
 }
 
+// The transpose of dy [B, n] into dyT [n, B] and, on the way, the |dy|
+// accumulation and non-finite flag of k_accum_abs (same order: b ascending
+// per column): one read of dy instead of two.  A CTA owns 32 columns and
+// walks the samples in 32-row tiles; one thread per column carries the sum.
+__global__ void k_transpose_accum(const float* __restrict__ in, float* __restrict__ out, int64_t R, int64_t C,
+                                  float* __restrict__ acc, unsigned long long* __restrict__ nonfinite,
+                                  unsigned long long tag) {
+    __shared__ float tile[32][33];
+    const int64_t c0 = (int64_t)blockIdx.x * 32;
+    const int64_t cs = c0 + threadIdx.x;   // the column this thread sums (threadIdx.y == 0)
+    const bool summer = threadIdx.y == 0 && cs < C;
+    float a = summer ? acc[cs] : 0.0f;
+    const bool was_finite = isfinite(a);
+    bool term_bad = false;
+    for (int64_t r0 = 0; r0 < R; r0 += 32) {
+        __syncthreads();   // the previous tile's readers are done
+        for (int j = threadIdx.y; j < 32; j += 8) {
+            const int64_t r = r0 + j, c = c0 + threadIdx.x;
+            if (r < R && c < C) tile[j][threadIdx.x] = in[r * C + c];
+        }
+        __syncthreads();
+        if (summer) {
+            const int nr = (int)(R - r0 < 32 ? R - r0 : 32);
+            for (int j = 0; j < nr; ++j) {
+                const float v = fabsf(tile[j][threadIdx.x]);
+                a = __fadd_rn(a, v);
+                term_bad |= !(v <= 3.402823466e38f);
+            }
+        }
+        for (int j = threadIdx.y; j < 32; j += 8) {
+            const int64_t c = c0 + j, r = r0 + threadIdx.x;
+            if (r < R && c < C) out[c * R + r] = tile[threadIdx.x][j];
+        }
+    }
+    if (!summer) return;
+    acc[cs] = a;
+    // as k_accum_abs: a non-finite sum that this call made non-finite, or
+    // one with an inf or NaN term
+    if (nonfinite && !isfinite(a) && (was_finite || term_bad)) *nonfinite = tag;
+}
+void launch_transpose_accum(const float* in, float* out, int64_t R, int64_t C, float* acc,
+                            unsigned long long* nonfinite, unsigned long long tag, cudaStream_t s) {
+    if (R == 0 || C == 0) return;
+    k_transpose_accum<<<(unsigned)((C + 31) / 32), dim3(32, 8), 0, s>>>(in, out, R, C, acc, nonfinite, tag);
+    count_launch();
+}
+
 // Same accumulation from the transposed input xT [n, B].
 __global__ void k_accum_abs_t(const float* __restrict__ xT, float* __restrict__ acc, int B, int64_t n) {
     const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;

@@ -1600,11 +1600,10 @@ static int backward_dense_impl(sili_layer* h, const float* x, const float* dy, i
     const float* dyd = nullptr;
     RC(stage_in(h, dy, (size_t)batch * n_out, h->dy_stage, &dyd, s));
     RC(h->dyT.reserve((int64_t)batch * n_out + 1));
-    launch_transpose(dyd, h->dyT.p, batch, n_out, s);
-    // accumulators, linear_disldo.hpp:515-520
+    // accumulators, linear_disldo.hpp:515-520 (the |dy| sums with dy's transpose)
     launch_accum_abs_t(h->xT.p, h->in_acc.p, batch, n_in, s);
     const unsigned long long dy_tag = (unsigned long long)h->call + 1;   // never 0, the flag's initial value
-    launch_accum_abs(dyd, h->grad_acc.p, batch, n_out, s, h->d_dyflag.p, dy_tag);
+    launch_transpose_accum(dyd, h->dyT.p, batch, n_out, h->grad_acc.p, h->d_dyflag.p, dy_tag, s);
     const bool dev_out = is_device_ptr(dx);
     float* dxd = dx;
     if (!dev_out) {
