@@ -695,6 +695,13 @@ def run_folded(args, dev, rank, world, dist, S, torch, which="config5"):
         ms = float(t.item())
         dist.all_reduce(nnz_t)
     total_nnz = int(nnz_t.item())
+    # device memory per synapse held by this rank's layers (format, derived
+    # column index, everything)
+    dev_b = {"format": 0, "index": 0, "total": 0}
+    for name in suffixes:
+        for k, v in stack.parts[name].layer.device_bytes().items():
+            dev_b[k] += v
+    dev_bps = {k: v / max(nnz_local, 1) for k, v in dev_b.items()}
     flops = 2.0 * total_nnz * B
     mem_gb = torch.cuda.max_memory_allocated(dev) / 1e9
     if rank != 0:
@@ -708,6 +715,7 @@ def run_folded(args, dev, rank, world, dist, S, torch, which="config5"):
                         f"with the next group's forwards; a group's suffixes on concurrent streams)",
             "collectives_per_step": len(groups) if world > 1 else 0,
             "build_s_rank0": build_s, "torch_mem_gb_rank0": mem_gb, "gpu_launches_rank0": launches,
+            "device_bytes_per_synapse_rank0": dev_bps,
             "data": f"synthetic: random N(0,0.02) pruned to {density * 100:g}% (uniform pattern), x ~ N(0,1)",
             "train": train}
 
@@ -1110,6 +1118,8 @@ def _leg_folded(f):
         out["train_tok_s"] = _r(f["train"]["value"])
     if f.get("parts_ms"):
         out["parts_ms"] = {k: _r(v, 3) for k, v in f["parts_ms"].items()}
+    if f.get("device_bytes_per_synapse_rank0"):
+        out["dev_B_per_syn"] = _r(f["device_bytes_per_synapse_rank0"]["total"], 3)
     return out
 
 

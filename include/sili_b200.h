@@ -61,6 +61,12 @@ int sili_kernel_launches(int64_t* count);
  * kernels' durations in milliseconds (synchronising the layer's stream). */
 int sili_layer_set_kernel_timing(sili_layer* h, int enable);
 int sili_layer_kernel_ms(sili_layer* h, float* forward_ms, float* backward_ms);
+/* device memory the layer holds, in bytes (allocated capacities): the
+ * delta-CSR format with its headroom (index bytes, value bytes, row
+ * offsets), the derived column index, and everything including scales,
+ * statistics and kept scratch.  No reference counterpart (the reference's
+ * layer lives in host memory); any pointer may be NULL. */
+int sili_layer_device_bytes(sili_layer* h, int64_t* format, int64_t* index, int64_t* total);
 /* Measurement utility, no counterpart in the reference: the device's FP32
  * FMA throughput (16 independent fma chains per thread, every SM full, best
  * of 4 timed launches of `iters` iterations), the denominator of the FP32

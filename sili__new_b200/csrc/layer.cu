@@ -401,12 +401,14 @@ int ensure_aux(sili_layer* h, cudaStream_t s) {
     launch_pad_csc(h->colcount.p, h->colptr.p, C, (int)R, h->crow.p, h->cvpos.p, s);
     CK(cudaGetLastError());
     // the rebuild's own arrays (24 bytes per synapse: the row and value
-    // position of every synapse, the sort's keys and values) are not read
-    // again until the next rebuild: a large layer gives them back, keeping
-    // only abs_cols, crow, cvpos, fcpos and cpack (20 bytes per synapse)
+    // position of every synapse, the sort's keys and values, plus the sort's
+    // temporary storage) are not read again until the next rebuild: a large
+    // layer gives them back, keeping only abs_cols, crow, cvpos, fcpos and
+    // cpack (20 bytes per synapse)
     if ((int64_t)nz * 24 > kRebuildKeepBytes) {
         h->frow.release(); h->fvpos.release();
         h->sort_k.release(); h->sort_ko.release(); h->sort_v.release(); h->sort_vo.release();
+        h->cub_tmp.release();   // the sort's temporary storage (about 8 bytes per synapse)
     }
     {   // rows with no synapse take the dead-row bootstrap (linear_disldo.hpp:1985-2042)
         std::vector<int> rp((size_t)R + 1);
@@ -658,6 +660,13 @@ int import_csr(sili_layer* h, const int* d_ptrs, const int* d_idx, const float* 
     h->val_n = vb;
     h->total_nnz = nnz;
     h->aux_dirty = true;
+    // a large layer gives back the import's scratch (8 bytes per synapse)
+    // and the arrays it replaced (the constructor's budget, or the last
+    // layout): the next rebuild allocates them again
+    if ((int64_t)nnz * 8 > kRebuildKeepBytes) {
+        h->imp_len.release(); h->imp_boff.release();
+        h->idx_spare.release(); h->val_spare.release();
+    }
     return SILI_OK;
 }
 
@@ -1087,6 +1096,45 @@ int sili_layer_kernel_ms(sili_layer* h, float* fwd, float* bwd) {
     if (bwd) *bwd = 0.f;
     if (h->ev_fwd && fwd) { CK(cudaEventSynchronize(h->ev[1])); CK(cudaEventElapsedTime(fwd, h->ev[0], h->ev[1])); }
     if (h->ev_bwd && bwd) { CK(cudaEventSynchronize(h->ev[3])); CK(cudaEventElapsedTime(bwd, h->ev[2], h->ev[3])); }
+    return SILI_OK;
+}
+
+// Bytes of device memory a layer holds, by role (capacities, headroom and
+// kept scratch included).
+extern "C++" {
+template <typename... Bufs>
+static int64_t dbytes(const Bufs&... b) {
+    return (int64_t(0) + ... + (b.cap * (int64_t)sizeof(*b.p)));
+}
+}
+int sili_layer_device_bytes(sili_layer* h, int64_t* format, int64_t* index, int64_t* total) {
+    RC(use(h));
+    const int64_t fmt = dbytes(h->idx, h->val, h->bs, h->be, h->es, h->ee);
+    const int64_t ix = dbytes(h->rowptr, h->abs_cols, h->frow, h->fvpos, h->colcount, h->colptr, h->crow, h->cvpos,
+                              h->sort_k, h->sort_ko, h->sort_v, h->sort_vo, h->colptr_x, h->padcnt, h->fcpos,
+                              h->cpack, h->cub_tmp);
+    int64_t rest = dbytes(h->vs, h->os, h->vsi, h->osi, h->vsm, h->is, h->ois, h->vstep, h->ostep, h->def_cw,
+                          h->def_ci, h->in_acc, h->grad_acc, h->out_degree, h->prow, h->pcol, h->pval, h->pb_keys,
+                          h->pb_iota, h->pb_in, h->pb_out, h->pb_flags, h->pb_pos, h->pb_tr, h->pb_tc, h->pb_counts,
+                          h->pb_tv, h->d_st, h->d_stmax, h->d_dyflag, h->xT, h->dyT, h->dxT, h->colg, h->colc,
+                          h->ytmp, h->x_stage, h->dy_stage, h->dx_stage, h->xsT, h->fold_raw, h->shard_nnz, h->rpart,
+                          h->presT, h->presX, h->dS, h->sgs, h->sgc, h->i_tmp0, h->i_tmp1, h->i_tmp2, h->f_tmp0,
+                          h->pow_tab);
+    rest += dbytes(h->b4_es, h->b4_alloc, h->b4_used, h->b4_nt, h->b4_bc, h->b4_tile, h->b4_sparse, h->b4_cnt,
+                   h->b4_hs, h->b4_mr, h->b4_mc, h->b4_cptr, h->b4_ctile, h->b4_cbr, h->b4_keys, h->b4_keys_o,
+                   h->b4_perm, h->b4_perm_o, h->b4_slots, h->b4_brs, h->b4_off, h->b4_xs, h->b4_part, h->tc_err,
+                   h->b4_pmap, h->b4_pmapT);
+    const auto& y = h->syn;
+    rest += dbytes(y.pr_ptr, y.keys, y.keys_o, y.ids, y.ids_o, y.od0, y.od_decs, y.scratch, y.did, y.res, y.s_idx,
+                   y.s_val, y.s_be, y.s_ee, y.s_od, y.s_nt, y.s_bc, y.s_tile, y.s_sp, y.s_alloc, y.s_cnt);
+    const auto& t = h->topk;
+    rest += dbytes(t.bits, t.keys, t.pk, t.pk_o, t.hist, t.cand, t.cand_o, t.eq, t.nsel, t.pid, t.pid_o, t.cptr,
+                   t.cnt, t.nptr, t.drop, t.sel, t.nge, t.di, t.nidx, t.dw, t.dm, t.nw, t.nimp);
+    rest += dbytes(h->imp_len, h->imp_boff, h->imp_rb, h->imp_rn, h->idx_spare, h->val_spare, h->csr_p, h->csr_i,
+                   h->csr_v);
+    if (format) *format = fmt;
+    if (index) *index = ix;
+    if (total) *total = fmt + ix + rest;
     return SILI_OK;
 }
 

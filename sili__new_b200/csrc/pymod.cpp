@@ -246,6 +246,15 @@ public:
         check(sili_layer_kernel_ms(h, &f, &b));
         return py::make_tuple(f, b);
     }
+    py::dict device_bytes() {
+        int64_t fmt = 0, ix = 0, tot = 0;
+        check(sili_layer_device_bytes(h, &fmt, &ix, &tot));
+        py::dict d;
+        d["format"] = fmt;
+        d["index"] = ix;
+        d["total"] = tot;
+        return d;
+    }
 
     void build_probes(int k, bool per_row) { check(sili_layer_build_probes(h, k, per_row ? 1 : 0)); }
     py::tuple probes() {
@@ -472,6 +481,7 @@ void bind_layer(py::module_& m, const char* name) {
         .def("sync", &T::sync)
         .def("set_kernel_timing", &T::set_kernel_timing, py::arg("enable"))
         .def("kernel_ms", &T::kernel_ms)
+        .def("device_bytes", &T::device_bytes)
         .def("build_probes", &T::build_probes, py::arg("k"), py::arg("per_row") = false)
         .def("probes", &T::probes)
         .def("synap_row_step", &T::synap_row_step, py::arg("current_row"), py::arg("importance_cutoff"),

@@ -362,3 +362,18 @@ def test_forward_sparse_vec_vs_oracle(S, B):
     x = relu_sparse_x(np.random.default_rng(B), B, n_in)
     px, ix, vx = O.dense_to_csr(x, 0.0)
     assert np.array_equal(g.forward_sparse(px, ix, vx, B), o.forward_sparse(px, ix, vx, B))
+
+
+def test_device_bytes(S):
+    """sili_layer_device_bytes: the format (index + value bytes with their
+    headroom, row offsets) and the derived column index (decoded columns,
+    CSC rows, value positions, synapse -> CSC map, packed words: 20 B per
+    synapse at least) within the layer's total."""
+    n_in, n_out = 300, 500
+    p, i, w, vs = random_layer(n_in, n_out, 30, seed=5)
+    g = setup_layer(S.SparseLinearLayerDeterministic(n_in, n_out, len(i) * 2), p, i, w, vs)
+    g.forward_dense(np.ones((4, n_in), np.float32))
+    d = g.device_bytes()
+    assert d["format"] >= 2 * len(i) + 32 * n_in
+    assert d["index"] >= 20 * len(i)
+    assert d["total"] >= d["format"] + d["index"]
